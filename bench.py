@@ -1,0 +1,381 @@
+#!/usr/bin/env python3
+"""INT8 samples/s and achieved INT8 TOPS of the B200 Npu(Int8) execution provider.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c1|c3a|c3b|c3c] [--impl ours|reference]
+
+N > 1 runs under torchrun (one process per GPU).  Weak scaling: every rank
+runs its own shard of a global batch of N x per-GPU batch; each Linear's
+activation absmax is max-all-reduced over NCCL so every rank quantizes
+exactly as one device running the global batch would.
+
+`value` times the program on device-resident inputs (CUDA events on the
+launching stream, L2 flushed by a 256 MiB write before every timed step,
+max over ranks).  `e2e` times the public host-buffer call
+(InferenceSession.run -> rg_session_run) from pinned memory, H2D and D2H
+included.  `--impl reference` times the CPU restatement of the reference
+Npu(Int8) path (oracle/) on the host cores, the reference itself being
+Rust that this image cannot compile.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "INT8 samples/sec and achieved TOPS vs B200 dense INT8 peak at 1/2/4/8 GPUs"
+L2_FLUSH_BYTES = 256 << 20
+NOMINAL_INT8_TOPS = 4500.0
+
+WORKLOADS = {
+    "c2": dict(name="small CNN INT8 (Conv(1,16,3,p1)+BN+ReLU, MaxPool2, Conv(16,32,3,p1)+BN+ReLU, MaxPool2, "
+                    "Flatten, Linear(1568,128)+ReLU, Linear(128,10)), x [B,1,28,28] ~ U(0,1)", batch=32768),
+    "c1": dict(name="README MLP INT8 (Linear(4,32)+BN1d+ReLU+Linear(32,3)), x [B,4] ~ N(0,1)", batch=65536),
+    "c3a": dict(name="fused INT8 Linear+GELU 4096x4096x4096", shape=(4096, 4096, 4096)),
+    "c3b": dict(name="fused INT8 Linear+GELU 16384x8192x8192", shape=(16384, 8192, 8192)),
+    "c3c": dict(name="fused INT8 Linear+GELU 65536x4096x14336", shape=(65536, 4096, 14336)),
+}
+
+
+def build_workload(cfg: str, rank: int, world: int, batch: int | None):
+    """(model, x shard, per-GPU units, units name) built with the reference generator."""
+    from rustgears_b200 import configs
+    w = WORKLOADS[cfg]
+    if cfg in ("c1", "c2"):
+        b = batch or w["batch"]
+        fn = configs.c2_cnn if cfg == "c2" else configs.c1_mlp
+        model, x = fn(b, row_offset=rank * b)
+        return model, x, b
+    m, k, n = w["shape"]
+    mb = batch or m
+    model, x = configs.c3_linear(m * world, k, n, rows=mb, row_offset=rank * mb)
+    return model, x, mb
+
+
+def program_macs(sess, x_shape) -> int:
+    import numpy as _np
+    one = (1,) + tuple(x_shape[1:])
+    sess.run(_np.zeros(one, _np.float32))
+    return int(sess.last_npu_profile().total_macs)
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([v.strip() for v in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) >= 9 for i in range(4)
+                          if r[5 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def measured_peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except OSError:
+        return {}
+
+
+def op_roofline(cfg, sess, per_op_ns, steps, units, peaks, traffic=None):
+    """Roofline of the dominant op: algorithmic bytes (HBM-bound ops) or INT8 ops
+    (tensor-bound GEMMs) per launch divided by its mean CUDA-event duration."""
+    prof = sess.last_npu_profile()
+    i = int(np.argmax(per_op_ns))
+    rec = prof.records[i]
+    dur_s = per_op_ns[i] / steps / 1e9
+    info = sess.op_info(i)
+    label = rec.op
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    int8_peak = 2.0 * peaks.get("bf16_tflops", 1590.0)
+    if cfg.startswith("c3"):
+        ops = 2.0 * rec.macs
+        achieved = ops / dur_s / 1e12
+        return {"kernel": label, "bound": "tensor", "achieved": achieved, "peak": int8_peak,
+                "unit": "TOPS", "frac": achieved / int8_peak, "traffic": traffic,
+                "peak_source": "2 x measured bf16 dense (MEASURED_PEAKS.json); nominal INT8 dense 4500",
+                "mean_launch_us": dur_s * 1e6}
+    # HBM-bound: algorithmic bytes = f32 input read + f32 output written (+ weights once)
+    in_elems = out_elems = 0
+    shapes = _op_shapes(sess, units)
+    in_shape, out_shape = shapes[i]
+    in_elems, out_elems = int(np.prod(in_shape)), int(np.prod(out_shape))
+    wbytes = info["wq_len"] + 4 * info["bias_len"]
+    algo = 4 * in_elems + 4 * out_elems + wbytes
+    achieved = algo / dur_s / 1e9
+    return {"kernel": label, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+            "frac": achieved / hbm, "traffic": traffic, "algorithmic_bytes": algo,
+            "peak_source": "measured hbm_gbs (MEASURED_PEAKS.json)", "mean_launch_us": dur_s * 1e6}
+
+
+def _op_shapes(sess, batch):
+    shapes = []
+    shape = None
+    for i in range(sess.num_ops()):
+        info = sess.op_info(i)
+        if shape is None:
+            shape = _input_shape_of(sess, batch)
+        out = _out_shape(info, shape)
+        shapes.append((shape, out))
+        shape = out
+    return shapes
+
+
+def _input_shape_of(sess, batch):
+    first = sess.raw_layers()[0]
+    if first.kind == 2:
+        return (batch, first.in_channels, 28, 28)
+    return (batch, first.in_features if first.kind == 1 else 1)
+
+
+def _out_shape(info, shape):
+    k = info["kind"]
+    if k == 1:
+        return tuple(shape[:-1]) + (info["out_features"],)
+    if k == 2:
+        n, c, h, w = shape
+        oh = (h + 2 * info["padding"] - info["kernel"]) // info["stride"] + 1
+        ow = (w + 2 * info["padding"] - info["kernel"]) // info["stride"] + 1
+        return (n, info["out_channels"], oh, ow)
+    if k == 4:
+        n, c, h, w = shape
+        return (n, c, (h - info["kernel"]) // info["stride"] + 1, (w - info["kernel"]) // info["stride"] + 1)
+    if k == 5:
+        return (shape[0], int(np.prod(shape[1:])))
+    return shape
+
+
+def cpu_baseline(cfg: str, model, x, steps: int = 0, target_s: float = 12.0):
+    """The oracle (CPU restatement of the reference path) on a bounded sample,
+    with every host core (the reference's rayon decomposition)."""
+    from oracle import oracle
+    from rustgears_b200.spec import as_dict
+    layers = [as_dict(l) for l in model.export()]
+    prog = oracle.Program(layers)
+    cores = os.cpu_count() or 1
+    if cfg.startswith("c3"):
+        # rows sampled from the full activation (the absmax covers all rows, as the reference's serial pass)
+        rows = 16
+        t0 = time.perf_counter()
+        oracle.linear_rows(prog.ops[0], prog, 0, x, 0, rows, nthreads=cores)
+        dt = time.perf_counter() - t0
+        per_row = dt / rows
+        rows = max(16, min(x.shape[0], int(target_s / max(per_row, 1e-9))))
+        rows = min(rows, 1024)
+        t0 = time.perf_counter()
+        oracle.linear_rows(prog.ops[0], prog, 0, x, 0, rows, nthreads=cores)
+        dt = time.perf_counter() - t0
+        m = x.shape[0]
+        return {"value": rows / dt / m, "unit": "GEMMs/s (rows/s / M)", "cores": cores, "kind": "port",
+                "sample": f"{rows} of {m} rows (scale over all rows), {cores} threads; extrapolated linearly in M",
+                "sample_seconds": dt}
+    n = min(64, x.shape[0])
+    t0 = time.perf_counter()
+    prog.execute(x[:n], nthreads=cores)
+    dt = time.perf_counter() - t0
+    n = int(min(x.shape[0], max(n, target_s / max(dt / n, 1e-9))))
+    t0 = time.perf_counter()
+    prog.execute(x[:n], nthreads=cores)
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "samples/s", "cores": cores, "kind": "port",
+            "sample": f"{n} samples of the benchmark batch through og_execute, {cores} threads",
+            "sample_seconds": dt}
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    cfg = args.config
+    model, x, units = build_workload(cfg, 0, 1, args.batch)
+    from oracle import oracle
+    from rustgears_b200.spec import as_dict
+    prog = oracle.Program([as_dict(l) for l in model.export()])
+    cores = os.cpu_count() or 1
+    c3 = cfg.startswith("c3")
+    sample = 64 if c3 else min(units, 2048 if cfg == "c2" else units)
+    ts = []
+    for step in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        if c3:
+            oracle.linear_rows(prog.ops[0], prog, 0, x, 0, sample, nthreads=cores)
+        else:
+            prog.execute(x[:sample], nthreads=cores)
+        if step >= args.warmup:
+            ts.append(time.perf_counter() - t0)
+    dt = float(np.sum(ts))
+    if c3:  # each step computes `sample` of the GEMM's `units` rows
+        value = sample * args.steps / dt / units
+        unit = "GEMMs/s"
+    else:
+        value = sample * args.steps / dt
+        unit = "samples/s"
+    line = {"metric": METRIC, "impl": "reference", "value": value, "unit": unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic", "config": {"workload": WORKLOADS[cfg]["name"], "per_step_sample": sample},
+            "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port",
+                             "sample": f"{sample} {'rows' if c3 else 'samples'} per step, {cores} threads "
+                                       "(CPU restatement of the reference Npu(Int8) path)"},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c2", choices=sorted(WORKLOADS))
+    ap.add_argument("--batch", type=int, default=None, help="per-GPU batch (rows for c3)")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import datetime
+
+    import torch
+    import torch.distributed as tdist
+
+    from rustgears_b200 import ExecutionProvider, InferenceSession, dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    cfg = args.config
+    model, x, units = build_workload(cfg, rank, world, args.batch)
+    sess = InferenceSession.from_module(model, ExecutionProvider.npu_int8(), device=local)
+    if world > 1:
+        uid = dist.exchange_unique_id(rank)
+        dist.attach(sess, rank, world, uid)
+    xd = torch.from_numpy(x).to(dev)
+    oshape = sess.output_shape(tuple(x.shape))
+    yd = torch.empty(oshape, dtype=torch.float32, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            tdist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        flush.fill_(1)
+        sess.run_device(xd, yd)
+    nops = sess.num_ops()
+    per_op_ns = np.zeros(nops)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    launches = 0
+    barrier()
+    with ClockSampler(local) as clocks:
+        for s in range(args.steps):
+            flush.fill_(s & 0xff)                      # 256 MiB write: evicts L2 before each timed step
+            evs[s][0].record(stream)
+            sess.run_device(xd, yd)                    # profiled run: per-op CUDA events on this stream
+            evs[s][1].record(stream)
+            prof = sess.last_npu_profile()
+            per_op_ns += np.array([r.duration_ns for r in prof.records], dtype=np.float64)
+            launches += prof.kernel_launches
+        barrier()
+    total_ms = float(sum(a.elapsed_time(b) for a, b in evs))
+    if world > 1:
+        t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    macs_unit = program_macs(sess, x.shape) if not cfg.startswith("c3") else int(np.prod(WORKLOADS[cfg]["shape"][1:]))
+    units_all = units * world
+    value = units_all / (ms_per_step / 1e3)
+    tops = value * 2.0 * macs_unit / 1e12
+
+    # end to end through the public host-buffer call, pinned host memory
+    xh = torch.from_numpy(x).pin_memory().numpy()
+    yh = torch.empty(oshape, dtype=torch.float32).pin_memory().numpy()
+    sess.run(xh, out=yh)
+    barrier()
+    e2e_steps = max(3, min(args.steps, 10))
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        sess.run(xh, out=yh)
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = units_all * e2e_steps / e2e_s
+
+    peaks = measured_peaks()
+    line = {
+        "metric": METRIC, "value": value, "unit": "samples/s" if not cfg.startswith("c3") else "GEMMs/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (reference generator, manual_seed(42))",
+        "config": {"workload": WORKLOADS[cfg]["name"], "global_batch": units_all, "per_gpu_batch": units,
+                   "parallelism": f"dp{world}", "l2": "flushed before every timed step (256 MiB write)"},
+        "tops": tops, "tops_frac_of_nominal_int8": tops / NOMINAL_INT8_TOPS,
+        "int8_macs_per_unit": macs_unit,
+        "roofline": op_roofline(cfg, sess, per_op_ns, args.steps, units, peaks),
+        "e2e": {"value": e2e_value, "unit": "samples/s" if not cfg.startswith("c3") else "GEMMs/s",
+                "h2d_bytes_per_step": int(xh.nbytes), "d2h_bytes_per_step": int(yh.nbytes),
+                "api": "InferenceSession.run (rg_session_run), pinned host buffers", "steps": e2e_steps},
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg, model, x)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del sess
+    if world > 1:
+        tdist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,157 @@
+"""TEST INFRASTRUCTURE ONLY: the benchmark configurations built with the
+oracle's restatement of the reference RNG and initialisers.
+
+Draw order (the reference's global RNG after ``manual_seed(seed)``):
+module construction order -- every ``Linear::new`` / ``Conv2d::new`` draws its
+weight and then its bias (nn/layers.rs:27-34, 108-119) -- then each BatchNorm's
+running statistics (mean ~ U(-0.1, 0.1), then var ~ U(0.5, 1.5)), then the
+input.  BatchNorm gamma = 1 and beta = 0 (nn/norm.rs:56-59); its export is
+``scale = g / sqrt(rv + eps)``, ``shift = b - rm * scale`` with eps = 1e-5
+(nn/norm.rs:335-343).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from .oracle import (ACT_GELU, ACT_RELU, ACTIVATION, CHANNEL_AFFINE, CONV2D, FLATTEN, LINEAR,
+                     MAXPOOL2D, Rng)
+
+
+def linear(rng: Rng, fin: int, fout: int) -> dict:  # Linear::new (nn/layers.rs:27-34)
+    w = rng.kaiming_uniform((fin, fout), fin)
+    b = rng.bias_uniform((fout,), fin)
+    return dict(kind=LINEAR, in_features=fin, out_features=fout, weight=w, bias=b)
+
+
+def conv2d(rng: Rng, cin: int, cout: int, k: int, stride: int = 1, padding: int = 0) -> dict:
+    fan_in = cin * k * k  # Conv2d::new (nn/layers.rs:108-119)
+    w = rng.kaiming_uniform((cout, cin, k, k), fan_in)
+    b = rng.bias_uniform((cout,), fan_in)
+    return dict(kind=CONV2D, in_channels=cin, out_channels=cout, kernel=k, stride=stride,
+                padding=padding, weight=w, bias=b)
+
+
+def batchnorm(c: int) -> dict:
+    """Placeholder until the stats are drawn; filled by ``draw_bn_stats``."""
+    return dict(kind=CHANNEL_AFFINE, _bn=c)
+
+
+def draw_bn_stats(rng: Rng, layers: list) -> list:
+    out = []
+    for l in layers:
+        if l.get("_bn"):
+            c = l["_bn"]
+            rm = rng.uniform_tensor((c,), -0.1, 0.1)
+            rv = rng.uniform_tensor((c,), 0.5, 1.5)
+            g = np.ones(c, np.float32)
+            b = np.zeros(c, np.float32)
+            eps = np.float32(1e-5)
+            scale = (g / np.sqrt(rv + eps)).astype(np.float32)
+            shift = (b - rm * scale).astype(np.float32)
+            out.append(dict(kind=CHANNEL_AFFINE, scale=scale, shift=shift))
+        else:
+            out.append(l)
+    return out
+
+
+def act(a: int, p: float = 0.0) -> dict:
+    return dict(kind=ACTIVATION, act=a, act_param=p)
+
+
+def c1_mlp(batch: int = 64, seed: int = 42):
+    """README MLP: Linear(4,32)+BN1d(32)+ReLU+Linear(32,3); x [batch,4] ~ N(0,1)."""
+    rng = Rng(seed)
+    layers = [linear(rng, 4, 32), batchnorm(32), act(ACT_RELU), linear(rng, 32, 3)]
+    layers = draw_bn_stats(rng, layers)
+    x = rng.randn((batch, 4))
+    return layers, x
+
+
+def c2_cnn(batch: int = 256, seed: int = 42):
+    """Small CNN: x [B,1,28,28] ~ U(0,1)."""
+    rng = Rng(seed)
+    layers = [conv2d(rng, 1, 16, 3, 1, 1), batchnorm(16), act(ACT_RELU), dict(kind=MAXPOOL2D, kernel=2, stride=2),
+              conv2d(rng, 16, 32, 3, 1, 1), batchnorm(32), act(ACT_RELU), dict(kind=MAXPOOL2D, kernel=2, stride=2),
+              dict(kind=FLATTEN), linear(rng, 1568, 128), act(ACT_RELU), linear(rng, 128, 10)]
+    layers = draw_bn_stats(rng, layers)
+    x = rng.uniform_tensor((batch, 1, 28, 28), 0.0, 1.0)
+    return layers, x
+
+
+def c3_linear(m: int, k: int, n: int, seed: int = 42, rows: int | None = None):
+    """Single fused INT8 Linear + GELU: W [K,N] ~ 0.02 N(0,1), bias ~ 0.01 N(0,1),
+    A [M,K] ~ N(0,1).  ``rows`` draws only the first rows of A (same values)."""
+    rng = Rng(seed)
+    w = rng.normal_init((k, n), 0.02)
+    b = rng.normal_init((n,), 0.01)
+    x = rng.randn((rows if rows is not None else m, k))
+    layers = [dict(kind=LINEAR, in_features=k, out_features=n, weight=w, bias=b), act(ACT_GELU)]
+    return layers, x
+
+
+def integration_model(seed: int = 2026):
+    """Structure of tests/integration.rs:128-164 (BN stats seeded instead of warmed
+    by a training forward, which is outside this path); x [8,1,8,8]."""
+    rng = Rng(seed)
+    layers = [conv2d(rng, 1, 4, 3, 1, 1), batchnorm(4), act(ACT_RELU), dict(kind=MAXPOOL2D, kernel=2, stride=2),
+              dict(kind=FLATTEN), linear(rng, 64, 16), batchnorm(16), act(ACT_RELU), linear(rng, 16, 4)]
+    layers = draw_bn_stats(rng, layers)
+    x = rng.randn((8, 1, 8, 8))
+    return layers, x
+
+
+def usage_doc_model(seed: int = 42):
+    """docs/USAGE.md:360-380 example: Linear(16,64)+BN1d(64)+ReLU+Linear(64,4), x [32,16]."""
+    rng = Rng(seed)
+    layers = [linear(rng, 16, 64), batchnorm(64), act(ACT_RELU), linear(rng, 64, 4)]
+    layers = draw_bn_stats(rng, layers)
+    x = rng.randn((32, 16))
+    return layers, x
+
+
+def acts_mlp(batch: int = 16, seed: int = 7):
+    """Every activation the IR has, fused and standalone, plus a final Softmax."""
+    from .oracle import ACT_LEAKY_RELU, ACT_SIGMOID, ACT_TANH, SOFTMAX
+    rng = Rng(seed)
+    layers = [linear(rng, 5, 7), act(ACT_SIGMOID), linear(rng, 7, 6), act(ACT_TANH),
+              linear(rng, 6, 9), act(ACT_GELU), act(ACT_LEAKY_RELU, 0.2), linear(rng, 9, 4),
+              act(ACT_LEAKY_RELU, 0.01), linear(rng, 4, 3), dict(kind=SOFTMAX)]
+    x = rng.randn((batch, 5))
+    return layers, x
+
+
+def strided_cnn(batch: int = 3, seed: int = 11):
+    """Strided/padded convs, incl. a 1x1 stride-2 conv that skips pixels, an odd
+    maxpool and a Linear on the flattened map."""
+    rng = Rng(seed)
+    layers = [conv2d(rng, 3, 8, 3, 2, 1), batchnorm(8), act(ACT_RELU),
+              conv2d(rng, 8, 12, 1, 2, 0),
+              dict(kind=MAXPOOL2D, kernel=3, stride=2),
+              conv2d(rng, 12, 16, 2, 1, 0), act(ACT_GELU),
+              dict(kind=FLATTEN), linear(rng, 16, 5)]
+    layers = draw_bn_stats(rng, layers)
+    x = rng.randn((batch, 3, 19, 17))
+    return layers, x
+
+
+def affine_first(batch: int = 6, seed: int = 5):
+    """A leading BatchNorm (no Linear/Conv to fold into: runs as a diagonal
+    FusedLinear, npu.rs:254-270) and a standalone activation."""
+    rng = Rng(seed)
+    layers = [batchnorm(10), act(ACT_RELU), linear(rng, 10, 6), batchnorm(6), linear(rng, 6, 4)]
+    layers = draw_bn_stats(rng, layers)
+    x = rng.randn((batch, 10))
+    return layers, x
+
+
+# name -> builder of (layers, x) used by the golden fixtures and the parity tests
+CASES = {
+    "usage_doc": usage_doc_model,
+    "integration": integration_model,
+    "c1_mlp_64": lambda: c1_mlp(64),
+    "c2_cnn_4": lambda: c2_cnn(4),
+    "c3_linear_small": lambda: c3_linear(32, 64, 48),
+    "acts_mlp": acts_mlp,
+    "strided_cnn": strided_cnn,
+    "affine_first": affine_first,
+}

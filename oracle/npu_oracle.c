@@ -1,0 +1,631 @@
+/*
+ * npu_oracle.c -- TEST INFRASTRUCTURE ONLY (parity checker and CPU baseline).
+ *
+ * A plain-C restatement of the RustGears Npu(Int8) inference path.  Build with
+ * `-O2 -ffp-contract=off -fno-fast-math` (oracle/Makefile): Rust never contracts
+ * a*b+c into an FMA, and Rust's f32::{tanh,exp,ln,cos} call glibc's
+ * tanhf/expf/logf/cosf on linux-gnu, which this file calls too.
+ *
+ * Threading mirrors the reference's rayon decomposition so that the timed CPU
+ * baseline does the same work split: rows for Linear when m*k*n >= 32768
+ * (quantize.rs:104), images for Conv2d when n >= 2 (npu.rs:331), planes for
+ * MaxPool2d when total >= 8192 (kernels.rs:201).  Integer accumulation and
+ * per-element f32 epilogues make every result independent of the thread count.
+ */
+#include "npu_oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+
+/* ------------------------------------------------------------------------ */
+/* parallel-for over [0, n) with static contiguous chunks                    */
+/* ------------------------------------------------------------------------ */
+typedef void (*og_body)(void* ctx, int64_t begin, int64_t end);
+typedef struct { og_body fn; void* ctx; int64_t b, e; } og_chunk;
+
+static void* og_chunk_run(void* p) {
+  og_chunk* c = (og_chunk*)p;
+  c->fn(c->ctx, c->b, c->e);
+  return NULL;
+}
+
+static void og_parallel_for(int64_t n, int32_t nthreads, og_body fn, void* ctx) {
+  if (n <= 0) return;
+  if (nthreads <= 1 || n == 1) { fn(ctx, 0, n); return; }
+  if (nthreads > n) nthreads = (int32_t)n;
+  if (nthreads > 256) nthreads = 256;
+  pthread_t th[256];
+  og_chunk ch[256];
+  int64_t per = n / nthreads, rem = n % nthreads, at = 0;
+  for (int32_t t = 0; t < nthreads; ++t) {
+    int64_t len = per + (t < rem ? 1 : 0);
+    ch[t].fn = fn; ch[t].ctx = ctx; ch[t].b = at; ch[t].e = at + len; at += len;
+  }
+  for (int32_t t = 1; t < nthreads; ++t) pthread_create(&th[t], NULL, og_chunk_run, &ch[t]);
+  og_chunk_run(&ch[0]);
+  for (int32_t t = 1; t < nthreads; ++t) pthread_join(th[t], NULL);
+}
+
+/* ------------------------------------------------------------------------ */
+/* RNG: src/rng.rs                                                           */
+/* ------------------------------------------------------------------------ */
+#define OG_GOLDEN 0x9E3779B97F4A7C15ull
+
+void og_rng_seed(og_rng* r, uint64_t seed) { r->state = seed ^ OG_GOLDEN; } /* rng.rs:16-18 */
+
+uint64_t og_rng_next_u64(og_rng* r) { /* rng.rs:21-27 */
+  r->state += OG_GOLDEN;
+  uint64_t z = r->state;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+float og_rng_uniform(og_rng* r) { /* rng.rs:30-32: 24 random bits / 2^24 (exact in f32) */
+  return (float)(og_rng_next_u64(r) >> 40) / 16777216.0f;
+}
+
+float og_rng_uniform_range(og_rng* r, float lo, float hi) { /* rng.rs:35-37 */
+  float u = og_rng_uniform(r);
+  float span = hi - lo;
+  float t = span * u;
+  return lo + t;
+}
+
+float og_rng_normal(og_rng* r) { /* rng.rs:40-44: Box-Muller, cosine branch only */
+  float u1 = fmaxf(og_rng_uniform(r), 1e-7f);
+  float u2 = og_rng_uniform(r);
+  const float two_pi = 2.0f * 3.14159265358979323846f; /* 2.0 * f32::consts::PI */
+  float a = sqrtf(-2.0f * logf(u1));
+  float b = cosf(two_pi * u2);
+  return a * b;
+}
+
+void og_fill_uniform_range(og_rng* r, float* out, int64_t n, float lo, float hi) {
+  for (int64_t i = 0; i < n; ++i) out[i] = og_rng_uniform_range(r, lo, hi);
+}
+void og_fill_normal(og_rng* r, float* out, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) out[i] = og_rng_normal(r);
+}
+void og_fill_normal_scaled(og_rng* r, float* out, int64_t n, float std) {
+  /* init::normal = randn(shape) then detach_scaled(std): v * s (nn/init.rs:18-20, 30-32) */
+  for (int64_t i = 0; i < n; ++i) { float v = og_rng_normal(r); out[i] = v * std; }
+}
+void og_fill_below(og_rng* r, int64_t* out, int64_t n, uint64_t bound) {
+  for (int64_t i = 0; i < n; ++i) out[i] = (int64_t)(og_rng_next_u64(r) % bound);
+}
+float og_kaiming_bound(int64_t fan_in) { /* init.rs:7 */
+  float f = (float)(fan_in > 1 ? fan_in : 1);
+  return sqrtf(6.0f / f);
+}
+float og_bias_bound(int64_t fan_in) { /* init.rs:24 */
+  float f = (float)(fan_in > 1 ? fan_in : 1);
+  return 1.0f / sqrtf(f);
+}
+
+/* ------------------------------------------------------------------------ */
+/* activations: inference/mod.rs:38-53 -> device/backend.rs:61-78            */
+/* ------------------------------------------------------------------------ */
+float og_act_apply(int32_t act, float param, float x) {
+  switch (act) {
+    case OG_ACT_NONE: return x;
+    case OG_ACT_RELU: return fmaxf(x, 0.0f);               /* x.max(0.0): NaN -> 0 */
+    case OG_ACT_SIGMOID: { float e = expf(-x); float d = 1.0f + e; return 1.0f / d; }
+    case OG_ACT_TANH: return tanhf(x);
+    case OG_ACT_GELU: {
+      /* 0.5 * x * (1.0 + (GELU_C * (x + 0.044715 * x * x * x)).tanh()), left to right */
+      const float gelu_c = 0.7978846f;
+      float c = 0.044715f * x; c = c * x; c = c * x;
+      float inner = x + c;
+      float t = tanhf(gelu_c * inner);
+      float h = 0.5f * x;
+      float s = 1.0f + t;
+      return h * s;
+    }
+    case OG_ACT_LEAKY_RELU: return x > 0.0f ? x : param * x;
+    default: return x;
+  }
+}
+
+/* ------------------------------------------------------------------------ */
+/* symmetric per-tensor quantization: inference/quantize.rs:18-35            */
+/* ------------------------------------------------------------------------ */
+float og_quant_scale(const float* v, int64_t n) {
+  float m = 0.0f;
+  for (int64_t i = 0; i < n; ++i) m = fmaxf(m, fabsf(v[i])); /* fold(0, max(|v|)): NaN ignored */
+  return m < 1e-12f ? 1.0f : m / 127.0f;
+}
+
+static inline int8_t og_q1(float v, float inv) {
+  float t = roundf(v * inv);                 /* round half away from zero */
+  if (isnan(t)) return 0;                    /* `as i8` maps NaN to 0 */
+  if (t < -127.0f) t = -127.0f;
+  if (t > 127.0f) t = 127.0f;
+  return (int8_t)t;
+}
+
+float og_quantize_into(const float* v, int64_t n, int8_t* out) {
+  float scale = og_quant_scale(v, n);
+  float inv = 1.0f / scale;
+  for (int64_t i = 0; i < n; ++i) out[i] = og_q1(v[i], inv);
+  return scale;
+}
+
+/* dot_i8: quantize.rs:68-88 (integer-exact; the unroll order cannot change the sum) */
+static inline int32_t og_dot_i8(const int8_t* a, const int8_t* b, int64_t len) {
+  int32_t a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+  int64_t i = 0;
+  for (; i + 4 <= len; i += 4) {
+    a0 += (int32_t)a[i] * b[i];
+    a1 += (int32_t)a[i + 1] * b[i + 1];
+    a2 += (int32_t)a[i + 2] * b[i + 2];
+    a3 += (int32_t)a[i + 3] * b[i + 3];
+  }
+  int32_t t = (a0 + a1) + (a2 + a3);
+  for (; i < len; ++i) t += (int32_t)a[i] * b[i];
+  return t;
+}
+
+/* int8_gemm_fused body for rows [b,e): quantize.rs:93-144 */
+typedef struct {
+  const int8_t* a; const int8_t* w; const float* bias; float cs;
+  int64_t k, n; int32_t act; float param; float* out; int32_t* acc;
+  int64_t row0;  /* row offset of out/acc relative to a */
+} og_gemm_ctx;
+
+static void og_gemm_rows(void* p, int64_t b, int64_t e) {
+  og_gemm_ctx* c = (og_gemm_ctx*)p;
+  for (int64_t r = b; r < e; ++r) {
+    const int8_t* arow = c->a + r * c->k;
+    float* orow = c->out + (r - c->row0) * c->n;
+    for (int64_t j = 0; j < c->n; ++j) {
+      int32_t acc = og_dot_i8(arow, c->w + j * c->k, c->k);
+      if (c->acc) c->acc[(r - c->row0) * c->n + j] = acc;
+      float v = (float)acc * c->cs;       /* (acc as f32) * combined_scale */
+      v = v + c->bias[j];                 /* + bias[c] */
+      orow[j] = og_act_apply(c->act, c->param, v);
+    }
+  }
+}
+
+/* ------------------------------------------------------------------------ */
+/* kernels.rs / shape.rs helpers                                             */
+/* ------------------------------------------------------------------------ */
+int64_t og_out_size(int64_t input, int64_t k, int64_t stride, int64_t pad) { /* kernels.rs:10-15 */
+  int64_t padded = input + 2 * pad;
+  if (k <= 0 || stride <= 0 || padded < k) return -1;
+  return (padded - k) / stride + 1;
+}
+
+void og_im2col(const float* x, int32_t c, int32_t h, int32_t w, int32_t k, int32_t stride,
+               int32_t pad, int32_t oh, int32_t ow, float* cols) { /* kernels.rs:28-96 */
+  int64_t l = (int64_t)oh * ow;
+  if (pad > 0) memset(cols, 0, sizeof(float) * (size_t)(c * k * k) * (size_t)l);
+  if (stride == 1) {
+    for (int32_t ch = 0; ch < c; ++ch) {
+      int64_t ch_off = (int64_t)ch * h * w;
+      for (int32_t ki = 0; ki < k; ++ki) {
+        int32_t dy = ki - pad;
+        int32_t oy_start = -dy > 0 ? -dy : 0;
+        int32_t oy_end = (h - dy) < oh ? (h - dy) : oh; if (oy_end < 0) oy_end = 0;
+        for (int32_t kj = 0; kj < k; ++kj) {
+          int32_t dx = kj - pad;
+          int32_t ox_start = -dx > 0 ? -dx : 0;
+          int32_t ox_end = (w - dx) < ow ? (w - dx) : ow; if (ox_end < 0) ox_end = 0;
+          if (ox_start >= ox_end) continue;
+          int32_t ix_start = ox_start + dx;
+          int32_t len = ox_end - ox_start;
+          int64_t base = ((int64_t)(ch * k + ki) * k + kj) * l;
+          for (int32_t oy = oy_start; oy < oy_end; ++oy) {
+            int32_t iy = oy + dy;
+            memcpy(cols + base + (int64_t)oy * ow + ox_start, x + ch_off + (int64_t)iy * w + ix_start,
+                   sizeof(float) * (size_t)len);
+          }
+        }
+      }
+    }
+  } else {
+    for (int32_t ch = 0; ch < c; ++ch)
+      for (int32_t ki = 0; ki < k; ++ki)
+        for (int32_t kj = 0; kj < k; ++kj) {
+          int64_t base = ((int64_t)(ch * k + ki) * k + kj) * l;
+          for (int32_t oy = 0; oy < oh; ++oy) {
+            int32_t iy = oy * stride + ki - pad;
+            if (iy < 0 || iy >= h) continue;
+            for (int32_t ox = 0; ox < ow; ++ox) {
+              int32_t ix = ox * stride + kj - pad;
+              if (ix < 0 || ix >= w) continue;
+              cols[base + (int64_t)oy * ow + ox] = x[((int64_t)ch * h + iy) * w + ix];
+            }
+          }
+        }
+  }
+}
+
+void og_transpose2d(const float* x, int64_t rows, int64_t cols, float* out) { /* shape.rs:105-123 */
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t c = 0; c < cols; ++c) out[c * rows + r] = x[r * cols + c];
+}
+
+/* max_pool2d: kernels.rs:165-213 (pad 0; strict > keeps the first of ties; NaN propagates) */
+typedef struct { const float* x; float* y; int32_t h, w, k, s, oh, ow; } og_pool_ctx;
+static void og_pool_planes(void* p, int64_t b, int64_t e) {
+  og_pool_ctx* c = (og_pool_ctx*)p;
+  for (int64_t plane = b; plane < e; ++plane) {
+    const float* xp = c->x + plane * (int64_t)c->h * c->w;
+    float* yp = c->y + plane * (int64_t)c->oh * c->ow;
+    for (int32_t oy = 0; oy < c->oh; ++oy)
+      for (int32_t ox = 0; ox < c->ow; ++ox) {
+        float best = -INFINITY;
+        for (int32_t ki = 0; ki < c->k; ++ki)
+          for (int32_t kj = 0; kj < c->k; ++kj) {
+            float v = xp[(int64_t)(oy * c->s + ki) * c->w + ox * c->s + kj];
+            if (v > best || isnan(v)) best = v;
+          }
+        yp[oy * c->ow + ox] = best;
+      }
+  }
+}
+void og_maxpool2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t k,
+                  int32_t stride, float* y, int32_t nthreads) {
+  og_pool_ctx ctx = { x, y, h, w, k, stride, (int32_t)og_out_size(h, k, stride, 0),
+                      (int32_t)og_out_size(w, k, stride, 0) };
+  int64_t planes = n * c, total = planes * ctx.oh * ctx.ow;
+  if (total <= 0) return;
+  og_parallel_for(planes, total >= 8192 ? nthreads : 1, og_pool_planes, &ctx);
+}
+
+void og_activation(const float* x, int64_t n, int32_t act, float param, float* y) {
+  for (int64_t i = 0; i < n; ++i) y[i] = og_act_apply(act, param, x[i]);
+}
+
+void og_softmax(const float* x, int64_t outer, int64_t last, float* y) { /* ops.rs:1058-1076 */
+  for (int64_t o = 0; o < outer; ++o) {
+    const float* xr = x + o * last; float* yr = y + o * last;
+    float mx = -INFINITY;
+    for (int64_t j = 0; j < last; ++j) mx = fmaxf(mx, xr[j]);
+    float s = 0.0f;
+    for (int64_t j = 0; j < last; ++j) { float e = expf(xr[j] - mx); yr[j] = e; s += e; }
+    for (int64_t j = 0; j < last; ++j) yr[j] = yr[j] / s;
+  }
+}
+
+/* ------------------------------------------------------------------------ */
+/* compile: inference/mod.rs:225-257 (fold) + npu.rs:188-276 (fuse+quantize) */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+  int32_t kind, in_f, out_f, in_c, out_c, k, stride, pad, act; float param;
+  float* w; int64_t w_len; float* b; int64_t b_len;
+} og_flayer;
+
+static og_flayer* og_fold(const og_layer* L, int32_t n, int32_t* out_n) {
+  og_flayer* out = (og_flayer*)calloc((size_t)(n > 0 ? n : 1), sizeof(og_flayer));
+  int32_t m = 0;
+  for (int32_t i = 0; i < n; ++i) {
+    const og_layer* l = &L[i];
+    if (l->kind == OG_LAYER_CHANNEL_AFFINE && m > 0) {
+      og_flayer* p = &out[m - 1];
+      int64_t c = l->weight_len;
+      if (p->kind == OG_LAYER_LINEAR && p->out_f == c) {
+        for (int64_t r = 0; r < p->in_f; ++r)
+          for (int64_t j = 0; j < p->out_f; ++j) p->w[r * p->out_f + j] *= l->weight[j];
+        for (int64_t j = 0; j < p->out_f; ++j) { float t = p->b[j] * l->weight[j]; p->b[j] = t + l->bias[j]; }
+        continue;
+      }
+      if (p->kind == OG_LAYER_CONV2D && p->out_c == c) {
+        int64_t plane = (int64_t)p->in_c * p->k * p->k;
+        for (int64_t o = 0; o < p->out_c; ++o) {
+          for (int64_t j = 0; j < plane; ++j) p->w[o * plane + j] *= l->weight[o];
+          float t = p->b[o] * l->weight[o]; p->b[o] = t + l->bias[o];
+        }
+        continue;
+      }
+    }
+    og_flayer* f = &out[m++];
+    f->kind = l->kind; f->in_f = l->in_features; f->out_f = l->out_features;
+    f->in_c = l->in_channels; f->out_c = l->out_channels; f->k = l->kernel;
+    f->stride = l->stride; f->pad = l->padding; f->act = l->act; f->param = l->act_param;
+    f->w_len = l->weight_len; f->b_len = l->bias_len;
+    if (l->weight_len) { f->w = (float*)malloc(sizeof(float) * (size_t)l->weight_len); memcpy(f->w, l->weight, sizeof(float) * (size_t)l->weight_len); }
+    if (l->bias_len) { f->b = (float*)malloc(sizeof(float) * (size_t)l->bias_len); memcpy(f->b, l->bias, sizeof(float) * (size_t)l->bias_len); }
+  }
+  *out_n = m;
+  return out;
+}
+
+void og_fold_batch_norm_count(const og_layer* layers, int32_t n, int32_t* out_count) {
+  int32_t m = 0;
+  og_flayer* f = og_fold(layers, n, &m);
+  for (int32_t i = 0; i < m; ++i) { free(f[i].w); free(f[i].b); }
+  free(f);
+  *out_count = m;
+}
+
+og_program* og_compile(const og_layer* layers, int32_t n_layers, int32_t precision) {
+  int32_t m = 0;
+  og_flayer* f = og_fold(layers, n_layers, &m);
+  og_program* p = (og_program*)calloc(1, sizeof(og_program));
+  p->precision = precision; p->original_layers = n_layers;
+  p->ops = (og_op*)calloc((size_t)(m > 0 ? m : 1), sizeof(og_op));
+  int32_t nops = 0;
+  for (int32_t i = 0; i < m; ++i) {
+    og_flayer* l = &f[i];
+    int32_t next_act = (i + 1 < m && f[i + 1].kind == OG_LAYER_ACTIVATION);
+    og_op* op = &p->ops[nops];
+    memset(op, 0, sizeof(*op));
+    if (l->kind == OG_LAYER_LINEAR || l->kind == OG_LAYER_CONV2D) {
+      op->kind = l->kind;
+      op->act = next_act ? f[i + 1].act : OG_ACT_NONE;
+      op->act_param = next_act ? f[i + 1].param : 0.0f;
+      int64_t wl = l->w_len;
+      op->wq = (int8_t*)malloc((size_t)(wl > 0 ? wl : 1)); op->wq_len = wl;
+      if (l->kind == OG_LAYER_LINEAR) {
+        op->in_features = l->in_f; op->out_features = l->out_f;
+        float* wt = (float*)malloc(sizeof(float) * (size_t)(wl > 0 ? wl : 1));
+        og_transpose2d(l->w, l->in_f, l->out_f, wt);       /* npu.rs:208: [in,out] -> [out,in] */
+        op->w_scale = og_quantize_into(wt, wl, op->wq);    /* npu.rs:209: per-tensor */
+        free(wt);
+      } else {
+        op->in_channels = l->in_c; op->out_channels = l->out_c; op->kernel = l->k;
+        op->stride = l->stride; op->padding = l->pad;
+        op->w_scale = og_quantize_into(l->w, wl, op->wq);  /* npu.rs:231: [O, C*k*k] per-tensor */
+      }
+      op->bias = (float*)malloc(sizeof(float) * (size_t)(l->b_len > 0 ? l->b_len : 1));
+      memcpy(op->bias, l->b, sizeof(float) * (size_t)l->b_len); op->bias_len = l->b_len;
+      p->fp32_bytes += (l->w_len + l->b_len) * 4;
+      p->npu_bytes += precision == OG_PREC_INT8 ? (wl + 4) + l->b_len * 4 : l->w_len * 2 + l->b_len * 2;
+      if (next_act) ++i;
+    } else if (l->kind == OG_LAYER_CHANNEL_AFFINE) {
+      /* standalone affine -> diagonal FusedLinear (npu.rs:254-270); no byte accounting */
+      int64_t c = l->w_len;
+      float* w = (float*)calloc((size_t)(c * c > 0 ? c * c : 1), sizeof(float));
+      for (int64_t j = 0; j < c; ++j) w[j * c + j] = l->w[j];
+      op->kind = OG_LAYER_LINEAR; op->in_features = (int32_t)c; op->out_features = (int32_t)c;
+      op->wq = (int8_t*)malloc((size_t)(c * c > 0 ? c * c : 1)); op->wq_len = c * c;
+      op->w_scale = og_quantize_into(w, c * c, op->wq);
+      free(w);
+      op->bias = (float*)malloc(sizeof(float) * (size_t)(c > 0 ? c : 1));
+      memcpy(op->bias, l->b, sizeof(float) * (size_t)c); op->bias_len = c;
+      op->act = OG_ACT_NONE;
+    } else {
+      op->kind = l->kind; op->kernel = l->k; op->stride = l->stride;
+      op->act = l->act; op->act_param = l->param;
+    }
+    ++nops;
+  }
+  for (int32_t i = 0; i < m; ++i) { free(f[i].w); free(f[i].b); }
+  free(f);
+  p->n_ops = nops;
+  return p;
+}
+
+void og_program_free(og_program* p) {
+  if (!p) return;
+  for (int32_t i = 0; i < p->n_ops; ++i) { free(p->ops[i].wq); free(p->ops[i].bias); }
+  free(p->ops); free(p);
+}
+
+/* Rust `{}` Display of an f32 (shortest round-trip repr, no exponent) for LeakyReLU(s). */
+static void og_fmt_f32(float v, char* buf, int cap) {
+  for (int prec = 1; prec <= 60; ++prec) {
+    snprintf(buf, (size_t)cap, "%.*f", prec, (double)v);
+    if (strtof(buf, NULL) == v) break;
+  }
+  /* Rust prints integral floats without a fraction ("1"), others in shortest form */
+  char* dot = strchr(buf, '.');
+  if (dot) {
+    char* end = buf + strlen(buf) - 1;
+    while (end > dot && *end == '0') *end-- = 0;
+    if (end == dot) *end = 0;
+  }
+}
+
+static const char* og_act_name(int32_t act, float param, char* tmp, int cap) {
+  switch (act) {
+    case OG_ACT_NONE: return "none";
+    case OG_ACT_RELU: return "ReLU";
+    case OG_ACT_SIGMOID: return "Sigmoid";
+    case OG_ACT_TANH: return "Tanh";
+    case OG_ACT_GELU: return "GELU";
+    case OG_ACT_LEAKY_RELU: { char f[64]; og_fmt_f32(param, f, 64); snprintf(tmp, (size_t)cap, "LeakyReLU(%s)", f); return tmp; }
+    default: return "?";
+  }
+}
+
+int32_t og_op_label(const og_op* op, char* buf, int32_t cap) { /* npu.rs:83-104 */
+  char t[96];
+  const char* an = og_act_name(op->act, op->act_param, t, 96);
+  switch (op->kind) {
+    case OG_LAYER_LINEAR:
+      if (op->act == OG_ACT_NONE) return snprintf(buf, (size_t)cap, "NPU::Gemm(%d->%d)", op->in_features, op->out_features);
+      return snprintf(buf, (size_t)cap, "NPU::FusedGemmAct(%d->%d, %s)", op->in_features, op->out_features, an);
+    case OG_LAYER_CONV2D:
+      if (op->act == OG_ACT_NONE) return snprintf(buf, (size_t)cap, "NPU::Conv2d(%d->%d, k=%d)", op->in_channels, op->out_channels, op->kernel);
+      return snprintf(buf, (size_t)cap, "NPU::FusedConv2dAct(%d->%d, k=%d, %s)", op->in_channels, op->out_channels, op->kernel, an);
+    case OG_LAYER_MAXPOOL2D: return snprintf(buf, (size_t)cap, "NPU::MaxPool2d(k=%d)", op->kernel);
+    case OG_LAYER_FLATTEN: return snprintf(buf, (size_t)cap, "NPU::Flatten");
+    case OG_LAYER_ACTIVATION: return snprintf(buf, (size_t)cap, "NPU::Act(%s)", an);
+    case OG_LAYER_SOFTMAX: return snprintf(buf, (size_t)cap, "NPU::Softmax");
+    default: return snprintf(buf, (size_t)cap, "NPU::?");
+  }
+}
+
+int32_t og_program_summary(const og_program* p, int32_t raw_count, char* buf, int32_t cap) { /* npu.rs:280-293 */
+  float ratio = p->npu_bytes == 0 ? 1.0f : (float)p->fp32_bytes / (float)p->npu_bytes;
+  int32_t at = snprintf(buf, (size_t)cap,
+      "InferenceSession [provider = NPU (%s), layers: %d -> %d fused ops, weights: %lld B -> %lld B (%.2fx compression)]\n  Pipeline: ",
+      p->precision == OG_PREC_INT8 ? "INT8" : "FP16", raw_count, p->n_ops,
+      (long long)p->fp32_bytes, (long long)p->npu_bytes, (double)ratio);
+  for (int32_t i = 0; i < p->n_ops; ++i) {
+    if (i && at < cap) at += snprintf(buf + at, (size_t)(cap - at), " -> ");
+    if (at < cap) at += og_op_label(&p->ops[i], buf + at, cap - at);
+  }
+  return at;
+}
+
+/* ------------------------------------------------------------------------ */
+/* per-op execution                                                          */
+/* ------------------------------------------------------------------------ */
+void og_op_linear(const og_op* op, const float* x, int64_t rows, float* y,
+                  float* a_scale, int8_t* aq, int32_t* acc, int32_t nthreads) {
+  int64_t k = op->in_features, n = op->out_features;
+  int8_t* q = aq ? aq : (int8_t*)malloc((size_t)(rows * k > 0 ? rows * k : 1));
+  float sa = og_quantize_into(x, rows * k, q);            /* QuantTensor::from_f32 (serial) */
+  if (a_scale) *a_scale = sa;
+  og_gemm_ctx c = { q, op->wq, op->bias, sa * op->w_scale, k, n, op->act, op->act_param, y, acc, 0 };
+  int32_t par = rows * k * n >= 32 * 1024;                /* quantize.rs:104 */
+  og_parallel_for(rows, par ? nthreads : 1, og_gemm_rows, &c);
+  if (!aq) free(q);
+}
+
+void og_op_linear_with_amax(const og_op* op, const float* x, int64_t rows, float amax, float* y,
+                            int32_t nthreads) {
+  /* FusedLinear with the activation absmax supplied by the caller (a batch shard
+   * quantizing with the max over every shard: the multi-device restatement). */
+  int64_t k = op->in_features, n = op->out_features;
+  float sa = amax < 1e-12f ? 1.0f : amax / 127.0f;
+  float inv = 1.0f / sa;
+  int8_t* q = (int8_t*)malloc((size_t)(rows * k > 0 ? rows * k : 1));
+  for (int64_t i = 0; i < rows * k; ++i) q[i] = og_q1(x[i], inv);
+  og_gemm_ctx c = { q, op->wq, op->bias, sa * op->w_scale, k, n, op->act, op->act_param, y, NULL, 0 };
+  og_parallel_for(rows, rows * k * n >= 32 * 1024 ? nthreads : 1, og_gemm_rows, &c);
+  free(q);
+}
+
+void og_op_linear_rows(const og_op* op, const float* x, int64_t rows, int64_t r0, int64_t r1,
+                       float* y, float* a_scale, int32_t* acc, int32_t nthreads) {
+  int64_t k = op->in_features, n = op->out_features;
+  float sa = og_quant_scale(x, rows * k);
+  float inv = 1.0f / sa;
+  int64_t sub = r1 - r0;
+  int8_t* q = (int8_t*)malloc((size_t)(sub * k > 0 ? sub * k : 1));
+  for (int64_t i = 0; i < sub * k; ++i) q[i] = og_q1(x[r0 * k + i], inv);
+  if (a_scale) *a_scale = sa;
+  og_gemm_ctx c = { q, op->wq, op->bias, sa * op->w_scale, k, n, op->act, op->act_param, y, acc, 0 };
+  og_parallel_for(sub, nthreads, og_gemm_rows, &c);
+  free(q);
+}
+
+typedef struct {
+  const og_op* op; const float* x; float* y; float* a_scales; int8_t* aq; int32_t* acc;
+  int32_t c, h, w, oh, ow;
+} og_conv_ctx;
+
+static void og_conv_images(void* p, int64_t b, int64_t e) { /* npu.rs:331-359 per image */
+  og_conv_ctx* c = (og_conv_ctx*)p;
+  const og_op* op = c->op;
+  int64_t l = (int64_t)c->oh * c->ow, ckk = (int64_t)c->c * op->kernel * op->kernel;
+  int64_t O = op->out_channels;
+  float* cols = (float*)malloc(sizeof(float) * (size_t)(ckk * l > 0 ? ckk * l : 1));
+  float* cols_t = (float*)malloc(sizeof(float) * (size_t)(ckk * l > 0 ? ckk * l : 1));
+  int8_t* q = (int8_t*)malloc((size_t)(ckk * l > 0 ? ckk * l : 1));
+  float* ylo = (float*)malloc(sizeof(float) * (size_t)(l * O > 0 ? l * O : 1));
+  int32_t* alo = c->acc ? (int32_t*)malloc(sizeof(int32_t) * (size_t)(l * O > 0 ? l * O : 1)) : NULL;
+  int64_t img_stride = (int64_t)c->c * c->h * c->w;
+  for (int64_t im = b; im < e; ++im) {
+    const float* img = c->x + im * img_stride;
+    og_im2col(img, c->c, c->h, c->w, op->kernel, op->stride, op->padding, c->oh, c->ow, cols);
+    og_transpose2d(cols, ckk, l, cols_t);
+    float sa = og_quantize_into(cols_t, ckk * l, q);     /* per-image scale */
+    if (c->a_scales) c->a_scales[im] = sa;
+    if (c->aq) { float inv = 1.0f / sa; for (int64_t i = 0; i < img_stride; ++i) c->aq[im * img_stride + i] = og_q1(img[i], inv); }
+    og_gemm_ctx g = { q, op->wq, op->bias, sa * op->w_scale, ckk, O, op->act, op->act_param, ylo, alo, 0 };
+    og_gemm_rows(&g, 0, l);                              /* int8_gemm_fused_serial */
+    og_transpose2d(ylo, l, O, c->y + im * O * l);        /* [L,O] -> [O,L] */
+    if (alo)
+      for (int64_t r = 0; r < l; ++r)
+        for (int64_t o = 0; o < O; ++o) c->acc[im * O * l + o * l + r] = alo[r * O + o];
+  }
+  free(cols); free(cols_t); free(q); free(ylo); free(alo);
+}
+
+void og_op_conv2d(const og_op* op, const float* x, int64_t n, int32_t h, int32_t w, float* y,
+                  float* a_scales, int8_t* aq, int32_t* acc, int32_t nthreads) {
+  og_conv_ctx c = { op, x, y, a_scales, aq, acc, op->in_channels, h, w,
+                    (int32_t)og_out_size(h, op->kernel, op->stride, op->padding),
+                    (int32_t)og_out_size(w, op->kernel, op->stride, op->padding) };
+  int64_t out_stride = (int64_t)op->out_channels * c.oh * c.ow;
+  og_parallel_for(n, (n >= 2 && out_stride > 0) ? nthreads : 1, og_conv_images, &c);
+}
+
+static int64_t og_now_ns(void) {
+  struct timespec ts; clock_gettime(CLOCK_MONOTONIC, &ts);
+  return (int64_t)ts.tv_sec * 1000000000ll + ts.tv_nsec;
+}
+
+int32_t og_execute(const og_program* p, const float* x, const int64_t* shape, int32_t ndim,
+                   float* y, int64_t y_cap, int64_t* y_shape, int32_t* y_ndim,
+                   int32_t nthreads, int64_t* op_ns, int64_t* op_macs) {
+  int64_t sh[8]; int32_t nd = ndim;
+  if (ndim < 1 || ndim > 8) return -1;
+  if (p->precision != OG_PREC_INT8) return -5;  /* only the Int8 arm is restated */
+  int64_t len = 1;
+  for (int32_t i = 0; i < ndim; ++i) { sh[i] = shape[i]; len *= shape[i]; }
+  float* data = (float*)malloc(sizeof(float) * (size_t)(len > 0 ? len : 1));
+  memcpy(data, x, sizeof(float) * (size_t)len);
+  for (int32_t oi = 0; oi < p->n_ops; ++oi) {
+    const og_op* op = &p->ops[oi];
+    int64_t t0 = og_now_ns(), macs = 0;
+    float* out = NULL;
+    switch (op->kind) {
+      case OG_LAYER_LINEAR: {
+        int64_t rows = len / op->in_features;
+        macs = rows * op->in_features * op->out_features;
+        out = (float*)malloc(sizeof(float) * (size_t)(rows * op->out_features > 0 ? rows * op->out_features : 1));
+        og_op_linear(op, data, rows, out, NULL, NULL, NULL, nthreads);
+        sh[nd - 1] = op->out_features; len = rows * op->out_features;
+        break;
+      }
+      case OG_LAYER_CONV2D: {
+        if (nd != 4 || sh[1] != op->in_channels) { free(data); return -2; }
+        int64_t n = sh[0], h = sh[2], w = sh[3];
+        int64_t oh = og_out_size(h, op->kernel, op->stride, op->padding);
+        int64_t ow = og_out_size(w, op->kernel, op->stride, op->padding);
+        if (oh <= 0 || ow <= 0) { free(data); return -2; }
+        macs = n * op->out_channels * (int64_t)op->in_channels * op->kernel * op->kernel * oh * ow;
+        out = (float*)malloc(sizeof(float) * (size_t)(n * op->out_channels * oh * ow > 0 ? n * op->out_channels * oh * ow : 1));
+        og_op_conv2d(op, data, n, (int32_t)h, (int32_t)w, out, NULL, NULL, NULL, nthreads);
+        sh[1] = op->out_channels; sh[2] = oh; sh[3] = ow; len = n * op->out_channels * oh * ow;
+        break;
+      }
+      case OG_LAYER_MAXPOOL2D: {
+        if (nd != 4) { free(data); return -2; }
+        int64_t oh = og_out_size(sh[2], op->kernel, op->stride, 0), ow = og_out_size(sh[3], op->kernel, op->stride, 0);
+        if (oh <= 0 || ow <= 0) { free(data); return -2; }
+        out = (float*)malloc(sizeof(float) * (size_t)(sh[0] * sh[1] * oh * ow > 0 ? sh[0] * sh[1] * oh * ow : 1));
+        og_maxpool2d(data, sh[0], (int32_t)sh[1], (int32_t)sh[2], (int32_t)sh[3], op->kernel, op->stride, out, nthreads);
+        sh[2] = oh; sh[3] = ow; len = sh[0] * sh[1] * oh * ow;
+        break;
+      }
+      case OG_LAYER_FLATTEN: {
+        int64_t rest = 1;
+        for (int32_t i = 1; i < nd; ++i) rest *= sh[i];
+        sh[1] = rest; nd = 2;
+        break;
+      }
+      case OG_LAYER_ACTIVATION:
+        og_activation(data, len, op->act, op->act_param, data);
+        break;
+      case OG_LAYER_SOFTMAX: {
+        int64_t last = sh[nd - 1];
+        out = (float*)malloc(sizeof(float) * (size_t)(len > 0 ? len : 1));
+        og_softmax(data, last ? len / last : 0, last, out);
+        break;
+      }
+      default: free(data); return -3;
+    }
+    if (out) { free(data); data = out; }
+    if (op_ns) op_ns[oi] = og_now_ns() - t0;
+    if (op_macs) op_macs[oi] = macs;
+  }
+  if (len > y_cap) { free(data); return -4; }
+  memcpy(y, data, sizeof(float) * (size_t)len);
+  for (int32_t i = 0; i < nd; ++i) y_shape[i] = sh[i];
+  *y_ndim = nd;
+  free(data);
+  return 0;
+}

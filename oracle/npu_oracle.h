@@ -1,0 +1,118 @@
+/*
+ * npu_oracle.h -- TEST INFRASTRUCTURE ONLY.
+ *
+ * CPU restatement of the RustGears Npu(Int8) inference path, used as the parity
+ * checker for the CUDA execution provider and as the timed CPU baseline.  Nothing
+ * in the product library links or calls this code.
+ *
+ * Every function cites the reference file:line it restates (paths relative to
+ * the RustGears project root).  Parity status: the reference cannot be compiled
+ * in this image (no Rust toolchain), so this restatement is pinned by the
+ * reference's known answers (tests/integration.rs:128-164 structure,
+ * docs/USAGE.md:376-380 byte and MAC counts) and by self-generated golden
+ * vectors; see tests/golden/.
+ */
+#ifndef RG_NPU_ORACLE_H
+#define RG_NPU_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- SplitMix64 generator: src/rng.rs:10-58 ---------------------------- */
+typedef struct { uint64_t state; } og_rng;
+
+void og_rng_seed(og_rng* r, uint64_t seed);                 /* rng.rs:16-18, manual_seed 71-73 */
+uint64_t og_rng_next_u64(og_rng* r);                        /* rng.rs:21-27 */
+float og_rng_uniform(og_rng* r);                            /* rng.rs:30-32 */
+float og_rng_uniform_range(og_rng* r, float lo, float hi);  /* rng.rs:35-37 */
+float og_rng_normal(og_rng* r);                             /* rng.rs:40-44 */
+void og_fill_uniform_range(og_rng* r, float* out, int64_t n, float lo, float hi); /* tensor/mod.rs:128-131 */
+void og_fill_normal(og_rng* r, float* out, int64_t n);      /* tensor/mod.rs:116-119 */
+void og_fill_normal_scaled(og_rng* r, float* out, int64_t n, float std); /* nn/init.rs:18-20,30-32 */
+void og_fill_below(og_rng* r, int64_t* out, int64_t n, uint64_t bound);  /* rng.rs:47-49 */
+float og_kaiming_bound(int64_t fan_in);                     /* nn/init.rs:6-9 */
+float og_bias_bound(int64_t fan_in);                        /* nn/init.rs:23-26 */
+
+/* ---- IR: src/inference/mod.rs:24-100 ----------------------------------- */
+enum {
+  OG_LAYER_LINEAR = 1, OG_LAYER_CONV2D = 2, OG_LAYER_CHANNEL_AFFINE = 3,
+  OG_LAYER_MAXPOOL2D = 4, OG_LAYER_FLATTEN = 5, OG_LAYER_ACTIVATION = 6,
+  OG_LAYER_SOFTMAX = 7
+};
+enum { OG_ACT_NONE = 0, OG_ACT_RELU = 1, OG_ACT_SIGMOID = 2, OG_ACT_TANH = 3,
+       OG_ACT_GELU = 4, OG_ACT_LEAKY_RELU = 5 };
+enum { OG_PREC_INT8 = 0, OG_PREC_FP16 = 1 };
+
+typedef struct {
+  int32_t kind;
+  int32_t in_features, out_features;                 /* Linear */
+  int32_t in_channels, out_channels, kernel, stride, padding; /* Conv2d; MaxPool uses kernel/stride */
+  const float* weight; int64_t weight_len;           /* Linear [in,out]; Conv [O,C,k,k]; Affine: scale */
+  const float* bias; int64_t bias_len;               /* bias; Affine: shift */
+  int32_t act; float act_param;                      /* Activation */
+} og_layer;
+
+/* Compiled program: src/inference/npu.rs:43-79 (NpuOp), 179-185 (NpuProgram). */
+typedef struct {
+  int32_t kind;           /* OG_LAYER_LINEAR / CONV2D / MAXPOOL2D / FLATTEN / ACTIVATION / SOFTMAX */
+  int32_t in_features, out_features;
+  int32_t in_channels, out_channels, kernel, stride, padding;
+  int8_t* wq; int64_t wq_len; float w_scale;   /* Linear: [out,in]; Conv: [O, C*k*k] */
+  float* bias; int64_t bias_len;
+  int32_t act; float act_param;
+} og_op;
+
+typedef struct {
+  int32_t precision, original_layers, n_ops, _pad;
+  og_op* ops;
+  int64_t fp32_bytes, npu_bytes;
+} og_program;
+
+float og_act_apply(int32_t act, float param, float x);      /* mod.rs:38-53 + device/backend.rs:61-78 */
+float og_quant_scale(const float* v, int64_t n);            /* quantize.rs:19-20 */
+float og_quantize_into(const float* v, int64_t n, int8_t* out); /* quantize.rs:27-35 */
+
+og_program* og_compile(const og_layer* layers, int32_t n_layers, int32_t precision); /* npu.rs:188-276 */
+void og_program_free(og_program* p);
+/* NpuOp::label (npu.rs:83-104); returns bytes written (excluding NUL). */
+int32_t og_op_label(const og_op* op, char* buf, int32_t cap);
+/* NpuProgram::summary (npu.rs:280-293). */
+int32_t og_program_summary(const og_program* p, int32_t raw_count, char* buf, int32_t cap);
+
+/* ---- per-op execution (npu.rs:296-421) ---------------------------------- */
+/* FusedLinear Int8 arm (npu.rs:307-318).  aq [rows,in] and acc [rows,out] are optional dumps. */
+void og_op_linear(const og_op* op, const float* x, int64_t rows, float* y,
+                  float* a_scale, int8_t* aq, int32_t* acc, int32_t nthreads);
+/* Same with the activation absmax given by the caller (max over all batch shards). */
+void og_op_linear_with_amax(const og_op* op, const float* x, int64_t rows, float amax, float* y,
+                            int32_t nthreads);
+/* Same, restricted to rows [r0, r1) with the scale taken over all `rows` (row sampling for huge M). */
+void og_op_linear_rows(const og_op* op, const float* x, int64_t rows, int64_t r0, int64_t r1,
+                       float* y, float* a_scale, int32_t* acc, int32_t nthreads);
+/* FusedConv2d Int8 arm (npu.rs:319-383).  y [n,O,oh,ow].  a_scales [n].  aq [n,C,H,W] (every pixel
+ * quantized with its image's scale) and acc [n,O,oh*ow] are optional dumps. */
+void og_op_conv2d(const og_op* op, const float* x, int64_t n, int32_t h, int32_t w, float* y,
+                  float* a_scales, int8_t* aq, int32_t* acc, int32_t nthreads);
+void og_maxpool2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t k,
+                  int32_t stride, float* y, int32_t nthreads);          /* kernels.rs:165-213 */
+void og_activation(const float* x, int64_t n, int32_t act, float param, float* y); /* npu.rs:395-399 */
+void og_softmax(const float* x, int64_t outer, int64_t last, float* y); /* tensor/ops.rs:1058-1076 */
+int64_t og_out_size(int64_t input, int64_t k, int64_t stride, int64_t pad); /* kernels.rs:10-15 */
+void og_im2col(const float* x, int32_t c, int32_t h, int32_t w, int32_t k, int32_t stride,
+               int32_t pad, int32_t oh, int32_t ow, float* cols);       /* kernels.rs:28-96 */
+void og_transpose2d(const float* x, int64_t rows, int64_t cols, float* out); /* shape.rs:105-123 */
+void og_fold_batch_norm_count(const og_layer* layers, int32_t n, int32_t* out_count);
+
+/* Whole-program execute (npu.rs:296-421).  y_cap elements; out shape written to y_shape/y_ndim.
+ * op_ns / op_macs receive the per-op OpRecord durations (ns) and MACs (n_ops entries each). */
+int32_t og_execute(const og_program* p, const float* x, const int64_t* shape, int32_t ndim,
+                   float* y, int64_t y_cap, int64_t* y_shape, int32_t* y_ndim,
+                   int32_t nthreads, int64_t* op_ns, int64_t* op_macs);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,432 @@
+"""TEST INFRASTRUCTURE ONLY: ctypes bindings to the C restatement of the
+RustGears Npu(Int8) path (``oracle/npu_oracle.c``).
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
+``bench.py`` may import this module.  It is the parity checker and the timed
+CPU baseline; the product library never calls it.
+
+Layer specs are duck-typed: any object with the attributes of the reference's
+``LayerSpec`` (``inference/mod.rs:70-100``) -- ``kind`` (RTIM tag 1..7),
+``in_features``/``out_features``, ``in_channels``/``out_channels``/``kernel``/
+``stride``/``padding``, ``weight``/``bias`` (f32 arrays; ``scale``/``shift``
+for ChannelAffine), ``act``/``act_param`` -- or a dict with those keys.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboracle.so")
+
+LINEAR, CONV2D, CHANNEL_AFFINE, MAXPOOL2D, FLATTEN, ACTIVATION, SOFTMAX = 1, 2, 3, 4, 5, 6, 7
+ACT_NONE, ACT_RELU, ACT_SIGMOID, ACT_TANH, ACT_GELU, ACT_LEAKY_RELU = 0, 1, 2, 3, 4, 5
+
+
+class _Rng(C.Structure):
+    _fields_ = [("state", C.c_uint64)]
+
+
+class _Layer(C.Structure):
+    _fields_ = [
+        ("kind", C.c_int32), ("in_features", C.c_int32), ("out_features", C.c_int32),
+        ("in_channels", C.c_int32), ("out_channels", C.c_int32), ("kernel", C.c_int32),
+        ("stride", C.c_int32), ("padding", C.c_int32),
+        ("weight", C.POINTER(C.c_float)), ("weight_len", C.c_int64),
+        ("bias", C.POINTER(C.c_float)), ("bias_len", C.c_int64),
+        ("act", C.c_int32), ("act_param", C.c_float),
+    ]
+
+
+class _Op(C.Structure):
+    _fields_ = [
+        ("kind", C.c_int32), ("in_features", C.c_int32), ("out_features", C.c_int32),
+        ("in_channels", C.c_int32), ("out_channels", C.c_int32), ("kernel", C.c_int32),
+        ("stride", C.c_int32), ("padding", C.c_int32),
+        ("wq", C.POINTER(C.c_int8)), ("wq_len", C.c_int64), ("w_scale", C.c_float),
+        ("bias", C.POINTER(C.c_float)), ("bias_len", C.c_int64),
+        ("act", C.c_int32), ("act_param", C.c_float),
+    ]
+
+
+class _Program(C.Structure):
+    _fields_ = [
+        ("precision", C.c_int32), ("original_layers", C.c_int32), ("n_ops", C.c_int32),
+        ("_pad", C.c_int32), ("ops", C.POINTER(_Op)),
+        ("fp32_bytes", C.c_int64), ("npu_bytes", C.c_int64),
+    ]
+
+
+def build():
+    """Compile liboracle.so with oracle/Makefile (gcc)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = C.CDLL(_LIB_PATH)
+        f32p, i8p, i32p, i64p = (C.POINTER(C.c_float), C.POINTER(C.c_int8),
+                                 C.POINTER(C.c_int32), C.POINTER(C.c_int64))
+        L.og_rng_seed.argtypes = [C.POINTER(_Rng), C.c_uint64]
+        L.og_rng_next_u64.argtypes = [C.POINTER(_Rng)]
+        L.og_rng_next_u64.restype = C.c_uint64
+        L.og_rng_uniform.argtypes = [C.POINTER(_Rng)]
+        L.og_rng_uniform.restype = C.c_float
+        L.og_rng_normal.argtypes = [C.POINTER(_Rng)]
+        L.og_rng_normal.restype = C.c_float
+        L.og_fill_uniform_range.argtypes = [C.POINTER(_Rng), f32p, C.c_int64, C.c_float, C.c_float]
+        L.og_fill_normal.argtypes = [C.POINTER(_Rng), f32p, C.c_int64]
+        L.og_fill_normal_scaled.argtypes = [C.POINTER(_Rng), f32p, C.c_int64, C.c_float]
+        L.og_fill_below.argtypes = [C.POINTER(_Rng), i64p, C.c_int64, C.c_uint64]
+        L.og_kaiming_bound.argtypes = [C.c_int64]
+        L.og_kaiming_bound.restype = C.c_float
+        L.og_bias_bound.argtypes = [C.c_int64]
+        L.og_bias_bound.restype = C.c_float
+        L.og_act_apply.argtypes = [C.c_int32, C.c_float, C.c_float]
+        L.og_act_apply.restype = C.c_float
+        L.og_quantize_into.argtypes = [f32p, C.c_int64, i8p]
+        L.og_quantize_into.restype = C.c_float
+        L.og_compile.argtypes = [C.POINTER(_Layer), C.c_int32, C.c_int32]
+        L.og_compile.restype = C.POINTER(_Program)
+        L.og_program_free.argtypes = [C.POINTER(_Program)]
+        L.og_op_label.argtypes = [C.POINTER(_Op), C.c_char_p, C.c_int32]
+        L.og_op_label.restype = C.c_int32
+        L.og_program_summary.argtypes = [C.POINTER(_Program), C.c_int32, C.c_char_p, C.c_int32]
+        L.og_program_summary.restype = C.c_int32
+        L.og_op_linear.argtypes = [C.POINTER(_Op), f32p, C.c_int64, f32p, f32p, i8p, i32p, C.c_int32]
+        L.og_op_linear_with_amax.argtypes = [C.POINTER(_Op), f32p, C.c_int64, C.c_float, f32p, C.c_int32]
+        L.og_op_linear_rows.argtypes = [C.POINTER(_Op), f32p, C.c_int64, C.c_int64, C.c_int64,
+                                        f32p, f32p, i32p, C.c_int32]
+        L.og_op_conv2d.argtypes = [C.POINTER(_Op), f32p, C.c_int64, C.c_int32, C.c_int32, f32p,
+                                   f32p, i8p, i32p, C.c_int32]
+        L.og_maxpool2d.argtypes = [f32p, C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                   C.c_int32, f32p, C.c_int32]
+        L.og_activation.argtypes = [f32p, C.c_int64, C.c_int32, C.c_float, f32p]
+        L.og_softmax.argtypes = [f32p, C.c_int64, C.c_int64, f32p]
+        L.og_out_size.argtypes = [C.c_int64] * 4
+        L.og_out_size.restype = C.c_int64
+        L.og_im2col.argtypes = [f32p] + [C.c_int32] * 8 + [f32p]
+        L.og_execute.argtypes = [C.POINTER(_Program), f32p, i64p, C.c_int32, f32p, C.c_int64,
+                                 i64p, i32p, C.c_int32, i64p, i64p]
+        L.og_execute.restype = C.c_int32
+        _lib = L
+    return _lib
+
+
+def _p(a, ct):
+    return a.ctypes.data_as(C.POINTER(ct)) if a is not None else None
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+# --------------------------------------------------------------------------
+# RNG (src/rng.rs)
+# --------------------------------------------------------------------------
+class Rng:
+    """SplitMix64 generator with the reference's f32 draws (rng.rs:10-58).
+
+    ``Rng(42)`` is the state ``manual_seed(42)`` installs (rng.rs:71-73)."""
+
+    def __init__(self, seed: int):
+        self._s = _Rng()
+        lib().og_rng_seed(C.byref(self._s), C.c_uint64(seed))
+
+    def next_u64(self) -> int:
+        return lib().og_rng_next_u64(C.byref(self._s))
+
+    def uniform(self) -> float:
+        return lib().og_rng_uniform(C.byref(self._s))
+
+    def normal(self) -> float:
+        return lib().og_rng_normal(C.byref(self._s))
+
+    def uniform_tensor(self, shape, lo, hi) -> np.ndarray:  # Tensor::uniform (tensor/mod.rs:128-131)
+        out = np.empty(int(np.prod(shape)), np.float32)
+        lib().og_fill_uniform_range(C.byref(self._s), _p(out, C.c_float), out.size,
+                                    C.c_float(lo), C.c_float(hi))
+        return out.reshape(shape)
+
+    def randn(self, shape) -> np.ndarray:  # Tensor::randn (tensor/mod.rs:116-119)
+        out = np.empty(int(np.prod(shape)), np.float32)
+        lib().og_fill_normal(C.byref(self._s), _p(out, C.c_float), out.size)
+        return out.reshape(shape)
+
+    def normal_init(self, shape, std) -> np.ndarray:  # init::normal (nn/init.rs:18-20)
+        out = np.empty(int(np.prod(shape)), np.float32)
+        lib().og_fill_normal_scaled(C.byref(self._s), _p(out, C.c_float), out.size, C.c_float(std))
+        return out.reshape(shape)
+
+    def below(self, shape, n) -> np.ndarray:  # Rng::below (rng.rs:47-49)
+        out = np.empty(int(np.prod(shape)), np.int64)
+        lib().og_fill_below(C.byref(self._s), _p(out, C.c_int64), out.size, C.c_uint64(n))
+        return out.reshape(shape)
+
+    def kaiming_uniform(self, shape, fan_in):  # nn/init.rs:6-9
+        b = lib().og_kaiming_bound(fan_in)
+        return self.uniform_tensor(shape, -b, b)
+
+    def bias_uniform(self, shape, fan_in):  # nn/init.rs:23-26
+        b = lib().og_bias_bound(fan_in)
+        return self.uniform_tensor(shape, -b, b)
+
+
+# --------------------------------------------------------------------------
+# compile / program
+# --------------------------------------------------------------------------
+def _get(spec, name, default=None):
+    if isinstance(spec, dict):
+        return spec.get(name, default)
+    return getattr(spec, name, default)
+
+
+def _to_layers(specs):
+    keep = []
+    arr = (_Layer * max(1, len(specs)))()
+    for i, s in enumerate(specs):
+        L = arr[i]
+        kind = int(_get(s, "kind"))
+        L.kind = kind
+        for f in ("in_features", "out_features", "in_channels", "out_channels", "kernel",
+                  "stride", "padding"):
+            setattr(L, f, int(_get(s, f, 0) or 0))
+        if kind == CHANNEL_AFFINE:
+            w, b = _get(s, "scale"), _get(s, "shift")
+        else:
+            w, b = _get(s, "weight"), _get(s, "bias")
+        if w is not None:
+            w = _f32(w).reshape(-1)
+            keep.append(w)
+            L.weight, L.weight_len = _p(w, C.c_float), w.size
+        if b is not None:
+            b = _f32(b).reshape(-1)
+            keep.append(b)
+            L.bias, L.bias_len = _p(b, C.c_float), b.size
+        L.act = int(_get(s, "act", 0) or 0)
+        L.act_param = float(_get(s, "act_param", 0.0) or 0.0)
+    return arr, keep
+
+
+class Op:
+    """Read-only view of one compiled NpuOp (npu.rs:43-79)."""
+
+    def __init__(self, raw: _Op):
+        self.raw = raw
+        for f, _ in _Op._fields_:
+            if f not in ("wq", "bias"):
+                setattr(self, f, getattr(raw, f))
+        self.wq = np.ctypeslib.as_array(raw.wq, shape=(raw.wq_len,)).copy() if raw.wq_len else None
+        self.bias = np.ctypeslib.as_array(raw.bias, shape=(raw.bias_len,)).copy() if raw.bias_len else None
+
+    def label(self) -> str:
+        buf = C.create_string_buffer(256)
+        lib().og_op_label(C.byref(self.raw), buf, 256)
+        return buf.value.decode()
+
+
+class Program:
+    """``npu::compile`` output (npu.rs:188-276) plus per-op executors."""
+
+    def __init__(self, specs, precision: int = 0):
+        arr, keep = _to_layers(list(specs))
+        self._p = lib().og_compile(arr, len(specs), precision)
+        P = self._p.contents
+        self.precision = P.precision
+        self.original_layers = P.original_layers
+        self.fp32_bytes = P.fp32_bytes
+        self.npu_bytes = P.npu_bytes
+        self.ops = [Op(P.ops[i]) for i in range(P.n_ops)]
+
+    def __del__(self):
+        try:
+            lib().og_program_free(self._p)
+        except Exception:
+            pass
+
+    def summary(self, raw_count: int) -> str:
+        buf = C.create_string_buffer(1 << 16)
+        lib().og_program_summary(self._p, raw_count, buf, 1 << 16)
+        return buf.value.decode()
+
+    def compression_ratio(self) -> float:
+        return 1.0 if self.npu_bytes == 0 else float(np.float32(self.fp32_bytes) / np.float32(self.npu_bytes))
+
+    def execute(self, x, nthreads: int = 1):
+        """Whole-program execute (npu.rs:296-421). Returns (y, per-op ns, per-op MACs)."""
+        x = _f32(x)
+        shape = np.array(x.shape, np.int64)
+        cap = _out_capacity(self, x.shape)
+        y = np.empty(cap, np.float32)
+        ys = np.zeros(8, np.int64)
+        nd = C.c_int32(0)
+        ns = np.zeros(len(self.ops), np.int64)
+        macs = np.zeros(len(self.ops), np.int64)
+        rc = lib().og_execute(self._p, _p(x, C.c_float), _p(shape, C.c_int64), x.ndim,
+                              _p(y, C.c_float), cap, _p(ys, C.c_int64), C.byref(nd), nthreads,
+                              _p(ns, C.c_int64), _p(macs, C.c_int64))
+        if rc != 0:
+            raise RuntimeError(f"og_execute failed with {rc}")
+        out_shape = tuple(int(v) for v in ys[: nd.value])
+        return y[: int(np.prod(out_shape))].reshape(out_shape).copy(), ns, macs
+
+    def run_sharded(self, x, allreduce_max, nthreads: int = 1):
+        """Execute one batch shard; every Linear quantizes with
+        ``allreduce_max(local_absmax)`` (the max over all shards)."""
+        data = _f32(x)
+        for i, op in enumerate(self.ops):
+            if op.kind == LINEAR:
+                rows = data.size // op.in_features
+                a = np.abs(data.reshape(-1))
+                local = np.float32(np.nanmax(a)) if a.size and not np.isnan(a).all() else np.float32(0)
+                amax = np.float32(allreduce_max(max(local, np.float32(0))))
+                y = np.empty((rows, op.out_features), np.float32)
+                lib().og_op_linear_with_amax(C.byref(self._p.contents.ops[i]), _p(data, C.c_float), rows,
+                                             C.c_float(amax), _p(y, C.c_float), nthreads)
+                y = y.reshape(data.shape[:-1] + (op.out_features,))
+            elif op.kind == CONV2D:
+                n, c, h, w = data.shape
+                oh = lib().og_out_size(h, op.kernel, op.stride, op.padding)
+                ow = lib().og_out_size(w, op.kernel, op.stride, op.padding)
+                y = np.empty((n, op.out_channels, oh, ow), np.float32)
+                lib().og_op_conv2d(C.byref(self._p.contents.ops[i]), _p(data, C.c_float), n, h, w,
+                                   _p(y, C.c_float), None, None, None, nthreads)
+            elif op.kind == MAXPOOL2D:
+                y = maxpool2d(data, op.kernel, op.stride, nthreads)
+            elif op.kind == FLATTEN:
+                y = data.reshape(data.shape[0], -1)
+            elif op.kind == ACTIVATION:
+                y = activation(data, op.act, op.act_param)
+            elif op.kind == SOFTMAX:
+                y = softmax(data)
+            data = np.ascontiguousarray(y)
+        return data
+
+    def run_traced(self, x, nthreads: int = 1):
+        """Execute op by op and record every intermediate (for golden vectors):
+        a list of dicts with the op label, input, a_scale(s), i8 activations,
+        i32 accumulators and the f32 output."""
+        trace = []
+        data = _f32(x)
+        for i, op in enumerate(self.ops):
+            rec = {"label": op.label(), "kind": op.kind}
+            if op.kind == LINEAR:
+                rows = data.size // op.in_features
+                y = np.empty((rows, op.out_features), np.float32)
+                aq = np.empty((rows, op.in_features), np.int8)
+                acc = np.empty((rows, op.out_features), np.int32)
+                sa = C.c_float(0)
+                lib().og_op_linear(C.byref(self._p.contents.ops[i]), _p(data, C.c_float), rows,
+                                   _p(y, C.c_float), C.byref(sa), _p(aq, C.c_int8), _p(acc, C.c_int32),
+                                   nthreads)
+                rec.update(a_scale=np.float32(sa.value), aq=aq, acc=acc)
+                y = y.reshape(data.shape[:-1] + (op.out_features,))
+            elif op.kind == CONV2D:
+                n, c, h, w = data.shape
+                oh = lib().og_out_size(h, op.kernel, op.stride, op.padding)
+                ow = lib().og_out_size(w, op.kernel, op.stride, op.padding)
+                y = np.empty((n, op.out_channels, oh, ow), np.float32)
+                sc = np.empty(n, np.float32)
+                aq = np.empty((n, c, h, w), np.int8)
+                acc = np.empty((n, op.out_channels, oh, ow), np.int32)
+                lib().og_op_conv2d(C.byref(self._p.contents.ops[i]), _p(data, C.c_float), n, h, w,
+                                   _p(y, C.c_float), _p(sc, C.c_float), _p(aq, C.c_int8),
+                                   _p(acc, C.c_int32), nthreads)
+                rec.update(a_scales=sc, aq=aq, acc=acc)
+            elif op.kind == MAXPOOL2D:
+                y = maxpool2d(data, op.kernel, op.stride, nthreads)
+            elif op.kind == FLATTEN:
+                y = data.reshape(data.shape[0], -1)
+            elif op.kind == ACTIVATION:
+                y = activation(data, op.act, op.act_param)
+            elif op.kind == SOFTMAX:
+                y = softmax(data)
+            else:
+                raise ValueError(op.kind)
+            rec["y"] = y
+            trace.append(rec)
+            data = np.ascontiguousarray(y)
+        return data, trace
+
+
+def _out_capacity(prog: Program, in_shape) -> int:
+    """Upper bound on every intermediate's element count (shape walk of execute)."""
+    shape = list(in_shape)
+    best = int(np.prod(shape))
+    for op in prog.ops:
+        if op.kind == LINEAR:
+            shape[-1] = op.out_features
+        elif op.kind == CONV2D:
+            n, _, h, w = shape
+            shape = [n, op.out_channels, int(lib().og_out_size(h, op.kernel, op.stride, op.padding)),
+                     int(lib().og_out_size(w, op.kernel, op.stride, op.padding))]
+        elif op.kind == MAXPOOL2D:
+            n, c, h, w = shape
+            shape = [n, c, int(lib().og_out_size(h, op.kernel, op.stride, 0)),
+                     int(lib().og_out_size(w, op.kernel, op.stride, 0))]
+        elif op.kind == FLATTEN:
+            shape = [shape[0], int(np.prod(shape[1:]))]
+        best = max(best, int(np.prod(shape)))
+    return max(best, 1)
+
+
+# --------------------------------------------------------------------------
+# single kernels
+# --------------------------------------------------------------------------
+def quantize(x):
+    """QuantTensor::from_f32 (quantize.rs:18-24) -> (i8 array, scale)."""
+    x = _f32(x)
+    q = np.empty(x.shape, np.int8)
+    s = lib().og_quantize_into(_p(x, C.c_float), x.size, _p(q, C.c_int8))
+    return q, np.float32(s)
+
+
+def act_apply(act: int, param: float, x):
+    x = _f32(x)
+    y = np.empty_like(x)
+    lib().og_activation(_p(x, C.c_float), x.size, act, C.c_float(param), _p(y, C.c_float))
+    return y
+
+
+def activation(x, act: int, param: float = 0.0):
+    return act_apply(act, param, x)
+
+
+def maxpool2d(x, k: int, stride: int, nthreads: int = 1):
+    x = _f32(x)
+    n, c, h, w = x.shape
+    oh = lib().og_out_size(h, k, stride, 0)
+    ow = lib().og_out_size(w, k, stride, 0)
+    y = np.empty((n, c, oh, ow), np.float32)
+    lib().og_maxpool2d(_p(x, C.c_float), n, c, h, w, k, stride, _p(y, C.c_float), nthreads)
+    return y
+
+
+def softmax(x):
+    x = _f32(x)
+    last = x.shape[-1]
+    y = np.empty_like(x)
+    lib().og_softmax(_p(x, C.c_float), x.size // last if last else 0, last, _p(y, C.c_float))
+    return y
+
+
+def linear_rows(op: Op, prog: Program, op_index: int, x, r0: int, r1: int, nthreads: int = 1):
+    """FusedLinear on rows [r0, r1) with the activation scale over the whole x
+    (row sampling for shapes too large for the CPU)."""
+    x = _f32(x)
+    rows = x.size // op.in_features
+    y = np.empty((r1 - r0, op.out_features), np.float32)
+    acc = np.empty((r1 - r0, op.out_features), np.int32)
+    sa = C.c_float(0)
+    lib().og_op_linear_rows(C.byref(prog._p.contents.ops[op_index]), _p(x, C.c_float), rows, r0, r1,
+                            _p(y, C.c_float), C.byref(sa), _p(acc, C.c_int32), nthreads)
+    return y, acc, np.float32(sa.value)

@@ -1,0 +1,53 @@
+"""The benchmark configurations, built with the reference's generator.
+
+Draw order after ``manual_seed(seed)``: module construction (each Linear /
+Conv2d draws weight then bias), then each BatchNorm's running statistics
+(mean ~ U(-0.1, 0.1), then var ~ U(0.5, 1.5)), then the input.  The inputs
+are synthetic with the shapes and distributions the configurations name.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import nn, rng
+
+
+def c1_mlp(batch: int = 64, seed: int = 42, row_offset: int = 0):
+    """README MLP: Linear(4,32)+BatchNorm1d(32)+ReLU+Linear(32,3); x [batch,4] ~ N(0,1).
+    ``row_offset`` draws rows [row_offset, row_offset + batch) of a larger batch."""
+    rng.manual_seed(seed)
+    model = nn.Sequential(nn.Linear(4, 32), nn.BatchNorm1d(32), nn.Relu(), nn.Linear(32, 3))
+    nn.draw_bn_stats(model)
+    rng.advance(2 * 4 * row_offset)
+    return model, rng.randn((batch, 4))
+
+
+def c2_cnn(batch: int = 256, seed: int = 42, row_offset: int = 0):
+    """Small CNN on x [B,1,28,28] ~ U(0,1) (images [row_offset, row_offset + batch))."""
+    rng.manual_seed(seed)
+    model = nn.Sequential(
+        nn.Conv2d(1, 16, 3).padding(1), nn.BatchNorm2d(16), nn.Relu(), nn.MaxPool2d(2),
+        nn.Conv2d(16, 32, 3).padding(1), nn.BatchNorm2d(32), nn.Relu(), nn.MaxPool2d(2),
+        nn.Flatten(), nn.Linear(1568, 128), nn.Relu(), nn.Linear(128, 10))
+    nn.draw_bn_stats(model)
+    rng.advance(28 * 28 * row_offset)
+    return model, rng.rand((batch, 1, 28, 28))
+
+
+C3_SHAPES = [(4096, 4096, 4096), (16384, 8192, 8192), (65536, 4096, 14336)]
+
+
+def c3_linear(m: int, k: int, n: int, seed: int = 42, rows: int | None = None, row_offset: int = 0):
+    """Fused INT8 Linear + GELU: W [K,N] ~ 0.02 N(0,1), bias ~ 0.01 N(0,1), A [M,K] ~ N(0,1).
+    ``rows`` draws only the first rows of A (identical values)."""
+    rng.manual_seed(seed)
+    w = rng.normal_init((k, n), 0.02)
+    b = rng.normal_init((n,), 0.01)
+    model = nn.Sequential(nn.Linear(k, n, weight=w, bias=b), nn.Gelu())
+    rng.advance(2 * k * row_offset)
+    x = rng.randn((rows if rows is not None else m, k))
+    return model, x
+
+
+def input_only(config: str, batch: int, seed: int = 42) -> np.ndarray:
+    return {"c1": c1_mlp, "c2": c2_cnn}[config](batch, seed)[1]

@@ -1,0 +1,176 @@
+// k_gemm_simt.cu -- i8 x i8 -> i32 GEMM on the CUDA cores (dp4a) with the fused
+// dequant + bias + activation epilogue.
+//
+// Reference: int8_gemm_fused / int8_gemm_fused_serial / dot_i8
+// (src/inference/quantize.rs:68-144).  Used for shapes too small or too
+// ragged for the tensor-core kernel (K = 4, N = 3, ...) and for every Conv2d
+// as an implicit GEMM: the A operand is gathered on the fly from the
+// per-image-quantized NHWC i8 activation (rows = (image, oy, ox), reduction =
+// (ky, kx, c)), replacing the reference's im2col + transpose + quantize.
+#include "rg_kernels.h"
+#include "rg_math.cuh"
+
+namespace rg {
+namespace {
+
+constexpr int BM = 64, BN = 64, BKW = 8;  // tile: 64 x 64 outputs, 32 bytes of K per stage
+constexpr int kThreads = 256;
+
+struct RowCtx {    // per-row gather state for the implicit-GEMM A operand
+  const int8_t* base;  // image base (NHWC)
+  int32_t iy0, ix0;    // top-left input coordinate of the window
+  bool valid;
+};
+
+__device__ __forceinline__ RowCtx make_row(const GemmArgs& p, int64_t r) {
+  RowCtx rc;
+  rc.valid = r < p.m;
+  if (!p.conv) {
+    rc.base = p.a + (rc.valid ? r : 0) * p.lda;
+    rc.iy0 = rc.ix0 = 0;
+    return rc;
+  }
+  const int64_t L = (int64_t)p.g.oh * p.g.ow;
+  const int64_t rr = rc.valid ? r : 0;
+  const int64_t img = rr / L;
+  const int32_t l = (int32_t)(rr - img * L);
+  const int32_t oy = l / p.g.ow, ox = l - oy * p.g.ow;
+  rc.base = p.a + img * (int64_t)p.g.h * p.g.w * p.g.cpad;
+  rc.iy0 = oy * p.g.stride - p.g.pad;
+  rc.ix0 = ox * p.g.stride - p.g.pad;
+  return rc;
+}
+
+// 4 consecutive reduction bytes [kk, kk+4) of row rc.
+__device__ __forceinline__ int32_t load_a_word(const GemmArgs& p, const RowCtx& rc, int64_t kk) {
+  if (!rc.valid || kk >= p.k) return 0;
+  if (!p.conv) return __ldg(reinterpret_cast<const int32_t*>(rc.base + kk));
+  const int32_t C = p.g.c, kw = p.g.k;
+  const int64_t kreal = (int64_t)kw * kw * C;
+  if ((C & 3) == 0) {
+    if (kk >= kreal) return 0;
+    const int32_t tap = (int32_t)(kk / C), ch = (int32_t)(kk - (int64_t)tap * C);
+    const int32_t ky = tap / kw, kx = tap - ky * kw;
+    const int32_t iy = rc.iy0 + ky, ix = rc.ix0 + kx;
+    if (iy < 0 || iy >= p.g.h || ix < 0 || ix >= p.g.w) return 0;
+    return __ldg(reinterpret_cast<const int32_t*>(rc.base + ((int64_t)iy * p.g.w + ix) * p.g.cpad + ch));
+  }
+  uint32_t wv = 0;
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    const int64_t kb = kk + b;
+    if (kb >= kreal) break;
+    const int32_t tap = (int32_t)(kb / C), ch = (int32_t)(kb - (int64_t)tap * C);
+    const int32_t ky = tap / kw, kx = tap - ky * kw;
+    const int32_t iy = rc.iy0 + ky, ix = rc.ix0 + kx;
+    if (iy < 0 || iy >= p.g.h || ix < 0 || ix >= p.g.w) continue;
+    const int8_t v = rc.base[((int64_t)iy * p.g.w + ix) * p.g.cpad + ch];
+    wv |= (uint32_t)(uint8_t)v << (8 * b);
+  }
+  return (int32_t)wv;
+}
+
+__device__ __forceinline__ void flush_max(unsigned* base, int64_t slot, float v) {
+  // Warp-aggregated atomicMax when the whole warp targets the same slot.
+  const int64_t s0 = __shfl_sync(0xffffffffu, slot, 0);
+  if (__all_sync(0xffffffffu, slot == s0)) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if ((threadIdx.x & 31) == 0 && v > 0.0f) atomicMax(base + s0, __float_as_uint(v));
+  } else if (slot >= 0 && v > 0.0f) {
+    atomicMax(base + slot, __float_as_uint(v));
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) k_gemm_simt(const GemmArgs p) {
+  __shared__ __align__(16) int32_t As[BKW][BM];
+  __shared__ __align__(16) int32_t Bs[BKW][BN];
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int64_t m0 = (int64_t)blockIdx.x * BM, n0 = (int64_t)blockIdx.y * BN;
+
+  // Each thread stages 2 A words and 2 B words per K step: rows lr and lr + 32, word lw.
+  const int lr = tid >> 3, lw = tid & 7;
+  const RowCtx ra0 = make_row(p, m0 + lr), ra1 = make_row(p, m0 + lr + 32);
+  const bool vb0 = n0 + lr < p.n, vb1 = n0 + lr + 32 < p.n;
+  const int8_t* wb0 = p.w + (vb0 ? n0 + lr : 0) * p.ldb;
+  const int8_t* wb1 = p.w + (vb1 ? n0 + lr + 32 : 0) * p.ldb;
+
+  int32_t acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0;
+
+  for (int64_t k0 = 0; k0 < p.k; k0 += BKW * 4) {
+    const int64_t kk = k0 + lw * 4;
+    const int32_t a0 = load_a_word(p, ra0, kk), a1 = load_a_word(p, ra1, kk);
+    const int32_t b0 = (vb0 && kk < p.k) ? __ldg(reinterpret_cast<const int32_t*>(wb0 + kk)) : 0;
+    const int32_t b1 = (vb1 && kk < p.k) ? __ldg(reinterpret_cast<const int32_t*>(wb1 + kk)) : 0;
+    __syncthreads();
+    As[lw][lr] = a0; As[lw][lr + 32] = a1;
+    Bs[lw][lr] = b0; Bs[lw][lr + 32] = b1;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < BKW; ++w) {
+      const int4 av = *reinterpret_cast<const int4*>(&As[w][ty * 4]);
+      const int4 bv = *reinterpret_cast<const int4*>(&Bs[w][tx * 4]);
+      const int32_t a[4] = {av.x, av.y, av.z, av.w};
+      const int32_t b[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = __dp4a(a[i], b[j], acc[i][j]);
+    }
+  }
+
+  // Fused epilogue: act((acc as f32) * (sa * sw) + bias[c]).
+  float mx_lo = 0.0f, mx_hi = 0.0f;
+  int64_t slot_lo = -1, slot_hi = -1;
+  const int64_t L = p.out_l;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t r = m0 + ty * 4 + i;
+    if (r >= p.m) continue;
+    const float sa = p.a_scale[p.rows_per_scale ? r / p.rows_per_scale : 0];
+    int64_t rowbase, colstride;
+    if (L) {
+      const int64_t img = r / L;
+      rowbase = img * p.n * L + (r - img * L);
+      colstride = L;
+    } else {
+      rowbase = r * p.n;
+      colstride = 1;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t c = n0 + tx * 4 + j;
+      if (c >= p.n) continue;
+      const float sw = p.w_scale_ch ? p.w_scale_ch[c] : p.w_scale;
+      const float cs = __fmul_rn(sa, sw);
+      const float v = epilogue(acc[i][j], cs, p.bias[c], p.act, p.act_param);
+      const int64_t o = rowbase + c * colstride;
+      p.out[o] = v;
+      if (p.acc) p.acc[o] = acc[i][j];
+      if (p.amax.ptr) {
+        const int64_t slot = p.amax.elems_per_slot ? o / p.amax.elems_per_slot : 0;
+        if (slot_lo < 0 || slot == slot_lo) { slot_lo = slot; mx_lo = fmaxf(mx_lo, fabsf(v)); }
+        else { slot_hi = slot; mx_hi = fmaxf(mx_hi, fabsf(v)); }
+      }
+    }
+  }
+  if (p.amax.ptr) {
+    flush_max(p.amax.ptr, slot_lo, mx_lo);
+    flush_max(p.amax.ptr, slot_hi, mx_hi);
+  }
+}
+
+}  // namespace
+
+void launch_gemm_simt(const GemmArgs& a, cudaStream_t st) {
+  if (a.m <= 0 || a.n <= 0) return;
+  dim3 grid((unsigned)((a.m + BM - 1) / BM), (unsigned)((a.n + BN - 1) / BN));
+  k_gemm_simt<<<grid, kThreads, 0, st>>>(a);
+}
+
+}  // namespace rg

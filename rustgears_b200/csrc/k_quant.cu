@@ -1,0 +1,199 @@
+// k_quant.cu -- activation absmax and symmetric INT8 quantization kernels.
+//
+// Reference: QuantTensor::from_f32 / quantize_into (src/inference/quantize.rs:18-35).
+// The reference folds max|v| serially over the whole tensor; max is exact and
+// order-free, so a parallel reduction gives the identical value.  HBM-bound:
+// 16-byte vector loads, warp-shuffle reduction, one atomic per block.
+#include "rg_kernels.h"
+#include "rg_math.cuh"
+
+namespace rg {
+namespace {
+
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide max of non-negative floats; one atomicMax on the uint bits by thread 0.
+__device__ __forceinline__ void block_max_to(float v, unsigned* dst) {
+  __shared__ float red[kThreads / 32];
+  v = warp_max(v);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  if (wid == 0) {
+    v = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0f;
+    v = warp_max(v);
+    if (lane == 0 && v > 0.0f) atomicMax(dst, __float_as_uint(v));
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) k_absmax(const float* __restrict__ x, int64_t n,
+                                                     unsigned* __restrict__ out) {
+  float m = 0.0f;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    const int64_t n4 = n >> 2;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    for (int64_t i = tid; i < n4; i += stride) {
+      const float4 v = __ldg(x4 + i);
+      m = fmaxf(m, fabsf(v.x)); m = fmaxf(m, fabsf(v.y));
+      m = fmaxf(m, fabsf(v.z)); m = fmaxf(m, fabsf(v.w));
+    }
+    for (int64_t i = (n4 << 2) + tid; i < n; i += stride) m = fmaxf(m, fabsf(__ldg(x + i)));
+  } else {
+    for (int64_t i = tid; i < n; i += stride) m = fmaxf(m, fabsf(__ldg(x + i)));
+  }
+  block_max_to(m, out);
+}
+
+// One thread per 16 output bytes of a row.
+__global__ void __launch_bounds__(kThreads) k_quantize_rows(const float* __restrict__ x, int64_t rows,
+                                                            int64_t k, int64_t ldq,
+                                                            const unsigned* __restrict__ amax_bits,
+                                                            int8_t* __restrict__ q,
+                                                            float* __restrict__ scale_out) {
+  const float scale = quant_scale(__uint_as_float(*amax_bits));
+  const float inv = quant_inv(scale);
+  if (blockIdx.x == 0 && threadIdx.x == 0 && scale_out) *scale_out = scale;
+  const int64_t chunks = ldq >> 4;
+  const int64_t total = rows * chunks;
+  const bool vec = ((k & 3) == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = t / chunks, c0 = (t - r * chunks) << 4;
+    const float* src = x + r * k + c0;
+    uint32_t word[4];
+    if (vec && c0 + 16 <= k) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(src) + j);
+        word[j] = (uint32_t)(quant1(v.x, inv) & 0xff) | ((uint32_t)(quant1(v.y, inv) & 0xff) << 8) |
+                  ((uint32_t)(quant1(v.z, inv) & 0xff) << 16) | ((uint32_t)(quant1(v.w, inv) & 0xff) << 24);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t wv = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const int64_t col = c0 + j * 4 + b;
+          const int32_t qv = col < k ? quant1(__ldg(src + j * 4 + b), inv) : 0;
+          wv |= (uint32_t)(qv & 0xff) << (8 * b);
+        }
+        word[j] = wv;
+      }
+    }
+    *reinterpret_cast<uint4*>(q + r * ldq + c0) = make_uint4(word[0], word[1], word[2], word[3]);
+  }
+}
+
+// grid (blocks_per_image, n): max |x| over covered pixels of each image.
+__global__ void __launch_bounds__(kThreads) k_image_absmax(const float* __restrict__ x, int32_t c,
+                                                           int32_t h, int32_t w,
+                                                           const uint8_t* __restrict__ row_cov,
+                                                           const uint8_t* __restrict__ col_cov,
+                                                           unsigned* __restrict__ amax) {
+  const int64_t img = blockIdx.y;
+  const int64_t per = (int64_t)c * h * w;
+  const float* xi = x + img * per;
+  float m = 0.0f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < per;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    if (row_cov) {
+      const int64_t p = i % ((int64_t)h * w);
+      const int32_t iy = (int32_t)(p / w), ix = (int32_t)(p - (int64_t)iy * w);
+      if (!row_cov[iy] || !col_cov[ix]) continue;
+    }
+    m = fmaxf(m, fabsf(__ldg(xi + i)));
+  }
+  block_max_to(m, amax + img);
+}
+
+// grid-stride over (image, pixel): NCHW f32 -> NHWC i8 (pixel stride cpad).
+__global__ void __launch_bounds__(kThreads) k_image_quantize_nhwc(const float* __restrict__ x, int64_t n,
+                                                                  int32_t c, int32_t hw, int32_t cpad,
+                                                                  const unsigned* __restrict__ amax,
+                                                                  int8_t* __restrict__ q,
+                                                                  float* __restrict__ scales) {
+  const int64_t total = n * hw;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t img = t / hw;
+    const int64_t p = t - img * hw;
+    const float scale = quant_scale(__uint_as_float(amax[img]));
+    const float inv = quant_inv(scale);
+    if (p == 0 && scales) scales[img] = scale;
+    const float* src = x + img * (int64_t)c * hw + p;
+    int8_t* dst = q + t * cpad;
+    for (int32_t ch = 0; ch < cpad; ++ch)
+      dst[ch] = (int8_t)(ch < c ? quant1(__ldg(src + (int64_t)ch * hw), inv) : 0);
+  }
+}
+
+__global__ void k_nhwc_to_nchw_i8(const int8_t* __restrict__ q, int64_t n, int32_t c, int32_t cpad,
+                                  int32_t hw, int8_t* __restrict__ out) {
+  const int64_t total = n * (int64_t)c * hw;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t img = t / ((int64_t)c * hw);
+    const int64_t rem = t - img * c * hw;
+    const int32_t ch = (int32_t)(rem / hw);
+    const int64_t p = rem - (int64_t)ch * hw;
+    out[t] = q[(img * hw + p) * cpad + ch];
+  }
+}
+
+int grid_for(int64_t work, int64_t per_block, int cap) {
+  int64_t g = (work + per_block - 1) / per_block;
+  if (g < 1) g = 1;
+  if (g > cap) g = cap;
+  return (int)g;
+}
+
+}  // namespace
+
+void launch_absmax(const float* x, int64_t n, unsigned* amax_bits, cudaStream_t st) {
+  if (n <= 0) return;
+  k_absmax<<<grid_for(n, kThreads * 16, 148 * 16), kThreads, 0, st>>>(x, n, amax_bits);
+}
+
+void launch_quantize_rows(const float* x, int64_t rows, int64_t k, int64_t ldq,
+                          const unsigned* amax_bits, int8_t* q, float* scale_out, cudaStream_t st) {
+  const int64_t work = rows * (ldq >> 4);
+  if (work <= 0) return;
+  k_quantize_rows<<<grid_for(work, kThreads, 148 * 32), kThreads, 0, st>>>(x, rows, k, ldq, amax_bits, q,
+                                                                           scale_out);
+}
+
+void launch_image_absmax(const float* x, int64_t n, int32_t c, int32_t h, int32_t w,
+                         const uint8_t* row_cov, const uint8_t* col_cov, unsigned* amax_bits,
+                         cudaStream_t st) {
+  const int64_t per = (int64_t)c * h * w;
+  if (n <= 0 || per <= 0) return;
+  dim3 grid(grid_for(per, kThreads * 8, 64), (unsigned)n);
+  k_image_absmax<<<grid, kThreads, 0, st>>>(x, c, h, w, row_cov, col_cov, amax_bits);
+}
+
+void launch_image_quantize_nhwc(const float* x, int64_t n, int32_t c, int32_t h, int32_t w,
+                                int32_t cpad, const unsigned* amax_bits, int8_t* q,
+                                float* scales_out, cudaStream_t st) {
+  const int64_t total = n * (int64_t)h * w;
+  if (total <= 0) return;
+  k_image_quantize_nhwc<<<grid_for(total, kThreads, 148 * 32), kThreads, 0, st>>>(
+      x, n, c, h * w, cpad, amax_bits, q, scales_out);
+}
+
+void launch_nhwc_to_nchw_i8(const int8_t* q, int64_t n, int32_t c, int32_t cpad, int32_t h,
+                            int32_t w, int8_t* out, cudaStream_t st) {
+  const int64_t total = n * (int64_t)c * h * w;
+  if (total <= 0) return;
+  k_nhwc_to_nchw_i8<<<grid_for(total, kThreads, 148 * 32), kThreads, 0, st>>>(q, n, c, cpad, h * w, out);
+}
+
+}  // namespace rg

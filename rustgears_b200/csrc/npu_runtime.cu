@@ -1,0 +1,1216 @@
+// npu_runtime.cu -- host runtime of the B200 INT8 execution provider and its C ABI.
+//
+// Replaces the CPU `NpuProgram` of RustGears:
+//   * compile (src/inference/npu.rs:188-276, mod.rs:225-257): BatchNorm folding,
+//     Linear/Conv2d + next-Activation fusion, symmetric per-tensor i8 weights,
+//     byte accounting; weights are uploaded once;
+//   * execute (npu.rs:296-421): one device program per call, ops launched on
+//     the session's stream, per-op CUDA events filling the OpRecord durations.
+// Each quantizing op's input absmax (per tensor for Linear, per image for
+// Conv2d) is produced in the epilogue of the kernel that writes that tensor,
+// so no op re-reads its input just to find the scale.
+#include <cuda_runtime.h>
+#include <nccl.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/rg_npu.h"
+#include "rg_kernels.h"
+#include "rg_math.cuh"
+
+namespace rg {
+
+// ----------------------------------------------------------------------------
+// errors
+// ----------------------------------------------------------------------------
+static thread_local std::string g_err = "ok";
+
+static rg_status fail(rg_status st, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return st;
+}
+
+#define RG_CUDA_TRY(expr)                                                                   \
+  do {                                                                                      \
+    cudaError_t e_ = (expr);                                                                \
+    if (e_ != cudaSuccess)                                                                  \
+      return fail(e_ == cudaErrorMemoryAllocation ? RG_ERR_OOM : RG_ERR_CUDA, "%s: %s (%s:%d)", \
+                  #expr, cudaGetErrorString(e_), __FILE__, __LINE__);                       \
+  } while (0)
+
+#define RG_NCCL_TRY(expr)                                                                   \
+  do {                                                                                      \
+    ncclResult_t r_ = (expr);                                                               \
+    if (r_ != ncclSuccess)                                                                  \
+      return fail(RG_ERR_NCCL, "%s: %s", #expr, ncclGetErrorString(r_));                    \
+  } while (0)
+
+#define RG_TRY(expr)                 \
+  do {                               \
+    rg_status s_ = (expr);           \
+    if (s_ != RG_OK) return s_;      \
+  } while (0)
+
+static int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+static int64_t out_size(int64_t input, int64_t k, int64_t stride, int64_t pad) {  // kernels.rs:10-15
+  const int64_t padded = input + 2 * pad;
+  if (k <= 0 || stride <= 0 || padded < k) return -1;
+  return (padded - k) / stride + 1;
+}
+
+// ----------------------------------------------------------------------------
+// device buffer
+// ----------------------------------------------------------------------------
+struct DevBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  ~DevBuf() { if (p) cudaFree(p); }
+  rg_status ensure(size_t n) {
+    if (n <= bytes) return RG_OK;
+    if (p) { cudaFree(p); p = nullptr; bytes = 0; }
+    const size_t want = std::max<size_t>(n, 256);
+    RG_CUDA_TRY(cudaMalloc(&p, want));
+    bytes = want;
+    return RG_OK;
+  }
+  template <class T> T* as() const { return reinterpret_cast<T*>(p); }
+};
+
+// ----------------------------------------------------------------------------
+// compiled program
+// ----------------------------------------------------------------------------
+struct HostLayer {
+  int32_t kind = 0, in_f = 0, out_f = 0, in_c = 0, out_c = 0, k = 0, stride = 0, pad = 0;
+  int32_t act = 0;
+  float param = 0.0f;
+  std::vector<float> w, b;
+};
+
+struct Op {
+  int32_t kind = 0;  // RG_LAYER_LINEAR / CONV2D / MAXPOOL2D / FLATTEN / ACTIVATION / SOFTMAX
+  int32_t in_f = 0, out_f = 0, in_c = 0, out_c = 0, k = 0, stride = 0, pad = 0;
+  int32_t act = 0;
+  float param = 0.0f;
+  float w_scale = 0.0f;          // per-tensor weight scale
+  std::vector<float> w_scale_ch;  // per-output-channel scales (extension)
+  std::vector<int8_t> wq;        // reference layout: Linear [out,in]; Conv [O, C*k*k]
+  std::vector<float> bias;
+  int64_t kdim = 0, kpad = 0;     // GEMM reduction length and its padded device stride
+  DevBuf d_w, d_bias, d_wsc;     // device weights [N, kpad] (conv: (ky,kx,c) order)
+  std::string label;
+};
+
+struct TraceRec {
+  std::vector<float> scales;
+  std::vector<int8_t> aq;
+  std::vector<int32_t> acc;
+  std::vector<float> out;
+};
+
+struct Profile {
+  bool valid = false;
+  int32_t launches = 0;
+  uint64_t total_macs = 0;
+  int64_t total_ns = 0;
+  std::vector<uint64_t> macs;
+  std::vector<int64_t> ns;
+};
+
+struct Session {
+  int device = 0;
+  int precision = RG_PREC_INT8;
+  int weight_quant = 0;
+  int flags = 0;
+  int num_sms = 148;
+  int original_layers = 0;
+  int64_t fp32_bytes = 0, npu_bytes = 0;
+  std::vector<Op> ops;
+  cudaStream_t stream = nullptr;
+  std::vector<cudaEvent_t> events;
+  std::mutex mu;
+  // workspace
+  DevBuf act0, act1, qbuf, amax, scales, accbuf, xin, yout, covbuf;
+  // profile + trace
+  Profile last;
+  bool trace = false;
+  std::vector<TraceRec> traces;
+  // multi-GPU
+  ncclComm_t comm = nullptr;
+  int rank = 0, world = 1;
+};
+
+static void act_name(int32_t act, float p, char* out, size_t cap) {
+  switch (act) {
+    case RG_ACT_NONE: snprintf(out, cap, "none"); break;
+    case RG_ACT_RELU: snprintf(out, cap, "ReLU"); break;
+    case RG_ACT_SIGMOID: snprintf(out, cap, "Sigmoid"); break;
+    case RG_ACT_TANH: snprintf(out, cap, "Tanh"); break;
+    case RG_ACT_GELU: snprintf(out, cap, "GELU"); break;
+    case RG_ACT_LEAKY_RELU: {
+      // Rust `{}` of an f32: shortest decimal that round-trips, no exponent.
+      char num[64];
+      for (int prec = 0; prec <= 60; ++prec) {
+        snprintf(num, sizeof num, "%.*f", prec, (double)p);
+        if (strtof(num, nullptr) == p) break;
+      }
+      snprintf(out, cap, "LeakyReLU(%s)", num);
+      break;
+    }
+    default: snprintf(out, cap, "?"); break;
+  }
+}
+
+static std::string make_label(const Op& op) {  // NpuOp::label (npu.rs:83-104)
+  char a[96], buf[192];
+  act_name(op.act, op.param, a, sizeof a);
+  switch (op.kind) {
+    case RG_LAYER_LINEAR:
+      if (op.act == RG_ACT_NONE) snprintf(buf, sizeof buf, "NPU::Gemm(%d->%d)", op.in_f, op.out_f);
+      else snprintf(buf, sizeof buf, "NPU::FusedGemmAct(%d->%d, %s)", op.in_f, op.out_f, a);
+      break;
+    case RG_LAYER_CONV2D:
+      if (op.act == RG_ACT_NONE) snprintf(buf, sizeof buf, "NPU::Conv2d(%d->%d, k=%d)", op.in_c, op.out_c, op.k);
+      else snprintf(buf, sizeof buf, "NPU::FusedConv2dAct(%d->%d, k=%d, %s)", op.in_c, op.out_c, op.k, a);
+      break;
+    case RG_LAYER_MAXPOOL2D: snprintf(buf, sizeof buf, "NPU::MaxPool2d(k=%d)", op.k); break;
+    case RG_LAYER_FLATTEN: snprintf(buf, sizeof buf, "NPU::Flatten"); break;
+    case RG_LAYER_ACTIVATION: snprintf(buf, sizeof buf, "NPU::Act(%s)", a); break;
+    case RG_LAYER_SOFTMAX: snprintf(buf, sizeof buf, "NPU::Softmax"); break;
+    default: snprintf(buf, sizeof buf, "NPU::?"); break;
+  }
+  return buf;
+}
+
+// Symmetric i8 quantization (quantize.rs:18-24) of n values; returns the scale.
+static float quantize_host(const float* v, int64_t n, int8_t* out) {
+  float m = 0.0f;
+  for (int64_t i = 0; i < n; ++i) m = fmaxf(m, fabsf(v[i]));
+  const float scale = quant_scale(m);
+  const float inv = quant_inv(scale);
+  for (int64_t i = 0; i < n; ++i) out[i] = (int8_t)quant1(v[i], inv);
+  return scale;
+}
+
+static rg_status validate_layer(const rg_layer_spec& l, int idx) {
+  switch (l.kind) {
+    case RG_LAYER_LINEAR:
+      if (l.in_features <= 0 || l.out_features <= 0 ||
+          l.weight_len != (int64_t)l.in_features * l.out_features || l.bias_len != l.out_features ||
+          !l.weight || !l.bias)
+        return fail(RG_ERR_INVALID_ARG, "layer %d: Linear(%d, %d) needs weight [in,out] and bias [out]", idx,
+                    l.in_features, l.out_features);
+      return RG_OK;
+    case RG_LAYER_CONV2D:
+      if (l.in_channels <= 0 || l.out_channels <= 0 || l.kernel <= 0 || l.stride <= 0 || l.padding < 0 ||
+          l.weight_len != (int64_t)l.out_channels * l.in_channels * l.kernel * l.kernel ||
+          l.bias_len != l.out_channels || !l.weight || !l.bias)
+        return fail(RG_ERR_INVALID_ARG, "layer %d: Conv2d(%d, %d, k=%d) has inconsistent weights", idx,
+                    l.in_channels, l.out_channels, l.kernel);
+      return RG_OK;
+    case RG_LAYER_CHANNEL_AFFINE:
+      if (l.weight_len <= 0 || l.bias_len != l.weight_len || !l.weight || !l.bias)
+        return fail(RG_ERR_INVALID_ARG, "layer %d: ChannelAffine needs scale and shift of equal length", idx);
+      return RG_OK;
+    case RG_LAYER_MAXPOOL2D:
+      if (l.kernel <= 0 || l.stride <= 0)
+        return fail(RG_ERR_INVALID_ARG, "layer %d: kernel and stride must be positive", idx);
+      return RG_OK;
+    case RG_LAYER_FLATTEN:
+    case RG_LAYER_SOFTMAX:
+      return RG_OK;
+    case RG_LAYER_ACTIVATION:
+      if (l.act < RG_ACT_NONE || l.act > RG_ACT_LEAKY_RELU)
+        return fail(RG_ERR_INVALID_ARG, "layer %d: unknown activation tag %d", idx, l.act);
+      return RG_OK;
+    default:
+      return fail(RG_ERR_INVALID_ARG, "layer %d: unknown layer tag %d", idx, l.kind);
+  }
+}
+
+// fold_batch_norm (src/inference/mod.rs:225-257): w *= s, b = b * s + shift (two roundings).
+static std::vector<HostLayer> fold(const rg_layer_spec* L, int32_t n) {
+  std::vector<HostLayer> out;
+  for (int32_t i = 0; i < n; ++i) {
+    const rg_layer_spec& l = L[i];
+    if (l.kind == RG_LAYER_CHANNEL_AFFINE && !out.empty()) {
+      HostLayer& p = out.back();
+      const int64_t c = l.weight_len;
+      if (p.kind == RG_LAYER_LINEAR && p.out_f == c) {
+        for (int64_t r = 0; r < p.in_f; ++r)
+          for (int64_t j = 0; j < p.out_f; ++j) p.w[r * p.out_f + j] = p.w[r * p.out_f + j] * l.weight[j];
+        for (int64_t j = 0; j < p.out_f; ++j) { const float t = p.b[j] * l.weight[j]; p.b[j] = t + l.bias[j]; }
+        continue;
+      }
+      if (p.kind == RG_LAYER_CONV2D && p.out_c == c) {
+        const int64_t plane = (int64_t)p.in_c * p.k * p.k;
+        for (int64_t o = 0; o < p.out_c; ++o) {
+          for (int64_t j = 0; j < plane; ++j) p.w[o * plane + j] = p.w[o * plane + j] * l.weight[o];
+          const float t = p.b[o] * l.weight[o];
+          p.b[o] = t + l.bias[o];
+        }
+        continue;
+      }
+    }
+    HostLayer h;
+    h.kind = l.kind; h.in_f = l.in_features; h.out_f = l.out_features; h.in_c = l.in_channels;
+    h.out_c = l.out_channels; h.k = l.kernel; h.stride = l.stride; h.pad = l.padding;
+    h.act = l.act; h.param = l.act_param;
+    if (l.weight_len > 0) h.w.assign(l.weight, l.weight + l.weight_len);
+    if (l.bias_len > 0) h.b.assign(l.bias, l.bias + l.bias_len);
+    out.push_back(std::move(h));
+  }
+  return out;
+}
+
+static rg_status upload_op(Op& op) {
+  // Device layout [N, kpad], K-contiguous, zero padded; conv reduction order (ky, kx, c).
+  const int64_t N = op.kind == RG_LAYER_LINEAR ? op.out_f : op.out_c;
+  std::vector<int8_t> dev((size_t)(N * op.kpad), 0);
+  if (op.kind == RG_LAYER_LINEAR) {
+    for (int64_t n = 0; n < N; ++n)
+      memcpy(&dev[(size_t)(n * op.kpad)], &op.wq[(size_t)(n * op.in_f)], (size_t)op.in_f);
+  } else {
+    const int64_t C = op.in_c, K = op.k;
+    for (int64_t o = 0; o < N; ++o)
+      for (int64_t c = 0; c < C; ++c)
+        for (int64_t ky = 0; ky < K; ++ky)
+          for (int64_t kx = 0; kx < K; ++kx)
+            dev[(size_t)(o * op.kpad + (ky * K + kx) * C + c)] = op.wq[(size_t)(((o * C + c) * K + ky) * K + kx)];
+  }
+  RG_TRY(op.d_w.ensure(dev.size()));
+  RG_CUDA_TRY(cudaMemcpy(op.d_w.p, dev.data(), dev.size(), cudaMemcpyHostToDevice));
+  RG_TRY(op.d_bias.ensure(op.bias.size() * sizeof(float)));
+  RG_CUDA_TRY(cudaMemcpy(op.d_bias.p, op.bias.data(), op.bias.size() * sizeof(float), cudaMemcpyHostToDevice));
+  if (!op.w_scale_ch.empty()) {
+    RG_TRY(op.d_wsc.ensure(op.w_scale_ch.size() * sizeof(float)));
+    RG_CUDA_TRY(cudaMemcpy(op.d_wsc.p, op.w_scale_ch.data(), op.w_scale_ch.size() * sizeof(float),
+                           cudaMemcpyHostToDevice));
+  }
+  return RG_OK;
+}
+
+static void quantize_weights(Op& op, const float* w_ref_layout, int64_t rows, int64_t cols, int per_channel) {
+  op.wq.resize((size_t)(rows * cols));
+  if (!per_channel) {
+    op.w_scale = quantize_host(w_ref_layout, rows * cols, op.wq.data());
+  } else {
+    op.w_scale = 0.0f;
+    op.w_scale_ch.resize((size_t)rows);
+    for (int64_t r = 0; r < rows; ++r)
+      op.w_scale_ch[(size_t)r] = quantize_host(w_ref_layout + r * cols, cols, op.wq.data() + r * cols);
+  }
+}
+
+// npu::compile (npu.rs:188-276).
+static rg_status compile(Session& s, const rg_layer_spec* layers, int32_t n) {
+  for (int32_t i = 0; i < n; ++i) RG_TRY(validate_layer(layers[i], i));
+  std::vector<HostLayer> f = fold(layers, n);
+  s.original_layers = n;
+  for (size_t i = 0; i < f.size(); ++i) {
+    HostLayer& l = f[i];
+    const bool next_act = i + 1 < f.size() && f[i + 1].kind == RG_LAYER_ACTIVATION;
+    Op op;
+    if (l.kind == RG_LAYER_LINEAR || l.kind == RG_LAYER_CONV2D) {
+      op.kind = l.kind;
+      op.act = next_act ? f[i + 1].act : RG_ACT_NONE;
+      op.param = next_act ? f[i + 1].param : 0.0f;
+      if (l.kind == RG_LAYER_LINEAR) {
+        op.in_f = l.in_f; op.out_f = l.out_f;
+        std::vector<float> wt((size_t)l.w.size());
+        for (int64_t r = 0; r < l.in_f; ++r)  // transpose2d [in,out] -> [out,in] (npu.rs:208)
+          for (int64_t c = 0; c < l.out_f; ++c) wt[(size_t)(c * l.in_f + r)] = l.w[(size_t)(r * l.out_f + c)];
+        quantize_weights(op, wt.data(), l.out_f, l.in_f, s.weight_quant);
+        op.kdim = l.in_f;
+      } else {
+        op.in_c = l.in_c; op.out_c = l.out_c; op.k = l.k; op.stride = l.stride; op.pad = l.pad;
+        op.kdim = (int64_t)l.in_c * l.k * l.k;
+        quantize_weights(op, l.w.data(), l.out_c, op.kdim, s.weight_quant);
+      }
+      op.kpad = round_up(op.kdim, 16);
+      op.bias = l.b;
+      s.fp32_bytes += (int64_t)(l.w.size() + l.b.size()) * 4;
+      s.npu_bytes += s.precision == RG_PREC_INT8 ? ((int64_t)op.wq.size() + 4) + (int64_t)l.b.size() * 4
+                                                 : (int64_t)l.w.size() * 2 + (int64_t)l.b.size() * 2;
+      if (next_act) ++i;
+    } else if (l.kind == RG_LAYER_CHANNEL_AFFINE) {
+      // standalone affine -> diagonal FusedLinear (npu.rs:254-270), no byte accounting
+      const int64_t c = (int64_t)l.w.size();
+      std::vector<float> w((size_t)(c * c), 0.0f);
+      for (int64_t j = 0; j < c; ++j) w[(size_t)(j * c + j)] = l.w[(size_t)j];
+      op.kind = RG_LAYER_LINEAR; op.in_f = (int32_t)c; op.out_f = (int32_t)c;
+      quantize_weights(op, w.data(), c, c, s.weight_quant);
+      op.kdim = c; op.kpad = round_up(c, 16);
+      op.bias = l.b;
+      op.act = RG_ACT_NONE;
+    } else {
+      op.kind = l.kind; op.k = l.k; op.stride = l.stride; op.act = l.act; op.param = l.param;
+    }
+    op.label = make_label(op);
+    if (op.kind == RG_LAYER_LINEAR || op.kind == RG_LAYER_CONV2D) RG_TRY(upload_op(op));
+    s.ops.push_back(std::move(op));
+  }
+  return RG_OK;
+}
+
+// ----------------------------------------------------------------------------
+// run planning
+// ----------------------------------------------------------------------------
+struct OpShape {
+  std::vector<int64_t> in, out;
+  int64_t in_elems = 0, out_elems = 0;
+  uint64_t macs = 0;
+};
+
+static rg_status plan_shapes(const Session& s, const int64_t* shape, int32_t ndim, std::vector<OpShape>& out) {
+  if (ndim < 1 || ndim > 8) return fail(RG_ERR_SHAPE, "input rank %d not supported", ndim);
+  std::vector<int64_t> sh(shape, shape + ndim);
+  for (int64_t d : sh)
+    if (d < 0) return fail(RG_ERR_SHAPE, "negative dimension in input shape");
+  auto numel = [](const std::vector<int64_t>& v) {
+    int64_t n = 1;
+    for (int64_t d : v) n *= d;
+    return n;
+  };
+  out.clear();
+  for (size_t i = 0; i < s.ops.size(); ++i) {
+    const Op& op = s.ops[i];
+    OpShape os;
+    os.in = sh;
+    os.in_elems = numel(sh);
+    switch (op.kind) {
+      case RG_LAYER_LINEAR: {
+        if (sh.back() != op.in_f)
+          return fail(RG_ERR_SHAPE, "op %zu (%s): last dim %lld != in_features %d", i, op.label.c_str(),
+                      (long long)sh.back(), op.in_f);
+        const int64_t rows = os.in_elems / op.in_f;
+        os.macs = (uint64_t)rows * op.in_f * op.out_f;
+        sh.back() = op.out_f;
+        break;
+      }
+      case RG_LAYER_CONV2D: {
+        if (sh.size() != 4 || sh[1] != op.in_c)
+          return fail(RG_ERR_SHAPE, "op %zu (%s): expected [N,%d,H,W] input", i, op.label.c_str(), op.in_c);
+        const int64_t oh = out_size(sh[2], op.k, op.stride, op.pad), ow = out_size(sh[3], op.k, op.stride, op.pad);
+        if (oh <= 0 || ow <= 0)
+          return fail(RG_ERR_SHAPE, "op %zu (%s): kernel %d larger than padded input", i, op.label.c_str(), op.k);
+        os.macs = (uint64_t)sh[0] * op.out_c * op.in_c * op.k * op.k * oh * ow;
+        sh = {sh[0], op.out_c, oh, ow};
+        break;
+      }
+      case RG_LAYER_MAXPOOL2D: {
+        if (sh.size() != 4) return fail(RG_ERR_SHAPE, "op %zu (%s): expected a 4-D input", i, op.label.c_str());
+        const int64_t oh = out_size(sh[2], op.k, op.stride, 0), ow = out_size(sh[3], op.k, op.stride, 0);
+        if (oh <= 0 || ow <= 0)
+          return fail(RG_ERR_SHAPE, "op %zu (%s): kernel %d larger than padded input", i, op.label.c_str(), op.k);
+        sh = {sh[0], sh[1], oh, ow};
+        break;
+      }
+      case RG_LAYER_FLATTEN: {
+        int64_t rest = 1;
+        for (size_t d = 1; d < sh.size(); ++d) rest *= sh[d];
+        sh = {sh[0], rest};
+        break;
+      }
+      default:
+        break;
+    }
+    os.out = sh;
+    os.out_elems = numel(sh);
+    out.push_back(std::move(os));
+  }
+  return RG_OK;
+}
+
+// Coverage of input rows/cols by a conv (a strided conv may skip pixels, which then
+// do not enter the reference's im2col absmax).
+static std::vector<uint8_t> coverage(int64_t in, int64_t k, int64_t stride, int64_t pad, int64_t out) {
+  std::vector<uint8_t> cov((size_t)in, 0);
+  for (int64_t o = 0; o < out; ++o)
+    for (int64_t t = 0; t < k; ++t) {
+      const int64_t i = o * stride + t - pad;
+      if (i >= 0 && i < in) cov[(size_t)i] = 1;
+    }
+  return cov;
+}
+
+static bool all_covered(const std::vector<uint8_t>& v) {
+  for (uint8_t c : v)
+    if (!c) return false;
+  return true;
+}
+
+struct RunPlan {
+  std::vector<OpShape> shapes;
+  // for every quantizing op: which earlier op writes its absmax (-1: a standalone pass)
+  std::vector<int> amax_src;
+  std::vector<int64_t> amax_slots;   // slots per op (1 or n images)
+  std::vector<int64_t> amax_off;     // offset into the amax / scales buffers
+  std::vector<std::vector<uint8_t>> rowcov, colcov;
+  int64_t total_slots = 0;
+  size_t cov_bytes = 0;
+};
+
+static rg_status make_plan(const Session& s, const int64_t* shape, int32_t ndim, RunPlan& P) {
+  RG_TRY(plan_shapes(s, shape, ndim, P.shapes));
+  const size_t n = s.ops.size();
+  P.amax_src.assign(n, -1);
+  P.amax_slots.assign(n, 0);
+  P.amax_off.assign(n, 0);
+  P.rowcov.assign(n, {});
+  P.colcov.assign(n, {});
+  int64_t off = 0;
+  for (size_t i = 0; i < n; ++i) {
+    const Op& op = s.ops[i];
+    if (op.kind != RG_LAYER_LINEAR && op.kind != RG_LAYER_CONV2D) continue;
+    const OpShape& os = P.shapes[i];
+    P.amax_slots[i] = op.kind == RG_LAYER_LINEAR ? 1 : os.in[0];
+    P.amax_off[i] = off;
+    off += std::max<int64_t>(P.amax_slots[i], 1);
+    bool full = true;
+    if (op.kind == RG_LAYER_CONV2D) {
+      P.rowcov[i] = coverage(os.in[2], op.k, op.stride, op.pad, os.out[2]);
+      P.colcov[i] = coverage(os.in[3], op.k, op.stride, op.pad, os.out[3]);
+      full = all_covered(P.rowcov[i]) && all_covered(P.colcov[i]);
+      if (!full) P.cov_bytes += P.rowcov[i].size() + P.colcov[i].size();
+    }
+    // the producing op (Flatten only reshapes)
+    int j = (int)i - 1;
+    while (j >= 0 && s.ops[(size_t)j].kind == RG_LAYER_FLATTEN) --j;
+    if (j < 0 || !full || (s.flags & RG_SESSION_NO_FUSION)) continue;
+    const int pk = s.ops[(size_t)j].kind;
+    if (pk == RG_LAYER_SOFTMAX && op.kind == RG_LAYER_CONV2D) continue;
+    if (pk == RG_LAYER_LINEAR || pk == RG_LAYER_CONV2D || pk == RG_LAYER_MAXPOOL2D ||
+        pk == RG_LAYER_ACTIVATION || pk == RG_LAYER_SOFTMAX)
+      P.amax_src[i] = j;
+  }
+  P.total_slots = off;
+  return RG_OK;
+}
+
+static int find_consumer(const Session& s, size_t j) {
+  for (size_t i = j + 1; i < s.ops.size(); ++i) {
+    if (s.ops[i].kind == RG_LAYER_FLATTEN) continue;
+    if (s.ops[i].kind == RG_LAYER_LINEAR || s.ops[i].kind == RG_LAYER_CONV2D) return (int)i;
+    return -1;
+  }
+  return -1;
+}
+
+template <class T>
+static rg_status d2h_vec(std::vector<T>& v, const void* src, int64_t n, cudaStream_t st) {
+  v.resize((size_t)std::max<int64_t>(n, 0));
+  if (n > 0) RG_CUDA_TRY(cudaMemcpyAsync(v.data(), src, (size_t)n * sizeof(T), cudaMemcpyDeviceToHost, st));
+  RG_CUDA_TRY(cudaStreamSynchronize(st));
+  return RG_OK;
+}
+
+// Runs the program on device buffers. x_dev is read only; the output is left in
+// the returned pointer (one of the session's activation buffers, or y_dev).
+static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float* y_dev, cudaStream_t st,
+                         bool record_events) {
+  const size_t n = s.ops.size();
+  int64_t max_elems = 1, max_q = 16;
+  for (size_t i = 0; i < n; ++i) {
+    max_elems = std::max(max_elems, P.shapes[i].out_elems);
+    const Op& op = s.ops[i];
+    if (op.kind == RG_LAYER_LINEAR) max_q = std::max(max_q, P.shapes[i].in_elems / op.in_f * op.kpad);
+    if (op.kind == RG_LAYER_CONV2D) max_q = std::max(max_q, P.shapes[i].in_elems);
+  }
+  RG_TRY(s.act0.ensure((size_t)max_elems * 4));
+  RG_TRY(s.act1.ensure((size_t)max_elems * 4));
+  RG_TRY(s.qbuf.ensure((size_t)round_up(max_q, 16) + 64));
+  RG_TRY(s.amax.ensure((size_t)std::max<int64_t>(P.total_slots, 1) * 4));
+  RG_TRY(s.scales.ensure((size_t)std::max<int64_t>(P.total_slots, 1) * 4));
+  if (P.cov_bytes) RG_TRY(s.covbuf.ensure(P.cov_bytes));
+  if (s.trace) {
+    int64_t max_acc = 1;
+    for (size_t i = 0; i < n; ++i)
+      if (s.ops[i].kind == RG_LAYER_LINEAR || s.ops[i].kind == RG_LAYER_CONV2D)
+        max_acc = std::max(max_acc, P.shapes[i].out_elems);
+    RG_TRY(s.accbuf.ensure((size_t)max_acc * 4));
+    s.traces.assign(n, TraceRec());
+  }
+  if (s.events.size() < n + 1) {
+    for (cudaEvent_t e : s.events) cudaEventDestroy(e);
+    s.events.assign(n + 1, nullptr);
+    for (auto& e : s.events) RG_CUDA_TRY(cudaEventCreate(&e));
+  }
+  unsigned* amax = s.amax.as<unsigned>();
+  float* scales = s.scales.as<float>();
+  RG_CUDA_TRY(cudaMemsetAsync(amax, 0, (size_t)std::max<int64_t>(P.total_slots, 1) * 4, st));
+  // coverage masks of strided convs
+  std::vector<const uint8_t*> rc(n, nullptr), cc(n, nullptr);
+  if (P.cov_bytes) {
+    std::vector<uint8_t> host;
+    for (size_t i = 0; i < n; ++i) {
+      if (P.rowcov[i].empty() || (all_covered(P.rowcov[i]) && all_covered(P.colcov[i]))) continue;
+      rc[i] = s.covbuf.as<uint8_t>() + host.size();
+      host.insert(host.end(), P.rowcov[i].begin(), P.rowcov[i].end());
+      cc[i] = s.covbuf.as<uint8_t>() + host.size();
+      host.insert(host.end(), P.colcov[i].begin(), P.colcov[i].end());
+    }
+    RG_CUDA_TRY(cudaMemcpyAsync(s.covbuf.p, host.data(), host.size(), cudaMemcpyHostToDevice, st));
+  }
+
+  const float* cur = x_dev;
+  int32_t launches = 0;
+  if (record_events) RG_CUDA_TRY(cudaEventRecord(s.events[0], st));
+  for (size_t i = 0; i < n; ++i) {
+    const Op& op = s.ops[i];
+    const OpShape& os = P.shapes[i];
+    const bool last = i + 1 == n;
+    float* dst = (cur == s.act0.as<float>()) ? s.act1.as<float>() : s.act0.as<float>();
+    if (last && y_dev) dst = y_dev;
+    // absmax sink for the consumer of this op's output
+    AmaxSink sink;
+    const int cons = find_consumer(s, i);
+    if (cons >= 0 && P.amax_src[(size_t)cons] == (int)i) {
+      sink.ptr = amax + P.amax_off[(size_t)cons];
+      sink.elems_per_slot = s.ops[(size_t)cons].kind == RG_LAYER_CONV2D
+                                ? P.shapes[(size_t)cons].in_elems / P.shapes[(size_t)cons].in[0]
+                                : 0;
+    }
+    switch (op.kind) {
+      case RG_LAYER_LINEAR:
+      case RG_LAYER_CONV2D: {
+        unsigned* my_amax = amax + P.amax_off[i];
+        float* my_scale = scales + P.amax_off[i];
+        int8_t* q = s.qbuf.as<int8_t>();
+        GemmArgs g;
+        if (op.kind == RG_LAYER_LINEAR) {
+          const int64_t rows = os.in_elems / op.in_f;
+          if (P.amax_src[i] < 0) { launch_absmax(cur, os.in_elems, my_amax, st); ++launches; }
+          if (s.comm && s.world > 1)
+            RG_NCCL_TRY(ncclAllReduce(my_amax, my_amax, 1, ncclUint32, ncclMax, s.comm, st));
+          launch_quantize_rows(cur, rows, op.in_f, op.kpad, my_amax, q, my_scale, st);
+          ++launches;
+          g.a = q; g.lda = op.kpad; g.conv = false;
+          g.m = rows; g.n = op.out_f; g.k = op.kpad;
+          g.rows_per_scale = 0;
+          g.out_l = 0;
+        } else {
+          const int64_t N = os.in[0];
+          const int32_t C = op.in_c, H = (int32_t)os.in[2], W = (int32_t)os.in[3];
+          if (P.amax_src[i] < 0) { launch_image_absmax(cur, N, C, H, W, rc[i], cc[i], my_amax, st); ++launches; }
+          launch_image_quantize_nhwc(cur, N, C, H, W, C, my_amax, q, my_scale, st);
+          ++launches;
+          g.a = q; g.conv = true;
+          g.g.h = H; g.g.w = W; g.g.c = C; g.g.cpad = C; g.g.k = op.k; g.g.stride = op.stride; g.g.pad = op.pad;
+          g.g.oh = (int32_t)os.out[2]; g.g.ow = (int32_t)os.out[3];
+          const int64_t L = os.out[2] * os.out[3];
+          g.m = N * L; g.n = op.out_c; g.k = op.kpad;
+          g.rows_per_scale = L;
+          g.out_l = L;
+        }
+        g.w = op.d_w.as<int8_t>(); g.ldb = op.kpad;
+        g.a_scale = my_scale;
+        g.w_scale = op.w_scale;
+        g.w_scale_ch = op.w_scale_ch.empty() ? nullptr : op.d_wsc.as<float>();
+        g.bias = op.d_bias.as<float>();
+        g.act = op.act; g.act_param = op.param;
+        g.out = dst;
+        g.acc = s.trace ? s.accbuf.as<int32_t>() : nullptr;
+        g.amax = sink;
+        if (gemm_tc_eligible(g)) launch_gemm_tc(g, s.num_sms, st);
+        else launch_gemm_simt(g, st);
+        ++launches;
+        RG_CUDA_TRY(cudaGetLastError());
+        if (s.trace) {
+          TraceRec& t = s.traces[i];
+          RG_TRY(d2h_vec(t.scales, my_scale, P.amax_slots[i], st));
+          RG_TRY(d2h_vec(t.acc, s.accbuf.p, os.out_elems, st));
+          if (op.kind == RG_LAYER_LINEAR) {
+            const int64_t rows = os.in_elems / op.in_f;
+            std::vector<int8_t> tmp;
+            RG_TRY(d2h_vec(tmp, q, rows * op.kpad, st));
+            t.aq.resize((size_t)(rows * op.in_f));
+            for (int64_t r = 0; r < rows; ++r)
+              memcpy(&t.aq[(size_t)(r * op.in_f)], &tmp[(size_t)(r * op.kpad)], (size_t)op.in_f);
+          } else {
+            std::vector<int8_t> tmp;
+            RG_TRY(d2h_vec(tmp, q, os.in_elems, st));
+            const int64_t N = os.in[0], C = os.in[1], HW = os.in[2] * os.in[3];
+            t.aq.resize((size_t)os.in_elems);
+            for (int64_t b = 0; b < N; ++b)
+              for (int64_t c = 0; c < C; ++c)
+                for (int64_t p = 0; p < HW; ++p) t.aq[(size_t)((b * C + c) * HW + p)] = tmp[(size_t)((b * HW + p) * C + c)];
+          }
+        }
+        cur = dst;
+        break;
+      }
+      case RG_LAYER_MAXPOOL2D:
+        launch_maxpool2d(cur, os.in[0], (int32_t)os.in[1], (int32_t)os.in[2], (int32_t)os.in[3], op.k,
+                         op.stride, dst, sink, st);
+        ++launches;
+        cur = dst;
+        break;
+      case RG_LAYER_FLATTEN:
+        if (last && y_dev) {
+          RG_CUDA_TRY(cudaMemcpyAsync(y_dev, cur, (size_t)os.out_elems * 4, cudaMemcpyDeviceToDevice, st));
+          cur = y_dev;
+        }
+        break;
+      case RG_LAYER_ACTIVATION:
+        launch_activation(cur, os.in_elems, op.act, op.param, dst, sink, st);
+        ++launches;
+        cur = dst;
+        break;
+      case RG_LAYER_SOFTMAX: {
+        const int64_t lastd = os.in.back();
+        launch_softmax(cur, lastd ? os.in_elems / lastd : 0, lastd, dst, sink, st);
+        ++launches;
+        cur = dst;
+        break;
+      }
+      default:
+        return fail(RG_ERR_UNSUPPORTED, "op %zu: unsupported kind %d", i, op.kind);
+    }
+    RG_CUDA_TRY(cudaGetLastError());
+    if (s.trace) RG_TRY(d2h_vec(s.traces[i].out, cur, os.out_elems, st));
+    if (record_events) RG_CUDA_TRY(cudaEventRecord(s.events[i + 1], st));
+  }
+  s.last.launches = launches;
+  if (y_dev && cur != y_dev) {
+    const int64_t elems = n ? P.shapes.back().out_elems : 0;
+    if (elems) RG_CUDA_TRY(cudaMemcpyAsync(y_dev, cur, (size_t)elems * 4, cudaMemcpyDeviceToDevice, st));
+  }
+  return RG_OK;
+}
+
+static rg_status collect_profile(Session& s, const RunPlan& P, bool have_events, int64_t total_ns) {
+  const size_t n = s.ops.size();
+  s.last.valid = true;
+  s.last.macs.assign(n, 0);
+  s.last.ns.assign(n, 0);
+  s.last.total_macs = 0;
+  for (size_t i = 0; i < n; ++i) {
+    s.last.macs[i] = P.shapes[i].macs;
+    s.last.total_macs += P.shapes[i].macs;
+    if (have_events) {
+      float ms = 0.0f;
+      RG_CUDA_TRY(cudaEventElapsedTime(&ms, s.events[i], s.events[i + 1]));
+      s.last.ns[i] = (int64_t)((double)ms * 1e6);
+    }
+  }
+  s.last.total_ns = total_ns;
+  return RG_OK;
+}
+
+static rg_status check_device(int dev) {
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0)
+    return fail(RG_ERR_NO_DEVICE, "no CUDA device visible (%s); this provider has no CPU fallback",
+                e == cudaSuccess ? "count 0" : cudaGetErrorString(e));
+  if (dev < 0 || dev >= count) return fail(RG_ERR_INVALID_ARG, "device %d out of range (%d visible)", dev, count);
+  cudaDeviceProp prop;
+  RG_CUDA_TRY(cudaGetDeviceProperties(&prop, dev));
+  if (prop.major != 10)
+    return fail(RG_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a only", dev, prop.major,
+                prop.minor);
+  return RG_OK;
+}
+
+// ----------------------------------------------------------------------------
+// RTIM reader (src/save.rs:227-279)
+// ----------------------------------------------------------------------------
+struct RtimLayers {
+  std::vector<rg_layer_spec> specs;
+  std::vector<std::vector<float>> store;
+};
+
+static rg_status read_rtim(const char* path, RtimLayers& out) {
+  FILE* f = fopen(path, "rb");
+  if (!f) return fail(RG_ERR_IO, "cannot open %s", path);
+  std::unique_ptr<FILE, int (*)(FILE*)> guard(f, fclose);
+  auto rd_u32 = [&](uint32_t& v) -> bool {
+    unsigned char b[4];
+    if (fread(b, 1, 4, f) != 4) return false;
+    v = (uint32_t)b[0] | ((uint32_t)b[1] << 8) | ((uint32_t)b[2] << 16) | ((uint32_t)b[3] << 24);
+    return true;
+  };
+  auto rd_f32 = [&](float& v) -> bool {
+    uint32_t u;
+    if (!rd_u32(u)) return false;
+    memcpy(&v, &u, 4);
+    return true;
+  };
+  auto rd_vec = [&](std::vector<float>& v) -> bool {
+    uint32_t n;
+    if (!rd_u32(n)) return false;
+    v.resize(n);
+    for (uint32_t i = 0; i < n; ++i)
+      if (!rd_f32(v[i])) return false;
+    return true;
+  };
+  char magic[4];
+  if (fread(magic, 1, 4, f) != 4 || memcmp(magic, "RTIM", 4) != 0)
+    return fail(RG_ERR_IO, "invalid RTIM model header");
+  uint32_t count;
+  if (!rd_u32(count)) return fail(RG_ERR_IO, "truncated RTIM file");
+  out.store.reserve((size_t)count * 2);
+  for (uint32_t i = 0; i < count; ++i) {
+    uint32_t tag;
+    if (!rd_u32(tag)) return fail(RG_ERR_IO, "truncated RTIM file");
+    rg_layer_spec l;
+    memset(&l, 0, sizeof l);
+    l.kind = (int32_t)tag;
+    uint32_t a = 0, b = 0, c = 0, d = 0, e = 0;
+    bool ok = true;
+    switch (tag) {
+      case 1:
+        ok = rd_u32(a) && rd_u32(b);
+        l.in_features = (int32_t)a; l.out_features = (int32_t)b;
+        break;
+      case 2:
+        ok = rd_u32(a) && rd_u32(b) && rd_u32(c) && rd_u32(d) && rd_u32(e);
+        l.in_channels = (int32_t)a; l.out_channels = (int32_t)b; l.kernel = (int32_t)c;
+        l.stride = (int32_t)d; l.padding = (int32_t)e;
+        break;
+      case 3: break;
+      case 4:
+        ok = rd_u32(a) && rd_u32(b);
+        l.kernel = (int32_t)a; l.stride = (int32_t)b;
+        break;
+      case 5: break;
+      case 6: {
+        float p;
+        ok = rd_u32(a) && rd_f32(p);
+        if (ok && a > 5) return fail(RG_ERR_IO, "unknown activation tag %u", a);
+        l.act = (int32_t)a;
+        l.act_param = a == 5 ? p : 0.0f;
+        break;
+      }
+      case 7: break;
+      default:
+        return fail(RG_ERR_IO, "unknown layer tag %u", tag);
+    }
+    if (ok && (tag == 1 || tag == 2 || tag == 3)) {
+      out.store.emplace_back();
+      std::vector<float>& w = out.store.back();
+      ok = rd_vec(w);
+      out.store.emplace_back();
+      std::vector<float>& bb = out.store.back();
+      ok = ok && rd_vec(bb);
+    }
+    if (!ok) return fail(RG_ERR_IO, "truncated RTIM file");
+    out.specs.push_back(l);
+  }
+  // pointers into store (stable after all pushes)
+  size_t si = 0;
+  for (auto& l : out.specs) {
+    if (l.kind == 1 || l.kind == 2 || l.kind == 3) {
+      l.weight = out.store[si].data(); l.weight_len = (int64_t)out.store[si].size(); ++si;
+      l.bias = out.store[si].data(); l.bias_len = (int64_t)out.store[si].size(); ++si;
+    }
+  }
+  return RG_OK;
+}
+
+}  // namespace rg
+
+// ============================================================================
+// C ABI
+// ============================================================================
+using namespace rg;
+
+struct rg_session {
+  Session s;
+};
+
+extern "C" {
+
+const char* rg_last_error(void) { return g_err.c_str(); }
+
+const char* rg_version(void) { return "rustgears-b200 0.1.0 (sm_100a)"; }
+
+int32_t rg_device_count(void) {
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  int ok = 0;
+  for (int d = 0; d < count; ++d) {
+    cudaDeviceProp p;
+    if (cudaGetDeviceProperties(&p, d) == cudaSuccess && p.major == 10) ++ok;
+  }
+  return ok;
+}
+
+rg_status rg_session_create(const rg_layer_spec* layers, int32_t n_layers, const rg_session_options* opts,
+                            rg_session** out) {
+  if (!out || (n_layers > 0 && !layers) || n_layers < 0) return fail(RG_ERR_INVALID_ARG, "null argument");
+  *out = nullptr;
+  rg_session_options o = {0, RG_PREC_INT8, 0, 0};
+  if (opts) o = *opts;
+  if (o.precision != RG_PREC_INT8)
+    return fail(RG_ERR_UNSUPPORTED, "precision %d: only NpuPrecision::Int8 runs on this provider", o.precision);
+  RG_TRY(check_device(o.device));
+  RG_CUDA_TRY(cudaSetDevice(o.device));
+  std::unique_ptr<rg_session> h(new rg_session());
+  Session& s = h->s;
+  s.device = o.device; s.precision = o.precision; s.weight_quant = o.weight_quant; s.flags = o.flags;
+  RG_CUDA_TRY(cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, o.device));
+  RG_CUDA_TRY(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking));
+  RG_TRY(compile(s, layers, n_layers));
+  *out = h.release();
+  return RG_OK;
+}
+
+rg_status rg_session_create_from_rtim(const char* path, const rg_session_options* opts, rg_session** out) {
+  if (!path || !out) return fail(RG_ERR_INVALID_ARG, "null argument");
+  RtimLayers L;
+  RG_TRY(read_rtim(path, L));
+  return rg_session_create(L.specs.data(), (int32_t)L.specs.size(), opts, out);
+}
+
+void rg_session_destroy(rg_session* h) {
+  if (!h) return;
+  Session& s = h->s;
+  cudaSetDevice(s.device);
+  if (s.stream) cudaStreamSynchronize(s.stream);
+  if (s.comm) ncclCommDestroy(s.comm);
+  for (cudaEvent_t e : s.events) cudaEventDestroy(e);
+  if (s.stream) cudaStreamDestroy(s.stream);
+  delete h;
+}
+
+rg_status rg_session_output_shape(rg_session* h, const int64_t* shape, int32_t ndim, int64_t* y_shape,
+                                  int32_t* y_ndim) {
+  if (!h || !shape || !y_shape || !y_ndim) return fail(RG_ERR_INVALID_ARG, "null argument");
+  std::vector<OpShape> sh;
+  RG_TRY(plan_shapes(h->s, shape, ndim, sh));
+  const std::vector<int64_t> o = sh.empty() ? std::vector<int64_t>(shape, shape + ndim) : sh.back().out;
+  for (size_t i = 0; i < o.size(); ++i) y_shape[i] = o[i];
+  *y_ndim = (int32_t)o.size();
+  return RG_OK;
+}
+
+static rg_status run_impl(rg_session* h, const float* x, bool x_host, const int64_t* shape, int32_t ndim, float* y,
+                          bool y_host, int64_t y_cap, int64_t* y_shape, int32_t* y_ndim, cudaStream_t user_st,
+                          bool async) {
+  if (!h || !x || !shape || !y || !y_shape || !y_ndim) return fail(RG_ERR_INVALID_ARG, "null argument");
+  Session& s = h->s;
+  std::lock_guard<std::mutex> lock(s.mu);
+  RG_CUDA_TRY(cudaSetDevice(s.device));
+  RunPlan P;
+  RG_TRY(make_plan(s, shape, ndim, P));
+  int64_t in_elems = 1;
+  for (int32_t i = 0; i < ndim; ++i) in_elems *= shape[i];
+  const std::vector<int64_t> oshape = P.shapes.empty() ? std::vector<int64_t>(shape, shape + ndim) : P.shapes.back().out;
+  int64_t out_elems = 1;
+  for (int64_t d : oshape) out_elems *= d;
+  if (out_elems > y_cap) return fail(RG_ERR_INVALID_ARG, "output needs %lld elements, capacity %lld",
+                                     (long long)out_elems, (long long)y_cap);
+  cudaStream_t st = user_st ? user_st : s.stream;
+  const bool events = !(s.flags & RG_SESSION_NO_PROFILE);
+  cudaEvent_t t0 = nullptr, t1 = nullptr;
+  if (events) {
+    RG_CUDA_TRY(cudaEventCreate(&t0));
+    RG_CUDA_TRY(cudaEventCreate(&t1));
+    RG_CUDA_TRY(cudaEventRecord(t0, st));
+  }
+  const float* xd = x;
+  if (x_host) {
+    RG_TRY(s.xin.ensure((size_t)std::max<int64_t>(in_elems, 1) * 4));
+    RG_CUDA_TRY(cudaMemcpyAsync(s.xin.p, x, (size_t)in_elems * 4, cudaMemcpyHostToDevice, st));
+    xd = s.xin.as<float>();
+  }
+  float* yd = y;
+  if (y_host) {
+    RG_TRY(s.yout.ensure((size_t)std::max<int64_t>(out_elems, 1) * 4));
+    yd = s.yout.as<float>();
+  }
+  rg_status rs;
+  if (s.ops.empty()) {
+    if (in_elems) RG_CUDA_TRY(cudaMemcpyAsync(yd, xd, (size_t)in_elems * 4, cudaMemcpyDeviceToDevice, st));
+    rs = RG_OK;
+  } else {
+    rs = execute(s, xd, P, yd, st, events);
+  }
+  if (rs != RG_OK) {
+    if (t0) cudaEventDestroy(t0);
+    if (t1) cudaEventDestroy(t1);
+    return rs;
+  }
+  if (y_host && out_elems)
+    RG_CUDA_TRY(cudaMemcpyAsync(y, yd, (size_t)out_elems * 4, cudaMemcpyDeviceToHost, st));
+  if (events) RG_CUDA_TRY(cudaEventRecord(t1, st));
+  for (size_t i = 0; i < oshape.size(); ++i) y_shape[i] = oshape[i];
+  *y_ndim = (int32_t)oshape.size();
+  if (async && !x_host && !y_host && !events && !s.trace) return RG_OK;
+  RG_CUDA_TRY(cudaStreamSynchronize(st));
+  int64_t total_ns = 0;
+  if (events) {
+    float ms = 0;
+    RG_CUDA_TRY(cudaEventElapsedTime(&ms, t0, t1));
+    total_ns = (int64_t)((double)ms * 1e6);
+    cudaEventDestroy(t0);
+    cudaEventDestroy(t1);
+  }
+  return collect_profile(s, P, events && !s.ops.empty(), total_ns);
+}
+
+rg_status rg_session_run(rg_session* h, const float* x, const int64_t* shape, int32_t ndim, float* y, int64_t y_cap,
+                         int64_t* y_shape, int32_t* y_ndim) {
+  return run_impl(h, x, true, shape, ndim, y, true, y_cap, y_shape, y_ndim, nullptr, false);
+}
+
+rg_status rg_session_run_device(rg_session* h, const float* x_dev, const int64_t* shape, int32_t ndim, float* y_dev,
+                                int64_t y_cap, int64_t* y_shape, int32_t* y_ndim, void* stream, int32_t flags) {
+  return run_impl(h, x_dev, false, shape, ndim, y_dev, false, y_cap, y_shape, y_ndim, (cudaStream_t)stream,
+                  (flags & RG_RUN_ASYNC) != 0);
+}
+
+rg_status rg_session_compilation_report(rg_session* h, char* buf, int64_t cap, int64_t* needed) {
+  if (!h) return fail(RG_ERR_INVALID_ARG, "null session");
+  const Session& s = h->s;
+  const float ratio = s.npu_bytes == 0 ? 1.0f : (float)s.fp32_bytes / (float)s.npu_bytes;
+  char head[512];
+  snprintf(head, sizeof head,
+           "InferenceSession [provider = NPU (%s), layers: %d -> %zu fused ops, weights: %lld B -> %lld B (%.2fx compression)]\n  Pipeline: ",
+           s.precision == RG_PREC_INT8 ? "INT8" : "FP16", s.original_layers, s.ops.size(), (long long)s.fp32_bytes,
+           (long long)s.npu_bytes, (double)ratio);
+  std::string r = head;
+  for (size_t i = 0; i < s.ops.size(); ++i) {
+    if (i) r += " -> ";
+    r += s.ops[i].label;
+  }
+  if (needed) *needed = (int64_t)r.size() + 1;
+  if (buf && cap > 0) {
+    const size_t n = std::min<size_t>(r.size(), (size_t)cap - 1);
+    memcpy(buf, r.data(), n);
+    buf[n] = 0;
+  }
+  return RG_OK;
+}
+
+rg_status rg_session_last_profile(rg_session* h, rg_profile* prof, rg_op_record* records, int32_t cap) {
+  if (!h || !prof) return fail(RG_ERR_INVALID_ARG, "null argument");
+  Session& s = h->s;
+  std::lock_guard<std::mutex> lock(s.mu);
+  if (!s.last.valid) return fail(RG_ERR_NO_PROFILE, "no run yet");
+  prof->precision = s.precision;
+  prof->original_layers = s.original_layers;
+  prof->fused_ops = (int32_t)s.ops.size();
+  prof->n_records = (int32_t)s.ops.size();
+  prof->fp32_weight_bytes = s.fp32_bytes;
+  prof->npu_weight_bytes = s.npu_bytes;
+  prof->total_macs = s.last.total_macs;
+  prof->total_time_ns = s.last.total_ns;
+  prof->kernel_launches = s.last.launches;
+  prof->_reserved = 0;
+  if (records)
+    for (int32_t i = 0; i < std::min<int32_t>(cap, (int32_t)s.ops.size()); ++i) {
+      memset(records[i].op, 0, sizeof records[i].op);
+      strncpy(records[i].op, s.ops[(size_t)i].label.c_str(), sizeof(records[i].op) - 1);
+      records[i].macs = s.last.macs[(size_t)i];
+      records[i].duration_ns = s.last.ns[(size_t)i];
+    }
+  return RG_OK;
+}
+
+rg_status rg_session_num_ops(rg_session* h, int32_t* n_ops) {
+  if (!h || !n_ops) return fail(RG_ERR_INVALID_ARG, "null argument");
+  *n_ops = (int32_t)h->s.ops.size();
+  return RG_OK;
+}
+
+rg_status rg_session_op_info(rg_session* h, int32_t i, rg_op_info* info) {
+  if (!h || !info) return fail(RG_ERR_INVALID_ARG, "null argument");
+  if (i < 0 || i >= (int32_t)h->s.ops.size()) return fail(RG_ERR_INVALID_ARG, "op %d out of range", i);
+  const Op& op = h->s.ops[(size_t)i];
+  memset(info, 0, sizeof *info);
+  info->kind = op.kind; info->in_features = op.in_f; info->out_features = op.out_f;
+  info->in_channels = op.in_c; info->out_channels = op.out_c; info->kernel = op.k;
+  info->stride = op.stride; info->padding = op.pad; info->act = op.act; info->act_param = op.param;
+  info->w_scale = op.w_scale; info->wq_len = (int64_t)op.wq.size(); info->bias_len = (int64_t)op.bias.size();
+  strncpy(info->label, op.label.c_str(), sizeof(info->label) - 1);
+  return RG_OK;
+}
+
+rg_status rg_session_op_weights(rg_session* h, int32_t i, int8_t* wq, int64_t cap, float* bias, int64_t bias_cap) {
+  if (!h) return fail(RG_ERR_INVALID_ARG, "null session");
+  if (i < 0 || i >= (int32_t)h->s.ops.size()) return fail(RG_ERR_INVALID_ARG, "op %d out of range", i);
+  const Op& op = h->s.ops[(size_t)i];
+  if (wq) {
+    if (cap < (int64_t)op.wq.size()) return fail(RG_ERR_INVALID_ARG, "weight buffer too small");
+    memcpy(wq, op.wq.data(), op.wq.size());
+  }
+  if (bias) {
+    if (bias_cap < (int64_t)op.bias.size()) return fail(RG_ERR_INVALID_ARG, "bias buffer too small");
+    memcpy(bias, op.bias.data(), op.bias.size() * 4);
+  }
+  return RG_OK;
+}
+
+rg_status rg_session_set_trace(rg_session* h, int32_t enable) {
+  if (!h) return fail(RG_ERR_INVALID_ARG, "null session");
+  std::lock_guard<std::mutex> lock(h->s.mu);
+  h->s.trace = enable != 0;
+  if (!h->s.trace) h->s.traces.clear();
+  return RG_OK;
+}
+
+rg_status rg_session_trace_get(rg_session* h, int32_t op, int32_t item, void* buf, int64_t cap_bytes, int64_t* n_bytes) {
+  if (!h || !n_bytes) return fail(RG_ERR_INVALID_ARG, "null argument");
+  Session& s = h->s;
+  std::lock_guard<std::mutex> lock(s.mu);
+  if (op < 0 || op >= (int32_t)s.traces.size()) return fail(RG_ERR_INVALID_ARG, "no trace for op %d", op);
+  const TraceRec& t = s.traces[(size_t)op];
+  const void* src = nullptr;
+  int64_t bytes = 0;
+  switch (item) {
+    case RG_TRACE_SCALES: src = t.scales.data(); bytes = (int64_t)t.scales.size() * 4; break;
+    case RG_TRACE_AQ: src = t.aq.data(); bytes = (int64_t)t.aq.size(); break;
+    case RG_TRACE_ACC: src = t.acc.data(); bytes = (int64_t)t.acc.size() * 4; break;
+    case RG_TRACE_OUT: src = t.out.data(); bytes = (int64_t)t.out.size() * 4; break;
+    default: return fail(RG_ERR_INVALID_ARG, "unknown trace item %d", item);
+  }
+  *n_bytes = bytes;
+  if (buf) {
+    if (cap_bytes < bytes) return fail(RG_ERR_INVALID_ARG, "trace buffer too small");
+    if (bytes) memcpy(buf, src, (size_t)bytes);
+  }
+  return RG_OK;
+}
+
+rg_status rg_nccl_unique_id(uint8_t id[128]) {
+  if (!id) return fail(RG_ERR_INVALID_ARG, "null argument");
+  ncclUniqueId u;
+  RG_NCCL_TRY(ncclGetUniqueId(&u));
+  static_assert(sizeof(u) == 128, "ncclUniqueId size");
+  memcpy(id, &u, 128);
+  return RG_OK;
+}
+
+rg_status rg_session_attach_comm(rg_session* h, const uint8_t id[128], int32_t rank, int32_t world) {
+  if (!h || !id) return fail(RG_ERR_INVALID_ARG, "null argument");
+  if (world < 1 || rank < 0 || rank >= world) return fail(RG_ERR_INVALID_ARG, "rank %d of %d", rank, world);
+  Session& s = h->s;
+  std::lock_guard<std::mutex> lock(s.mu);
+  RG_CUDA_TRY(cudaSetDevice(s.device));
+  if (s.comm) {
+    ncclCommDestroy(s.comm);
+    s.comm = nullptr;
+  }
+  ncclUniqueId u;
+  memcpy(&u, id, 128);
+  RG_NCCL_TRY(ncclCommInitRank(&s.comm, world, u, rank));
+  s.rank = rank;
+  s.world = world;
+  return RG_OK;
+}
+
+rg_status rg_session_allgather(rg_session* h, const float* send_dev, float* recv_dev, int64_t count, void* stream) {
+  if (!h || !send_dev || !recv_dev) return fail(RG_ERR_INVALID_ARG, "null argument");
+  Session& s = h->s;
+  if (!s.comm) return fail(RG_ERR_INVALID_ARG, "no communicator attached");
+  RG_CUDA_TRY(cudaSetDevice(s.device));
+  cudaStream_t st = stream ? (cudaStream_t)stream : s.stream;
+  RG_NCCL_TRY(ncclAllGather(send_dev, recv_dev, (size_t)count, ncclFloat32, s.comm, st));
+  RG_CUDA_TRY(cudaStreamSynchronize(st));
+  return RG_OK;
+}
+
+// ---- kernel-level entry points ---------------------------------------------------
+rg_status rg_absmax_f32(const float* x, int64_t n, float* amax, void* stream) {
+  if ((!x && n > 0) || !amax || n < 0) return fail(RG_ERR_INVALID_ARG, "null argument");
+  cudaStream_t st = (cudaStream_t)stream;
+  RG_CUDA_TRY(cudaMemsetAsync(amax, 0, 4, st));
+  launch_absmax(x, n, reinterpret_cast<unsigned*>(amax), st);
+  RG_CUDA_TRY(cudaGetLastError());
+  return RG_OK;
+}
+
+rg_status rg_quantize_f32_i8(const float* x, int64_t rows, int64_t k, int64_t ldq, const float* amax, int8_t* q,
+                             float* scale, void* stream) {
+  if (!x || !amax || !q || rows < 0 || k <= 0 || ldq < k || (ldq & 15))
+    return fail(RG_ERR_INVALID_ARG, "bad quantize arguments (ldq must be a multiple of 16 and >= k)");
+  launch_quantize_rows(x, rows, k, ldq, reinterpret_cast<const unsigned*>(amax), q, scale, (cudaStream_t)stream);
+  RG_CUDA_TRY(cudaGetLastError());
+  return RG_OK;
+}
+
+static rg_status gemm_args_check(const int8_t* a, const int8_t* w, int64_t m, int64_t n, int64_t ld,
+                                 const float* a_scale, const float* bias, float* out) {
+  if (!a || !w || !a_scale || !bias || !out) return fail(RG_ERR_INVALID_ARG, "null argument");
+  if (m < 0 || n <= 0 || ld <= 0 || (ld & 15)) return fail(RG_ERR_INVALID_ARG, "ld must be a positive multiple of 16");
+  if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
+    return fail(RG_ERR_INVALID_ARG, "operands must be 16-byte aligned");
+  return RG_OK;
+}
+
+rg_status rg_gemm_i8_fused(const int8_t* a, const int8_t* w, int64_t m, int64_t n, int64_t ld, const float* a_scale,
+                           float w_scale, const float* bias, int32_t act, float act_param, float* out, int32_t* acc,
+                           float* out_amax, void* stream) {
+  RG_TRY(gemm_args_check(a, w, m, n, ld, a_scale, bias, out));
+  if (act < RG_ACT_NONE || act > RG_ACT_LEAKY_RELU) return fail(RG_ERR_INVALID_ARG, "unknown activation %d", act);
+  GemmArgs g;
+  g.a = a; g.lda = ld; g.w = w; g.ldb = ld; g.m = m; g.n = n; g.k = ld;
+  g.a_scale = a_scale; g.w_scale = w_scale; g.bias = bias; g.act = act; g.act_param = act_param;
+  g.out = out; g.acc = acc;
+  g.amax.ptr = reinterpret_cast<unsigned*>(out_amax);
+  int dev = 0, sms = 148;
+  RG_CUDA_TRY(cudaGetDevice(&dev));
+  RG_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  if (gemm_tc_eligible(g)) launch_gemm_tc(g, sms, (cudaStream_t)stream);
+  else launch_gemm_simt(g, (cudaStream_t)stream);
+  RG_CUDA_TRY(cudaGetLastError());
+  return RG_OK;
+}
+
+int64_t rg_linear_i8_workspace_size(int64_t m, int64_t ld) { return round_up(m * ld, 256) + 256; }
+
+rg_status rg_linear_i8(const float* x, int64_t m, int64_t k, const int8_t* w, int64_t n, int64_t ld, float w_scale,
+                       const float* bias, int32_t act, float act_param, float* out, void* workspace, void* stream) {
+  if (!x || !workspace || k <= 0 || ld < k) return fail(RG_ERR_INVALID_ARG, "bad linear arguments");
+  cudaStream_t st = (cudaStream_t)stream;
+  int8_t* q = reinterpret_cast<int8_t*>(workspace);
+  unsigned* amax = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(workspace) + round_up(m * ld, 256));
+  float* scale = reinterpret_cast<float*>(amax + 1);
+  RG_CUDA_TRY(cudaMemsetAsync(amax, 0, 4, st));
+  launch_absmax(x, m * k, amax, st);
+  RG_TRY(rg_quantize_f32_i8(x, m, k, ld, reinterpret_cast<float*>(amax), q, scale, stream));
+  return rg_gemm_i8_fused(q, w, m, n, ld, scale, w_scale, bias, act, act_param, out, nullptr, nullptr, stream);
+}
+
+rg_status rg_maxpool2d_f32(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t k, int32_t stride,
+                           float* y, void* stream) {
+  if (!x || !y || k <= 0 || stride <= 0 || h < k || w < k) return fail(RG_ERR_INVALID_ARG, "bad pool arguments");
+  launch_maxpool2d(x, n, c, h, w, k, stride, y, AmaxSink(), (cudaStream_t)stream);
+  RG_CUDA_TRY(cudaGetLastError());
+  return RG_OK;
+}
+
+rg_status rg_softmax_f32(const float* x, int64_t outer, int64_t last, float* y, void* stream) {
+  if (!x || !y) return fail(RG_ERR_INVALID_ARG, "null argument");
+  launch_softmax(x, outer, last, y, AmaxSink(), (cudaStream_t)stream);
+  RG_CUDA_TRY(cudaGetLastError());
+  return RG_OK;
+}
+
+rg_status rg_activation_f32(const float* x, int64_t n, int32_t act, float act_param, float* y, void* stream) {
+  if (!x || !y) return fail(RG_ERR_INVALID_ARG, "null argument");
+  if (act < RG_ACT_NONE || act > RG_ACT_LEAKY_RELU) return fail(RG_ERR_INVALID_ARG, "unknown activation %d", act);
+  launch_activation(x, n, act, act_param, y, AmaxSink(), (cudaStream_t)stream);
+  RG_CUDA_TRY(cudaGetLastError());
+  return RG_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,76 @@
+// rg_kernels.h -- launchers of the device kernels (internal to librg_npu.so).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rg {
+
+// Where the absmax of an op's output goes (the next quantizing op's input scale).
+struct AmaxSink {
+  unsigned* ptr = nullptr;   // float bits of max|x| (non-negative floats order like uints)
+  int64_t elems_per_slot = 0;  // 0: one slot for the whole tensor; else slot = elem / elems_per_slot
+};
+
+// ---- quantization (k_quant.cu) ------------------------------------------------
+// amax_bits[0] = max |x| (NaN ignored). Caller zeroes amax_bits first.
+void launch_absmax(const float* x, int64_t n, unsigned* amax_bits, cudaStream_t st);
+// x [rows,k] f32 -> q [rows,ldq] i8 with the per-tensor scale from amax_bits; scale_out[0] = scale.
+void launch_quantize_rows(const float* x, int64_t rows, int64_t k, int64_t ldq,
+                          const unsigned* amax_bits, int8_t* q, float* scale_out, cudaStream_t st);
+// Per-image absmax over the pixels a conv actually reads (row/col coverage masks; NULL = all).
+void launch_image_absmax(const float* x, int64_t n, int32_t c, int32_t h, int32_t w,
+                         const uint8_t* row_cov, const uint8_t* col_cov, unsigned* amax_bits,
+                         cudaStream_t st);
+// NCHW f32 -> NHWC i8 (channels padded to cpad with zeros) with per-image scales.
+void launch_image_quantize_nhwc(const float* x, int64_t n, int32_t c, int32_t h, int32_t w,
+                                int32_t cpad, const unsigned* amax_bits, int8_t* q,
+                                float* scales_out, cudaStream_t st);
+// NHWC i8 (cpad) -> NCHW i8 (c) for traces.
+void launch_nhwc_to_nchw_i8(const int8_t* q, int64_t n, int32_t c, int32_t cpad, int32_t h,
+                            int32_t w, int8_t* out, cudaStream_t st);
+
+// ---- GEMM (k_gemm_simt.cu, k_gemm_tc.cu) ---------------------------------------
+struct ConvGeom {      // implicit-GEMM A operand: rows = (img, oy, ox), k = (ky, kx, c)
+  int32_t h = 0, w = 0, c = 0, cpad = 0, k = 0, stride = 1, pad = 0, oh = 0, ow = 0;
+};
+
+struct GemmArgs {
+  // A: dense i8 [m, lda] (conv == false) or gathered from NHWC i8 (conv == true)
+  const int8_t* a = nullptr;
+  int64_t lda = 0;
+  bool conv = false;
+  ConvGeom g;
+  // B: weights [n, ldb] i8, K-contiguous (ldb multiple of 16, zero-padded)
+  const int8_t* w = nullptr;
+  int64_t ldb = 0;
+  int64_t m = 0, n = 0, k = 0;   // k = padded reduction length (multiple of 16)
+  // epilogue
+  const float* a_scale = nullptr;  // device; index = row / rows_per_scale
+  int64_t rows_per_scale = 0;      // 0: one scale for all rows
+  float w_scale = 1.0f;
+  const float* w_scale_ch = nullptr;  // per-output-channel weight scales (extension), or NULL
+  const float* bias = nullptr;
+  int32_t act = 0;
+  float act_param = 0.0f;
+  float* out = nullptr;
+  int64_t out_l = 0;               // 0: row-major [m,n]; L>0: NCHW out[(r/L)*n*L + c*L + r%L]
+  int32_t* acc = nullptr;          // optional i32 dump, same layout as out
+  AmaxSink amax;                   // optional absmax of out
+};
+
+void launch_gemm_simt(const GemmArgs& a, cudaStream_t st);
+// tcgen05 path; returns false when the shape is not eligible.
+bool gemm_tc_eligible(const GemmArgs& a);
+void launch_gemm_tc(const GemmArgs& a, int num_sms, cudaStream_t st);
+
+// ---- misc (k_misc.cu) ----------------------------------------------------------
+void launch_maxpool2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t k,
+                      int32_t s, float* y, AmaxSink amax, cudaStream_t st);
+void launch_activation(const float* x, int64_t n, int32_t act, float p, float* y, AmaxSink amax,
+                       cudaStream_t st);
+void launch_softmax(const float* x, int64_t outer, int64_t last, float* y, AmaxSink amax,
+                    cudaStream_t st);
+void launch_fill_u32(unsigned* p, unsigned v, int64_t n, cudaStream_t st);
+void launch_bits_to_float(const unsigned* bits, float* out, int64_t n, cudaStream_t st);
+
+}  // namespace rg

@@ -1,0 +1,282 @@
+// rg_math.cuh -- scalar arithmetic of the Npu(Int8) path, shared by every kernel.
+//
+// Every function reproduces the reference's f32 arithmetic operation by
+// operation (round-to-nearest, no contraction: the library is compiled with
+// -fmad=false and the critical steps use explicit __f*_rn intrinsics), so
+// the device results are bit-identical to the reference CPU path.
+//
+// Transcendentals: the reference calls Rust's f32::tanh / f32::exp, i.e.
+// glibc 2.39's tanhf / expf on x86-64 linux-gnu.  glibc is not correctly
+// rounded (tanhf differs from the correctly rounded result on ~2.8% of all
+// floats), so the device uses restatements of glibc's own published methods:
+//   * tanhf: the fdlibm method (Sun Microsystems, 1993), tanh via expm1 with
+//     expm1 by argument reduction x = k ln2 + r and a rational approximation
+//     of r (e^r + 1)/(e^r - 1);
+//   * expf: the method of ARM's optimized-routines (Szabolcs Nagy, 2017) that
+//     glibc ships since 2.27: x/ln2 split into k/32 + r, 2^(k/32) from a
+//     32-entry table, a cubic for 2^r evaluated in double.  On x86-64 CPUs
+//     with FMA glibc selects its FMA build, whose rounding the fma() calls
+//     below reproduce.
+// Both restatements match glibc 2.39 on all 2^32 f32 inputs (checked
+// exhaustively on the host); the GPU tests re-check them on the device.
+#pragma once
+#include <stdint.h>
+
+#ifdef __CUDACC__
+#define RG_HD __host__ __device__ __forceinline__
+#else
+#define RG_HD inline
+#endif
+
+namespace rg {
+
+enum : int32_t { ACT_NONE = 0, ACT_RELU = 1, ACT_SIGMOID = 2, ACT_TANH = 3, ACT_GELU = 4,
+                 ACT_LEAKY_RELU = 5 };
+
+RG_HD uint32_t f2u(float f) {
+#ifdef __CUDA_ARCH__
+  return __float_as_uint(f);
+#else
+  union { float f; uint32_t u; } v; v.f = f; return v.u;
+#endif
+}
+RG_HD float u2f(uint32_t u) {
+#ifdef __CUDA_ARCH__
+  return __uint_as_float(u);
+#else
+  union { float f; uint32_t u; } v; v.u = u; return v.f;
+#endif
+}
+RG_HD uint64_t d2u(double d) {
+#ifdef __CUDA_ARCH__
+  return (uint64_t)__double_as_longlong(d);
+#else
+  union { double d; uint64_t u; } v; v.d = d; return v.u;
+#endif
+}
+RG_HD double u2d(uint64_t u) {
+#ifdef __CUDA_ARCH__
+  return __longlong_as_double((long long)u);
+#else
+  union { double d; uint64_t u; } v; v.u = u; return v.d;
+#endif
+}
+
+#ifdef __CUDA_ARCH__
+#define RG_MUL(a, b) __fmul_rn((a), (b))
+#define RG_ADD(a, b) __fadd_rn((a), (b))
+#define RG_SUB(a, b) __fsub_rn((a), (b))
+#define RG_DIV(a, b) __fdiv_rn((a), (b))
+#else
+#define RG_MUL(a, b) ((a) * (b))
+#define RG_ADD(a, b) ((a) + (b))
+#define RG_SUB(a, b) ((a) - (b))
+#define RG_DIV(a, b) ((a) / (b))
+#endif
+
+RG_HD float fmax_ignore_nan(float a, float b) { return fmaxf(a, b); }  // IEEE maxNum == f32::max
+
+// expm1 for the tanh argument range (|x| < 44); fdlibm method, f32 steps.
+RG_HD float expm1_f32(float x) {
+  const float ln2_hi = u2f(0x3f317180u), ln2_lo = u2f(0x3717f7d1u), invln2 = u2f(0x3fb8aa3bu);
+  const float q1 = u2f(0xbd088889u), q2 = u2f(0x3ad00d01u), q3 = u2f(0xb8a670cdu),
+              q4 = u2f(0x36867e54u), q5 = u2f(0xb457edbbu);
+  uint32_t hx = f2u(x);
+  const bool neg = (hx >> 31) != 0;
+  hx &= 0x7fffffffu;
+  if (hx >= 0x4195b844u) {  // |x| >= 27 ln2: saturates to -1 (negative side); tanh never asks above
+    if (hx > 0x7f800000u) return RG_ADD(x, x);
+    if (neg) return -1.0f;
+  }
+  float hi, lo, c = 0.0f, t;
+  int k;
+  if (hx > 0x3eb17218u) {                          // |x| > ln2 / 2: reduce
+    if (hx < 0x3F851592u) {                        // |x| < 3 ln2 / 2
+      if (!neg) { hi = RG_SUB(x, ln2_hi); lo = ln2_lo; k = 1; }
+      else { hi = RG_ADD(x, ln2_hi); lo = -ln2_lo; k = -1; }
+    } else {
+      k = (int)RG_ADD(RG_MUL(invln2, x), neg ? -0.5f : 0.5f);
+      t = (float)k;
+      hi = RG_SUB(x, RG_MUL(t, ln2_hi));
+      lo = RG_MUL(t, ln2_lo);
+    }
+    x = RG_SUB(hi, lo);
+    c = RG_SUB(RG_SUB(hi, x), lo);
+  } else if (hx < 0x33000000u) {
+    return x;                                      // |x| < 2^-25
+  } else {
+    k = 0;
+  }
+  const float hfx = RG_MUL(0.5f, x);
+  const float hxs = RG_MUL(x, hfx);
+  float r1 = RG_MUL(hxs, q5);
+  r1 = RG_MUL(hxs, RG_ADD(q4, r1));
+  r1 = RG_MUL(hxs, RG_ADD(q3, r1));
+  r1 = RG_MUL(hxs, RG_ADD(q2, r1));
+  r1 = RG_MUL(hxs, RG_ADD(q1, r1));
+  r1 = RG_ADD(1.0f, r1);
+  t = RG_SUB(3.0f, RG_MUL(r1, hfx));
+  float e = RG_MUL(hxs, RG_DIV(RG_SUB(r1, t), RG_SUB(6.0f, RG_MUL(x, t))));
+  if (k == 0) return RG_SUB(x, RG_SUB(RG_MUL(x, e), hxs));
+  e = RG_SUB(RG_MUL(x, RG_SUB(e, c)), c);
+  e = RG_SUB(e, hxs);
+  if (k == -1) return RG_SUB(RG_MUL(0.5f, RG_SUB(x, e)), 0.5f);
+  if (k == 1) {
+    if (x < -0.25f) return RG_MUL(-2.0f, RG_SUB(e, RG_ADD(x, 0.5f)));
+    return RG_ADD(1.0f, RG_MUL(2.0f, RG_SUB(x, e)));
+  }
+  float y;
+  if (k <= -2 || k > 56) {
+    y = RG_SUB(1.0f, RG_SUB(e, x));
+    y = u2f(f2u(y) + ((uint32_t)k << 23));
+    return RG_SUB(y, 1.0f);
+  }
+  if (k < 23) {
+    t = u2f(0x3f800000u - (0x1000000u >> k));     // 1 - 2^-k
+    y = RG_SUB(t, RG_SUB(e, x));
+  } else {
+    t = u2f((uint32_t)(0x7f - k) << 23);           // 2^-k
+    y = RG_SUB(x, RG_ADD(e, t));
+    y = RG_ADD(y, 1.0f);
+  }
+  return u2f(f2u(y) + ((uint32_t)k << 23));
+}
+
+// tanh, glibc/fdlibm method (identical on all 2^32 inputs to glibc 2.39 tanhf).
+RG_HD float tanh_f32(float x) {
+  const uint32_t jx = f2u(x), ix = jx & 0x7fffffffu;
+  if (ix >= 0x7f800000u) {                         // inf or NaN
+    return (jx >> 31) ? RG_SUB(RG_DIV(1.0f, x), 1.0f) : RG_ADD(RG_DIV(1.0f, x), 1.0f);
+  }
+  float z;
+  if (ix < 0x41b00000u) {                          // |x| < 22
+    if (ix < 0x24000000u) return RG_MUL(x, RG_ADD(1.0f, x));  // |x| < 2^-55
+    if (ix >= 0x3f800000u) {                       // |x| >= 1
+      const float t = expm1_f32(RG_MUL(2.0f, fabsf(x)));
+      z = RG_SUB(1.0f, RG_DIV(2.0f, RG_ADD(t, 2.0f)));
+    } else {
+      const float t = expm1_f32(RG_MUL(-2.0f, fabsf(x)));
+      z = RG_DIV(-t, RG_ADD(t, 2.0f));
+    }
+  } else {
+    z = 1.0f;
+  }
+  return (jx >> 31) ? -z : z;
+}
+
+// 2^(i/32) rounded to double, minus i << 47 (the table of the expf method).
+#define RG_EXP2_TABLE                                                                  \
+  {0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full,                 \
+   0x3fef9301d0125b51ull, 0x3fef72b83c7d517bull, 0x3fef54873168b9aaull,                 \
+   0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull, 0x3fef06fe0a31b715ull,                 \
+   0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,                 \
+   0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull,                 \
+   0x3feea47eb03a5585ull, 0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull,                 \
+   0x3feea11473eb0187ull, 0x3feea589994cce13ull, 0x3feeace5422aa0dbull,                 \
+   0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,                 \
+   0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull,                 \
+   0x3fef3720dcef9069ull, 0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full,                 \
+   0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull}
+
+#ifdef __CUDACC__
+static __constant__ const uint64_t k_exp2_table[32] = RG_EXP2_TABLE;
+#endif
+static const uint64_t h_exp2_table[32] = RG_EXP2_TABLE;
+#ifdef __CUDA_ARCH__
+#define RG_EXP2_T(i) k_exp2_table[(i)]
+#else
+#define RG_EXP2_T(i) h_exp2_table[(i)]
+#endif
+
+// exp, optimized-routines method in its FMA form (identical on all 2^32 inputs to glibc 2.39 expf
+// on an x86-64 CPU with FMA).
+RG_HD float exp_f32(float x) {
+  const uint32_t ax = f2u(x) & 0x7fffffffu;
+  if (ax >= 0x42b00000u) {                         // |x| >= 88
+    if (f2u(x) == 0xff800000u) return 0.0f;
+    if (ax >= 0x7f800000u) return RG_ADD(x, x);
+    if (x > u2f(0x42b17217u)) return u2f(0x7f800000u);
+    if (x < -u2f(0x42cff1b4u)) return 0.0f;
+  }
+  const double inv_ln2_n = 0x1.71547652b82fep+0 * 32.0;
+  const double shift = 0x1.8p+52;
+  const double c0 = 0x1.c6af84b912394p-5 / 32.0 / 32.0 / 32.0;
+  const double c1 = 0x1.ebfce50fac4f3p-3 / 32.0 / 32.0;
+  const double c2 = 0x1.62e42ff0c52d6p-1 / 32.0;
+  const double xd = (double)x;
+#ifdef __CUDA_ARCH__
+  const double z = __dmul_rn(inv_ln2_n, xd);
+  double kd = __dadd_rn(z, shift);
+  const uint64_t ki = d2u(kd);
+  kd = __dsub_rn(kd, shift);
+#else
+  volatile double zv = inv_ln2_n * xd;
+  const double z = zv;
+  volatile double kdv = z + shift;
+  double kd = kdv;
+  const uint64_t ki = d2u(kd);
+  kd = kd - shift;
+#endif
+  (void)z;
+  const double r = fma(inv_ln2_n, xd, -kd);
+  uint64_t t = RG_EXP2_T(ki % 32);
+  t += ki << (52 - 5);
+  const double s = u2d(t);
+  const double zz = fma(c0, r, c1);
+#ifdef __CUDA_ARCH__
+  const double r2 = __dmul_rn(r, r);
+#else
+  const double r2 = r * r;
+#endif
+  double y = fma(c2, r, 1.0);
+  y = fma(zz, r2, y);
+#ifdef __CUDA_ARCH__
+  y = __dmul_rn(y, s);
+  return __double2float_rn(y);
+#else
+  y = y * s;
+  return (float)y;
+#endif
+}
+
+// Activation::apply (src/inference/mod.rs:38-53, src/device/backend.rs:61-78).
+RG_HD float act_apply(int32_t act, float p, float x) {
+  switch (act) {
+    case ACT_RELU: return fmaxf(x, 0.0f);                       // x.max(0.0): NaN -> 0
+    case ACT_SIGMOID: return RG_DIV(1.0f, RG_ADD(1.0f, exp_f32(-x)));
+    case ACT_TANH: return tanh_f32(x);
+    case ACT_GELU: {
+      const float gelu_c = 0.7978846f;                           // GELU_C (backend.rs:61)
+      float c = RG_MUL(0.044715f, x);
+      c = RG_MUL(c, x);
+      c = RG_MUL(c, x);
+      const float t = tanh_f32(RG_MUL(gelu_c, RG_ADD(x, c)));
+      return RG_MUL(RG_MUL(0.5f, x), RG_ADD(1.0f, t));
+    }
+    case ACT_LEAKY_RELU: return x > 0.0f ? x : RG_MUL(p, x);
+    default: return x;
+  }
+}
+
+// QuantTensor scale from an absmax (quantize.rs:20) and its reciprocal (quantize.rs:21).
+RG_HD float quant_scale(float amax) { return amax < 1e-12f ? 1.0f : RG_DIV(amax, 127.0f); }
+RG_HD float quant_inv(float scale) { return RG_DIV(1.0f, scale); }
+
+// (v * inv).round().clamp(-127, 127) as i8 (quantize.rs:22): half away from zero, NaN -> 0.
+RG_HD int32_t quant1(float v, float inv) {
+  const float t = roundf(RG_MUL(v, inv));
+  if (t != t) return 0;
+  return (int32_t)fminf(fmaxf(t, -127.0f), 127.0f);
+}
+
+// Epilogue of int8_gemm_fused (quantize.rs:109-111): act((acc as f32) * cs + bias).
+RG_HD float epilogue(int32_t acc, float cs, float bias, int32_t act, float p) {
+#ifdef __CUDA_ARCH__
+  const float a = __int2float_rn(acc);
+#else
+  const float a = (float)acc;
+#endif
+  return act_apply(act, p, RG_ADD(RG_MUL(a, cs), bias));
+}
+
+}  // namespace rg

@@ -1,0 +1,208 @@
+"""Model-side builders whose ``export()`` yields the reference's ``LayerSpec``s.
+
+Construction draws weights from the global generator in the reference's
+order (``Linear::new`` weight then bias, nn/layers.rs:27-34; ``Conv2d::new``,
+108-119; kaiming/bias bounds, nn/init.rs:6-26), so ``manual_seed(s)`` followed
+by the same ``Sequential`` gives bit-identical parameters.  Only inference
+export lives here: forward/backward training code is the reference's.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import rng
+from .spec import Activation, ActivationLayer, ChannelAffine, Conv2d as Conv2dSpec, Flatten as FlattenSpec
+from .spec import Linear as LinearSpec, MaxPool2d as MaxPool2dSpec, Softmax as SoftmaxSpec
+
+
+class Module:
+    """`Module` trait subset used by `InferenceSession::from_module` (nn/mod.rs:26-68)."""
+
+    training = True
+
+    def name(self) -> str:
+        return type(self).__name__
+
+    def set_training(self, t: bool) -> None:
+        self.training = t
+
+    def eval(self) -> None:
+        self.set_training(False)
+
+    def train(self) -> None:
+        self.set_training(True)
+
+    def export(self):
+        raise NotImplementedError(f"layer '{self.name()}' does not support export")
+
+
+class Sequential(Module):
+    def __init__(self, *layers):
+        self.layers = list(layers)
+
+    def add(self, layer: Module) -> "Sequential":
+        self.layers.append(layer)
+        return self
+
+    def set_training(self, t: bool) -> None:
+        for l in self.layers:
+            l.set_training(t)
+
+    def export(self):  # nn/mod.rs:204-210
+        out = []
+        for l in self.layers:
+            out.extend(l.export())
+        return out
+
+
+class Linear(Module):
+    """Weight [in, out] (kaiming uniform), bias [out] (bias uniform)."""
+
+    def __init__(self, in_features: int, out_features: int, weight=None, bias=None):
+        self.in_features, self.out_features = in_features, out_features
+        self.weight = (np.asarray(weight, np.float32).reshape(in_features, out_features) if weight is not None
+                       else rng.kaiming_uniform((in_features, out_features), in_features))
+        if bias is not None:
+            self.bias = np.asarray(bias, np.float32).reshape(out_features)
+        elif weight is None:
+            self.bias = rng.bias_uniform((out_features,), in_features)
+        else:
+            self.bias = None
+
+    @classmethod
+    def no_bias(cls, in_features: int, out_features: int) -> "Linear":
+        l = cls(in_features, out_features)
+        l.bias = None
+        return l
+
+    def name(self) -> str:
+        return f"Linear({self.in_features}, {self.out_features})"
+
+    def export(self):  # nn/layers.rs:74-81
+        b = self.bias if self.bias is not None else np.zeros(self.out_features, np.float32)
+        return [LinearSpec(self.in_features, self.out_features, self.weight, b)]
+
+
+class Conv2d(Module):
+    def __init__(self, in_channels: int, out_channels: int, kernel_size: int, weight=None, bias=None):
+        fan_in = in_channels * kernel_size * kernel_size
+        self.in_channels, self.out_channels, self.kernel_size = in_channels, out_channels, kernel_size
+        self.stride_, self.padding_ = 1, 0
+        self.weight = (np.asarray(weight, np.float32).reshape(out_channels, in_channels, kernel_size, kernel_size)
+                       if weight is not None else
+                       rng.kaiming_uniform((out_channels, in_channels, kernel_size, kernel_size), fan_in))
+        self.bias = (np.asarray(bias, np.float32).reshape(out_channels) if bias is not None
+                     else rng.bias_uniform((out_channels,), fan_in))
+
+    def stride(self, s: int) -> "Conv2d":
+        self.stride_ = s
+        return self
+
+    def padding(self, p: int) -> "Conv2d":
+        self.padding_ = p
+        return self
+
+    def export(self):  # nn/layers.rs:151-161
+        return [Conv2dSpec(self.in_channels, self.out_channels, self.kernel_size, self.stride_, self.padding_,
+                           self.weight, self.bias)]
+
+
+class BatchNorm(Module):
+    """Exported as ``ChannelAffine`` (nn/norm.rs:335-343): scale = g / sqrt(rv + eps)."""
+
+    def __init__(self, num_features: int, spatial: bool = False):
+        self.num_features = num_features
+        self.spatial = spatial
+        self.gamma = np.ones(num_features, np.float32)
+        self.beta = np.zeros(num_features, np.float32)
+        self.running_mean = np.zeros(num_features, np.float32)
+        self.running_var = np.ones(num_features, np.float32)
+        self.eps = np.float32(1e-5)
+
+    def name(self) -> str:
+        return f"BatchNorm{'2d' if self.spatial else '1d'}({self.num_features})"
+
+    def export(self):
+        scale = (self.gamma / np.sqrt((self.running_var + self.eps).astype(np.float32))).astype(np.float32)
+        shift = (self.beta - (self.running_mean * scale).astype(np.float32)).astype(np.float32)
+        return [ChannelAffine(scale, shift)]
+
+
+def BatchNorm1d(num_features: int) -> BatchNorm:
+    return BatchNorm(num_features, False)
+
+
+def BatchNorm2d(num_features: int) -> BatchNorm:
+    return BatchNorm(num_features, True)
+
+
+class MaxPool2d(Module):
+    def __init__(self, kernel: int, stride: int | None = None):
+        self.kernel, self.stride = kernel, kernel if stride is None else stride
+
+    def export(self):
+        return [MaxPool2dSpec(self.kernel, self.stride)]
+
+
+class Flatten(Module):
+    def export(self):
+        return [FlattenSpec()]
+
+
+class Identity(Module):
+    def export(self):
+        return []
+
+
+class Dropout(Module):
+    def __init__(self, p: float):
+        self.p = p
+
+    def export(self):  # inference is the identity (nn/layers.rs:411-413)
+        return []
+
+
+class _Act(Module):
+    ACT = Activation.NONE
+
+    def export(self):
+        return [ActivationLayer(self.ACT)]
+
+
+class Relu(_Act):
+    ACT = Activation.RELU
+
+
+class Sigmoid(_Act):
+    ACT = Activation.SIGMOID
+
+
+class Tanh(_Act):
+    ACT = Activation.TANH
+
+
+class Gelu(_Act):
+    ACT = Activation.GELU
+
+
+class LeakyRelu(Module):
+    def __init__(self, slope: float):
+        self.slope = slope
+
+    def export(self):
+        return [ActivationLayer(Activation.leaky_relu(self.slope))]
+
+
+class Softmax(Module):
+    def export(self):
+        return [SoftmaxSpec()]
+
+
+def draw_bn_stats(model: Module, mean_range=(-0.1, 0.1), var_range=(0.5, 1.5)) -> None:
+    """Seeded BatchNorm running statistics (benchmark configurations): for each
+    BatchNorm in order, running_mean ~ U(mean_range) then running_var ~ U(var_range)."""
+    layers = model.layers if isinstance(model, Sequential) else [model]
+    for l in layers:
+        if isinstance(l, BatchNorm):
+            l.running_mean = rng.uniform((l.num_features,), *mean_range)
+            l.running_var = rng.uniform((l.num_features,), *var_range)

@@ -1,0 +1,152 @@
+"""The portable layer IR: ``LayerSpec`` and ``Activation``
+(src/inference/mod.rs:24-100), with the reference's Display strings."""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+
+LINEAR, CONV2D, CHANNEL_AFFINE, MAXPOOL2D, FLATTEN, ACTIVATION, SOFTMAX = 1, 2, 3, 4, 5, 6, 7
+
+
+def _fmt_f32(v: float) -> str:
+    """Rust `{}` of an f32: the shortest decimal that round-trips, no exponent."""
+    f = np.float32(v)
+    for prec in range(0, 61):
+        s = f"{float(f):.{prec}f}"
+        if np.float32(float(s)) == f:
+            return s
+    return repr(float(f))
+
+
+class Activation:
+    """`Activation` enum (mod.rs:24-33); codes are the .rtim tags (save.rs:206-214)."""
+
+    NONE_CODE, RELU_CODE, SIGMOID_CODE, TANH_CODE, GELU_CODE, LEAKY_RELU_CODE = range(6)
+    _NAMES = {0: "none", 1: "ReLU", 2: "Sigmoid", 3: "Tanh", 4: "GELU"}
+
+    __slots__ = ("code", "param")
+
+    def __init__(self, code: int, param: float = 0.0):
+        if code not in range(6):
+            raise ValueError(f"unknown activation tag {code}")
+        self.code = int(code)
+        self.param = float(np.float32(param)) if code == 5 else 0.0
+
+    @classmethod
+    def leaky_relu(cls, slope: float) -> "Activation":
+        return cls(5, slope)
+
+    def __eq__(self, other):
+        return isinstance(other, Activation) and (self.code, self.param) == (other.code, other.param)
+
+    def __hash__(self):
+        return hash((self.code, self.param))
+
+    def __str__(self) -> str:  # impl Display (mod.rs:56-67)
+        if self.code == 5:
+            return f"LeakyReLU({_fmt_f32(self.param)})"
+        return self._NAMES[self.code]
+
+    def __repr__(self) -> str:
+        return f"Activation.{str(self)}"
+
+
+Activation.NONE = Activation(0)
+Activation.RELU = Activation(1)
+Activation.SIGMOID = Activation(2)
+Activation.TANH = Activation(3)
+Activation.GELU = Activation(4)
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.float32).reshape(-1))
+
+
+@dataclass
+class Linear:
+    in_features: int
+    out_features: int
+    weight: np.ndarray  # [in, out] row-major
+    bias: np.ndarray
+    kind: int = field(default=LINEAR, init=False)
+
+    def __post_init__(self):
+        self.weight, self.bias = _f32(self.weight), _f32(self.bias)
+
+
+@dataclass
+class Conv2d:
+    in_channels: int
+    out_channels: int
+    kernel: int
+    stride: int
+    padding: int
+    weight: np.ndarray  # [O, C, k, k]
+    bias: np.ndarray
+    kind: int = field(default=CONV2D, init=False)
+
+    def __post_init__(self):
+        self.weight, self.bias = _f32(self.weight), _f32(self.bias)
+
+
+@dataclass
+class ChannelAffine:
+    scale: np.ndarray
+    shift: np.ndarray
+    kind: int = field(default=CHANNEL_AFFINE, init=False)
+
+    def __post_init__(self):
+        self.scale, self.shift = _f32(self.scale), _f32(self.shift)
+
+
+@dataclass
+class MaxPool2d:
+    kernel: int
+    stride: int
+    kind: int = field(default=MAXPOOL2D, init=False)
+
+
+@dataclass
+class Flatten:
+    kind: int = field(default=FLATTEN, init=False)
+
+
+@dataclass
+class ActivationLayer:
+    act: Activation
+    kind: int = field(default=ACTIVATION, init=False)
+
+
+@dataclass
+class Softmax:
+    kind: int = field(default=SOFTMAX, init=False)
+
+
+class LayerSpec:
+    """Namespace mirroring the Rust enum: ``LayerSpec.Linear(...)`` etc."""
+
+    Linear = Linear
+    Conv2d = Conv2d
+    ChannelAffine = ChannelAffine
+    MaxPool2d = MaxPool2d
+    Flatten = Flatten
+    Activation = ActivationLayer
+    Softmax = Softmax
+
+
+def as_dict(spec) -> dict:
+    """Flat view (the oracle and the C ABI take these field names)."""
+    d = {"kind": spec.kind}
+    if spec.kind == LINEAR:
+        d.update(in_features=spec.in_features, out_features=spec.out_features, weight=spec.weight, bias=spec.bias)
+    elif spec.kind == CONV2D:
+        d.update(in_channels=spec.in_channels, out_channels=spec.out_channels, kernel=spec.kernel,
+                 stride=spec.stride, padding=spec.padding, weight=spec.weight, bias=spec.bias)
+    elif spec.kind == CHANNEL_AFFINE:
+        d.update(scale=spec.scale, shift=spec.shift)
+    elif spec.kind == MAXPOOL2D:
+        d.update(kernel=spec.kernel, stride=spec.stride)
+    elif spec.kind == ACTIVATION:
+        d.update(act=spec.act.code, act_param=spec.act.param)
+    return d

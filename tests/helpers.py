@@ -1,0 +1,43 @@
+"""Shared helpers for the tests."""
+import numpy as np
+
+
+def assert_same(a, b, what=""):
+    """Bit-exact equality of values: NaN matches NaN, -0.0 matches +0.0."""
+    a, b = np.asarray(a), np.asarray(b)
+    assert a.shape == b.shape, f"{what}: shape {a.shape} != {b.shape}"
+    if a.dtype.kind == "f":
+        ok = (a == b) | (np.isnan(a) & np.isnan(b))
+    else:
+        ok = a == b
+    if not ok.all():
+        idx = np.argwhere(~ok)[:5]
+        raise AssertionError(f"{what}: {int((~ok).sum())} of {a.size} differ; first {idx.tolist()}: "
+                             f"{[a[tuple(i)] for i in idx]} vs {[b[tuple(i)] for i in idx]}")
+
+
+def spec_from_dict(d):
+    """Oracle-style layer dict -> product LayerSpec object."""
+    from rustgears_b200 import spec as S
+    k = d["kind"]
+    if k == S.LINEAR:
+        return S.Linear(d["in_features"], d["out_features"], d["weight"], d["bias"])
+    if k == S.CONV2D:
+        return S.Conv2d(d["in_channels"], d["out_channels"], d["kernel"], d["stride"], d["padding"],
+                        d["weight"], d["bias"])
+    if k == S.CHANNEL_AFFINE:
+        return S.ChannelAffine(d["scale"], d["shift"])
+    if k == S.MAXPOOL2D:
+        return S.MaxPool2d(d["kernel"], d["stride"])
+    if k == S.FLATTEN:
+        return S.Flatten()
+    if k == S.ACTIVATION:
+        return S.ActivationLayer(S.Activation(d["act"], d.get("act_param", 0.0)))
+    if k == S.SOFTMAX:
+        return S.Softmax()
+    raise ValueError(k)
+
+
+def session_for(layers, **kw):
+    from rustgears_b200 import ExecutionProvider, InferenceSession
+    return InferenceSession.from_layers([spec_from_dict(l) for l in layers], ExecutionProvider.npu_int8(), **kw)

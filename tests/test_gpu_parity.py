@@ -1,0 +1,170 @@
+"""Device path vs the oracle and the golden fixtures, through the C ABI.
+
+Bar: bit-exact for the i8 activations, i32 accumulators and activation
+scales, and for the f32 outputs too (every f32 step is restated operation by
+operation; the f32 tolerance the path allows, 1e-5 relative, is not needed).
+"""
+import os
+import threading
+
+import numpy as np
+import pytest
+
+from oracle import configs, oracle
+from rustgears_b200 import ExecutionProvider, InferenceSession, _native, rtim
+from tests.helpers import assert_same, session_for, spec_from_dict
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+pytestmark = pytest.mark.gpu
+
+
+def _compare_trace(sess, g, nops):
+    for i in range(nops):
+        assert sess.op_info(i)["label"] == str(g[f"op{i}_label"])
+        assert_same(sess.trace(i, _native.RG_TRACE_OUT).reshape(g[f"op{i}_y"].shape), g[f"op{i}_y"], f"op{i} out")
+        if f"op{i}_aq" in g:
+            assert_same(sess.trace(i, _native.RG_TRACE_SCALES), g[f"op{i}_scales"], f"op{i} scales")
+            assert_same(sess.trace(i, _native.RG_TRACE_AQ).reshape(g[f"op{i}_aq"].shape), g[f"op{i}_aq"], f"op{i} aq")
+            assert_same(sess.trace(i, _native.RG_TRACE_ACC).reshape(g[f"op{i}_acc"].shape), g[f"op{i}_acc"],
+                        f"op{i} acc")
+
+
+@pytest.mark.parametrize("name", sorted(configs.CASES))
+def test_session_matches_golden(gpu, oracle_lib, name):
+    g = np.load(os.path.join(GOLDEN, f"{name}.npz"))
+    layers, x = configs.CASES[name]()
+    sess = session_for(layers)
+    assert sess.compilation_report() == str(g["summary"])
+    sess.set_trace(True)
+    y = sess.run(x)
+    assert_same(y, g["y"], "output")
+    _compare_trace(sess, g, int(g["n_ops"]))
+    prof = sess.last_npu_profile()
+    assert prof.original_layers == len(layers) and prof.fused_ops == int(g["n_ops"])
+    assert (prof.fp32_weight_bytes, prof.npu_weight_bytes) == (int(g["fp32_bytes"]), int(g["npu_bytes"]))
+    _, _, macs = oracle.Program(layers).execute(x)
+    assert [r.macs for r in prof.records] == macs.tolist() and prof.total_macs == int(macs.sum())
+    assert [r.op for r in prof.records] == [str(g[f"op{i}_label"]) for i in range(int(g["n_ops"]))]
+
+
+def test_quantized_weights_match_oracle(gpu, oracle_lib):
+    for name in sorted(configs.CASES):
+        layers, _ = configs.CASES[name]()
+        prog = oracle.Program(layers)
+        sess = session_for(layers)
+        for i, op in enumerate(prog.ops):
+            info = sess.op_info(i)
+            if op.wq is not None:
+                wq, b = sess.op_weights(i)
+                assert np.array_equal(wq, op.wq), (name, i)
+                assert np.array_equal(b, op.bias), (name, i)
+                assert np.float32(info["w_scale"]) == np.float32(op.w_scale), (name, i)
+
+
+@pytest.mark.parametrize("case,batch", [("c1", 65536), ("c1", 1), ("c2", 256), ("c2", 1), ("c2", 3)])
+def test_configs_at_batch(gpu, oracle_lib, case, batch):
+    layers, x = {"c1": configs.c1_mlp, "c2": configs.c2_cnn}[case](batch)
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=os.cpu_count() or 1)
+    assert_same(session_for(layers).run(x), ref, f"{case} batch {batch}")
+
+
+@pytest.mark.parametrize("mkn", [(1, 16, 16), (77, 100, 33), (256, 512, 384), (130, 1568, 128), (64, 4, 3)])
+def test_linear_shapes(gpu, oracle_lib, mkn):
+    m, k, n = mkn
+    layers, x = configs.c3_linear(m, k, n, seed=m + k + n)
+    prog = oracle.Program(layers)
+    ref, trace = prog.run_traced(x)
+    sess = session_for(layers)
+    sess.set_trace(True)
+    assert_same(sess.run(x), ref, f"linear {mkn}")
+    assert_same(sess.trace(0, _native.RG_TRACE_ACC).reshape(m, n), trace[0]["acc"], "acc")
+
+
+def test_empty_batch(gpu, oracle_lib):
+    layers, _ = configs.c2_cnn(1)
+    y = session_for(layers).run(np.zeros((0, 1, 28, 28), np.float32))
+    assert y.shape == (0, 10)
+    layers, _ = configs.c1_mlp(1)
+    assert session_for(layers).run(np.zeros((0, 4), np.float32)).shape == (0, 3)
+
+
+def test_special_values(gpu, oracle_lib):
+    layers, x = configs.c1_mlp(64)
+    prog = oracle.Program(layers)
+    sess = session_for(layers)
+    cases = {"zeros": np.zeros_like(x), "nan": x.copy(), "inf": x.copy(), "tiny": x * np.float32(1e-30),
+             "huge": x * np.float32(1e30)}
+    cases["nan"][3, 1] = np.nan
+    cases["inf"][5, 2] = np.inf
+    for what, xx in cases.items():
+        ref, _, _ = prog.execute(xx)
+        assert_same(sess.run(xx), ref, what)
+
+
+def test_rtim_drop_in(gpu, oracle_lib, tmp_path):
+    layers, x = configs.c2_cnn(5)
+    specs = [spec_from_dict(l) for l in layers]
+    p = tmp_path / "c2.rtim"
+    rtim.save_layers(specs, p)
+    a = InferenceSession.from_rtim(str(p), ExecutionProvider.npu_int8())
+    b = InferenceSession.from_layers(rtim.load_inference_layers(p), ExecutionProvider.npu_int8())
+    ref, _, _ = oracle.Program(layers).execute(x)
+    assert_same(a.run(x), ref, "from_rtim")
+    assert_same(b.run(x), ref, "load_inference_layers + from_layers")
+    assert a.compilation_report() == b.compilation_report()
+
+
+def test_run_device_and_concurrency(gpu, oracle_lib):
+    torch = gpu
+    layers, x = configs.c2_cnn(64)
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
+    sess = session_for(layers)
+    xd = torch.from_numpy(x).cuda()
+    yd = sess.run_device(xd)
+    torch.cuda.synchronize()
+    assert_same(yd.cpu().numpy(), ref, "run_device")
+    results = [None] * 4
+
+    def worker(i):
+        results[i] = sess.run(x)
+
+    ts = [threading.Thread(target=worker, args=(i,)) for i in range(4)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    for r in results:
+        assert_same(r, ref, "concurrent run")
+
+
+def test_shape_errors(gpu):
+    layers, _ = configs.c2_cnn(1)
+    sess = session_for(layers)
+    with pytest.raises(_native.ShapeError):
+        sess.run(np.zeros((2, 3, 28, 28), np.float32))
+    with pytest.raises(_native.ShapeError):
+        sess.run(np.zeros((2, 28, 28), np.float32))
+    layers, _ = configs.c1_mlp(1)
+    with pytest.raises(_native.ShapeError):
+        session_for(layers).run(np.zeros((4, 5), np.float32))
+
+
+@pytest.mark.parametrize("shape", [(4096, 4096, 4096), (16384, 8192, 8192)])
+def test_c3_full_size_sampled_rows(gpu, oracle_lib, shape):
+    """Full-size C3: the device runs every row; rows sampled across the batch are
+    checked against the oracle, whose scale is the absmax over the whole input."""
+    torch = gpu
+    from rustgears_b200 import configs as pconfigs
+    m, k, n = shape
+    model, x = pconfigs.c3_linear(m, k, n)
+    layers = model.export()
+    sess = InferenceSession.from_layers(layers, ExecutionProvider.npu_int8())
+    xd = torch.from_numpy(x).cuda()
+    yd = sess.run_device(xd)
+    torch.cuda.synchronize()
+    from rustgears_b200.spec import as_dict
+    prog = oracle.Program([as_dict(l) for l in layers])
+    rows = np.unique(np.concatenate([[0, m - 1], np.random.default_rng(1).integers(0, m, 30)]))
+    for r in rows:
+        yr, _, _ = oracle.linear_rows(prog.ops[0], prog, 0, x, int(r), int(r) + 1, nthreads=8)
+        assert_same(yd[int(r)].cpu().numpy(), yr[0], f"row {r}")
