@@ -58,7 +58,7 @@ def build(verbose: bool = False) -> str:
         return LIB
     _, libdir = nccl_dirs()
     cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + [
-        "-L", libdir, "-l:libnccl.so.2", "-Xlinker", "-rpath," + libdir, "-lcudart"]
+        "-L", libdir, "-l:libnccl.so.2", "-Xlinker", "-rpath," + libdir, "-cudart", "static"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

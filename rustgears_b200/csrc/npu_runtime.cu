@@ -57,6 +57,20 @@ static rg_status fail(rg_status st, const char* fmt, ...) {
       return fail(RG_ERR_NCCL, "%s: %s", #expr, ncclGetErrorString(r_));                    \
   } while (0)
 
+#define RG_LAUNCHED(name)                                                                   \
+  do {                                                                                      \
+    cudaError_t e_ = cudaGetLastError();                                                    \
+    if (e_ != cudaSuccess)                                                                  \
+      return fail(RG_ERR_CUDA, "launch of %s failed: %s", name, cudaGetErrorString(e_));    \
+  } while (0)
+
+#define RG_PENDING(where)                                                                   \
+  do {                                                                                      \
+    cudaError_t e_ = cudaGetLastError();                                                    \
+    if (e_ != cudaSuccess)                                                                  \
+      return fail(RG_ERR_CUDA, "pending CUDA error before %s: %s", where, cudaGetErrorString(e_)); \
+  } while (0)
+
 #define RG_TRY(expr)                 \
   do {                               \
     rg_status s_ = (expr);           \
@@ -74,9 +88,21 @@ static int64_t out_size(int64_t input, int64_t k, int64_t stride, int64_t pad) {
 // ----------------------------------------------------------------------------
 // device buffer
 // ----------------------------------------------------------------------------
-struct DevBuf {
+struct DevBuf {  // owning, move-only device allocation
   void* p = nullptr;
   size_t bytes = 0;
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  DevBuf(DevBuf&& o) noexcept : p(o.p), bytes(o.bytes) { o.p = nullptr; o.bytes = 0; }
+  DevBuf& operator=(DevBuf&& o) noexcept {
+    if (this != &o) {
+      if (p) cudaFree(p);
+      p = o.p; bytes = o.bytes;
+      o.p = nullptr; o.bytes = 0;
+    }
+    return *this;
+  }
   ~DevBuf() { if (p) cudaFree(p); }
   rg_status ensure(size_t n) {
     if (n <= bytes) return RG_OK;
@@ -565,6 +591,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
     RG_CUDA_TRY(cudaMemcpyAsync(s.covbuf.p, host.data(), host.size(), cudaMemcpyHostToDevice, st));
   }
 
+  RG_PENDING("the first launch");
   const float* cur = x_dev;
   int32_t launches = 0;
   if (record_events) RG_CUDA_TRY(cudaEventRecord(s.events[0], st));
@@ -579,9 +606,16 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
     const int cons = find_consumer(s, i);
     if (cons >= 0 && P.amax_src[(size_t)cons] == (int)i) {
       sink.ptr = amax + P.amax_off[(size_t)cons];
-      sink.elems_per_slot = s.ops[(size_t)cons].kind == RG_LAYER_CONV2D
-                                ? P.shapes[(size_t)cons].in_elems / P.shapes[(size_t)cons].in[0]
+      const int64_t imgs = P.shapes[(size_t)cons].in[0];
+      sink.elems_per_slot = (s.ops[(size_t)cons].kind == RG_LAYER_CONV2D && imgs > 0)
+                                ? P.shapes[(size_t)cons].in_elems / imgs
                                 : 0;
+    }
+    if (os.in_elems == 0 || os.out_elems == 0) {  // empty batch: nothing to launch
+      if (s.trace) s.traces[i] = TraceRec();
+      if (op.kind != RG_LAYER_FLATTEN) cur = dst;
+      if (record_events) RG_CUDA_TRY(cudaEventRecord(s.events[i + 1], st));
+      continue;
     }
     switch (op.kind) {
       case RG_LAYER_LINEAR:
@@ -592,11 +626,12 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         GemmArgs g;
         if (op.kind == RG_LAYER_LINEAR) {
           const int64_t rows = os.in_elems / op.in_f;
-          if (P.amax_src[i] < 0) { launch_absmax(cur, os.in_elems, my_amax, st); ++launches; }
+          if (P.amax_src[i] < 0) { launch_absmax(cur, os.in_elems, my_amax, st); ++launches; RG_LAUNCHED("absmax"); }
           if (s.comm && s.world > 1)
             RG_NCCL_TRY(ncclAllReduce(my_amax, my_amax, 1, ncclUint32, ncclMax, s.comm, st));
           launch_quantize_rows(cur, rows, op.in_f, op.kpad, my_amax, q, my_scale, st);
           ++launches;
+          RG_LAUNCHED("quantize_rows");
           g.a = q; g.lda = op.kpad; g.conv = false;
           g.m = rows; g.n = op.out_f; g.k = op.kpad;
           g.rows_per_scale = 0;
@@ -604,9 +639,10 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         } else {
           const int64_t N = os.in[0];
           const int32_t C = op.in_c, H = (int32_t)os.in[2], W = (int32_t)os.in[3];
-          if (P.amax_src[i] < 0) { launch_image_absmax(cur, N, C, H, W, rc[i], cc[i], my_amax, st); ++launches; }
+          if (P.amax_src[i] < 0) { launch_image_absmax(cur, N, C, H, W, rc[i], cc[i], my_amax, st); ++launches; RG_LAUNCHED("image_absmax"); }
           launch_image_quantize_nhwc(cur, N, C, H, W, C, my_amax, q, my_scale, st);
           ++launches;
+          RG_LAUNCHED("image_quantize_nhwc");
           g.a = q; g.conv = true;
           g.g.h = H; g.g.w = W; g.g.c = C; g.g.cpad = C; g.g.k = op.k; g.g.stride = op.stride; g.g.pad = op.pad;
           g.g.oh = (int32_t)os.out[2]; g.g.ow = (int32_t)os.out[3];
@@ -627,7 +663,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         if (gemm_tc_eligible(g)) launch_gemm_tc(g, s.num_sms, st);
         else launch_gemm_simt(g, st);
         ++launches;
-        RG_CUDA_TRY(cudaGetLastError());
+        RG_LAUNCHED(gemm_tc_eligible(g) ? "gemm_tc" : "gemm_simt");
         if (s.trace) {
           TraceRec& t = s.traces[i];
           RG_TRY(d2h_vec(t.scales, my_scale, P.amax_slots[i], st));
