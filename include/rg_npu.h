@@ -217,6 +217,19 @@ int64_t rg_linear_i8_workspace_size(int64_t m, int64_t ld);
 rg_status rg_linear_i8(const float* x, int64_t m, int64_t k, const int8_t* w, int64_t n,
                        int64_t ld, float w_scale, const float* bias, int32_t act,
                        float act_param, float* out, void* workspace, void* stream);
+/* rg_linear_i8 without the workspace argument, for callers that cannot
+ * allocate device memory (a host that owns every byte of device memory
+ * through its own pool, or a hot loop that must not call cudaMalloc).  No
+ * counterpart in the reference.  Scratch is a static device array inside the
+ * library (RG_LINEAR_NOALLOC_MAX_BYTES of quantized activations, i.e.
+ * m * ld <= 16 MiB; larger calls fail with RG_ERR_INVALID_ARG), held by every
+ * GPU that loads the library until exit.  All calls on a device share it:
+ * calls that overlap on the GPU race.  The first call on a device looks up
+ * the scratch address and should come before any stream capture. */
+#define RG_LINEAR_NOALLOC_MAX_BYTES (16u << 20)
+rg_status rg_linear_i8_noalloc(const float* x, int64_t m, int64_t k, const int8_t* w, int64_t n,
+                               int64_t ld, float w_scale, const float* bias, int32_t act,
+                               float act_param, float* out, void* stream);
 /* max_pool2d (src/kernels.rs:165-213), NCHW f32, no padding. */
 rg_status rg_maxpool2d_f32(const float* x, int64_t n, int32_t c, int32_t h, int32_t w,
                            int32_t k, int32_t stride, float* y, void* stream);

@@ -99,6 +99,7 @@ SIGNATURES = {
     "rg_gemm_i8_fused": ([_vp, _vp, _i64, _i64, _i64, _vp, _f32, _vp, _i32, _f32, _vp, _vp, _vp, _vp], _i32),
     "rg_linear_i8_workspace_size": ([_i64, _i64], _i64),
     "rg_linear_i8": ([_vp, _i64, _i64, _vp, _i64, _i64, _f32, _vp, _i32, _f32, _vp, _vp, _vp], _i32),
+    "rg_linear_i8_noalloc": ([_vp, _i64, _i64, _vp, _i64, _i64, _f32, _vp, _i32, _f32, _vp, _vp], _i32),
     "rg_maxpool2d_f32": ([_vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _vp], _i32),
     "rg_softmax_f32": ([_vp, _i64, _i64, _vp, _vp], _i32),
     "rg_activation_f32": ([_vp, _i64, _i32, _f32, _vp, _vp], _i32),

@@ -42,6 +42,11 @@ static rg_status fail(rg_status st, const char* fmt, ...) {
   return st;
 }
 
+rg_status set_last_error(rg_status st, const char* msg) {
+  g_err = msg;
+  return st;
+}
+
 #define RG_CUDA_TRY(expr)                                                                   \
   do {                                                                                      \
     cudaError_t e_ = (expr);                                                                \

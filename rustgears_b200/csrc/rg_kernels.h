@@ -3,7 +3,12 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/rg_npu.h"
+
 namespace rg {
+
+// Sets the calling thread's rg_last_error() message; returns st.
+rg_status set_last_error(rg_status st, const char* msg);
 
 // Where the absmax of an op's output goes (the next quantizing op's input scale).
 struct AmaxSink {
