@@ -178,6 +178,7 @@ struct Session {
   Profile last;
   bool trace = false;
   std::vector<TraceRec> traces;
+  bool used_tc = false;  // a tcgen05 kernel ran since the last error-word check
   // multi-GPU
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1;
@@ -665,10 +666,15 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         g.out = dst;
         g.acc = s.trace ? s.accbuf.as<int32_t>() : nullptr;
         g.amax = sink;
-        if (gemm_tc_eligible(g)) launch_gemm_tc(g, s.num_sms, st);
-        else launch_gemm_simt(g, st);
+        const bool tc = gemm_tc_eligible(g);
+        if (tc) {
+          if (!launch_gemm_tc(g, s.num_sms, st)) return fail(RG_ERR_CUDA, "op %zu: TMA descriptor encoding failed", i);
+          s.used_tc = true;
+        } else {
+          launch_gemm_simt(g, st);
+        }
         ++launches;
-        RG_LAUNCHED(gemm_tc_eligible(g) ? "gemm_tc" : "gemm_simt");
+        RG_LAUNCHED(tc ? "gemm_tc" : "gemm_simt");
         if (s.trace) {
           TraceRec& t = s.traces[i];
           RG_TRY(d2h_vec(t.scales, my_scale, P.amax_slots[i], st));
@@ -996,6 +1002,11 @@ static rg_status run_impl(rg_session* h, const float* x, bool x_host, const int6
   *y_ndim = (int32_t)oshape.size();
   if (async && !x_host && !y_host && !events && !s.trace) return RG_OK;
   RG_CUDA_TRY(cudaStreamSynchronize(st));
+  if (s.used_tc) {
+    s.used_tc = false;
+    if (gemm_tc_take_error() != 0)
+      return fail(RG_ERR_TIMEOUT, "a tensor-core GEMM gave up on a bounded wait; results are invalid");
+  }
   int64_t total_ns = 0;
   if (events) {
     float ms = 0;
@@ -1210,8 +1221,11 @@ rg_status rg_gemm_i8_fused(const int8_t* a, const int8_t* w, int64_t m, int64_t 
   int dev = 0, sms = 148;
   RG_CUDA_TRY(cudaGetDevice(&dev));
   RG_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  if (gemm_tc_eligible(g)) launch_gemm_tc(g, sms, (cudaStream_t)stream);
-  else launch_gemm_simt(g, (cudaStream_t)stream);
+  if (gemm_tc_eligible(g)) {
+    if (!launch_gemm_tc(g, sms, (cudaStream_t)stream)) return fail(RG_ERR_CUDA, "TMA descriptor encoding failed");
+  } else {
+    launch_gemm_simt(g, (cudaStream_t)stream);
+  }
   RG_CUDA_TRY(cudaGetLastError());
   return RG_OK;
 }

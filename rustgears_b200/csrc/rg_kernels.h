@@ -64,9 +64,13 @@ struct GemmArgs {
 };
 
 void launch_gemm_simt(const GemmArgs& a, cudaStream_t st);
-// tcgen05 path; returns false when the shape is not eligible.
+// tcgen05 path.  eligible(): shape/alignment/driver checks.  launch() returns false
+// when the TMA descriptors could not be encoded (nothing was launched).
 bool gemm_tc_eligible(const GemmArgs& a);
-void launch_gemm_tc(const GemmArgs& a, int num_sms, cudaStream_t st);
+bool launch_gemm_tc(const GemmArgs& a, int num_sms, cudaStream_t st);
+// Reads and clears the device error word the tcgen05 kernels set when a bounded
+// wait gave up (synchronous; 0 = no error).
+int gemm_tc_take_error();
 
 // ---- misc (k_misc.cu) ----------------------------------------------------------
 void launch_maxpool2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t k,

@@ -142,26 +142,73 @@ RG_HD float expm1_f32(float x) {
   return u2f(f2u(y) + ((uint32_t)k << 23));
 }
 
-// tanh, glibc/fdlibm method (identical on all 2^32 inputs to glibc 2.39 tanhf).
+// expm1 on the arguments tanh_f32 gives it (a = 2|x| in [2, 44) or a = -2|x| in
+// (-2, 0]), evaluated without divergent branches: the reduction x = k ln2 + (hi - lo)
+// with t = (float)k reproduces expm1_f32's reduction cases exactly (k = 0 gives
+// hi = a, lo = c = 0; k = -1 gives hi = a + ln2_hi, lo = -ln2_lo), and the
+// reconstructions are computed side by side and selected by k.  On that domain k is
+// never 1 (a >= 2 gives k >= 3), so that reconstruction is omitted.  Bit-identical
+// to expm1_f32 on the domain.
+RG_HD float expm1_tanh_arg(float a) {
+  const float ln2_hi = u2f(0x3f317180u), ln2_lo = u2f(0x3717f7d1u), invln2 = u2f(0x3fb8aa3bu);
+  const float q1 = u2f(0xbd088889u), q2 = u2f(0x3ad00d01u), q3 = u2f(0xb8a670cdu),
+              q4 = u2f(0x36867e54u), q5 = u2f(0xb457edbbu);
+  const uint32_t hx = f2u(a) & 0x7fffffffu;
+  const bool neg = a < 0.0f;
+  int k = (int)RG_ADD(RG_MUL(invln2, a), neg ? -0.5f : 0.5f);
+  k = hx < 0x3F851592u ? (neg ? -1 : 1) : k;
+  k = hx > 0x3eb17218u ? k : 0;
+  const float t = (float)k;
+  const float hi = RG_SUB(a, RG_MUL(t, ln2_hi));
+  const float lo = RG_MUL(t, ln2_lo);
+  const float x = RG_SUB(hi, lo);
+  const float c = RG_SUB(RG_SUB(hi, x), lo);
+  const float hfx = RG_MUL(0.5f, x);
+  const float hxs = RG_MUL(x, hfx);
+  float r1 = RG_MUL(hxs, q5);
+  r1 = RG_MUL(hxs, RG_ADD(q4, r1));
+  r1 = RG_MUL(hxs, RG_ADD(q3, r1));
+  r1 = RG_MUL(hxs, RG_ADD(q2, r1));
+  r1 = RG_MUL(hxs, RG_ADD(q1, r1));
+  r1 = RG_ADD(1.0f, r1);
+  const float tt = RG_SUB(3.0f, RG_MUL(r1, hfx));
+  const float e = RG_MUL(hxs, RG_DIV(RG_SUB(r1, tt), RG_SUB(6.0f, RG_MUL(x, tt))));
+  const float res0 = RG_SUB(x, RG_SUB(RG_MUL(x, e), hxs));               // k == 0
+  const float e2 = RG_SUB(RG_SUB(RG_MUL(x, RG_SUB(e, c)), c), hxs);
+  const float res_m1 = RG_SUB(RG_MUL(0.5f, RG_SUB(x, e2)), 0.5f);         // k == -1
+  const uint32_t kshift = (uint32_t)k << 23;
+  const float ya = RG_SUB(1.0f, RG_SUB(e2, x));
+  const float res_a = RG_SUB(u2f(f2u(ya) + kshift), 1.0f);                // k <= -2 or k > 56
+  const int kc = k < 1 ? 1 : (k > 31 ? 31 : k);                           // in-range shifts only
+  const float yb = RG_SUB(u2f(0x3f800000u - (0x1000000u >> kc)), RG_SUB(e2, x));
+  const float res_b = u2f(f2u(yb) + kshift);                              // 2 <= k < 23
+  const int kd = k < 0 ? 0 : (k > 126 ? 126 : k);
+  const float yc = RG_ADD(RG_SUB(x, RG_ADD(e2, u2f((uint32_t)(0x7f - kd) << 23))), 1.0f);
+  const float res_c = u2f(f2u(yc) + kshift);                              // 23 <= k <= 56
+  float r = res_c;
+  r = k < 23 ? res_b : r;
+  r = (k <= -2 || k > 56) ? res_a : r;
+  r = k == -1 ? res_m1 : r;
+  r = k == 0 ? res0 : r;
+  return hx < 0x33000000u ? a : r;                                        // |a| < 2^-25
+}
+
+// tanh, glibc/fdlibm method (identical on all 2^32 inputs to glibc 2.39 tanhf):
+// |x| >= 1: 1 - 2 / (expm1(2|x|) + 2); else -expm1(-2|x|) / (expm1(-2|x|) + 2).
+// One expm1 and one division per element, the cases resolved by selects.
 RG_HD float tanh_f32(float x) {
   const uint32_t jx = f2u(x), ix = jx & 0x7fffffffu;
-  if (ix >= 0x7f800000u) {                         // inf or NaN
-    return (jx >> 31) ? RG_SUB(RG_DIV(1.0f, x), 1.0f) : RG_ADD(RG_DIV(1.0f, x), 1.0f);
-  }
-  float z;
-  if (ix < 0x41b00000u) {                          // |x| < 22
-    if (ix < 0x24000000u) return RG_MUL(x, RG_ADD(1.0f, x));  // |x| < 2^-55
-    if (ix >= 0x3f800000u) {                       // |x| >= 1
-      const float t = expm1_f32(RG_MUL(2.0f, fabsf(x)));
-      z = RG_SUB(1.0f, RG_DIV(2.0f, RG_ADD(t, 2.0f)));
-    } else {
-      const float t = expm1_f32(RG_MUL(-2.0f, fabsf(x)));
-      z = RG_DIV(-t, RG_ADD(t, 2.0f));
-    }
-  } else {
-    z = 1.0f;
-  }
-  return (jx >> 31) ? -z : z;
+  const bool big = ix >= 0x3f800000u;                 // |x| >= 1
+  const float ax = ix < 0x41b00000u ? fabsf(x) : 1.0f;  // keep the main path finite
+  const float two_ax = RG_MUL(2.0f, ax);
+  const float t = expm1_tanh_arg(big ? two_ax : -two_ax);
+  const float q = RG_DIV(big ? 2.0f : -t, RG_ADD(t, 2.0f));
+  float z = big ? RG_SUB(1.0f, q) : q;
+  z = ix < 0x41b00000u ? z : 1.0f;                    // |x| >= 22 (and inf)
+  z = (jx >> 31) ? -z : z;
+  z = ix < 0x24000000u ? RG_MUL(x, RG_ADD(1.0f, x)) : z;  // |x| < 2^-55
+  if (ix > 0x7f800000u) z = RG_ADD(x, x);             // NaN
+  return z;
 }
 
 // 2^(i/32) rounded to double, minus i << 47 (the table of the expf method).
