@@ -16,6 +16,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <cmath>
 #include <memory>
 #include <mutex>
 #include <string>
@@ -141,6 +142,7 @@ struct Op {
   std::vector<float> bias;
   int64_t kdim = 0, kpad = 0;     // GEMM reduction length and its padded device stride
   DevBuf d_w, d_bias, d_wsc;     // device weights [N, kpad] (conv: (ky,kx,c) order)
+  bool bias_finite = true;
   std::string label;
 };
 
@@ -171,6 +173,7 @@ struct Session {
   std::vector<Op> ops;
   cudaStream_t stream = nullptr;
   std::vector<cudaEvent_t> events;
+  std::vector<int> ev_of;  // ev_of[i]: event marking the start of op i (ops that launch nothing share one)
   std::mutex mu;
   // workspace
   DevBuf act0, act1, qbuf, amax, scales, accbuf, xin, yout, covbuf;
@@ -391,6 +394,8 @@ static rg_status compile(Session& s, const rg_layer_spec* layers, int32_t n) {
       op.kind = l.kind; op.k = l.k; op.stride = l.stride; op.act = l.act; op.param = l.param;
     }
     op.label = make_label(op);
+    for (float b : op.bias)
+      if (!std::isfinite(b)) op.bias_finite = false;
     if (op.kind == RG_LAYER_LINEAR || op.kind == RG_LAYER_CONV2D) RG_TRY(upload_op(op));
     s.ops.push_back(std::move(op));
   }
@@ -493,7 +498,32 @@ struct RunPlan {
   std::vector<std::vector<uint8_t>> rowcov, colcov;
   int64_t total_slots = 0;
   size_t cov_bytes = 0;
+  std::vector<uint8_t> block_start;  // op i starts a fused Conv-Pool-Conv-Pool block
 };
+
+// Activations f with max(f(a), f(b)) == f(max(a, b)) under round-to-nearest.
+static bool non_decreasing(int32_t act, float p) {
+  return act == RG_ACT_NONE || act == RG_ACT_RELU || (act == RG_ACT_LEAKY_RELU && p >= 0.0f);
+}
+
+// ops[i..i+3] = Conv(k3 s1 p1) MaxPool(2,2) Conv(k3 s1 p1) MaxPool(2,2) on a shape the
+// fused kernel is instantiated for.
+static bool block_at(const Session& s, const std::vector<OpShape>& shapes, size_t i) {
+  if (i + 3 >= s.ops.size() || s.trace || (s.flags & RG_SESSION_NO_FUSION)) return false;
+  const Op& c1 = s.ops[i];
+  const Op& m1 = s.ops[i + 1];
+  const Op& c2 = s.ops[i + 2];
+  const Op& m2 = s.ops[i + 3];
+  auto conv_ok = [](const Op& c) {
+    return c.kind == RG_LAYER_CONV2D && c.k == 3 && c.stride == 1 && c.pad == 1 && c.w_scale_ch.empty() &&
+           c.bias_finite && non_decreasing(c.act, c.param);
+  };
+  auto pool_ok = [](const Op& m) { return m.kind == RG_LAYER_MAXPOOL2D && m.k == 2 && m.stride == 2; };
+  if (!conv_ok(c1) || !pool_ok(m1) || !conv_ok(c2) || !pool_ok(m2)) return false;
+  const std::vector<int64_t>& in = shapes[i].in;
+  return in.size() == 4 &&
+         convblock_supported((int)in[1], c1.out_c, c2.out_c, (int)in[2], (int)in[3], c1.act, c2.act);
+}
 
 static rg_status make_plan(const Session& s, const int64_t* shape, int32_t ndim, RunPlan& P) {
   RG_TRY(plan_shapes(s, shape, ndim, P.shapes));
@@ -529,6 +559,12 @@ static rg_status make_plan(const Session& s, const int64_t* shape, int32_t ndim,
       P.amax_src[i] = j;
   }
   P.total_slots = off;
+  P.block_start.assign(n, 0);
+  for (size_t i = 0; i < n; ++i)
+    if (block_at(s, P.shapes, i)) {
+      P.block_start[i] = 1;
+      i += 3;
+    }
   return RG_OK;
 }
 
@@ -600,6 +636,8 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
   RG_PENDING("the first launch");
   const float* cur = x_dev;
   int32_t launches = 0;
+  s.ev_of.assign(n + 1, 0);
+  int next_ev = 1;
   if (record_events) RG_CUDA_TRY(cudaEventRecord(s.events[0], st));
   for (size_t i = 0; i < n; ++i) {
     const Op& op = s.ops[i];
@@ -617,10 +655,38 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
                                 ? P.shapes[(size_t)cons].in_elems / imgs
                                 : 0;
     }
+    if (P.block_start[i] && os.in_elems > 0) {
+      // Conv-Pool-Conv-Pool in one kernel; its time is recorded on the first op.
+      const Op& c2 = s.ops[i + 2];
+      const OpShape& last_os = P.shapes[i + 3];
+      ConvBlockArgs cb;
+      cb.x = cur; cb.n = os.in[0]; cb.c0 = (int32_t)os.in[1]; cb.c1 = op.out_c; cb.c2 = c2.out_c;
+      cb.h = (int32_t)os.in[2]; cb.w = (int32_t)os.in[3];
+      cb.w1 = op.d_w.as<int8_t>(); cb.kpad1 = (int32_t)op.kpad; cb.w2 = c2.d_w.as<int8_t>(); cb.kpad2 = (int32_t)c2.kpad;
+      cb.w1_scale = op.w_scale; cb.w2_scale = c2.w_scale; cb.b1 = op.d_bias.as<float>(); cb.b2 = c2.d_bias.as<float>();
+      cb.act1 = op.act; cb.act2 = c2.act; cb.p1 = op.param; cb.p2 = c2.param;
+      float* bdst = (i + 3 + 1 == n && y_dev) ? y_dev : dst;
+      cb.out = bdst;
+      const int bcons = find_consumer(s, i + 3);
+      if (bcons >= 0 && P.amax_src[(size_t)bcons] == (int)(i + 3)) {
+        cb.amax = amax + P.amax_off[(size_t)bcons];
+        cb.amax_per_image = s.ops[(size_t)bcons].kind == RG_LAYER_CONV2D ? 1 : 0;
+      }
+      launch_convblock(cb, s.num_sms, st);
+      ++launches;
+      RG_LAUNCHED("convblock");
+      cur = bdst;
+      (void)last_os;
+      if (record_events) RG_CUDA_TRY(cudaEventRecord(s.events[(size_t)next_ev], st));
+      s.ev_of[i + 1] = next_ev++;
+      for (size_t j = i + 2; j <= i + 4; ++j) s.ev_of[j] = s.ev_of[i + 1];
+      i += 3;
+      continue;
+    }
     if (os.in_elems == 0 || os.out_elems == 0) {  // empty batch: nothing to launch
       if (s.trace) s.traces[i] = TraceRec();
       if (op.kind != RG_LAYER_FLATTEN) cur = dst;
-      if (record_events) RG_CUDA_TRY(cudaEventRecord(s.events[i + 1], st));
+      s.ev_of[i + 1] = s.ev_of[i];
       continue;
     }
     switch (op.kind) {
@@ -728,7 +794,12 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
     }
     RG_CUDA_TRY(cudaGetLastError());
     if (s.trace) RG_TRY(d2h_vec(s.traces[i].out, cur, os.out_elems, st));
-    if (record_events) RG_CUDA_TRY(cudaEventRecord(s.events[i + 1], st));
+    if (op.kind == RG_LAYER_FLATTEN) {
+      s.ev_of[i + 1] = s.ev_of[i];  // a reshape: no kernel, no event
+    } else {
+      if (record_events) RG_CUDA_TRY(cudaEventRecord(s.events[(size_t)next_ev], st));
+      s.ev_of[i + 1] = next_ev++;
+    }
   }
   s.last.launches = launches;
   if (y_dev && cur != y_dev) {
@@ -749,7 +820,8 @@ static rg_status collect_profile(Session& s, const RunPlan& P, bool have_events,
     s.last.total_macs += P.shapes[i].macs;
     if (have_events) {
       float ms = 0.0f;
-      RG_CUDA_TRY(cudaEventElapsedTime(&ms, s.events[i], s.events[i + 1]));
+      const int e0 = s.ev_of[i], e1 = s.ev_of[i + 1];
+      if (e1 != e0) RG_CUDA_TRY(cudaEventElapsedTime(&ms, s.events[(size_t)e0], s.events[(size_t)e1]));
       s.last.ns[i] = (int64_t)((double)ms * 1e6);
     }
   }

@@ -72,6 +72,29 @@ bool launch_gemm_tc(const GemmArgs& a, int num_sms, cudaStream_t st);
 // wait gave up (synchronous; 0 = no error).
 int gemm_tc_take_error();
 
+// ---- fused CNN block (k_convblock.cu) ------------------------------------------
+// Conv(C0->C1,k3,s1,p1)+act -> MaxPool(2,2) -> Conv(C1->C2,k3,s1,p1)+act -> MaxPool(2,2),
+// per-image quantization of each conv input, all intermediates in shared memory.
+struct ConvBlockArgs {
+  const float* x = nullptr;          // [n, c0, h, w] f32
+  int64_t n = 0;
+  int32_t c0 = 0, c1 = 0, c2 = 0, h = 0, w = 0;
+  const int8_t* w1 = nullptr;        // [c1, kpad1], reduction order (ky, kx, c)
+  int32_t kpad1 = 0;
+  const int8_t* w2 = nullptr;        // [c2, kpad2]
+  int32_t kpad2 = 0;
+  float w1_scale = 1.0f, w2_scale = 1.0f;
+  const float* b1 = nullptr;
+  const float* b2 = nullptr;
+  int32_t act1 = 0, act2 = 0;        // non-decreasing activations only (see convblock_supported)
+  float p1 = 0.0f, p2 = 0.0f;
+  float* out = nullptr;              // [n, c2, h/4, w/4]
+  unsigned* amax = nullptr;          // optional absmax sink of out
+  int64_t amax_per_image = 0;
+};
+bool convblock_supported(int c0, int c1, int c2, int h, int w, int act1, int act2);
+void launch_convblock(const ConvBlockArgs& a, int num_sms, cudaStream_t st);
+
 // ---- misc (k_misc.cu) ----------------------------------------------------------
 void launch_maxpool2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t k,
                       int32_t s, float* y, AmaxSink amax, cudaStream_t st);

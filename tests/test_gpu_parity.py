@@ -168,3 +168,28 @@ def test_c3_full_size_sampled_rows(gpu, oracle_lib, shape):
     for r in rows:
         yr, _, _ = oracle.linear_rows(prog.ops[0], prog, 0, x, int(r), int(r) + 1, nthreads=8)
         assert_same(yd[int(r)].cpu().numpy(), yr[0], f"row {r}")
+
+
+@pytest.mark.parametrize("special", ["plain", "zero_nan_huge", "inf", "leaky"])
+def test_fused_cnn_block_matches_unfused_and_oracle(gpu, oracle_lib, special):
+    """The Conv-Pool-Conv-Pool kernel (pools on the i32 accumulators, exact because the
+    epilogue is monotone) against the op-by-op path and the oracle; an image holding
+    inf takes the kernel's reference-order fallback."""
+    layers, x = configs.c2_cnn(12)
+    x = x.copy()
+    if special == "zero_nan_huge":
+        x[1] = 0.0
+        x[3, 0, 5, 5] = np.nan
+        x[4] *= np.float32(1e30)
+        x[5] *= -1.0
+    elif special == "inf":
+        x[2, 0, 3, 4] = np.inf
+    elif special == "leaky":
+        layers = [dict(l, act=5, act_param=0.1) if l["kind"] == 6 else l for l in layers]
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
+    fused = session_for(layers)
+    unfused = session_for(layers, flags=_native.RG_SESSION_NO_FUSION)
+    assert_same(fused.run(x), ref, "fused")
+    assert_same(unfused.run(x), ref, "unfused")
+    prof = fused.last_npu_profile()
+    assert prof.kernel_launches < unfused.last_npu_profile().kernel_launches
