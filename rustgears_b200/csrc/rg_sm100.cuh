@@ -1,7 +1,7 @@
 // rg_sm100.cuh -- thin inline-PTX wrappers for the sm_100a features the tensor-core
-// kernels use: mbarriers (with bounded waits), TMA tile loads (no multicast: this
-// library runs on several GPUs), and tcgen05 (TMEM alloc, MMA kind::i8, commit,
-// loads).  Written from the PTX ISA; descriptor bit layouts as documented there.
+// kernels use: mbarriers (with bounded waits), TMA tile loads (every CTA loads its
+// own tiles from its own GPU's memory), and tcgen05 (TMEM alloc, MMA kind::i8,
+// commit, loads).  Written from the PTX ISA; descriptor bit layouts as documented there.
 #pragma once
 #include <cuda.h>
 #include <stdint.h>
