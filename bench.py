@@ -273,6 +273,20 @@ def run_reference(args, rank: int, world: int):
     print(json.dumps(line), flush=True)
 
 
+def run_probe(args):
+    """Run the workload a few times on cuda:0 and print the last profile."""
+    import torch
+
+    from rustgears_b200 import ExecutionProvider, InferenceSession
+    model, x, _ = build_workload(args.config, 0, 1, args.batch)
+    sess = InferenceSession.from_module(model, ExecutionProvider.npu_int8(), device=0)
+    xd = torch.from_numpy(x).cuda()
+    for _ in range(args.steps):
+        sess.run_device(xd)
+    torch.cuda.synchronize()
+    print(sess.last_npu_profile())
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -282,12 +296,17 @@ def main():
     ap.add_argument("--batch", type=int, default=None, help="per-GPU batch (rows for c3)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--probe", action="store_true",
+                    help="run the workload --steps times and print the profile (for ncu captures; no timing)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.probe:
+        run_probe(args)
         return
 
     import datetime

@@ -1,6 +1,6 @@
 // k_convblock.cu -- one kernel for the CNN block
 //   FusedConv2d(1->16, k3 s1 p1, act) -> MaxPool2d(2,2) -> FusedConv2d(16->C2, k3 s1 p1, act) -> MaxPool2d(2,2)
-// on 28x28 images, every intermediate of an image kept in shared memory.
+// on 28x28 images, every intermediate of an image kept in shared memory or registers.
 //
 // Reference semantics (src/inference/npu.rs:319-383, kernels.rs:28-96,165-213,
 // quantize.rs:27-35,122-144):
@@ -19,14 +19,17 @@
 //   conv1: an im2col tile built per image, K packed as 4*ky + kx (three 4-byte runs of
 //          the padded input row, 12 of 32 bytes used).  Tile (g, pos) holds window
 //          position pos = dy*2 + dx of pool windows 128g..128g+127, so the 4 pixels of
-//          a window land in one TMEM lane, 4 column blocks apart: the window max is
-//          3 register max ops per channel;
-//   conv2: no im2col at all.  With 16 channels (16 bytes) per pixel, the operand rows
-//          of one tap are consecutive pixels of the padded 16-wide NHWC map, so each
-//          MMA K step (two taps) reads the quantized map in place: rows 16 B apart
-//          (SBO = 128), the second tap LBO bytes after the first.  Output rows are
-//          pixels on the 16-wide grid (columns 14, 15 computed and dropped); a 2x2
-//          window is lanes {x, x^1, x^16, x^17} of one warp.
+//          a window land in one TMEM lane, 4 column blocks apart.
+//   conv2: no im2col.  The quantized 16-channel map is stored padded (16 x 16 pixels
+//          of 16 bytes) with each row column-interleaved: the 8 even columns, then the
+//          8 odd ones.  For output column parity dx, the operand rows (y, j) of tap
+//          (ky, kx) -- input column 2j + dx + kx -- are then 8 consecutive 16-byte
+//          pixels of one half row (a core matrix) and 8-row groups are image rows
+//          (SBO = 256): each MMA K step reads the map in place.  The two dx tiles
+//          go to two TMEM column blocks, so the horizontal pool max is in-thread and
+//          the vertical one is a single shuffle (rows y, y+1 are lanes l, l^8).
+//          K steps pair taps in the order of their offsets for that dx (LBO > 0);
+//          the weights are staged once per order.
 #include <cuda_runtime.h>
 
 #include "rg_kernels.h"
@@ -38,31 +41,39 @@ namespace {
 
 using namespace sm100;
 
+__device__ int g_cb_error;  // set when an MMA-completion wait gave up (read by the host)
+
 constexpr int kThreads = 256;
 constexpr int H = 28, W = 28, C1 = 16;
-constexpr int P1 = 14;                 // pooled conv1 map is 14 x 14
-constexpr int WP = 16;                 // padded width of that map (14 + 2)
+constexpr int P1 = 14;                 // pooled conv1 map is 14 x 14 (16 x 16 padded)
 constexpr int P2 = 7;                  // pooled conv2 map is 7 x 7
 constexpr int Rows1 = H * W;           // 784 conv1 output pixels
 constexpr int MT1 = 8;                 // conv1 tiles: 2 groups of 128 windows x 4 window positions
-constexpr int MT2 = 2;                 // conv2 rows: 16 output rows x 16 = 256
 constexpr int Q1W = 32;                // padded conv1 input row pitch (bytes)
 constexpr int SBO1 = 256;              // conv1 tile: 2 chunks x 128 B per 8-row group
+constexpr int Q2ROW = 256;             // conv2 map row: 16 pixels x 16 B (even half, odd half)
 
-__host__ __device__ constexpr int rup(int v, int m) { return (v + m - 1) / m * m; }
+// Tap order per output-column parity dx: the taps of each kernel row sorted by their
+// byte offset in the interleaved row, so every K-step pair has a positive LBO.
+// dx = 0: kx offsets 0 (kx0), 16 (kx2), 128 (kx1); dx = 1: 16 (kx1), 128 (kx0), 144 (kx2).
+__host__ __device__ constexpr int tap_order(int dx, int i) {
+  return (i / 3) * 3 + (dx == 0 ? (i % 3 == 0 ? 0 : i % 3 == 1 ? 2 : 1) : (i % 3 == 0 ? 1 : i % 3 == 1 ? 0 : 2));
+}
+__host__ __device__ constexpr int tap_offset(int dx, int tap) {  // bytes from the (row 0, j 0) pixel
+  return (tap / 3) * Q2ROW + ((dx + tap % 3) & 1) * 128 + ((dx + tap % 3) >> 1) * 16;
+}
 
 template <int C2>
 struct Lay {
-  static constexpr int K2P = 160, CH2 = 10, SBO2W = CH2 * 128;  // W2 tile: 10 chunks per 8-row group
+  static constexpr int K2P = 160, SBO2W = 10 * 128;            // W2 tile: 10 chunks per 8-row group
   static constexpr int OFF_Q1 = 0;                              // i8 [30][32] (+1 spare word row)
   static constexpr int OFF_A1 = OFF_Q1 + 1024;                  // conv1 im2col: 8 x 128 rows x 32 B
   static constexpr int OFF_W1 = OFF_A1 + MT1 * 128 * 32;        // W1: 16 rows x 32 B
-  static constexpr int OFF_P1 = OFF_W1 + C1 * 32;               // f32 [196][16] pooled conv1
-  static constexpr int OFF_Q2 = OFF_P1 + P1 * P1 * C1 * 4;      // i8 [19][16][16] padded NHWC
-  static constexpr int OFF_W2 = OFF_Q2 + 19 * WP * C1;          // W2: C2 rows x 160 B
-  static constexpr int OFF_MISC = OFF_W2 + C2 * K2P;
+  static constexpr int OFF_Q2 = OFF_W1 + C1 * 32;               // i8 [19 rows][256 B], interleaved
+  static constexpr int OFF_W2 = OFF_Q2 + 19 * Q2ROW;            // W2 in the dx = 0 and dx = 1 tap orders
+  static constexpr int OFF_MISC = OFF_W2 + 2 * C2 * K2P;
   static constexpr int SMEM = OFF_MISC + 128;
-  static constexpr int TMEM_COLS = 128;  // conv1: 8 x 16 columns; conv2 reuses 0..2*C2
+  static constexpr int TMEM_COLS = 128;  // conv1: 8 x 16 columns; conv2 reuses 0 .. 2*C2
 };
 
 struct CBParams {
@@ -112,46 +123,9 @@ __device__ __forceinline__ float epi(int32_t acc, float cs, float bias, float p)
   return v;
 }
 
-// 2x2 window of 16 accumulator columns held by lanes {l, l^m1, l^m2, l^(m1|m2)}; every lane
-// of the window ends with the 4 channels c0 + s + 4k (k = 0..3, s = this lane's slot).
-template <int ACT, int M1, int M2>
-__device__ __forceinline__ void window4(const uint32_t (&acc)[16], bool fast, float cs, const float* bias, int c0,
-                                        float p, int slot, float (&out)[4]) {
-  const int lane = threadIdx.x & 31;
-  if (fast) {
-    int32_t m[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      int32_t v = (int32_t)acc[j];
-      v = max(v, __shfl_xor_sync(0xffffffffu, v, M1));
-      v = max(v, __shfl_xor_sync(0xffffffffu, v, M2));
-      m[j] = v;
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int32_t a = slot == 0 ? m[4 * k] : slot == 1 ? m[4 * k + 1] : slot == 2 ? m[4 * k + 2] : m[4 * k + 3];
-      out[k] = epi<ACT>(a, cs, __ldg(bias + c0 + 4 * k + slot), p);
-    }
-  } else {
-    // reference order: epilogue per pixel, then max over the window in (dy, dx) order
-    const int base = lane & ~(M1 | M2);
-    float best[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const float v = epi<ACT>((int32_t)acc[j], cs, __ldg(bias + c0 + j), p);
-      float b = -INFINITY;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int src = base | ((q >> 1) ? M2 : 0) | ((q & 1) ? M1 : 0);
-        const float vq = __shfl_sync(0xffffffffu, v, src);
-        if (vq > b || vq != vq) b = vq;
-      }
-      best[j] = b;
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k)
-      out[k] = slot == 0 ? best[4 * k] : slot == 1 ? best[4 * k + 1] : slot == 2 ? best[4 * k + 2] : best[4 * k + 3];
-  }
+__device__ __forceinline__ uint32_t pack4(float a, float b, float c, float d, float inv) {
+  return (uint32_t)(quant1(a, inv) & 0xff) | ((uint32_t)(quant1(b, inv) & 0xff) << 8) |
+         ((uint32_t)(quant1(c, inv) & 0xff) << 16) | ((uint32_t)(quant1(d, inv) & 0xff) << 24);
 }
 
 template <int C2, int ACT1, int ACT2>
@@ -161,7 +135,6 @@ __global__ void __launch_bounds__(kThreads, 3) k_convblock(const CBParams p) {
   uint8_t* q1 = sm + L::OFF_Q1;
   uint8_t* a1 = sm + L::OFF_A1;
   uint8_t* w1s = sm + L::OFF_W1;
-  float* p1s = reinterpret_cast<float*>(sm + L::OFF_P1);
   uint8_t* q2 = sm + L::OFF_Q2;
   uint8_t* w2s = sm + L::OFF_W2;
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::OFF_MISC);
@@ -176,9 +149,11 @@ __global__ void __launch_bounds__(kThreads, 3) k_convblock(const CBParams p) {
     const int n = i / 12, b = i % 12, ky = b >> 2, kx = b & 3;
     if (kx < 3) w1s[canon(n, 0, SBO1) + b] = (uint8_t)p.w1[(int64_t)n * p.kpad1 + 3 * ky + kx];
   }
-  for (int i = tid; i < C2 * 144; i += kThreads) {  // W2 bytes (ky, kx, c); bytes 144..159 stay zero
-    const int n = i / 144, b = i % 144;
-    w2s[canon(n, b >> 4, L::SBO2W) + (b & 15)] = (uint8_t)p.w2[(int64_t)n * p.kpad2 + b];
+  for (int i = tid; i < 2 * C2 * 144; i += kThreads) {  // W2 chunk k holds tap tap_order(dx, k); 144.. stay 0
+    const int dx = i / (C2 * 144), rem = i % (C2 * 144), n = rem / 144, b = rem % 144;
+    const int k = b >> 4, tap = tap_order(dx, k);
+    w2s[dx * C2 * L::K2P + canon(n, k, L::SBO2W) + (b & 15)] =
+        (uint8_t)p.w2[(int64_t)n * p.kpad2 + tap * 16 + (b & 15)];
   }
   if (tid == 0) {
     mbar_init(bar, 1);
@@ -194,6 +169,7 @@ __global__ void __launch_bounds__(kThreads, 3) k_convblock(const CBParams p) {
   constexpr uint32_t idesc2 = idesc_i8(128, C2);
   float feat_amax = 0.0f;
   const int q = warp & 3;  // TMEM lane quadrant of this warp
+  const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
 
   // Each thread < 196 owns 4 pixels of the image; the next image's pixels are fetched
   // while the current one is being processed.
@@ -247,111 +223,131 @@ __global__ void __launch_bounds__(kThreads, 3) k_convblock(const CBParams p) {
                idesc1, 0);
       mma_commit(bar);
     }
-    mbar_wait_sleep(bar, phase, 4000000000ull);
+    if (!mbar_wait_sleep(bar, phase, 4000000000ull) && tid == 0) atomicExch(&g_cb_error, 1);
     phase ^= 1;
     tc_fence_after();
     // ---- 4. conv1 epilogue: lane = pool window, max over the 4 position tiles ----------
     const bool fast1 = isfinite(cs1);
-    float m2 = 0.0f;
-    {
-      const int g = warp >> 2, w = 128 * g + 32 * q + lane;  // this lane's pool window
-      const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-      float v[16];
-      if (fast1) {
-        int32_t mx[16];
-        uint32_t acc[16];
-        tmem_ld16(lane_base + (uint32_t)((4 * g) * C1), acc);
+    const int g = warp >> 2, win = 128 * g + 32 * q + lane;  // this lane's pool window
+    float v[16];
+    if (fast1) {
+      int32_t mx[16];
+      uint32_t acc[16];
+      tmem_ld16(lane_base + (uint32_t)((4 * g) * C1), acc);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) mx[j] = (int32_t)acc[j];
+#pragma unroll
+      for (int pos = 1; pos < 4; ++pos) {
+        tmem_ld16(lane_base + (uint32_t)((4 * g + pos) * C1), acc);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) mx[j] = (int32_t)acc[j];
-#pragma unroll
-        for (int pos = 1; pos < 4; ++pos) {
-          tmem_ld16(lane_base + (uint32_t)((4 * g + pos) * C1), acc);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 16; ++j) mx[j] = max(mx[j], (int32_t)acc[j]);
-        }
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = epi<ACT1>(mx[j], cs1, __ldg(p.b1 + j), p.p1);
-      } else {  // reference order: activation per pixel, NaN-propagating max in (dy, dx) order
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = -INFINITY;
-#pragma unroll 1
-        for (int pos = 0; pos < 4; ++pos) {
-          uint32_t acc[16];
-          tmem_ld16(lane_base + (uint32_t)((4 * g + pos) * C1), acc);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float e = epi<ACT1>((int32_t)acc[j], cs1, __ldg(p.b1 + j), p.p1);
-            if (e > v[j] || e != e) v[j] = e;
-          }
-        }
+        for (int j = 0; j < 16; ++j) mx[j] = max(mx[j], (int32_t)acc[j]);
       }
-      if (w < P1 * P1) {
-        float4* dst = reinterpret_cast<float4*>(p1s + w * C1);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          dst[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-          m2 = fmaxf(m2, fmaxf(fmaxf(fabsf(v[4 * k]), fabsf(v[4 * k + 1])), fmaxf(fabsf(v[4 * k + 2]), fabsf(v[4 * k + 3]))));
+      for (int j = 0; j < 16; ++j) v[j] = epi<ACT1>(mx[j], cs1, __ldg(p.b1 + j), p.p1);
+    } else {  // reference order: activation per pixel, NaN-propagating max in (dy, dx) order
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = -INFINITY;
+#pragma unroll 1
+      for (int pos = 0; pos < 4; ++pos) {
+        uint32_t acc[16];
+        tmem_ld16(lane_base + (uint32_t)((4 * g + pos) * C1), acc);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float e = epi<ACT1>((int32_t)acc[j], cs1, __ldg(p.b1 + j), p.p1);
+          if (e > v[j] || e != e) v[j] = e;
         }
       }
     }
+    const bool win_ok = win < P1 * P1;
+    float m2 = 0.0f;
+    if (win_ok)
+#pragma unroll
+      for (int j = 0; j < 16; ++j) m2 = fmaxf(m2, fabsf(v[j]));
     tc_fence_before();
     const float s2 = quant_scale(block_max(m2, red, tid)), inv2 = quant_inv(s2);
     const float cs2 = __fmul_rn(s2, p.w2_scale);
-    // ---- 5. requantize into the padded 16-wide NHWC map (4 channels per thread step) -----
-    for (int i = tid; i < P1 * P1 * (C1 / 4); i += kThreads) {
-      const int w = i >> 2, c4 = i & 3, py = w / P1, px = w % P1;
-      const float4 f = *reinterpret_cast<const float4*>(p1s + w * C1 + c4 * 4);
-      const uint32_t word = (uint32_t)(quant1(f.x, inv2) & 0xff) | ((uint32_t)(quant1(f.y, inv2) & 0xff) << 8) |
-                            ((uint32_t)(quant1(f.z, inv2) & 0xff) << 16) | ((uint32_t)(quant1(f.w, inv2) & 0xff) << 24);
-      *reinterpret_cast<uint32_t*>(q2 + ((py + 1) * WP + (px + 1)) * C1 + c4 * 4) = word;
+    // ---- 5. requantize from registers into the interleaved padded map: one 16-B store ---
+    if (win_ok) {
+      const int py = win / P1 + 1, px = win % P1 + 1;  // padded coordinates
+      *reinterpret_cast<uint4*>(q2 + py * Q2ROW + (px & 1) * 128 + (px >> 1) * 16) =
+          make_uint4(pack4(v[0], v[1], v[2], v[3], inv2), pack4(v[4], v[5], v[6], v[7], inv2),
+                     pack4(v[8], v[9], v[10], v[11], inv2), pack4(v[12], v[13], v[14], v[15], inv2));
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
     __syncthreads();
-    // ---- 6. conv2 straight from the map: 2 M-tiles x 5 K steps (tap pairs) ---------------
+    // ---- 6. conv2 straight from the map: 2 column parities x 5 K steps ------------------
     if (tid == 0) {
       tc_fence_after();
       const uint32_t q2a = smem_addr(q2), w2a = smem_addr(w2s);
 #pragma unroll
-      for (int t = 0; t < MT2; ++t)
+      for (int dx = 0; dx < 2; ++dx)
 #pragma unroll
         for (int s = 0; s < 5; ++s) {
-          const int ta = 2 * s, tb = 2 * s + 1;  // tap 9 (s = 4) meets zero weights
-          const uint32_t off_a = (uint32_t)(((8 * t + ta / 3) * WP + ta % 3) * C1);
-          const uint32_t off_b = tb < 9 ? (uint32_t)(((8 * t + tb / 3) * WP + tb % 3) * C1) : off_a + 16u;
-          mma_i8(tmem + (uint32_t)(t * C2), desc_noswz(q2a + off_a, off_b - off_a, 128),
-                 desc_noswz(w2a + s * 256, 128, L::SBO2W), idesc2, s > 0);
+          const uint32_t oa = (uint32_t)tap_offset(dx, tap_order(dx, 2 * s));
+          const uint32_t ob = s < 4 ? (uint32_t)tap_offset(dx, tap_order(dx, 2 * s + 1)) : oa + 16u;  // zero weights
+          mma_i8(tmem + (uint32_t)(dx * C2), desc_noswz(q2a + oa, ob - oa, Q2ROW),
+                 desc_noswz(w2a + (uint32_t)(dx * C2 * L::K2P + s * 256), 128, L::SBO2W), idesc2, s > 0);
         }
       mma_commit(bar);
     }
-    mbar_wait_sleep(bar, phase, 4000000000ull);
+    if (!mbar_wait_sleep(bar, phase, 4000000000ull) && tid == 0) atomicExch(&g_cb_error, 1);
     phase ^= 1;
     tc_fence_after();
-    // ---- 7. conv2 epilogue: window = lanes {x, x^1, x^16, x^17}, features to global -----
+    // ---- 7. conv2 epilogue: lane (y, j) = 8*y + j; window (y/2, j) = lanes l, l ^ 8 -----
     const bool fast2 = isfinite(cs2);
     {
-      const int t = warp >> 2;
-      const int py = 4 * t + q;            // pooled row of this warp
-      const int px = (lane & 15) >> 1;     // pooled column of this lane's window
-      const int slot = (lane & 1) | ((lane >> 4) << 1);
-      const bool ok = py < P2 && px < P2;
-      float* og = p.out + img * (int64_t)(C2 * P2 * P2) + py * P2 + px;
+      const int c0 = (warp >> 2) * 16;            // channel chunk of this warp
+      const int y = 4 * q + (lane >> 3), j = lane & 7;
+      const int py = y >> 1, half = y & 1;        // half: which 8 of the 16 channels this lane finishes
+      const bool ok = c0 < C2 && py < P2 && j < P2;
       float mo = 0.0f;
-#pragma unroll 1
-      for (int c0 = 0; c0 < C2; c0 += 16) {
-        uint32_t acc[16];
-        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(t * C2 + c0), acc);
+      if (c0 < C2) {
+        uint32_t a0[16], a1v[16];
+        tmem_ld16(lane_base + (uint32_t)(c0), a0);
+        tmem_ld16(lane_base + (uint32_t)(C2 + c0), a1v);
         tmem_ld_wait();
-        float v[4];
-        window4<ACT2, 1, 16>(acc, fast2, cs2, p.b2, c0, p.p2, slot, v);
-        if (ok) {
+        float out[8];
+        if (fast2) {
+          int32_t mx[16];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            og[(c0 + 4 * k + slot) * (P2 * P2)] = v[k];
-            mo = fmaxf(mo, fabsf(v[k]));
+          for (int k = 0; k < 16; ++k) {
+            const int32_t h = max((int32_t)a0[k], (int32_t)a1v[k]);
+            mx[k] = max(h, __shfl_xor_sync(0xffffffffu, h, 8));
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            out[k] = epi<ACT2>(half ? mx[8 + k] : mx[k], cs2, __ldg(p.b2 + c0 + half * 8 + k), p.p2);
+        } else {  // reference order (dy, dx): (y0,dx0), (y0,dx1), (y1,dx0), (y1,dx1)
+          float best[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const float bk = __ldg(p.b2 + c0 + k);
+            const float e0 = epi<ACT2>((int32_t)a0[k], cs2, bk, p.p2);
+            const float e1 = epi<ACT2>((int32_t)a1v[k], cs2, bk, p.p2);
+            const float f0 = __shfl_sync(0xffffffffu, e0, lane & ~8);
+            const float f1 = __shfl_sync(0xffffffffu, e1, lane & ~8);
+            const float f2 = __shfl_sync(0xffffffffu, e0, lane | 8);
+            const float f3 = __shfl_sync(0xffffffffu, e1, lane | 8);
+            float b = -INFINITY;
+            if (f0 > b || f0 != f0) b = f0;
+            if (f1 > b || f1 != f1) b = f1;
+            if (f2 > b || f2 != f2) b = f2;
+            if (f3 > b || f3 != f3) b = f3;
+            best[k] = b;
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k) out[k] = half ? best[8 + k] : best[k];
+        }
+        if (ok) {
+          float* og = p.out + img * (int64_t)(C2 * P2 * P2) + (int64_t)(c0 + half * 8) * (P2 * P2) + py * P2 + j;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            og[k * (P2 * P2)] = out[k];
+            mo = fmaxf(mo, fabsf(out[k]));
           }
         }
       }
@@ -417,6 +413,13 @@ bool convblock_supported(int c0, int c1, int c2, int h, int w, int act1, int act
   if (c0 != 1 || c1 != C1 || h != H || w != W || (c2 != 16 && c2 != 32)) return false;
   auto simple = [](int a) { return a == ACT_NONE || a == ACT_RELU; };
   return (simple(act1) && simple(act2)) || (act1 == ACT_LEAKY_RELU && act2 == ACT_LEAKY_RELU);
+}
+
+int convblock_take_error() {
+  int h = 0, z = 0;
+  if (cudaMemcpyFromSymbol(&h, g_cb_error, sizeof h) != cudaSuccess) return -1;
+  if (h) cudaMemcpyToSymbol(g_cb_error, &z, sizeof z);
+  return h;
 }
 
 void launch_convblock(const ConvBlockArgs& a, int num_sms, cudaStream_t st) {

@@ -165,7 +165,69 @@ __global__ void __launch_bounds__(kThreads) k_gemm_simt(const GemmArgs p) {
   }
 }
 
+// Narrow GEMM (N <= 32, dense A): one thread per output row streams its i8 row with
+// 16-byte loads against the weights held as broadcast words in shared memory, all N
+// accumulators in registers.  Used for the last Linear layers (N = 3, 10, 32 ...)
+// whose few columns would leave a 64 x 64 tile mostly idle.
+constexpr int kNarrowThreads = 128;
+constexpr int kNarrowMaxN = 32;
+
+__global__ void __launch_bounds__(kNarrowThreads) k_gemm_narrow(const GemmArgs p) {
+  extern __shared__ __align__(16) int32_t wsm[];  // [n][k/4]
+  const int kw = (int)(p.k >> 2);
+  for (int i = threadIdx.x; i < (int)p.n * kw; i += blockDim.x) {
+    const int c = i / kw, w = i - c * kw;
+    wsm[i] = __ldg(reinterpret_cast<const int32_t*>(p.w + (int64_t)c * p.ldb) + w);
+  }
+  __syncthreads();
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  float mx = 0.0f;
+  if (r < p.m) {
+    int32_t acc[kNarrowMaxN];
+#pragma unroll
+    for (int j = 0; j < kNarrowMaxN; ++j) acc[j] = 0;
+    const int4* arow = reinterpret_cast<const int4*>(p.a + r * p.lda);
+    for (int k4 = 0; k4 < kw / 4; ++k4) {
+      const int4 av = __ldg(arow + k4);
+#pragma unroll
+      for (int j = 0; j < kNarrowMaxN; ++j) {
+        if (j < p.n) {
+          const int4 wv = *reinterpret_cast<const int4*>(wsm + j * kw + 4 * k4);
+          acc[j] = __dp4a(av.x, wv.x, acc[j]);
+          acc[j] = __dp4a(av.y, wv.y, acc[j]);
+          acc[j] = __dp4a(av.z, wv.z, acc[j]);
+          acc[j] = __dp4a(av.w, wv.w, acc[j]);
+        }
+      }
+    }
+    const float sa = p.a_scale[0];
+#pragma unroll
+    for (int j = 0; j < kNarrowMaxN; ++j) {
+      if (j < p.n) {
+        const float sw = p.w_scale_ch ? p.w_scale_ch[j] : p.w_scale;
+        const float v = epilogue(acc[j], __fmul_rn(sa, sw), __ldg(p.bias + j), p.act, p.act_param);
+        p.out[r * p.n + j] = v;
+        if (p.acc) p.acc[r * p.n + j] = acc[j];
+        mx = fmaxf(mx, fabsf(v));
+      }
+    }
+  }
+  if (p.amax.ptr) flush_max(p.amax.ptr, 0, mx);
+}
+
 }  // namespace
+
+bool gemm_narrow_eligible(const GemmArgs& a) {
+  return !a.conv && a.out_l == 0 && a.rows_per_scale == 0 && a.amax.elems_per_slot == 0 && a.n >= 1 &&
+         a.n <= kNarrowMaxN && (a.k & 15) == 0 && a.lda == a.k && a.ldb >= a.k && a.n * a.k * 4 <= 48 * 1024 &&
+         ((reinterpret_cast<uintptr_t>(a.a) | reinterpret_cast<uintptr_t>(a.w)) & 15) == 0 && (a.ldb & 3) == 0;
+}
+
+void launch_gemm_narrow(const GemmArgs& a, cudaStream_t st) {
+  if (a.m <= 0) return;
+  const int grid = (int)((a.m + kNarrowThreads - 1) / kNarrowThreads);
+  k_gemm_narrow<<<grid, kNarrowThreads, (size_t)(a.n * a.k), st>>>(a);
+}
 
 void launch_gemm_simt(const GemmArgs& a, cudaStream_t st) {
   if (a.m <= 0 || a.n <= 0) return;

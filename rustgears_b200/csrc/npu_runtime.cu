@@ -673,6 +673,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         cb.amax_per_image = s.ops[(size_t)bcons].kind == RG_LAYER_CONV2D ? 1 : 0;
       }
       launch_convblock(cb, s.num_sms, st);
+      s.used_tc = true;
       ++launches;
       RG_LAUNCHED("convblock");
       cur = bdst;
@@ -733,14 +734,17 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         g.acc = s.trace ? s.accbuf.as<int32_t>() : nullptr;
         g.amax = sink;
         const bool tc = gemm_tc_eligible(g);
+        const bool narrow = !tc && gemm_narrow_eligible(g);
         if (tc) {
           if (!launch_gemm_tc(g, s.num_sms, st)) return fail(RG_ERR_CUDA, "op %zu: TMA descriptor encoding failed", i);
           s.used_tc = true;
+        } else if (narrow) {
+          launch_gemm_narrow(g, st);
         } else {
           launch_gemm_simt(g, st);
         }
         ++launches;
-        RG_LAUNCHED(tc ? "gemm_tc" : "gemm_simt");
+        RG_LAUNCHED(tc ? "gemm_tc" : narrow ? "gemm_narrow" : "gemm_simt");
         if (s.trace) {
           TraceRec& t = s.traces[i];
           RG_TRY(d2h_vec(t.scales, my_scale, P.amax_slots[i], st));
@@ -1076,8 +1080,8 @@ static rg_status run_impl(rg_session* h, const float* x, bool x_host, const int6
   RG_CUDA_TRY(cudaStreamSynchronize(st));
   if (s.used_tc) {
     s.used_tc = false;
-    if (gemm_tc_take_error() != 0)
-      return fail(RG_ERR_TIMEOUT, "a tensor-core GEMM gave up on a bounded wait; results are invalid");
+    if (gemm_tc_take_error() != 0 || convblock_take_error() != 0)
+      return fail(RG_ERR_TIMEOUT, "a tensor-core kernel gave up on a bounded wait; results are invalid");
   }
   int64_t total_ns = 0;
   if (events) {
@@ -1295,6 +1299,8 @@ rg_status rg_gemm_i8_fused(const int8_t* a, const int8_t* w, int64_t m, int64_t 
   RG_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   if (gemm_tc_eligible(g)) {
     if (!launch_gemm_tc(g, sms, (cudaStream_t)stream)) return fail(RG_ERR_CUDA, "TMA descriptor encoding failed");
+  } else if (gemm_narrow_eligible(g)) {
+    launch_gemm_narrow(g, (cudaStream_t)stream);
   } else {
     launch_gemm_simt(g, (cudaStream_t)stream);
   }

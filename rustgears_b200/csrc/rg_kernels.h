@@ -64,6 +64,9 @@ struct GemmArgs {
 };
 
 void launch_gemm_simt(const GemmArgs& a, cudaStream_t st);
+// Narrow dense GEMM (N <= 32) on the CUDA cores: one thread per output row.
+bool gemm_narrow_eligible(const GemmArgs& a);
+void launch_gemm_narrow(const GemmArgs& a, cudaStream_t st);
 // tcgen05 path.  eligible(): shape/alignment/driver checks.  launch() returns false
 // when the TMA descriptors could not be encoded (nothing was launched).
 bool gemm_tc_eligible(const GemmArgs& a);
@@ -94,6 +97,8 @@ struct ConvBlockArgs {
 };
 bool convblock_supported(int c0, int c1, int c2, int h, int w, int act1, int act2);
 void launch_convblock(const ConvBlockArgs& a, int num_sms, cudaStream_t st);
+// Reads and clears the device error word the fused block sets when a bounded wait gave up.
+int convblock_take_error();
 
 // ---- misc (k_misc.cu) ----------------------------------------------------------
 void launch_maxpool2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t k,
