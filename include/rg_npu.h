@@ -238,6 +238,12 @@ rg_status rg_softmax_f32(const float* x, int64_t outer, int64_t last, float* y, 
 /* Activation::apply elementwise (src/inference/mod.rs:38-53). */
 rg_status rg_activation_f32(const float* x, int64_t n, int32_t act, float act_param, float* y,
                             void* stream);
+/* Device self-test of the division used on the tanh / GELU path (no counterpart in
+ * the reference): evaluates tanh and GELU with that division and with the IEEE
+ * division for every one of the 2^32 f32 bit patterns and writes the number of
+ * inputs whose results differ in any bit to mismatches[0] (tanh) and
+ * mismatches[1] (GELU).  Synchronous, on the current device, ~0.1 s. */
+rg_status rg_selftest_tanh_division(uint64_t mismatches[2]);
 
 /* ---------------------------------------------------------------------------
  * Deterministic generator used by the benchmark configurations: SplitMix64

@@ -82,6 +82,7 @@ __device__ __forceinline__ void flush_max(unsigned* base, int64_t slot, float v)
   }
 }
 
+template <int ACT>
 __global__ void __launch_bounds__(kThreads) k_gemm_simt(const GemmArgs p) {
   __shared__ __align__(16) int32_t As[BKW][BM];
   __shared__ __align__(16) int32_t Bs[BKW][BN];
@@ -148,7 +149,7 @@ __global__ void __launch_bounds__(kThreads) k_gemm_simt(const GemmArgs p) {
       if (c >= p.n) continue;
       const float sw = p.w_scale_ch ? p.w_scale_ch[c] : p.w_scale;
       const float cs = __fmul_rn(sa, sw);
-      const float v = epilogue(acc[i][j], cs, p.bias[c], p.act, p.act_param);
+      const float v = epilogue_t<ACT>(acc[i][j], cs, p.bias[c], p.act_param);
       const int64_t o = rowbase + c * colstride;
       p.out[o] = v;
       if (p.acc) p.acc[o] = acc[i][j];
@@ -165,74 +166,107 @@ __global__ void __launch_bounds__(kThreads) k_gemm_simt(const GemmArgs p) {
   }
 }
 
-// Narrow GEMM (N <= 32, dense A): one thread per output row streams its i8 row with
-// 16-byte loads against the weights held as broadcast words in shared memory, all N
-// accumulators in registers.  Used for the last Linear layers (N = 3, 10, 32 ...)
-// whose few columns would leave a 64 x 64 tile mostly idle.
 constexpr int kNarrowThreads = 128;
 constexpr int kNarrowMaxN = 32;
 
+// Narrow-N Linear (N <= 32): one thread per output row, the whole weight matrix
+// zero-padded to NT rows in shared memory, NT accumulators in registers (no
+// predicates in the dot loop).  The accumulators are then staged through shared
+// memory so that the epilogue runs once per output element, in a rolled loop
+// over the block's contiguous [rows, n] output range: coalesced stores, and one
+// copy of the activation code rather than NT unrolled copies.  Used for the last
+// Linear layers (N = 3, 10, 32 ...) where a 128-wide tensor-core tile is mostly idle.
+template <int NT>
 __global__ void __launch_bounds__(kNarrowThreads) k_gemm_narrow(const GemmArgs p) {
-  extern __shared__ __align__(16) int32_t wsm[];  // [n][k/4]
+  extern __shared__ __align__(16) int32_t sm[];
   const int kw = (int)(p.k >> 2);
-  for (int i = threadIdx.x; i < (int)p.n * kw; i += blockDim.x) {
+  int32_t* wsm = sm;                                        // [NT][kw], rows >= n are zero
+  int32_t* tile = sm + NT * kw;                             // [kNarrowThreads][NT + 1]
+  float* cs_sm = reinterpret_cast<float*>(tile + kNarrowThreads * (NT + 1));  // [NT]
+  float* bias_sm = cs_sm + NT;                                                // [NT]
+#pragma unroll 4
+  for (int i = threadIdx.x; i < NT * kw; i += kNarrowThreads) {
     const int c = i / kw, w = i - c * kw;
-    wsm[i] = __ldg(reinterpret_cast<const int32_t*>(p.w + (int64_t)c * p.ldb) + w);
+    wsm[i] = c < (int)p.n ? __ldg(reinterpret_cast<const int32_t*>(p.w + (int64_t)c * p.ldb) + w) : 0;
+  }
+  if (threadIdx.x < (unsigned)p.n) {
+    const float sw = p.w_scale_ch ? p.w_scale_ch[threadIdx.x] : p.w_scale;
+    cs_sm[threadIdx.x] = __fmul_rn(p.a_scale[0], sw);
+    bias_sm[threadIdx.x] = p.bias[threadIdx.x];
   }
   __syncthreads();
-  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  float mx = 0.0f;
-  if (r < p.m) {
-    int32_t acc[kNarrowMaxN];
+  const int64_t r0 = (int64_t)blockIdx.x * kNarrowThreads;
+  const int rows = (int)min((int64_t)kNarrowThreads, p.m - r0);
+  if ((int)threadIdx.x < rows) {
+    int32_t acc[NT];
 #pragma unroll
-    for (int j = 0; j < kNarrowMaxN; ++j) acc[j] = 0;
-    const int4* arow = reinterpret_cast<const int4*>(p.a + r * p.lda);
+    for (int j = 0; j < NT; ++j) acc[j] = 0;
+    const int4* arow = reinterpret_cast<const int4*>(p.a + (r0 + threadIdx.x) * p.lda);
+#pragma unroll 8
     for (int k4 = 0; k4 < kw / 4; ++k4) {
       const int4 av = __ldg(arow + k4);
 #pragma unroll
-      for (int j = 0; j < kNarrowMaxN; ++j) {
-        if (j < p.n) {
-          const int4 wv = *reinterpret_cast<const int4*>(wsm + j * kw + 4 * k4);
-          acc[j] = __dp4a(av.x, wv.x, acc[j]);
-          acc[j] = __dp4a(av.y, wv.y, acc[j]);
-          acc[j] = __dp4a(av.z, wv.z, acc[j]);
-          acc[j] = __dp4a(av.w, wv.w, acc[j]);
-        }
+      for (int j = 0; j < NT; ++j) {
+        const int4 wv = *reinterpret_cast<const int4*>(wsm + j * kw + 4 * k4);
+        acc[j] = __dp4a(av.x, wv.x, acc[j]);
+        acc[j] = __dp4a(av.y, wv.y, acc[j]);
+        acc[j] = __dp4a(av.z, wv.z, acc[j]);
+        acc[j] = __dp4a(av.w, wv.w, acc[j]);
       }
     }
-    const float sa = p.a_scale[0];
 #pragma unroll
-    for (int j = 0; j < kNarrowMaxN; ++j) {
-      if (j < p.n) {
-        const float sw = p.w_scale_ch ? p.w_scale_ch[j] : p.w_scale;
-        const float v = epilogue(acc[j], __fmul_rn(sa, sw), __ldg(p.bias + j), p.act, p.act_param);
-        p.out[r * p.n + j] = v;
-        if (p.acc) p.acc[r * p.n + j] = acc[j];
-        mx = fmaxf(mx, fabsf(v));
-      }
-    }
+    for (int j = 0; j < NT; ++j) tile[threadIdx.x * (NT + 1) + j] = acc[j];
+  }
+  __syncthreads();
+  const int n = (int)p.n;
+  float* out = p.out + r0 * n;
+  int32_t* accd = p.acc ? p.acc + r0 * n : nullptr;
+  float mx = 0.0f;
+#pragma unroll 1
+  for (int e = threadIdx.x; e < rows * n; e += kNarrowThreads) {
+    const int rr = e / n, j = e - rr * n;
+    const int32_t a = tile[rr * (NT + 1) + j];
+    const float v = epilogue(a, cs_sm[j], bias_sm[j], p.act, p.act_param);
+    out[e] = v;
+    if (accd) accd[e] = a;
+    mx = fmaxf(mx, fabsf(v));
   }
   if (p.amax.ptr) flush_max(p.amax.ptr, 0, mx);
 }
 
+int narrow_width(int64_t n) { return n <= 4 ? 4 : n <= 8 ? 8 : n <= 16 ? 16 : 32; }
+size_t narrow_smem(int nt, int64_t k) { return (size_t)nt * k + (size_t)kNarrowThreads * (nt + 1) * 4 + 8 * nt; }
+
 }  // namespace
 
 bool gemm_narrow_eligible(const GemmArgs& a) {
-  return !a.conv && a.out_l == 0 && a.rows_per_scale == 0 && a.amax.elems_per_slot == 0 && a.n >= 1 &&
-         a.n <= kNarrowMaxN && (a.k & 15) == 0 && a.lda == a.k && a.ldb >= a.k && a.n * a.k * 4 <= 48 * 1024 &&
+  return a.n >= 1 && a.n <= kNarrowMaxN && narrow_smem(narrow_width(a.n), a.k) <= 48 * 1024 && !a.conv &&
+         a.out_l == 0 && a.rows_per_scale == 0 && a.amax.elems_per_slot == 0 && (a.k & 15) == 0 && a.lda == a.k && a.ldb >= a.k &&
          ((reinterpret_cast<uintptr_t>(a.a) | reinterpret_cast<uintptr_t>(a.w)) & 15) == 0 && (a.ldb & 3) == 0;
 }
 
 void launch_gemm_narrow(const GemmArgs& a, cudaStream_t st) {
   if (a.m <= 0) return;
   const int grid = (int)((a.m + kNarrowThreads - 1) / kNarrowThreads);
-  k_gemm_narrow<<<grid, kNarrowThreads, (size_t)(a.n * a.k), st>>>(a);
+  switch (narrow_width(a.n)) {
+    case 4: k_gemm_narrow<4><<<grid, kNarrowThreads, narrow_smem(4, a.k), st>>>(a); break;
+    case 8: k_gemm_narrow<8><<<grid, kNarrowThreads, narrow_smem(8, a.k), st>>>(a); break;
+    case 16: k_gemm_narrow<16><<<grid, kNarrowThreads, narrow_smem(16, a.k), st>>>(a); break;
+    default: k_gemm_narrow<32><<<grid, kNarrowThreads, narrow_smem(32, a.k), st>>>(a); break;
+  }
 }
 
 void launch_gemm_simt(const GemmArgs& a, cudaStream_t st) {
   if (a.m <= 0 || a.n <= 0) return;
   dim3 grid((unsigned)((a.m + BM - 1) / BM), (unsigned)((a.n + BN - 1) / BN));
-  k_gemm_simt<<<grid, kThreads, 0, st>>>(a);
+  switch (a.act) {
+    case ACT_RELU: k_gemm_simt<ACT_RELU><<<grid, kThreads, 0, st>>>(a); break;
+    case ACT_SIGMOID: k_gemm_simt<ACT_SIGMOID><<<grid, kThreads, 0, st>>>(a); break;
+    case ACT_TANH: k_gemm_simt<ACT_TANH><<<grid, kThreads, 0, st>>>(a); break;
+    case ACT_GELU: k_gemm_simt<ACT_GELU><<<grid, kThreads, 0, st>>>(a); break;
+    case ACT_LEAKY_RELU: k_gemm_simt<ACT_LEAKY_RELU><<<grid, kThreads, 0, st>>>(a); break;
+    default: k_gemm_simt<ACT_NONE><<<grid, kThreads, 0, st>>>(a); break;
+  }
 }
 
 }  // namespace rg

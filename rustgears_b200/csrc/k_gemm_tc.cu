@@ -11,7 +11,9 @@
 //               accumulator; two accumulators (2 x BN columns) so the epilogue
 //               of one tile overlaps the main loop of the next;
 //   warps 2-17  epilogue: tcgen05.ld (32 lanes x 16 columns), exact f32 epilogue,
-//               16-byte stores, running absmax for the next layer's scale.
+//               the 32 x 16 f32 result staged in shared memory (64-byte swizzle:
+//               lane = row writes conflict-free) and written by one TMA tile store,
+//               running absmax for the next layer's scale.
 // Every mbarrier wait is bounded: on timeout the CTA raises an abort flag, the
 // roles leave their loops, in-flight copies and MMAs are drained (bounded), TMEM
 // is freed and a device error word is set for the host to report.
@@ -19,6 +21,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "rg_kernels.h"
@@ -43,7 +46,9 @@ struct Cfg {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kBarBytes = 256;
-  static constexpr int kSmem = 1024 /*align slack*/ + kStages * kStageBytes + kBarBytes;
+  static constexpr int kStgBytes = kEpiWarps * 32 * 16 * 4;  // one 32 x 16 f32 tile per epilogue warp
+  static constexpr int kSmem = 1024 /*align slack*/ + kStages * kStageBytes + kStgBytes + kBarBytes;
+  static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
 };
 
 struct TcParams {
@@ -58,6 +63,8 @@ struct TcParams {
   int32_t* acc;             // optional [m, n]
   unsigned* amax;           // optional: max |out| (float bits)
   int32_t tiles_m, tiles_n;
+  int32_t tma_store;        // out written through map_o (n % 4 == 0, 16-byte aligned base)
+  int32_t vec_cols;         // bias / w_scale_ch 16-byte aligned and n % 4 == 0: vector loads
 };
 
 __device__ int g_tc_error;  // set when a bounded wait gave up (read by the host)
@@ -74,15 +81,16 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
   nb = in / gm;
 }
 
-template <int BN>
+template <int BN, int ACT>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
-              const TcParams p) {
+              const __grid_constant__ CUtensorMap map_o, const TcParams p) {
   using C = Cfg<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_base = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  float* stg_base = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes);  // 1024-aligned
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes + C::kStgBytes);
   uint64_t* full = bars;                       // [kStages]
   uint64_t* empty = bars + C::kStages;         // [kStages]
   uint64_t* tfull = bars + 2 * C::kStages;     // [2]
@@ -109,6 +117,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
     tma_prefetch_desc(&map_a);
     tma_prefetch_desc(&map_w);
+    if (p.tma_store) tma_prefetch_desc(&map_o);
   }
   if (warp == 1) tmem_alloc(tmem_slot, C::kTmemCols);
   tc_fence_before();
@@ -182,6 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- epilogue ----------------
     const int q = warp & 3;                 // TMEM lane quadrant this warp may access
     const int part = (warp - 2) >> 2;       // which quarter of the BN columns
+    float* stg = stg_base + (warp - 2) * (32 * 16);
     constexpr int kCols = BN / (kEpiWarps / 4);
     const float sa = p.a_scale[0];
     const float cs_tensor = __fmul_rn(sa, p.w_scale);
@@ -196,7 +206,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool got = mbar_wait(&tfull[buf], aphase, abort);
       if (!__all_sync(0xffffffffu, got)) { *abort = 1; break; }
       tc_fence_after();
-      const int64_t row = (int64_t)mb * BM + q * 32 + lane;
+      const int64_t row0 = (int64_t)mb * BM + q * 32;
+      const int64_t row = row0 + lane;
       const bool row_ok = row < p.m;
 #pragma unroll 1
       for (int c0 = part * kCols; c0 < (part + 1) * kCols; c0 += 16) {
@@ -204,41 +215,70 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + c0), v);
         tmem_ld_wait();
         const int64_t col0 = (int64_t)nb * BN + c0;
-        if (row_ok && col0 < p.n) {
-          float o[16];
+        if (col0 >= p.n || row0 >= p.m) continue;  // warp-uniform
+        float o[16];
+        if (p.vec_cols && col0 + 16 <= p.n) {
+          // Full chunk: scale and bias as 16-byte loads.
+          const float4* bp = reinterpret_cast<const float4*>(p.bias + col0);
+          const float4* sp = reinterpret_cast<const float4*>(p.w_scale_ch + col0);
+#pragma unroll
+          for (int j4 = 0; j4 < 4; ++j4) {
+            const float4 b = __ldg(bp + j4);
+            float4 cs = make_float4(cs_tensor, cs_tensor, cs_tensor, cs_tensor);
+            if (p.w_scale_ch) {
+              const float4 sw = __ldg(sp + j4);
+              cs = make_float4(__fmul_rn(sa, sw.x), __fmul_rn(sa, sw.y), __fmul_rn(sa, sw.z), __fmul_rn(sa, sw.w));
+            }
+            o[4 * j4] = epilogue_t<ACT>((int32_t)v[4 * j4], cs.x, b.x, p.act_param);
+            o[4 * j4 + 1] = epilogue_t<ACT>((int32_t)v[4 * j4 + 1], cs.y, b.y, p.act_param);
+            o[4 * j4 + 2] = epilogue_t<ACT>((int32_t)v[4 * j4 + 2], cs.z, b.z, p.act_param);
+            o[4 * j4 + 3] = epilogue_t<ACT>((int32_t)v[4 * j4 + 3], cs.w, b.w, p.act_param);
+          }
+          if (row_ok) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(o[j]));
+          }
+        } else {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int64_t c = col0 + j;
             const int64_t cc = c < p.n ? c : p.n - 1;
             const float cs = p.w_scale_ch ? __fmul_rn(sa, __ldg(p.w_scale_ch + cc)) : cs_tensor;
-            o[j] = epilogue((int32_t)v[j], cs, __ldg(p.bias + cc), p.act, p.act_param);
-            if (c < p.n) amax = fmaxf(amax, fabsf(o[j]));
+            o[j] = epilogue_t<ACT>((int32_t)v[j], cs, __ldg(p.bias + cc), p.act_param);
+            if (c < p.n && row_ok) amax = fmaxf(amax, fabsf(o[j]));
           }
+        }
+        if (p.tma_store) {
+          // The previous chunk's store must have finished reading the staging tile.
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 4; ++j)  // 16-byte chunk j of row `lane`, 64-byte swizzle
+            *reinterpret_cast<float4*>(stg + lane * 16 + ((j ^ ((lane >> 1) & 3)) << 2)) =
+                make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&map_o, stg, (int32_t)col0, (int32_t)row0);
+            bulk_commit();
+          }
+        } else if (row_ok) {
           float* dst = p.out + row * p.n + col0;
-          if (col0 + 16 <= p.n && (p.n & 3) == 0) {
 #pragma unroll
-            for (int j = 0; j < 16; j += 4)
-              *reinterpret_cast<float4*>(dst + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
-            if (p.acc) {
-              int32_t* ad = p.acc + row * p.n + col0;
+          for (int j = 0; j < 16; ++j)
+            if (col0 + j < p.n) dst[j] = o[j];
+        }
+        if (p.acc && row_ok) {
 #pragma unroll
-              for (int j = 0; j < 16; j += 4)
-                *reinterpret_cast<int4*>(ad + j) = make_int4((int)v[j], (int)v[j + 1], (int)v[j + 2], (int)v[j + 3]);
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              if (col0 + j < p.n) {
-                dst[j] = o[j];
-                if (p.acc) p.acc[row * p.n + col0 + j] = (int32_t)v[j];
-              }
-          }
+          for (int j = 0; j < 16; ++j)
+            if (col0 + j < p.n) p.acc[row * p.n + col0 + j] = (int32_t)v[j];
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
     }
+    if (p.tma_store && lane == 0) bulk_wait_all();
     if (p.amax) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -268,6 +308,19 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+// Output map: f32 [rows, cols] row-major, 32 x 16 boxes, 64-byte swizzle.
+bool make_out_map(CUtensorMap* map, float* base, int64_t rows, int64_t cols) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 4};
+  cuuint32_t box[2] = {16, 32};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t ld, int box_rows) {
   auto fn = encode_fn();
   if (!fn) return false;
@@ -280,25 +333,44 @@ bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t ld, int 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN>
+template <int BN, int ACT>
 bool launch_bn(const GemmArgs& a, int num_sms, cudaStream_t st) {
   using C = Cfg<BN>;
   static std::once_flag once;
   std::call_once(once, [] {
-    cudaFuncSetAttribute(k_gemm_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    cudaFuncSetAttribute(k_gemm_tc<BN, ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
   });
-  CUtensorMap ma, mw;
+  CUtensorMap ma, mw, mo;
   if (!make_map(&ma, a.a, a.m, a.lda, BM) || !make_map(&mw, a.w, a.n, a.ldb, BN)) return false;
+  memset(&mo, 0, sizeof mo);
+  const bool tma_store = (a.n & 3) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 &&
+                         make_out_map(&mo, a.out, a.m, a.n);
   TcParams p;
   p.m = a.m; p.n = a.n; p.k = a.k;
   p.a_scale = a.a_scale; p.w_scale = a.w_scale; p.w_scale_ch = a.w_scale_ch; p.bias = a.bias;
   p.act = a.act; p.act_param = a.act_param; p.out = a.out; p.acc = a.acc; p.amax = a.amax.ptr;
   p.tiles_m = (int)((a.m + BM - 1) / BM);
   p.tiles_n = (int)((a.n + BN - 1) / BN);
+  p.tma_store = tma_store ? 1 : 0;
+  p.vec_cols = (a.n & 3) == 0 &&
+               ((reinterpret_cast<uintptr_t>(a.bias) | reinterpret_cast<uintptr_t>(a.w_scale_ch)) & 15) == 0;
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < num_sms ? tiles : num_sms;
-  k_gemm_tc<BN><<<grid, kThreads, C::kSmem, st>>>(ma, mw, p);
+  k_gemm_tc<BN, ACT><<<grid, kThreads, C::kSmem, st>>>(ma, mw, mo, p);
   return true;
+}
+
+template <int BN>
+bool launch_act(const GemmArgs& a, int num_sms, cudaStream_t st) {
+  switch (a.act) {
+    case ACT_NONE: return launch_bn<BN, ACT_NONE>(a, num_sms, st);
+    case ACT_RELU: return launch_bn<BN, ACT_RELU>(a, num_sms, st);
+    case ACT_SIGMOID: return launch_bn<BN, ACT_SIGMOID>(a, num_sms, st);
+    case ACT_TANH: return launch_bn<BN, ACT_TANH>(a, num_sms, st);
+    case ACT_GELU: return launch_bn<BN, ACT_GELU>(a, num_sms, st);
+    case ACT_LEAKY_RELU: return launch_bn<BN, ACT_LEAKY_RELU>(a, num_sms, st);
+    default: return false;
+  }
 }
 
 }  // namespace
@@ -312,7 +384,7 @@ bool gemm_tc_eligible(const GemmArgs& a) {
 }
 
 bool launch_gemm_tc(const GemmArgs& a, int num_sms, cudaStream_t st) {
-  return a.n >= 256 ? launch_bn<256>(a, num_sms, st) : launch_bn<128>(a, num_sms, st);
+  return a.n >= 256 ? launch_act<256>(a, num_sms, st) : launch_act<128>(a, num_sms, st);
 }
 
 int gemm_tc_take_error() {

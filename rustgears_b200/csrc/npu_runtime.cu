@@ -1346,4 +1346,18 @@ rg_status rg_activation_f32(const float* x, int64_t n, int32_t act, float act_pa
   return RG_OK;
 }
 
+rg_status rg_selftest_tanh_division(uint64_t mismatches[2]) {
+  if (!mismatches) return fail(RG_ERR_INVALID_ARG, "null argument");
+  DevBuf counts;
+  const rg_status st = counts.ensure(2 * sizeof(unsigned long long));
+  if (st != RG_OK) return st;
+  launch_selftest_tanh_division(counts.as<unsigned long long>(), nullptr);
+  RG_CUDA_TRY(cudaGetLastError());
+  unsigned long long h[2];
+  RG_CUDA_TRY(cudaMemcpy(h, counts.p, sizeof h, cudaMemcpyDeviceToHost));
+  mismatches[0] = h[0];
+  mismatches[1] = h[1];
+  return RG_OK;
+}
+
 }  // extern "C"

@@ -74,6 +74,31 @@ RG_HD double u2d(uint64_t u) {
 #define RG_DIV(a, b) ((a) / (b))
 #endif
 
+// Division rounded to nearest for the well-scaled operands of the tanh path
+// (normal, finite divisor and quotient): Markstein's method -- a reciprocal
+// estimate (PTX rcp.approx), one Newton-Raphson step y += y (1 - b y), the
+// quotient q = a y, and one correction q += (a - b q) y with the remainder
+// formed exactly by an FMA (P. Markstein, "Computation of elementary functions
+// on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990).  Five
+// FMA-pipe operations and one reciprocal estimate, against the IEEE division's
+// range checks.  Its equality with the IEEE division on the path's whole input
+// range (every f32 input of tanh_f32) is checked exhaustively on the device.
+template <bool kNR>
+RG_HD float div_path(float a, float b) {
+#ifdef __CUDA_ARCH__
+  if (kNR) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(b));
+    y = __fmaf_rn(y, __fmaf_rn(-b, y, 1.0f), y);
+    const float q = __fmul_rn(a, y);
+    return __fmaf_rn(__fmaf_rn(-b, q, a), y, q);
+  }
+  return __fdiv_rn(a, b);
+#else
+  return a / b;
+#endif
+}
+
 RG_HD float fmax_ignore_nan(float a, float b) { return fmaxf(a, b); }  // IEEE maxNum == f32::max
 
 // expm1 for the tanh argument range (|x| < 44); fdlibm method, f32 steps.
@@ -149,6 +174,7 @@ RG_HD float expm1_f32(float x) {
 // reconstructions are computed side by side and selected by k.  On that domain k is
 // never 1 (a >= 2 gives k >= 3), so that reconstruction is omitted.  Bit-identical
 // to expm1_f32 on the domain.
+template <bool kNR = true>
 RG_HD float expm1_tanh_arg(float a) {
   const float ln2_hi = u2f(0x3f317180u), ln2_lo = u2f(0x3717f7d1u), invln2 = u2f(0x3fb8aa3bu);
   const float q1 = u2f(0xbd088889u), q2 = u2f(0x3ad00d01u), q3 = u2f(0xb8a670cdu),
@@ -172,7 +198,7 @@ RG_HD float expm1_tanh_arg(float a) {
   r1 = RG_MUL(hxs, RG_ADD(q1, r1));
   r1 = RG_ADD(1.0f, r1);
   const float tt = RG_SUB(3.0f, RG_MUL(r1, hfx));
-  const float e = RG_MUL(hxs, RG_DIV(RG_SUB(r1, tt), RG_SUB(6.0f, RG_MUL(x, tt))));
+  const float e = RG_MUL(hxs, div_path<kNR>(RG_SUB(r1, tt), RG_SUB(6.0f, RG_MUL(x, tt))));
   const float res0 = RG_SUB(x, RG_SUB(RG_MUL(x, e), hxs));               // k == 0
   const float e2 = RG_SUB(RG_SUB(RG_MUL(x, RG_SUB(e, c)), c), hxs);
   const float res_m1 = RG_SUB(RG_MUL(0.5f, RG_SUB(x, e2)), 0.5f);         // k == -1
@@ -196,13 +222,14 @@ RG_HD float expm1_tanh_arg(float a) {
 // tanh, glibc/fdlibm method (identical on all 2^32 inputs to glibc 2.39 tanhf):
 // |x| >= 1: 1 - 2 / (expm1(2|x|) + 2); else -expm1(-2|x|) / (expm1(-2|x|) + 2).
 // One expm1 and one division per element, the cases resolved by selects.
+template <bool kNR = true>
 RG_HD float tanh_f32(float x) {
   const uint32_t jx = f2u(x), ix = jx & 0x7fffffffu;
   const bool big = ix >= 0x3f800000u;                 // |x| >= 1
   const float ax = ix < 0x41b00000u ? fabsf(x) : 1.0f;  // keep the main path finite
   const float two_ax = RG_MUL(2.0f, ax);
-  const float t = expm1_tanh_arg(big ? two_ax : -two_ax);
-  const float q = RG_DIV(big ? 2.0f : -t, RG_ADD(t, 2.0f));
+  const float t = expm1_tanh_arg<kNR>(big ? two_ax : -two_ax);
+  const float q = div_path<kNR>(big ? 2.0f : -t, RG_ADD(t, 2.0f));
   float z = big ? RG_SUB(1.0f, q) : q;
   z = ix < 0x41b00000u ? z : 1.0f;                    // |x| >= 22 (and inf)
   z = (jx >> 31) ? -z : z;
@@ -286,20 +313,24 @@ RG_HD float exp_f32(float x) {
 #endif
 }
 
+// GELU (tanh form) of Activation::apply (src/device/backend.rs:61-68).
+template <bool kNR = true>
+RG_HD float gelu_f32(float x) {
+  const float gelu_c = 0.7978846f;                               // GELU_C (backend.rs:61)
+  float c = RG_MUL(0.044715f, x);
+  c = RG_MUL(c, x);
+  c = RG_MUL(c, x);
+  const float t = tanh_f32<kNR>(RG_MUL(gelu_c, RG_ADD(x, c)));
+  return RG_MUL(RG_MUL(0.5f, x), RG_ADD(1.0f, t));
+}
+
 // Activation::apply (src/inference/mod.rs:38-53, src/device/backend.rs:61-78).
 RG_HD float act_apply(int32_t act, float p, float x) {
   switch (act) {
     case ACT_RELU: return fmaxf(x, 0.0f);                       // x.max(0.0): NaN -> 0
     case ACT_SIGMOID: return RG_DIV(1.0f, RG_ADD(1.0f, exp_f32(-x)));
     case ACT_TANH: return tanh_f32(x);
-    case ACT_GELU: {
-      const float gelu_c = 0.7978846f;                           // GELU_C (backend.rs:61)
-      float c = RG_MUL(0.044715f, x);
-      c = RG_MUL(c, x);
-      c = RG_MUL(c, x);
-      const float t = tanh_f32(RG_MUL(gelu_c, RG_ADD(x, c)));
-      return RG_MUL(RG_MUL(0.5f, x), RG_ADD(1.0f, t));
-    }
+    case ACT_GELU: return gelu_f32(x);
     case ACT_LEAKY_RELU: return x > 0.0f ? x : RG_MUL(p, x);
     default: return x;
   }
@@ -325,5 +356,13 @@ RG_HD float epilogue(int32_t acc, float cs, float bias, int32_t act, float p) {
 #endif
   return act_apply(act, p, RG_ADD(RG_MUL(a, cs), bias));
 }
+
+// Same with the activation fixed at compile time: the switch folds away, so a
+// kernel instantiated per activation carries only that activation's code.
+template <int ACT>
+RG_HD float epilogue_t(int32_t acc, float cs, float bias, float p) {
+  return epilogue(acc, cs, bias, ACT, p);
+}
+
 
 }  // namespace rg

@@ -31,3 +31,11 @@ def test_activation_sweep(gpu, oracle_lib, act, param):
                                                   C.c_void_p(yd.data_ptr()), None))
     torch.cuda.synchronize()
     assert_same(yd.cpu().numpy(), ref, f"act {act}")
+
+
+def test_fast_division_is_exact_on_every_input(gpu):
+    """tanh / GELU divide with Markstein's reciprocal-and-correction sequence; the
+    device self-test compares them with the IEEE division on all 2^32 f32 inputs."""
+    counts = (C.c_uint64 * 2)()
+    _native.check(_native.lib().rg_selftest_tanh_division(counts))
+    assert list(counts) == [0, 0]
