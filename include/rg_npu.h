@@ -238,12 +238,13 @@ rg_status rg_softmax_f32(const float* x, int64_t outer, int64_t last, float* y, 
 /* Activation::apply elementwise (src/inference/mod.rs:38-53). */
 rg_status rg_activation_f32(const float* x, int64_t n, int32_t act, float act_param, float* y,
                             void* stream);
-/* Device self-test of the division used on the tanh / GELU path (no counterpart in
- * the reference): evaluates tanh and GELU with that division and with the IEEE
- * division for every one of the 2^32 f32 bit patterns and writes the number of
- * inputs whose results differ in any bit to mismatches[0] (tanh) and
- * mismatches[1] (GELU).  Synchronous, on the current device, ~0.1 s. */
-rg_status rg_selftest_tanh_division(uint64_t mismatches[2]);
+/* Device self-test of the fast arithmetic the kernels use (no counterpart in the
+ * reference): for every one of the 2^32 f32 bit patterns, evaluates each fast path
+ * and the plain IEEE / libdevice form and counts the inputs whose results differ:
+ * mismatches[0] tanh, [1] GELU (division), [2] the quantization scale from an
+ * absmax (non-negative inputs), [3] its reciprocal, [4] the rounding of a
+ * quantization argument (|t| < 2^23 and NaN).  Synchronous, current device, ~0.2 s. */
+rg_status rg_selftest_fast_paths(uint64_t mismatches[5]);
 
 /* ---------------------------------------------------------------------------
  * Deterministic generator used by the benchmark configurations: SplitMix64

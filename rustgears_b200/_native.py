@@ -103,7 +103,7 @@ SIGNATURES = {
     "rg_maxpool2d_f32": ([_vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _vp], _i32),
     "rg_softmax_f32": ([_vp, _i64, _i64, _vp, _vp], _i32),
     "rg_activation_f32": ([_vp, _i64, _i32, _f32, _vp, _vp], _i32),
-    "rg_selftest_tanh_division": ([_vp], _i32),
+    "rg_selftest_fast_paths": ([_vp], _i32),
     "rg_rng_seed": ([C.POINTER(RngC), _u64], None),
     "rg_rng_next_u64": ([C.POINTER(RngC)], _u64),
     "rg_rng_fill_uniform": ([C.POINTER(RngC), _f32p, _i64, _f32, _f32], None),

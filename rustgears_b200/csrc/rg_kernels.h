@@ -103,9 +103,10 @@ int convblock_take_error();
 // ---- misc (k_misc.cu) ----------------------------------------------------------
 void launch_maxpool2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t k,
                       int32_t s, float* y, AmaxSink amax, cudaStream_t st);
-// Counts inputs where tanh / GELU with the fast division differ from the IEEE
-// division (all 2^32 f32 inputs); counts[0] tanh, counts[1] GELU (zeroed first).
-void launch_selftest_tanh_division(unsigned long long* counts, cudaStream_t st);
+// Counts f32 inputs where a fast path changes a result, over all 2^32 bit patterns
+// (zeroed first): counts[0] tanh, [1] GELU, [2] quant_scale, [3] quant_inv,
+// [4] round_half_away.
+void launch_selftest_fast_division(unsigned long long* counts, cudaStream_t st);
 void launch_activation(const float* x, int64_t n, int32_t act, float p, float* y, AmaxSink amax,
                        cudaStream_t st);
 void launch_softmax(const float* x, int64_t outer, int64_t last, float* y, AmaxSink amax,

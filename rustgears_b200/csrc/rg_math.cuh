@@ -337,8 +337,25 @@ RG_HD float act_apply(int32_t act, float p, float x) {
 }
 
 // QuantTensor scale from an absmax (quantize.rs:20) and its reciprocal (quantize.rs:21).
-RG_HD float quant_scale(float amax) { return amax < 1e-12f ? 1.0f : RG_DIV(amax, 127.0f); }
-RG_HD float quant_inv(float scale) { return RG_DIV(1.0f, scale); }
+// On the device the divisions use div_path<true> for finite operands (amax >= 1e-12
+// and scale in [7.8e-15, 2.7e36]: normal dividends, divisors and quotients); the IEEE
+// division handles infinities.  Equal to the IEEE results for every f32 absmax
+// (checked exhaustively on the device).
+template <bool kNR = true>
+RG_HD float quant_scale(float amax) {
+  if (amax < 1e-12f) return 1.0f;
+#ifdef __CUDA_ARCH__
+  if (kNR && isfinite(amax)) return div_path<true>(amax, 127.0f);
+#endif
+  return RG_DIV(amax, 127.0f);
+}
+template <bool kNR = true>
+RG_HD float quant_inv(float scale) {
+#ifdef __CUDA_ARCH__
+  if (kNR && isfinite(scale)) return div_path<true>(1.0f, scale);
+#endif
+  return RG_DIV(1.0f, scale);
+}
 
 // (v * inv).round().clamp(-127, 127) as i8 (quantize.rs:22): half away from zero, NaN -> 0.
 RG_HD int32_t quant1(float v, float inv) {
@@ -346,6 +363,26 @@ RG_HD int32_t quant1(float v, float inv) {
   if (t != t) return 0;
   return (int32_t)fminf(fmaxf(t, -127.0f), 127.0f);
 }
+
+// Round half away from zero to an integer, for |t| < 2^23 and NaN (-> 0):
+// t + copysign(0.5 - 2^-25, t) rounds (to nearest even) past the next integer
+// exactly when |frac(t)| >= 0.5, so truncating it gives roundf(t); the bias below
+// one half keeps |t| = 0.5 - 2^-25 from rounding up.  The device conversion turns
+// NaN into 0.  Equal to roundf + NaN -> 0 on every f32 with |t| < 2^23 (checked
+// exhaustively on the device).
+RG_HD int32_t round_half_away(float t) {
+#ifdef __CUDA_ARCH__
+  const float h = __uint_as_float((__float_as_uint(t) & 0x80000000u) | 0x3effffffu);
+  return __float2int_rz(__fadd_rn(t, h));
+#else
+  const float r = roundf(t);
+  return r != r ? 0 : (int32_t)r;
+#endif
+}
+
+// quant1 for a value of the tensor whose absmax gave `inv` (|v| <= amax):
+// |v * inv| <= 127 (1 + 3 * 2^-24) < 127.5, so the clamp never acts and is left out.
+RG_HD int32_t quant1_bounded(float v, float inv) { return round_half_away(RG_MUL(v, inv)); }
 
 // Epilogue of int8_gemm_fused (quantize.rs:109-111): act((acc as f32) * cs + bias).
 RG_HD float epilogue(int32_t acc, float cs, float bias, int32_t act, float p) {

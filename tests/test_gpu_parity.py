@@ -193,3 +193,34 @@ def test_fused_cnn_block_matches_unfused_and_oracle(gpu, oracle_lib, special):
     assert_same(unfused.run(x), ref, "unfused")
     prof = fused.last_npu_profile()
     assert prof.kernel_launches < unfused.last_npu_profile().kernel_launches
+
+
+def test_fused_cnn_block_pipeline_depth(gpu, oracle_lib):
+    """1500 images: every CTA of the persistent block kernel runs ~10 images through its
+    rings (input slots, double-buffered operands and TMEM), with special images spread
+    over the batch so the per-image fallback runs mid-pipeline."""
+    layers, x = configs.c2_cnn(1500)
+    x = x.copy()
+    x[7] = 0.0
+    x[300, 0, 1, 2] = np.nan
+    x[301] *= np.float32(1e30)
+    x[777, 0, 9, 9] = np.inf
+    x[1499, 0, 27, 27] = -np.inf
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
+    assert_same(session_for(layers).run(x), ref, "fused, 1500 images")
+
+
+def test_fused_cnn_block_unaligned_input_view(gpu, oracle_lib):
+    """The block kernel bulk-copies images and needs 16-byte aligned input; an input view
+    4 bytes into its allocation takes the op-by-op path with the same results."""
+    torch = gpu
+    layers, x = configs.c2_cnn(5)
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
+    sess = session_for(layers)
+    flat = torch.empty(x.size + 1, dtype=torch.float32, device="cuda")
+    view = flat[1:].view(x.shape)
+    view.copy_(torch.from_numpy(x))
+    assert view.data_ptr() % 16 == 4
+    y = sess.run_device(view)
+    torch.cuda.synchronize()
+    assert_same(y.cpu().numpy(), ref, "unaligned view")

@@ -33,9 +33,11 @@ def test_activation_sweep(gpu, oracle_lib, act, param):
     assert_same(yd.cpu().numpy(), ref, f"act {act}")
 
 
-def test_fast_division_is_exact_on_every_input(gpu):
-    """tanh / GELU divide with Markstein's reciprocal-and-correction sequence; the
-    device self-test compares them with the IEEE division on all 2^32 f32 inputs."""
-    counts = (C.c_uint64 * 2)()
-    _native.check(_native.lib().rg_selftest_tanh_division(counts))
-    assert list(counts) == [0, 0]
+def test_fast_paths_are_exact_on_every_input(gpu):
+    """tanh, GELU, the quantization scale and its reciprocal divide with Markstein's
+    reciprocal-and-correction sequence and quantization rounds by a biased add and
+    truncation; the device self-test compares each with the IEEE division / roundf
+    on all 2^32 f32 inputs."""
+    counts = (C.c_uint64 * 5)()
+    _native.check(_native.lib().rg_selftest_fast_paths(counts))
+    assert list(counts) == [0, 0, 0, 0, 0]
