@@ -68,50 +68,60 @@ def program_macs(sess, x_shape) -> int:
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    """SM clock, power and clock-event (throttle) reasons of the benchmark GPU, polled
+    through NVML every 2 ms while the timed region runs (a timed region of tens of
+    milliseconds is too short for nvidia-smi's 100 ms loop)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4), ("hw_power_brake_slowdown", 0x80))
 
-    def __init__(self, index: int):
-        self.index, self.rows, self.proc = index, [], None
+    def __init__(self, device: int):
+        self.device, self.rows, self.h, self.max_mhz = device, [], None, None
+        self.stop = threading.Event()
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-            t0 = time.time()
-            while not self.rows and time.time() - t0 < 3.0:  # NVML start-up before the timed region
-                time.sleep(0.01)
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(self.device).uuid)
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self.nv = pynvml
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+            self._sample()
             self.rows.clear()
-        except OSError:
-            self.proc = None
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        except Exception:  # no NVML: the line reports no samples
+            self.h = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([v.strip() for v in line.split(",")])
+    def _sample(self):
+        nv = self.nv
+        self.rows.append((float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)),
+                          int(nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)),
+                          nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0))
+
+    def _run(self):
+        while not self.stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            time.sleep(0.002)
 
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        if self.h is not None:
+            self.stop.set()
+            self.t.join(timeout=5)
 
     def summary(self) -> dict:
-        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows if len(r) >= 9 for i in range(4)
-                          if r[5 + i].lower() == "active"})
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+        sm = [r[0] for r in self.rows]
+        reasons = sorted({name for r in self.rows for name, bit in self.REASONS if r[1] & bit})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.rows),
+                "power_w_median": float(np.median([r[2] for r in self.rows])) if self.rows else None,
+                "source": "NVML, 2 ms poll over the timed region"}
 
 
 def measured_peaks() -> dict:

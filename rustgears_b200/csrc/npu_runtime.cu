@@ -172,6 +172,8 @@ struct Session {
   int64_t fp32_bytes = 0, npu_bytes = 0;
   std::vector<Op> ops;
   cudaStream_t stream = nullptr;
+  cudaStream_t copy_stream = nullptr;      // host-input copies that overlap the first op
+  std::vector<cudaEvent_t> chunk_events;   // one per input chunk (timing disabled)
   std::vector<cudaEvent_t> events;
   std::vector<int> ev_of;  // ev_of[i]: event marking the start of op i (ops that launch nothing share one)
   std::mutex mu;
@@ -585,10 +587,26 @@ static rg_status d2h_vec(std::vector<T>& v, const void* src, int64_t n, cudaStre
   return RG_OK;
 }
 
-// Runs the program on device buffers. x_dev is read only; the output is left in
-// the returned pointer (one of the session's activation buffers, or y_dev).
+// Host input fed in chunks: when the program starts with a fused conv block (whose
+// quantization is per image), the input copy is split along the batch on the copy
+// stream and the block runs on each chunk as soon as it has landed, so the PCIe
+// transfer overlaps the block; the ops after the block run once on the whole batch.
+struct HostFeed {
+  const float* x = nullptr;  // host input, nullptr: x_dev already holds the input
+  int64_t chunk = 0;         // images per chunk
+};
+constexpr int64_t kFeedMinChunk = 2048;  // images; smaller chunks underfill the GPU
+constexpr int kFeedMaxChunks = 8;
+
+static bool feed_chunked(const Session& s, const RunPlan& P) {
+  return !s.ops.empty() && P.block_start[0] && !s.trace && P.shapes[0].in[0] >= 2 * kFeedMinChunk;
+}
+
+// Runs the program on device buffers. x_dev is read only (with a HostFeed it is
+// the staging buffer the feed fills); the output is left in y_dev or one of the
+// session's activation buffers.
 static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float* y_dev, cudaStream_t st,
-                         bool record_events) {
+                         bool record_events, const HostFeed& feed = HostFeed()) {
   const size_t n = s.ops.size();
   int64_t max_elems = 1, max_q = 16;
   for (size_t i = 0; i < n; ++i) {
@@ -674,10 +692,32 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         cb.amax = amax + P.amax_off[(size_t)bcons];
         cb.amax_per_image = s.ops[(size_t)bcons].kind == RG_LAYER_CONV2D ? 1 : 0;
       }
-      launch_convblock(cb, s.num_sms, st);
+      if (i == 0 && feed.x) {
+        // chunked host input: copy chunk c on the copy stream, run the block on it
+        const int64_t img_in = os.in_elems / cb.n, img_out = last_os.out_elems / cb.n;
+        float* xs = const_cast<float*>(cur);
+        int c = 0;
+        for (int64_t off = 0; off < cb.n; off += feed.chunk, ++c) {
+          const int64_t cnt = std::min<int64_t>(feed.chunk, cb.n - off);
+          RG_CUDA_TRY(cudaMemcpyAsync(xs + off * img_in, feed.x + off * img_in, (size_t)(cnt * img_in) * 4,
+                                      cudaMemcpyHostToDevice, s.copy_stream));
+          RG_CUDA_TRY(cudaEventRecord(s.chunk_events[(size_t)c], s.copy_stream));
+          RG_CUDA_TRY(cudaStreamWaitEvent(st, s.chunk_events[(size_t)c], 0));
+          ConvBlockArgs cc = cb;
+          cc.x = xs + off * img_in;
+          cc.n = cnt;
+          cc.out = bdst + off * img_out;
+          if (cb.amax && cb.amax_per_image) cc.amax = cb.amax + off;
+          launch_convblock(cc, s.num_sms, st);
+          ++launches;
+          RG_LAUNCHED("convblock");
+        }
+      } else {
+        launch_convblock(cb, s.num_sms, st);
+        ++launches;
+        RG_LAUNCHED("convblock");
+      }
       s.used_tc = true;
-      ++launches;
-      RG_LAUNCHED("convblock");
       cur = bdst;
       (void)last_os;
       if (record_events) RG_CUDA_TRY(cudaEventRecord(s.events[(size_t)next_ev], st));
@@ -992,6 +1032,9 @@ rg_status rg_session_create(const rg_layer_spec* layers, int32_t n_layers, const
   s.device = o.device; s.precision = o.precision; s.weight_quant = o.weight_quant; s.flags = o.flags;
   RG_CUDA_TRY(cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, o.device));
   RG_CUDA_TRY(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking));
+  RG_CUDA_TRY(cudaStreamCreateWithFlags(&s.copy_stream, cudaStreamNonBlocking));
+  s.chunk_events.assign(kFeedMaxChunks, nullptr);
+  for (auto& e : s.chunk_events) RG_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   RG_TRY(compile(s, layers, n_layers));
   *out = h.release();
   return RG_OK;
@@ -1009,9 +1052,13 @@ void rg_session_destroy(rg_session* h) {
   Session& s = h->s;
   cudaSetDevice(s.device);
   if (s.stream) cudaStreamSynchronize(s.stream);
+  if (s.copy_stream) cudaStreamSynchronize(s.copy_stream);
   if (s.comm) ncclCommDestroy(s.comm);
   for (cudaEvent_t e : s.events) cudaEventDestroy(e);
+  for (cudaEvent_t e : s.chunk_events)
+    if (e) cudaEventDestroy(e);
   if (s.stream) cudaStreamDestroy(s.stream);
+  if (s.copy_stream) cudaStreamDestroy(s.copy_stream);
   delete h;
 }
 
@@ -1051,10 +1098,22 @@ static rg_status run_impl(rg_session* h, const float* x, bool x_host, const int6
     RG_CUDA_TRY(cudaEventRecord(t0, st));
   }
   const float* xd = x;
+  HostFeed feed;
   if (x_host) {
     RG_TRY(s.xin.ensure((size_t)std::max<int64_t>(in_elems, 1) * 4));
-    RG_CUDA_TRY(cudaMemcpyAsync(s.xin.p, x, (size_t)in_elems * 4, cudaMemcpyHostToDevice, st));
     xd = s.xin.as<float>();
+    if (feed_chunked(s, P)) {
+      const int64_t batch = P.shapes[0].in[0];
+      feed.x = x;
+      feed.chunk = std::max<int64_t>(kFeedMinChunk, (batch + kFeedMaxChunks - 1) / kFeedMaxChunks);
+      // the copy stream must not overwrite the staging buffer before earlier work on
+      // this stream (a previous run's reads of it) is done
+      cudaEvent_t ready = s.chunk_events[0];
+      RG_CUDA_TRY(cudaEventRecord(ready, st));
+      RG_CUDA_TRY(cudaStreamWaitEvent(s.copy_stream, ready, 0));
+    } else {
+      RG_CUDA_TRY(cudaMemcpyAsync(s.xin.p, x, (size_t)in_elems * 4, cudaMemcpyHostToDevice, st));
+    }
   }
   float* yd = y;
   if (y_host) {
@@ -1066,7 +1125,7 @@ static rg_status run_impl(rg_session* h, const float* x, bool x_host, const int6
     if (in_elems) RG_CUDA_TRY(cudaMemcpyAsync(yd, xd, (size_t)in_elems * 4, cudaMemcpyDeviceToDevice, st));
     rs = RG_OK;
   } else {
-    rs = execute(s, xd, P, yd, st, events);
+    rs = execute(s, xd, P, yd, st, events, feed);
   }
   if (rs != RG_OK) {
     if (t0) cudaEventDestroy(t0);

@@ -224,3 +224,19 @@ def test_fused_cnn_block_unaligned_input_view(gpu, oracle_lib):
     y = sess.run_device(view)
     torch.cuda.synchronize()
     assert_same(y.cpu().numpy(), ref, "unaligned view")
+
+
+def test_host_input_fed_in_chunks(gpu, oracle_lib):
+    """A host-buffer run of a program that starts with the fused CNN block copies the
+    input in chunks on a second stream and runs the block per chunk (6000 images: three
+    chunks); results equal the oracle, special images on both sides of a chunk edge."""
+    layers, x = configs.c2_cnn(6000)
+    x = x.copy()
+    x[2047, 0, 0, 0] = np.inf
+    x[2048] = 0.0
+    x[4095, 0, 13, 13] = np.nan
+    x[5999] *= np.float32(-3.0)
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
+    sess = session_for(layers)
+    assert_same(sess.run(x), ref, "chunked host input")
+    assert_same(sess.run(x), ref, "chunked host input, second run")
