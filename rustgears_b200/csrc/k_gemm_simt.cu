@@ -7,6 +7,8 @@
 // as an implicit GEMM: the A operand is gathered on the fly from the
 // per-image-quantized NHWC i8 activation (rows = (image, oy, ox), reduction =
 // (ky, kx, c)), replacing the reference's im2col + transpose + quantize.
+#include <algorithm>
+
 #include "rg_kernels.h"
 #include "rg_math.cuh"
 
@@ -176,12 +178,29 @@ constexpr int kNarrowMaxN = 32;
 // over the block's contiguous [rows, n] output range: coalesced stores, and one
 // copy of the activation code rather than NT unrolled copies.  Used for the last
 // Linear layers (N = 3, 10, 32 ...) where a 128-wide tensor-core tile is mostly idle.
-template <int NT>
+// Four f32 values of row `row` from column k0 (zero past af_k), quantized, packed.
+__device__ __forceinline__ int32_t load_q4(const GemmArgs& p, const float* row, int64_t k0, bool vec, float inv) {
+  float4 v;
+  if (vec && k0 + 4 <= p.af_k) {
+    v = __ldg(reinterpret_cast<const float4*>(row + k0));
+  } else {
+    v.x = k0 < p.af_k ? __ldg(row + k0) : 0.0f;
+    v.y = k0 + 1 < p.af_k ? __ldg(row + k0 + 1) : 0.0f;
+    v.z = k0 + 2 < p.af_k ? __ldg(row + k0 + 2) : 0.0f;
+    v.w = k0 + 3 < p.af_k ? __ldg(row + k0 + 3) : 0.0f;
+  }
+  return (int32_t)((uint32_t)(quant1_bounded(v.x, inv) & 0xff) | ((uint32_t)(quant1_bounded(v.y, inv) & 0xff) << 8) |
+                   ((uint32_t)(quant1_bounded(v.z, inv) & 0xff) << 16) |
+                   ((uint32_t)(quant1_bounded(v.w, inv) & 0xff) << 24));
+}
+
+template <int NT, bool QA, int TPR>
 __global__ void __launch_bounds__(kNarrowThreads) k_gemm_narrow(const GemmArgs p) {
+  constexpr int RPB = kNarrowThreads / TPR;  // rows per block; TPR threads share a row's K
   extern __shared__ __align__(16) int32_t sm[];
   const int kw = (int)(p.k >> 2);
   int32_t* wsm = sm;                                        // [NT][kw], rows >= n are zero
-  int32_t* tile = sm + NT * kw;                             // [kNarrowThreads][NT + 1]
+  int32_t* tile = sm + NT * kw;                             // [RPB][NT + 1]
   float* cs_sm = reinterpret_cast<float*>(tile + kNarrowThreads * (NT + 1));  // [NT]
   float* bias_sm = cs_sm + NT;                                                // [NT]
 #pragma unroll 4
@@ -189,47 +208,87 @@ __global__ void __launch_bounds__(kNarrowThreads) k_gemm_narrow(const GemmArgs p
     const int c = i / kw, w = i - c * kw;
     wsm[i] = c < (int)p.n ? __ldg(reinterpret_cast<const int32_t*>(p.w + (int64_t)c * p.ldb) + w) : 0;
   }
+  float sa = 0.0f, inv = 0.0f;
+  if (QA) {
+    sa = quant_scale(__uint_as_float(*p.af_amax));
+    inv = quant_inv(sa);
+  } else {
+    sa = p.a_scale[0];
+  }
   if (threadIdx.x < (unsigned)p.n) {
     const float sw = p.w_scale_ch ? p.w_scale_ch[threadIdx.x] : p.w_scale;
-    cs_sm[threadIdx.x] = __fmul_rn(p.a_scale[0], sw);
+    cs_sm[threadIdx.x] = __fmul_rn(sa, sw);
     bias_sm[threadIdx.x] = p.bias[threadIdx.x];
   }
   __syncthreads();
-  const int64_t r0 = (int64_t)blockIdx.x * kNarrowThreads;
-  const int rows = (int)min((int64_t)kNarrowThreads, p.m - r0);
-  if ((int)threadIdx.x < rows) {
+  const int lr = threadIdx.x / TPR, part = threadIdx.x % TPR;
+  const int groups = kw / 4 / TPR;  // 16-element K groups of this thread
+  const int n = (int)p.n;
+  const uint32_t magic = n > 1 ? (uint32_t)((0x100000000ull + (uint64_t)n - 1) / (uint64_t)n) : 0u;
+  float mx = 0.0f;
+  // persistent: the block walks row tiles of RPB rows with its staged weights
+  for (int64_t r0 = (int64_t)blockIdx.x * RPB; r0 < p.m; r0 += (int64_t)gridDim.x * RPB) {
+    const int rows = (int)min((int64_t)RPB, p.m - r0);
     int32_t acc[NT];
 #pragma unroll
     for (int j = 0; j < NT; ++j) acc[j] = 0;
-    const int4* arow = reinterpret_cast<const int4*>(p.a + (r0 + threadIdx.x) * p.lda);
-#pragma unroll 8
-    for (int k4 = 0; k4 < kw / 4; ++k4) {
-      const int4 av = __ldg(arow + k4);
+    if (lr < rows) {
+      if (QA) {
+        const float* row = p.af + (r0 + lr) * p.af_k;
+        const bool vec = (p.af_k & 3) == 0 && (reinterpret_cast<uintptr_t>(p.af) & 15) == 0;
+#pragma unroll 2
+        for (int gi = 0; gi < groups; ++gi) {
+          const int k4 = part * groups + gi;
+          const int32_t a0 = load_q4(p, row, 16 * k4, vec, inv), a1 = load_q4(p, row, 16 * k4 + 4, vec, inv),
+                        a2 = load_q4(p, row, 16 * k4 + 8, vec, inv), a3 = load_q4(p, row, 16 * k4 + 12, vec, inv);
 #pragma unroll
-      for (int j = 0; j < NT; ++j) {
-        const int4 wv = *reinterpret_cast<const int4*>(wsm + j * kw + 4 * k4);
-        acc[j] = __dp4a(av.x, wv.x, acc[j]);
-        acc[j] = __dp4a(av.y, wv.y, acc[j]);
-        acc[j] = __dp4a(av.z, wv.z, acc[j]);
-        acc[j] = __dp4a(av.w, wv.w, acc[j]);
+          for (int j = 0; j < NT; ++j) {
+            const int4 wv = *reinterpret_cast<const int4*>(wsm + j * kw + 4 * k4);
+            acc[j] = __dp4a(a0, wv.x, acc[j]);
+            acc[j] = __dp4a(a1, wv.y, acc[j]);
+            acc[j] = __dp4a(a2, wv.z, acc[j]);
+            acc[j] = __dp4a(a3, wv.w, acc[j]);
+          }
+        }
+      } else {
+        const int4* arow = reinterpret_cast<const int4*>(p.a + (r0 + lr) * p.lda);
+#pragma unroll 4
+        for (int gi = 0; gi < groups; ++gi) {
+          const int k4 = part * groups + gi;
+          const int4 av = __ldg(arow + k4);
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            const int4 wv = *reinterpret_cast<const int4*>(wsm + j * kw + 4 * k4);
+            acc[j] = __dp4a(av.x, wv.x, acc[j]);
+            acc[j] = __dp4a(av.y, wv.y, acc[j]);
+            acc[j] = __dp4a(av.z, wv.z, acc[j]);
+            acc[j] = __dp4a(av.w, wv.w, acc[j]);
+          }
+        }
       }
     }
+    // integer partial sums of one row: exact in any order
 #pragma unroll
-    for (int j = 0; j < NT; ++j) tile[threadIdx.x * (NT + 1) + j] = acc[j];
-  }
-  __syncthreads();
-  const int n = (int)p.n;
-  float* out = p.out + r0 * n;
-  int32_t* accd = p.acc ? p.acc + r0 * n : nullptr;
-  float mx = 0.0f;
-#pragma unroll 1
-  for (int e = threadIdx.x; e < rows * n; e += kNarrowThreads) {
-    const int rr = e / n, j = e - rr * n;
-    const int32_t a = tile[rr * (NT + 1) + j];
-    const float v = epilogue(a, cs_sm[j], bias_sm[j], p.act, p.act_param);
-    out[e] = v;
-    if (accd) accd[e] = a;
-    mx = fmaxf(mx, fabsf(v));
+    for (int o = TPR / 2; o > 0; o >>= 1)
+#pragma unroll
+      for (int j = 0; j < NT; ++j) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+    if (lr < rows && part == 0)
+#pragma unroll
+      for (int j = 0; j < NT; ++j) tile[lr * (NT + 1) + j] = acc[j];
+    __syncthreads();
+    float* out = p.out + r0 * n;
+    int32_t* accd = p.acc ? p.acc + r0 * n : nullptr;
+#pragma unroll 4
+    for (int e = threadIdx.x; e < rows * n; e += kNarrowThreads) {
+      // e / n as a multiply-high by ceil(2^32 / n): exact for e < 2^16, 2 <= n <= 32
+      const int rr = n == 1 ? e : (int)__umulhi((uint32_t)e, magic), j = e - rr * n;
+      const int32_t a = tile[rr * (NT + 1) + j];
+      const float v = epilogue(a, cs_sm[j], bias_sm[j], p.act, p.act_param);
+      out[e] = v;
+      if (accd) accd[e] = a;
+      mx = fmaxf(mx, fabsf(v));
+    }
+    __syncthreads();  // the tile is rewritten by the next row tile
   }
   if (p.amax.ptr) flush_max(p.amax.ptr, 0, mx);
 }
@@ -240,20 +299,57 @@ size_t narrow_smem(int nt, int64_t k) { return (size_t)nt * k + (size_t)kNarrowT
 }  // namespace
 
 bool gemm_narrow_eligible(const GemmArgs& a) {
+  const bool a_ok = a.af ? (a.af_amax != nullptr && a.af_k <= a.k)
+                         : (a.lda == a.k && (reinterpret_cast<uintptr_t>(a.a) & 15) == 0);
   return a.n >= 1 && a.n <= kNarrowMaxN && narrow_smem(narrow_width(a.n), a.k) <= 48 * 1024 && !a.conv &&
-         a.out_l == 0 && a.rows_per_scale == 0 && a.amax.elems_per_slot == 0 && (a.k & 15) == 0 && a.lda == a.k && a.ldb >= a.k &&
-         ((reinterpret_cast<uintptr_t>(a.a) | reinterpret_cast<uintptr_t>(a.w)) & 15) == 0 && (a.ldb & 3) == 0;
+         a.out_l == 0 && a.rows_per_scale == 0 && a.amax.elems_per_slot == 0 && (a.k & 15) == 0 && a_ok &&
+         a.ldb >= a.k && (reinterpret_cast<uintptr_t>(a.w) & 15) == 0 && (a.ldb & 3) == 0;
+}
+
+template <int NT, bool QA, int TPR>
+void launch_narrow_k(const GemmArgs& a, size_t sm, cudaStream_t st) {
+  // persistent grid: as many blocks as are resident at once (at most one per row tile)
+  static int per_sm = 0, num_sms = 0;
+  if (per_sm == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_gemm_narrow<NT, QA, TPR>, kNarrowThreads, sm);
+    if (per_sm < 1) per_sm = 1;
+  }
+  const int64_t rpb = kNarrowThreads / TPR, tiles = (a.m + rpb - 1) / rpb;
+  const int grid = (int)std::min<int64_t>(tiles, (int64_t)per_sm * num_sms);
+  k_gemm_narrow<NT, QA, TPR><<<grid, kNarrowThreads, sm, st>>>(a);
+}
+
+template <int NT, bool QA>
+void launch_narrow_tpr(const GemmArgs& a, size_t sm, cudaStream_t st) {
+  const int groups = (int)(a.k / 16);  // 16-element K groups per row
+  const int tpr = groups % 8 == 0 ? 8 : groups % 4 == 0 ? 4 : groups % 2 == 0 ? 2 : 1;
+  switch (tpr) {
+    case 8: launch_narrow_k<NT, QA, 8>(a, sm, st); break;
+    case 4: launch_narrow_k<NT, QA, 4>(a, sm, st); break;
+    case 2: launch_narrow_k<NT, QA, 2>(a, sm, st); break;
+    default: launch_narrow_k<NT, QA, 1>(a, sm, st); break;
+  }
+}
+
+template <bool QA>
+void launch_narrow_q(const GemmArgs& a, cudaStream_t st) {
+  const int nt = narrow_width(a.n);
+  const size_t sm = narrow_smem(nt, a.k);
+  switch (nt) {
+    case 4: launch_narrow_tpr<4, QA>(a, sm, st); break;
+    case 8: launch_narrow_tpr<8, QA>(a, sm, st); break;
+    case 16: launch_narrow_tpr<16, QA>(a, sm, st); break;
+    default: launch_narrow_tpr<32, QA>(a, sm, st); break;
+  }
 }
 
 void launch_gemm_narrow(const GemmArgs& a, cudaStream_t st) {
   if (a.m <= 0) return;
-  const int grid = (int)((a.m + kNarrowThreads - 1) / kNarrowThreads);
-  switch (narrow_width(a.n)) {
-    case 4: k_gemm_narrow<4><<<grid, kNarrowThreads, narrow_smem(4, a.k), st>>>(a); break;
-    case 8: k_gemm_narrow<8><<<grid, kNarrowThreads, narrow_smem(8, a.k), st>>>(a); break;
-    case 16: k_gemm_narrow<16><<<grid, kNarrowThreads, narrow_smem(16, a.k), st>>>(a); break;
-    default: k_gemm_narrow<32><<<grid, kNarrowThreads, narrow_smem(32, a.k), st>>>(a); break;
-  }
+  if (a.af) launch_narrow_q<true>(a, st);
+  else launch_narrow_q<false>(a, st);
 }
 
 void launch_gemm_simt(const GemmArgs& a, cudaStream_t st) {

@@ -739,18 +739,30 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         float* my_scale = scales + P.amax_off[i];
         int8_t* q = s.qbuf.as<int8_t>();
         GemmArgs g;
+        bool fused_q = false;
         if (op.kind == RG_LAYER_LINEAR) {
           const int64_t rows = os.in_elems / op.in_f;
           if (P.amax_src[i] < 0) { launch_absmax(cur, os.in_elems, my_amax, st); ++launches; RG_LAUNCHED("absmax"); }
           if (s.comm && s.world > 1)
             RG_NCCL_TRY(ncclAllReduce(my_amax, my_amax, 1, ncclUint32, ncclMax, s.comm, st));
-          launch_quantize_rows(cur, rows, op.in_f, op.kpad, my_amax, q, my_scale, st);
-          ++launches;
-          RG_LAUNCHED("quantize_rows");
-          g.a = q; g.lda = op.kpad; g.conv = false;
+          g.conv = false;
           g.m = rows; g.n = op.out_f; g.k = op.kpad;
           g.rows_per_scale = 0;
           g.out_l = 0;
+          // Narrow layers read the f32 activation and quantize it while loading (one
+          // launch, one pass); trace runs keep the separate quantizer (they record A_q).
+          GemmArgs gf = g;
+          gf.af = cur; gf.af_k = op.in_f; gf.af_amax = my_amax;
+          gf.w = op.d_w.as<int8_t>(); gf.ldb = op.kpad; gf.amax = sink;
+          fused_q = !s.trace && gemm_narrow_eligible(gf);
+          if (fused_q) {
+            g.af = cur; g.af_k = op.in_f; g.af_amax = my_amax;
+          } else {
+            launch_quantize_rows(cur, rows, op.in_f, op.kpad, my_amax, q, my_scale, st);
+            ++launches;
+            RG_LAUNCHED("quantize_rows");
+            g.a = q; g.lda = op.kpad;
+          }
         } else {
           const int64_t N = os.in[0];
           const int32_t C = op.in_c, H = (int32_t)os.in[2], W = (int32_t)os.in[3];
@@ -775,8 +787,8 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         g.out = dst;
         g.acc = s.trace ? s.accbuf.as<int32_t>() : nullptr;
         g.amax = sink;
-        const bool tc = gemm_tc_eligible(g);
-        const bool narrow = !tc && gemm_narrow_eligible(g);
+        const bool tc = !fused_q && gemm_tc_eligible(g);
+        const bool narrow = fused_q || (!tc && gemm_narrow_eligible(g));
         if (tc) {
           if (!launch_gemm_tc(g, s.num_sms, st)) return fail(RG_ERR_CUDA, "op %zu: TMA descriptor encoding failed", i);
           s.used_tc = true;

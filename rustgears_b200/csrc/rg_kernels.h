@@ -43,6 +43,11 @@ struct GemmArgs {
   // A: dense i8 [m, lda] (conv == false) or gathered from NHWC i8 (conv == true)
   const int8_t* a = nullptr;
   int64_t lda = 0;
+  // ... or f32 [m, af_k] row-major, quantized while it is loaded with the per-tensor
+  // scale of absmax *af_amax (kernels that support it; a and a_scale are then unused)
+  const float* af = nullptr;
+  int64_t af_k = 0;
+  const unsigned* af_amax = nullptr;
   bool conv = false;
   ConvGeom g;
   // B: weights [n, ldb] i8, K-contiguous (ldb multiple of 16, zero-padded)
@@ -64,7 +69,8 @@ struct GemmArgs {
 };
 
 void launch_gemm_simt(const GemmArgs& a, cudaStream_t st);
-// Narrow dense GEMM (N <= 32) on the CUDA cores: one thread per output row.
+// Narrow dense GEMM (N <= 32) on the CUDA cores: one thread per output row; takes an
+// i8 A, or an f32 A (af) that it quantizes on the fly.
 bool gemm_narrow_eligible(const GemmArgs& a);
 void launch_gemm_narrow(const GemmArgs& a, cudaStream_t st);
 // tcgen05 path.  eligible(): shape/alignment/driver checks.  launch() returns false

@@ -68,7 +68,8 @@ def test_configs_at_batch(gpu, oracle_lib, case, batch):
     assert_same(session_for(layers).run(x), ref, f"{case} batch {batch}")
 
 
-@pytest.mark.parametrize("mkn", [(1, 16, 16), (77, 100, 33), (256, 512, 384), (130, 1568, 128), (64, 4, 3)])
+@pytest.mark.parametrize("mkn", [(1, 16, 16), (77, 100, 33), (256, 512, 384), (130, 1568, 128), (64, 4, 3),
+                                 (300, 7, 1), (129, 33, 5), (1000, 100, 17), (70, 3, 32)])
 def test_linear_shapes(gpu, oracle_lib, mkn):
     m, k, n = mkn
     layers, x = configs.c3_linear(m, k, n, seed=m + k + n)
@@ -78,6 +79,8 @@ def test_linear_shapes(gpu, oracle_lib, mkn):
     sess.set_trace(True)
     assert_same(sess.run(x), ref, f"linear {mkn}")
     assert_same(sess.trace(0, _native.RG_TRACE_ACC).reshape(m, n), trace[0]["acc"], "acc")
+    # without tracing, narrow layers quantize their f32 input while loading it
+    assert_same(session_for(layers).run(x), ref, f"linear {mkn}, untraced")
 
 
 def test_empty_batch(gpu, oracle_lib):
