@@ -58,7 +58,15 @@ typedef enum rg_layer_kind {
   RG_LAYER_MAXPOOL2D = 4,       /* kernel, stride; no padding */
   RG_LAYER_FLATTEN = 5,
   RG_LAYER_ACTIVATION = 6,      /* act, act_param */
-  RG_LAYER_SOFTMAX = 7
+  RG_LAYER_SOFTMAX = 7,
+  /* Extensions (no reference LayerSpec or .rtim tag): residual blocks and adaptive
+   * average pooling, for ResNet-style networks.  A block is
+   *   RESIDUAL_BEGIN, <main-path layers>, [SHORTCUT_CONV2D, ChannelAffine], RESIDUAL_END
+   * and computes y = act(main(x) + shortcut(x)) with shortcut = identity or the conv. */
+  RG_LAYER_RESIDUAL_BEGIN = 8,        /* saves the current activation as the block input */
+  RG_LAYER_RESIDUAL_END = 9,          /* y = act(x + saved) with act, act_param; pops the saved input */
+  RG_LAYER_SHORTCUT_CONV2D = 10,      /* Conv2d fields; applied to the saved input, replacing it */
+  RG_LAYER_ADAPTIVE_AVGPOOL2D = 11    /* output size: kernel = height, stride = width */
 } rg_layer_kind;
 
 typedef enum rg_activation {

@@ -13,8 +13,8 @@ from __future__ import annotations
 
 import numpy as np
 
-from .oracle import (ACT_GELU, ACT_RELU, ACTIVATION, CHANNEL_AFFINE, CONV2D, FLATTEN, LINEAR,
-                     MAXPOOL2D, Rng)
+from .oracle import (ACT_GELU, ACT_RELU, ACTIVATION, ADAPTIVE_AVGPOOL2D, CHANNEL_AFFINE, CONV2D, FLATTEN,
+                     LINEAR, MAXPOOL2D, RESIDUAL_BEGIN, RESIDUAL_END, SHORTCUT_CONV2D, Rng)
 
 
 def linear(rng: Rng, fin: int, fout: int) -> dict:  # Linear::new (nn/layers.rs:27-34)
@@ -144,6 +144,48 @@ def affine_first(batch: int = 6, seed: int = 5):
     return layers, x
 
 
+def basic_block(rng: Rng, cin: int, cout: int, stride: int) -> list:
+    """ResNet basic block (extension kinds): conv3x3/stride + BN + ReLU, conv3x3 + BN,
+    projection conv1x1/stride + BN when the shape changes, add, ReLU.  Weights are
+    drawn conv1, conv2, projection (construction order)."""
+    layers = [dict(kind=RESIDUAL_BEGIN), conv2d(rng, cin, cout, 3, stride, 1), batchnorm(cout), act(ACT_RELU),
+              conv2d(rng, cout, cout, 3, 1, 1), batchnorm(cout)]
+    if stride != 1 or cin != cout:
+        sc = conv2d(rng, cin, cout, 1, stride, 0)
+        sc["kind"] = SHORTCUT_CONV2D
+        layers += [sc, batchnorm(cout)]
+    return layers + [dict(kind=RESIDUAL_END, act=ACT_RELU, act_param=0.0)]
+
+
+def resnet(batch: int, image: int, widths, classes: int, seed: int = 42, stem_k: int = 7):
+    """ResNet-18 layout: conv7x7/2 p3 + BN + ReLU, MaxPool 3x3/2
+    (pad 0, the reference's max_pool2d), 4 stages of 2 basic blocks (first block of
+    stages 2-4 stride 2 with a projection), AdaptiveAvgPool2d(1), Flatten, Linear.
+    x ~ N(0,1) [batch, 3, image, image].  Conv and Linear weights are drawn in module
+    order, then the BatchNorm statistics, then the input."""
+    rng = Rng(seed)
+    layers = [conv2d(rng, 3, widths[0], stem_k, 2, stem_k // 2), batchnorm(widths[0]), act(ACT_RELU),
+              dict(kind=MAXPOOL2D, kernel=3, stride=2)]
+    cin = widths[0]
+    for si, w in enumerate(widths):
+        for bi in range(2):
+            layers += basic_block(rng, cin, w, 2 if (si > 0 and bi == 0) else 1)
+            cin = w
+    layers += [dict(kind=ADAPTIVE_AVGPOOL2D, kernel=1, stride=1), dict(kind=FLATTEN), linear(rng, cin, classes)]
+    layers = draw_bn_stats(rng, layers)
+    x = rng.randn((batch, 3, image, image))
+    return layers, x
+
+
+def resnet18(batch: int = 2, image: int = 224, seed: int = 42):
+    return resnet(batch, image, (64, 128, 256, 512), 1000, seed)
+
+
+def resnet_mini(batch: int = 3, seed: int = 9):
+    """Two-stage residual net on 24x24 inputs (identity and projection blocks)."""
+    return resnet(batch, 24, (8, 16), 10, seed, stem_k=3)
+
+
 # name -> builder of (layers, x) used by the golden fixtures and the parity tests
 CASES = {
     "usage_doc": usage_doc_model,
@@ -154,4 +196,5 @@ CASES = {
     "acts_mlp": acts_mlp,
     "strided_cnn": strided_cnn,
     "affine_first": affine_first,
+    "resnet_mini": resnet_mini,
 }

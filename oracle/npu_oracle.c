@@ -14,6 +14,8 @@
  */
 #include "npu_oracle.h"
 
+#define OG_MAX_RESIDUAL 8
+
 #include <math.h>
 #include <pthread.h>
 #include <stdio.h>
@@ -283,6 +285,29 @@ void og_activation(const float* x, int64_t n, int32_t act, float param, float* y
   for (int64_t i = 0; i < n; ++i) y[i] = og_act_apply(act, param, x[i]);
 }
 
+/* Extension: adaptive_avg_pool2d (tensor/ops.rs:994-1014): region rows
+ * [y*h/oh, ceil((y+1)*h/oh)), columns likewise; f32 sum in row-major order from 0,
+ * then one division by the region's element count. */
+void og_adaptive_avgpool2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t oh,
+                           int32_t ow, float* y) {
+  for (int64_t plane = 0; plane < n * c; ++plane)
+    for (int32_t oy = 0; oy < oh; ++oy)
+      for (int32_t ox = 0; ox < ow; ++ox) {
+        const int32_t y0 = oy * h / oh, y1 = ((oy + 1) * h + oh - 1) / oh;
+        const int32_t x0 = ox * w / ow, x1 = ((ox + 1) * w + ow - 1) / ow;
+        float sum = 0.0f;
+        for (int32_t yy = y0; yy < y1; ++yy)
+          for (int32_t xx = x0; xx < x1; ++xx) sum += x[(plane * h + yy) * w + xx];
+        y[(plane * oh + oy) * ow + ox] = sum / (float)((y1 - y0) * (x1 - x0));
+      }
+}
+
+/* Extension: residual add (tensor/ops.rs:67-76 binary Add, same shapes) followed by
+ * the block's activation: y = act(x + s). */
+void og_residual_add(const float* x, const float* sv, int64_t n, int32_t act, float param, float* y) {
+  for (int64_t i = 0; i < n; ++i) y[i] = og_act_apply(act, param, x[i] + sv[i]);
+}
+
 void og_softmax(const float* x, int64_t outer, int64_t last, float* y) { /* ops.rs:1058-1076 */
   for (int64_t o = 0; o < outer; ++o) {
     const float* xr = x + o * last; float* yr = y + o * last;
@@ -316,7 +341,7 @@ static og_flayer* og_fold(const og_layer* L, int32_t n, int32_t* out_n) {
         for (int64_t j = 0; j < p->out_f; ++j) { float t = p->b[j] * l->weight[j]; p->b[j] = t + l->bias[j]; }
         continue;
       }
-      if (p->kind == OG_LAYER_CONV2D && p->out_c == c) {
+      if ((p->kind == OG_LAYER_CONV2D || p->kind == OG_LAYER_SHORTCUT_CONV2D) && p->out_c == c) {
         int64_t plane = (int64_t)p->in_c * p->k * p->k;
         for (int64_t o = 0; o < p->out_c; ++o) {
           for (int64_t j = 0; j < plane; ++j) p->w[o * plane + j] *= l->weight[o];
@@ -357,7 +382,10 @@ og_program* og_compile(const og_layer* layers, int32_t n_layers, int32_t precisi
     int32_t next_act = (i + 1 < m && f[i + 1].kind == OG_LAYER_ACTIVATION);
     og_op* op = &p->ops[nops];
     memset(op, 0, sizeof(*op));
-    if (l->kind == OG_LAYER_LINEAR || l->kind == OG_LAYER_CONV2D) {
+    if (l->kind == OG_LAYER_LINEAR || l->kind == OG_LAYER_CONV2D || l->kind == OG_LAYER_SHORTCUT_CONV2D) {
+      /* a shortcut conv works on the saved block input: an Activation after it belongs
+       * to the main path, so it is not fused */
+      if (l->kind == OG_LAYER_SHORTCUT_CONV2D) next_act = 0;
       op->kind = l->kind;
       op->act = next_act ? f[i + 1].act : OG_ACT_NONE;
       op->act_param = next_act ? f[i + 1].param : 0.0f;
@@ -450,6 +478,13 @@ int32_t og_op_label(const og_op* op, char* buf, int32_t cap) { /* npu.rs:83-104 
     case OG_LAYER_FLATTEN: return snprintf(buf, (size_t)cap, "NPU::Flatten");
     case OG_LAYER_ACTIVATION: return snprintf(buf, (size_t)cap, "NPU::Act(%s)", an);
     case OG_LAYER_SOFTMAX: return snprintf(buf, (size_t)cap, "NPU::Softmax");
+    case OG_LAYER_RESIDUAL_BEGIN: return snprintf(buf, (size_t)cap, "NPU::ResidualBegin");
+    case OG_LAYER_RESIDUAL_END:
+      if (op->act == OG_ACT_NONE) return snprintf(buf, (size_t)cap, "NPU::ResidualAdd");
+      return snprintf(buf, (size_t)cap, "NPU::ResidualAdd(%s)", an);
+    case OG_LAYER_SHORTCUT_CONV2D:
+      return snprintf(buf, (size_t)cap, "NPU::ShortcutConv2d(%d->%d, k=%d)", op->in_channels, op->out_channels, op->kernel);
+    case OG_LAYER_ADAPTIVE_AVGPOOL2D: return snprintf(buf, (size_t)cap, "NPU::AdaptiveAvgPool2d(%dx%d)", op->kernel, op->stride);
     default: return snprintf(buf, (size_t)cap, "NPU::?");
   }
 }
@@ -567,6 +602,10 @@ int32_t og_execute(const og_program* p, const float* x, const int64_t* shape, in
   for (int32_t i = 0; i < ndim; ++i) { sh[i] = shape[i]; len *= shape[i]; }
   float* data = (float*)malloc(sizeof(float) * (size_t)(len > 0 ? len : 1));
   memcpy(data, x, sizeof(float) * (size_t)len);
+  /* residual blocks (extension): a stack of saved block inputs */
+  float* saved[OG_MAX_RESIDUAL]; int64_t saved_sh[OG_MAX_RESIDUAL][8], saved_len[OG_MAX_RESIDUAL];
+  int32_t saved_nd[OG_MAX_RESIDUAL], depth = 0;
+#define OG_EXEC_FAIL(rc) do { for (int32_t d_ = 0; d_ < depth; ++d_) free(saved[d_]); free(data); return (rc); } while (0)
   for (int32_t oi = 0; oi < p->n_ops; ++oi) {
     const og_op* op = &p->ops[oi];
     int64_t t0 = og_now_ns(), macs = 0;
@@ -581,11 +620,11 @@ int32_t og_execute(const og_program* p, const float* x, const int64_t* shape, in
         break;
       }
       case OG_LAYER_CONV2D: {
-        if (nd != 4 || sh[1] != op->in_channels) { free(data); return -2; }
+        if (nd != 4 || sh[1] != op->in_channels) OG_EXEC_FAIL(-2);
         int64_t n = sh[0], h = sh[2], w = sh[3];
         int64_t oh = og_out_size(h, op->kernel, op->stride, op->padding);
         int64_t ow = og_out_size(w, op->kernel, op->stride, op->padding);
-        if (oh <= 0 || ow <= 0) { free(data); return -2; }
+        if (oh <= 0 || ow <= 0) OG_EXEC_FAIL(-2);
         macs = n * op->out_channels * (int64_t)op->in_channels * op->kernel * op->kernel * oh * ow;
         out = (float*)malloc(sizeof(float) * (size_t)(n * op->out_channels * oh * ow > 0 ? n * op->out_channels * oh * ow : 1));
         og_op_conv2d(op, data, n, (int32_t)h, (int32_t)w, out, NULL, NULL, NULL, nthreads);
@@ -593,9 +632,9 @@ int32_t og_execute(const og_program* p, const float* x, const int64_t* shape, in
         break;
       }
       case OG_LAYER_MAXPOOL2D: {
-        if (nd != 4) { free(data); return -2; }
+        if (nd != 4) OG_EXEC_FAIL(-2);
         int64_t oh = og_out_size(sh[2], op->kernel, op->stride, 0), ow = og_out_size(sh[3], op->kernel, op->stride, 0);
-        if (oh <= 0 || ow <= 0) { free(data); return -2; }
+        if (oh <= 0 || ow <= 0) OG_EXEC_FAIL(-2);
         out = (float*)malloc(sizeof(float) * (size_t)(sh[0] * sh[1] * oh * ow > 0 ? sh[0] * sh[1] * oh * ow : 1));
         og_maxpool2d(data, sh[0], (int32_t)sh[1], (int32_t)sh[2], (int32_t)sh[3], op->kernel, op->stride, out, nthreads);
         sh[2] = oh; sh[3] = ow; len = sh[0] * sh[1] * oh * ow;
@@ -616,16 +655,62 @@ int32_t og_execute(const og_program* p, const float* x, const int64_t* shape, in
         og_softmax(data, last ? len / last : 0, last, out);
         break;
       }
-      default: free(data); return -3;
+      case OG_LAYER_RESIDUAL_BEGIN: {
+        if (depth >= OG_MAX_RESIDUAL) OG_EXEC_FAIL(-2);
+        saved[depth] = (float*)malloc(sizeof(float) * (size_t)(len > 0 ? len : 1));
+        memcpy(saved[depth], data, sizeof(float) * (size_t)len);
+        for (int32_t d = 0; d < nd; ++d) saved_sh[depth][d] = sh[d];
+        saved_nd[depth] = nd; saved_len[depth] = len;
+        ++depth;
+        break;
+      }
+      case OG_LAYER_SHORTCUT_CONV2D: {  /* the conv of the a-10 semantics, on the saved input */
+        if (depth < 1) OG_EXEC_FAIL(-2);
+        int64_t* ss = saved_sh[depth - 1];
+        if (saved_nd[depth - 1] != 4 || ss[1] != op->in_channels) OG_EXEC_FAIL(-2);
+        int64_t n = ss[0], h = ss[2], w = ss[3];
+        int64_t oh = og_out_size(h, op->kernel, op->stride, op->padding);
+        int64_t ow = og_out_size(w, op->kernel, op->stride, op->padding);
+        if (oh <= 0 || ow <= 0) OG_EXEC_FAIL(-2);
+        macs = n * op->out_channels * (int64_t)op->in_channels * op->kernel * op->kernel * oh * ow;
+        int64_t olen = n * op->out_channels * oh * ow;
+        float* so = (float*)malloc(sizeof(float) * (size_t)(olen > 0 ? olen : 1));
+        og_op_conv2d(op, saved[depth - 1], n, (int32_t)h, (int32_t)w, so, NULL, NULL, NULL, nthreads);
+        free(saved[depth - 1]);
+        saved[depth - 1] = so;
+        ss[1] = op->out_channels; ss[2] = oh; ss[3] = ow; saved_len[depth - 1] = olen;
+        break;
+      }
+      case OG_LAYER_RESIDUAL_END: {
+        if (depth < 1) OG_EXEC_FAIL(-2);
+        if (saved_nd[depth - 1] != nd || saved_len[depth - 1] != len) OG_EXEC_FAIL(-2);
+        for (int32_t d = 0; d < nd; ++d)
+          if (saved_sh[depth - 1][d] != sh[d]) OG_EXEC_FAIL(-2);
+        og_residual_add(data, saved[depth - 1], len, op->act, op->act_param, data);
+        --depth;
+        free(saved[depth]);
+        break;
+      }
+      case OG_LAYER_ADAPTIVE_AVGPOOL2D: {
+        if (nd != 4 || op->kernel <= 0 || op->stride <= 0 || sh[2] <= 0 || sh[3] <= 0) OG_EXEC_FAIL(-2);
+        int64_t olen = sh[0] * sh[1] * op->kernel * op->stride;
+        out = (float*)malloc(sizeof(float) * (size_t)(olen > 0 ? olen : 1));
+        og_adaptive_avgpool2d(data, sh[0], (int32_t)sh[1], (int32_t)sh[2], (int32_t)sh[3], op->kernel, op->stride, out);
+        sh[2] = op->kernel; sh[3] = op->stride; len = olen;
+        break;
+      }
+      default: OG_EXEC_FAIL(-3);
     }
     if (out) { free(data); data = out; }
     if (op_ns) op_ns[oi] = og_now_ns() - t0;
     if (op_macs) op_macs[oi] = macs;
   }
-  if (len > y_cap) { free(data); return -4; }
+  if (depth != 0) OG_EXEC_FAIL(-2);  /* an unclosed residual block */
+  if (len > y_cap) OG_EXEC_FAIL(-4);
   memcpy(y, data, sizeof(float) * (size_t)len);
   for (int32_t i = 0; i < nd; ++i) y_shape[i] = sh[i];
   *y_ndim = nd;
   free(data);
   return 0;
 }
+#undef OG_EXEC_FAIL

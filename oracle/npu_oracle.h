@@ -40,7 +40,10 @@ float og_bias_bound(int64_t fan_in);                        /* nn/init.rs:23-26 
 enum {
   OG_LAYER_LINEAR = 1, OG_LAYER_CONV2D = 2, OG_LAYER_CHANNEL_AFFINE = 3,
   OG_LAYER_MAXPOOL2D = 4, OG_LAYER_FLATTEN = 5, OG_LAYER_ACTIVATION = 6,
-  OG_LAYER_SOFTMAX = 7
+  OG_LAYER_SOFTMAX = 7,
+  /* extensions (see include/rg_npu.h): residual blocks, adaptive average pooling */
+  OG_LAYER_RESIDUAL_BEGIN = 8, OG_LAYER_RESIDUAL_END = 9, OG_LAYER_SHORTCUT_CONV2D = 10,
+  OG_LAYER_ADAPTIVE_AVGPOOL2D = 11
 };
 enum { OG_ACT_NONE = 0, OG_ACT_RELU = 1, OG_ACT_SIGMOID = 2, OG_ACT_TANH = 3,
        OG_ACT_GELU = 4, OG_ACT_LEAKY_RELU = 5 };
@@ -99,6 +102,10 @@ void og_op_conv2d(const og_op* op, const float* x, int64_t n, int32_t h, int32_t
 void og_maxpool2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t k,
                   int32_t stride, float* y, int32_t nthreads);          /* kernels.rs:165-213 */
 void og_activation(const float* x, int64_t n, int32_t act, float param, float* y); /* npu.rs:395-399 */
+/* extensions: adaptive average pooling (tensor/ops.rs:994-1014) and y = act(x + s) */
+void og_adaptive_avgpool2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t oh,
+                           int32_t ow, float* y);
+void og_residual_add(const float* x, const float* s, int64_t n, int32_t act, float param, float* y);
 void og_softmax(const float* x, int64_t outer, int64_t last, float* y); /* tensor/ops.rs:1058-1076 */
 int64_t og_out_size(int64_t input, int64_t k, int64_t stride, int64_t pad); /* kernels.rs:10-15 */
 void og_im2col(const float* x, int32_t c, int32_t h, int32_t w, int32_t k, int32_t stride,

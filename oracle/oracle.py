@@ -23,6 +23,8 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB_PATH = os.path.join(_HERE, "liboracle.so")
 
 LINEAR, CONV2D, CHANNEL_AFFINE, MAXPOOL2D, FLATTEN, ACTIVATION, SOFTMAX = 1, 2, 3, 4, 5, 6, 7
+# extensions (no reference LayerSpec): residual blocks, adaptive average pooling
+RESIDUAL_BEGIN, RESIDUAL_END, SHORTCUT_CONV2D, ADAPTIVE_AVGPOOL2D = 8, 9, 10, 11
 ACT_NONE, ACT_RELU, ACT_SIGMOID, ACT_TANH, ACT_GELU, ACT_LEAKY_RELU = 0, 1, 2, 3, 4, 5
 
 
@@ -112,6 +114,9 @@ def lib():
                                    C.c_int32, f32p, C.c_int32]
         L.og_activation.argtypes = [f32p, C.c_int64, C.c_int32, C.c_float, f32p]
         L.og_softmax.argtypes = [f32p, C.c_int64, C.c_int64, f32p]
+        L.og_adaptive_avgpool2d.argtypes = [f32p, C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                            C.c_int32, f32p]
+        L.og_residual_add.argtypes = [f32p, f32p, C.c_int64, C.c_int32, C.c_float, f32p]
         L.og_out_size.argtypes = [C.c_int64] * 4
         L.og_out_size.restype = C.c_int64
         L.og_im2col.argtypes = [f32p] + [C.c_int32] * 8 + [f32p]
@@ -283,6 +288,7 @@ class Program:
         """Execute one batch shard; every Linear quantizes with
         ``allreduce_max(local_absmax)`` (the max over all shards)."""
         data = _f32(x)
+        saved = []
         for i, op in enumerate(self.ops):
             if op.kind == LINEAR:
                 rows = data.size // op.in_features
@@ -308,8 +314,33 @@ class Program:
                 y = activation(data, op.act, op.act_param)
             elif op.kind == SOFTMAX:
                 y = softmax(data)
+            else:
+                y = self._extension_step(i, op, data, saved, nthreads)
             data = np.ascontiguousarray(y)
         return data
+
+    def _conv_on(self, i, op, data, nthreads):
+        n, c, h, w = data.shape
+        oh = lib().og_out_size(h, op.kernel, op.stride, op.padding)
+        ow = lib().og_out_size(w, op.kernel, op.stride, op.padding)
+        y = np.empty((n, op.out_channels, oh, ow), np.float32)
+        lib().og_op_conv2d(C.byref(self._p.contents.ops[i]), _p(data, C.c_float), n, h, w,
+                           _p(y, C.c_float), None, None, None, nthreads)
+        return y
+
+    def _extension_step(self, i, op, data, saved, nthreads):
+        """Residual blocks and adaptive pooling (extension kinds): returns the new main tensor."""
+        if op.kind == RESIDUAL_BEGIN:
+            saved.append(np.ascontiguousarray(data).copy())
+            return data
+        if op.kind == SHORTCUT_CONV2D:
+            saved[-1] = self._conv_on(i, op, saved[-1], nthreads)
+            return data
+        if op.kind == RESIDUAL_END:
+            return residual_add(data, saved.pop(), op.act, op.act_param)
+        if op.kind == ADAPTIVE_AVGPOOL2D:
+            return adaptive_avgpool2d(data, op.kernel, op.stride)
+        raise ValueError(op.kind)
 
     def run_traced(self, x, nthreads: int = 1):
         """Execute op by op and record every intermediate (for golden vectors):
@@ -317,6 +348,7 @@ class Program:
         i32 accumulators and the f32 output."""
         trace = []
         data = _f32(x)
+        saved = []
         for i, op in enumerate(self.ops):
             rec = {"label": op.label(), "kind": op.kind}
             if op.kind == LINEAR:
@@ -351,8 +383,9 @@ class Program:
             elif op.kind == SOFTMAX:
                 y = softmax(data)
             else:
-                raise ValueError(op.kind)
-            rec["y"] = y
+                y = self._extension_step(i, op, data, saved, nthreads)
+            # a shortcut conv's output is the new saved block input; the main path goes on
+            rec["y"] = saved[-1] if op.kind == SHORTCUT_CONV2D else y
             trace.append(rec)
             data = np.ascontiguousarray(y)
         return data, trace
@@ -375,6 +408,8 @@ def _out_capacity(prog: Program, in_shape) -> int:
                      int(lib().og_out_size(w, op.kernel, op.stride, 0))]
         elif op.kind == FLATTEN:
             shape = [shape[0], int(np.prod(shape[1:]))]
+        elif op.kind == ADAPTIVE_AVGPOOL2D:
+            shape = [shape[0], shape[1], op.kernel, op.stride]
         best = max(best, int(np.prod(shape)))
     return max(best, 1)
 
@@ -416,6 +451,22 @@ def softmax(x):
     last = x.shape[-1]
     y = np.empty_like(x)
     lib().og_softmax(_p(x, C.c_float), x.size // last if last else 0, last, _p(y, C.c_float))
+    return y
+
+
+def adaptive_avgpool2d(x, oh: int, ow: int):
+    x = _f32(x)
+    n, c, h, w = x.shape
+    y = np.empty((n, c, oh, ow), np.float32)
+    lib().og_adaptive_avgpool2d(_p(x, C.c_float), n, c, h, w, oh, ow, _p(y, C.c_float))
+    return y
+
+
+def residual_add(x, s, act: int, param: float = 0.0):
+    x, s = _f32(x), _f32(s)
+    assert x.shape == s.shape
+    y = np.empty_like(x)
+    lib().og_residual_add(_p(x, C.c_float), _p(s, C.c_float), x.size, act, C.c_float(param), _p(y, C.c_float))
     return y
 
 

@@ -49,5 +49,30 @@ def c3_linear(m: int, k: int, n: int, seed: int = 42, rows: int | None = None, r
     return model, x
 
 
+def resnet(batch: int, image: int, widths, classes: int, seed: int = 42, stem_k: int = 7, row_offset: int = 0):
+    """ResNet-18 layout (extension kinds): conv stem k x k / 2 + BN + ReLU, MaxPool 3x3/2
+    (pad 0, the reference's max_pool2d), 4 stages of 2 basic blocks (first block of
+    stages 2+ stride 2 with a projection), AdaptiveAvgPool2d(1), Flatten, Linear.
+    x ~ N(0,1) [batch, 3, image, image] (images [row_offset, row_offset + batch))."""
+    rng.manual_seed(seed)
+    layers = [nn.Conv2d(3, widths[0], stem_k).stride(2).padding(stem_k // 2), nn.BatchNorm2d(widths[0]), nn.Relu(),
+              nn.MaxPool2d(3, 2)]
+    cin = widths[0]
+    for si, w in enumerate(widths):
+        for bi in range(2):
+            layers.append(nn.BasicBlock(cin, w, 2 if (si > 0 and bi == 0) else 1))
+            cin = w
+    layers += [nn.AdaptiveAvgPool2d(1), nn.Flatten(), nn.Linear(cin, classes)]
+    model = nn.Sequential(*layers)
+    nn.draw_bn_stats(model)
+    rng.advance(2 * 3 * image * image * row_offset)
+    return model, rng.randn((batch, 3, image, image))
+
+
+def c4_resnet18(batch: int = 128, seed: int = 42, row_offset: int = 0, image: int = 224):
+    """ResNet-18-shaped INT8 CNN, x [B,3,224,224] ~ N(0,1), 1000 classes."""
+    return resnet(batch, image, (64, 128, 256, 512), 1000, seed, 7, row_offset)
+
+
 def input_only(config: str, batch: int, seed: int = 42) -> np.ndarray:
     return {"c1": c1_mlp, "c2": c2_cnn}[config](batch, seed)[1]

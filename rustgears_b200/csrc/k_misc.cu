@@ -1,4 +1,5 @@
-// k_misc.cu -- memory-bound NpuOps: MaxPool2d, standalone Activation, Softmax.
+// k_misc.cu -- memory-bound NpuOps: MaxPool2d, standalone Activation, Softmax, and the
+// extension ops residual add (+ activation) and adaptive average pooling.
 //
 // Each kernel can also emit the absmax of its output (per tensor or per image)
 // for the next quantizing op, so no separate absmax pass re-reads the tensor.
@@ -102,6 +103,53 @@ __global__ void __launch_bounds__(kThreads) k_softmax(const float* __restrict__ 
   if (amax) block_max_to(m, amax);
 }
 
+// Extension: y = act(x + s) (binary Add, tensor/ops.rs:67-76, then the block's activation).
+__global__ void __launch_bounds__(kThreads) k_residual_add(const float* __restrict__ x, const float* __restrict__ sv,
+                                                           int64_t n, int32_t act, float p, float* __restrict__ y,
+                                                           unsigned* amax, int64_t per_slot) {
+  const int64_t slot = blockIdx.y;
+  const int64_t e0 = slot * per_slot;
+  const int64_t e1 = min(n, e0 + per_slot);
+  float m = 0.0f;
+  for (int64_t i = e0 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < e1;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = act_apply(act, p, __fadd_rn(__ldg(x + i), __ldg(sv + i)));
+    y[i] = v;
+    m = fmaxf(m, fabsf(v));
+  }
+  if (amax) block_max_to(m, amax + slot);
+}
+
+// Extension: adaptive_avg_pool2d (tensor/ops.rs:994-1014): rows [y*h/oh, ceil((y+1)h/oh)),
+// columns likewise; serial f32 sum in row-major order from 0, one division by the count.
+__global__ void __launch_bounds__(kThreads) k_adaptive_avgpool(const float* __restrict__ x, int64_t planes,
+                                                               int32_t h, int32_t w, int32_t oh, int32_t ow,
+                                                               float* __restrict__ y, unsigned* amax,
+                                                               int64_t planes_per_slot) {
+  const int64_t slot = blockIdx.y;
+  const int64_t p0 = slot * planes_per_slot;
+  const int64_t p1 = min(planes, p0 + planes_per_slot);
+  const int64_t per = (p1 - p0) * oh * ow;
+  float m = 0.0f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < per;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t o = p0 * oh * ow + i;
+    const int64_t plane = o / ((int64_t)oh * ow);
+    const int32_t rem = (int32_t)(o - plane * oh * ow);
+    const int32_t oy = rem / ow, ox = rem - oy * ow;
+    const int32_t y0 = oy * h / oh, y1 = ((oy + 1) * h + oh - 1) / oh;
+    const int32_t x0 = ox * w / ow, x1 = ((ox + 1) * w + ow - 1) / ow;
+    const float* xp = x + plane * (int64_t)h * w;
+    float sum = 0.0f;
+    for (int32_t yy = y0; yy < y1; ++yy)
+      for (int32_t xx = x0; xx < x1; ++xx) sum = __fadd_rn(sum, __ldg(xp + (int64_t)yy * w + xx));
+    const float v = __fdiv_rn(sum, (float)((y1 - y0) * (x1 - x0)));
+    y[o] = v;
+    m = fmaxf(m, fabsf(v));
+  }
+  if (amax) block_max_to(m, amax + slot);
+}
+
 __global__ void k_fill_u32(unsigned* p, unsigned v, int64_t n) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
@@ -145,6 +193,28 @@ void launch_activation(const float* x, int64_t n, int32_t act, float p, float* y
   const int64_t slots = (n + per_slot - 1) / per_slot;
   dim3 grid(grid_for(per_slot, kThreads * 4, slots > 1 ? 64 : 148 * 16), (unsigned)slots);
   k_activation<<<grid, kThreads, 0, st>>>(x, n, act, p, y, amax.ptr, per_slot);
+}
+
+void launch_residual_add(const float* x, const float* sv, int64_t n, int32_t act, float p, float* y,
+                         AmaxSink amax, cudaStream_t st) {
+  if (n <= 0) return;
+  int64_t per_slot = (amax.ptr && amax.elems_per_slot > 0) ? amax.elems_per_slot : n;
+  const int64_t slots = (n + per_slot - 1) / per_slot;
+  dim3 grid(grid_for(per_slot, kThreads * 4, slots > 1 ? 64 : 148 * 16), (unsigned)slots);
+  k_residual_add<<<grid, kThreads, 0, st>>>(x, sv, n, act, p, y, amax.ptr, per_slot);
+}
+
+void launch_adaptive_avgpool(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t oh, int32_t ow,
+                             float* y, AmaxSink amax, cudaStream_t st) {
+  const int64_t planes = n * c;
+  if (planes <= 0 || oh <= 0 || ow <= 0) return;
+  int64_t planes_per_slot = planes;
+  if (amax.ptr && amax.elems_per_slot > 0) planes_per_slot = amax.elems_per_slot / ((int64_t)oh * ow);
+  if (planes_per_slot <= 0) planes_per_slot = planes;
+  const int64_t slots = (planes + planes_per_slot - 1) / planes_per_slot;
+  const int64_t per = planes_per_slot * oh * ow;
+  dim3 grid(grid_for(per, kThreads, slots > 1 ? 64 : 148 * 16), (unsigned)slots);
+  k_adaptive_avgpool<<<grid, kThreads, 0, st>>>(x, planes, h, w, oh, ow, y, amax.ptr, planes_per_slot);
 }
 
 void launch_softmax(const float* x, int64_t outer, int64_t last, float* y, AmaxSink amax,

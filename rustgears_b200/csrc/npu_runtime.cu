@@ -178,7 +178,7 @@ struct Session {
   std::vector<int> ev_of;  // ev_of[i]: event marking the start of op i (ops that launch nothing share one)
   std::mutex mu;
   // workspace
-  DevBuf act0, act1, qbuf, amax, scales, accbuf, xin, yout, covbuf;
+  DevBuf act0, act1, act2, act3, qbuf, amax, scales, accbuf, xin, yout, covbuf;
   // profile + trace
   Profile last;
   bool trace = false;
@@ -226,6 +226,16 @@ static std::string make_label(const Op& op) {  // NpuOp::label (npu.rs:83-104)
     case RG_LAYER_FLATTEN: snprintf(buf, sizeof buf, "NPU::Flatten"); break;
     case RG_LAYER_ACTIVATION: snprintf(buf, sizeof buf, "NPU::Act(%s)", a); break;
     case RG_LAYER_SOFTMAX: snprintf(buf, sizeof buf, "NPU::Softmax"); break;
+    // extension ops
+    case RG_LAYER_RESIDUAL_BEGIN: snprintf(buf, sizeof buf, "NPU::ResidualBegin"); break;
+    case RG_LAYER_RESIDUAL_END:
+      if (op.act == RG_ACT_NONE) snprintf(buf, sizeof buf, "NPU::ResidualAdd");
+      else snprintf(buf, sizeof buf, "NPU::ResidualAdd(%s)", a);
+      break;
+    case RG_LAYER_SHORTCUT_CONV2D:
+      snprintf(buf, sizeof buf, "NPU::ShortcutConv2d(%d->%d, k=%d)", op.in_c, op.out_c, op.k);
+      break;
+    case RG_LAYER_ADAPTIVE_AVGPOOL2D: snprintf(buf, sizeof buf, "NPU::AdaptiveAvgPool2d(%dx%d)", op.k, op.stride); break;
     default: snprintf(buf, sizeof buf, "NPU::?"); break;
   }
   return buf;
@@ -251,6 +261,7 @@ static rg_status validate_layer(const rg_layer_spec& l, int idx) {
                     l.in_features, l.out_features);
       return RG_OK;
     case RG_LAYER_CONV2D:
+    case RG_LAYER_SHORTCUT_CONV2D:
       if (l.in_channels <= 0 || l.out_channels <= 0 || l.kernel <= 0 || l.stride <= 0 || l.padding < 0 ||
           l.weight_len != (int64_t)l.out_channels * l.in_channels * l.kernel * l.kernel ||
           l.bias_len != l.out_channels || !l.weight || !l.bias)
@@ -267,7 +278,13 @@ static rg_status validate_layer(const rg_layer_spec& l, int idx) {
       return RG_OK;
     case RG_LAYER_FLATTEN:
     case RG_LAYER_SOFTMAX:
+    case RG_LAYER_RESIDUAL_BEGIN:
       return RG_OK;
+    case RG_LAYER_ADAPTIVE_AVGPOOL2D:
+      if (l.kernel <= 0 || l.stride <= 0)
+        return fail(RG_ERR_INVALID_ARG, "layer %d: adaptive pool output size must be positive", idx);
+      return RG_OK;
+    case RG_LAYER_RESIDUAL_END:
     case RG_LAYER_ACTIVATION:
       if (l.act < RG_ACT_NONE || l.act > RG_ACT_LEAKY_RELU)
         return fail(RG_ERR_INVALID_ARG, "layer %d: unknown activation tag %d", idx, l.act);
@@ -291,7 +308,7 @@ static std::vector<HostLayer> fold(const rg_layer_spec* L, int32_t n) {
         for (int64_t j = 0; j < p.out_f; ++j) { const float t = p.b[j] * l.weight[j]; p.b[j] = t + l.bias[j]; }
         continue;
       }
-      if (p.kind == RG_LAYER_CONV2D && p.out_c == c) {
+      if ((p.kind == RG_LAYER_CONV2D || p.kind == RG_LAYER_SHORTCUT_CONV2D) && p.out_c == c) {
         const int64_t plane = (int64_t)p.in_c * p.k * p.k;
         for (int64_t o = 0; o < p.out_c; ++o) {
           for (int64_t j = 0; j < plane; ++j) p.w[o * plane + j] = p.w[o * plane + j] * l.weight[o];
@@ -354,13 +371,25 @@ static void quantize_weights(Op& op, const float* w_ref_layout, int64_t rows, in
 // npu::compile (npu.rs:188-276).
 static rg_status compile(Session& s, const rg_layer_spec* layers, int32_t n) {
   for (int32_t i = 0; i < n; ++i) RG_TRY(validate_layer(layers[i], i));
+  int depth = 0;  // residual blocks must nest and close
+  for (int32_t i = 0; i < n; ++i) {
+    const int32_t k = layers[i].kind;
+    if (k == RG_LAYER_RESIDUAL_BEGIN) ++depth;
+    if ((k == RG_LAYER_RESIDUAL_END || k == RG_LAYER_SHORTCUT_CONV2D) && depth == 0)
+      return fail(RG_ERR_INVALID_ARG, "layer %d: %s outside a residual block", i,
+                  k == RG_LAYER_RESIDUAL_END ? "ResidualEnd" : "ShortcutConv2d");
+    if (k == RG_LAYER_RESIDUAL_END) --depth;
+  }
+  if (depth != 0) return fail(RG_ERR_INVALID_ARG, "%d residual block(s) not closed", depth);
   std::vector<HostLayer> f = fold(layers, n);
   s.original_layers = n;
   for (size_t i = 0; i < f.size(); ++i) {
     HostLayer& l = f[i];
-    const bool next_act = i + 1 < f.size() && f[i + 1].kind == RG_LAYER_ACTIVATION;
+    // an Activation after a shortcut conv belongs to the main path: not fused into it
+    const bool next_act =
+        i + 1 < f.size() && f[i + 1].kind == RG_LAYER_ACTIVATION && l.kind != RG_LAYER_SHORTCUT_CONV2D;
     Op op;
-    if (l.kind == RG_LAYER_LINEAR || l.kind == RG_LAYER_CONV2D) {
+    if (l.kind == RG_LAYER_LINEAR || l.kind == RG_LAYER_CONV2D || l.kind == RG_LAYER_SHORTCUT_CONV2D) {
       op.kind = l.kind;
       op.act = next_act ? f[i + 1].act : RG_ACT_NONE;
       op.param = next_act ? f[i + 1].param : 0.0f;
@@ -398,7 +427,8 @@ static rg_status compile(Session& s, const rg_layer_spec* layers, int32_t n) {
     op.label = make_label(op);
     for (float b : op.bias)
       if (!std::isfinite(b)) op.bias_finite = false;
-    if (op.kind == RG_LAYER_LINEAR || op.kind == RG_LAYER_CONV2D) RG_TRY(upload_op(op));
+    if (op.kind == RG_LAYER_LINEAR || op.kind == RG_LAYER_CONV2D || op.kind == RG_LAYER_SHORTCUT_CONV2D)
+      RG_TRY(upload_op(op));
     s.ops.push_back(std::move(op));
   }
   return RG_OK;
@@ -424,11 +454,29 @@ static rg_status plan_shapes(const Session& s, const int64_t* shape, int32_t ndi
     return n;
   };
   out.clear();
+  std::vector<std::vector<int64_t>> saved;  // residual block inputs
   for (size_t i = 0; i < s.ops.size(); ++i) {
     const Op& op = s.ops[i];
     OpShape os;
     os.in = sh;
     os.in_elems = numel(sh);
+    if (op.kind == RG_LAYER_SHORTCUT_CONV2D) {  // works on the saved block input, not the main path
+      std::vector<int64_t>& ss = saved.back();
+      if (ss.size() != 4 || ss[1] != op.in_c)
+        return fail(RG_ERR_SHAPE, "op %zu (%s): expected a saved [N,%d,H,W] block input", i, op.label.c_str(),
+                    op.in_c);
+      const int64_t oh = out_size(ss[2], op.k, op.stride, op.pad), ow = out_size(ss[3], op.k, op.stride, op.pad);
+      if (oh <= 0 || ow <= 0)
+        return fail(RG_ERR_SHAPE, "op %zu (%s): kernel %d larger than padded input", i, op.label.c_str(), op.k);
+      os.in = ss;
+      os.in_elems = numel(ss);
+      os.macs = (uint64_t)ss[0] * op.out_c * op.in_c * op.k * op.k * oh * ow;
+      ss = {ss[0], op.out_c, oh, ow};
+      os.out = ss;
+      os.out_elems = numel(ss);
+      out.push_back(std::move(os));
+      continue;
+    }
     switch (op.kind) {
       case RG_LAYER_LINEAR: {
         if (sh.back() != op.in_f)
@@ -463,6 +511,20 @@ static rg_status plan_shapes(const Session& s, const int64_t* shape, int32_t ndi
         sh = {sh[0], rest};
         break;
       }
+      case RG_LAYER_RESIDUAL_BEGIN:
+        saved.push_back(sh);
+        break;
+      case RG_LAYER_RESIDUAL_END:
+        if (saved.back() != sh)
+          return fail(RG_ERR_SHAPE, "op %zu (%s): main path and shortcut shapes differ (%lld vs %lld elements)", i,
+                      op.label.c_str(), (long long)numel(sh), (long long)numel(saved.back()));
+        saved.pop_back();
+        break;
+      case RG_LAYER_ADAPTIVE_AVGPOOL2D:
+        if (sh.size() != 4 || sh[2] <= 0 || sh[3] <= 0)
+          return fail(RG_ERR_SHAPE, "op %zu (%s): expected a non-empty [N,C,H,W] input", i, op.label.c_str());
+        sh = {sh[0], sh[1], op.k, op.stride};
+        break;
       default:
         break;
     }
@@ -503,6 +565,12 @@ struct RunPlan {
   std::vector<uint8_t> block_start;  // op i starts a fused Conv-Pool-Conv-Pool block
 };
 
+// Ops that leave the main-path tensor as it is (reshape, saving a block input, a
+// shortcut conv on the saved input).
+static bool main_path_noop(int32_t kind) {
+  return kind == RG_LAYER_FLATTEN || kind == RG_LAYER_RESIDUAL_BEGIN || kind == RG_LAYER_SHORTCUT_CONV2D;
+}
+
 // Activations f with max(f(a), f(b)) == f(max(a, b)) under round-to-nearest.
 static bool non_decreasing(int32_t act, float p) {
   return act == RG_ACT_NONE || act == RG_ACT_RELU || (act == RG_ACT_LEAKY_RELU && p >= 0.0f);
@@ -538,26 +606,30 @@ static rg_status make_plan(const Session& s, const int64_t* shape, int32_t ndim,
   int64_t off = 0;
   for (size_t i = 0; i < n; ++i) {
     const Op& op = s.ops[i];
-    if (op.kind != RG_LAYER_LINEAR && op.kind != RG_LAYER_CONV2D) continue;
+    const bool conv_like = op.kind == RG_LAYER_CONV2D || op.kind == RG_LAYER_SHORTCUT_CONV2D;
+    if (op.kind != RG_LAYER_LINEAR && !conv_like) continue;
     const OpShape& os = P.shapes[i];
     P.amax_slots[i] = op.kind == RG_LAYER_LINEAR ? 1 : os.in[0];
     P.amax_off[i] = off;
     off += std::max<int64_t>(P.amax_slots[i], 1);
     bool full = true;
-    if (op.kind == RG_LAYER_CONV2D) {
+    if (conv_like) {
       P.rowcov[i] = coverage(os.in[2], op.k, op.stride, op.pad, os.out[2]);
       P.colcov[i] = coverage(os.in[3], op.k, op.stride, op.pad, os.out[3]);
       full = all_covered(P.rowcov[i]) && all_covered(P.colcov[i]);
       if (!full) P.cov_bytes += P.rowcov[i].size() + P.colcov[i].size();
     }
-    // the producing op (Flatten only reshapes)
+    // a shortcut conv reads the saved block input: its own absmax pass
+    if (op.kind == RG_LAYER_SHORTCUT_CONV2D) continue;
+    // the producing op (Flatten only reshapes; a residual begin / shortcut leaves the main path)
     int j = (int)i - 1;
-    while (j >= 0 && s.ops[(size_t)j].kind == RG_LAYER_FLATTEN) --j;
+    while (j >= 0 && main_path_noop(s.ops[(size_t)j].kind)) --j;
     if (j < 0 || !full || (s.flags & RG_SESSION_NO_FUSION)) continue;
     const int pk = s.ops[(size_t)j].kind;
     if (pk == RG_LAYER_SOFTMAX && op.kind == RG_LAYER_CONV2D) continue;
     if (pk == RG_LAYER_LINEAR || pk == RG_LAYER_CONV2D || pk == RG_LAYER_MAXPOOL2D ||
-        pk == RG_LAYER_ACTIVATION || pk == RG_LAYER_SOFTMAX)
+        pk == RG_LAYER_ACTIVATION || pk == RG_LAYER_SOFTMAX || pk == RG_LAYER_RESIDUAL_END ||
+        pk == RG_LAYER_ADAPTIVE_AVGPOOL2D)
       P.amax_src[i] = j;
   }
   P.total_slots = off;
@@ -571,8 +643,9 @@ static rg_status make_plan(const Session& s, const int64_t* shape, int32_t ndim,
 }
 
 static int find_consumer(const Session& s, size_t j) {
+  if (s.ops[j].kind == RG_LAYER_SHORTCUT_CONV2D) return -1;  // its output feeds the residual add
   for (size_t i = j + 1; i < s.ops.size(); ++i) {
-    if (s.ops[i].kind == RG_LAYER_FLATTEN) continue;
+    if (main_path_noop(s.ops[i].kind)) continue;
     if (s.ops[i].kind == RG_LAYER_LINEAR || s.ops[i].kind == RG_LAYER_CONV2D) return (int)i;
     return -1;
   }
@@ -615,8 +688,26 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
     if (op.kind == RG_LAYER_LINEAR) max_q = std::max(max_q, P.shapes[i].in_elems / op.in_f * op.kpad);
     if (op.kind == RG_LAYER_CONV2D) max_q = std::max(max_q, P.shapes[i].in_elems);
   }
+  bool residual = false;
+  for (size_t i = 0; i < n; ++i) residual = residual || s.ops[i].kind == RG_LAYER_RESIDUAL_BEGIN;
   RG_TRY(s.act0.ensure((size_t)max_elems * 4));
   RG_TRY(s.act1.ensure((size_t)max_elems * 4));
+  if (residual) {  // saved block inputs (and shortcut outputs) stay live across main-path ops
+    RG_TRY(s.act2.ensure((size_t)max_elems * 4));
+    RG_TRY(s.act3.ensure((size_t)max_elems * 4));
+  }
+  float* pool[4] = {s.act0.as<float>(), s.act1.as<float>(), residual ? s.act2.as<float>() : nullptr,
+                    residual ? s.act3.as<float>() : nullptr};
+  std::vector<const float*> saved;  // residual block inputs, innermost last
+  auto pick_dst = [&](const float* avoid) -> float* {
+    for (float* b : pool) {
+      if (!b || b == avoid) continue;
+      bool busy = false;
+      for (const float* v : saved) busy = busy || v == b;
+      if (!busy) return b;
+    }
+    return nullptr;
+  };
   RG_TRY(s.qbuf.ensure((size_t)round_up(max_q, 16) + 64));
   RG_TRY(s.amax.ensure((size_t)std::max<int64_t>(P.total_slots, 1) * 4));
   RG_TRY(s.scales.ensure((size_t)std::max<int64_t>(P.total_slots, 1) * 4));
@@ -661,7 +752,14 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
     const Op& op = s.ops[i];
     const OpShape& os = P.shapes[i];
     const bool last = i + 1 == n;
-    float* dst = (cur == s.act0.as<float>()) ? s.act1.as<float>() : s.act0.as<float>();
+    if (op.kind == RG_LAYER_RESIDUAL_BEGIN) {  // the block input stays where it is
+      saved.push_back(cur);
+      if (s.trace) RG_TRY(d2h_vec(s.traces[i].out, cur, os.out_elems, st));
+      s.ev_of[i + 1] = s.ev_of[i];
+      continue;
+    }
+    float* dst = pick_dst(op.kind == RG_LAYER_SHORTCUT_CONV2D ? saved.back() : cur);
+    if (!dst) return fail(RG_ERR_UNSUPPORTED, "op %zu: residual blocks nested too deeply", i);
     if (last && y_dev) dst = y_dev;
     // absmax sink for the consumer of this op's output
     AmaxSink sink;
@@ -728,13 +826,21 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
     }
     if (os.in_elems == 0 || os.out_elems == 0) {  // empty batch: nothing to launch
       if (s.trace) s.traces[i] = TraceRec();
-      if (op.kind != RG_LAYER_FLATTEN) cur = dst;
+      if (op.kind == RG_LAYER_RESIDUAL_END) saved.pop_back();
+      if (op.kind == RG_LAYER_SHORTCUT_CONV2D) {
+        saved.back() = dst;
+      } else if (op.kind != RG_LAYER_FLATTEN) {
+        cur = dst;
+      }
       s.ev_of[i + 1] = s.ev_of[i];
       continue;
     }
     switch (op.kind) {
       case RG_LAYER_LINEAR:
-      case RG_LAYER_CONV2D: {
+      case RG_LAYER_CONV2D:
+      case RG_LAYER_SHORTCUT_CONV2D: {
+        const bool shortcut = op.kind == RG_LAYER_SHORTCUT_CONV2D;
+        const float* src = shortcut ? saved.back() : cur;
         unsigned* my_amax = amax + P.amax_off[i];
         float* my_scale = scales + P.amax_off[i];
         int8_t* q = s.qbuf.as<int8_t>();
@@ -766,8 +872,8 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         } else {
           const int64_t N = os.in[0];
           const int32_t C = op.in_c, H = (int32_t)os.in[2], W = (int32_t)os.in[3];
-          if (P.amax_src[i] < 0) { launch_image_absmax(cur, N, C, H, W, rc[i], cc[i], my_amax, st); ++launches; RG_LAUNCHED("image_absmax"); }
-          launch_image_quantize_nhwc(cur, N, C, H, W, C, my_amax, q, my_scale, st);
+          if (P.amax_src[i] < 0) { launch_image_absmax(src, N, C, H, W, rc[i], cc[i], my_amax, st); ++launches; RG_LAUNCHED("image_absmax"); }
+          launch_image_quantize_nhwc(src, N, C, H, W, C, my_amax, q, my_scale, st);
           ++launches;
           RG_LAUNCHED("image_quantize_nhwc");
           g.a = q; g.conv = true;
@@ -820,9 +926,26 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
                 for (int64_t p = 0; p < HW; ++p) t.aq[(size_t)((b * C + c) * HW + p)] = tmp[(size_t)((b * HW + p) * C + c)];
           }
         }
-        cur = dst;
+        if (shortcut) {
+          saved.back() = dst;  // the shortcut replaces the saved block input
+          if (s.trace) RG_TRY(d2h_vec(s.traces[i].out, dst, os.out_elems, st));
+        } else {
+          cur = dst;
+        }
         break;
       }
+      case RG_LAYER_RESIDUAL_END:
+        launch_residual_add(cur, saved.back(), os.in_elems, op.act, op.param, dst, sink, st);
+        ++launches;
+        saved.pop_back();
+        cur = dst;
+        break;
+      case RG_LAYER_ADAPTIVE_AVGPOOL2D:
+        launch_adaptive_avgpool(cur, os.in[0], (int32_t)os.in[1], (int32_t)os.in[2], (int32_t)os.in[3], op.k,
+                                op.stride, dst, sink, st);
+        ++launches;
+        cur = dst;
+        break;
       case RG_LAYER_MAXPOOL2D:
         launch_maxpool2d(cur, os.in[0], (int32_t)os.in[1], (int32_t)os.in[2], (int32_t)os.in[3], op.k,
                          op.stride, dst, sink, st);
@@ -851,7 +974,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         return fail(RG_ERR_UNSUPPORTED, "op %zu: unsupported kind %d", i, op.kind);
     }
     RG_CUDA_TRY(cudaGetLastError());
-    if (s.trace) RG_TRY(d2h_vec(s.traces[i].out, cur, os.out_elems, st));
+    if (s.trace && op.kind != RG_LAYER_SHORTCUT_CONV2D) RG_TRY(d2h_vec(s.traces[i].out, cur, os.out_elems, st));
     if (op.kind == RG_LAYER_FLATTEN) {
       s.ev_of[i + 1] = s.ev_of[i];  // a reshape: no kernel, no event
     } else {

@@ -113,6 +113,11 @@ void launch_maxpool2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w
 // (zeroed first): counts[0] tanh, [1] GELU, [2] quant_scale, [3] quant_inv,
 // [4] round_half_away.
 void launch_selftest_fast_division(unsigned long long* counts, cudaStream_t st);
+// Extensions: y = act(x + s) elementwise; adaptive average pooling to oh x ow.
+void launch_residual_add(const float* x, const float* s, int64_t n, int32_t act, float p, float* y,
+                         AmaxSink amax, cudaStream_t st);
+void launch_adaptive_avgpool(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t oh, int32_t ow,
+                             float* y, AmaxSink amax, cudaStream_t st);
 void launch_activation(const float* x, int64_t n, int32_t act, float p, float* y, AmaxSink amax,
                        cudaStream_t st);
 void launch_softmax(const float* x, int64_t outer, int64_t last, float* y, AmaxSink amax,

@@ -13,6 +13,7 @@ import numpy as np
 from . import rng
 from .spec import Activation, ActivationLayer, ChannelAffine, Conv2d as Conv2dSpec, Flatten as FlattenSpec
 from .spec import Linear as LinearSpec, MaxPool2d as MaxPool2dSpec, Softmax as SoftmaxSpec
+from .spec import AdaptiveAvgPool2d as AdaptiveAvgPool2dSpec, ResidualBegin, ResidualEnd, ShortcutConv2d
 
 
 class Module:
@@ -198,11 +199,52 @@ class Softmax(Module):
         return [SoftmaxSpec()]
 
 
+class AdaptiveAvgPool2d(Module):
+    """Extension export (the reference has the op, tensor/ops.rs:994-1014, but no LayerSpec)."""
+
+    def __init__(self, out_h: int, out_w: int | None = None):
+        self.out_h, self.out_w = out_h, out_h if out_w is None else out_w
+
+    def export(self):
+        return [AdaptiveAvgPool2dSpec(self.out_h, self.out_w)]
+
+
+class BasicBlock(Module):
+    """ResNet basic block (extension export): y = relu(bn2(conv2(relu(bn1(conv1(x))))) + shortcut(x)),
+    shortcut = identity, or bn(conv1x1/stride(x)) when the stride or width changes.
+    Construction draws conv1, bn1, conv2, bn2, then the projection conv, in that order."""
+
+    def __init__(self, in_ch: int, out_ch: int, stride: int = 1):
+        self.conv1 = Conv2d(in_ch, out_ch, 3).stride(stride).padding(1)
+        self.bn1 = BatchNorm2d(out_ch)
+        self.conv2 = Conv2d(out_ch, out_ch, 3).padding(1)
+        self.bn2 = BatchNorm2d(out_ch)
+        self.proj = None
+        if stride != 1 or in_ch != out_ch:
+            self.proj = Conv2d(in_ch, out_ch, 1).stride(stride)
+            self.proj_bn = BatchNorm2d(out_ch)
+
+    def batchnorms(self):
+        return [self.bn1, self.bn2] + ([self.proj_bn] if self.proj is not None else [])
+
+    def export(self):
+        out = [ResidualBegin()]
+        out += self.conv1.export() + self.bn1.export() + [ActivationLayer(Activation.RELU)]
+        out += self.conv2.export() + self.bn2.export()
+        if self.proj is not None:
+            c = self.proj
+            out += [ShortcutConv2d(c.in_channels, c.out_channels, c.kernel_size, c.stride_, c.padding_, c.weight,
+                                   c.bias)] + self.proj_bn.export()
+        out += [ResidualEnd(Activation.RELU)]
+        return out
+
+
 def draw_bn_stats(model: Module, mean_range=(-0.1, 0.1), var_range=(0.5, 1.5)) -> None:
     """Seeded BatchNorm running statistics (benchmark configurations): for each
     BatchNorm in order, running_mean ~ U(mean_range) then running_var ~ U(var_range)."""
     layers = model.layers if isinstance(model, Sequential) else [model]
     for l in layers:
-        if isinstance(l, BatchNorm):
-            l.running_mean = rng.uniform((l.num_features,), *mean_range)
-            l.running_var = rng.uniform((l.num_features,), *var_range)
+        for bn in (l.batchnorms() if isinstance(l, BasicBlock) else [l]):
+            if isinstance(bn, BatchNorm):
+                bn.running_mean = rng.uniform((bn.num_features,), *mean_range)
+                bn.running_var = rng.uniform((bn.num_features,), *var_range)

@@ -16,7 +16,8 @@ from dataclasses import dataclass, field
 import numpy as np
 
 from . import _native
-from .spec import ACTIVATION, CHANNEL_AFFINE, CONV2D, LINEAR, Activation
+from .spec import (ACTIVATION, ADAPTIVE_AVGPOOL2D, CHANNEL_AFFINE, CONV2D, LINEAR, RESIDUAL_END, SHORTCUT_CONV2D,
+                   Activation)
 
 _MAX_RANK = 8
 
@@ -139,7 +140,7 @@ def _layer_structs(layers):
         if l.kind == LINEAR:
             s.in_features, s.out_features = l.in_features, l.out_features
             w, b = l.weight, l.bias
-        elif l.kind == CONV2D:
+        elif l.kind in (CONV2D, SHORTCUT_CONV2D):
             s.in_channels, s.out_channels, s.kernel = l.in_channels, l.out_channels, l.kernel
             s.stride, s.padding = l.stride, l.padding
             w, b = l.weight, l.bias
@@ -149,7 +150,9 @@ def _layer_structs(layers):
             w = b = None
             if hasattr(l, "kernel"):
                 s.kernel, s.stride = l.kernel, l.stride
-            if l.kind == ACTIVATION:
+            if l.kind == ADAPTIVE_AVGPOOL2D:
+                s.kernel, s.stride = l.out_h, l.out_w
+            if l.kind in (ACTIVATION, RESIDUAL_END):
                 act = l.act if isinstance(l.act, Activation) else Activation(int(l.act))
                 s.act, s.act_param = act.code, act.param
         if w is not None:

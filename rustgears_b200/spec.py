@@ -7,6 +7,8 @@ from dataclasses import dataclass, field
 import numpy as np
 
 LINEAR, CONV2D, CHANNEL_AFFINE, MAXPOOL2D, FLATTEN, ACTIVATION, SOFTMAX = 1, 2, 3, 4, 5, 6, 7
+# extensions (no reference LayerSpec): residual blocks, adaptive average pooling
+RESIDUAL_BEGIN, RESIDUAL_END, SHORTCUT_CONV2D, ADAPTIVE_AVGPOOL2D = 8, 9, 10, 11
 
 
 def _fmt_f32(v: float) -> str:
@@ -123,6 +125,43 @@ class Softmax:
     kind: int = field(default=SOFTMAX, init=False)
 
 
+# --- extensions: ResNet-style residual blocks and adaptive average pooling ---------
+@dataclass
+class ResidualBegin:
+    """Saves the current activation as the input of a residual block."""
+    kind: int = field(default=RESIDUAL_BEGIN, init=False)
+
+
+@dataclass
+class ShortcutConv2d:
+    """A Conv2d (same fields and INT8 semantics) applied to the saved block input."""
+    in_channels: int
+    out_channels: int
+    kernel: int
+    stride: int
+    padding: int
+    weight: np.ndarray  # [O, C, k, k]
+    bias: np.ndarray
+    kind: int = field(default=SHORTCUT_CONV2D, init=False)
+
+    def __post_init__(self):
+        self.weight, self.bias = _f32(self.weight), _f32(self.bias)
+
+
+@dataclass
+class ResidualEnd:
+    """y = act(x + saved): closes the block (f32 add, then the activation)."""
+    act: Activation = field(default_factory=lambda: Activation(0))
+    kind: int = field(default=RESIDUAL_END, init=False)
+
+
+@dataclass
+class AdaptiveAvgPool2d:
+    out_h: int
+    out_w: int
+    kind: int = field(default=ADAPTIVE_AVGPOOL2D, init=False)
+
+
 class LayerSpec:
     """Namespace mirroring the Rust enum: ``LayerSpec.Linear(...)`` etc."""
 
@@ -133,6 +172,11 @@ class LayerSpec:
     Flatten = Flatten
     Activation = ActivationLayer
     Softmax = Softmax
+    # extensions
+    ResidualBegin = ResidualBegin
+    ShortcutConv2d = ShortcutConv2d
+    ResidualEnd = ResidualEnd
+    AdaptiveAvgPool2d = AdaptiveAvgPool2d
 
 
 def as_dict(spec) -> dict:
@@ -149,4 +193,11 @@ def as_dict(spec) -> dict:
         d.update(kernel=spec.kernel, stride=spec.stride)
     elif spec.kind == ACTIVATION:
         d.update(act=spec.act.code, act_param=spec.act.param)
+    elif spec.kind == SHORTCUT_CONV2D:
+        d.update(in_channels=spec.in_channels, out_channels=spec.out_channels, kernel=spec.kernel,
+                 stride=spec.stride, padding=spec.padding, weight=spec.weight, bias=spec.bias)
+    elif spec.kind == RESIDUAL_END:
+        d.update(act=spec.act.code, act_param=spec.act.param)
+    elif spec.kind == ADAPTIVE_AVGPOOL2D:
+        d.update(kernel=spec.out_h, stride=spec.out_w)
     return d

@@ -1,7 +1,7 @@
 """Generates the golden fixtures in this folder from the oracle (the CPU
 restatement of the reference Npu(Int8) path).  Run from the repo root:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [case ...]
 
 Each case's .npz holds the input, every op's activation scale(s), i8
 activations, i32 accumulators and f32 output, the program summary and the
@@ -39,7 +39,8 @@ def trace_case(name):
 
 def main():
     oracle.build()
-    for name in configs.CASES:
+    names = sys.argv[1:] or list(configs.CASES)  # e.g. `make_golden.py resnet_mini`
+    for name in names:
         d = trace_case(name)
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **d)
         print(name, "ops:", int(d["n_ops"]), "out:", d["y"].shape)

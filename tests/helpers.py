@@ -35,6 +35,15 @@ def spec_from_dict(d):
         return S.ActivationLayer(S.Activation(d["act"], d.get("act_param", 0.0)))
     if k == S.SOFTMAX:
         return S.Softmax()
+    if k == S.RESIDUAL_BEGIN:
+        return S.ResidualBegin()
+    if k == S.SHORTCUT_CONV2D:
+        return S.ShortcutConv2d(d["in_channels"], d["out_channels"], d["kernel"], d["stride"], d["padding"],
+                                d["weight"], d["bias"])
+    if k == S.RESIDUAL_END:
+        return S.ResidualEnd(S.Activation(d.get("act", 0), d.get("act_param", 0.0)))
+    if k == S.ADAPTIVE_AVGPOOL2D:
+        return S.AdaptiveAvgPool2d(d["kernel"], d["stride"])
     raise ValueError(k)
 
 

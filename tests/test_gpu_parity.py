@@ -243,3 +243,44 @@ def test_host_input_fed_in_chunks(gpu, oracle_lib):
     sess = session_for(layers)
     assert_same(sess.run(x), ref, "chunked host input")
     assert_same(sess.run(x), ref, "chunked host input, second run")
+
+
+def test_resnet18_full_size_matches_oracle(gpu, oracle_lib):
+    """BASELINE configs[3] layout at 224 x 224 (batch 2): residual blocks, projection
+    shortcuts, stride-2 convs with their covered-pixel absmax, adaptive pooling."""
+    layers, x = configs.resnet18(2)
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=16)
+    assert_same(session_for(layers).run(x), ref, "resnet18")
+
+
+@pytest.mark.parametrize("special", ["plain", "zero_nan_inf"])
+def test_resnet_mini_special_images(gpu, oracle_lib, special):
+    layers, x = configs.resnet_mini(batch=5)
+    x = x.copy()
+    if special == "zero_nan_inf":
+        x[0] = 0.0
+        x[1, 2, 3, 4] = np.nan
+        x[3, 0, 0, 0] = np.inf
+        x[4] *= np.float32(1e20)
+    ref, _, _ = oracle.Program(layers).execute(x)
+    assert_same(session_for(layers).run(x), ref, special)
+    assert session_for(layers).run(x[:0]).shape == (0, 10)
+
+
+def test_residual_ir_errors(gpu):
+    from rustgears_b200 import spec as S
+    conv = lambda c: S.Conv2d(c, c, 3, 1, 1, np.zeros((c, c, 3, 3), np.float32), np.zeros(c, np.float32))
+    bad = [
+        [S.ResidualBegin(), conv(4)],                                   # not closed
+        [conv(4), S.ResidualEnd()],                                     # end without begin
+        [S.ShortcutConv2d(4, 4, 1, 1, 0, np.zeros((4, 4, 1, 1), np.float32), np.zeros(4, np.float32))],
+    ]
+    for layers in bad:
+        with pytest.raises(_native.RgError):
+            InferenceSession.from_layers(layers, ExecutionProvider.npu_int8())
+    # main path and shortcut disagree in shape: a shape error at run time
+    sess = InferenceSession.from_layers(
+        [S.ResidualBegin(), S.Conv2d(4, 8, 3, 1, 1, np.zeros((8, 4, 3, 3), np.float32), np.zeros(8, np.float32)),
+         S.ResidualEnd()], ExecutionProvider.npu_int8())
+    with pytest.raises(_native.RgError):
+        sess.run(np.zeros((1, 4, 5, 5), np.float32))
