@@ -42,6 +42,8 @@ WORKLOADS = {
     "c3a": dict(name="fused INT8 Linear+GELU 4096x4096x4096", shape=(4096, 4096, 4096)),
     "c3b": dict(name="fused INT8 Linear+GELU 16384x8192x8192", shape=(16384, 8192, 8192)),
     "c3c": dict(name="fused INT8 Linear+GELU 65536x4096x14336", shape=(65536, 4096, 14336)),
+    "c4": dict(name="ResNet-18-shaped INT8 CNN (residual-block IR extension): x [B,3,224,224] ~ N(0,1), "
+                    "conv7x7/2 + maxpool3x3/2 (pad 0) + 8 basic blocks + avgpool + Linear(512,1000)", batch=128),
 }
 
 
@@ -49,9 +51,9 @@ def build_workload(cfg: str, rank: int, world: int, batch: int | None):
     """(model, x shard, per-GPU units, units name) built with the reference generator."""
     from rustgears_b200 import configs
     w = WORKLOADS[cfg]
-    if cfg in ("c1", "c2"):
+    if cfg in ("c1", "c2", "c4"):
         b = batch or w["batch"]
-        fn = configs.c2_cnn if cfg == "c2" else configs.c1_mlp
+        fn = {"c1": configs.c1_mlp, "c2": configs.c2_cnn, "c4": configs.c4_resnet18}[cfg]
         model, x = fn(b, row_offset=rank * b)
         return model, x, b
     m, k, n = w["shape"]
@@ -132,7 +134,7 @@ def measured_peaks() -> dict:
         return {}
 
 
-def op_roofline(cfg, sess, per_op_ns, steps, units, peaks, traffic=None):
+def op_roofline(cfg, sess, per_op_ns, steps, x_shape, peaks, traffic=None):
     """Roofline of the dominant kernel.  A kernel covers one op, or several when the
     library fused them (the fused-away ops report no time).  Algorithmic work: 2 x
     the INT8 MACs; algorithmic bytes: the kernel's f32 input read + f32 output
@@ -150,7 +152,7 @@ def op_roofline(cfg, sess, per_op_ns, steps, units, peaks, traffic=None):
     gi = int(np.argmax([per_op_ns[a:b].sum() for a, b in groups]))
     a, b = groups[gi]
     dur_s = per_op_ns[a:b].sum() / steps / 1e9
-    shapes = _op_shapes(sess, units)
+    shapes = _op_shapes(sess, x_shape)
     in_bytes = 4 * int(np.prod(shapes[a][0]))
     out_bytes = 4 * int(np.prod(shapes[b - 1][1]))
     wbytes = sum(sess.op_info(k)["wq_len"] + 4 * sess.op_info(k)["bias_len"] for k in range(a, b))
@@ -171,30 +173,34 @@ def op_roofline(cfg, sess, per_op_ns, steps, units, peaks, traffic=None):
                 peak_source="measured hbm_gbs (MEASURED_PEAKS.json)")
 
 
-def _op_shapes(sess, batch):
-    shapes = []
-    shape = None
+def _op_shapes(sess, x_shape):
+    """(input, output) shape of every op for the input shape x_shape; a shortcut conv
+    reads and replaces the saved residual-block input."""
+    shapes, saved = [], []
+    shape = tuple(x_shape)
     for i in range(sess.num_ops()):
         info = sess.op_info(i)
-        if shape is None:
-            shape = _input_shape_of(sess, batch)
+        if info["kind"] == 8:
+            saved.append(shape)
+        if info["kind"] == 10:
+            out = _out_shape(dict(info, kind=2), saved[-1])
+            shapes.append((saved[-1], out))
+            saved[-1] = out
+            continue
+        if info["kind"] == 9:
+            saved.pop()
         out = _out_shape(info, shape)
         shapes.append((shape, out))
         shape = out
     return shapes
 
 
-def _input_shape_of(sess, batch):
-    first = sess.raw_layers()[0]
-    if first.kind == 2:
-        return (batch, first.in_channels, 28, 28)
-    return (batch, first.in_features if first.kind == 1 else 1)
-
-
 def _out_shape(info, shape):
     k = info["kind"]
     if k == 1:
         return tuple(shape[:-1]) + (info["out_features"],)
+    if k == 11:
+        return (shape[0], shape[1], info["kernel"], info["stride"])
     if k == 2:
         n, c, h, w = shape
         oh = (h + 2 * info["padding"] - info["kernel"]) // info["stride"] + 1
@@ -232,7 +238,7 @@ def cpu_baseline(cfg: str, model, x, steps: int = 0, target_s: float = 12.0):
         return {"value": rows / dt / m, "unit": "GEMMs/s (rows/s / M)", "cores": cores, "kind": "port",
                 "sample": f"{rows} of {m} rows (scale over all rows), {cores} threads; extrapolated linearly in M",
                 "sample_seconds": dt}
-    n = min(64, x.shape[0])
+    n = min(2 if cfg == "c4" else 64, x.shape[0])
     t0 = time.perf_counter()
     prog.execute(x[:n], nthreads=cores)
     dt = time.perf_counter() - t0
@@ -255,7 +261,7 @@ def run_reference(args, rank: int, world: int):
     prog = oracle.Program([as_dict(l) for l in model.export()])
     cores = os.cpu_count() or 1
     c3 = cfg.startswith("c3")
-    sample = 64 if c3 else min(units, 2048 if cfg == "c2" else units)
+    sample = 64 if c3 else min(units, {"c2": 2048, "c4": 4}.get(cfg, units))
     ts = []
     for step in range(args.warmup + args.steps):
         t0 = time.perf_counter()
@@ -402,7 +408,7 @@ def main():
                    "parallelism": f"dp{world}", "l2": "flushed before every timed step (256 MiB write)"},
         "tops": tops, "tops_frac_of_nominal_int8": tops / NOMINAL_INT8_TOPS,
         "int8_macs_per_unit": macs_unit,
-        "roofline": op_roofline(cfg, sess, per_op_ns, args.steps, units, peaks),
+        "roofline": op_roofline(cfg, sess, per_op_ns, args.steps, x.shape, peaks),
         "e2e": {"value": e2e_value, "unit": "samples/s" if not cfg.startswith("c3") else "GEMMs/s",
                 "h2d_bytes_per_step": int(xh.nbytes), "d2h_bytes_per_step": int(yh.nbytes),
                 "api": "InferenceSession.run (rg_session_run), pinned host buffers", "steps": e2e_steps},

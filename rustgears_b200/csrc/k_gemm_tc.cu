@@ -375,6 +375,8 @@ bool launch_act(const GemmArgs& a, int num_sms, cudaStream_t st) {
 
 }  // namespace
 
+PFN_cuTensorMapEncodeTiled_v12000 tma_encode_fn() { return encode_fn(); }
+
 bool gemm_tc_eligible(const GemmArgs& a) {
   if (a.conv || a.out_l != 0 || a.rows_per_scale != 0 || a.amax.elems_per_slot != 0) return false;
   if (a.m <= 0 || a.n < 16 || a.k < 32 || (a.k & 15) || a.lda != a.k || a.ldb != a.k) return false;

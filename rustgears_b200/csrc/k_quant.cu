@@ -136,6 +136,44 @@ __global__ void __launch_bounds__(kThreads) k_image_quantize_nhwc(const float* _
   }
 }
 
+// Same result for cpad a multiple of 16, as a tiled transpose: block (pixels
+// 32 bx .. +31, channels 16 by .. +15, image bz) reads the NCHW f32 tile with
+// coalesced row loads, quantizes it with the image's scale and writes each pixel's
+// 16 channel bytes as four packed words (zeros for channels >= c).
+__global__ void __launch_bounds__(128) k_image_quantize_nhwc_tiled(const float* __restrict__ x, int32_t c,
+                                                                   int32_t hw, int32_t cpad,
+                                                                   const unsigned* __restrict__ amax,
+                                                                   int8_t* __restrict__ q,
+                                                                   float* __restrict__ scales) {
+  __shared__ float tile[16][33];
+  const int64_t img = blockIdx.z;
+  const int32_t p0 = blockIdx.x * 32, c0 = blockIdx.y * 16;
+  const float scale = quant_scale(__uint_as_float(amax[img]));
+  const float inv = quant_inv(scale);
+  if (scales && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) scales[img] = scale;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const float* src = x + img * (int64_t)c * hw;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int32_t ch = c0 + ty + 4 * i, px = p0 + tx;
+    tile[ty + 4 * i][tx] = (ch < c && px < hw) ? __ldg(src + (int64_t)ch * hw + px) : 0.0f;
+  }
+  __syncthreads();
+  const int pl = threadIdx.x >> 2, quad = threadIdx.x & 3;  // pixel in tile, 4-channel group
+  const int32_t px = p0 + pl;
+  if (px < hw) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int cl = 4 * quad + b;
+      // clamped: a strided conv's scale covers only the pixels it reads, others may exceed it
+      const int32_t v = c0 + cl < c ? quant1(tile[cl][pl], inv) : 0;
+      word |= (uint32_t)(v & 0xff) << (8 * b);
+    }
+    *reinterpret_cast<uint32_t*>(q + (img * hw + px) * (int64_t)cpad + c0 + 4 * quad) = word;
+  }
+}
+
 __global__ void k_nhwc_to_nchw_i8(const int8_t* __restrict__ q, int64_t n, int32_t c, int32_t cpad,
                                   int32_t hw, int8_t* __restrict__ out) {
   const int64_t total = n * (int64_t)c * hw;
@@ -185,6 +223,12 @@ void launch_image_quantize_nhwc(const float* x, int64_t n, int32_t c, int32_t h,
                                 float* scales_out, cudaStream_t st) {
   const int64_t total = n * (int64_t)h * w;
   if (total <= 0) return;
+  if ((cpad & 15) == 0) {  // channel-padded layout: tiled transpose
+    const int32_t hw = h * w;
+    dim3 grid((unsigned)((hw + 31) / 32), (unsigned)(cpad / 16), (unsigned)n);
+    k_image_quantize_nhwc_tiled<<<grid, 128, 0, st>>>(x, c, hw, cpad, amax_bits, q, scales_out);
+    return;
+  }
   k_image_quantize_nhwc<<<grid_for(total, kThreads, 148 * 32), kThreads, 0, st>>>(
       x, n, c, h * w, cpad, amax_bits, q, scales_out);
 }

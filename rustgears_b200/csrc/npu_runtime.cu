@@ -141,6 +141,7 @@ struct Op {
   std::vector<int8_t> wq;        // reference layout: Linear [out,in]; Conv [O, C*k*k]
   std::vector<float> bias;
   int64_t kdim = 0, kpad = 0;     // GEMM reduction length and its padded device stride
+  int32_t cpad = 0;               // conv: channels per tap in the device layouts (16-aligned, or 1)
   DevBuf d_w, d_bias, d_wsc;     // device weights [N, kpad] (conv: (ky,kx,c) order)
   bool bias_finite = true;
   std::string label;
@@ -336,13 +337,13 @@ static rg_status upload_op(Op& op) {
   if (op.kind == RG_LAYER_LINEAR) {
     for (int64_t n = 0; n < N; ++n)
       memcpy(&dev[(size_t)(n * op.kpad)], &op.wq[(size_t)(n * op.in_f)], (size_t)op.in_f);
-  } else {
-    const int64_t C = op.in_c, K = op.k;
+  } else {  // reduction order (ky, kx, c), c padded to cpad with zeros
+    const int64_t C = op.in_c, K = op.k, CP = op.cpad;
     for (int64_t o = 0; o < N; ++o)
       for (int64_t c = 0; c < C; ++c)
         for (int64_t ky = 0; ky < K; ++ky)
           for (int64_t kx = 0; kx < K; ++kx)
-            dev[(size_t)(o * op.kpad + (ky * K + kx) * C + c)] = op.wq[(size_t)(((o * C + c) * K + ky) * K + kx)];
+            dev[(size_t)(o * op.kpad + (ky * K + kx) * CP + c)] = op.wq[(size_t)(((o * C + c) * K + ky) * K + kx)];
   }
   RG_TRY(op.d_w.ensure(dev.size()));
   RG_CUDA_TRY(cudaMemcpy(op.d_w.p, dev.data(), dev.size(), cudaMemcpyHostToDevice));
@@ -402,8 +403,11 @@ static rg_status compile(Session& s, const rg_layer_spec* layers, int32_t n) {
         op.kdim = l.in_f;
       } else {
         op.in_c = l.in_c; op.out_c = l.out_c; op.k = l.k; op.stride = l.stride; op.pad = l.pad;
-        op.kdim = (int64_t)l.in_c * l.k * l.k;
-        quantize_weights(op, l.w.data(), l.out_c, op.kdim, s.weight_quant);
+        // channels padded to 16 per tap so the tensor-core conv gathers 16-byte chunks
+        // (a single channel stays unpadded: the fused CNN block reads it directly)
+        op.cpad = l.in_c == 1 ? 1 : (int32_t)round_up(l.in_c, 16);
+        quantize_weights(op, l.w.data(), l.out_c, (int64_t)l.in_c * l.k * l.k, s.weight_quant);
+        op.kdim = (int64_t)op.cpad * l.k * l.k;
       }
       op.kpad = round_up(op.kdim, 16);
       op.bias = l.b;
@@ -686,7 +690,10 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
     max_elems = std::max(max_elems, P.shapes[i].out_elems);
     const Op& op = s.ops[i];
     if (op.kind == RG_LAYER_LINEAR) max_q = std::max(max_q, P.shapes[i].in_elems / op.in_f * op.kpad);
-    if (op.kind == RG_LAYER_CONV2D) max_q = std::max(max_q, P.shapes[i].in_elems);
+    if (op.kind == RG_LAYER_CONV2D || op.kind == RG_LAYER_SHORTCUT_CONV2D) {
+      const std::vector<int64_t>& in = P.shapes[i].in;  // NHWC with channels padded to cpad
+      max_q = std::max(max_q, in[0] * in[2] * in[3] * op.cpad);
+    }
   }
   bool residual = false;
   for (size_t i = 0; i < n; ++i) residual = residual || s.ops[i].kind == RG_LAYER_RESIDUAL_BEGIN;
@@ -873,11 +880,13 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
           const int64_t N = os.in[0];
           const int32_t C = op.in_c, H = (int32_t)os.in[2], W = (int32_t)os.in[3];
           if (P.amax_src[i] < 0) { launch_image_absmax(src, N, C, H, W, rc[i], cc[i], my_amax, st); ++launches; RG_LAUNCHED("image_absmax"); }
-          launch_image_quantize_nhwc(src, N, C, H, W, C, my_amax, q, my_scale, st);
+          launch_image_quantize_nhwc(src, N, C, H, W, op.cpad, my_amax, q, my_scale, st);
           ++launches;
           RG_LAUNCHED("image_quantize_nhwc");
           g.a = q; g.conv = true;
-          g.g.h = H; g.g.w = W; g.g.c = C; g.g.cpad = C; g.g.k = op.k; g.g.stride = op.stride; g.g.pad = op.pad;
+          // padded channels hold zeros in both operands: the reduction runs over cpad per tap
+          g.g.h = H; g.g.w = W; g.g.c = op.cpad; g.g.cpad = op.cpad; g.g.k = op.k; g.g.stride = op.stride;
+          g.g.pad = op.pad;
           g.g.oh = (int32_t)os.out[2]; g.g.ow = (int32_t)os.out[3];
           const int64_t L = os.out[2] * os.out[3];
           g.m = N * L; g.n = op.out_c; g.k = op.kpad;
@@ -893,9 +902,13 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         g.out = dst;
         g.acc = s.trace ? s.accbuf.as<int32_t>() : nullptr;
         g.amax = sink;
-        const bool tc = !fused_q && gemm_tc_eligible(g);
-        const bool narrow = fused_q || (!tc && gemm_narrow_eligible(g));
-        if (tc) {
+        const bool conv_tc = g.conv && conv_tc_eligible(g);
+        const bool tc = !fused_q && !g.conv && gemm_tc_eligible(g);
+        const bool narrow = fused_q || (!tc && !conv_tc && gemm_narrow_eligible(g));
+        if (conv_tc) {
+          if (!launch_conv_tc(g, s.num_sms, st)) return fail(RG_ERR_CUDA, "op %zu: TMA descriptor encoding failed", i);
+          s.used_tc = true;
+        } else if (tc) {
           if (!launch_gemm_tc(g, s.num_sms, st)) return fail(RG_ERR_CUDA, "op %zu: TMA descriptor encoding failed", i);
           s.used_tc = true;
         } else if (narrow) {
@@ -904,7 +917,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
           launch_gemm_simt(g, st);
         }
         ++launches;
-        RG_LAUNCHED(tc ? "gemm_tc" : narrow ? "gemm_narrow" : "gemm_simt");
+        RG_LAUNCHED(conv_tc ? "conv_tc" : tc ? "gemm_tc" : narrow ? "gemm_narrow" : "gemm_simt");
         if (s.trace) {
           TraceRec& t = s.traces[i];
           RG_TRY(d2h_vec(t.scales, my_scale, P.amax_slots[i], st));
@@ -917,13 +930,13 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
             for (int64_t r = 0; r < rows; ++r)
               memcpy(&t.aq[(size_t)(r * op.in_f)], &tmp[(size_t)(r * op.kpad)], (size_t)op.in_f);
           } else {
+            const int64_t N = os.in[0], C = os.in[1], HW = os.in[2] * os.in[3], CP = op.cpad;
             std::vector<int8_t> tmp;
-            RG_TRY(d2h_vec(tmp, q, os.in_elems, st));
-            const int64_t N = os.in[0], C = os.in[1], HW = os.in[2] * os.in[3];
+            RG_TRY(d2h_vec(tmp, q, N * HW * CP, st));
             t.aq.resize((size_t)os.in_elems);
             for (int64_t b = 0; b < N; ++b)
               for (int64_t c = 0; c < C; ++c)
-                for (int64_t p = 0; p < HW; ++p) t.aq[(size_t)((b * C + c) * HW + p)] = tmp[(size_t)((b * HW + p) * C + c)];
+                for (int64_t p = 0; p < HW; ++p) t.aq[(size_t)((b * C + c) * HW + p)] = tmp[(size_t)((b * HW + p) * CP + c)];
           }
         }
         if (shortcut) {
@@ -1276,7 +1289,7 @@ static rg_status run_impl(rg_session* h, const float* x, bool x_host, const int6
   RG_CUDA_TRY(cudaStreamSynchronize(st));
   if (s.used_tc) {
     s.used_tc = false;
-    if (gemm_tc_take_error() != 0 || convblock_take_error() != 0)
+    if (gemm_tc_take_error() != 0 || convblock_take_error() != 0 || conv_tc_take_error() != 0)
       return fail(RG_ERR_TIMEOUT, "a tensor-core kernel gave up on a bounded wait; results are invalid");
   }
   int64_t total_ns = 0;

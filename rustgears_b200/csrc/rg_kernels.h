@@ -77,6 +77,11 @@ void launch_gemm_narrow(const GemmArgs& a, cudaStream_t st);
 // when the TMA descriptors could not be encoded (nothing was launched).
 bool gemm_tc_eligible(const GemmArgs& a);
 bool launch_gemm_tc(const GemmArgs& a, int num_sms, cudaStream_t st);
+// tcgen05 implicit-GEMM conv (A gathered from the NHWC i8 operand, channels padded to
+// a multiple of 16, g.c == g.cpad; NCHW output, per-image scales).
+bool conv_tc_eligible(const GemmArgs& a);
+bool launch_conv_tc(const GemmArgs& a, int num_sms, cudaStream_t st);
+int conv_tc_take_error();
 // Reads and clears the device error word the tcgen05 kernels set when a bounded
 // wait gave up (synchronous; 0 = no error).
 int gemm_tc_take_error();
