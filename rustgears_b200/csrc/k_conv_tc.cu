@@ -177,13 +177,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         ix0 = ox * p.stride - p.pad;
       }
       const int8_t* base = p.a + (int64_t)img * p.h * p.w * p.cpad;
-      // (tap, channel) of the first chunk of stage kb, advanced incrementally
+      // (tap, channel) of the next chunk to load, advanced incrementally; the loads of
+      // stage kb + 1 are in flight while stage kb waits for its slot and is stored
       int32_t c0 = 0, kx = 0, ky = 0, k0 = 0;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const bool got = mbar_wait(&empty[stage], phase ^ 1, abort);
-        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
-        uint8_t* sa = smem + stage * C::kStageBytes;
-        uint4 v[8];
+      auto load_stage = [&](uint4 (&v)[8]) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           v[j] = make_uint4(0u, 0u, 0u, 0u);
@@ -197,8 +194,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (++kx == p.k) { kx = 0; ++ky; }
           }
         }
+      };
+      uint4 cur[8], nxt[8];
+      load_stage(nxt);
+      for (int kb = 0; kb < num_kb; ++kb) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(sa + a_off + j * 128) = v[j];
+        for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+        if (kb + 1 < num_kb) load_stage(nxt);
+        const bool got = mbar_wait(&empty[stage], phase ^ 1, abort);
+        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+        uint8_t* sa = smem + stage * C::kStageBytes;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(sa + a_off + j * 128) = cur[j];
         fence_async_smem();  // generic-proxy stores -> visible to the tensor core
         __syncwarp();
         if (lane == 0) {
