@@ -44,6 +44,9 @@ WORKLOADS = {
     "c3c": dict(name="fused INT8 Linear+GELU 65536x4096x14336", shape=(65536, 4096, 14336)),
     "c4": dict(name="ResNet-18-shaped INT8 CNN (residual-block IR extension): x [B,3,224,224] ~ N(0,1), "
                     "conv7x7/2 + maxpool3x3/2 (pad 0) + 8 basic blocks + avgpool + Linear(512,1000)", batch=128),
+    "c5": dict(name="transformer encoder INT8 (embedding/RMSNorm/attention/SwiGLU IR extension): 12 pre-norm "
+                    "layers d_model 1024, 16 heads, SwiGLU hidden 2816, vocab 32000, seq 512, f32 attention",
+               batch=64),
 }
 
 
@@ -51,9 +54,10 @@ def build_workload(cfg: str, rank: int, world: int, batch: int | None):
     """(model, x shard, per-GPU units, units name) built with the reference generator."""
     from rustgears_b200 import configs
     w = WORKLOADS[cfg]
-    if cfg in ("c1", "c2", "c4"):
+    if cfg in ("c1", "c2", "c4", "c5"):
         b = batch or w["batch"]
-        fn = {"c1": configs.c1_mlp, "c2": configs.c2_cnn, "c4": configs.c4_resnet18}[cfg]
+        fn = {"c1": configs.c1_mlp, "c2": configs.c2_cnn, "c4": configs.c4_resnet18,
+              "c5": configs.c5_transformer}[cfg]
         model, x = fn(b, row_offset=rank * b)
         return model, x, b
     m, k, n = w["shape"]
@@ -201,6 +205,8 @@ def _out_shape(info, shape):
         return tuple(shape[:-1]) + (info["out_features"],)
     if k == 11:
         return (shape[0], shape[1], info["kernel"], info["stride"])
+    if k == 12:
+        return tuple(shape) + (info["out_features"],)
     if k == 2:
         n, c, h, w = shape
         oh = (h + 2 * info["padding"] - info["kernel"]) // info["stride"] + 1
@@ -238,14 +244,15 @@ def cpu_baseline(cfg: str, model, x, steps: int = 0, target_s: float = 12.0):
         return {"value": rows / dt / m, "unit": "GEMMs/s (rows/s / M)", "cores": cores, "kind": "port",
                 "sample": f"{rows} of {m} rows (scale over all rows), {cores} threads; extrapolated linearly in M",
                 "sample_seconds": dt}
-    n = min(2 if cfg == "c4" else 64, x.shape[0])
+    n = min({"c4": 2, "c5": 1}.get(cfg, 64), x.shape[0])
     t0 = time.perf_counter()
     prog.execute(x[:n], nthreads=cores)
     dt = time.perf_counter() - t0
-    n = int(min(x.shape[0], max(n, target_s / max(dt / n, 1e-9))))
-    t0 = time.perf_counter()
-    prog.execute(x[:n], nthreads=cores)
-    dt = time.perf_counter() - t0
+    if dt < target_s / 2:
+        n = int(min(x.shape[0], max(n, target_s / max(dt / n, 1e-9))))
+        t0 = time.perf_counter()
+        prog.execute(x[:n], nthreads=cores)
+        dt = time.perf_counter() - t0
     return {"value": n / dt, "unit": "samples/s", "cores": cores, "kind": "port",
             "sample": f"{n} samples of the benchmark batch through og_execute, {cores} threads",
             "sample_seconds": dt}
@@ -261,7 +268,7 @@ def run_reference(args, rank: int, world: int):
     prog = oracle.Program([as_dict(l) for l in model.export()])
     cores = os.cpu_count() or 1
     c3 = cfg.startswith("c3")
-    sample = 64 if c3 else min(units, {"c2": 2048, "c4": 4}.get(cfg, units))
+    sample = 64 if c3 else min(units, {"c2": 2048, "c4": 4, "c5": 1}.get(cfg, units))
     ts = []
     for step in range(args.warmup + args.steps):
         t0 = time.perf_counter()

@@ -66,7 +66,17 @@ typedef enum rg_layer_kind {
   RG_LAYER_RESIDUAL_BEGIN = 8,        /* saves the current activation as the block input */
   RG_LAYER_RESIDUAL_END = 9,          /* y = act(x + saved) with act, act_param; pops the saved input */
   RG_LAYER_SHORTCUT_CONV2D = 10,      /* Conv2d fields; applied to the saved input, replacing it */
-  RG_LAYER_ADAPTIVE_AVGPOOL2D = 11    /* output size: kernel = height, stride = width */
+  RG_LAYER_ADAPTIVE_AVGPOOL2D = 11,   /* output size: kernel = height, stride = width */
+  /* Extensions for the transformer configuration (no reference LayerSpec; the blocks
+   * compose the reference's Embedding, RMSNorm, MultiHeadAttention and SwiGLU with
+   * their Linears on the INT8 path).  Weights are [in,out] row-major like Linear. */
+  RG_LAYER_EMBEDDING = 12,  /* in_features = vocabulary V, out_features = d; weight [V, d];
+                               input: token ids (f32 values), output [.., d] */
+  RG_LAYER_RMSNORM = 13,    /* in_features = d; weight [d]; act_param = eps */
+  RG_LAYER_ATTENTION = 14,  /* non-causal multi-head attention: in_features = d, out_features =
+                               heads; weight = [Wq; Wk; Wv; Wo] (4 x [d, d]); bias = [bq; bk; bv; bo] */
+  RG_LAYER_SWIGLU = 15      /* in_features = d, out_features = hidden h; weight = [Wgate [d,h];
+                               Wup [d,h]; Wdown [h,d]]; no bias */
 } rg_layer_kind;
 
 typedef enum rg_activation {

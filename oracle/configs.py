@@ -13,8 +13,9 @@ from __future__ import annotations
 
 import numpy as np
 
-from .oracle import (ACT_GELU, ACT_RELU, ACTIVATION, ADAPTIVE_AVGPOOL2D, CHANNEL_AFFINE, CONV2D, FLATTEN,
-                     LINEAR, MAXPOOL2D, RESIDUAL_BEGIN, RESIDUAL_END, SHORTCUT_CONV2D, Rng)
+from .oracle import (ACT_GELU, ACT_RELU, ACTIVATION, ADAPTIVE_AVGPOOL2D, ATTENTION, CHANNEL_AFFINE, CONV2D,
+                     EMBEDDING, FLATTEN, LINEAR, MAXPOOL2D, RESIDUAL_BEGIN, RESIDUAL_END, RMSNORM, SHORTCUT_CONV2D,
+                     SWIGLU, Rng)
 
 
 def linear(rng: Rng, fin: int, fout: int) -> dict:  # Linear::new (nn/layers.rs:27-34)
@@ -186,6 +187,51 @@ def resnet_mini(batch: int = 3, seed: int = 9):
     return resnet(batch, 24, (8, 16), 10, seed, stem_k=3)
 
 
+def transformer(batch: int, seq: int, d: int, heads: int, hidden: int, n_layers: int, vocab: int,
+                seed: int = 42):
+    """Pre-norm transformer encoder (extension kinds): Embedding (table ~ 0.02 N(0,1)),
+    then per layer x += Attention(RMSNorm(x)) and x += SwiGLU(RMSNorm(x)); attention
+    Linears with bias (MultiHeadAttention::new, nn/attention.rs:130-143), SwiGLU Linears
+    bias-free (SwiGLU::new, nn/layers.rs:492-497), RMSNorm weight ones, eps 1e-6.
+    Draw order: the table, then per layer Wq, bq, Wk, bk, Wv, bv, Wo, bo, then Wgate,
+    Wup, Wdown each followed by its dropped bias; then the token ids ~ U[0, vocab)
+    [batch, seq] as f32."""
+    rng = Rng(seed)
+    table = rng.normal_init((vocab, d), 0.02)
+    layers = [dict(kind=EMBEDDING, in_features=vocab, out_features=d, weight=table)]
+    for _ in range(n_layers):
+        w, b = [], []
+        for _ in range(4):
+            w.append(rng.kaiming_uniform((d, d), d))
+            b.append(rng.bias_uniform((d,), d))
+        # Linear::no_bias builds Linear::new and drops the bias (nn/layers.rs:37-41): the
+        # bias is still drawn
+        g = rng.kaiming_uniform((d, hidden), d); rng.bias_uniform((hidden,), d)
+        u = rng.kaiming_uniform((d, hidden), d); rng.bias_uniform((hidden,), d)
+        dn = rng.kaiming_uniform((hidden, d), hidden); rng.bias_uniform((d,), hidden)
+        norm = lambda: dict(kind=RMSNORM, in_features=d, weight=np.ones(d, np.float32), act_param=1e-6)
+        layers += [dict(kind=RESIDUAL_BEGIN), norm(),
+                   dict(kind=ATTENTION, in_features=d, out_features=heads, weight=np.concatenate([x.ravel() for x in w]),
+                        bias=np.concatenate(b)),
+                   dict(kind=RESIDUAL_END, act=0, act_param=0.0),
+                   dict(kind=RESIDUAL_BEGIN), norm(),
+                   dict(kind=SWIGLU, in_features=d, out_features=hidden,
+                        weight=np.concatenate([g.ravel(), u.ravel(), dn.ravel()])),
+                   dict(kind=RESIDUAL_END, act=0, act_param=0.0)]
+    ids = rng.below((batch, seq), vocab).astype(np.float32)
+    return layers, ids
+
+
+def transformer_c5(batch: int = 64, seq: int = 512, n_layers: int = 12, seed: int = 42):
+    """The transformer benchmark configuration: 12 layers, d_model 1024, 16 heads, SwiGLU
+    hidden 2816, vocabulary 32000, sequence 512."""
+    return transformer(batch, seq, 1024, 16, 2816, n_layers, 32000, seed)
+
+
+def transformer_mini(batch: int = 2, seq: int = 12, seed: int = 13):
+    return transformer(batch, seq, 64, 4, 96, 2, 500, seed)
+
+
 # name -> builder of (layers, x) used by the golden fixtures and the parity tests
 CASES = {
     "usage_doc": usage_doc_model,
@@ -197,4 +243,5 @@ CASES = {
     "strided_cnn": strided_cnn,
     "affine_first": affine_first,
     "resnet_mini": resnet_mini,
+    "transformer_mini": transformer_mini,
 }

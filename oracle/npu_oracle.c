@@ -308,6 +308,117 @@ void og_residual_add(const float* x, const float* sv, int64_t n, int32_t act, fl
   for (int64_t i = 0; i < n; ++i) y[i] = og_act_apply(act, param, x[i] + sv[i]);
 }
 
+/* ---- transformer extensions ------------------------------------------------- */
+
+/* Embedding::forward (nn/layers.rs:438-446): row ids[r] of the table; the id is the f32
+ * value cast `as usize` (truncation, NaN and negatives saturate to 0); an id >= V is
+ * the reference's assertion failure (-6 here). */
+int32_t og_embedding(const og_op* op, const float* ids, int64_t n, float* y) {
+  const int64_t v = op->in_features, d = op->out_features;
+  for (int64_t r = 0; r < n; ++r) {
+    const float f = ids[r];
+    uint64_t idx = 0;
+    if (f >= 18446744073709551616.0f) idx = UINT64_MAX;
+    else if (f >= 1.0f) idx = (uint64_t)f;
+    if (idx >= (uint64_t)v) return -6;
+    memcpy(y + r * d, op->extra + (int64_t)idx * d, sizeof(float) * (size_t)d);
+  }
+  return 0;
+}
+
+/* RMSNorm::forward (nn/norm.rs:413-417): rms = sqrt(mean_dim(x*x, -1) + eps) with the
+ * squares summed serially from 0 (sum_dim, tensor/ops.rs:715-727) and the mean as a
+ * multiplication by 1/d (mean_dim, 755-758); y = (x / rms) * weight. */
+void og_rmsnorm(const og_op* op, const float* x, int64_t rows, float* y) {
+  const int64_t d = op->in_features;
+  const float inv_d = 1.0f / (float)d;
+  for (int64_t r = 0; r < rows; ++r) {
+    const float* xr = x + r * d;
+    float s = 0.0f;
+    for (int64_t i = 0; i < d; ++i) { const float sq = xr[i] * xr[i]; s += sq; }
+    const float rms = sqrtf(s * inv_d + op->act_param);
+    for (int64_t i = 0; i < d; ++i) y[r * d + i] = (xr[i] / rms) * op->extra[i];
+  }
+}
+
+/* cpu_matmul per batch (device/cpu.rs:43-64 with matmul_avx2 233-395): every output
+ * starts at 0 and accumulates fma(a[i][p], b[p][j], c) for p = 0..k-1 in order;
+ * columns past the last full 8-wide block accumulate unfused (c += a * b). */
+void og_bmm_fma(const float* a, const float* bm, int64_t batch, int64_t m, int64_t k, int64_t n, float* c) {
+  const int64_t nv = n / 8 * 8;
+  for (int64_t b = 0; b < batch; ++b) {
+    const float* ab = a + b * m * k;
+    const float* bb = bm + b * k * n;
+    float* cb = c + b * m * n;
+    for (int64_t i = 0; i < m; ++i)
+      for (int64_t j = 0; j < n; ++j) {
+        float acc = 0.0f;
+        if (j < nv) {
+          for (int64_t p = 0; p < k; ++p) acc = fmaf(ab[i * k + p], bb[p * n + j], acc);
+        } else {
+          for (int64_t p = 0; p < k; ++p) { const float t = ab[i * k + p] * bb[p * n + j]; acc += t; }
+        }
+        cb[i * n + j] = acc;
+      }
+  }
+}
+
+/* MultiHeadAttention, non-causal (nn/attention.rs:162-196) with its q, k, v, o Linears
+ * on the INT8 path: heads split [b, t, h, dh] -> [b*h, t, dh], scores = bmm(q, k^T) *
+ * (1 / sqrt(dh)), softmax over keys, bmm(p, v), heads merged, o projection. */
+void og_attention(const og_op* op, const float* x, int64_t b, int64_t t, float* y, int32_t nthreads) {
+  const int64_t d = op->in_features, h = op->out_features, dh = d / h, rows = b * t;
+  float* q = (float*)malloc(sizeof(float) * (size_t)(rows * d));
+  float* k = (float*)malloc(sizeof(float) * (size_t)(rows * d));
+  float* v = (float*)malloc(sizeof(float) * (size_t)(rows * d));
+  og_op_linear(&op->sub[0], x, rows, q, NULL, NULL, NULL, nthreads);
+  og_op_linear(&op->sub[1], x, rows, k, NULL, NULL, NULL, nthreads);
+  og_op_linear(&op->sub[2], x, rows, v, NULL, NULL, NULL, nthreads);
+  const int64_t bh = b * h;
+  float* qs = (float*)malloc(sizeof(float) * (size_t)(bh * t * dh));
+  float* kt = (float*)malloc(sizeof(float) * (size_t)(bh * dh * t));   /* k transposed: [bh, dh, t] */
+  float* vs = (float*)malloc(sizeof(float) * (size_t)(bh * t * dh));
+  for (int64_t bi = 0; bi < b; ++bi)
+    for (int64_t ti = 0; ti < t; ++ti)
+      for (int64_t hi = 0; hi < h; ++hi)
+        for (int64_t e = 0; e < dh; ++e) {
+          const int64_t src = (bi * t + ti) * d + hi * dh + e, g = bi * h + hi;
+          qs[(g * t + ti) * dh + e] = q[src];
+          kt[(g * dh + e) * t + ti] = k[src];
+          vs[(g * t + ti) * dh + e] = v[src];
+        }
+  float* sc = (float*)malloc(sizeof(float) * (size_t)(bh * t * t));
+  og_bmm_fma(qs, kt, bh, t, dh, t, sc);
+  const float scale = 1.0f / sqrtf((float)dh);
+  for (int64_t i = 0; i < bh * t * t; ++i) sc[i] = sc[i] * scale;
+  og_softmax(sc, bh * t, t, sc);
+  float* o = (float*)malloc(sizeof(float) * (size_t)(bh * t * dh));
+  og_bmm_fma(sc, vs, bh, t, t, dh, o);
+  float* merged = q;  /* reuse: [b, t, d] */
+  for (int64_t g = 0; g < bh; ++g)
+    for (int64_t ti = 0; ti < t; ++ti)
+      for (int64_t e = 0; e < dh; ++e)
+        merged[((g / h) * t + ti) * d + (g % h) * dh + e] = o[(g * t + ti) * dh + e];
+  og_op_linear(&op->sub[3], merged, rows, y, NULL, NULL, NULL, nthreads);
+  free(q); free(k); free(v); free(qs); free(kt); free(vs); free(sc); free(o);
+}
+
+/* SwiGLU::forward (nn/layers.rs:507-513) with bias-free INT8 Linears:
+ * down((g * sigmoid(g)) * u), g = gate(x), u = up(x). */
+void og_swiglu(const og_op* op, const float* x, int64_t rows, float* y, int32_t nthreads) {
+  const int64_t hd = op->out_features;
+  float* g = (float*)malloc(sizeof(float) * (size_t)(rows * hd));
+  float* u = (float*)malloc(sizeof(float) * (size_t)(rows * hd));
+  og_op_linear(&op->sub[0], x, rows, g, NULL, NULL, NULL, nthreads);
+  og_op_linear(&op->sub[1], x, rows, u, NULL, NULL, NULL, nthreads);
+  for (int64_t i = 0; i < rows * hd; ++i) {
+    const float silu = g[i] * og_act_apply(OG_ACT_SIGMOID, 0.0f, g[i]);
+    g[i] = silu * u[i];
+  }
+  og_op_linear(&op->sub[2], g, rows, y, NULL, NULL, NULL, nthreads);
+  free(g); free(u);
+}
+
 void og_softmax(const float* x, int64_t outer, int64_t last, float* y) { /* ops.rs:1058-1076 */
   for (int64_t o = 0; o < outer; ++o) {
     const float* xr = x + o * last; float* yr = y + o * last;
@@ -370,6 +481,24 @@ void og_fold_batch_norm_count(const og_layer* layers, int32_t n, int32_t* out_co
   *out_count = m;
 }
 
+/* An INT8 Linear as npu::compile builds one (npu.rs:207-216): W [in,out] transposed to
+ * [out,in], per-tensor i8; a NULL bias is a bias-free Linear (zeros, no f32 bias bytes). */
+static void og_make_linear(og_program* p, og_op* op, const float* w_in_out, int32_t in, int32_t out,
+                           const float* b) {
+  memset(op, 0, sizeof(*op));
+  op->kind = OG_LAYER_LINEAR; op->in_features = in; op->out_features = out; op->act = OG_ACT_NONE;
+  const int64_t wl = (int64_t)in * out;
+  float* wt = (float*)malloc(sizeof(float) * (size_t)(wl > 0 ? wl : 1));
+  og_transpose2d(w_in_out, in, out, wt);
+  op->wq = (int8_t*)malloc((size_t)(wl > 0 ? wl : 1)); op->wq_len = wl;
+  op->w_scale = og_quantize_into(wt, wl, op->wq);
+  free(wt);
+  op->bias = (float*)calloc((size_t)(out > 0 ? out : 1), sizeof(float)); op->bias_len = out;
+  if (b) memcpy(op->bias, b, sizeof(float) * (size_t)out);
+  p->fp32_bytes += (wl + (b ? out : 0)) * 4;
+  p->npu_bytes += (wl + 4) + (b ? out : 0) * 4;
+}
+
 og_program* og_compile(const og_layer* layers, int32_t n_layers, int32_t precision) {
   int32_t m = 0;
   og_flayer* f = og_fold(layers, n_layers, &m);
@@ -419,6 +548,26 @@ og_program* og_compile(const og_layer* layers, int32_t n_layers, int32_t precisi
       op->bias = (float*)malloc(sizeof(float) * (size_t)(c > 0 ? c : 1));
       memcpy(op->bias, l->b, sizeof(float) * (size_t)c); op->bias_len = c;
       op->act = OG_ACT_NONE;
+    } else if (l->kind == OG_LAYER_ATTENTION || l->kind == OG_LAYER_SWIGLU) {
+      const int32_t d = l->in_f, hdim = l->out_f;
+      op->kind = l->kind; op->in_features = d; op->out_features = hdim;
+      if (l->kind == OG_LAYER_ATTENTION) {   /* out_features = heads */
+        op->sub = (og_op*)calloc(4, sizeof(og_op)); op->n_sub = 4;
+        for (int32_t j = 0; j < 4; ++j)
+          og_make_linear(p, &op->sub[j], l->w + (int64_t)j * d * d, d, d, l->b + (int64_t)j * d);
+      } else {                               /* out_features = hidden */
+        op->sub = (og_op*)calloc(3, sizeof(og_op)); op->n_sub = 3;
+        og_make_linear(p, &op->sub[0], l->w, d, hdim, NULL);
+        og_make_linear(p, &op->sub[1], l->w + (int64_t)d * hdim, d, hdim, NULL);
+        og_make_linear(p, &op->sub[2], l->w + 2 * (int64_t)d * hdim, hdim, d, NULL);
+      }
+    } else if (l->kind == OG_LAYER_EMBEDDING || l->kind == OG_LAYER_RMSNORM) {
+      op->kind = l->kind; op->in_features = l->in_f; op->out_features = l->out_f;
+      op->act_param = l->param;
+      op->extra = (float*)malloc(sizeof(float) * (size_t)(l->w_len > 0 ? l->w_len : 1));
+      memcpy(op->extra, l->w, sizeof(float) * (size_t)l->w_len); op->extra_len = l->w_len;
+      p->fp32_bytes += l->w_len * 4;   /* kept in f32 on both paths */
+      p->npu_bytes += l->w_len * 4;
     } else {
       op->kind = l->kind; op->kernel = l->k; op->stride = l->stride;
       op->act = l->act; op->act_param = l->param;
@@ -433,7 +582,11 @@ og_program* og_compile(const og_layer* layers, int32_t n_layers, int32_t precisi
 
 void og_program_free(og_program* p) {
   if (!p) return;
-  for (int32_t i = 0; i < p->n_ops; ++i) { free(p->ops[i].wq); free(p->ops[i].bias); }
+  for (int32_t i = 0; i < p->n_ops; ++i) {
+    for (int32_t j = 0; j < p->ops[i].n_sub; ++j) { free(p->ops[i].sub[j].wq); free(p->ops[i].sub[j].bias); }
+    free(p->ops[i].sub); free(p->ops[i].extra);
+    free(p->ops[i].wq); free(p->ops[i].bias);
+  }
   free(p->ops); free(p);
 }
 
@@ -485,6 +638,10 @@ int32_t og_op_label(const og_op* op, char* buf, int32_t cap) { /* npu.rs:83-104 
     case OG_LAYER_SHORTCUT_CONV2D:
       return snprintf(buf, (size_t)cap, "NPU::ShortcutConv2d(%d->%d, k=%d)", op->in_channels, op->out_channels, op->kernel);
     case OG_LAYER_ADAPTIVE_AVGPOOL2D: return snprintf(buf, (size_t)cap, "NPU::AdaptiveAvgPool2d(%dx%d)", op->kernel, op->stride);
+    case OG_LAYER_EMBEDDING: return snprintf(buf, (size_t)cap, "NPU::Embedding(%d, %d)", op->in_features, op->out_features);
+    case OG_LAYER_RMSNORM: return snprintf(buf, (size_t)cap, "NPU::RMSNorm(%d)", op->in_features);
+    case OG_LAYER_ATTENTION: return snprintf(buf, (size_t)cap, "NPU::Attention(d=%d, heads=%d)", op->in_features, op->out_features);
+    case OG_LAYER_SWIGLU: return snprintf(buf, (size_t)cap, "NPU::SwiGLU(%d->%d->%d)", op->in_features, op->out_features, op->in_features);
     default: return snprintf(buf, (size_t)cap, "NPU::?");
   }
 }
@@ -697,6 +854,38 @@ int32_t og_execute(const og_program* p, const float* x, const int64_t* shape, in
         out = (float*)malloc(sizeof(float) * (size_t)(olen > 0 ? olen : 1));
         og_adaptive_avgpool2d(data, sh[0], (int32_t)sh[1], (int32_t)sh[2], (int32_t)sh[3], op->kernel, op->stride, out);
         sh[2] = op->kernel; sh[3] = op->stride; len = olen;
+        break;
+      }
+      case OG_LAYER_EMBEDDING: {
+        if (nd >= 8) OG_EXEC_FAIL(-2);
+        int64_t olen = len * op->out_features;
+        out = (float*)malloc(sizeof(float) * (size_t)(olen > 0 ? olen : 1));
+        if (og_embedding(op, data, len, out) != 0) { free(out); OG_EXEC_FAIL(-6); }
+        sh[nd++] = op->out_features; len = olen;
+        break;
+      }
+      case OG_LAYER_RMSNORM: {
+        if (sh[nd - 1] != op->in_features) OG_EXEC_FAIL(-2);
+        out = (float*)malloc(sizeof(float) * (size_t)(len > 0 ? len : 1));
+        og_rmsnorm(op, data, len / op->in_features, out);
+        break;
+      }
+      case OG_LAYER_ATTENTION: {
+        if (nd != 3 || sh[2] != op->in_features || op->out_features <= 0 || op->in_features % op->out_features)
+          OG_EXEC_FAIL(-2);
+        const int64_t t = sh[1], dh = op->in_features / op->out_features;
+        macs = 4 * sh[0] * t * (int64_t)op->in_features * op->in_features;   /* INT8 projections */
+        (void)dh;
+        out = (float*)malloc(sizeof(float) * (size_t)(len > 0 ? len : 1));
+        if (len) og_attention(op, data, sh[0], t, out, nthreads);
+        break;
+      }
+      case OG_LAYER_SWIGLU: {
+        if (sh[nd - 1] != op->in_features) OG_EXEC_FAIL(-2);
+        const int64_t rows = len / op->in_features;
+        macs = 3 * rows * (int64_t)op->in_features * op->out_features;
+        out = (float*)malloc(sizeof(float) * (size_t)(len > 0 ? len : 1));
+        if (len) og_swiglu(op, data, rows, out, nthreads);
         break;
       }
       default: OG_EXEC_FAIL(-3);

@@ -43,7 +43,9 @@ enum {
   OG_LAYER_SOFTMAX = 7,
   /* extensions (see include/rg_npu.h): residual blocks, adaptive average pooling */
   OG_LAYER_RESIDUAL_BEGIN = 8, OG_LAYER_RESIDUAL_END = 9, OG_LAYER_SHORTCUT_CONV2D = 10,
-  OG_LAYER_ADAPTIVE_AVGPOOL2D = 11
+  OG_LAYER_ADAPTIVE_AVGPOOL2D = 11,
+  /* extensions for the transformer configuration (see include/rg_npu.h) */
+  OG_LAYER_EMBEDDING = 12, OG_LAYER_RMSNORM = 13, OG_LAYER_ATTENTION = 14, OG_LAYER_SWIGLU = 15
 };
 enum { OG_ACT_NONE = 0, OG_ACT_RELU = 1, OG_ACT_SIGMOID = 2, OG_ACT_TANH = 3,
        OG_ACT_GELU = 4, OG_ACT_LEAKY_RELU = 5 };
@@ -59,13 +61,17 @@ typedef struct {
 } og_layer;
 
 /* Compiled program: src/inference/npu.rs:43-79 (NpuOp), 179-185 (NpuProgram). */
-typedef struct {
+typedef struct og_op {
   int32_t kind;           /* OG_LAYER_LINEAR / CONV2D / MAXPOOL2D / FLATTEN / ACTIVATION / SOFTMAX */
   int32_t in_features, out_features;
   int32_t in_channels, out_channels, kernel, stride, padding;
   int8_t* wq; int64_t wq_len; float w_scale;   /* Linear: [out,in]; Conv: [O, C*k*k] */
   float* bias; int64_t bias_len;
   int32_t act; float act_param;
+  /* extensions: the INT8 Linears inside an attention block (q, k, v, o) or a SwiGLU
+   * (gate, up, down), and an f32 array (embedding table [V, d], RMSNorm weight [d]) */
+  struct og_op* sub; int32_t n_sub, _pad2;
+  float* extra; int64_t extra_len;
 } og_op;
 
 typedef struct {
@@ -106,6 +112,12 @@ void og_activation(const float* x, int64_t n, int32_t act, float param, float* y
 void og_adaptive_avgpool2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t oh,
                            int32_t ow, float* y);
 void og_residual_add(const float* x, const float* s, int64_t n, int32_t act, float param, float* y);
+/* transformer extensions: 0 on success, -6 for an embedding id out of range */
+int32_t og_embedding(const og_op* op, const float* ids, int64_t n, float* y);
+void og_rmsnorm(const og_op* op, const float* x, int64_t rows, float* y);
+void og_attention(const og_op* op, const float* x, int64_t b, int64_t t, float* y, int32_t nthreads);
+void og_swiglu(const og_op* op, const float* x, int64_t rows, float* y, int32_t nthreads);
+void og_bmm_fma(const float* a, const float* bm, int64_t batch, int64_t m, int64_t k, int64_t n, float* c);
 void og_softmax(const float* x, int64_t outer, int64_t last, float* y); /* tensor/ops.rs:1058-1076 */
 int64_t og_out_size(int64_t input, int64_t k, int64_t stride, int64_t pad); /* kernels.rs:10-15 */
 void og_im2col(const float* x, int32_t c, int32_t h, int32_t w, int32_t k, int32_t stride,

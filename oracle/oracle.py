@@ -25,6 +25,8 @@ _LIB_PATH = os.path.join(_HERE, "liboracle.so")
 LINEAR, CONV2D, CHANNEL_AFFINE, MAXPOOL2D, FLATTEN, ACTIVATION, SOFTMAX = 1, 2, 3, 4, 5, 6, 7
 # extensions (no reference LayerSpec): residual blocks, adaptive average pooling
 RESIDUAL_BEGIN, RESIDUAL_END, SHORTCUT_CONV2D, ADAPTIVE_AVGPOOL2D = 8, 9, 10, 11
+# extensions for the transformer configuration
+EMBEDDING, RMSNORM, ATTENTION, SWIGLU = 12, 13, 14, 15
 ACT_NONE, ACT_RELU, ACT_SIGMOID, ACT_TANH, ACT_GELU, ACT_LEAKY_RELU = 0, 1, 2, 3, 4, 5
 
 
@@ -44,14 +46,19 @@ class _Layer(C.Structure):
 
 
 class _Op(C.Structure):
-    _fields_ = [
-        ("kind", C.c_int32), ("in_features", C.c_int32), ("out_features", C.c_int32),
-        ("in_channels", C.c_int32), ("out_channels", C.c_int32), ("kernel", C.c_int32),
-        ("stride", C.c_int32), ("padding", C.c_int32),
-        ("wq", C.POINTER(C.c_int8)), ("wq_len", C.c_int64), ("w_scale", C.c_float),
-        ("bias", C.POINTER(C.c_float)), ("bias_len", C.c_int64),
-        ("act", C.c_int32), ("act_param", C.c_float),
-    ]
+    pass
+
+
+_Op._fields_ = [
+    ("kind", C.c_int32), ("in_features", C.c_int32), ("out_features", C.c_int32),
+    ("in_channels", C.c_int32), ("out_channels", C.c_int32), ("kernel", C.c_int32),
+    ("stride", C.c_int32), ("padding", C.c_int32),
+    ("wq", C.POINTER(C.c_int8)), ("wq_len", C.c_int64), ("w_scale", C.c_float),
+    ("bias", C.POINTER(C.c_float)), ("bias_len", C.c_int64),
+    ("act", C.c_int32), ("act_param", C.c_float),
+    ("sub", C.POINTER(_Op)), ("n_sub", C.c_int32), ("_pad2", C.c_int32),
+    ("extra", C.POINTER(C.c_float)), ("extra_len", C.c_int64),
+]
 
 
 class _Program(C.Structure):
@@ -117,6 +124,12 @@ def lib():
         L.og_adaptive_avgpool2d.argtypes = [f32p, C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                             C.c_int32, f32p]
         L.og_residual_add.argtypes = [f32p, f32p, C.c_int64, C.c_int32, C.c_float, f32p]
+        L.og_embedding.argtypes = [C.POINTER(_Op), f32p, C.c_int64, f32p]
+        L.og_embedding.restype = C.c_int32
+        L.og_rmsnorm.argtypes = [C.POINTER(_Op), f32p, C.c_int64, f32p]
+        L.og_attention.argtypes = [C.POINTER(_Op), f32p, C.c_int64, C.c_int64, f32p, C.c_int32]
+        L.og_swiglu.argtypes = [C.POINTER(_Op), f32p, C.c_int64, f32p, C.c_int32]
+        L.og_bmm_fma.argtypes = [f32p, f32p, C.c_int64, C.c_int64, C.c_int64, C.c_int64, f32p]
         L.og_out_size.argtypes = [C.c_int64] * 4
         L.og_out_size.restype = C.c_int64
         L.og_im2col.argtypes = [f32p] + [C.c_int32] * 8 + [f32p]
@@ -228,8 +241,9 @@ class Op:
     def __init__(self, raw: _Op):
         self.raw = raw
         for f, _ in _Op._fields_:
-            if f not in ("wq", "bias"):
+            if f not in ("wq", "bias", "sub", "extra"):
                 setattr(self, f, getattr(raw, f))
+        self.sub = [Op(raw.sub[j]) for j in range(raw.n_sub)]
         self.wq = np.ctypeslib.as_array(raw.wq, shape=(raw.wq_len,)).copy() if raw.wq_len else None
         self.bias = np.ctypeslib.as_array(raw.bias, shape=(raw.bias_len,)).copy() if raw.bias_len else None
 
@@ -340,7 +354,24 @@ class Program:
             return residual_add(data, saved.pop(), op.act, op.act_param)
         if op.kind == ADAPTIVE_AVGPOOL2D:
             return adaptive_avgpool2d(data, op.kernel, op.stride)
-        raise ValueError(op.kind)
+        raw = C.byref(self._p.contents.ops[i])
+        data = _f32(data)
+        if op.kind == EMBEDDING:
+            y = np.empty(data.shape + (op.out_features,), np.float32)
+            if lib().og_embedding(raw, _p(data, C.c_float), data.size, _p(y, C.c_float)) != 0:
+                raise IndexError("Embedding: index out of range")
+            return y
+        y = np.empty_like(data)
+        if op.kind == RMSNORM:
+            lib().og_rmsnorm(raw, _p(data, C.c_float), data.size // op.in_features, _p(y, C.c_float))
+        elif op.kind == ATTENTION:
+            b, t, _ = data.shape
+            lib().og_attention(raw, _p(data, C.c_float), b, t, _p(y, C.c_float), nthreads)
+        elif op.kind == SWIGLU:
+            lib().og_swiglu(raw, _p(data, C.c_float), data.size // op.in_features, _p(y, C.c_float), nthreads)
+        else:
+            raise ValueError(op.kind)
+        return y
 
     def run_traced(self, x, nthreads: int = 1):
         """Execute op by op and record every intermediate (for golden vectors):
@@ -410,6 +441,10 @@ def _out_capacity(prog: Program, in_shape) -> int:
             shape = [shape[0], int(np.prod(shape[1:]))]
         elif op.kind == ADAPTIVE_AVGPOOL2D:
             shape = [shape[0], shape[1], op.kernel, op.stride]
+        elif op.kind == EMBEDDING:
+            shape = shape + [op.out_features]
+        elif op.kind == SWIGLU:
+            best = max(best, int(np.prod(shape[:-1])) * op.out_features)
         best = max(best, int(np.prod(shape)))
     return max(best, 1)
 

@@ -74,5 +74,23 @@ def c4_resnet18(batch: int = 128, seed: int = 42, row_offset: int = 0, image: in
     return resnet(batch, image, (64, 128, 256, 512), 1000, seed, 7, row_offset)
 
 
+def transformer(batch: int, seq: int, d: int, heads: int, hidden: int, n_layers: int, vocab: int,
+                seed: int = 42, row_offset: int = 0):
+    """Pre-norm transformer encoder (extension kinds): Embedding(vocab, d) with the table
+    ~ 0.02 N(0,1), then n_layers x PreNormEncoderLayer(d, heads, hidden); token ids
+    ~ U[0, vocab) [batch, seq] as f32 (sequences [row_offset, row_offset + batch))."""
+    rng.manual_seed(seed)
+    model = nn.Sequential(nn.Embedding(vocab, d, std=0.02),
+                          *[nn.PreNormEncoderLayer(d, heads, hidden) for _ in range(n_layers)])
+    rng.advance(seq * row_offset)
+    return model, rng.below((batch, seq), vocab).astype(np.float32)
+
+
+def c5_transformer(batch: int = 64, seed: int = 42, row_offset: int = 0, seq: int = 512, n_layers: int = 12):
+    """The transformer configuration: 12 layers, d_model 1024, 16 heads, SwiGLU hidden
+    2816, vocabulary 32000, sequence 512, batch 64."""
+    return transformer(batch, seq, 1024, 16, 2816, n_layers, 32000, seed, row_offset)
+
+
 def input_only(config: str, batch: int, seed: int = 42) -> np.ndarray:
     return {"c1": c1_mlp, "c2": c2_cnn}[config](batch, seed)[1]

@@ -145,6 +145,11 @@ struct Op {
   DevBuf d_w, d_bias, d_wsc;     // device weights [N, kpad] (conv: (ky,kx,c) order)
   bool bias_finite = true;
   std::string label;
+  // transformer extension: the INT8 Linears inside an op (attention: fused QKV
+  // [3d, d] with per-column scales, then Wo; SwiGLU: fused gate|up [2h, d], then
+  // Wdown) and an f32 array (embedding table [V, d], RMSNorm weight [d])
+  std::vector<Op> subs;
+  DevBuf d_ext;
 };
 
 struct TraceRec {
@@ -180,11 +185,13 @@ struct Session {
   std::mutex mu;
   // workspace
   DevBuf act0, act1, act2, act3, qbuf, amax, scales, accbuf, xin, yout, covbuf;
+  DevBuf ext0, ext1;  // attention / SwiGLU intermediates (QKV or gate|up, merged heads or g*u)
   // profile + trace
   Profile last;
   bool trace = false;
   std::vector<TraceRec> traces;
   bool used_tc = false;  // a tcgen05 kernel ran since the last error-word check
+  bool used_embed = false;  // an embedding gather ran since the last error-word check
   // multi-GPU
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1;
@@ -237,6 +244,10 @@ static std::string make_label(const Op& op) {  // NpuOp::label (npu.rs:83-104)
       snprintf(buf, sizeof buf, "NPU::ShortcutConv2d(%d->%d, k=%d)", op.in_c, op.out_c, op.k);
       break;
     case RG_LAYER_ADAPTIVE_AVGPOOL2D: snprintf(buf, sizeof buf, "NPU::AdaptiveAvgPool2d(%dx%d)", op.k, op.stride); break;
+    case RG_LAYER_EMBEDDING: snprintf(buf, sizeof buf, "NPU::Embedding(%d, %d)", op.in_f, op.out_f); break;
+    case RG_LAYER_RMSNORM: snprintf(buf, sizeof buf, "NPU::RMSNorm(%d)", op.in_f); break;
+    case RG_LAYER_ATTENTION: snprintf(buf, sizeof buf, "NPU::Attention(d=%d, heads=%d)", op.in_f, op.out_f); break;
+    case RG_LAYER_SWIGLU: snprintf(buf, sizeof buf, "NPU::SwiGLU(%d->%d->%d)", op.in_f, op.out_f, op.in_f); break;
     default: snprintf(buf, sizeof buf, "NPU::?"); break;
   }
   return buf;
@@ -289,6 +300,29 @@ static rg_status validate_layer(const rg_layer_spec& l, int idx) {
     case RG_LAYER_ACTIVATION:
       if (l.act < RG_ACT_NONE || l.act > RG_ACT_LEAKY_RELU)
         return fail(RG_ERR_INVALID_ARG, "layer %d: unknown activation tag %d", idx, l.act);
+      return RG_OK;
+    case RG_LAYER_EMBEDDING:
+      if (l.in_features <= 0 || l.out_features <= 0 || !l.weight ||
+          l.weight_len != (int64_t)l.in_features * l.out_features)
+        return fail(RG_ERR_INVALID_ARG, "layer %d: Embedding(%d, %d) needs a table [V, d]", idx, l.in_features,
+                    l.out_features);
+      return RG_OK;
+    case RG_LAYER_RMSNORM:
+      if (l.in_features <= 0 || !l.weight || l.weight_len != l.in_features)
+        return fail(RG_ERR_INVALID_ARG, "layer %d: RMSNorm(%d) needs a weight [d]", idx, l.in_features);
+      return RG_OK;
+    case RG_LAYER_ATTENTION:
+      if (l.in_features <= 0 || l.out_features <= 0 || l.in_features % l.out_features != 0 || !l.weight ||
+          !l.bias || l.weight_len != 4 * (int64_t)l.in_features * l.in_features || l.bias_len != 4 * (int64_t)l.in_features)
+        return fail(RG_ERR_INVALID_ARG,
+                    "layer %d: Attention(d=%d, heads=%d) needs heads | d, weight 4 x [d, d] and bias 4 x [d]", idx,
+                    l.in_features, l.out_features);
+      return RG_OK;
+    case RG_LAYER_SWIGLU:
+      if (l.in_features <= 0 || l.out_features <= 0 || !l.weight ||
+          l.weight_len != 3 * (int64_t)l.in_features * l.out_features)
+        return fail(RG_ERR_INVALID_ARG, "layer %d: SwiGLU(%d->%d) needs weight [d,h] [d,h] [h,d]", idx,
+                    l.in_features, l.out_features);
       return RG_OK;
     default:
       return fail(RG_ERR_INVALID_ARG, "layer %d: unknown layer tag %d", idx, l.kind);
@@ -369,6 +403,37 @@ static void quantize_weights(Op& op, const float* w_ref_layout, int64_t rows, in
   }
 }
 
+// Linears that read the same input, each weight [in, out_each] row-major with its own
+// per-tensor scale (Linear::new / Linear::no_bias on the INT8 path, a-7/a-9 semantics),
+// quantized into one fused Op whose output columns hold the parts side by side: the
+// parts' scales become per-column scales.  Byte accounting per part as for a Linear.
+static rg_status fuse_linears(Session& s, int32_t in, int32_t out_each, const std::vector<const float*>& ws,
+                              const std::vector<const float*>& bs, Op& op) {
+  const int64_t parts = (int64_t)ws.size(), n = out_each * parts;
+  op.kind = RG_LAYER_LINEAR; op.in_f = in; op.out_f = (int32_t)n; op.act = RG_ACT_NONE;
+  op.kdim = in; op.kpad = round_up(in, 16);
+  op.wq.assign((size_t)(n * in), 0);
+  op.bias.assign((size_t)n, 0.0f);
+  if (parts > 1) op.w_scale_ch.assign((size_t)n, 0.0f);
+  std::vector<float> wt((size_t)in * out_each);
+  for (int64_t j = 0; j < parts; ++j) {
+    const float* w = ws[(size_t)j];
+    for (int64_t r = 0; r < in; ++r)  // transpose2d [in,out] -> [out,in] (npu.rs:208)
+      for (int64_t c = 0; c < out_each; ++c) wt[(size_t)(c * in + r)] = w[r * out_each + c];
+    const float sc = quantize_host(wt.data(), (int64_t)in * out_each, op.wq.data() + j * out_each * in);
+    if (parts > 1) {
+      for (int64_t c = 0; c < out_each; ++c) op.w_scale_ch[(size_t)(j * out_each + c)] = sc;
+    } else {
+      op.w_scale = sc;
+    }
+    if (bs[(size_t)j]) memcpy(op.bias.data() + j * out_each, bs[(size_t)j], sizeof(float) * (size_t)out_each);
+    s.fp32_bytes += ((int64_t)in * out_each + (bs[(size_t)j] ? out_each : 0)) * 4;
+    s.npu_bytes += ((int64_t)in * out_each + 4) + (bs[(size_t)j] ? (int64_t)out_each * 4 : 0);
+  }
+  op.label = make_label(op);
+  return upload_op(op);
+}
+
 // npu::compile (npu.rs:188-276).
 static rg_status compile(Session& s, const rg_layer_spec* layers, int32_t n) {
   for (int32_t i = 0; i < n; ++i) RG_TRY(validate_layer(layers[i], i));
@@ -425,6 +490,27 @@ static rg_status compile(Session& s, const rg_layer_spec* layers, int32_t n) {
       op.kdim = c; op.kpad = round_up(c, 16);
       op.bias = l.b;
       op.act = RG_ACT_NONE;
+    } else if (l.kind == RG_LAYER_ATTENTION) {
+      const int32_t d = l.in_f;
+      op.kind = l.kind; op.in_f = d; op.out_f = l.out_f;  // out_f = heads
+      const int64_t dd = (int64_t)d * d;
+      op.subs.resize(2);
+      RG_TRY(fuse_linears(s, d, d, {l.w.data(), l.w.data() + dd, l.w.data() + 2 * dd},
+                          {l.b.data(), l.b.data() + d, l.b.data() + 2 * d}, op.subs[0]));
+      RG_TRY(fuse_linears(s, d, d, {l.w.data() + 3 * dd}, {l.b.data() + 3 * d}, op.subs[1]));
+    } else if (l.kind == RG_LAYER_SWIGLU) {
+      const int32_t d = l.in_f, hd = l.out_f;
+      op.kind = l.kind; op.in_f = d; op.out_f = hd;
+      const int64_t dh = (int64_t)d * hd;
+      op.subs.resize(2);
+      RG_TRY(fuse_linears(s, d, hd, {l.w.data(), l.w.data() + dh}, {nullptr, nullptr}, op.subs[0]));
+      RG_TRY(fuse_linears(s, hd, d, {l.w.data() + 2 * dh}, {nullptr}, op.subs[1]));
+    } else if (l.kind == RG_LAYER_EMBEDDING || l.kind == RG_LAYER_RMSNORM) {
+      op.kind = l.kind; op.in_f = l.in_f; op.out_f = l.out_f; op.param = l.param;
+      RG_TRY(op.d_ext.ensure(l.w.size() * sizeof(float)));
+      RG_CUDA_TRY(cudaMemcpy(op.d_ext.p, l.w.data(), l.w.size() * sizeof(float), cudaMemcpyHostToDevice));
+      s.fp32_bytes += (int64_t)l.w.size() * 4;  // kept in f32 on both paths
+      s.npu_bytes += (int64_t)l.w.size() * 4;
     } else {
       op.kind = l.kind; op.k = l.k; op.stride = l.stride; op.act = l.act; op.param = l.param;
     }
@@ -529,6 +615,22 @@ static rg_status plan_shapes(const Session& s, const int64_t* shape, int32_t ndi
           return fail(RG_ERR_SHAPE, "op %zu (%s): expected a non-empty [N,C,H,W] input", i, op.label.c_str());
         sh = {sh[0], sh[1], op.k, op.stride};
         break;
+      case RG_LAYER_EMBEDDING:
+        if (sh.size() >= 8) return fail(RG_ERR_SHAPE, "op %zu (%s): input rank too high", i, op.label.c_str());
+        sh.push_back(op.out_f);
+        break;
+      case RG_LAYER_RMSNORM:
+      case RG_LAYER_SWIGLU:
+        if (sh.back() != op.in_f)
+          return fail(RG_ERR_SHAPE, "op %zu (%s): last dim %lld != %d", i, op.label.c_str(), (long long)sh.back(),
+                      op.in_f);
+        if (op.kind == RG_LAYER_SWIGLU) os.macs = 3ull * (uint64_t)(os.in_elems / op.in_f) * op.in_f * op.out_f;
+        break;
+      case RG_LAYER_ATTENTION:
+        if (sh.size() != 3 || sh[2] != op.in_f)
+          return fail(RG_ERR_SHAPE, "op %zu (%s): expected a [B, T, %d] input", i, op.label.c_str(), op.in_f);
+        os.macs = 4ull * (uint64_t)sh[0] * sh[1] * op.in_f * op.in_f;  // the INT8 projections
+        break;
       default:
         break;
     }
@@ -611,9 +713,10 @@ static rg_status make_plan(const Session& s, const int64_t* shape, int32_t ndim,
   for (size_t i = 0; i < n; ++i) {
     const Op& op = s.ops[i];
     const bool conv_like = op.kind == RG_LAYER_CONV2D || op.kind == RG_LAYER_SHORTCUT_CONV2D;
-    if (op.kind != RG_LAYER_LINEAR && !conv_like) continue;
+    const bool inner = op.kind == RG_LAYER_ATTENTION || op.kind == RG_LAYER_SWIGLU;  // two Linears in a row
+    if (op.kind != RG_LAYER_LINEAR && !conv_like && !inner) continue;
     const OpShape& os = P.shapes[i];
-    P.amax_slots[i] = op.kind == RG_LAYER_LINEAR ? 1 : os.in[0];
+    P.amax_slots[i] = op.kind == RG_LAYER_LINEAR ? 1 : inner ? 2 : os.in[0];
     P.amax_off[i] = off;
     off += std::max<int64_t>(P.amax_slots[i], 1);
     bool full = true;
@@ -633,7 +736,8 @@ static rg_status make_plan(const Session& s, const int64_t* shape, int32_t ndim,
     if (pk == RG_LAYER_SOFTMAX && op.kind == RG_LAYER_CONV2D) continue;
     if (pk == RG_LAYER_LINEAR || pk == RG_LAYER_CONV2D || pk == RG_LAYER_MAXPOOL2D ||
         pk == RG_LAYER_ACTIVATION || pk == RG_LAYER_SOFTMAX || pk == RG_LAYER_RESIDUAL_END ||
-        pk == RG_LAYER_ADAPTIVE_AVGPOOL2D)
+        pk == RG_LAYER_ADAPTIVE_AVGPOOL2D || pk == RG_LAYER_EMBEDDING || pk == RG_LAYER_RMSNORM ||
+        pk == RG_LAYER_ATTENTION || pk == RG_LAYER_SWIGLU)
       P.amax_src[i] = j;
   }
   P.total_slots = off;
@@ -650,7 +754,9 @@ static int find_consumer(const Session& s, size_t j) {
   if (s.ops[j].kind == RG_LAYER_SHORTCUT_CONV2D) return -1;  // its output feeds the residual add
   for (size_t i = j + 1; i < s.ops.size(); ++i) {
     if (main_path_noop(s.ops[i].kind)) continue;
-    if (s.ops[i].kind == RG_LAYER_LINEAR || s.ops[i].kind == RG_LAYER_CONV2D) return (int)i;
+    const int32_t k = s.ops[i].kind;
+    if (k == RG_LAYER_LINEAR || k == RG_LAYER_CONV2D || k == RG_LAYER_ATTENTION || k == RG_LAYER_SWIGLU)
+      return (int)i;
     return -1;
   }
   return -1;
@@ -679,13 +785,49 @@ static bool feed_chunked(const Session& s, const RunPlan& P) {
   return !s.ops.empty() && P.block_start[0] && !s.trace && P.shapes[0].in[0] >= 2 * kFeedMinChunk;
 }
 
+// One INT8 Linear inside an extension op: the f32 input quantized with the per-tensor
+// scale of absmax *am (first taken as the max over all ranks), then the GEMM; out is
+// [rows, lin.out_f] f32, its absmax optionally sent to `sink`.
+static rg_status run_inner_linear(Session& s, const Op& lin, const float* src, int64_t rows, unsigned* am,
+                                  float* sc, float* out, AmaxSink sink, cudaStream_t st, int32_t& launches) {
+  if (s.comm && s.world > 1) RG_NCCL_TRY(ncclAllReduce(am, am, 1, ncclUint32, ncclMax, s.comm, st));
+  int8_t* q = s.qbuf.as<int8_t>();
+  launch_quantize_rows(src, rows, lin.in_f, lin.kpad, am, q, sc, st);
+  ++launches;
+  RG_LAUNCHED("quantize_rows");
+  GemmArgs g;
+  g.a = q; g.lda = lin.kpad;
+  g.m = rows; g.n = lin.out_f; g.k = lin.kpad;
+  g.w = lin.d_w.as<int8_t>(); g.ldb = lin.kpad;
+  g.a_scale = sc;
+  g.w_scale = lin.w_scale;
+  g.w_scale_ch = lin.w_scale_ch.empty() ? nullptr : lin.d_wsc.as<float>();
+  g.bias = lin.d_bias.as<float>();
+  g.act = RG_ACT_NONE;
+  g.out = out;
+  g.amax = sink;
+  const bool tc = gemm_tc_eligible(g);
+  const bool narrow = !tc && gemm_narrow_eligible(g);
+  if (tc) {
+    if (!launch_gemm_tc(g, s.num_sms, st)) return fail(RG_ERR_CUDA, "%s: TMA descriptor encoding failed", lin.label.c_str());
+    s.used_tc = true;
+  } else if (narrow) {
+    launch_gemm_narrow(g, st);
+  } else {
+    launch_gemm_simt(g, st);
+  }
+  ++launches;
+  RG_LAUNCHED(tc ? "gemm_tc" : narrow ? "gemm_narrow" : "gemm_simt");
+  return RG_OK;
+}
+
 // Runs the program on device buffers. x_dev is read only (with a HostFeed it is
 // the staging buffer the feed fills); the output is left in y_dev or one of the
 // session's activation buffers.
 static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float* y_dev, cudaStream_t st,
                          bool record_events, const HostFeed& feed = HostFeed()) {
   const size_t n = s.ops.size();
-  int64_t max_elems = 1, max_q = 16;
+  int64_t max_elems = 1, max_q = 16, max_ext0 = 0, max_ext1 = 0;
   for (size_t i = 0; i < n; ++i) {
     max_elems = std::max(max_elems, P.shapes[i].out_elems);
     const Op& op = s.ops[i];
@@ -694,6 +836,16 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
       const std::vector<int64_t>& in = P.shapes[i].in;  // NHWC with channels padded to cpad
       max_q = std::max(max_q, in[0] * in[2] * in[3] * op.cpad);
     }
+    if (op.kind == RG_LAYER_ATTENTION || op.kind == RG_LAYER_SWIGLU) {
+      const int64_t rows = P.shapes[i].in_elems / op.in_f;
+      for (const Op& l : op.subs) max_q = std::max(max_q, rows * l.kpad);
+      max_ext0 = std::max(max_ext0, rows * op.subs[0].out_f);
+      max_ext1 = std::max(max_ext1, rows * op.subs[1].in_f);
+    }
+  }
+  if (max_ext0) {
+    RG_TRY(s.ext0.ensure((size_t)max_ext0 * 4));
+    RG_TRY(s.ext1.ensure((size_t)max_ext1 * 4));
   }
   bool residual = false;
   for (size_t i = 0; i < n; ++i) residual = residual || s.ops[i].kind == RG_LAYER_RESIDUAL_BEGIN;
@@ -980,6 +1132,47 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         const int64_t lastd = os.in.back();
         launch_softmax(cur, lastd ? os.in_elems / lastd : 0, lastd, dst, sink, st);
         ++launches;
+        cur = dst;
+        break;
+      }
+      case RG_LAYER_EMBEDDING:
+        launch_embedding(cur, os.in_elems, op.d_ext.as<float>(), op.in_f, op.out_f, dst, sink, st);
+        ++launches;
+        RG_LAUNCHED("embedding");
+        s.used_embed = true;
+        cur = dst;
+        break;
+      case RG_LAYER_RMSNORM:
+        // mean_dim multiplies the sum by 1/d (tensor/ops.rs:755-758)
+        launch_rmsnorm(cur, os.in_elems / op.in_f, op.in_f, op.d_ext.as<float>(), op.param, 1.0f / (float)op.in_f,
+                       dst, sink, st);
+        ++launches;
+        RG_LAUNCHED("rmsnorm");
+        cur = dst;
+        break;
+      case RG_LAYER_ATTENTION:
+      case RG_LAYER_SWIGLU: {
+        unsigned* am = amax + P.amax_off[i];  // [0]: the op's input, [1]: the inner activation
+        float* sc = scales + P.amax_off[i];
+        const int64_t rows = os.in_elems / op.in_f;
+        if (P.amax_src[i] < 0) { launch_absmax(cur, os.in_elems, am, st); ++launches; RG_LAUNCHED("absmax"); }
+        AmaxSink inner;
+        inner.ptr = am + 1;
+        float* e0 = s.ext0.as<float>();
+        float* e1 = s.ext1.as<float>();
+        RG_TRY(run_inner_linear(s, op.subs[0], cur, rows, am, sc, e0, AmaxSink(), st, launches));
+        if (op.kind == RG_LAYER_ATTENTION) {
+          const int32_t d = op.in_f, heads = op.out_f, dh = d / heads;
+          const float scale = 1.0f / std::sqrt((float)dh);  // attention.rs: mul_scalar(1 / sqrt(dh))
+          RG_TRY(launch_attention(e0, 3 * (int64_t)d, os.in[0], (int32_t)os.in[1], heads, dh, scale, e1, d, inner, st));
+          ++launches;
+          RG_LAUNCHED("attention");
+        } else {
+          launch_swiglu_mul(e0, rows, op.out_f, e1, inner, st);
+          ++launches;
+          RG_LAUNCHED("swiglu_mul");
+        }
+        RG_TRY(run_inner_linear(s, op.subs[1], e1, rows, am + 1, sc + 1, dst, sink, st, launches));
         cur = dst;
         break;
       }
@@ -1291,6 +1484,11 @@ static rg_status run_impl(rg_session* h, const float* x, bool x_host, const int6
     s.used_tc = false;
     if (gemm_tc_take_error() != 0 || convblock_take_error() != 0 || conv_tc_take_error() != 0)
       return fail(RG_ERR_TIMEOUT, "a tensor-core kernel gave up on a bounded wait; results are invalid");
+  }
+  if (s.used_embed) {
+    s.used_embed = false;
+    if (embedding_take_error() != 0)
+      return fail(RG_ERR_INVALID_ARG, "Embedding: a token id is not below the vocabulary size");
   }
   int64_t total_ns = 0;
   if (events) {

@@ -127,6 +127,20 @@ void launch_activation(const float* x, int64_t n, int32_t act, float p, float* y
                        cudaStream_t st);
 void launch_softmax(const float* x, int64_t outer, int64_t last, float* y, AmaxSink amax,
                     cudaStream_t st);
+// Transformer extension (k_transformer.cu).  Token ids are f32 values; an id >= v sets
+// a device error word (embedding_take_error reads and clears it, synchronously).
+void launch_embedding(const float* ids, int64_t n, const float* table, int64_t v, int32_t d, float* y,
+                      AmaxSink amax, cudaStream_t st);
+int embedding_take_error();
+void launch_rmsnorm(const float* x, int64_t rows, int32_t d, const float* w, float eps, float inv_d, float* y,
+                    AmaxSink amax, cudaStream_t st);
+// gu [rows, 2h] = [g | u] -> y [rows, h] = (g * sigmoid(g)) * u
+void launch_swiglu_mul(const float* gu, int64_t rows, int32_t h, float* y, AmaxSink amax, cudaStream_t st);
+// qkv [b*t, ld] (q, k, v of head hh at columns hh*dh, d + hh*dh, 2d + hh*dh) ->
+// out [b*t, ldo] with the heads merged; scores scaled by `scale` before the softmax.
+rg_status launch_attention(const float* qkv, int64_t ld, int64_t b, int32_t t, int32_t heads, int32_t dh,
+                           float scale, float* out, int64_t ldo, AmaxSink amax, cudaStream_t st);
+bool attention_fast_eligible(int32_t t, int32_t dh, const float* qkv, int64_t ld, const float* out, int64_t ldo);
 void launch_fill_u32(unsigned* p, unsigned v, int64_t n, cudaStream_t st);
 void launch_bits_to_float(const unsigned* bits, float* out, int64_t n, cudaStream_t st);
 

@@ -14,6 +14,8 @@ from . import rng
 from .spec import Activation, ActivationLayer, ChannelAffine, Conv2d as Conv2dSpec, Flatten as FlattenSpec
 from .spec import Linear as LinearSpec, MaxPool2d as MaxPool2dSpec, Softmax as SoftmaxSpec
 from .spec import AdaptiveAvgPool2d as AdaptiveAvgPool2dSpec, ResidualBegin, ResidualEnd, ShortcutConv2d
+from .spec import Attention as AttentionSpec, Embedding as EmbeddingSpec, RMSNorm as RMSNormSpec
+from .spec import SwiGLU as SwiGLUSpec
 
 
 class Module:
@@ -237,6 +239,79 @@ class BasicBlock(Module):
                                    c.bias)] + self.proj_bn.export()
         out += [ResidualEnd(Activation.RELU)]
         return out
+
+
+class Embedding(Module):
+    """Embedding::new (nn/layers.rs:430-433) draws the table ~ std * N(0,1) (std 0.1;
+    configurations may pass their own std or table)."""
+
+    def __init__(self, num_embeddings: int, dim: int, weight=None, std: float = 0.1):
+        self.num_embeddings, self.dim = num_embeddings, dim
+        self.weight = (np.asarray(weight, np.float32).reshape(num_embeddings, dim) if weight is not None
+                       else rng.normal_init((num_embeddings, dim), std))
+
+    def export(self):
+        return [EmbeddingSpec(self.num_embeddings, self.dim, self.weight)]
+
+
+class RMSNorm(Module):
+    """RMSNorm::new (nn/norm.rs:396-403): weight ones, eps 1e-6 (no draws)."""
+
+    def __init__(self, dim: int, eps: float = 1e-6):
+        self.dim, self.eps = dim, eps
+        self.weight = np.ones(dim, np.float32)
+
+    def export(self):
+        return [RMSNormSpec(self.dim, self.weight, self.eps)]
+
+
+class MultiHeadAttention(Module):
+    """MultiHeadAttention::new (nn/attention.rs:130-143), non-causal, no RoPE:
+    Linear::new for wq, wk, wv, wo in that order."""
+
+    def __init__(self, d_model: int, heads: int):
+        if d_model <= 0 or heads <= 0 or d_model % heads:
+            raise ValueError("d_model must be a positive multiple of heads")
+        self.d_model, self.heads = d_model, heads
+        self.wq, self.wk = Linear(d_model, d_model), Linear(d_model, d_model)
+        self.wv, self.wo = Linear(d_model, d_model), Linear(d_model, d_model)
+
+    def export(self):
+        return [AttentionSpec(self.d_model, self.heads, self.wq.weight, self.wq.bias, self.wk.weight, self.wk.bias,
+                              self.wv.weight, self.wv.bias, self.wo.weight, self.wo.bias)]
+
+
+class SwiGLU(Module):
+    """SwiGLU::new (nn/layers.rs:492-497): Linear::no_bias gate, up, down (each still
+    draws its dropped bias)."""
+
+    def __init__(self, in_features: int, hidden_features: int, out_features: int | None = None):
+        out_features = in_features if out_features is None else out_features
+        if out_features != in_features:
+            raise ValueError("the SwiGLU op keeps the model width (out_features == in_features)")
+        self.in_features, self.hidden_features = in_features, hidden_features
+        self.gate = Linear.no_bias(in_features, hidden_features)
+        self.up = Linear.no_bias(in_features, hidden_features)
+        self.down = Linear.no_bias(hidden_features, in_features)
+
+    def export(self):
+        return [SwiGLUSpec(self.in_features, self.hidden_features, self.gate.weight, self.up.weight,
+                           self.down.weight)]
+
+
+class PreNormEncoderLayer(Module):
+    """x += Attention(RMSNorm(x)); x += SwiGLU(RMSNorm(x)) (extension export; built in
+    the order norm1, attention, norm2, SwiGLU)."""
+
+    def __init__(self, d_model: int, heads: int, hidden: int):
+        self.norm1 = RMSNorm(d_model)
+        self.attn = MultiHeadAttention(d_model, heads)
+        self.norm2 = RMSNorm(d_model)
+        self.ffn = SwiGLU(d_model, hidden)
+
+    def export(self):
+        return ([ResidualBegin()] + self.norm1.export() + self.attn.export() + [ResidualEnd(Activation.NONE)] +
+                [ResidualBegin()] + self.norm2.export() + self.ffn.export() + [ResidualEnd(Activation.NONE)])
 
 
 def draw_bn_stats(model: Module, mean_range=(-0.1, 0.1), var_range=(0.5, 1.5)) -> None:

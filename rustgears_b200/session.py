@@ -16,8 +16,8 @@ from dataclasses import dataclass, field
 import numpy as np
 
 from . import _native
-from .spec import (ACTIVATION, ADAPTIVE_AVGPOOL2D, CHANNEL_AFFINE, CONV2D, LINEAR, RESIDUAL_END, SHORTCUT_CONV2D,
-                   Activation)
+from .spec import (ACTIVATION, ADAPTIVE_AVGPOOL2D, ATTENTION, CHANNEL_AFFINE, CONV2D, EMBEDDING, LINEAR,
+                   RESIDUAL_END, RMSNORM, SHORTCUT_CONV2D, SWIGLU, Activation, as_dict)
 
 _MAX_RANK = 8
 
@@ -146,6 +146,11 @@ def _layer_structs(layers):
             w, b = l.weight, l.bias
         elif l.kind == CHANNEL_AFFINE:
             w, b = l.scale, l.shift
+        elif l.kind in (EMBEDDING, RMSNORM, ATTENTION, SWIGLU):
+            d = as_dict(l)
+            s.in_features, s.out_features = d["in_features"], d.get("out_features", 0)
+            s.act_param = d.get("act_param", 0.0)
+            w, b = d["weight"], d.get("bias", np.zeros(0, np.float32))
         else:
             w = b = None
             if hasattr(l, "kernel"):

@@ -9,6 +9,8 @@ import numpy as np
 LINEAR, CONV2D, CHANNEL_AFFINE, MAXPOOL2D, FLATTEN, ACTIVATION, SOFTMAX = 1, 2, 3, 4, 5, 6, 7
 # extensions (no reference LayerSpec): residual blocks, adaptive average pooling
 RESIDUAL_BEGIN, RESIDUAL_END, SHORTCUT_CONV2D, ADAPTIVE_AVGPOOL2D = 8, 9, 10, 11
+# extensions for transformer encoders: token embedding, RMSNorm, multi-head attention, SwiGLU
+EMBEDDING, RMSNORM, ATTENTION, SWIGLU = 12, 13, 14, 15
 
 
 def _fmt_f32(v: float) -> str:
@@ -162,6 +164,80 @@ class AdaptiveAvgPool2d:
     kind: int = field(default=ADAPTIVE_AVGPOOL2D, init=False)
 
 
+# --- extensions: transformer encoder ops (f32 outside the INT8 Linears) -----------
+@dataclass
+class Embedding:
+    """Embedding::forward (nn/layers.rs:438-446): token ids (f32 values) -> table rows."""
+    vocab: int
+    dim: int
+    table: np.ndarray  # [vocab, dim]
+    kind: int = field(default=EMBEDDING, init=False)
+
+    def __post_init__(self):
+        self.table = _f32(self.table)
+
+
+@dataclass
+class RMSNorm:
+    """RMSNorm::forward (nn/norm.rs:413-417): x / sqrt(mean(x^2) + eps) * weight."""
+    dim: int
+    weight: np.ndarray
+    eps: float = 1e-6
+    kind: int = field(default=RMSNORM, init=False)
+
+    def __post_init__(self):
+        self.weight = _f32(self.weight)
+        self.eps = float(np.float32(self.eps))
+
+
+@dataclass
+class Attention:
+    """Non-causal multi-head attention (nn/attention.rs:162-196) whose q, k, v and o
+    projections (each Linear::new, weight [d, d], bias [d]) run on the INT8 path."""
+    dim: int
+    heads: int
+    wq: np.ndarray
+    bq: np.ndarray
+    wk: np.ndarray
+    bk: np.ndarray
+    wv: np.ndarray
+    bv: np.ndarray
+    wo: np.ndarray
+    bo: np.ndarray
+    kind: int = field(default=ATTENTION, init=False)
+
+    def __post_init__(self):
+        for n in ("wq", "bq", "wk", "bk", "wv", "bv", "wo", "bo"):
+            setattr(self, n, _f32(getattr(self, n)))
+
+    @property
+    def weight(self) -> np.ndarray:
+        return np.concatenate([self.wq, self.wk, self.wv, self.wo])
+
+    @property
+    def bias(self) -> np.ndarray:
+        return np.concatenate([self.bq, self.bk, self.bv, self.bo])
+
+
+@dataclass
+class SwiGLU:
+    """SwiGLU (nn/layers.rs:507-513): down((g * sigmoid(g)) * u) with bias-free INT8
+    Linears gate, up [dim, hidden] and down [hidden, dim]."""
+    dim: int
+    hidden: int
+    w_gate: np.ndarray
+    w_up: np.ndarray
+    w_down: np.ndarray
+    kind: int = field(default=SWIGLU, init=False)
+
+    def __post_init__(self):
+        self.w_gate, self.w_up, self.w_down = _f32(self.w_gate), _f32(self.w_up), _f32(self.w_down)
+
+    @property
+    def weight(self) -> np.ndarray:
+        return np.concatenate([self.w_gate, self.w_up, self.w_down])
+
+
 class LayerSpec:
     """Namespace mirroring the Rust enum: ``LayerSpec.Linear(...)`` etc."""
 
@@ -177,6 +253,10 @@ class LayerSpec:
     ShortcutConv2d = ShortcutConv2d
     ResidualEnd = ResidualEnd
     AdaptiveAvgPool2d = AdaptiveAvgPool2d
+    Embedding = Embedding
+    RMSNorm = RMSNorm
+    Attention = Attention
+    SwiGLU = SwiGLU
 
 
 def as_dict(spec) -> dict:
@@ -200,4 +280,12 @@ def as_dict(spec) -> dict:
         d.update(act=spec.act.code, act_param=spec.act.param)
     elif spec.kind == ADAPTIVE_AVGPOOL2D:
         d.update(kernel=spec.out_h, stride=spec.out_w)
+    elif spec.kind == EMBEDDING:
+        d.update(in_features=spec.vocab, out_features=spec.dim, weight=spec.table)
+    elif spec.kind == RMSNORM:
+        d.update(in_features=spec.dim, weight=spec.weight, act_param=spec.eps)
+    elif spec.kind == ATTENTION:
+        d.update(in_features=spec.dim, out_features=spec.heads, weight=spec.weight, bias=spec.bias)
+    elif spec.kind == SWIGLU:
+        d.update(in_features=spec.dim, out_features=spec.hidden, weight=spec.weight)
     return d

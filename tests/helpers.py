@@ -44,6 +44,19 @@ def spec_from_dict(d):
         return S.ResidualEnd(S.Activation(d.get("act", 0), d.get("act_param", 0.0)))
     if k == S.ADAPTIVE_AVGPOOL2D:
         return S.AdaptiveAvgPool2d(d["kernel"], d["stride"])
+    if k == S.EMBEDDING:
+        return S.Embedding(d["in_features"], d["out_features"], d["weight"])
+    if k == S.RMSNORM:
+        return S.RMSNorm(d["in_features"], d["weight"], d.get("act_param", 1e-6))
+    if k == S.ATTENTION:
+        dm = d["in_features"]
+        w = np.asarray(d["weight"], np.float32).reshape(4, dm * dm)
+        b = np.asarray(d["bias"], np.float32).reshape(4, dm)
+        return S.Attention(dm, d["out_features"], w[0], b[0], w[1], b[1], w[2], b[2], w[3], b[3])
+    if k == S.SWIGLU:
+        dm, h = d["in_features"], d["out_features"]
+        w = np.asarray(d["weight"], np.float32).ravel()
+        return S.SwiGLU(dm, h, w[:dm * h], w[dm * h:2 * dm * h], w[2 * dm * h:])
     raise ValueError(k)
 
 
