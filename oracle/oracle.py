@@ -328,10 +328,55 @@ class Program:
                 y = activation(data, op.act, op.act_param)
             elif op.kind == SOFTMAX:
                 y = softmax(data)
+            elif op.kind in (ATTENTION, SWIGLU):
+                y = self._inner_sharded(i, op, data, allreduce_max, nthreads)
             else:
                 y = self._extension_step(i, op, data, saved, nthreads)
             data = np.ascontiguousarray(y)
         return data
+
+    def _inner_sharded(self, i, op, data, allreduce_max, nthreads):
+        """Attention / SwiGLU on one batch shard: each inner Linear quantizes with the
+        max over all shards of its input's absmax (og_attention / og_swiglu composed
+        from the oracle's pieces with that scale)."""
+        raw = self._p.contents.ops[i]
+
+        def lin(j, v):
+            v = np.ascontiguousarray(v, np.float32)
+            sub = raw.sub[j]
+            rows = v.size // sub.in_features
+            a = np.abs(v.reshape(-1))
+            local = np.float32(np.nanmax(a)) if a.size and not np.isnan(a).all() else np.float32(0)
+            amax = np.float32(allreduce_max(max(local, np.float32(0))))
+            y = np.empty((rows, sub.out_features), np.float32)
+            lib().og_op_linear_with_amax(C.byref(sub), _p(v, C.c_float), rows, C.c_float(amax), _p(y, C.c_float),
+                                         nthreads)
+            return y
+        d = op.in_features
+        x2 = data.reshape(-1, d)
+        if op.kind == SWIGLU:
+            g, u = self._two(lin, x2)
+            m = (g * act_apply(2, 0.0, g)).astype(np.float32)
+            m = (m * u).astype(np.float32)
+            return lin(2, m).reshape(data.shape)
+        b, t, _ = data.shape
+        h = op.out_features
+        dh = d // h
+        q, k, v = (lin(j, x2).reshape(b, t, h, dh).transpose(0, 2, 1, 3).reshape(b * h, t, dh).copy()
+                   for j in range(3))
+        kt = np.ascontiguousarray(k.transpose(0, 2, 1))
+        sc = np.empty((b * h, t, t), np.float32)
+        lib().og_bmm_fma(_p(q, C.c_float), _p(kt, C.c_float), b * h, t, dh, t, _p(sc, C.c_float))
+        sc = (sc * (np.float32(1.0) / np.sqrt(np.float32(dh))).astype(np.float32)).astype(np.float32)
+        pm = np.ascontiguousarray(softmax(sc))
+        o = np.empty((b * h, t, dh), np.float32)
+        lib().og_bmm_fma(_p(pm, C.c_float), _p(v, C.c_float), b * h, t, t, dh, _p(o, C.c_float))
+        merged = o.reshape(b, h, t, dh).transpose(0, 2, 1, 3).reshape(b * t, d)
+        return lin(3, merged).reshape(data.shape)
+
+    @staticmethod
+    def _two(lin, x2):
+        return lin(0, x2), lin(1, x2)
 
     def _conv_on(self, i, op, data, nthreads):
         n, c, h, w = data.shape

@@ -89,61 +89,94 @@ __global__ void __launch_bounds__(kThreads) k_embedding(const float* __restrict_
 }
 
 // ---------------------------------------------------------------------------
-// RMSNorm: a warp owns 32 rows.  The rows are staged through shared memory in 32x32
-// tiles (coalesced loads) so that each lane can add its own row's squares serially.
+// RMSNorm: a block stages `rpb` whole rows in shared memory (coalesced 16-byte loads,
+// row pitch d + 1 so that the per-row readers hit distinct banks), one thread per row
+// adds the squares serially, then all threads normalise from shared memory.  Several
+// blocks per SM overlap one block's serial sums with the others' copies.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads) k_rmsnorm(const float* __restrict__ x, int64_t rows, int32_t d,
-                                                      const float* __restrict__ w, float eps, float inv_d,
-                                                      float* __restrict__ y, unsigned* amax) {
-  __shared__ float tile[kThreads / 32][32][33];
-  __shared__ float rms_s[kThreads / 32][32];
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int64_t r0 = ((int64_t)blockIdx.x * (kThreads / 32) + wid) * 32;
+                                                      int32_t rpb, bool vec, const float* __restrict__ w, float eps,
+                                                      float inv_d, float* __restrict__ y, unsigned* amax) {
+  extern __shared__ float xs[];  // [rpb][d + 1]
+  __shared__ float rms_s[32];
+  const int ld = d + 1;
   float m = 0.0f;
-  if (r0 < rows) {
-    const int nr = rows - r0 < 32 ? (int)(rows - r0) : 32;
-    float s = 0.0f;
-    for (int32_t c0 = 0; c0 < d; c0 += 32) {
-      const int nc = min(32, d - c0);
-#pragma unroll 8
-      for (int rr = 0; rr < 32; ++rr)
-        tile[wid][rr][lane] = (rr < nr && lane < nc) ? __ldg(x + (r0 + rr) * d + c0 + lane) : 0.0f;
-      __syncwarp();
-      for (int c = 0; c < nc; ++c) {
-        const float v = tile[wid][lane][c];
-        s = __fadd_rn(s, __fmul_rn(v, v));
-      }
-      __syncwarp();
+  for (int64_t r0 = (int64_t)blockIdx.x * rpb; r0 < rows; r0 += (int64_t)gridDim.x * rpb) {
+    const int nr = rows - r0 < rpb ? (int)(rows - r0) : rpb;
+    const float* src = x + r0 * d;
+    if (vec) {
+      const int d4 = d >> 2;
+#pragma unroll 4
+      for (int r = 0; r < nr; ++r)
+        for (int c4 = threadIdx.x; c4 < d4; c4 += kThreads) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(src + (int64_t)r * d) + c4);
+          float* dst = xs + r * ld + 4 * c4;
+          dst[0] = v.x; dst[1] = v.y; dst[2] = v.z; dst[3] = v.w;
+        }
+    } else {
+      for (int r = 0; r < nr; ++r)
+        for (int c = threadIdx.x; c < d; c += kThreads) xs[r * ld + c] = __ldg(src + (int64_t)r * d + c);
     }
-    rms_s[wid][lane] = __fsqrt_rn(__fadd_rn(__fmul_rn(s, inv_d), eps));
-    __syncwarp();
-    for (int rr = 0; rr < nr; ++rr) {
-      const float r = rms_s[wid][rr];
-      const float* xr = x + (r0 + rr) * d;
-      float* yr = y + (r0 + rr) * d;
-      for (int32_t c = lane; c < d; c += 32) {
-        const float v = __fmul_rn(__fdiv_rn(__ldg(xr + c), r), __ldg(w + c));
+    __syncthreads();
+    if ((int)threadIdx.x < nr) {  // serial sum of squares in column order
+      const float* row = xs + threadIdx.x * ld;
+      float s = 0.0f;
+#pragma unroll 8
+      for (int c = 0; c < d; ++c) s = __fadd_rn(s, __fmul_rn(row[c], row[c]));
+      rms_s[threadIdx.x] = __fsqrt_rn(__fadd_rn(__fmul_rn(s, inv_d), eps));
+    }
+    __syncthreads();
+    for (int r = 0; r < nr; ++r) {
+      const float rr = rms_s[r];
+      float* yr = y + (r0 + r) * d;
+      for (int c = threadIdx.x; c < d; c += kThreads) {
+        const float v = __fmul_rn(__fdiv_rn(xs[r * ld + c], rr), __ldg(w + c));
         yr[c] = v;
         m = fmaxf(m, fabsf(v));
       }
     }
+    __syncthreads();
   }
   if (amax) block_max_to(m, amax);
 }
 
 // ---------------------------------------------------------------------------
-// SwiGLU gate product: gu [rows, 2h] holds g in columns [0, h) and u in [h, 2h).
+// SwiGLU gate product: gu [rows, 2h] holds g in columns [0, h) and u in [h, 2h); one
+// block per row.  sigmoid(g) = 1 / (1 + exp(-g)) (device/backend.rs:72) with the exp
+// table in shared memory (the lanes of a warp index different entries).
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ float swiglu1(float g, float u, ExpTablePtr et) {
+  const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_f32_with(-g, et)));
+  return __fmul_rn(__fmul_rn(g, sig), u);
+}
+
 __global__ void __launch_bounds__(kThreads) k_swiglu_mul(const float* __restrict__ gu, int64_t rows, int32_t h,
-                                                         float* __restrict__ y, unsigned* amax) {
-  const int64_t n = rows * h;
+                                                         bool vec, float* __restrict__ y, unsigned* amax) {
+  __shared__ uint64_t tab[32];
+  if (threadIdx.x < 32) tab[threadIdx.x] = ExpTableConst{}(threadIdx.x);
+  __syncthreads();
+  const ExpTablePtr et{tab};
   float m = 0.0f;
-  for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += (int64_t)gridDim.x * kThreads) {
-    const int64_t r = i / h, c = i - r * h;
-    const float g = __ldg(gu + r * 2 * h + c), u = __ldg(gu + r * 2 * h + h + c);
-    const float v = __fmul_rn(__fmul_rn(g, act_apply(ACT_SIGMOID, 0.0f, g)), u);
-    y[i] = v;
-    m = fmaxf(m, fabsf(v));
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float* gr = gu + r * 2 * h;
+    const float* ur = gr + h;
+    float* yr = y + r * h;
+    if (vec) {  // h % 4 == 0 and gu, y 16-byte aligned
+      for (int32_t c = threadIdx.x; c < (h >> 2); c += kThreads) {
+        const float4 g = __ldg(reinterpret_cast<const float4*>(gr) + c);
+        const float4 u = __ldg(reinterpret_cast<const float4*>(ur) + c);
+        const float4 v = make_float4(swiglu1(g.x, u.x, et), swiglu1(g.y, u.y, et), swiglu1(g.z, u.z, et),
+                                     swiglu1(g.w, u.w, et));
+        reinterpret_cast<float4*>(yr)[c] = v;
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      }
+    } else {
+      for (int32_t c = threadIdx.x; c < h; c += kThreads) {
+        const float v = swiglu1(__ldg(gr + c), __ldg(ur + c), et);
+        yr[c] = v;
+        m = fmaxf(m, fabsf(v));
+      }
+    }
   }
   if (amax) block_max_to(m, amax);
 }
@@ -211,213 +244,305 @@ __global__ void __launch_bounds__(128) k_attention_row(const float* __restrict__
 
 // ---------------------------------------------------------------------------
 // Attention for head size 64 and t % 8 == 0, t <= kMaxT (every score column an FMA
-// chain).  One CTA per (64 queries, batch*head), 8 warps:
-//  phase 1  S = Q K^T for 128-key chunks: warp w owns queries 8w..8w+7, lane l keys
-//           4l..4l+3 of the chunk, 32 FMA chains over the 64 dims;
-//  softmax  per query row over all t scores in shared memory;
-//  phase 2  O = P V for 128-key chunks: warp w owns queries 8w..8w+7, lane (qh, eg)
-//           queries 4qh..4qh+3 x dims 4eg..4eg+3, FMA chains over the keys in order.
-// K and V chunks stream through a double buffer with cp.async (K transposed by 4-byte
-// copies), so the next chunk lands while the current one is used and V's first chunk
-// lands during the softmax.  Shared-memory layouts (floats):
-//  Qs [64 dims][64 queries], KV[2][128 x 64] (K^T [64 dims][128 keys] or V [128][64]),
-//  S [t][64 queries]; Q, K^T and S rows swizzle their 16-byte groups (XOR of the group
-//  index with the dim (Q, K) or key/4 (S)) to keep the transposing stores and the
-//  row reads conflict-free.
+// chain).  One CTA per (32 queries, batch*head), 8 warps, two CTAs per SM (one CTA's
+// softmax overlaps the other's FMA phases):
+//  phase 1  S = Q K^T over 128-key chunks: warp (wq, wk) owns queries 16wq..16wq+15 x
+//           keys 32wk..32wk+31 of the chunk, lane (qg, kg) 4 queries x 4 keys; FMA
+//           chains over the 64 dims; the row maxima are kept on the way;
+//  softmax  exp(s - max) in parallel, the serial sum per row, the division;
+//  phase 2  O = P V over 64-key chunks: warp (wq, we) owns queries 16wq.. x dims
+//           16we..16we+15, lane (qg, eg) 4 queries x 2 dims; FMA chains over the keys
+//           in order.
+// The FMAs are paired (f32x2: each lane rounded once, exactly as fmaf).  The operand
+// that a pair multiplies twice is stored twice in shared memory (Q in phase 1, V in
+// phase 2), so every pair comes straight from a 16-byte load, and within a warp the
+// lanes share their loads four or eight ways (one wavefront each).  K chunks are
+// transposed by 4-byte cp.async copies.  Shared memory (floats): Qd [64 dims][32
+// queries x 2] (after phase 1: row maxima, sums, the exp table), KV 8192 (K^T [64
+// dims][128 keys], or Vd [64 keys][64 dims x 2]), S [t][32 queries].  Q, K^T and S
+// rows swizzle their 16-byte groups: XOR of the group index with dim & 7 (Q, K^T) or
+// (key / 4) & 7 (S).
 // ---------------------------------------------------------------------------
-constexpr int kAQ = 64, kAK = 128, kADh = 64, kAThreads = 256, kMaxT = 512;
-constexpr int kAQsFloats = kADh * kAQ;     // 4096
-constexpr int kAChunkFloats = kAK * kADh;  // 8192
+constexpr int kAQ = 32, kAK = 128, kAV = 64, kADh = 64, kAThreads = 256, kMaxT = 512;
+constexpr int kAQdFloats = kADh * kAQ * 2;  // 4096
+constexpr int kAChunkFloats = 8192;         // K^T chunk (64 x 128) or Vd chunk (64 x 128)
 
 __device__ __forceinline__ void cp_async4(float* dst, const float* src, bool valid) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(sm100::smem_addr(dst)), "l"(src),
                "r"(valid ? 4 : 0)
                : "memory");
 }
-__device__ __forceinline__ void cp_async16(float* dst, const float* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sm100::smem_addr(dst)), "l"(src),
-               "r"(valid ? 16 : 0)
-               : "memory");
-}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-__global__ void __launch_bounds__(kAThreads, 1) k_attention64(const float* __restrict__ qkv, int64_t ld, int32_t t,
+// d.x = fma(a.x, b.x, c.x), d.y = fma(a.y, b.y, c.y), each rounded once as fmaf.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)),
+        "l"(*reinterpret_cast<uint64_t*>(&c)));
+  return *reinterpret_cast<float2*>(&d);
+}
+
+__global__ void __launch_bounds__(kAThreads, 2) k_attention64(const float* __restrict__ qkv, int64_t ld, int32_t t,
                                                              int32_t heads, float scale, float* __restrict__ out,
                                                              int64_t ldo, unsigned* amax) {
   extern __shared__ __align__(16) float sm[];
-  float* Qs = sm;
-  float* KV = sm + kAQsFloats;
-  float* S = KV + 2 * kAChunkFloats;
-  float* red = S + (size_t)t * kAQ;  // [4][64]
+  float* Qd = sm;
+  float* KV = sm + kAQdFloats;
+  float* S = KV + kAChunkFloats;
+  // after phase 1 the Qd region holds: [4 key quarters][32] maxima, [32] row max, [32] sum, table
+  float* wmax = Qd;
+  float* rowv = Qd + 4 * kAQ;
+  uint64_t* tab = reinterpret_cast<uint64_t*>(Qd + 6 * kAQ);
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int32_t q0 = blockIdx.x * kAQ;
   const int32_t g = blockIdx.y;
   const int32_t bi = g / heads, hh = g - bi * heads;
   const int32_t d = heads * kADh;
   const int64_t base = (int64_t)bi * t;
-  const float* qg = qkv + (int64_t)hh * kADh;
-  const float* kg = qkv + d + (int64_t)hh * kADh;
-  const float* vg = qkv + 2 * (int64_t)d + (int64_t)hh * kADh;
-  const int nk = (t + kAK - 1) / kAK;
+  const float* qsrc = qkv + (int64_t)hh * kADh;
+  const float* ksrc = qkv + d + (int64_t)hh * kADh;
+  const float* vsrc = qkv + 2 * (int64_t)d + (int64_t)hh * kADh;
+  const int nk = (t + kAK - 1) / kAK, nv = (t + kAV - 1) / kAV;
 
-  // 4-byte transposing copies: a warp covers 4 rows (queries or keys) x 8 dims, so the
-  // global reads are whole 32-byte sectors and the swizzled stores hit 32 banks.
-  auto load_q = [&]() {
+  // Q: each value twice, group (2 queries) index XOR dim & 7.  A warp covers 4 queries x
+  // 8 dims (whole 32-byte sectors).  idx bits: [2:0] dim low, [4:3] query low, [7:5]
+  // dim high, [10:8] query high.
 #pragma unroll 4
-    for (int it = 0; it < (kAQ * kADh) / kAThreads; ++it) {
-      const int idx = it * kAThreads + tid;
-      const int rsub = (idx >> 3) & 3, p = ((idx >> 5) & 7) * 8 + (idx & 7);
-      const int row = (idx >> 8) * 4 + rsub;  // 0..63
-      // idx bits: [2:0] dim low, [4:3] row low, [7:5] dim high, [11:8] row high
-      const int32_t qrow = q0 + row;
-      const bool ok = qrow < t;
-      const float* src = qg + (base + (ok ? qrow : 0)) * ld + p;
-      cp_async4(Qs + p * kAQ + ((((row >> 2) ^ (p & 7))) << 2) + (row & 3), src, ok);
-    }
-  };
-  auto load_k = [&](int c, float* buf) {
-    const int32_t k0 = c * kAK;
-#pragma unroll 4
-    for (int it = 0; it < kAChunkFloats / kAThreads; ++it) {
-      const int idx = it * kAThreads + tid;
-      const int rsub = (idx >> 3) & 3, p = ((idx >> 5) & 7) * 8 + (idx & 7);
-      const int key = (idx >> 8) * 4 + rsub;  // 0..127
-      const int32_t krow = k0 + key;
-      const bool ok = krow < t;
-      const float* src = kg + (base + (ok ? krow : 0)) * ld + p;
-      cp_async4(buf + p * kAK + ((((key >> 2) ^ (p & 7))) << 2) + (key & 3), src, ok);
-    }
-  };
-  auto load_v = [&](int c, float* buf) {
-    const int32_t k0 = c * kAK;
-#pragma unroll 4
-    for (int it = 0; it < kAChunkFloats / 4 / kAThreads; ++it) {
-      const int idx = it * kAThreads + tid;
-      const int key = idx >> 4, e4 = idx & 15;
-      const int32_t krow = k0 + key;
-      const bool ok = krow < t;
-      const float* src = vg + (base + (ok ? krow : 0)) * ld + e4 * 4;
-      cp_async16(buf + key * kADh + e4 * 4, src, ok);
-    }
-  };
-  auto issue = [&](int c) {  // chunk stream: K chunks 0..nk-1, then V chunks
-    float* buf = KV + (c & 1) * kAChunkFloats;
-    if (c < nk) load_k(c, buf);
-    else load_v(c - nk, buf);
-    cp_async_commit();
-  };
-
-  load_q();
-  issue(0);
-  float o[4][4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) o[i][e] = 0.0f;
-  const int qh = lane >> 4, eg = lane & 15;
-
-  for (int c = 0; c < 2 * nk; ++c) {
-    if (c + 1 < 2 * nk) {
-      issue(c + 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    const float* buf = KV + (c & 1) * kAChunkFloats;
+  for (int it = 0; it < (kAQ * kADh) / kAThreads; ++it) {
+    const int idx = it * kAThreads + tid;
+    const int p = ((idx >> 5) & 7) * 8 + (idx & 7);
+    const int q = (idx >> 8) * 4 + ((idx >> 3) & 3);  // 0..31
+    const bool ok = q0 + q < t;
+    const float* src = qsrc + (base + (ok ? q0 + q : 0)) * ld + p;
+    float* dst = Qd + p * (2 * kAQ) + ((((q >> 1) ^ (p & 7))) << 2) + 2 * (q & 1);
+    cp_async4(dst, src, ok);
+    cp_async4(dst + 1, src, ok);
+  }
+  // K and V chunks are fetched into registers one chunk ahead (global loads in flight
+  // while the current chunk is used) and written to shared memory between chunks.
+  // K: a warp covers 4 keys x 8 dims per step (whole 32-byte sectors; the transposing
+  // stores hit 32 banks); V: 16-byte loads, each value stored twice.
+  float kst[kAChunkFloats / kAThreads];  // 32 K values
+  float4 vst[kAV * kADh / 4 / kAThreads];  // 4 x 4 V values
+  auto fetch = [&](int c) {
     if (c < nk) {
-      // ---- phase 1: scores of queries 8w..8w+7 x keys 4*lane..4*lane+3 of chunk c ----
-      float acc[8][4];
+      const int32_t k0 = c * kAK;
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
-#pragma unroll 8
-      for (int p = 0; p < kADh; ++p) {
-        const int sp = p & 7;
-        const float4 qa = *reinterpret_cast<const float4*>(Qs + p * kAQ + (((2 * w) ^ sp) << 2));
-        const float4 qb = *reinterpret_cast<const float4*>(Qs + p * kAQ + (((2 * w + 1) ^ sp) << 2));
-        const float4 kv = *reinterpret_cast<const float4*>(buf + p * kAK + ((lane ^ sp) << 2));
-        const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-        const float kk[4] = {kv.x, kv.y, kv.z, kv.w};
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(qv[i], kk[j], acc[i][j]);
-      }
-      const int32_t key0 = c * kAK + 4 * lane;
-      if (key0 < t) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int32_t key = key0 + j;  // t % 8 == 0: a group of 4 keys is all valid or all past t
-          const int s = (key >> 2) & 7;
-          float* row = S + (size_t)key * kAQ;
-          *reinterpret_cast<float4*>(row + (((2 * w) ^ s) << 2)) =
-              make_float4(__fmul_rn(acc[0][j], scale), __fmul_rn(acc[1][j], scale), __fmul_rn(acc[2][j], scale),
-                          __fmul_rn(acc[3][j], scale));
-          *reinterpret_cast<float4*>(row + (((2 * w + 1) ^ s) << 2)) =
-              make_float4(__fmul_rn(acc[4][j], scale), __fmul_rn(acc[5][j], scale), __fmul_rn(acc[6][j], scale),
-                          __fmul_rn(acc[7][j], scale));
-        }
-      }
-      if (c == nk - 1) {
-        // ---- softmax over each query row (V's first chunk is in flight) ----
-        __syncthreads();
-        const int q = tid & 63, part = tid >> 6;
-        const int grp = q >> 2, qe = q & 3;
-        const int32_t j0 = part * (t / 4), j1 = j0 + t / 4;  // t % 8 == 0
-        float mx = -INFINITY;
-        for (int32_t j = j0; j < j1; ++j) mx = fmaxf(mx, S[(size_t)j * kAQ + ((grp ^ ((j >> 2) & 7)) << 2) + qe]);
-        red[part * 64 + q] = mx;
-        __syncthreads();
-        mx = fmaxf(fmaxf(red[q], red[64 + q]), fmaxf(red[128 + q], red[192 + q]));
-        for (int32_t j = j0; j < j1; ++j) {
-          float* sp = S + (size_t)j * kAQ + ((grp ^ ((j >> 2) & 7)) << 2) + qe;
-          *sp = exp_f32(__fsub_rn(*sp, mx));
-        }
-        __syncthreads();
-        if (part == 0) {  // serial sum in key order
-          float s = 0.0f;
-          for (int32_t j = 0; j < t; ++j) s = __fadd_rn(s, S[(size_t)j * kAQ + ((grp ^ ((j >> 2) & 7)) << 2) + qe]);
-          red[q] = s;
-        }
-        __syncthreads();
-        const float s = red[q];
-        for (int32_t j = j0; j < j1; ++j) {
-          float* sp = S + (size_t)j * kAQ + ((grp ^ ((j >> 2) & 7)) << 2) + qe;
-          *sp = __fdiv_rn(*sp, s);
-        }
+      for (int it = 0; it < kAChunkFloats / kAThreads; ++it) {
+        const int idx = it * kAThreads + tid;
+        const int p = ((idx >> 5) & 7) * 8 + (idx & 7);
+        const int key = (idx >> 8) * 4 + ((idx >> 3) & 3);  // 0..127
+        kst[it] = k0 + key < t ? __ldg(ksrc + (base + k0 + key) * ld + p) : 0.0f;
       }
     } else {
-      // ---- phase 2: O += P V over the keys of V chunk c - nk, in key order ----
-      const int32_t k0 = (c - nk) * kAK;
-      const int jn = min(kAK, t - k0);
-      const int qg4 = 2 * w + qh;
-      for (int jl = 0; jl < jn; ++jl) {
-        const int32_t j = k0 + jl;
-        const float4 pv = *reinterpret_cast<const float4*>(S + (size_t)j * kAQ + ((qg4 ^ ((j >> 2) & 7)) << 2));
-        const float4 vv = *reinterpret_cast<const float4*>(buf + jl * kADh + eg * 4);
-        const float pp[4] = {pv.x, pv.y, pv.z, pv.w};
-        const float vx[4] = {vv.x, vv.y, vv.z, vv.w};
+      const int32_t k0 = (c - nk) * kAV;
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) o[i][e] = fmaf(pp[i], vx[e], o[i][e]);
+      for (int it = 0; it < kAV * kADh / 4 / kAThreads; ++it) {
+        const int idx = it * kAThreads + tid;
+        const int key = idx >> 4, e4 = idx & 15;
+        vst[it] = k0 + key < t ? __ldg(reinterpret_cast<const float4*>(vsrc + (base + k0 + key) * ld) + e4)
+                               : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       }
     }
+  };
+  auto commit = [&](int c) {
+    if (c < nk) {
+#pragma unroll
+      for (int it = 0; it < kAChunkFloats / kAThreads; ++it) {
+        const int idx = it * kAThreads + tid;
+        const int p = ((idx >> 5) & 7) * 8 + (idx & 7);
+        const int key = (idx >> 8) * 4 + ((idx >> 3) & 3);
+        KV[p * kAK + (((key >> 2) ^ (p & 7)) << 2) + (key & 3)] = kst[it];
+      }
+    } else {
+#pragma unroll
+      for (int it = 0; it < kAV * kADh / 4 / kAThreads; ++it) {
+        const int idx = it * kAThreads + tid;
+        const int key = idx >> 4, e4 = idx & 15;
+        float4* dst = reinterpret_cast<float4*>(KV + key * (2 * kADh) + 8 * e4);
+        dst[0] = make_float4(vst[it].x, vst[it].x, vst[it].y, vst[it].y);
+        dst[1] = make_float4(vst[it].z, vst[it].z, vst[it].w, vst[it].w);
+      }
+    }
+  };
+
+  const int qg = lane >> 3, kg = lane & 7;  // lane split (phase 2: qg, eg = kg)
+  const int wq = w >> 2, wk = w & 3;        // warp split (phase 2: wq, we = wk)
+  const int qgrp = 4 * wq + qg;             // this lane's group of 4 queries (0..7)
+  const int kgrp = 8 * wk + kg;             // phase 1: this lane's group of 4 keys in a chunk
+  // phase 1 operand addresses for dims u, u + 8, ... (the swizzle depends on dim & 7)
+  const float* qrow[8];
+  const float* krow[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    qrow[u] = Qd + u * (2 * kAQ) + (((2 * qgrp) ^ u) << 2);  // queries 4qgrp, 4qgrp+1 (each twice)
+    krow[u] = KV + u * kAK + ((kgrp ^ u) << 2);
+  }
+  int poff[8];  // phase 2: offset of this lane's query group in S rows j with (j / 4) & 7 == u
+#pragma unroll
+  for (int u = 0; u < 8; ++u) poff[u] = (qgrp ^ u) << 2;
+  float rmax[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+  float2 o[2][2];  // [query pair (4qgrp, +1) / (+2, +3)][dim 16we + 2eg + e]
+#pragma unroll
+  for (int i = 0; i < 2; ++i) o[i][0] = o[i][1] = make_float2(0.0f, 0.0f);
+
+  cp_async_commit();
+  fetch(0);
+  commit(0);
+  cp_async_wait_all();
+  __syncthreads();
+  // ---- phase 1 ----
+  for (int c = 0; c < nk; ++c) {
+    fetch(c + 1);  // the next K chunk, or V's first chunk
+    float2 acc[4][2];  // [query][key pair (k0, k1) / (k2, k3)]
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int p = 0; p < kADh; ++p) {  // fully unrolled: every address is a base + constant
+      const int u = p & 7;
+      const float4 qa = *reinterpret_cast<const float4*>(qrow[u] + (p - u) * (2 * kAQ));
+      // the next group (queries 4qgrp+2, +3): index (2qgrp + 1) ^ u = ((2qgrp) ^ u) + (u odd ? -1 : 1)
+      const float4 qb = *reinterpret_cast<const float4*>(qrow[u] + (p - u) * (2 * kAQ) + ((u & 1) ? -4 : 4));
+      const float4 kv = *reinterpret_cast<const float4*>(krow[u] + (p - u) * kAK);
+      const float2 k01 = make_float2(kv.x, kv.y), k23 = make_float2(kv.z, kv.w);
+      const float2 qd[4] = {make_float2(qa.x, qa.y), make_float2(qa.z, qa.w), make_float2(qb.x, qb.y),
+                            make_float2(qb.z, qb.w)};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc[i][0] = fma2(qd[i], k01, acc[i][0]);
+        acc[i][1] = fma2(qd[i], k23, acc[i][1]);
+      }
+    }
+    const int32_t key0 = c * kAK + 4 * kgrp;
+    if (key0 < t) {  // t % 8 == 0: a group of 4 keys is all valid or all past t
+      const int sw = (key0 >> 2) & 7;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float sc[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 a = acc[i][j >> 1];
+          sc[i] = __fmul_rn((j & 1) ? a.y : a.x, scale);
+          rmax[i] = fmaxf(rmax[i], sc[i]);
+        }
+        *reinterpret_cast<float4*>(S + (size_t)(key0 + j) * kAQ + ((qgrp ^ sw) << 2)) =
+            make_float4(sc[0], sc[1], sc[2], sc[3]);
+      }
+    }
+    __syncthreads();  // K chunk (and, after the last, Qd) free
+    if (c + 1 < nk) {
+      commit(c + 1);
+      __syncthreads();
+    }
+  }
+
+  // ---- softmax over each query row ----
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {  // max over the warp's 8 key groups
+    rmax[i] = fmaxf(rmax[i], __shfl_xor_sync(0xffffffffu, rmax[i], 1));
+    rmax[i] = fmaxf(rmax[i], __shfl_xor_sync(0xffffffffu, rmax[i], 2));
+    rmax[i] = fmaxf(rmax[i], __shfl_xor_sync(0xffffffffu, rmax[i], 4));
+  }
+  if (kg == 0)
+    *reinterpret_cast<float4*>(wmax + wk * kAQ + 4 * qgrp) = make_float4(rmax[0], rmax[1], rmax[2], rmax[3]);
+  if (tid < 32) tab[tid] = ExpTableConst{}((uint32_t)tid);
+  __syncthreads();
+  {
+    const int q = tid & 31, part = tid >> 5;
+    const int grp = q >> 2, qe = q & 3;
+    const int32_t span = t >> 3, j0 = part * span;  // t % 8 == 0
+    const float mx = fmaxf(fmaxf(wmax[q], wmax[kAQ + q]), fmaxf(wmax[2 * kAQ + q], wmax[3 * kAQ + q]));
+    const ExpTablePtr et{tab};
+    auto at = [&](int32_t j) { return S + (size_t)j * kAQ + ((grp ^ ((j >> 2) & 7)) << 2) + qe; };
+    int32_t j = j0;
+    for (; j + 4 <= j0 + span; j += 4) {  // four independent exps per step
+      float v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = *at(j + u);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = exp_f32_with(__fsub_rn(v[u], mx), et);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) *at(j + u) = v[u];
+    }
+    for (; j < j0 + span; ++j) *at(j) = exp_f32_with(__fsub_rn(*at(j), mx), et);
     __syncthreads();
+    if (part == 0) {  // serial sum in key order
+      float sum = 0.0f;
+#pragma unroll 8
+      for (int32_t jj = 0; jj < t; ++jj) sum = __fadd_rn(sum, *at(jj));
+      rowv[kAQ + q] = sum;
+    }
+    __syncthreads();
+    const float sum = rowv[kAQ + q];
+    for (j = j0; j + 4 <= j0 + span; j += 4) {
+      float v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = *at(j + u);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = __fdiv_rn(v[u], sum);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) *at(j + u) = v[u];
+    }
+    for (; j < j0 + span; ++j) *at(j) = __fdiv_rn(*at(j), sum);
+  }
+  commit(nk);  // V's first chunk (fetched before the last K chunk's FMAs)
+  __syncthreads();
+
+  // ---- phase 2: O += P V, keys in order ----
+  const float* vcol = KV + (8 * wk + kg) * 4;  // this lane's dims 16we + 2eg, +1 (each twice)
+  for (int c = 0; c < nv; ++c) {
+    if (c + 1 < nv) fetch(nk + c + 1);
+    const int32_t k0 = c * kAV;
+    const int jn = min(kAV, t - k0);  // a multiple of 8
+    const float* pbase = S + (size_t)k0 * kAQ;
+    auto step4 = [&](const float* prow, const float* vrow) {  // one group of 4 keys, in order
+      float4 pv[4], vv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        pv[u] = *reinterpret_cast<const float4*>(prow + u * kAQ);
+        vv[u] = *reinterpret_cast<const float4*>(vrow + u * (2 * kADh));
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float2 p01 = make_float2(pv[u].x, pv[u].y), p23 = make_float2(pv[u].z, pv[u].w);
+        const float2 v0 = make_float2(vv[u].x, vv[u].y), v1 = make_float2(vv[u].z, vv[u].w);
+        o[0][0] = fma2(p01, v0, o[0][0]);
+        o[0][1] = fma2(p01, v1, o[0][1]);
+        o[1][0] = fma2(p23, v0, o[1][0]);
+        o[1][1] = fma2(p23, v1, o[1][1]);
+      }
+    };
+    if (jn == kAV) {  // whole chunk: 32-key blocks, the 8 swizzle offsets as constants
+#pragma unroll 1
+      for (int j32 = 0; j32 < kAV; j32 += 32) {
+#pragma unroll
+        for (int gq = 0; gq < 8; ++gq) step4(pbase + (j32 + 4 * gq) * kAQ + poff[gq], vcol + (j32 + 4 * gq) * (2 * kADh));
+      }
+    } else {
+      for (int j4 = 0; j4 < jn; j4 += 4)
+        step4(pbase + j4 * kAQ + ((qgrp ^ ((j4 >> 2) & 7)) << 2), vcol + j4 * (2 * kADh));
+    }
+    __syncthreads();  // the V chunk is free
+    if (c + 1 < nv) {
+      commit(nk + c + 1);
+      __syncthreads();
+    }
   }
   float m = 0.0f;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int32_t q = q0 + 8 * w + 4 * qh + i;
-    if (q < t) {
-      *reinterpret_cast<float4*>(out + (base + q) * ldo + (int64_t)hh * kADh + eg * 4) =
-          make_float4(o[i][0], o[i][1], o[i][2], o[i][3]);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) m = fmaxf(m, fabsf(o[i][e]));
+  for (int i = 0; i < 2; ++i) {
+    const int32_t qa = q0 + 4 * qgrp + 2 * i;
+    float* dst = out + (base + qa) * ldo + (int64_t)hh * kADh + 16 * wk + 2 * kg;
+    if (qa < t) {
+      *reinterpret_cast<float2*>(dst) = make_float2(o[i][0].x, o[i][1].x);
+      m = fmaxf(m, fmaxf(fabsf(o[i][0].x), fabsf(o[i][1].x)));
+    }
+    if (qa + 1 < t) {
+      *reinterpret_cast<float2*>(dst + ldo) = make_float2(o[i][0].y, o[i][1].y);
+      m = fmaxf(m, fmaxf(fabsf(o[i][0].y), fabsf(o[i][1].y)));
     }
   }
   if (amax) block_max_to(m, amax);
@@ -431,7 +556,7 @@ int grid_for(int64_t work, int per_block, int cap) {
 }  // namespace
 
 size_t attention64_smem(int32_t t) {
-  return (size_t)(kAQsFloats + 2 * kAChunkFloats + (size_t)t * kAQ + 4 * 64) * sizeof(float);
+  return (size_t)(kAQdFloats + kAChunkFloats + (size_t)t * kAQ) * sizeof(float);
 }
 
 void launch_embedding(const float* ids, int64_t n, const float* table, int64_t v, int32_t d, float* y,
@@ -440,16 +565,26 @@ void launch_embedding(const float* ids, int64_t n, const float* table, int64_t v
   k_embedding<<<grid_for(n, kThreads / 32, 148 * 16), kThreads, 0, st>>>(ids, n, table, v, d, y, amax.ptr);
 }
 
-void launch_rmsnorm(const float* x, int64_t rows, int32_t d, const float* w, float eps, float inv_d, float* y,
-                    AmaxSink amax, cudaStream_t st) {
-  if (rows <= 0) return;
-  const int64_t blocks = (rows + kThreads - 1) / kThreads;  // 32 rows per warp, 8 warps
-  k_rmsnorm<<<(unsigned)blocks, kThreads, 0, st>>>(x, rows, d, w, eps, inv_d, y, amax.ptr);
+rg_status launch_rmsnorm(const float* x, int64_t rows, int32_t d, const float* w, float eps, float inv_d, float* y,
+                         AmaxSink amax, cudaStream_t st) {
+  if (rows <= 0) return RG_OK;
+  const int32_t rpb = (int32_t)std::max<int64_t>(1, std::min<int64_t>(32, 16384 / d));
+  const size_t smem = (size_t)rpb * (d + 1) * sizeof(float);
+  if (smem > 200 * 1024) return set_last_error(RG_ERR_UNSUPPORTED, "RMSNorm: rows longer than 51199 elements");
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(k_rmsnorm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return set_last_error(RG_ERR_CUDA, "RMSNorm: shared-memory opt-in failed");
+  const bool vec = (d & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  const int64_t blocks = std::min<int64_t>((rows + rpb - 1) / rpb, 148 * 32);
+  k_rmsnorm<<<(unsigned)blocks, kThreads, smem, st>>>(x, rows, d, rpb, vec, w, eps, inv_d, y, amax.ptr);
+  return RG_OK;
 }
 
 void launch_swiglu_mul(const float* gu, int64_t rows, int32_t h, float* y, AmaxSink amax, cudaStream_t st) {
   if (rows <= 0 || h <= 0) return;
-  k_swiglu_mul<<<grid_for(rows * h, kThreads, 148 * 16), kThreads, 0, st>>>(gu, rows, h, y, amax.ptr);
+  // the vector path needs 16-byte aligned rows; a caller's odd base takes the scalar one
+  const bool vec = (h & 3) == 0 && ((reinterpret_cast<uintptr_t>(gu) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  k_swiglu_mul<<<(unsigned)std::min<int64_t>(rows, 148 * 64), kThreads, 0, st>>>(gu, rows, h, vec, y, amax.ptr);
 }
 
 bool attention_fast_eligible(int32_t t, int32_t dh, const float* qkv, int64_t ld, const float* out, int64_t ldo) {

@@ -1144,8 +1144,8 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         break;
       case RG_LAYER_RMSNORM:
         // mean_dim multiplies the sum by 1/d (tensor/ops.rs:755-758)
-        launch_rmsnorm(cur, os.in_elems / op.in_f, op.in_f, op.d_ext.as<float>(), op.param, 1.0f / (float)op.in_f,
-                       dst, sink, st);
+        RG_TRY(launch_rmsnorm(cur, os.in_elems / op.in_f, op.in_f, op.d_ext.as<float>(), op.param,
+                              1.0f / (float)op.in_f, dst, sink, st));
         ++launches;
         RG_LAUNCHED("rmsnorm");
         cur = dst;

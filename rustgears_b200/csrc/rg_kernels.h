@@ -132,8 +132,8 @@ void launch_softmax(const float* x, int64_t outer, int64_t last, float* y, AmaxS
 void launch_embedding(const float* ids, int64_t n, const float* table, int64_t v, int32_t d, float* y,
                       AmaxSink amax, cudaStream_t st);
 int embedding_take_error();
-void launch_rmsnorm(const float* x, int64_t rows, int32_t d, const float* w, float eps, float inv_d, float* y,
-                    AmaxSink amax, cudaStream_t st);
+rg_status launch_rmsnorm(const float* x, int64_t rows, int32_t d, const float* w, float eps, float inv_d, float* y,
+                         AmaxSink amax, cudaStream_t st);
 // gu [rows, 2h] = [g | u] -> y [rows, h] = (g * sigmoid(g)) * u
 void launch_swiglu_mul(const float* gu, int64_t rows, int32_t h, float* y, AmaxSink amax, cudaStream_t st);
 // qkv [b*t, ld] (q, k, v of head hh at columns hh*dh, d + hh*dh, 2d + hh*dh) ->

@@ -262,9 +262,21 @@ static const uint64_t h_exp2_table[32] = RG_EXP2_TABLE;
 #define RG_EXP2_T(i) h_exp2_table[(i)]
 #endif
 
+// The 2^(i/32) table read through the constant bank (host: the host copy).
+struct ExpTableConst {
+  RG_HD uint64_t operator()(uint32_t i) const { return RG_EXP2_T(i); }
+};
+// ... or through a pointer (a shared-memory copy serves lanes that index different
+// entries in one access, where the constant bank serialises them).
+struct ExpTablePtr {
+  const uint64_t* p;
+  RG_HD uint64_t operator()(uint32_t i) const { return p[i]; }
+};
+
 // exp, optimized-routines method in its FMA form (identical on all 2^32 inputs to glibc 2.39 expf
 // on an x86-64 CPU with FMA).
-RG_HD float exp_f32(float x) {
+template <class Tab>
+RG_HD float exp_f32_with(float x, Tab tab) {
   const uint32_t ax = f2u(x) & 0x7fffffffu;
   if (ax >= 0x42b00000u) {                         // |x| >= 88
     if (f2u(x) == 0xff800000u) return 0.0f;
@@ -293,7 +305,7 @@ RG_HD float exp_f32(float x) {
 #endif
   (void)z;
   const double r = fma(inv_ln2_n, xd, -kd);
-  uint64_t t = RG_EXP2_T(ki % 32);
+  uint64_t t = tab((uint32_t)(ki % 32));
   t += ki << (52 - 5);
   const double s = u2d(t);
   const double zz = fma(c0, r, c1);
@@ -312,6 +324,8 @@ RG_HD float exp_f32(float x) {
   return (float)y;
 #endif
 }
+
+RG_HD float exp_f32(float x) { return exp_f32_with(x, ExpTableConst{}); }
 
 // GELU (tanh form) of Activation::apply (src/device/backend.rs:61-68).
 template <bool kNR = true>

@@ -55,7 +55,7 @@ def _worker(rank, world, port, case, out_dir):
         tdist.destroy_process_group()
 
 
-@pytest.mark.parametrize("case", ["c2_cnn_4", "c1_mlp_64", "integration", "affine_first"])
+@pytest.mark.parametrize("case", ["c2_cnn_4", "c1_mlp_64", "integration", "affine_first", "transformer_mini"])
 def test_sharded_equals_single(oracle_lib, tmp_path, case):
     from oracle import configs, oracle
     world = 2
@@ -66,7 +66,7 @@ def test_sharded_equals_single(oracle_lib, tmp_path, case):
     ref, _, _ = oracle.Program(layers).execute(x)
     assert np.array_equal(y, ref)
     # the per-shard scale would NOT give the same answer when a Linear sees the batch
-    if any(l["kind"] == 1 for l in layers):
+    if any(l["kind"] in (1, 14, 15) for l in layers):
         prog = oracle.Program(layers)
         local = [prog.run_sharded(x[a:b], lambda v: v) for a, b in
                  (dist.shard_range(x.shape[0], r, world) for r in range(world))]

@@ -1,5 +1,6 @@
-"""Batch sharding over 2 GPUs (one process per GPU, NCCL): every Linear's absmax is
-max-all-reduced, so the gathered output equals one device's output bit for bit.
+"""Batch sharding over 2 GPUs (one process per GPU, NCCL): every Linear's absmax (each
+inner projection of attention and SwiGLU included) is max-all-reduced, so the
+gathered output equals one device's output bit for bit.
 Skipped when fewer than 2 GPUs are visible."""
 import os
 import socket
@@ -52,7 +53,7 @@ def _rank(rank, world, port, case, out_dir):
         tdist.destroy_process_group()
 
 
-@pytest.mark.parametrize("case", ["c2_cnn_4", "c1_mlp_64", "integration"])
+@pytest.mark.parametrize("case", ["c2_cnn_4", "c1_mlp_64", "integration", "transformer_mini", "resnet_mini"])
 def test_two_gpu_sharding_is_bit_exact(gpu, oracle_lib, tmp_path, case):
     torch = gpu
     if torch.cuda.device_count() < 2:
