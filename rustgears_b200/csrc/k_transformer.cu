@@ -244,32 +244,37 @@ __global__ void __launch_bounds__(128) k_attention_row(const float* __restrict__
 
 // ---------------------------------------------------------------------------
 // Attention for head size 64 and t % 8 == 0, t <= kMaxT (every score column an FMA
-// chain).  One CTA per (32 queries, batch*head), 8 warps, two CTAs per SM (one CTA's
-// softmax overlaps the other's FMA phases):
-//  phase 1  S = Q K^T over 128-key chunks: warp (wq, wk) owns queries 16wq..16wq+15 x
-//           keys 32wk..32wk+31 of the chunk, lane (qg, kg) 4 queries x 4 keys; FMA
-//           chains over the 64 dims; the row maxima are kept on the way;
+// chain).  One CTA per (64 queries, batch*head), 8 warps, one CTA per SM.  Shared
+// memory delivers 128 B per cycle to the registers of an SM, against 128 FMAs per
+// cycle, so the operand bytes per FMA decide the speed: the register tiles are
+//  phase 1  S = Q K^T over 256-key chunks, lane tile 8 queries x 8 keys (64 chains
+//           over the 64 dims; 1 B of operands per FMA): warp w owns keys
+//           32w..32w+31 of the chunk, lane (qg, kg) queries {4qg..+3, 32+4qg..+3} x
+//           keys {4kg..+3, 16+4kg..+3} of the warp's; the row maxima kept on the way;
 //  softmax  exp(s - max) in parallel, the serial sum per row, the division;
-//  phase 2  O = P V over 64-key chunks: warp (wq, we) owns queries 16wq.. x dims
-//           16we..16we+15, lane (qg, eg) 4 queries x 2 dims; FMA chains over the keys
-//           in order.
-// The FMAs are paired (f32x2: each lane rounded once, exactly as fmaf).  The operand
-// that a pair multiplies twice is stored twice in shared memory (Q in phase 1, V in
-// phase 2), so every pair comes straight from a 16-byte load, and within a warp the
-// lanes share their loads four or eight ways (one wavefront each).  K chunks are
-// transposed by 4-byte cp.async copies.  Shared memory (floats): Qd [64 dims][32
-// queries x 2] (after phase 1: row maxima, sums, the exp table), KV 8192 (K^T [64
-// dims][128 keys], or Vd [64 keys][64 dims x 2]), S [t][32 queries].  Q, K^T and S
-// rows swizzle their 16-byte groups: XOR of the group index with dim & 7 (Q, K^T) or
-// (key / 4) & 7 (S).
+//  phase 2  O = P V over 256-key chunks, lane tile 4 queries x 4 dims (2 B per FMA):
+//           warp (wq, we) owns queries 32wq.. x dims 16we.., lane (qg, eg) queries
+//           32wq + 4qg.. x dims 16we + 4eg..; chains over the keys in order.
+// FMAs are paired (f32x2: each lane rounded once, exactly as fmaf) with the shared
+// operand duplicated in registers.  Shared memory (floats): Q^T [64 dims][64
+// queries] 16 KB, KV 64 KB (K^T [64 dims][256 keys] or V [256 keys][64]), S [t][64
+// queries] (t = 512: 128 KB).  Q^T, K^T and S rows swizzle their 16-byte groups:
+// XOR of the group index with dim & 7 (Q^T, K^T) or (key / 4) & 7 (S), so the
+// transposing stores and every row read are conflict-free.
 // ---------------------------------------------------------------------------
-constexpr int kAQ = 32, kAK = 128, kAV = 64, kADh = 64, kAThreads = 256, kMaxT = 512;
-constexpr int kAQdFloats = kADh * kAQ * 2;  // 4096
-constexpr int kAChunkFloats = 8192;         // K^T chunk (64 x 128) or Vd chunk (64 x 128)
+constexpr int kAQ = 64, kAK = 256, kADh = 64, kAThreads = 256, kMaxT = 512;
+constexpr int kAQsFloats = kADh * kAQ;     // 4096
+constexpr int kAChunkFloats = kAK * kADh;  // 16384
+constexpr int kAMiscFloats = 8 * kAQ + kAQ + 64;  // per-warp maxima, row sums, the exp table
 
 __device__ __forceinline__ void cp_async4(float* dst, const float* src, bool valid) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(sm100::smem_addr(dst)), "l"(src),
                "r"(valid ? 4 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async16(float* dst, const float* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sm100::smem_addr(dst)), "l"(src),
+               "r"(valid ? 16 : 0)
                : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
@@ -285,17 +290,16 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
   return *reinterpret_cast<float2*>(&d);
 }
 
-__global__ void __launch_bounds__(kAThreads, 2) k_attention64(const float* __restrict__ qkv, int64_t ld, int32_t t,
+__global__ void __launch_bounds__(kAThreads, 1) k_attention64(const float* __restrict__ qkv, int64_t ld, int32_t t,
                                                              int32_t heads, float scale, float* __restrict__ out,
                                                              int64_t ldo, unsigned* amax) {
   extern __shared__ __align__(16) float sm[];
-  float* Qd = sm;
-  float* KV = sm + kAQdFloats;
+  float* Qs = sm;
+  float* KV = sm + kAQsFloats;
   float* S = KV + kAChunkFloats;
-  // after phase 1 the Qd region holds: [4 key quarters][32] maxima, [32] row max, [32] sum, table
-  float* wmax = Qd;
-  float* rowv = Qd + 4 * kAQ;
-  uint64_t* tab = reinterpret_cast<uint64_t*>(Qd + 6 * kAQ);
+  float* wmax = S + (size_t)t * kAQ;  // [8 warps][64 queries]
+  float* rsum = wmax + 8 * kAQ;       // [64]
+  uint64_t* tab = reinterpret_cast<uint64_t*>(rsum + kAQ);
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int32_t q0 = blockIdx.x * kAQ;
   const int32_t g = blockIdx.y;
@@ -305,156 +309,133 @@ __global__ void __launch_bounds__(kAThreads, 2) k_attention64(const float* __res
   const float* qsrc = qkv + (int64_t)hh * kADh;
   const float* ksrc = qkv + d + (int64_t)hh * kADh;
   const float* vsrc = qkv + 2 * (int64_t)d + (int64_t)hh * kADh;
-  const int nk = (t + kAK - 1) / kAK, nv = (t + kAV - 1) / kAV;
+  const int nk = (t + kAK - 1) / kAK;
+  if (tid < 32) tab[tid] = ExpTableConst{}((uint32_t)tid);
 
-  // Q: each value twice, group (2 queries) index XOR dim & 7.  A warp covers 4 queries x
-  // 8 dims (whole 32-byte sectors).  idx bits: [2:0] dim low, [4:3] query low, [7:5]
-  // dim high, [10:8] query high.
+  // 4-byte transposing copies: a warp covers 4 rows (queries or keys) x 8 dims (whole
+  // 32-byte sectors; the swizzled stores hit 32 banks).  idx bits: [2:0] dim low,
+  // [4:3] row low, [7:5] dim high, [..:8] row high.
 #pragma unroll 4
-  for (int it = 0; it < (kAQ * kADh) / kAThreads; ++it) {
+  for (int it = 0; it < kAQsFloats / kAThreads; ++it) {
     const int idx = it * kAThreads + tid;
     const int p = ((idx >> 5) & 7) * 8 + (idx & 7);
-    const int q = (idx >> 8) * 4 + ((idx >> 3) & 3);  // 0..31
-    const bool ok = q0 + q < t;
-    const float* src = qsrc + (base + (ok ? q0 + q : 0)) * ld + p;
-    float* dst = Qd + p * (2 * kAQ) + ((((q >> 1) ^ (p & 7))) << 2) + 2 * (q & 1);
-    cp_async4(dst, src, ok);
-    cp_async4(dst + 1, src, ok);
+    const int row = (idx >> 8) * 4 + ((idx >> 3) & 3);  // 0..63
+    const bool ok = q0 + row < t;
+    cp_async4(Qs + p * kAQ + (((row >> 2) ^ (p & 7)) << 2) + (row & 3), qsrc + (base + (ok ? q0 + row : 0)) * ld + p,
+              ok);
   }
-  // K and V chunks are fetched into registers one chunk ahead (global loads in flight
-  // while the current chunk is used) and written to shared memory between chunks.
-  // K: a warp covers 4 keys x 8 dims per step (whole 32-byte sectors; the transposing
-  // stores hit 32 banks); V: 16-byte loads, each value stored twice.
-  float kst[kAChunkFloats / kAThreads];  // 32 K values
-  float4 vst[kAV * kADh / 4 / kAThreads];  // 4 x 4 V values
-  auto fetch = [&](int c) {
+  auto load_chunk = [&](int c) {  // chunk stream: K chunks 0..nk-1, then V chunks
     if (c < nk) {
       const int32_t k0 = c * kAK;
-#pragma unroll
+#pragma unroll 8
       for (int it = 0; it < kAChunkFloats / kAThreads; ++it) {
         const int idx = it * kAThreads + tid;
         const int p = ((idx >> 5) & 7) * 8 + (idx & 7);
-        const int key = (idx >> 8) * 4 + ((idx >> 3) & 3);  // 0..127
-        kst[it] = k0 + key < t ? __ldg(ksrc + (base + k0 + key) * ld + p) : 0.0f;
+        const int key = (idx >> 8) * 4 + ((idx >> 3) & 3);  // 0..255
+        const bool ok = k0 + key < t;
+        cp_async4(KV + p * kAK + (((key >> 2) ^ (p & 7)) << 2) + (key & 3),
+                  ksrc + (base + (ok ? k0 + key : 0)) * ld + p, ok);
       }
     } else {
-      const int32_t k0 = (c - nk) * kAV;
-#pragma unroll
-      for (int it = 0; it < kAV * kADh / 4 / kAThreads; ++it) {
+      const int32_t k0 = (c - nk) * kAK;
+#pragma unroll 4
+      for (int it = 0; it < kAChunkFloats / 4 / kAThreads; ++it) {
         const int idx = it * kAThreads + tid;
         const int key = idx >> 4, e4 = idx & 15;
-        vst[it] = k0 + key < t ? __ldg(reinterpret_cast<const float4*>(vsrc + (base + k0 + key) * ld) + e4)
-                               : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        const bool ok = k0 + key < t;
+        cp_async16(KV + key * kADh + e4 * 4, vsrc + (base + (ok ? k0 + key : 0)) * ld + e4 * 4, ok);
       }
     }
-  };
-  auto commit = [&](int c) {
-    if (c < nk) {
-#pragma unroll
-      for (int it = 0; it < kAChunkFloats / kAThreads; ++it) {
-        const int idx = it * kAThreads + tid;
-        const int p = ((idx >> 5) & 7) * 8 + (idx & 7);
-        const int key = (idx >> 8) * 4 + ((idx >> 3) & 3);
-        KV[p * kAK + (((key >> 2) ^ (p & 7)) << 2) + (key & 3)] = kst[it];
-      }
-    } else {
-#pragma unroll
-      for (int it = 0; it < kAV * kADh / 4 / kAThreads; ++it) {
-        const int idx = it * kAThreads + tid;
-        const int key = idx >> 4, e4 = idx & 15;
-        float4* dst = reinterpret_cast<float4*>(KV + key * (2 * kADh) + 8 * e4);
-        dst[0] = make_float4(vst[it].x, vst[it].x, vst[it].y, vst[it].y);
-        dst[1] = make_float4(vst[it].z, vst[it].z, vst[it].w, vst[it].w);
-      }
-    }
+    cp_async_commit();
   };
 
-  const int qg = lane >> 3, kg = lane & 7;  // lane split (phase 2: qg, eg = kg)
-  const int wq = w >> 2, wk = w & 3;        // warp split (phase 2: wq, we = wk)
-  const int qgrp = 4 * wq + qg;             // this lane's group of 4 queries (0..7)
-  const int kgrp = 8 * wk + kg;             // phase 1: this lane's group of 4 keys in a chunk
-  // phase 1 operand addresses for dims u, u + 8, ... (the swizzle depends on dim & 7)
-  const float* qrow[8];
-  const float* krow[8];
-#pragma unroll
-  for (int u = 0; u < 8; ++u) {
-    qrow[u] = Qd + u * (2 * kAQ) + (((2 * qgrp) ^ u) << 2);  // queries 4qgrp, 4qgrp+1 (each twice)
-    krow[u] = KV + u * kAK + ((kgrp ^ u) << 2);
-  }
-  int poff[8];  // phase 2: offset of this lane's query group in S rows j with (j / 4) & 7 == u
-#pragma unroll
-  for (int u = 0; u < 8; ++u) poff[u] = (qgrp ^ u) << 2;
-  float rmax[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-  float2 o[2][2];  // [query pair (4qgrp, +1) / (+2, +3)][dim 16we + 2eg + e]
-#pragma unroll
-  for (int i = 0; i < 2; ++i) o[i][0] = o[i][1] = make_float2(0.0f, 0.0f);
-
-  cp_async_commit();
-  fetch(0);
-  commit(0);
-  cp_async_wait_all();
-  __syncthreads();
   // ---- phase 1 ----
-  for (int c = 0; c < nk; ++c) {
-    fetch(c + 1);  // the next K chunk, or V's first chunk
-    float2 acc[4][2];  // [query][key pair (k0, k1) / (k2, k3)]
+  const int qg = lane >> 2, kg = lane & 3;  // phase 1 lane split
+  float rmax[8];  // [query slot]: slots 0..3 = queries 4qg.., 4..7 = 32 + 4qg..
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = make_float2(0.0f, 0.0f);
+  for (int i = 0; i < 8; ++i) rmax[i] = -INFINITY;
+  {
+    // operand rows for dims u, u + 8, ...: the swizzle depends on dim & 7 only
+    const float* qrow[8];
+    const float* krow[8];
 #pragma unroll
-    for (int p = 0; p < kADh; ++p) {  // fully unrolled: every address is a base + constant
-      const int u = p & 7;
-      const float4 qa = *reinterpret_cast<const float4*>(qrow[u] + (p - u) * (2 * kAQ));
-      // the next group (queries 4qgrp+2, +3): index (2qgrp + 1) ^ u = ((2qgrp) ^ u) + (u odd ? -1 : 1)
-      const float4 qb = *reinterpret_cast<const float4*>(qrow[u] + (p - u) * (2 * kAQ) + ((u & 1) ? -4 : 4));
-      const float4 kv = *reinterpret_cast<const float4*>(krow[u] + (p - u) * kAK);
-      const float2 k01 = make_float2(kv.x, kv.y), k23 = make_float2(kv.z, kv.w);
-      const float2 qd[4] = {make_float2(qa.x, qa.y), make_float2(qa.z, qa.w), make_float2(qb.x, qb.y),
-                            make_float2(qb.z, qb.w)};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        acc[i][0] = fma2(qd[i], k01, acc[i][0]);
-        acc[i][1] = fma2(qd[i], k23, acc[i][1]);
-      }
+    for (int u = 0; u < 8; ++u) {
+      qrow[u] = Qs + u * kAQ + ((qg ^ u) << 2);              // group qg; group qg + 8 at +32 floats
+      krow[u] = KV + u * kAK + (((8 * w + kg) ^ u) << 2);    // group 8w + kg
     }
-    const int32_t key0 = c * kAK + 4 * kgrp;
-    if (key0 < t) {  // t % 8 == 0: a group of 4 keys is all valid or all past t
-      const int sw = (key0 >> 2) & 7;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float sc[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 a = acc[i][j >> 1];
-          sc[i] = __fmul_rn((j & 1) ? a.y : a.x, scale);
-          rmax[i] = fmaxf(rmax[i], sc[i]);
-        }
-        *reinterpret_cast<float4*>(S + (size_t)(key0 + j) * kAQ + ((qgrp ^ sw) << 2)) =
-            make_float4(sc[0], sc[1], sc[2], sc[3]);
-      }
-    }
-    __syncthreads();  // K chunk (and, after the last, Qd) free
-    if (c + 1 < nk) {
-      commit(c + 1);
+    for (int c = 0; c < nk; ++c) {
+      load_chunk(c);  // (the first group also carries Q)
+      cp_async_wait_all();
       __syncthreads();
+      float2 acc[8][4];  // [query slot][key pair: (k0,k1) (k2,k3) of group kg, then of group kg + 4]
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.0f, 0.0f);
+#pragma unroll 8
+      for (int p = 0; p < kADh; ++p) {
+        const int u = p & 7;
+        const float* qr = qrow[u] + (p - u) * kAQ;
+        const float* kr = krow[u] + (p - u) * kAK;
+        const float4 qa = *reinterpret_cast<const float4*>(qr);
+        const float4 qb = *reinterpret_cast<const float4*>(qr + 32);  // group qg + 8: the XOR leaves bit 3
+        const float4 ka = *reinterpret_cast<const float4*>(kr);
+        // group 8w + kg + 4: its swizzled index differs in bit 2 only, by +4 or -4 groups
+        const float4 kb = *reinterpret_cast<const float4*>(kr + ((u & 4) ? -16 : 16));
+        const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+        const float2 kp[4] = {make_float2(ka.x, ka.y), make_float2(ka.z, ka.w), make_float2(kb.x, kb.y),
+                              make_float2(kb.z, kb.w)};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float2 qd = make_float2(qv[i], qv[i]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = fma2(qd, kp[j], acc[i][j]);
+        }
+      }
+      // scaled scores to S (rows = keys), running row maxima
+#pragma unroll
+      for (int kh = 0; kh < 2; ++kh) {  // key group kg, then kg + 4
+        const int32_t key0 = c * kAK + 32 * w + 16 * kh + 4 * kg;
+        if (key0 < t) {  // t % 8 == 0: a group of 4 keys is all valid or all past t
+          const int sw = (key0 >> 2) & 7;
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            float sc[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float2 a = acc[i][2 * kh + (jj >> 1)];
+              sc[i] = __fmul_rn((jj & 1) ? a.y : a.x, scale);
+              rmax[i] = fmaxf(rmax[i], sc[i]);
+            }
+            float* row = S + (size_t)(key0 + jj) * kAQ;
+            *reinterpret_cast<float4*>(row + ((qg ^ sw) << 2)) = make_float4(sc[0], sc[1], sc[2], sc[3]);
+            *reinterpret_cast<float4*>(row + (((qg + 8) ^ sw) << 2)) = make_float4(sc[4], sc[5], sc[6], sc[7]);
+          }
+        }
+      }
+      __syncthreads();  // the K chunk is free
     }
   }
+  load_chunk(nk);  // V's first chunk lands while the softmax runs
 
   // ---- softmax over each query row ----
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {  // max over the warp's 8 key groups
+  for (int i = 0; i < 8; ++i) {  // max over the warp's 4 key groups (lanes kg)
     rmax[i] = fmaxf(rmax[i], __shfl_xor_sync(0xffffffffu, rmax[i], 1));
     rmax[i] = fmaxf(rmax[i], __shfl_xor_sync(0xffffffffu, rmax[i], 2));
-    rmax[i] = fmaxf(rmax[i], __shfl_xor_sync(0xffffffffu, rmax[i], 4));
   }
-  if (kg == 0)
-    *reinterpret_cast<float4*>(wmax + wk * kAQ + 4 * qgrp) = make_float4(rmax[0], rmax[1], rmax[2], rmax[3]);
-  if (tid < 32) tab[tid] = ExpTableConst{}((uint32_t)tid);
+  if (kg == 0) {
+    *reinterpret_cast<float4*>(wmax + w * kAQ + 4 * qg) = make_float4(rmax[0], rmax[1], rmax[2], rmax[3]);
+    *reinterpret_cast<float4*>(wmax + w * kAQ + 32 + 4 * qg) = make_float4(rmax[4], rmax[5], rmax[6], rmax[7]);
+  }
   __syncthreads();
   {
-    const int q = tid & 31, part = tid >> 5;
+    const int q = tid & 63, part = tid >> 6;
     const int grp = q >> 2, qe = q & 3;
-    const int32_t span = t >> 3, j0 = part * span;  // t % 8 == 0
-    const float mx = fmaxf(fmaxf(wmax[q], wmax[kAQ + q]), fmaxf(wmax[2 * kAQ + q], wmax[3 * kAQ + q]));
+    const int32_t span = t >> 2, j0 = part * span;  // t % 8 == 0
+    float mx = wmax[q];
+#pragma unroll
+    for (int ww = 1; ww < 8; ++ww) mx = fmaxf(mx, wmax[ww * kAQ + q]);
     const ExpTablePtr et{tab};
     auto at = [&](int32_t j) { return S + (size_t)j * kAQ + ((grp ^ ((j >> 2) & 7)) << 2) + qe; };
     int32_t j = j0;
@@ -473,10 +454,10 @@ __global__ void __launch_bounds__(kAThreads, 2) k_attention64(const float* __res
       float sum = 0.0f;
 #pragma unroll 8
       for (int32_t jj = 0; jj < t; ++jj) sum = __fadd_rn(sum, *at(jj));
-      rowv[kAQ + q] = sum;
+      rsum[q] = sum;
     }
     __syncthreads();
-    const float sum = rowv[kAQ + q];
+    const float sum = rsum[q];
     for (j = j0; j + 4 <= j0 + span; j += 4) {
       float v[4];
 #pragma unroll
@@ -488,61 +469,72 @@ __global__ void __launch_bounds__(kAThreads, 2) k_attention64(const float* __res
     }
     for (; j < j0 + span; ++j) *at(j) = __fdiv_rn(*at(j), sum);
   }
-  commit(nk);  // V's first chunk (fetched before the last K chunk's FMAs)
-  __syncthreads();
 
   // ---- phase 2: O += P V, keys in order ----
-  const float* vcol = KV + (8 * wk + kg) * 4;  // this lane's dims 16we + 2eg, +1 (each twice)
-  for (int c = 0; c < nv; ++c) {
-    if (c + 1 < nv) fetch(nk + c + 1);
-    const int32_t k0 = c * kAV;
-    const int jn = min(kAV, t - k0);  // a multiple of 8
+  const int wq = w >> 2, we = w & 3;
+  const int pg = lane >> 2, eg = lane & 3;  // phase 2 lane split
+  const int qgrp = 8 * wq + pg;             // this lane's group of 4 queries (0..15)
+  int poff[8];  // offset of the query group in S rows j with (j / 4) & 7 == u
+#pragma unroll
+  for (int u = 0; u < 8; ++u) poff[u] = (qgrp ^ u) << 2;
+  float2 o[2][4];  // [query pair (4qgrp, +1) / (+2, +3)][dim 16we + 4eg + e]
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[i][e] = make_float2(0.0f, 0.0f);
+  const float* vcol = KV + 16 * we + 4 * eg;
+  for (int c = 0; c < nk; ++c) {
+    cp_async_wait_all();
+    __syncthreads();
+    const int32_t k0 = c * kAK;
+    const int jn = min(kAK, t - k0);  // a multiple of 8
     const float* pbase = S + (size_t)k0 * kAQ;
     auto step4 = [&](const float* prow, const float* vrow) {  // one group of 4 keys, in order
       float4 pv[4], vv[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         pv[u] = *reinterpret_cast<const float4*>(prow + u * kAQ);
-        vv[u] = *reinterpret_cast<const float4*>(vrow + u * (2 * kADh));
+        vv[u] = *reinterpret_cast<const float4*>(vrow + u * kADh);
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const float2 p01 = make_float2(pv[u].x, pv[u].y), p23 = make_float2(pv[u].z, pv[u].w);
-        const float2 v0 = make_float2(vv[u].x, vv[u].y), v1 = make_float2(vv[u].z, vv[u].w);
-        o[0][0] = fma2(p01, v0, o[0][0]);
-        o[0][1] = fma2(p01, v1, o[0][1]);
-        o[1][0] = fma2(p23, v0, o[1][0]);
-        o[1][1] = fma2(p23, v1, o[1][1]);
+        const float2 pp[2] = {make_float2(pv[u].x, pv[u].y), make_float2(pv[u].z, pv[u].w)};
+        const float ve[4] = {vv[u].x, vv[u].y, vv[u].z, vv[u].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 vd = make_float2(ve[e], ve[e]);
+          o[0][e] = fma2(pp[0], vd, o[0][e]);
+          o[1][e] = fma2(pp[1], vd, o[1][e]);
+        }
       }
     };
-    if (jn == kAV) {  // whole chunk: 32-key blocks, the 8 swizzle offsets as constants
+    if (jn == kAK) {  // whole chunk: 32-key blocks, the 8 swizzle offsets as constants
 #pragma unroll 1
-      for (int j32 = 0; j32 < kAV; j32 += 32) {
+      for (int j32 = 0; j32 < kAK; j32 += 32) {
 #pragma unroll
-        for (int gq = 0; gq < 8; ++gq) step4(pbase + (j32 + 4 * gq) * kAQ + poff[gq], vcol + (j32 + 4 * gq) * (2 * kADh));
+        for (int gq = 0; gq < 8; ++gq) step4(pbase + (j32 + 4 * gq) * kAQ + poff[gq], vcol + (j32 + 4 * gq) * kADh);
       }
     } else {
       for (int j4 = 0; j4 < jn; j4 += 4)
-        step4(pbase + j4 * kAQ + ((qgrp ^ ((j4 >> 2) & 7)) << 2), vcol + j4 * (2 * kADh));
+        step4(pbase + j4 * kAQ + ((qgrp ^ ((j4 >> 2) & 7)) << 2), vcol + j4 * kADh);
     }
     __syncthreads();  // the V chunk is free
-    if (c + 1 < nv) {
-      commit(nk + c + 1);
-      __syncthreads();
-    }
+    if (c + 1 < nk) load_chunk(nk + c + 1);
   }
   float m = 0.0f;
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const int32_t qa = q0 + 4 * qgrp + 2 * i;
-    float* dst = out + (base + qa) * ldo + (int64_t)hh * kADh + 16 * wk + 2 * kg;
+    float* dst = out + (base + qa) * ldo + (int64_t)hh * kADh + 16 * we + 4 * eg;
     if (qa < t) {
-      *reinterpret_cast<float2*>(dst) = make_float2(o[i][0].x, o[i][1].x);
-      m = fmaxf(m, fmaxf(fabsf(o[i][0].x), fabsf(o[i][1].x)));
+      *reinterpret_cast<float4*>(dst) = make_float4(o[i][0].x, o[i][1].x, o[i][2].x, o[i][3].x);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) m = fmaxf(m, fabsf(o[i][e].x));
     }
     if (qa + 1 < t) {
-      *reinterpret_cast<float2*>(dst + ldo) = make_float2(o[i][0].y, o[i][1].y);
-      m = fmaxf(m, fmaxf(fabsf(o[i][0].y), fabsf(o[i][1].y)));
+      *reinterpret_cast<float4*>(dst + ldo) = make_float4(o[i][0].y, o[i][1].y, o[i][2].y, o[i][3].y);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) m = fmaxf(m, fabsf(o[i][e].y));
     }
   }
   if (amax) block_max_to(m, amax);
@@ -556,7 +548,7 @@ int grid_for(int64_t work, int per_block, int cap) {
 }  // namespace
 
 size_t attention64_smem(int32_t t) {
-  return (size_t)(kAQdFloats + kAChunkFloats + (size_t)t * kAQ) * sizeof(float);
+  return (size_t)(kAQsFloats + kAChunkFloats + (size_t)t * kAQ + kAMiscFloats) * sizeof(float);
 }
 
 void launch_embedding(const float* ids, int64_t n, const float* table, int64_t v, int32_t d, float* y,
