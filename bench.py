@@ -177,6 +177,49 @@ def op_roofline(cfg, sess, per_op_ns, steps, x_shape, peaks, traffic=None):
                 peak_source="measured hbm_gbs (MEASURED_PEAKS.json)")
 
 
+def attention_roofline(x_shape, dev, clocks_summary, reps: int = 5):
+    """C5's dominant kernel is the f32 attention (exact FMA order, CUDA-core FMA pipe),
+    timed alone through rg_attention_f32 on one layer's shapes with CUDA events on
+    the launching stream.  Work: 2 x 64 FMAs per (query, key) per head; peak: the
+    FP32 FMA rate (SMs x 128 FMA/clk x 2 FLOP x the SM clock sampled under load),
+    no FP32 figure being in MEASURED_PEAKS.json."""
+    import ctypes as C
+
+    import torch
+
+    from rustgears_b200 import _native
+    b, t = int(x_shape[0]), int(x_shape[1])
+    heads, dh = 16, 64
+    d = heads * dh
+    qkv = torch.randn((b * t, 3 * d), dtype=torch.float32, device=dev)
+    out = torch.empty((b * t, d), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    L = _native.lib()
+    call = lambda: _native.check(L.rg_attention_f32(C.c_void_p(qkv.data_ptr()), 3 * d, b, t, heads, dh,
+                                                    C.c_void_p(out.data_ptr()), d, C.c_void_p(stream.cuda_stream)))
+    for _ in range(2):
+        call()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for _ in range(reps):
+        call()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    dur_s = e0.elapsed_time(e1) / reps / 1e3
+    flops = 2.0 * 2.0 * b * heads * t * t * dh
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    mhz = clocks_summary.get("sm_mhz") or 1965.0
+    peak = sms * 128 * 2 * mhz * 1e6 / 1e12
+    achieved = flops / dur_s / 1e12
+    return {"kernel": "k_attention64 (f32 QK^T, softmax, P.V; rg_attention_f32)", "bound": "fp32",
+            "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "mean_launch_us": dur_s * 1e6, "flops_per_launch": flops, "traffic": None,
+            "peak_source": f"FP32 FMA peak: {sms} SMs x 128 FMA/clk x 2 at the sampled {mhz:.0f} MHz "
+                           "(no FP32 figure in MEASURED_PEAKS.json)",
+            "note": "the INT8 projections of the same layers run on the tensor cores (k_gemm_tc)"}
+
+
 def _op_shapes(sess, x_shape):
     """(input, output) shape of every op for the input shape x_shape; a shortcut conv
     reads and replaces the saved residual-block input."""
@@ -422,6 +465,9 @@ def main():
         "gpu_launches": launches,
         "clocks": clocks.summary(),
     }
+    if cfg == "c5":
+        line["roofline_int8_projections"] = line["roofline"]
+        line["roofline"] = attention_roofline(x.shape, dev, line["clocks"])
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, model, x)
     if rank == 0:

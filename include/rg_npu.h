@@ -256,6 +256,13 @@ rg_status rg_softmax_f32(const float* x, int64_t outer, int64_t last, float* y, 
 /* Activation::apply elementwise (src/inference/mod.rs:38-53). */
 rg_status rg_activation_f32(const float* x, int64_t n, int32_t act, float act_param, float* y,
                             void* stream);
+/* Extension (the transformer layer kind RG_LAYER_ATTENTION): non-causal multi-head
+ * attention core in f32 (src/nn/attention.rs:178-196): qkv [batch*t, ld] holds q, k,
+ * v of head h at columns h*dh, d + h*dh, 2d + h*dh (d = heads*dh); out [batch*t, ldo]
+ * receives softmax(q k^T * (1/sqrt(dh))) v with the heads merged.  Both matmuls
+ * follow the reference CPU matmul's FMA order (src/device/cpu.rs:234-395). */
+rg_status rg_attention_f32(const float* qkv, int64_t ld, int64_t batch, int32_t t, int32_t heads,
+                           int32_t head_dim, float* out, int64_t ldo, void* stream);
 /* Device self-test of the fast arithmetic the kernels use (no counterpart in the
  * reference): for every one of the 2^32 f32 bit patterns, evaluates each fast path
  * and the plain IEEE / libdevice form and counts the inputs whose results differ:

@@ -550,6 +550,23 @@ def residual_add(x, s, act: int, param: float = 0.0):
     return y
 
 
+def attention_core(qkv, b: int, t: int, heads: int, dh: int):
+    """The f32 core of og_attention on projected q, k, v: qkv [b*t, 3d] -> [b*t, d]
+    (heads split, bmm with k^T in the CPU matmul's FMA order, * 1/sqrt(dh), softmax,
+    bmm with v, heads merged; nn/attention.rs:178-196)."""
+    d = heads * dh
+    qkv = _f32(qkv).reshape(b, t, 3, heads, dh)
+    q, k, v = (np.ascontiguousarray(qkv[:, :, j].transpose(0, 2, 1, 3).reshape(b * heads, t, dh)) for j in range(3))
+    kt = np.ascontiguousarray(k.transpose(0, 2, 1))
+    sc = np.empty((b * heads, t, t), np.float32)
+    lib().og_bmm_fma(_p(q, C.c_float), _p(kt, C.c_float), b * heads, t, dh, t, _p(sc, C.c_float))
+    sc = (sc * (np.float32(1.0) / np.sqrt(np.float32(dh))).astype(np.float32)).astype(np.float32)
+    pm = np.ascontiguousarray(softmax(sc))
+    o = np.empty((b * heads, t, dh), np.float32)
+    lib().og_bmm_fma(_p(pm, C.c_float), _p(v, C.c_float), b * heads, t, t, dh, _p(o, C.c_float))
+    return o.reshape(b, heads, t, dh).transpose(0, 2, 1, 3).reshape(b * t, d)
+
+
 def linear_rows(op: Op, prog: Program, op_index: int, x, r0: int, r1: int, nthreads: int = 1):
     """FusedLinear on rows [r0, r1) with the activation scale over the whole x
     (row sampling for shapes too large for the CPU)."""

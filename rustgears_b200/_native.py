@@ -102,6 +102,7 @@ SIGNATURES = {
     "rg_linear_i8_noalloc": ([_vp, _i64, _i64, _vp, _i64, _i64, _f32, _vp, _i32, _f32, _vp, _vp], _i32),
     "rg_maxpool2d_f32": ([_vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _vp], _i32),
     "rg_softmax_f32": ([_vp, _i64, _i64, _vp, _vp], _i32),
+    "rg_attention_f32": ([_vp, _i64, _i64, _i32, _i32, _i32, _vp, _i64, _vp], _i32),
     "rg_activation_f32": ([_vp, _i64, _i32, _f32, _vp, _vp], _i32),
     "rg_selftest_fast_paths": ([_vp], _i32),
     "rg_rng_seed": ([C.POINTER(RngC), _u64], None),

@@ -1753,6 +1753,18 @@ rg_status rg_activation_f32(const float* x, int64_t n, int32_t act, float act_pa
   return RG_OK;
 }
 
+rg_status rg_attention_f32(const float* qkv, int64_t ld, int64_t batch, int32_t t, int32_t heads, int32_t head_dim,
+                           float* out, int64_t ldo, void* stream) {
+  if (!qkv || !out) return fail(RG_ERR_INVALID_ARG, "null argument");
+  if (batch < 0 || t < 0 || heads <= 0 || head_dim <= 0 || ld < 3 * (int64_t)heads * head_dim ||
+      ldo < (int64_t)heads * head_dim)
+    return fail(RG_ERR_INVALID_ARG, "attention: inconsistent sizes");
+  const float scale = 1.0f / std::sqrt((float)head_dim);  // attention.rs: mul_scalar(1 / sqrt(dh))
+  RG_TRY(launch_attention(qkv, ld, batch, t, heads, head_dim, scale, out, ldo, AmaxSink(), (cudaStream_t)stream));
+  RG_CUDA_TRY(cudaGetLastError());
+  return RG_OK;
+}
+
 rg_status rg_selftest_fast_paths(uint64_t mismatches[5]) {
   if (!mismatches) return fail(RG_ERR_INVALID_ARG, "null argument");
   DevBuf counts;

@@ -95,3 +95,19 @@ def test_maxpool_softmax_activation(gpu, oracle_lib):
         _native.check(L.rg_activation_f32(ptr(zd), z.size, act, C.c_float(p), ptr(yd), None))
         torch.cuda.synchronize()
         assert_same(yd.cpu().numpy(), oracle.activation(z, act, p), f"act {act}")
+
+
+@pytest.mark.parametrize("b,t,heads,dh", [(2, 512, 2, 64), (1, 136, 3, 64), (2, 13, 4, 12), (1, 520, 1, 64),
+                                          (3, 8, 2, 64)])
+def test_attention_core(gpu, oracle_lib, b, t, heads, dh):
+    """rg_attention_f32 against the oracle's attention core (both attention kernels)."""
+    torch = gpu
+    L = _native.lib()
+    d = heads * dh
+    qkv = (np.random.default_rng(t + dh).standard_normal((b * t, 3 * d)) * 2).astype(np.float32)
+    ref = oracle.attention_core(qkv, b, t, heads, dh)
+    xd = torch.from_numpy(qkv).cuda()
+    yd = torch.empty((b * t, d), dtype=torch.float32, device="cuda")
+    _native.check(L.rg_attention_f32(ptr(xd), 3 * d, b, t, heads, dh, ptr(yd), d, None))
+    torch.cuda.synchronize()
+    assert_same(yd.cpu().numpy(), ref, f"attention b{b} t{t} h{heads} dh{dh}")

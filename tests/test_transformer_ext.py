@@ -127,6 +127,9 @@ def test_attention_composition(oracle_lib):
     oracle.lib().og_bmm_fma(_p(np.ascontiguousarray(p)), _p(v), b * h, t, t, dh, _p(o))
     merged = o.reshape(b, h, t, dh).transpose(0, 2, 1, 3).reshape(b * t, d).copy()
     assert_same(y.reshape(b * t, d), lin(3, merged), "attention")
+    # the core the device entry rg_attention_f32 is checked against
+    qkv = np.concatenate([lin(j, xs) for j in range(3)], axis=1)
+    assert_same(oracle.attention_core(qkv, b, t, h, dh), merged, "attention core")
 
 
 def test_swiglu_composition(oracle_lib):
