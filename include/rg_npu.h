@@ -109,6 +109,7 @@ typedef struct rg_session_options {
 
 #define RG_SESSION_NO_PROFILE 1   /* skip per-op CUDA events (records carry 0 durations) */
 #define RG_SESSION_NO_FUSION 2    /* disable multi-op kernels (each NpuOp runs on its own) */
+#define RG_SESSION_NO_GRAPH 4     /* do not replay repeated device-buffer runs from a CUDA graph */
 
 /* Replaces `InferenceSession::from_layers(layers, ExecutionProvider::npu_int8())`
  * (src/inference/mod.rs:162-180) and `npu::compile` (src/inference/npu.rs:188-276):
@@ -137,7 +138,11 @@ rg_status rg_session_run(rg_session* s, const float* x, const int64_t* shape, in
 
 /* Same program on DEVICE buffers of the session's device; enqueued on
  * `stream` (a cudaStream_t, NULL = the session's own stream) and
- * synchronised before return unless RG_RUN_ASYNC is passed in `flags`. */
+ * synchronised before return unless RG_RUN_ASYNC is passed in `flags`.  An
+ * asynchronous run records no per-op timing (last_profile keeps the previous
+ * synchronous run's) and its device error words are checked by the next
+ * synchronous run.  Repeated runs with the same shape and buffers replay a
+ * CUDA graph of the program (see RG_SESSION_NO_GRAPH). */
 #define RG_RUN_ASYNC 1
 rg_status rg_session_run_device(rg_session* s, const float* x_dev, const int64_t* shape,
                                 int32_t ndim, float* y_dev, int64_t y_cap, int64_t* y_shape,

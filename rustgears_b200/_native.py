@@ -16,7 +16,7 @@ RG_OK = 0
 RG_ERR_INVALID_ARG, RG_ERR_SHAPE, RG_ERR_CUDA, RG_ERR_NCCL, RG_ERR_TIMEOUT = 1, 2, 3, 4, 5
 RG_ERR_UNSUPPORTED, RG_ERR_IO, RG_ERR_OOM, RG_ERR_NO_DEVICE, RG_ERR_NO_PROFILE = 6, 7, 8, 9, 10
 RG_TRACE_SCALES, RG_TRACE_AQ, RG_TRACE_ACC, RG_TRACE_OUT = 0, 1, 2, 3
-RG_SESSION_NO_PROFILE, RG_SESSION_NO_FUSION = 1, 2
+RG_SESSION_NO_PROFILE, RG_SESSION_NO_FUSION, RG_SESSION_NO_GRAPH = 1, 2, 4
 RG_RUN_ASYNC = 1
 
 

@@ -18,6 +18,7 @@
 #include <algorithm>
 #include <cmath>
 #include <memory>
+#include <memory>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -195,6 +196,27 @@ struct Session {
   // multi-GPU
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1;
+  // Repeated device-buffer runs (same shape, same input and output pointers) replay the
+  // program from a CUDA graph captured on the second such run: one launch instead of
+  // the host planning and per-kernel launches.
+  struct Graph {
+    std::vector<int64_t> shape;
+    const void* x = nullptr;
+    void* y = nullptr;
+    bool events = false;
+    int seen = 0;                    // identical runs so far (capture on the second)
+    bool off = false;                // capture failed or not applicable: run directly
+    cudaGraphExec_t exec = nullptr;
+    int32_t launches = 0;
+    bool used_tc = false, used_embed = false;
+    std::vector<int> ev_of;
+    std::shared_ptr<void> plan;      // the RunPlan the graph was captured with
+  } graph;
+  bool capturing = false;
+  cudaEvent_t t0 = nullptr, t1 = nullptr;  // whole-run timing
+  ~Session() {
+    if (graph.exec) cudaGraphExecDestroy(graph.exec);
+  }
 };
 
 static void act_name(int32_t act, float p, char* out, size_t cap) {
@@ -906,7 +928,11 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
   int32_t launches = 0;
   s.ev_of.assign(n + 1, 0);
   int next_ev = 1;
-  if (record_events) RG_CUDA_TRY(cudaEventRecord(s.events[0], st));
+  // inside a graph capture an event record must be external to be timed afterwards
+  auto record = [&](cudaEvent_t e) {
+    return s.capturing ? cudaEventRecordWithFlags(e, st, cudaEventRecordExternal) : cudaEventRecord(e, st);
+  };
+  if (record_events) RG_CUDA_TRY(record(s.events[0]));
   for (size_t i = 0; i < n; ++i) {
     const Op& op = s.ops[i];
     const OpShape& os = P.shapes[i];
@@ -977,7 +1003,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
       s.used_tc = true;
       cur = bdst;
       (void)last_os;
-      if (record_events) RG_CUDA_TRY(cudaEventRecord(s.events[(size_t)next_ev], st));
+      if (record_events) RG_CUDA_TRY(record(s.events[(size_t)next_ev]));
       s.ev_of[i + 1] = next_ev++;
       for (size_t j = i + 2; j <= i + 4; ++j) s.ev_of[j] = s.ev_of[i + 1];
       i += 3;
@@ -1184,7 +1210,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
     if (op.kind == RG_LAYER_FLATTEN) {
       s.ev_of[i + 1] = s.ev_of[i];  // a reshape: no kernel, no event
     } else {
-      if (record_events) RG_CUDA_TRY(cudaEventRecord(s.events[(size_t)next_ev], st));
+      if (record_events) RG_CUDA_TRY(record(s.events[(size_t)next_ev]));
       s.ev_of[i + 1] = next_ev++;
     }
   }
@@ -1398,6 +1424,10 @@ void rg_session_destroy(rg_session* h) {
   for (cudaEvent_t e : s.events) cudaEventDestroy(e);
   for (cudaEvent_t e : s.chunk_events)
     if (e) cudaEventDestroy(e);
+  if (s.t0) cudaEventDestroy(s.t0);
+  if (s.t1) cudaEventDestroy(s.t1);
+  if (s.graph.exec) cudaGraphExecDestroy(s.graph.exec);
+  s.graph.exec = nullptr;
   if (s.stream) cudaStreamDestroy(s.stream);
   if (s.copy_stream) cudaStreamDestroy(s.copy_stream);
   delete h;
@@ -1414,6 +1444,71 @@ rg_status rg_session_output_shape(rg_session* h, const int64_t* shape, int32_t n
   return RG_OK;
 }
 
+// The program on device buffers through the session's CUDA graph, capturing it on
+// the second identical run (the first sizes every buffer and sets every kernel
+// attribute outside the capture).  Returns false when the run is not replayable
+// and must go through execute() directly.
+static rg_status run_graph(Session& s, const float* xd, const int64_t* shape, int32_t ndim, float* yd,
+                           cudaStream_t st, bool events, std::shared_ptr<RunPlan>& P, bool& done) {
+  done = false;
+  Session::Graph& g = s.graph;
+  const std::vector<int64_t> key(shape, shape + ndim);
+  if (g.shape == key && g.x == xd && g.y == yd && g.events == events) {
+    if (g.exec) {
+      RG_CUDA_TRY(cudaGraphLaunch(g.exec, st));
+      s.used_tc = s.used_tc || g.used_tc;
+      s.used_embed = s.used_embed || g.used_embed;
+      s.last.launches = g.launches;
+      s.ev_of = g.ev_of;
+      P = std::static_pointer_cast<RunPlan>(g.plan);
+      done = true;
+      return RG_OK;
+    }
+    if (g.off || ++g.seen < 2) return RG_OK;
+  } else {
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+    g = Session::Graph();
+    g.shape = key; g.x = xd; g.y = yd; g.events = events; g.seen = 1;
+    return RG_OK;
+  }
+  // second identical run: capture it
+  P = std::make_shared<RunPlan>();
+  RG_TRY(make_plan(s, shape, ndim, *P));
+  if (P->cov_bytes) {  // (its host-to-device mask copy stays outside graphs)
+    g.off = true;
+    return RG_OK;
+  }
+  RG_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  s.capturing = true;
+  const bool tc0 = s.used_tc, emb0 = s.used_embed;
+  s.used_tc = s.used_embed = false;
+  rg_status rs = execute(s, xd, *P, yd, st, events);
+  s.capturing = false;
+  cudaGraph_t graph = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(st, &graph);
+  cudaError_t ie = cudaErrorUnknown;
+  if (rs == RG_OK && ce == cudaSuccess) ie = cudaGraphInstantiate(&g.exec, graph, 0);
+  if (graph) cudaGraphDestroy(graph);
+  if (ie != cudaSuccess) {  // not capturable: this run and the next ones go through execute()
+    g.exec = nullptr;
+    g.off = true;
+    s.used_tc = tc0;
+    s.used_embed = emb0;
+    cudaGetLastError();
+    return RG_OK;
+  }
+  g.used_tc = s.used_tc;
+  g.used_embed = s.used_embed;
+  g.launches = s.last.launches;
+  g.ev_of = s.ev_of;
+  g.plan = P;
+  s.used_tc = s.used_tc || tc0;
+  s.used_embed = s.used_embed || emb0;
+  RG_CUDA_TRY(cudaGraphLaunch(g.exec, st));
+  done = true;
+  return RG_OK;
+}
+
 static rg_status run_impl(rg_session* h, const float* x, bool x_host, const int64_t* shape, int32_t ndim, float* y,
                           bool y_host, int64_t y_cap, int64_t* y_shape, int32_t* y_ndim, cudaStream_t user_st,
                           bool async) {
@@ -1421,8 +1516,16 @@ static rg_status run_impl(rg_session* h, const float* x, bool x_host, const int6
   Session& s = h->s;
   std::lock_guard<std::mutex> lock(s.mu);
   RG_CUDA_TRY(cudaSetDevice(s.device));
-  RunPlan P;
-  RG_TRY(make_plan(s, shape, ndim, P));
+  std::shared_ptr<RunPlan> Pp;
+  const bool same_as_graph = !x_host && !y_host && s.graph.exec && s.graph.x == x && s.graph.y == y &&
+                             s.graph.shape == std::vector<int64_t>(shape, shape + ndim);
+  if (same_as_graph) {
+    Pp = std::static_pointer_cast<RunPlan>(s.graph.plan);
+  } else {
+    Pp = std::make_shared<RunPlan>();
+    RG_TRY(make_plan(s, shape, ndim, *Pp));
+  }
+  const RunPlan& P = *Pp;
   int64_t in_elems = 1;
   for (int32_t i = 0; i < ndim; ++i) in_elems *= shape[i];
   const std::vector<int64_t> oshape = P.shapes.empty() ? std::vector<int64_t>(shape, shape + ndim) : P.shapes.back().out;
@@ -1431,13 +1534,13 @@ static rg_status run_impl(rg_session* h, const float* x, bool x_host, const int6
   if (out_elems > y_cap) return fail(RG_ERR_INVALID_ARG, "output needs %lld elements, capacity %lld",
                                      (long long)out_elems, (long long)y_cap);
   cudaStream_t st = user_st ? user_st : s.stream;
-  const bool events = !(s.flags & RG_SESSION_NO_PROFILE);
-  cudaEvent_t t0 = nullptr, t1 = nullptr;
-  if (events) {
-    RG_CUDA_TRY(cudaEventCreate(&t0));
-    RG_CUDA_TRY(cudaEventCreate(&t1));
-    RG_CUDA_TRY(cudaEventRecord(t0, st));
+  const bool async_run = async && !x_host && !y_host && !s.trace;
+  const bool events = !(s.flags & RG_SESSION_NO_PROFILE) && !async_run;
+  if (events && !s.t0) {
+    RG_CUDA_TRY(cudaEventCreate(&s.t0));
+    RG_CUDA_TRY(cudaEventCreate(&s.t1));
   }
+  if (events) RG_CUDA_TRY(cudaEventRecord(s.t0, st));
   const float* xd = x;
   HostFeed feed;
   if (x_host) {
@@ -1461,24 +1564,24 @@ static rg_status run_impl(rg_session* h, const float* x, bool x_host, const int6
     RG_TRY(s.yout.ensure((size_t)std::max<int64_t>(out_elems, 1) * 4));
     yd = s.yout.as<float>();
   }
-  rg_status rs;
+  rg_status rs = RG_OK;
+  bool done = false;
   if (s.ops.empty()) {
     if (in_elems) RG_CUDA_TRY(cudaMemcpyAsync(yd, xd, (size_t)in_elems * 4, cudaMemcpyDeviceToDevice, st));
-    rs = RG_OK;
-  } else {
-    rs = execute(s, xd, P, yd, st, events, feed);
+    done = true;
+  } else if (!x_host && !y_host && !s.trace && s.world == 1 && !(s.flags & RG_SESSION_NO_GRAPH)) {
+    std::shared_ptr<RunPlan> Pg;
+    rs = run_graph(s, xd, shape, ndim, yd, st, events, Pg, done);
+    if (rs == RG_OK && done && Pg) Pp = Pg;
   }
-  if (rs != RG_OK) {
-    if (t0) cudaEventDestroy(t0);
-    if (t1) cudaEventDestroy(t1);
-    return rs;
-  }
+  if (rs == RG_OK && !done) rs = execute(s, xd, *Pp, yd, st, events, feed);
+  if (rs != RG_OK) return rs;
   if (y_host && out_elems)
     RG_CUDA_TRY(cudaMemcpyAsync(y, yd, (size_t)out_elems * 4, cudaMemcpyDeviceToHost, st));
-  if (events) RG_CUDA_TRY(cudaEventRecord(t1, st));
+  if (events) RG_CUDA_TRY(cudaEventRecord(s.t1, st));
   for (size_t i = 0; i < oshape.size(); ++i) y_shape[i] = oshape[i];
   *y_ndim = (int32_t)oshape.size();
-  if (async && !x_host && !y_host && !events && !s.trace) return RG_OK;
+  if (async_run) return RG_OK;
   RG_CUDA_TRY(cudaStreamSynchronize(st));
   if (s.used_tc) {
     s.used_tc = false;
@@ -1493,12 +1596,10 @@ static rg_status run_impl(rg_session* h, const float* x, bool x_host, const int6
   int64_t total_ns = 0;
   if (events) {
     float ms = 0;
-    RG_CUDA_TRY(cudaEventElapsedTime(&ms, t0, t1));
+    RG_CUDA_TRY(cudaEventElapsedTime(&ms, s.t0, s.t1));
     total_ns = (int64_t)((double)ms * 1e6);
-    cudaEventDestroy(t0);
-    cudaEventDestroy(t1);
   }
-  return collect_profile(s, P, events && !s.ops.empty(), total_ns);
+  return collect_profile(s, *Pp, events && !s.ops.empty(), total_ns);
 }
 
 rg_status rg_session_run(rg_session* h, const float* x, const int64_t* shape, int32_t ndim, float* y, int64_t y_cap,

@@ -140,6 +140,34 @@ def test_run_device_and_concurrency(gpu, oracle_lib):
         assert_same(r, ref, "concurrent run")
 
 
+@pytest.mark.parametrize("case", ["c2_cnn_4", "transformer_mini", "resnet_mini", "c1_mlp_64"])
+def test_repeated_device_runs_replay_a_graph(gpu, oracle_lib, case):
+    """Identical device-buffer runs replay a captured CUDA graph from the second one on:
+    same results (also after the input changes in place), per-op profile records
+    still timed; a session with RG_SESSION_NO_GRAPH agrees."""
+    torch = gpu
+    layers, x = configs.CASES[case]()
+    ref, _, macs = oracle.Program(layers).execute(x, nthreads=8)
+    for flags in (0, _native.RG_SESSION_NO_GRAPH):
+        sess = session_for(layers, flags=flags)
+        xd = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+        yd = torch.empty(ref.shape, dtype=torch.float32, device="cuda")
+        for _ in range(4):
+            yd.fill_(np.nan)
+            sess.run_device(xd, yd)
+            torch.cuda.synchronize()
+            assert_same(yd.cpu().numpy(), ref, f"run {flags}")
+            prof = sess.last_npu_profile()
+            assert [r.macs for r in prof.records] == macs.tolist()
+            assert prof.total_time_ns > 0
+        x2 = (x * np.float32(0.5)).astype(np.float32)
+        xd.copy_(torch.from_numpy(x2))
+        sess.run_device(xd, yd)
+        torch.cuda.synchronize()
+        ref2, _, _ = oracle.Program(layers).execute(x2, nthreads=8)
+        assert_same(yd.cpu().numpy(), ref2, f"new input {flags}")
+
+
 def test_shape_errors(gpu):
     layers, _ = configs.c2_cnn(1)
     sess = session_for(layers)
