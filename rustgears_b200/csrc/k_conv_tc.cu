@@ -64,6 +64,7 @@ struct Cfg {
 struct ConvTcParams {
   const int8_t* a;          // NHWC i8 [n_img, h, w, cpad]
   int32_t n_img, h, w, cpad, k, stride, pad, oh, ow;
+  int32_t kxp;              // narrow operand (cpad 4): taps per kernel row, a multiple of 4
   int64_t m;                // n_img * oh * ow
   int32_t n;                // output channels
   int32_t kdim;             // k * k * cpad (multiple of 16)
@@ -73,6 +74,9 @@ struct ConvTcParams {
   const float* bias;
   float act_param;
   float* out;               // NCHW [n_img, n, oh, ow]
+  const float* residual;    // optional, same layout: out = res_act(epilogue + residual)
+  int32_t res_act;
+  float res_param;
   int32_t* acc;             // optional, same layout
   unsigned* amax;           // optional absmax sink
   int64_t amax_per_slot;    // 0: one slot; else elements per slot (n * oh * ow: per image)
@@ -112,7 +116,9 @@ __device__ __forceinline__ void flush_slot_max(unsigned* base, int64_t slot, flo
   }
 }
 
-template <int BN, int ACT>
+// NARROW: a 4-byte operand pixel (up to 4 channels, e.g. an RGB stem); a 16-byte K
+// chunk then holds 4 consecutive taps of one kernel row, loaded as 4 pixel words.
+template <int BN, int ACT, bool NARROW>
 __global__ void __launch_bounds__(kThreads, 1)
     k_conv_tc(const __grid_constant__ CUtensorMap map_w, const ConvTcParams p) {
   using C = Cfg<BN>;
@@ -184,14 +190,31 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           v[j] = make_uint4(0u, 0u, 0u, 0u);
-          const int32_t iy = iy0 + ky, ix = ix0 + kx;
-          if (valid && k0 < p.kdim && iy >= 0 && iy < p.h && ix >= 0 && ix < p.w)
-            v[j] = __ldg(reinterpret_cast<const uint4*>(base + ((int64_t)iy * p.w + ix) * p.cpad + c0));
-          k0 += 16;
-          c0 += 16;
-          if (c0 == p.cpad) {
-            c0 = 0;
-            if (++kx == p.k) { kx = 0; ++ky; }
+          const int32_t iy = iy0 + ky;
+          if (NARROW) {  // taps kx..kx+3 of kernel row ky: 4 pixel words
+            if (valid && k0 < p.kdim && iy >= 0 && iy < p.h) {
+              const uint32_t* rowp = reinterpret_cast<const uint32_t*>(base + (int64_t)iy * p.w * 4);
+              uint32_t wv[4];
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                const int32_t ix = ix0 + kx + t;
+                wv[t] = (kx + t < p.k && ix >= 0 && ix < p.w) ? __ldg(rowp + ix) : 0u;
+              }
+              v[j] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            }
+            k0 += 16;
+            kx += 4;
+            if (kx == p.kxp) { kx = 0; ++ky; }
+          } else {
+            const int32_t ix = ix0 + kx;
+            if (valid && k0 < p.kdim && iy >= 0 && iy < p.h && ix >= 0 && ix < p.w)
+              v[j] = __ldg(reinterpret_cast<const uint4*>(base + ((int64_t)iy * p.w + ix) * p.cpad + c0));
+            k0 += 16;
+            c0 += 16;
+            if (c0 == p.cpad) {
+              c0 = 0;
+              if (++kx == p.k) { kx = 0; ++ky; }
+            }
           }
         }
       };
@@ -285,6 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float sa = row_ok ? p.a_scale[img] : 0.0f;
       const float cs_tensor = __fmul_rn(sa, p.w_scale);
       float* obase = p.out + img * (int64_t)p.n * hw_out + pix;
+      const float* rbase = p.residual ? p.residual + img * (int64_t)p.n * hw_out + pix : nullptr;
       float mx = 0.0f;
 #pragma unroll 1
       for (int c0 = part * kCols; c0 < (part + 1) * kCols; c0 += 16) {
@@ -294,12 +318,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
         const int64_t col0 = (int64_t)nb * BN + c0;
         if (row_ok && col0 < p.n) {
+          // the residual values first: all 16 loads in flight before the stores
+          float res[16];
+          if (rbase) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) res[j] = col0 + j < p.n ? __ldg(rbase + (col0 + j) * hw_out) : 0.0f;
+          }
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int64_t c = col0 + j;
             if (c < p.n) {
               const float cs = p.w_scale_ch ? __fmul_rn(sa, __ldg(p.w_scale_ch + c)) : cs_tensor;
-              const float o = epilogue_t<ACT>((int32_t)v[j], cs, __ldg(p.bias + c), p.act_param);
+              float o = epilogue_t<ACT>((int32_t)v[j], cs, __ldg(p.bias + c), p.act_param);
+              if (rbase) {  // the block's activation: none, ReLU or LeakyReLU (the fusable ones)
+                o = __fadd_rn(o, res[j]);
+                if (p.res_act == ACT_RELU) o = fmaxf(o, 0.0f);
+                else if (p.res_act == ACT_LEAKY_RELU) o = o > 0.0f ? o : __fmul_rn(p.res_param, o);
+              }
               obase[c * hw_out] = o;
               if (p.acc) p.acc[img * (int64_t)p.n * hw_out + c * hw_out + pix] = (int32_t)v[j];
               mx = fmaxf(mx, fabsf(o));
@@ -335,12 +370,12 @@ bool make_w_map(CUtensorMap* map, const void* base, int64_t rows, int64_t ld, in
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int ACT>
+template <int BN, int ACT, bool NARROW>
 bool launch_bn(const GemmArgs& a, int num_sms, cudaStream_t st) {
   using C = Cfg<BN>;
   static std::once_flag once;
   std::call_once(once, [] {
-    cudaFuncSetAttribute(k_conv_tc<BN, ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    cudaFuncSetAttribute(k_conv_tc<BN, ACT, NARROW>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
   });
   CUtensorMap mw;
   if (!make_w_map(&mw, a.w, a.n, a.ldb, BN)) return false;
@@ -349,27 +384,29 @@ bool launch_bn(const GemmArgs& a, int num_sms, cudaStream_t st) {
   p.n_img = (int32_t)(a.m / a.out_l);
   p.h = a.g.h; p.w = a.g.w; p.cpad = a.g.cpad; p.k = a.g.k; p.stride = a.g.stride; p.pad = a.g.pad;
   p.oh = a.g.oh; p.ow = a.g.ow;
+  p.kxp = a.g.kxp ? a.g.kxp : a.g.k;
   p.m = a.m; p.n = (int32_t)a.n; p.kdim = (int32_t)a.k;
   p.a_scale = a.a_scale; p.w_scale = a.w_scale; p.w_scale_ch = a.w_scale_ch; p.bias = a.bias;
   p.act_param = a.act_param; p.out = a.out; p.acc = a.acc;
+  p.residual = a.residual; p.res_act = a.res_act; p.res_param = a.res_param;
   p.amax = a.amax.ptr; p.amax_per_slot = a.amax.elems_per_slot;
   p.tiles_m = (int)((a.m + BM - 1) / BM);
   p.tiles_n = (int)((a.n + BN - 1) / BN);
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < num_sms ? tiles : num_sms;
-  k_conv_tc<BN, ACT><<<grid, kThreads, C::kSmem, st>>>(mw, p);
+  k_conv_tc<BN, ACT, NARROW><<<grid, kThreads, C::kSmem, st>>>(mw, p);
   return true;
 }
 
-template <int BN>
+template <int BN, bool NARROW = false>
 bool launch_act(const GemmArgs& a, int num_sms, cudaStream_t st) {
   switch (a.act) {
-    case ACT_NONE: return launch_bn<BN, ACT_NONE>(a, num_sms, st);
-    case ACT_RELU: return launch_bn<BN, ACT_RELU>(a, num_sms, st);
-    case ACT_SIGMOID: return launch_bn<BN, ACT_SIGMOID>(a, num_sms, st);
-    case ACT_TANH: return launch_bn<BN, ACT_TANH>(a, num_sms, st);
-    case ACT_GELU: return launch_bn<BN, ACT_GELU>(a, num_sms, st);
-    case ACT_LEAKY_RELU: return launch_bn<BN, ACT_LEAKY_RELU>(a, num_sms, st);
+    case ACT_NONE: return launch_bn<BN, ACT_NONE, NARROW>(a, num_sms, st);
+    case ACT_RELU: return launch_bn<BN, ACT_RELU, NARROW>(a, num_sms, st);
+    case ACT_SIGMOID: return launch_bn<BN, ACT_SIGMOID, NARROW>(a, num_sms, st);
+    case ACT_TANH: return launch_bn<BN, ACT_TANH, NARROW>(a, num_sms, st);
+    case ACT_GELU: return launch_bn<BN, ACT_GELU, NARROW>(a, num_sms, st);
+    case ACT_LEAKY_RELU: return launch_bn<BN, ACT_LEAKY_RELU, NARROW>(a, num_sms, st);
     default: return false;
   }
 }
@@ -380,9 +417,12 @@ bool launch_act(const GemmArgs& a, int num_sms, cudaStream_t st) {
 // weights, NCHW output, per-image activation scales, and enough work for the tensor cores.
 bool conv_tc_eligible(const GemmArgs& a) {
   if (!a.conv || a.out_l <= 0 || a.rows_per_scale != a.out_l) return false;
-  if ((a.g.cpad & 15) || a.g.c != a.g.cpad || a.n < 16 || (a.k & 15) ||
-      a.k != (int64_t)a.g.k * a.g.k * a.g.cpad || a.ldb != a.k)
+  const bool narrow = a.g.cpad == 4;
+  const int32_t kxp = a.g.kxp ? a.g.kxp : a.g.k;
+  if (narrow ? (kxp & 3) || kxp < a.g.k || a.k != (int64_t)a.g.k * kxp * 4
+             : (a.g.cpad & 15) || kxp != a.g.k || a.k != (int64_t)a.g.k * a.g.k * a.g.cpad)
     return false;
+  if (a.g.c != a.g.cpad || a.n < 16 || (a.k & 15) || a.ldb != a.k) return false;
   if (a.amax.ptr && a.amax.elems_per_slot != 0 && a.amax.elems_per_slot != a.n * a.out_l) return false;
   if ((reinterpret_cast<uintptr_t>(a.a) | reinterpret_cast<uintptr_t>(a.w)) & 15) return false;
   if (a.m * a.n * a.k < (int64_t)1 << 22) return false;
@@ -390,6 +430,7 @@ bool conv_tc_eligible(const GemmArgs& a) {
 }
 
 bool launch_conv_tc(const GemmArgs& a, int num_sms, cudaStream_t st) {
+  if (a.g.cpad == 4) return launch_act<64, true>(a, num_sms, st);
   if (a.n >= 256) return launch_act<256>(a, num_sms, st);
   if (a.n >= 128) return launch_act<128>(a, num_sms, st);
   return launch_act<64>(a, num_sms, st);

@@ -47,14 +47,15 @@ __device__ __forceinline__ RowCtx make_row(const GemmArgs& p, int64_t r) {
 __device__ __forceinline__ int32_t load_a_word(const GemmArgs& p, const RowCtx& rc, int64_t kk) {
   if (!rc.valid || kk >= p.k) return 0;
   if (!p.conv) return __ldg(reinterpret_cast<const int32_t*>(rc.base + kk));
-  const int32_t C = p.g.c, kw = p.g.k;
-  const int64_t kreal = (int64_t)kw * kw * C;
+  // K order (ky, kx, c) with kxp taps per kernel row (taps kx >= k are zero padding)
+  const int32_t C = p.g.c, kw = p.g.k, kxp = p.g.kxp ? p.g.kxp : p.g.k;
+  const int64_t kreal = (int64_t)kw * kxp * C;
   if ((C & 3) == 0) {
     if (kk >= kreal) return 0;
     const int32_t tap = (int32_t)(kk / C), ch = (int32_t)(kk - (int64_t)tap * C);
-    const int32_t ky = tap / kw, kx = tap - ky * kw;
+    const int32_t ky = tap / kxp, kx = tap - ky * kxp;
     const int32_t iy = rc.iy0 + ky, ix = rc.ix0 + kx;
-    if (iy < 0 || iy >= p.g.h || ix < 0 || ix >= p.g.w) return 0;
+    if (kx >= kw || iy < 0 || iy >= p.g.h || ix < 0 || ix >= p.g.w) return 0;
     return __ldg(reinterpret_cast<const int32_t*>(rc.base + ((int64_t)iy * p.g.w + ix) * p.g.cpad + ch));
   }
   uint32_t wv = 0;
@@ -63,9 +64,9 @@ __device__ __forceinline__ int32_t load_a_word(const GemmArgs& p, const RowCtx& 
     const int64_t kb = kk + b;
     if (kb >= kreal) break;
     const int32_t tap = (int32_t)(kb / C), ch = (int32_t)(kb - (int64_t)tap * C);
-    const int32_t ky = tap / kw, kx = tap - ky * kw;
+    const int32_t ky = tap / kxp, kx = tap - ky * kxp;
     const int32_t iy = rc.iy0 + ky, ix = rc.ix0 + kx;
-    if (iy < 0 || iy >= p.g.h || ix < 0 || ix >= p.g.w) continue;
+    if (kx >= kw || iy < 0 || iy >= p.g.h || ix < 0 || ix >= p.g.w) continue;
     const int8_t v = rc.base[((int64_t)iy * p.g.w + ix) * p.g.cpad + ch];
     wv |= (uint32_t)(uint8_t)v << (8 * b);
   }

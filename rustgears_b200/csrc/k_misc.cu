@@ -3,6 +3,8 @@
 //
 // Each kernel can also emit the absmax of its output (per tensor or per image)
 // for the next quantizing op, so no separate absmax pass re-reads the tensor.
+#include <algorithm>
+
 #include "rg_kernels.h"
 #include "rg_math.cuh"
 
@@ -30,34 +32,53 @@ __device__ __forceinline__ void block_max_to(float v, unsigned* dst) {
   }
 }
 
-// grid (blocks, slots): slot = image (per-image sink) or 0; each block covers part of one slot.
-// max_pool2d (src/kernels.rs:165-213): pad 0, `if v > best || v.is_nan()`.
+// max_pool2d (src/kernels.rs:165-213): pad 0, `if v > best || v.is_nan()` in window
+// order.  One thread per output; K (2 and 3 as template instances, 0 = any size at
+// run time) fixes the window so that all of its loads are in flight together.
+// grid.y strides over the absmax slots (an image, or the whole tensor).
+template <int K>
 __global__ void __launch_bounds__(kThreads) k_maxpool2d(const float* __restrict__ x, int64_t planes,
-                                                        int32_t h, int32_t w, int32_t k, int32_t s,
+                                                        int32_t h, int32_t w, int32_t kr, int32_t s,
                                                         int32_t oh, int32_t ow, float* __restrict__ y,
                                                         unsigned* amax, int64_t planes_per_slot) {
-  const int64_t slot = blockIdx.y;
-  const int64_t p0 = slot * planes_per_slot;
-  const int64_t p1 = min(planes, p0 + planes_per_slot);
-  const int64_t per = (p1 - p0) * oh * ow;
-  float m = 0.0f;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < per;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t o = p0 * oh * ow + i;
-    const int64_t plane = o / ((int64_t)oh * ow);
-    const int32_t rem = (int32_t)(o - plane * oh * ow);
-    const int32_t oy = rem / ow, ox = rem - oy * ow;
-    const float* xp = x + plane * (int64_t)h * w + (int64_t)(oy * s) * w + ox * s;
-    float best = -INFINITY;
-    for (int32_t ki = 0; ki < k; ++ki)
-      for (int32_t kj = 0; kj < k; ++kj) {
-        const float v = __ldg(xp + (int64_t)ki * w + kj);
-        if (v > best || v != v) best = v;
+  const int32_t k = K ? K : kr;
+  const int64_t slots = (planes + planes_per_slot - 1) / planes_per_slot;
+  const int32_t per_plane = oh * ow;
+  for (int64_t slot = blockIdx.y; slot < slots; slot += gridDim.y) {
+    const int64_t p0 = slot * planes_per_slot;
+    const int64_t outs = (min(planes, p0 + planes_per_slot) - p0) * per_plane;
+    float m = 0.0f;
+    for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < outs; i += (int64_t)gridDim.x * kThreads) {
+      // 32-bit division where the slot's output count allows it (the usual case)
+      const int64_t pl = outs < 0x7fffffff ? (int64_t)((uint32_t)i / (uint32_t)per_plane) : i / per_plane;
+      const int32_t rem = (int32_t)(i - pl * per_plane);
+      const int32_t oy = rem / ow, ox = rem - oy * ow;
+      const float* xp = x + (p0 + pl) * (int64_t)h * w + (int64_t)(oy * s) * w + ox * s;
+      float best = -INFINITY;
+      if (K) {
+        float v[K ? K * K : 1];
+#pragma unroll
+        for (int ki = 0; ki < K; ++ki)
+#pragma unroll
+          for (int kj = 0; kj < K; ++kj) v[ki * K + kj] = __ldg(xp + ki * w + kj);
+#pragma unroll
+        for (int t = 0; t < K * K; ++t)
+          if (v[t] > best || v[t] != v[t]) best = v[t];
+      } else {
+        for (int32_t ki = 0; ki < k; ++ki)
+          for (int32_t kj = 0; kj < k; ++kj) {
+            const float v = __ldg(xp + ki * w + kj);
+            if (v > best || v != v) best = v;
+          }
       }
-    y[o] = best;
-    m = fmaxf(m, fabsf(best));
+      y[(p0 + pl) * per_plane + rem] = best;
+      m = fmaxf(m, fabsf(best));
+    }
+    if (amax) {
+      block_max_to(m, amax + slot);
+      __syncthreads();  // the reduction buffer is reused by the next slot
+    }
   }
-  if (amax) block_max_to(m, amax + slot);
 }
 
 __global__ void __launch_bounds__(kThreads) k_activation(const float* __restrict__ x, int64_t n,
@@ -180,10 +201,16 @@ void launch_maxpool2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w
   if (amax.ptr && amax.elems_per_slot > 0) planes_per_slot = amax.elems_per_slot / ((int64_t)oh * ow);
   if (planes_per_slot <= 0) planes_per_slot = planes;
   const int64_t slots = (planes + planes_per_slot - 1) / planes_per_slot;
-  const int64_t per = planes_per_slot * oh * ow;
-  int bx = grid_for(per, kThreads * 4, slots > 1 ? 64 : 148 * 16);
-  dim3 grid(bx, (unsigned)slots);
-  k_maxpool2d<<<grid, kThreads, 0, st>>>(x, planes, h, w, k, s, oh, ow, y, amax.ptr, planes_per_slot);
+  const int64_t outs_per_slot = planes_per_slot * oh * ow;
+  const int64_t want = std::max<int64_t>(1, 148 * 32 / std::max<int64_t>(slots, 1));
+  const unsigned bx = (unsigned)std::max<int64_t>(1, std::min<int64_t>((outs_per_slot + kThreads - 1) / kThreads, want));
+  const dim3 grid(bx, (unsigned)std::min<int64_t>(slots, 65535));
+  if (k == 2)
+    k_maxpool2d<2><<<grid, kThreads, 0, st>>>(x, planes, h, w, k, s, oh, ow, y, amax.ptr, planes_per_slot);
+  else if (k == 3)
+    k_maxpool2d<3><<<grid, kThreads, 0, st>>>(x, planes, h, w, k, s, oh, ow, y, amax.ptr, planes_per_slot);
+  else
+    k_maxpool2d<0><<<grid, kThreads, 0, st>>>(x, planes, h, w, k, s, oh, ow, y, amax.ptr, planes_per_slot);
 }
 
 void launch_activation(const float* x, int64_t n, int32_t act, float p, float* y, AmaxSink amax,

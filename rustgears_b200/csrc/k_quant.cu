@@ -4,6 +4,8 @@
 // The reference folds max|v| serially over the whole tensor; max is exact and
 // order-free, so a parallel reduction gives the identical value.  HBM-bound:
 // 16-byte vector loads, warp-shuffle reduction, one atomic per block.
+#include <algorithm>
+
 #include "rg_kernels.h"
 #include "rg_math.cuh"
 
@@ -94,25 +96,57 @@ __global__ void __launch_bounds__(kThreads) k_quantize_rows(const float* __restr
 }
 
 // grid (blocks_per_image, n): max |x| over covered pixels of each image.
-__global__ void __launch_bounds__(kThreads) k_image_absmax(const float* __restrict__ x, int32_t c,
+// Per-image absmax.  Without coverage masks a flat strided pass over the image; with
+// them (a strided conv that skips rows / columns), a warp per (channel, row): rows
+// the conv never reads are skipped whole, lanes run along the row.  grid.y strides
+// over the images.
+__global__ void __launch_bounds__(kThreads) k_image_absmax(const float* __restrict__ x, int64_t n, int32_t c,
                                                            int32_t h, int32_t w,
                                                            const uint8_t* __restrict__ row_cov,
                                                            const uint8_t* __restrict__ col_cov,
                                                            unsigned* __restrict__ amax) {
-  const int64_t img = blockIdx.y;
   const int64_t per = (int64_t)c * h * w;
-  const float* xi = x + img * per;
-  float m = 0.0f;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < per;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    if (row_cov) {
-      const int64_t p = i % ((int64_t)h * w);
-      const int32_t iy = (int32_t)(p / w), ix = (int32_t)(p - (int64_t)iy * w);
-      if (!row_cov[iy] || !col_cov[ix]) continue;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int64_t img = blockIdx.y; img < n; img += gridDim.y) {
+    const float* xi = x + img * per;
+    float m = 0.0f;
+    if (!row_cov) {
+      for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < per; i += (int64_t)gridDim.x * blockDim.x)
+        m = fmaxf(m, fabsf(__ldg(xi + i)));
+    } else {
+      const int32_t rows = c * h;
+      for (int32_t rr = blockIdx.x * (kThreads / 32) + wid; rr < rows; rr += gridDim.x * (kThreads / 32)) {
+        if (!row_cov[rr % h]) continue;  // warp-uniform
+        const float* xr = xi + (int64_t)rr * w;
+        for (int32_t ix = lane; ix < w; ix += 32)
+          if (col_cov[ix]) m = fmaxf(m, fabsf(__ldg(xr + ix)));
+      }
     }
-    m = fmaxf(m, fabsf(__ldg(xi + i)));
+    block_max_to(m, amax + img);
+    __syncthreads();  // the reduction buffer is reused by the next image
   }
-  block_max_to(m, amax + img);
+}
+
+// NCHW f32 (c <= 4 channels) -> NHWC i8 with 4-byte pixels (zero-padded channels): a
+// thread per pixel, one 4-byte store; grid.y strides over the images.
+__global__ void __launch_bounds__(kThreads) k_image_quantize_nhwc4(const float* __restrict__ x, int64_t n,
+                                                                   int32_t c, int32_t hw,
+                                                                   const unsigned* __restrict__ amax,
+                                                                   int8_t* __restrict__ q,
+                                                                   float* __restrict__ scales) {
+  for (int64_t img = blockIdx.y; img < n; img += gridDim.y) {
+    const float scale = quant_scale(__uint_as_float(amax[img]));
+    const float inv = quant_inv(scale);
+    if (blockIdx.x == 0 && threadIdx.x == 0 && scales) scales[img] = scale;
+    const float* xi = x + img * (int64_t)c * hw;
+    uint32_t* qi = reinterpret_cast<uint32_t*>(q) + img * (int64_t)hw;
+    for (int32_t p = blockIdx.x * kThreads + threadIdx.x; p < hw; p += gridDim.x * kThreads) {
+      uint32_t wv = 0;
+      for (int32_t ch = 0; ch < c; ++ch)
+        wv |= (uint32_t)(uint8_t)(int8_t)quant1(__ldg(xi + (int64_t)ch * hw + p), inv) << (8 * ch);
+      qi[p] = wv;
+    }
+  }
 }
 
 // grid-stride over (image, pixel): NCHW f32 -> NHWC i8 (pixel stride cpad).
@@ -214,8 +248,9 @@ void launch_image_absmax(const float* x, int64_t n, int32_t c, int32_t h, int32_
                          cudaStream_t st) {
   const int64_t per = (int64_t)c * h * w;
   if (n <= 0 || per <= 0) return;
-  dim3 grid(grid_for(per, kThreads * 8, 64), (unsigned)n);
-  k_image_absmax<<<grid, kThreads, 0, st>>>(x, c, h, w, row_cov, col_cov, amax_bits);
+  const int64_t work = row_cov ? (int64_t)c * h * 32 : per;  // lanes in use per image
+  dim3 grid(grid_for(work, kThreads * 8, 64), (unsigned)std::min<int64_t>(n, 65535));
+  k_image_absmax<<<grid, kThreads, 0, st>>>(x, n, c, h, w, row_cov, col_cov, amax_bits);
 }
 
 void launch_image_quantize_nhwc(const float* x, int64_t n, int32_t c, int32_t h, int32_t w,
@@ -223,7 +258,14 @@ void launch_image_quantize_nhwc(const float* x, int64_t n, int32_t c, int32_t h,
                                 float* scales_out, cudaStream_t st) {
   const int64_t total = n * (int64_t)h * w;
   if (total <= 0) return;
-  if ((cpad & 15) == 0) {  // channel-padded layout: tiled transpose
+  if (cpad == 4 && c <= 4) {
+    const int32_t hw = h * w;
+    const dim3 grid((unsigned)std::min<int64_t>((hw + kThreads - 1) / kThreads, 64),
+                    (unsigned)std::min<int64_t>(n, 65535));
+    k_image_quantize_nhwc4<<<grid, kThreads, 0, st>>>(x, n, c, hw, amax_bits, q, scales_out);
+    return;
+  }
+  if ((cpad & 15) == 0 && n <= 65535) {  // channel-padded layout: tiled transpose (grid.z = image)
     const int32_t hw = h * w;
     dim3 grid((unsigned)((hw + 31) / 32), (unsigned)(cpad / 16), (unsigned)n);
     k_image_quantize_nhwc_tiled<<<grid, 128, 0, st>>>(x, c, hw, cpad, amax_bits, q, scales_out);

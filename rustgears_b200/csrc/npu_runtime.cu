@@ -142,7 +142,8 @@ struct Op {
   std::vector<int8_t> wq;        // reference layout: Linear [out,in]; Conv [O, C*k*k]
   std::vector<float> bias;
   int64_t kdim = 0, kpad = 0;     // GEMM reduction length and its padded device stride
-  int32_t cpad = 0;               // conv: channels per tap in the device layouts (16-aligned, or 1)
+  int32_t cpad = 0;               // conv: channels per tap in the device layouts (16-aligned, 4, or 1)
+  int32_t kxp = 0;                // conv: taps per kernel row in the K order (k; with cpad 4: a multiple of 4)
   DevBuf d_w, d_bias, d_wsc;     // device weights [N, kpad] (conv: (ky,kx,c) order)
   bool bias_finite = true;
   std::string label;
@@ -399,7 +400,7 @@ static rg_status upload_op(Op& op) {
       for (int64_t c = 0; c < C; ++c)
         for (int64_t ky = 0; ky < K; ++ky)
           for (int64_t kx = 0; kx < K; ++kx)
-            dev[(size_t)(o * op.kpad + (ky * K + kx) * CP + c)] = op.wq[(size_t)(((o * C + c) * K + ky) * K + kx)];
+            dev[(size_t)(o * op.kpad + (ky * op.kxp + kx) * CP + c)] = op.wq[(size_t)(((o * C + c) * K + ky) * K + kx)];
   }
   RG_TRY(op.d_w.ensure(dev.size()));
   RG_CUDA_TRY(cudaMemcpy(op.d_w.p, dev.data(), dev.size(), cudaMemcpyHostToDevice));
@@ -492,9 +493,12 @@ static rg_status compile(Session& s, const rg_layer_spec* layers, int32_t n) {
         op.in_c = l.in_c; op.out_c = l.out_c; op.k = l.k; op.stride = l.stride; op.pad = l.pad;
         // channels padded to 16 per tap so the tensor-core conv gathers 16-byte chunks
         // (a single channel stays unpadded: the fused CNN block reads it directly)
-        op.cpad = l.in_c == 1 ? 1 : (int32_t)round_up(l.in_c, 16);
+        // (2-4 channels, e.g. an RGB stem: a 4-byte pixel, taps per kernel row padded to a
+        // multiple of 4 so that a 16-byte chunk holds 4 taps)
+        op.cpad = l.in_c == 1 ? 1 : l.in_c <= 4 ? 4 : (int32_t)round_up(l.in_c, 16);
+        op.kxp = op.cpad == 4 ? (int32_t)round_up(l.k, 4) : l.k;
         quantize_weights(op, l.w.data(), l.out_c, (int64_t)l.in_c * l.k * l.k, s.weight_quant);
-        op.kdim = (int64_t)op.cpad * l.k * l.k;
+        op.kdim = (int64_t)op.cpad * l.k * op.kxp;
       }
       op.kpad = round_up(op.kdim, 16);
       op.bias = l.b;
@@ -924,6 +928,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
   }
 
   RG_PENDING("the first launch");
+  bool fused_residual = false;
   const float* cur = x_dev;
   int32_t launches = 0;
   s.ev_of.assign(n + 1, 0);
@@ -1025,6 +1030,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
       case RG_LAYER_CONV2D:
       case RG_LAYER_SHORTCUT_CONV2D: {
         const bool shortcut = op.kind == RG_LAYER_SHORTCUT_CONV2D;
+        fused_residual = false;
         const float* src = shortcut ? saved.back() : cur;
         unsigned* my_amax = amax + P.amax_off[i];
         float* my_scale = scales + P.amax_off[i];
@@ -1063,7 +1069,8 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
           RG_LAUNCHED("image_quantize_nhwc");
           g.a = q; g.conv = true;
           // padded channels hold zeros in both operands: the reduction runs over cpad per tap
-          g.g.h = H; g.g.w = W; g.g.c = op.cpad; g.g.cpad = op.cpad; g.g.k = op.k; g.g.stride = op.stride;
+          g.g.h = H; g.g.w = W; g.g.c = op.cpad; g.g.cpad = op.cpad; g.g.k = op.k; g.g.kxp = op.kxp;
+          g.g.stride = op.stride;
           g.g.pad = op.pad;
           g.g.oh = (int32_t)os.out[2]; g.g.ow = (int32_t)os.out[3];
           const int64_t L = os.out[2] * os.out[3];
@@ -1080,6 +1087,29 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         g.out = dst;
         g.acc = s.trace ? s.accbuf.as<int32_t>() : nullptr;
         g.amax = sink;
+        // A main-path conv right before a residual block's end takes the add (and the
+        // block's activation) into its epilogue; the add then launches nothing.
+        if (op.kind == RG_LAYER_CONV2D && !s.trace && i + 1 < n && s.ops[i + 1].kind == RG_LAYER_RESIDUAL_END &&
+            !saved.empty() && P.shapes[i + 1].in_elems == os.out_elems && conv_tc_eligible(g) &&
+            (s.ops[i + 1].act == RG_ACT_NONE || s.ops[i + 1].act == RG_ACT_RELU ||
+             s.ops[i + 1].act == RG_ACT_LEAKY_RELU)) {
+          const Op& re = s.ops[i + 1];
+          g.residual = saved.back();
+          g.res_act = re.act;
+          g.res_param = re.param;
+          if (i + 2 == n && y_dev) g.out = dst = y_dev;
+          AmaxSink rsink;
+          const int rcons = find_consumer(s, i + 1);
+          if (rcons >= 0 && P.amax_src[(size_t)rcons] == (int)(i + 1)) {
+            rsink.ptr = amax + P.amax_off[(size_t)rcons];
+            const int64_t imgs = P.shapes[(size_t)rcons].in[0];
+            rsink.elems_per_slot = (s.ops[(size_t)rcons].kind == RG_LAYER_CONV2D && imgs > 0)
+                                       ? P.shapes[(size_t)rcons].in_elems / imgs
+                                       : 0;
+          }
+          g.amax = rsink;
+          fused_residual = true;
+        }
         const bool conv_tc = g.conv && conv_tc_eligible(g);
         const bool tc = !fused_q && !g.conv && gemm_tc_eligible(g);
         const bool narrow = fused_q || (!tc && !conv_tc && gemm_narrow_eligible(g));
@@ -1212,6 +1242,12 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
     } else {
       if (record_events) RG_CUDA_TRY(record(s.events[(size_t)next_ev]));
       s.ev_of[i + 1] = next_ev++;
+    }
+    if (fused_residual) {  // the residual end ran inside the conv: 0 ns on its record
+      fused_residual = false;
+      saved.pop_back();
+      s.ev_of[i + 2] = s.ev_of[i + 1];
+      ++i;
     }
   }
   s.last.launches = launches;

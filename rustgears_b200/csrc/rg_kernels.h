@@ -37,6 +37,8 @@ void launch_nhwc_to_nchw_i8(const int8_t* q, int64_t n, int32_t c, int32_t cpad,
 // ---- GEMM (k_gemm_simt.cu, k_gemm_tc.cu) ---------------------------------------
 struct ConvGeom {      // implicit-GEMM A operand: rows = (img, oy, ox), k = (ky, kx, c)
   int32_t h = 0, w = 0, c = 0, cpad = 0, k = 0, stride = 1, pad = 0, oh = 0, ow = 0;
+  int32_t kxp = 0;     // taps per kernel row in the K order (0: k); narrow operands (cpad 4)
+                       // pad it to a multiple of 4 so that a 16-byte K chunk is 4 taps
 };
 
 struct GemmArgs {
@@ -66,6 +68,11 @@ struct GemmArgs {
   int64_t out_l = 0;               // 0: row-major [m,n]; L>0: NCHW out[(r/L)*n*L + c*L + r%L]
   int32_t* acc = nullptr;          // optional i32 dump, same layout as out
   AmaxSink amax;                   // optional absmax of out
+  // tcgen05 conv only: out = res_act(epilogue + residual), residual in out's layout
+  // (a residual block's closing add fused into the conv before it)
+  const float* residual = nullptr;
+  int32_t res_act = 0;
+  float res_param = 0.0f;
 };
 
 void launch_gemm_simt(const GemmArgs& a, cudaStream_t st);
