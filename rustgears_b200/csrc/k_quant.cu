@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(kThreads) k_image_absmax(const float* __restri
                                                            int32_t h, int32_t w,
                                                            const uint8_t* __restrict__ row_cov,
                                                            const uint8_t* __restrict__ col_cov,
-                                                           unsigned* __restrict__ amax) {
+                                                           bool cov_smem, unsigned* __restrict__ amax) {
   const int64_t per = (int64_t)c * h * w;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   for (int64_t img = blockIdx.y; img < n; img += gridDim.y) {
@@ -114,12 +114,21 @@ __global__ void __launch_bounds__(kThreads) k_image_absmax(const float* __restri
       for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < per; i += (int64_t)gridDim.x * blockDim.x)
         m = fmaxf(m, fabsf(__ldg(xi + i)));
     } else {
+      // the masks in shared memory (the launcher bounds h and w); rows the conv never
+      // reads are skipped whole
+      extern __shared__ uint8_t cov_s[];  // [h] rows then [w] columns
+      if (cov_smem) {
+        for (int32_t i = threadIdx.x; i < h + w; i += kThreads) cov_s[i] = i < h ? row_cov[i] : col_cov[i - h];
+        __syncthreads();
+      }
+      const uint8_t* rcov = cov_smem ? cov_s : row_cov;
+      const uint8_t* ccov = cov_smem ? cov_s + h : col_cov;
       const int32_t rows = c * h;
       for (int32_t rr = blockIdx.x * (kThreads / 32) + wid; rr < rows; rr += gridDim.x * (kThreads / 32)) {
-        if (!row_cov[rr % h]) continue;  // warp-uniform
+        if (!rcov[rr % h]) continue;  // warp-uniform
         const float* xr = xi + (int64_t)rr * w;
         for (int32_t ix = lane; ix < w; ix += 32)
-          if (col_cov[ix]) m = fmaxf(m, fabsf(__ldg(xr + ix)));
+          if (ccov[ix]) m = fmaxf(m, fabsf(__ldg(xr + ix)));
       }
     }
     block_max_to(m, amax + img);
@@ -208,6 +217,52 @@ __global__ void __launch_bounds__(128) k_image_quantize_nhwc_tiled(const float* 
   }
 }
 
+// The same for channel counts padded to a multiple of 64: a block quantizes 32 pixels x
+// 64 channels (8 coalesced row loads per thread in flight), and each pixel's 64 channel
+// bytes leave as four 16-byte stores (a warp writes 512 contiguous bytes when cpad = 64).
+__global__ void __launch_bounds__(256) k_image_quantize_nhwc_t64(const float* __restrict__ x, int32_t c,
+                                                                 int32_t hw, int32_t cpad,
+                                                                 const unsigned* __restrict__ amax,
+                                                                 int8_t* __restrict__ q,
+                                                                 float* __restrict__ scales) {
+  __shared__ float tile[64][33];
+  const int64_t img = blockIdx.z;
+  const int32_t p0 = blockIdx.x * 32, c0 = blockIdx.y * 64;
+  const float scale = quant_scale(__uint_as_float(amax[img]));
+  const float inv = quant_inv(scale);
+  if (scales && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) scales[img] = scale;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const float* src = x + img * (int64_t)c * hw;
+  const bool px_ok = p0 + tx < hw;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int32_t ch = c0 + ty + 8 * i;
+    tile[ty + 8 * i][tx] = (ch < c && px_ok) ? __ldg(src + (int64_t)ch * hw + p0 + tx) : 0.0f;
+  }
+  __syncthreads();
+  if (threadIdx.x < 128) {
+    const int pl = threadIdx.x >> 2, grp = threadIdx.x & 3;  // pixel in tile, 16-channel group
+    const int32_t px = p0 + pl;
+    if (px < hw) {
+      uint32_t wv[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const int cl = 16 * grp + 4 * k + b;
+          // clamped: a strided conv's scale covers only the pixels it reads
+          const int32_t v = c0 + cl < c ? quant1(tile[cl][pl], inv) : 0;
+          word |= (uint32_t)(v & 0xff) << (8 * b);
+        }
+        wv[k] = word;
+      }
+      *reinterpret_cast<uint4*>(q + (img * hw + px) * (int64_t)cpad + c0 + 16 * grp) =
+          make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    }
+  }
+}
+
 __global__ void k_nhwc_to_nchw_i8(const int8_t* __restrict__ q, int64_t n, int32_t c, int32_t cpad,
                                   int32_t hw, int8_t* __restrict__ out) {
   const int64_t total = n * (int64_t)c * hw;
@@ -250,7 +305,9 @@ void launch_image_absmax(const float* x, int64_t n, int32_t c, int32_t h, int32_
   if (n <= 0 || per <= 0) return;
   const int64_t work = row_cov ? (int64_t)c * h * 32 : per;  // lanes in use per image
   dim3 grid(grid_for(work, kThreads * 8, 64), (unsigned)std::min<int64_t>(n, 65535));
-  k_image_absmax<<<grid, kThreads, 0, st>>>(x, n, c, h, w, row_cov, col_cov, amax_bits);
+  const bool cov_smem = row_cov && h + w <= 32 * 1024;  // the masks fit the default shared memory
+  k_image_absmax<<<grid, kThreads, cov_smem ? (size_t)(h + w) : 0, st>>>(x, n, c, h, w, row_cov, col_cov,
+                                                                           cov_smem, amax_bits);
 }
 
 void launch_image_quantize_nhwc(const float* x, int64_t n, int32_t c, int32_t h, int32_t w,
@@ -263,6 +320,12 @@ void launch_image_quantize_nhwc(const float* x, int64_t n, int32_t c, int32_t h,
     const dim3 grid((unsigned)std::min<int64_t>((hw + kThreads - 1) / kThreads, 64),
                     (unsigned)std::min<int64_t>(n, 65535));
     k_image_quantize_nhwc4<<<grid, kThreads, 0, st>>>(x, n, c, hw, amax_bits, q, scales_out);
+    return;
+  }
+  if ((cpad & 63) == 0 && n <= 65535) {
+    const int32_t hw = h * w;
+    dim3 grid((unsigned)((hw + 31) / 32), (unsigned)(cpad / 64), (unsigned)n);
+    k_image_quantize_nhwc_t64<<<grid, 256, 0, st>>>(x, c, hw, cpad, amax_bits, q, scales_out);
     return;
   }
   if ((cpad & 15) == 0 && n <= 65535) {  // channel-padded layout: tiled transpose (grid.z = image)

@@ -1089,12 +1089,20 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         g.amax = sink;
         // A main-path conv right before a residual block's end takes the add (and the
         // block's activation) into its epilogue; the add then launches nothing.
-        if (op.kind == RG_LAYER_CONV2D && !s.trace && i + 1 < n && s.ops[i + 1].kind == RG_LAYER_RESIDUAL_END &&
-            !saved.empty() && P.shapes[i + 1].in_elems == os.out_elems && conv_tc_eligible(g) &&
+        // A shortcut conv right before the end does the same with the main path as its
+        // residual (the f32 add commutes): its output becomes the main path.
+        if ((op.kind == RG_LAYER_CONV2D || shortcut) && !s.trace && i + 1 < n &&
+            s.ops[i + 1].kind == RG_LAYER_RESIDUAL_END && !saved.empty() &&
+            P.shapes[i + 1].in_elems == os.out_elems && conv_tc_eligible(g) &&
             (s.ops[i + 1].act == RG_ACT_NONE || s.ops[i + 1].act == RG_ACT_RELU ||
              s.ops[i + 1].act == RG_ACT_LEAKY_RELU)) {
           const Op& re = s.ops[i + 1];
-          g.residual = saved.back();
+          g.residual = shortcut ? cur : saved.back();
+          if (shortcut) {  // the output must not overwrite the main path it adds
+            float* d2 = pick_dst(cur);
+            if (!d2) return fail(RG_ERR_UNSUPPORTED, "op %zu: residual blocks nested too deeply", i);
+            g.out = dst = d2;
+          }
           g.res_act = re.act;
           g.res_param = re.param;
           if (i + 2 == n && y_dev) g.out = dst = y_dev;
@@ -1147,7 +1155,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
                 for (int64_t p = 0; p < HW; ++p) t.aq[(size_t)((b * C + c) * HW + p)] = tmp[(size_t)((b * HW + p) * CP + c)];
           }
         }
-        if (shortcut) {
+        if (shortcut && !fused_residual) {
           saved.back() = dst;  // the shortcut replaces the saved block input
           if (s.trace) RG_TRY(d2h_vec(s.traces[i].out, dst, os.out_elems, st));
         } else {
