@@ -1,0 +1,421 @@
+// k_conv3x3.cu -- 3x3 / stride 1 / pad 1 Conv2d on the tcgen05 tensor cores as a direct
+// convolution over zero-padded input tiles (no im2col gather).
+//
+// Reference: the FusedConv2d arm of NpuProgram::execute (src/inference/npu.rs:319-383):
+// per image, im2col (kernels.rs:28-96), quantize with the image's scale, int8 GEMM with
+// the fused epilogue, NCHW f32.  The i32 sums do not depend on the reduction order, so
+// the taps may be accumulated one after the other.
+//
+// Index the zero-padded image by flat positions f = py * (W + 2) + px (py, px in the
+// padded (H + 2) x (W + 2) grid).  The output pixel centred at f reads, for tap
+// (ky, kx), the padded pixel f + (ky - 1) (W + 2) + (kx - 1): every tap's A operand is
+// the same run of 128 consecutive positions shifted by a constant.  So a CTA tile is
+// 128 consecutive centre positions of one image; the operand is stored as 16-channel
+// chunk planes [img][chunk][h][w][16 B], so per 64-channel stage 4 TMA loads (rows of
+// 16 (W + 2) contiguous bytes) bring the padded input rows the tile needs as 4 planes
+// [rows][W + 2][16 B] (out-of-range rows and columns read as zeros: the padding), and
+// the MMA warp issues 9 taps x 2 MMAs whose A descriptors point into the planes at
+// the tap's row offset (no-swizzle K-major layout with 16-byte rows: an 8-row group is
+// 128 contiguous bytes, so any row offset is a valid start).  Positions on the padding
+// columns are computed and discarded (2 of W + 2 per row).  Weights for the stage
+// arrive by one bulk copy, pre-arranged by the host in the same core-matrix layout.
+//
+//   warp 0     producer (lane 0): 4 TMA tile loads + 1 weight bulk copy per stage
+//   warp 1     MMA issuer (lane 0): 18 tcgen05.mma (M 128, K 32) per stage into one
+//              of two TMEM accumulators
+//   warps 2-17 epilogue: tcgen05.ld, act(f32(acc) * (s_img * s_w) + bias), optional
+//              fused residual add, NCHW stores, per-image absmax for the next conv
+// Every mbarrier wait is bounded; on timeout the CTA raises an abort flag, the roles
+// leave their loops, copies and MMAs in flight are drained, TMEM is freed and a device
+// error word is set for the host.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "rg_kernels.h"
+#include "rg_math.cuh"
+#include "rg_sm100.cuh"
+
+namespace rg {
+
+PFN_cuTensorMapEncodeTiled_v12000 tma_encode_fn();  // k_gemm_tc.cu
+
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128;         // centre positions per tile (TMEM lanes)
+constexpr int kCS = 64;         // channels per stage (4 chunk planes of 16 bytes)
+constexpr int kEpiWarps = 16;   // 4 per TMEM lane quadrant (the stores and residual loads are latency-bound)
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kBarBytes = 256;
+
+struct C3Params {
+  int32_t n_img, h, w, cpad, n;    // n: output channels
+  int32_t tiles_m, tiles_n, stages_k;  // tiles per image, N tiles, 64-channel stages
+  int32_t rbox;                    // padded rows per TMA box
+  int32_t plane_bytes;             // rbox * (w + 2) * 16: what one TMA load writes
+  int32_t plane_stride;            // plane_bytes rounded up to 128 (TMA destination alignment)
+  int32_t stage_bytes, ring;       // bytes per ring slot (A planes + weights), slots
+  const int8_t* wd;                // weights [tiles_n][stages_k][9][4][BN][16]
+  const float* a_scale;            // per image
+  float w_scale;
+  const float* w_scale_ch;
+  const float* bias;
+  float act_param;
+  float* out;                      // NCHW [n_img, n, h, w]
+  const float* residual;           // optional: out = res_act(epilogue + residual)
+  int32_t res_act;
+  float res_param;
+  int32_t* acc;                    // optional i32 dump, NCHW
+  unsigned* amax;                  // optional absmax sink
+  int64_t amax_per_slot;           // 0: one slot; else n * h * w (per image)
+};
+
+__device__ int g_c3_error;
+
+__device__ __forceinline__ uint64_t desc_rows16(uint32_t saddr, uint32_t lbo) {
+  // no-swizzle K-major: rows 16 bytes apart (8-row groups 128 B apart), K chunks `lbo` apart
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)(128 >> 4) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version; layout type 0 = no swizzle
+  return d;
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t c0,
+                                            int32_t c1, int32_t c2, int32_t c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, "
+      "%6}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+// tile -> (image, centre tile within the image, N tile); N tiles vary fastest so the
+// CTAs working on one image's input tile run close together (L2 reuse).
+__device__ __forceinline__ void c3_coords(int64_t tile, const C3Params& p, int32_t& img, int32_t& mt, int32_t& nb) {
+  nb = (int32_t)(tile % p.tiles_n);
+  const int64_t rest = tile / p.tiles_n;
+  mt = (int32_t)(rest % p.tiles_m);
+  img = (int32_t)(rest / p.tiles_m);
+}
+
+__device__ __forceinline__ void flush_slot_max(unsigned* base, int64_t slot, float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0 && v > 0.0f && slot >= 0) atomicMax(base + slot, __float_as_uint(v));
+}
+
+template <int BN, int ACT>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_conv3x3(const __grid_constant__ CUtensorMap map_in, const C3Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)p.ring * p.stage_bytes);
+  uint64_t* full = bars;              // [ring]
+  uint64_t* empty = bars + p.ring;    // [ring]
+  uint64_t* tfull = empty + p.ring;   // [2]
+  uint64_t* tempty = tfull + 2;       // [2]
+  uint64_t* done = tempty + 2;        // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  constexpr int kBBytes = 9 * 4 * BN * 16;
+  constexpr int kTmemCols = 2 * BN;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t num_tiles = (int64_t)p.n_img * p.tiles_m * p.tiles_n;
+  const int32_t wp = p.w + 2;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.ring; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kEpiWarps);
+    }
+    mbar_init(done, 1);
+    *abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&map_in);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      const uint32_t a_bytes = 4u * (uint32_t)p.plane_bytes;
+      const uint32_t a_span = 4u * (uint32_t)p.plane_stride;
+      uint32_t issued_parity[8];
+      bool issued[8];
+      for (int s = 0; s < 8; ++s) issued[s] = false;
+      for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int32_t img, mt, nb;
+        c3_coords(tile, p, img, mt, nb);
+        const int32_t r_lo = (BM * mt) / wp;  // first padded row the tile reads
+        for (int s = 0; s < p.stages_k; ++s) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort)) { ok = false; break; }
+          uint8_t* sa = smem + (size_t)stage * p.stage_bytes;
+          mbar_arrive_expect_tx(&full[stage], a_bytes + kBBytes);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)  // chunk plane j: channels s*64 + 16j .. +15; x from pixel -1
+            tma_load_4d(sa + j * p.plane_stride, &map_in, &full[stage], -2, r_lo - 1, s * 4 + j, img);
+          bulk_load(sa + a_span, p.wd + ((int64_t)nb * p.stages_k + s) * kBBytes, kBBytes, &full[stage]);
+          issued[stage] = true;
+          issued_parity[stage] = phase;
+          if (++stage == p.ring) { stage = 0; phase ^= 1; }
+        }
+      }
+      // drain: every copy issued must have landed before the CTA exits
+      volatile int never = 0;
+      for (int s = 0; s < p.ring; ++s)
+        if (issued[s]) mbar_wait(&full[s], issued_parity[s], &never, 200000000ull);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_i8(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int iter = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++iter) {
+        int32_t img, mt, nb;
+        c3_coords(tile, p, img, mt, nb);
+        const int32_t r_lo = (BM * mt) / wp;
+        const int32_t a_row0 = wp + 1 + BM * mt - r_lo * wp;  // centre f0 in the tile's flat rows
+        const int buf = iter & 1;
+        const uint32_t aphase = (iter >> 1) & 1;
+        if (!mbar_wait(&tempty[buf], aphase ^ 1, abort)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
+        for (int s = 0; s < p.stages_k; ++s) {
+          if (!mbar_wait(&full[stage], phase, abort)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_addr(smem + (size_t)stage * p.stage_bytes);
+          const uint32_t sb = sa + 4u * (uint32_t)p.plane_stride;
+#pragma unroll
+          for (int t = 0; t < 9; ++t) {
+            const int32_t row = a_row0 + (t / 3 - 1) * wp + (t % 3 - 1);
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk)
+              mma_i8(d_tmem, desc_rows16(sa + (uint32_t)(2 * kk * p.plane_stride + row * 16), (uint32_t)p.plane_stride),
+                     desc_rows16(sb + (uint32_t)((t * 4 + 2 * kk) * BN * 16), BN * 16), idesc,
+                     (s | t | kk) != 0);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == p.ring) { stage = 0; phase ^= 1; }
+        }
+        if (ok) mma_commit(&tfull[buf]);
+      }
+      mma_commit(done);
+      volatile int never = 0;
+      mbar_wait(done, 0, &never, 200000000ull);
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int e = warp - 2;
+    const int q = warp & 3;           // TMEM lane quadrant this warp may access
+    const int part = e >> 2;          // which quarter of the BN columns
+    constexpr int kCols = BN / (kEpiWarps / 4);
+    const int64_t hw = (int64_t)p.h * p.w;
+    int iter = 0;
+    for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++iter) {
+      int32_t img, mt, nb;
+      c3_coords(tile, p, img, mt, nb);
+      const int buf = iter & 1;
+      const uint32_t aphase = (iter >> 1) & 1;
+      const int32_t f = wp + 1 + BM * mt + q * 32 + lane;  // this lane's centre position
+      const int32_t py = f / wp, px = f - py * wp;
+      const bool valid = py >= 1 && py <= p.h && px >= 1 && px <= p.w;
+      const int64_t pix = valid ? (int64_t)(py - 1) * p.w + (px - 1) : 0;
+      const float sa = p.a_scale[img];
+      const float cs_tensor = __fmul_rn(sa, p.w_scale);
+      float* obase = p.out + (int64_t)img * p.n * hw + pix;
+      const float* rbase = p.residual ? p.residual + (int64_t)img * p.n * hw + pix : nullptr;
+      const int32_t colw = nb * BN + part * kCols;  // this warp's first column
+      // the residual values do not depend on the accumulator: their loads are in flight
+      // while the MMAs of this tile finish
+      float res[kCols];
+      if (rbase) {
+#pragma unroll
+        for (int j = 0; j < kCols; ++j)
+          res[j] = valid && colw + j < p.n ? __ldg(rbase + (int64_t)(colw + j) * hw) : 0.0f;
+      }
+      const bool got = mbar_wait(&tfull[buf], aphase, abort);
+      if (!__all_sync(0xffffffffu, got)) { *abort = 1; break; }
+      tc_fence_after();
+      float mx = 0.0f;
+#pragma unroll
+      for (int cc = 0; cc < kCols; cc += 16) {
+        uint32_t v[16];
+        __syncwarp();  // the warp-wide TMEM load runs converged
+        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + part * kCols + cc), v);
+        tmem_ld_wait();
+        const int32_t col0 = colw + cc;
+        if (valid && col0 < p.n) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int32_t c = col0 + j;
+            if (c < p.n) {
+              const float cs = p.w_scale_ch ? __fmul_rn(sa, __ldg(p.w_scale_ch + c)) : cs_tensor;
+              float o = epilogue_t<ACT>((int32_t)v[j], cs, __ldg(p.bias + c), p.act_param);
+              if (rbase) {  // the residual block's activation: none, ReLU or LeakyReLU
+                o = __fadd_rn(o, res[cc + j]);
+                if (p.res_act == ACT_RELU) o = fmaxf(o, 0.0f);
+                else if (p.res_act == ACT_LEAKY_RELU) o = o > 0.0f ? o : __fmul_rn(p.res_param, o);
+              }
+              obase[(int64_t)c * hw] = o;
+              if (p.acc) p.acc[(int64_t)img * p.n * hw + (int64_t)c * hw + pix] = (int32_t)v[j];
+              mx = fmaxf(mx, fabsf(o));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+      if (p.amax) flush_slot_max(p.amax, p.amax_per_slot ? img : 0, mx);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort) atomicExch(&g_c3_error, 1);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// Input map: chunk-planar i8 [n][cpad / 16][h][w][16 B] as 4 dims of 8-byte elements
+// (2w, h, chunks, n); boxes of one chunk plane x rbox rows x (w + 2) pixels, starting one
+// pixel (two elements, 16 bytes) left of the image.
+bool make_in_map(CUtensorMap* map, const void* base, int32_t n, int32_t h, int32_t w, int32_t cpad, int32_t rbox) {
+  auto fn = tma_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)2 * w, (cuuint64_t)h, (cuuint64_t)(cpad / 16), (cuuint64_t)n};
+  cuuint64_t strides[3] = {(cuuint64_t)16 * w, (cuuint64_t)16 * w * h, (cuuint64_t)16 * w * h * (cpad / 16)};
+  cuuint32_t box[4] = {(cuuint32_t)(2 * (w + 2)), (cuuint32_t)rbox, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int ACT>
+bool launch_bn(const GemmArgs& a, const int8_t* wd, int num_sms, cudaStream_t st) {
+  const int32_t W = a.g.w, H = a.g.h, wp = W + 2;
+  C3Params p;
+  p.n_img = (int32_t)(a.m / ((int64_t)H * W));
+  p.h = H; p.w = W; p.cpad = a.g.cpad; p.n = (int32_t)a.n;
+  p.tiles_m = (H * wp - 2 + BM - 1) / BM;
+  p.tiles_n = (int32_t)((a.n + BN - 1) / BN);
+  p.stages_k = a.g.cpad / kCS;
+  p.rbox = (3 * W + 134) / wp + 1;
+  p.plane_bytes = p.rbox * wp * 16;
+  p.plane_stride = (p.plane_bytes + 127) / 128 * 128;
+  const int a_bytes = 4 * p.plane_stride;
+  p.stage_bytes = (a_bytes + 9 * 4 * BN * 16 + 1023) / 1024 * 1024;
+  p.ring = (227 * 1024 - 1024 - kBarBytes) / p.stage_bytes;
+  if (p.ring > 8) p.ring = 8;
+  if (p.ring < 2) return false;
+  const int smem = 1024 + p.ring * p.stage_bytes + kBarBytes;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaFuncSetAttribute(k_conv3x3<BN, ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  });
+  CUtensorMap mi;
+  if (!make_in_map(&mi, a.a, p.n_img, H, W, a.g.cpad, p.rbox)) return false;
+  p.wd = wd;
+  p.a_scale = a.a_scale; p.w_scale = a.w_scale; p.w_scale_ch = a.w_scale_ch; p.bias = a.bias;
+  p.act_param = a.act_param; p.out = a.out; p.acc = a.acc;
+  p.residual = a.residual; p.res_act = a.res_act; p.res_param = a.res_param;
+  p.amax = a.amax.ptr; p.amax_per_slot = a.amax.elems_per_slot;
+  const int64_t tiles = (int64_t)p.n_img * p.tiles_m * p.tiles_n;
+  const int grid = tiles < num_sms ? (int)tiles : num_sms;
+  k_conv3x3<BN, ACT><<<grid, kThreads, smem, st>>>(mi, p);
+  return true;
+}
+
+template <int BN>
+bool launch_act(const GemmArgs& a, const int8_t* wd, int num_sms, cudaStream_t st) {
+  switch (a.act) {
+    case ACT_NONE: return launch_bn<BN, ACT_NONE>(a, wd, num_sms, st);
+    case ACT_RELU: return launch_bn<BN, ACT_RELU>(a, wd, num_sms, st);
+    case ACT_SIGMOID: return launch_bn<BN, ACT_SIGMOID>(a, wd, num_sms, st);
+    case ACT_TANH: return launch_bn<BN, ACT_TANH>(a, wd, num_sms, st);
+    case ACT_GELU: return launch_bn<BN, ACT_GELU>(a, wd, num_sms, st);
+    case ACT_LEAKY_RELU: return launch_bn<BN, ACT_LEAKY_RELU>(a, wd, num_sms, st);
+    default: return false;
+  }
+}
+
+}  // namespace
+
+int conv3x3_bn(int32_t out_channels) { return out_channels >= 128 ? 128 : 64; }
+
+bool conv3x3_shape_ok(int64_t n_img, int32_t h, int32_t w, int32_t cpad, int32_t k, int32_t stride, int32_t pad,
+                      int32_t out_channels) {
+  if (k != 3 || stride != 1 || pad != 1 || (cpad & 63) || out_channels < 16 || n_img > 65535) return false;
+  if (2 * (w + 2) > 256 || (3 * w + 134) / (w + 2) + 1 > 256) return false;  // box extents
+  if (n_img * h * w * (int64_t)out_channels * 9 * cpad < (int64_t)1 << 22) return false;
+  return tma_encode_fn() != nullptr;
+}
+
+bool conv3x3_eligible(const GemmArgs& a) {
+  if (!a.conv || a.out_l <= 0 || a.rows_per_scale != a.out_l) return false;
+  if (a.g.c != a.g.cpad || a.g.oh != a.g.h || a.g.ow != a.g.w) return false;
+  if (!conv3x3_shape_ok(a.m / a.out_l, a.g.h, a.g.w, a.g.cpad, a.g.k, a.g.stride, a.g.pad, (int32_t)a.n)) return false;
+  if (a.amax.ptr && a.amax.elems_per_slot != 0 && a.amax.elems_per_slot != a.n * a.out_l) return false;
+  if (reinterpret_cast<uintptr_t>(a.a) & 15) return false;
+  if (a.m * a.n * a.k < (int64_t)1 << 22) return false;
+  return tma_encode_fn() != nullptr;
+}
+
+// Host-side weight arrangement: w [N][C * 9] (reference order c, ky, kx) quantized ->
+// [tiles_n][C / 64][9 taps][4 chunks][BN rows][16 B], zero-padded rows past N.
+void conv3x3_arrange_weights(const int8_t* wq, int32_t n, int32_t c, int32_t cpad, int8_t* out) {
+  const int32_t bn = conv3x3_bn(n), tiles_n = (n + bn - 1) / bn, sk = cpad / kCS;
+  const size_t per = (size_t)9 * 4 * bn * 16;
+  memset(out, 0, per * sk * tiles_n);
+  for (int32_t o = 0; o < n; ++o) {
+    const int32_t nb = o / bn, r = o % bn;
+    for (int32_t ch = 0; ch < c; ++ch) {
+      const int32_t s = ch / kCS, j = (ch % kCS) / 16, b = ch % 16;
+      for (int32_t t = 0; t < 9; ++t)
+        out[((size_t)nb * sk + s) * per + (((size_t)t * 4 + j) * bn + r) * 16 + b] = wq[((size_t)o * c + ch) * 9 + t];
+    }
+  }
+}
+
+size_t conv3x3_weight_bytes(int32_t n, int32_t cpad) {
+  const int32_t bn = conv3x3_bn(n);
+  return (size_t)((n + bn - 1) / bn) * (cpad / kCS) * 9 * 4 * bn * 16;
+}
+
+bool launch_conv3x3(const GemmArgs& a, const int8_t* wd, int num_sms, cudaStream_t st) {
+  return conv3x3_bn((int32_t)a.n) == 128 ? launch_act<128>(a, wd, num_sms, st) : launch_act<64>(a, wd, num_sms, st);
+}
+
+int conv3x3_take_error() {
+  int h = 0, z = 0;
+  if (cudaMemcpyFromSymbol(&h, g_c3_error, sizeof h) != cudaSuccess) return -1;
+  if (h) cudaMemcpyToSymbol(g_c3_error, &z, sizeof z);
+  return h;
+}
+
+}  // namespace rg

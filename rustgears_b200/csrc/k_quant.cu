@@ -220,8 +220,9 @@ __global__ void __launch_bounds__(128) k_image_quantize_nhwc_tiled(const float* 
 // The same for channel counts padded to a multiple of 64: a block quantizes 32 pixels x
 // 64 channels (8 coalesced row loads per thread in flight), and each pixel's 64 channel
 // bytes leave as four 16-byte stores (a warp writes 512 contiguous bytes when cpad = 64).
+// planar: write [img][cpad / 16][hw][16] (16-channel chunk planes) instead of NHWC.
 __global__ void __launch_bounds__(256) k_image_quantize_nhwc_t64(const float* __restrict__ x, int32_t c,
-                                                                 int32_t hw, int32_t cpad,
+                                                                 int32_t hw, int32_t cpad, bool planar,
                                                                  const unsigned* __restrict__ amax,
                                                                  int8_t* __restrict__ q,
                                                                  float* __restrict__ scales) {
@@ -257,8 +258,9 @@ __global__ void __launch_bounds__(256) k_image_quantize_nhwc_t64(const float* __
         }
         wv[k] = word;
       }
-      *reinterpret_cast<uint4*>(q + (img * hw + px) * (int64_t)cpad + c0 + 16 * grp) =
-          make_uint4(wv[0], wv[1], wv[2], wv[3]);
+      const int64_t off = planar ? ((img * (cpad / 16) + (c0 / 16 + grp)) * (int64_t)hw + px) * 16
+                                 : (img * hw + px) * (int64_t)cpad + c0 + 16 * grp;
+      *reinterpret_cast<uint4*>(q + off) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
     }
   }
 }
@@ -310,6 +312,14 @@ void launch_image_absmax(const float* x, int64_t n, int32_t c, int32_t h, int32_
                                                                            cov_smem, amax_bits);
 }
 
+void launch_image_quantize_planar16(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t cpad,
+                                    const unsigned* amax_bits, int8_t* q, float* scales_out, cudaStream_t st) {
+  const int32_t hw = h * w;
+  if (n <= 0 || hw <= 0) return;
+  dim3 grid((unsigned)((hw + 31) / 32), (unsigned)(cpad / 64), (unsigned)n);
+  k_image_quantize_nhwc_t64<<<grid, 256, 0, st>>>(x, c, hw, cpad, true, amax_bits, q, scales_out);
+}
+
 void launch_image_quantize_nhwc(const float* x, int64_t n, int32_t c, int32_t h, int32_t w,
                                 int32_t cpad, const unsigned* amax_bits, int8_t* q,
                                 float* scales_out, cudaStream_t st) {
@@ -325,7 +335,7 @@ void launch_image_quantize_nhwc(const float* x, int64_t n, int32_t c, int32_t h,
   if ((cpad & 63) == 0 && n <= 65535) {
     const int32_t hw = h * w;
     dim3 grid((unsigned)((hw + 31) / 32), (unsigned)(cpad / 64), (unsigned)n);
-    k_image_quantize_nhwc_t64<<<grid, 256, 0, st>>>(x, c, hw, cpad, amax_bits, q, scales_out);
+    k_image_quantize_nhwc_t64<<<grid, 256, 0, st>>>(x, c, hw, cpad, false, amax_bits, q, scales_out);
     return;
   }
   if ((cpad & 15) == 0 && n <= 65535) {  // channel-padded layout: tiled transpose (grid.z = image)

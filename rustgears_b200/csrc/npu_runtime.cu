@@ -145,6 +145,7 @@ struct Op {
   int32_t cpad = 0;               // conv: channels per tap in the device layouts (16-aligned, 4, or 1)
   int32_t kxp = 0;                // conv: taps per kernel row in the K order (k; with cpad 4: a multiple of 4)
   DevBuf d_w, d_bias, d_wsc;     // device weights [N, kpad] (conv: (ky,kx,c) order)
+  DevBuf d_w3;                   // 3x3 / stride 1 convs: the direct kernel's weight arrangement
   bool bias_finite = true;
   std::string label;
   // transformer extension: the INT8 Linears inside an op (attention: fused QKV
@@ -404,6 +405,12 @@ static rg_status upload_op(Op& op) {
   }
   RG_TRY(op.d_w.ensure(dev.size()));
   RG_CUDA_TRY(cudaMemcpy(op.d_w.p, dev.data(), dev.size(), cudaMemcpyHostToDevice));
+  if (op.kind == RG_LAYER_CONV2D && op.k == 3 && op.stride == 1 && op.pad == 1 && op.cpad % 64 == 0) {
+    std::vector<int8_t> w3(conv3x3_weight_bytes(op.out_c, op.cpad));
+    conv3x3_arrange_weights(op.wq.data(), op.out_c, op.in_c, op.cpad, w3.data());
+    RG_TRY(op.d_w3.ensure(w3.size()));
+    RG_CUDA_TRY(cudaMemcpy(op.d_w3.p, w3.data(), w3.size(), cudaMemcpyHostToDevice));
+  }
   RG_TRY(op.d_bias.ensure(op.bias.size() * sizeof(float)));
   RG_CUDA_TRY(cudaMemcpy(op.d_bias.p, op.bias.data(), op.bias.size() * sizeof(float), cudaMemcpyHostToDevice));
   if (!op.w_scale_ch.empty()) {
@@ -1031,6 +1038,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
       case RG_LAYER_SHORTCUT_CONV2D: {
         const bool shortcut = op.kind == RG_LAYER_SHORTCUT_CONV2D;
         fused_residual = false;
+        bool use3 = false;
         const float* src = shortcut ? saved.back() : cur;
         unsigned* my_amax = amax + P.amax_off[i];
         float* my_scale = scales + P.amax_off[i];
@@ -1064,9 +1072,13 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
           const int64_t N = os.in[0];
           const int32_t C = op.in_c, H = (int32_t)os.in[2], W = (int32_t)os.in[3];
           if (P.amax_src[i] < 0) { launch_image_absmax(src, N, C, H, W, rc[i], cc[i], my_amax, st); ++launches; RG_LAUNCHED("image_absmax"); }
-          launch_image_quantize_nhwc(src, N, C, H, W, op.cpad, my_amax, q, my_scale, st);
+          // the direct 3x3 kernel reads 16-channel chunk planes; every other conv, NHWC
+          use3 = op.kind == RG_LAYER_CONV2D && op.d_w3.p && !s.trace &&
+                 conv3x3_shape_ok(N, H, W, op.cpad, op.k, op.stride, op.pad, op.out_c);
+          if (use3) launch_image_quantize_planar16(src, N, C, H, W, op.cpad, my_amax, q, my_scale, st);
+          else launch_image_quantize_nhwc(src, N, C, H, W, op.cpad, my_amax, q, my_scale, st);
           ++launches;
-          RG_LAUNCHED("image_quantize_nhwc");
+          RG_LAUNCHED("image_quantize");
           g.a = q; g.conv = true;
           // padded channels hold zeros in both operands: the reduction runs over cpad per tap
           g.g.h = H; g.g.w = W; g.g.c = op.cpad; g.g.cpad = op.cpad; g.g.k = op.k; g.g.kxp = op.kxp;
@@ -1093,7 +1105,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         // residual (the f32 add commutes): its output becomes the main path.
         if ((op.kind == RG_LAYER_CONV2D || shortcut) && !s.trace && i + 1 < n &&
             s.ops[i + 1].kind == RG_LAYER_RESIDUAL_END && !saved.empty() &&
-            P.shapes[i + 1].in_elems == os.out_elems && conv_tc_eligible(g) &&
+            P.shapes[i + 1].in_elems == os.out_elems && (use3 ? conv3x3_eligible(g) : conv_tc_eligible(g)) &&
             (s.ops[i + 1].act == RG_ACT_NONE || s.ops[i + 1].act == RG_ACT_RELU ||
              s.ops[i + 1].act == RG_ACT_LEAKY_RELU)) {
           const Op& re = s.ops[i + 1];
@@ -1118,10 +1130,15 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
           g.amax = rsink;
           fused_residual = true;
         }
-        const bool conv_tc = g.conv && conv_tc_eligible(g);
+        if (use3 && (!conv3x3_eligible(g) || !launch_conv3x3(g, op.d_w3.as<int8_t>(), s.num_sms, st)))
+          return fail(RG_ERR_CUDA, "op %zu: the direct 3x3 conv could not be launched", i);
+        const bool conv3 = use3;
+        const bool conv_tc = !conv3 && g.conv && conv_tc_eligible(g);
         const bool tc = !fused_q && !g.conv && gemm_tc_eligible(g);
         const bool narrow = fused_q || (!tc && !conv_tc && gemm_narrow_eligible(g));
-        if (conv_tc) {
+        if (conv3) {
+          s.used_tc = true;
+        } else if (conv_tc) {
           if (!launch_conv_tc(g, s.num_sms, st)) return fail(RG_ERR_CUDA, "op %zu: TMA descriptor encoding failed", i);
           s.used_tc = true;
         } else if (tc) {
@@ -1133,7 +1150,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
           launch_gemm_simt(g, st);
         }
         ++launches;
-        RG_LAUNCHED(conv_tc ? "conv_tc" : tc ? "gemm_tc" : narrow ? "gemm_narrow" : "gemm_simt");
+        RG_LAUNCHED(conv3 ? "conv3x3" : conv_tc ? "conv_tc" : tc ? "gemm_tc" : narrow ? "gemm_narrow" : "gemm_simt");
         if (s.trace) {
           TraceRec& t = s.traces[i];
           RG_TRY(d2h_vec(t.scales, my_scale, P.amax_slots[i], st));
@@ -1629,7 +1646,8 @@ static rg_status run_impl(rg_session* h, const float* x, bool x_host, const int6
   RG_CUDA_TRY(cudaStreamSynchronize(st));
   if (s.used_tc) {
     s.used_tc = false;
-    if (gemm_tc_take_error() != 0 || convblock_take_error() != 0 || conv_tc_take_error() != 0)
+    if (gemm_tc_take_error() != 0 || convblock_take_error() != 0 || conv_tc_take_error() != 0 ||
+        conv3x3_take_error() != 0)
       return fail(RG_ERR_TIMEOUT, "a tensor-core kernel gave up on a bounded wait; results are invalid");
   }
   if (s.used_embed) {

@@ -30,6 +30,10 @@ void launch_image_absmax(const float* x, int64_t n, int32_t c, int32_t h, int32_
 void launch_image_quantize_nhwc(const float* x, int64_t n, int32_t c, int32_t h, int32_t w,
                                 int32_t cpad, const unsigned* amax_bits, int8_t* q,
                                 float* scales_out, cudaStream_t st);
+// The same scale, written as 16-channel chunk planes [n][cpad / 16][h * w][16] (cpad a
+// multiple of 64, n <= 65535): the input layout of the direct 3x3 conv.
+void launch_image_quantize_planar16(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t cpad,
+                                    const unsigned* amax_bits, int8_t* q, float* scales_out, cudaStream_t st);
 // NHWC i8 (cpad) -> NCHW i8 (c) for traces.
 void launch_nhwc_to_nchw_i8(const int8_t* q, int64_t n, int32_t c, int32_t cpad, int32_t h,
                             int32_t w, int8_t* out, cudaStream_t st);
@@ -89,6 +93,19 @@ bool launch_gemm_tc(const GemmArgs& a, int num_sms, cudaStream_t st);
 bool conv_tc_eligible(const GemmArgs& a);
 bool launch_conv_tc(const GemmArgs& a, int num_sms, cudaStream_t st);
 int conv_tc_take_error();
+// 3x3 / stride 1 / pad 1 convs (channels padded to a multiple of 64) as a direct
+// convolution over zero-padded TMA input tiles of the chunk-planar operand
+// (launch_image_quantize_planar16); weights pre-arranged by
+// conv3x3_arrange_weights into conv3x3_weight_bytes(n, cpad) bytes.  launch() returns
+// false when the tensor map could not be encoded (nothing was launched).
+bool conv3x3_eligible(const GemmArgs& a);
+// The shape test of conv3x3_eligible, before the operand is quantized (which layout).
+bool conv3x3_shape_ok(int64_t n_img, int32_t h, int32_t w, int32_t cpad, int32_t k, int32_t stride, int32_t pad,
+                      int32_t out_channels);
+size_t conv3x3_weight_bytes(int32_t n, int32_t cpad);
+void conv3x3_arrange_weights(const int8_t* wq, int32_t n, int32_t c, int32_t cpad, int8_t* out);
+bool launch_conv3x3(const GemmArgs& a, const int8_t* wd, int num_sms, cudaStream_t st);
+int conv3x3_take_error();
 // Reads and clears the device error word the tcgen05 kernels set when a bounded
 // wait gave up (synchronous; 0 = no error).
 int gemm_tc_take_error();

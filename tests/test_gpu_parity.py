@@ -312,3 +312,23 @@ def test_residual_ir_errors(gpu):
          S.ResidualEnd()], ExecutionProvider.npu_int8())
     with pytest.raises(_native.RgError):
         sess.run(np.zeros((1, 4, 5, 5), np.float32))
+
+
+@pytest.mark.parametrize("b,c,n,h,w,act", [(2, 64, 64, 56, 56, 1), (3, 128, 80, 13, 9, 0), (1, 64, 256, 7, 7, 4),
+                                           (2, 192, 64, 5, 31, 1), (4, 64, 128, 1, 1, 0), (1, 64, 64, 3, 120, 5)])
+def test_direct_3x3_conv(gpu, oracle_lib, b, c, n, h, w, act):
+    """3x3 / stride 1 / pad 1 convs with channels padded to a multiple of 64 run on the
+    direct kernel (zero-padded TMA tiles, shifted A operands): every shape class against
+    the oracle, with and without a residual block around it."""
+    rng = np.random.default_rng(b * 1000 + c + n + h * w)
+    wgt = (rng.standard_normal((n, c, 3, 3)) * 0.05).astype(np.float32)
+    bias = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    x = rng.standard_normal((b, c, h, w)).astype(np.float32)
+    conv = dict(kind=oracle.CONV2D, in_channels=c, out_channels=n, kernel=3, stride=1, padding=1, weight=wgt, bias=bias)
+    layers = [conv] + ([dict(kind=oracle.ACTIVATION, act=act, act_param=0.1)] if act else [])
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
+    assert_same(session_for(layers).run(x), ref, f"conv {c}->{n} {h}x{w}")
+    if n == c:  # a residual block around it: the add fused into the conv's epilogue
+        blk = [dict(kind=oracle.RESIDUAL_BEGIN), conv, dict(kind=oracle.RESIDUAL_END, act=1, act_param=0.0)]
+        ref2, _, _ = oracle.Program(blk).execute(x, nthreads=8)
+        assert_same(session_for(blk).run(x), ref2, "residual")
