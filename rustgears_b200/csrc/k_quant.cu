@@ -158,6 +158,39 @@ __global__ void __launch_bounds__(kThreads) k_image_quantize_nhwc4(const float* 
   }
 }
 
+// NCHW f32 (c <= 4 channels, even h and w) -> space-to-depth i8 pixels [n][h/2][w/2][16 B]:
+// byte (dy * 2 + dx) * 4 + ch of s2d pixel (sy, sx) = channel ch of pixel (2 sy + dy,
+// 2 sx + dx), zero for ch >= c.  A thread per s2d pixel, one 16-byte store; grid.y
+// strides over the images.
+__global__ void __launch_bounds__(kThreads) k_image_quantize_s2d(const float* __restrict__ x, int64_t n,
+                                                                 int32_t c, int32_t h, int32_t w,
+                                                                 const unsigned* __restrict__ amax,
+                                                                 int8_t* __restrict__ q,
+                                                                 float* __restrict__ scales) {
+  const int32_t w2 = w / 2, hw2 = (h / 2) * w2;
+  const int32_t hw = h * w;
+  for (int64_t img = blockIdx.y; img < n; img += gridDim.y) {
+    const float scale = quant_scale(__uint_as_float(amax[img]));
+    const float inv = quant_inv(scale);
+    if (blockIdx.x == 0 && threadIdx.x == 0 && scales) scales[img] = scale;
+    const float* xi = x + img * (int64_t)c * hw;
+    uint4* qi = reinterpret_cast<uint4*>(q) + img * (int64_t)hw2;
+    for (int32_t p = blockIdx.x * kThreads + threadIdx.x; p < hw2; p += gridDim.x * kThreads) {
+      const int32_t sy = p / w2, sx = p - sy * w2;
+      uint32_t wv[4] = {0u, 0u, 0u, 0u};
+      for (int32_t ch = 0; ch < c; ++ch) {
+        const float* r0 = xi + (int64_t)ch * hw + (2 * sy) * w + 2 * sx;
+        const float v00 = __ldg(r0), v01 = __ldg(r0 + 1), v10 = __ldg(r0 + w), v11 = __ldg(r0 + w + 1);
+        wv[0] |= (uint32_t)(uint8_t)(int8_t)quant1(v00, inv) << (8 * ch);
+        wv[1] |= (uint32_t)(uint8_t)(int8_t)quant1(v01, inv) << (8 * ch);
+        wv[2] |= (uint32_t)(uint8_t)(int8_t)quant1(v10, inv) << (8 * ch);
+        wv[3] |= (uint32_t)(uint8_t)(int8_t)quant1(v11, inv) << (8 * ch);
+      }
+      qi[p] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    }
+  }
+}
+
 // grid-stride over (image, pixel): NCHW f32 -> NHWC i8 (pixel stride cpad).
 __global__ void __launch_bounds__(kThreads) k_image_quantize_nhwc(const float* __restrict__ x, int64_t n,
                                                                   int32_t c, int32_t hw, int32_t cpad,
@@ -318,6 +351,15 @@ void launch_image_quantize_planar16(const float* x, int64_t n, int32_t c, int32_
   if (n <= 0 || hw <= 0) return;
   dim3 grid((unsigned)((hw + 31) / 32), (unsigned)(cpad / 64), (unsigned)n);
   k_image_quantize_nhwc_t64<<<grid, 256, 0, st>>>(x, c, hw, cpad, true, amax_bits, q, scales_out);
+}
+
+void launch_image_quantize_s2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, const unsigned* amax_bits,
+                               int8_t* q, float* scales_out, cudaStream_t st) {
+  const int32_t hw2 = (h / 2) * (w / 2);
+  if (n <= 0 || hw2 <= 0) return;
+  const dim3 grid((unsigned)std::min<int64_t>((hw2 + kThreads - 1) / kThreads, 64),
+                  (unsigned)std::min<int64_t>(n, 65535));
+  k_image_quantize_s2d<<<grid, kThreads, 0, st>>>(x, n, c, h, w, amax_bits, q, scales_out);
 }
 
 void launch_image_quantize_nhwc(const float* x, int64_t n, int32_t c, int32_t h, int32_t w,

@@ -146,6 +146,7 @@ struct Op {
   int32_t kxp = 0;                // conv: taps per kernel row in the K order (k; with cpad 4: a multiple of 4)
   DevBuf d_w, d_bias, d_wsc;     // device weights [N, kpad] (conv: (ky,kx,c) order)
   DevBuf d_w3;                   // 3x3 / stride 1 convs: the direct kernel's weight arrangement
+  DevBuf d_ws;                   // 7x7 / stride 2 stems (<= 4 channels -> 64): the fused stem's arrangement
   bool bias_finite = true;
   std::string label;
   // transformer extension: the INT8 Linears inside an op (attention: fused QKV
@@ -410,6 +411,12 @@ static rg_status upload_op(Op& op) {
     conv3x3_arrange_weights(op.wq.data(), op.out_c, op.in_c, op.cpad, w3.data());
     RG_TRY(op.d_w3.ensure(w3.size()));
     RG_CUDA_TRY(cudaMemcpy(op.d_w3.p, w3.data(), w3.size(), cudaMemcpyHostToDevice));
+  }
+  if (op.kind == RG_LAYER_CONV2D && op.k == 7 && op.stride == 2 && op.pad == 3 && op.in_c <= 4 && op.out_c == 64) {
+    std::vector<int8_t> ws(stem_weight_bytes());
+    stem_arrange_weights(op.wq.data(), op.in_c, ws.data());
+    RG_TRY(op.d_ws.ensure(ws.size()));
+    RG_CUDA_TRY(cudaMemcpy(op.d_ws.p, ws.data(), ws.size(), cudaMemcpyHostToDevice));
   }
   RG_TRY(op.d_bias.ensure(op.bias.size() * sizeof(float)));
   RG_CUDA_TRY(cudaMemcpy(op.d_bias.p, op.bias.data(), op.bias.size() * sizeof(float), cudaMemcpyHostToDevice));
@@ -702,6 +709,7 @@ struct RunPlan {
   int64_t total_slots = 0;
   size_t cov_bytes = 0;
   std::vector<uint8_t> block_start;  // op i starts a fused Conv-Pool-Conv-Pool block
+  std::vector<uint8_t> stem_start;   // op i is a 7x7 / 2 stem conv fused with the MaxPool(3, 2) after it
 };
 
 // Ops that leave the main-path tensor as it is (reshape, saving a block input, a
@@ -732,6 +740,17 @@ static bool block_at(const Session& s, const std::vector<OpShape>& shapes, size_
   const std::vector<int64_t>& in = shapes[i].in;
   return in.size() == 4 &&
          convblock_supported((int)in[1], c1.out_c, c2.out_c, (int)in[2], (int)in[3], c1.act, c2.act);
+}
+
+// ops[i..i+1] = Conv(k7 s2 p3, <= 4 -> 64 channels) MaxPool(3, 2): the fused stem.
+static bool stem_at(const Session& s, const std::vector<OpShape>& shapes, size_t i) {
+  if (i + 1 >= s.ops.size() || s.trace || (s.flags & RG_SESSION_NO_FUSION)) return false;
+  const Op& c = s.ops[i];
+  const Op& m = s.ops[i + 1];
+  if (c.kind != RG_LAYER_CONV2D || !c.d_ws.p || m.kind != RG_LAYER_MAXPOOL2D) return false;
+  const std::vector<int64_t>& in = shapes[i].in;
+  return in.size() == 4 && stem_pool_shape_ok(in[0], (int32_t)in[1], (int32_t)in[2], (int32_t)in[3], c.k, c.stride,
+                                               c.pad, c.out_c, m.k, m.stride);
 }
 
 static rg_status make_plan(const Session& s, const int64_t* shape, int32_t ndim, RunPlan& P) {
@@ -775,10 +794,14 @@ static rg_status make_plan(const Session& s, const int64_t* shape, int32_t ndim,
   }
   P.total_slots = off;
   P.block_start.assign(n, 0);
+  P.stem_start.assign(n, 0);
   for (size_t i = 0; i < n; ++i)
     if (block_at(s, P.shapes, i)) {
       P.block_start[i] = 1;
       i += 3;
+    } else if (stem_at(s, P.shapes, i)) {
+      P.stem_start[i] = 1;
+      ++i;
     }
   return RG_OK;
 }
@@ -867,7 +890,8 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
     if (op.kind == RG_LAYER_LINEAR) max_q = std::max(max_q, P.shapes[i].in_elems / op.in_f * op.kpad);
     if (op.kind == RG_LAYER_CONV2D || op.kind == RG_LAYER_SHORTCUT_CONV2D) {
       const std::vector<int64_t>& in = P.shapes[i].in;  // NHWC with channels padded to cpad
-      max_q = std::max(max_q, in[0] * in[2] * in[3] * op.cpad);
+      // (the fused stem's space-to-depth operand: 16 bytes per 2 x 2 pixels)
+      max_q = std::max(max_q, in[0] * in[2] * in[3] * std::max<int64_t>(op.cpad, P.stem_start[i] ? 4 : 0));
     }
     if (op.kind == RG_LAYER_ATTENTION || op.kind == RG_LAYER_SWIGLU) {
       const int64_t rows = P.shapes[i].in_elems / op.in_f;
@@ -1019,6 +1043,53 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
       s.ev_of[i + 1] = next_ev++;
       for (size_t j = i + 2; j <= i + 4; ++j) s.ev_of[j] = s.ev_of[i + 1];
       i += 3;
+      continue;
+    }
+    if (P.stem_start[i] && os.in_elems > 0) {
+      // Conv(7x7 / 2) + act + MaxPool(3, 2) in one kernel; its time is recorded on the conv.
+      const Op& mp = s.ops[i + 1];
+      unsigned* my_amax = amax + P.amax_off[i];
+      float* my_scale = scales + P.amax_off[i];
+      const int64_t N = os.in[0];
+      const int32_t C = (int32_t)os.in[1], H = (int32_t)os.in[2], W = (int32_t)os.in[3];
+      if (P.amax_src[i] < 0) {
+        launch_image_absmax(cur, N, C, H, W, rc[i], cc[i], my_amax, st);
+        ++launches;
+        RG_LAUNCHED("image_absmax");
+      }
+      int8_t* q = s.qbuf.as<int8_t>();
+      if (s.qbuf.bytes < (size_t)(N * H * W * 4))
+        return fail(RG_ERR_UNSUPPORTED, "op %zu: the quantized-operand buffer is too small for the stem", i);
+      launch_image_quantize_s2d(cur, N, C, H, W, my_amax, q, my_scale, st);
+      ++launches;
+      RG_LAUNCHED("image_quantize_s2d");
+      StemPoolArgs sp;
+      sp.q = q; sp.n = N; sp.h = H; sp.w = W;
+      sp.wd = op.d_ws.as<int8_t>();
+      sp.a_scale = my_scale; sp.w_scale = op.w_scale;
+      sp.w_scale_ch = op.w_scale_ch.empty() ? nullptr : op.d_wsc.as<float>();
+      sp.bias = op.d_bias.as<float>();
+      sp.act = op.act; sp.act_param = op.param;
+      sp.out = (i + 2 == n && y_dev) ? y_dev : dst;
+      const int pcons = find_consumer(s, i + 1);
+      if (pcons >= 0 && P.amax_src[(size_t)pcons] == (int)(i + 1)) {
+        sp.amax.ptr = amax + P.amax_off[(size_t)pcons];
+        const int64_t imgs = P.shapes[(size_t)pcons].in[0];
+        sp.amax.elems_per_slot = (s.ops[(size_t)pcons].kind == RG_LAYER_CONV2D && imgs > 0)
+                                     ? P.shapes[(size_t)pcons].in_elems / imgs
+                                     : 0;
+      }
+      if (!launch_stem_pool(sp, s.num_sms, st))
+        return fail(RG_ERR_CUDA, "op %zu: the fused stem could not be launched", i);
+      ++launches;
+      RG_LAUNCHED("stem_pool");
+      s.used_tc = true;
+      cur = sp.out;
+      (void)mp;
+      if (record_events) RG_CUDA_TRY(record(s.events[(size_t)next_ev]));
+      s.ev_of[i + 1] = next_ev++;
+      s.ev_of[i + 2] = s.ev_of[i + 1];
+      i += 1;
       continue;
     }
     if (os.in_elems == 0 || os.out_elems == 0) {  // empty batch: nothing to launch
@@ -1647,7 +1718,7 @@ static rg_status run_impl(rg_session* h, const float* x, bool x_host, const int6
   if (s.used_tc) {
     s.used_tc = false;
     if (gemm_tc_take_error() != 0 || convblock_take_error() != 0 || conv_tc_take_error() != 0 ||
-        conv3x3_take_error() != 0)
+        conv3x3_take_error() != 0 || stem_take_error() != 0)
       return fail(RG_ERR_TIMEOUT, "a tensor-core kernel gave up on a bounded wait; results are invalid");
   }
   if (s.used_embed) {

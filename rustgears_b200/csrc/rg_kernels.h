@@ -34,6 +34,10 @@ void launch_image_quantize_nhwc(const float* x, int64_t n, int32_t c, int32_t h,
 // multiple of 64, n <= 65535): the input layout of the direct 3x3 conv.
 void launch_image_quantize_planar16(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t cpad,
                                     const unsigned* amax_bits, int8_t* q, float* scales_out, cudaStream_t st);
+// NCHW f32 (c <= 4, even h, w) -> space-to-depth i8 pixels [n][h/2][w/2][16 B] (byte
+// (dy * 2 + dx) * 4 + ch), per-image scales: the input layout of the fused stem.
+void launch_image_quantize_s2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, const unsigned* amax_bits,
+                               int8_t* q, float* scales_out, cudaStream_t st);
 // NHWC i8 (cpad) -> NCHW i8 (c) for traces.
 void launch_nhwc_to_nchw_i8(const int8_t* q, int64_t n, int32_t c, int32_t cpad, int32_t h,
                             int32_t w, int8_t* out, cudaStream_t st);
@@ -109,6 +113,31 @@ int conv3x3_take_error();
 // Reads and clears the device error word the tcgen05 kernels set when a bounded
 // wait gave up (synchronous; 0 = no error).
 int gemm_tc_take_error();
+
+// ---- fused stem (k_stem.cu) ------------------------------------------------------
+// Conv2d(c <= 4 -> 64, k 7, s 2, p 3) + act, then MaxPool2d(3, 2), one kernel over the
+// space-to-depth operand (launch_image_quantize_s2d); weights pre-arranged by
+// stem_arrange_weights into stem_weight_bytes() bytes.  Output NCHW [n, 64, ph, pw].
+struct StemPoolArgs {
+  const int8_t* q = nullptr;       // s2d operand
+  int64_t n = 0;
+  int32_t h = 0, w = 0;            // conv input size (even)
+  const int8_t* wd = nullptr;
+  const float* a_scale = nullptr;  // per image
+  float w_scale = 1.0f;
+  const float* w_scale_ch = nullptr;
+  const float* bias = nullptr;
+  int32_t act = 0;
+  float act_param = 0.0f;
+  float* out = nullptr;
+  AmaxSink amax;                   // of the pooled output
+};
+bool stem_pool_shape_ok(int64_t n_img, int32_t c, int32_t h, int32_t w, int32_t k, int32_t stride, int32_t pad,
+                        int32_t out_channels, int32_t pool_k, int32_t pool_s);
+size_t stem_weight_bytes();
+void stem_arrange_weights(const int8_t* wq, int32_t c, int8_t* out);
+bool launch_stem_pool(const StemPoolArgs& a, int num_sms, cudaStream_t st);
+int stem_take_error();
 
 // ---- fused CNN block (k_convblock.cu) ------------------------------------------
 // Conv(C0->C1,k3,s1,p1)+act -> MaxPool(2,2) -> Conv(C1->C2,k3,s1,p1)+act -> MaxPool(2,2),

@@ -332,3 +332,28 @@ def test_direct_3x3_conv(gpu, oracle_lib, b, c, n, h, w, act):
         blk = [dict(kind=oracle.RESIDUAL_BEGIN), conv, dict(kind=oracle.RESIDUAL_END, act=1, act_param=0.0)]
         ref2, _, _ = oracle.Program(blk).execute(x, nthreads=8)
         assert_same(session_for(blk).run(x), ref2, "residual")
+
+
+@pytest.mark.parametrize("b,c,h,w,act", [(2, 3, 224, 224, 1), (3, 1, 32, 46, 0), (1, 4, 20, 226, 5), (5, 2, 8, 8, 4),
+                                         (2, 3, 64, 30, 2)])
+def test_fused_stem(gpu, oracle_lib, b, c, h, w, act):
+    """Conv(k7 s2 p3 -> 64) + activation + MaxPool(3, 2), the ResNet stem: one kernel over
+    the space-to-depth operand with the pool folded into the conv's epilogue, against the
+    oracle (and against the session's own unfused path)."""
+    from rustgears_b200 import _native
+    rng = np.random.default_rng(b * 100 + c + h + w)
+    wgt = (rng.standard_normal((64, c, 7, 7)) * 0.05).astype(np.float32)
+    bias = (rng.standard_normal(64) * 0.1).astype(np.float32)
+    x = rng.standard_normal((b, c, h, w)).astype(np.float32)
+    layers = [dict(kind=oracle.CONV2D, in_channels=c, out_channels=64, kernel=7, stride=2, padding=3, weight=wgt,
+                   bias=bias)]
+    if act:
+        layers.append(dict(kind=oracle.ACTIVATION, act=act, act_param=0.1))
+    layers.append(dict(kind=oracle.MAXPOOL2D, kernel=3, stride=2))
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
+    sess = session_for(layers)
+    assert_same(sess.run(x), ref, f"stem {c}ch {h}x{w}")
+    assert sess.last_npu_profile().kernel_launches == 3  # absmax, s2d quantizer, fused stem
+    plain = session_for(layers, flags=_native.RG_SESSION_NO_FUSION)
+    assert_same(plain.run(x), ref, "unfused")
+    assert plain.last_npu_profile().kernel_launches > 3
