@@ -111,8 +111,27 @@ __global__ void __launch_bounds__(kThreads) k_image_absmax(const float* __restri
     const float* xi = x + img * per;
     float m = 0.0f;
     if (!row_cov) {
-      for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < per; i += (int64_t)gridDim.x * blockDim.x)
-        m = fmaxf(m, fabsf(__ldg(xi + i)));
+      if (((per | reinterpret_cast<uintptr_t>(x)) & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+        // 16-byte loads, four in flight per thread
+        const float4* x4 = reinterpret_cast<const float4*>(xi);
+        const int64_t per4 = per / 4, step = (int64_t)gridDim.x * blockDim.x;
+        int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+        for (; i + 3 * step < per4; i += 4 * step) {
+          float4 a[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) a[k] = __ldg(x4 + i + k * step);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            m = fmaxf(fmaxf(m, fmaxf(fabsf(a[k].x), fabsf(a[k].y))), fmaxf(fabsf(a[k].z), fabsf(a[k].w)));
+        }
+        for (; i < per4; i += step) {
+          const float4 a = __ldg(x4 + i);
+          m = fmaxf(fmaxf(m, fmaxf(fabsf(a.x), fabsf(a.y))), fmaxf(fabsf(a.z), fabsf(a.w)));
+        }
+      } else {
+        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < per; i += (int64_t)gridDim.x * blockDim.x)
+          m = fmaxf(m, fabsf(__ldg(xi + i)));
+      }
     } else {
       // the masks in shared memory (the launcher bounds h and w); rows the conv never
       // reads are skipped whole
@@ -212,90 +231,51 @@ __global__ void __launch_bounds__(kThreads) k_image_quantize_nhwc(const float* _
   }
 }
 
-// Same result for cpad a multiple of 16, as a tiled transpose: block (pixels
-// 32 bx .. +31, channels 16 by .. +15, image bz) reads the NCHW f32 tile with
-// coalesced row loads, quantizes it with the image's scale and writes each pixel's
-// 16 channel bytes as four packed words (zeros for channels >= c).
-__global__ void __launch_bounds__(128) k_image_quantize_nhwc_tiled(const float* __restrict__ x, int32_t c,
-                                                                   int32_t hw, int32_t cpad,
-                                                                   const unsigned* __restrict__ amax,
-                                                                   int8_t* __restrict__ q,
-                                                                   float* __restrict__ scales) {
-  __shared__ float tile[16][33];
+// NCHW f32 -> 16-channel groups of i8 with the image's scale: a thread per (pixel,
+// 16-channel group) loads the group's 16 values (each load instruction of a warp reads
+// 32 consecutive pixels of one channel), quantizes them and stores the 16 bytes once.
+// PLANAR: [img][cpad / 16][hw][16] (16-channel chunk planes); else NHWC [img][hw][cpad].
+// BOUNDED: the scale came from this whole tensor (|v| <= amax), so the clamp never acts
+// (quant1_bounded); else a strided conv's scale covers only the pixels it reads and
+// others may exceed it (quant1).  Channels past c are written as zeros.
+__device__ __forceinline__ uint32_t pack4_i8(int32_t b0, int32_t b1, int32_t b2, int32_t b3) {
+  return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+}
+
+template <bool BOUNDED, bool PLANAR>
+__global__ void __launch_bounds__(256) k_image_quantize_g16(const float* __restrict__ x, int32_t c, int32_t hw,
+                                                            int32_t cpad, const unsigned* __restrict__ amax,
+                                                            int8_t* __restrict__ q, float* __restrict__ scales) {
   const int64_t img = blockIdx.z;
-  const int32_t p0 = blockIdx.x * 32, c0 = blockIdx.y * 16;
+  const int32_t g = blockIdx.y;
   const float scale = quant_scale(__uint_as_float(amax[img]));
   const float inv = quant_inv(scale);
   if (scales && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) scales[img] = scale;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  const float* src = x + img * (int64_t)c * hw;
+  const int32_t nch = c - 16 * g;  // channels of this group that exist (<= 0: padding only)
+  const float* src = x + (img * c + 16 * g) * (int64_t)hw;
+  for (int32_t px = blockIdx.x * 256 + threadIdx.x; px < hw; px += gridDim.x * 256) {
+    float v[16];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int32_t ch = c0 + ty + 4 * i, px = p0 + tx;
-    tile[ty + 4 * i][tx] = (ch < c && px < hw) ? __ldg(src + (int64_t)ch * hw + px) : 0.0f;
-  }
-  __syncthreads();
-  const int pl = threadIdx.x >> 2, quad = threadIdx.x & 3;  // pixel in tile, 4-channel group
-  const int32_t px = p0 + pl;
-  if (px < hw) {
-    uint32_t word = 0;
+    for (int k = 0; k < 16; ++k) v[k] = k < nch ? __ldg(src + (int64_t)k * hw + px) : 0.0f;
+    int32_t t[16];
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const int cl = 4 * quad + b;
-      // clamped: a strided conv's scale covers only the pixels it reads, others may exceed it
-      const int32_t v = c0 + cl < c ? quant1(tile[cl][pl], inv) : 0;
-      word |= (uint32_t)(v & 0xff) << (8 * b);
-    }
-    *reinterpret_cast<uint32_t*>(q + (img * hw + px) * (int64_t)cpad + c0 + 4 * quad) = word;
+    for (int k = 0; k < 16; ++k) t[k] = BOUNDED ? quant1_bounded(v[k], inv) : quant1(v[k], inv);
+    const uint4 word = make_uint4(pack4_i8(t[0], t[1], t[2], t[3]), pack4_i8(t[4], t[5], t[6], t[7]),
+                                  pack4_i8(t[8], t[9], t[10], t[11]), pack4_i8(t[12], t[13], t[14], t[15]));
+    const int64_t off = PLANAR ? ((img * (cpad / 16) + g) * (int64_t)hw + px) * 16
+                               : (img * hw + px) * (int64_t)cpad + 16 * g;
+    *reinterpret_cast<uint4*>(q + off) = word;
   }
 }
 
-// The same for channel counts padded to a multiple of 64: a block quantizes 32 pixels x
-// 64 channels (8 coalesced row loads per thread in flight), and each pixel's 64 channel
-// bytes leave as four 16-byte stores (a warp writes 512 contiguous bytes when cpad = 64).
-// planar: write [img][cpad / 16][hw][16] (16-channel chunk planes) instead of NHWC.
-__global__ void __launch_bounds__(256) k_image_quantize_nhwc_t64(const float* __restrict__ x, int32_t c,
-                                                                 int32_t hw, int32_t cpad, bool planar,
-                                                                 const unsigned* __restrict__ amax,
-                                                                 int8_t* __restrict__ q,
-                                                                 float* __restrict__ scales) {
-  __shared__ float tile[64][33];
-  const int64_t img = blockIdx.z;
-  const int32_t p0 = blockIdx.x * 32, c0 = blockIdx.y * 64;
-  const float scale = quant_scale(__uint_as_float(amax[img]));
-  const float inv = quant_inv(scale);
-  if (scales && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) scales[img] = scale;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  const float* src = x + img * (int64_t)c * hw;
-  const bool px_ok = p0 + tx < hw;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int32_t ch = c0 + ty + 8 * i;
-    tile[ty + 8 * i][tx] = (ch < c && px_ok) ? __ldg(src + (int64_t)ch * hw + p0 + tx) : 0.0f;
-  }
-  __syncthreads();
-  if (threadIdx.x < 128) {
-    const int pl = threadIdx.x >> 2, grp = threadIdx.x & 3;  // pixel in tile, 16-channel group
-    const int32_t px = p0 + pl;
-    if (px < hw) {
-      uint32_t wv[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          const int cl = 16 * grp + 4 * k + b;
-          // clamped: a strided conv's scale covers only the pixels it reads
-          const int32_t v = c0 + cl < c ? quant1(tile[cl][pl], inv) : 0;
-          word |= (uint32_t)(v & 0xff) << (8 * b);
-        }
-        wv[k] = word;
-      }
-      const int64_t off = planar ? ((img * (cpad / 16) + (c0 / 16 + grp)) * (int64_t)hw + px) * 16
-                                 : (img * hw + px) * (int64_t)cpad + c0 + 16 * grp;
-      *reinterpret_cast<uint4*>(q + off) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-    }
-  }
+template <bool PLANAR>
+void launch_g16(const float* x, int64_t n, int32_t c, int32_t hw, int32_t cpad, bool bounded, const unsigned* amax,
+                int8_t* q, float* scales, cudaStream_t st) {
+  const dim3 grid((unsigned)std::min<int64_t>((hw + 255) / 256, 1024), (unsigned)(cpad / 16), (unsigned)n);
+  if (bounded)
+    k_image_quantize_g16<true, PLANAR><<<grid, 256, 0, st>>>(x, c, hw, cpad, amax, q, scales);
+  else
+    k_image_quantize_g16<false, PLANAR><<<grid, 256, 0, st>>>(x, c, hw, cpad, amax, q, scales);
 }
 
 __global__ void k_nhwc_to_nchw_i8(const int8_t* __restrict__ q, int64_t n, int32_t c, int32_t cpad,
@@ -333,11 +313,77 @@ void launch_quantize_rows(const float* x, int64_t rows, int64_t k, int64_t ldq,
                                                                            scale_out);
 }
 
+// Per-image absmax over the pixels a strided conv reads, VEC consecutive columns per
+// thread (w a multiple of VEC, so they share a row): lanes on rows the conv never
+// reads issue no load, so only the covered rows' sectors are fetched.  grid.y strides
+// over the images; the masks are staged in shared memory.
+template <int VEC>
+__global__ void __launch_bounds__(kThreads) k_image_absmax_cov(const float* __restrict__ x, int64_t n, int32_t c,
+                                                               int32_t h, int32_t w,
+                                                               const uint8_t* __restrict__ row_cov,
+                                                               const uint8_t* __restrict__ col_cov,
+                                                               unsigned* __restrict__ amax) {
+  extern __shared__ uint8_t cov_s[];  // [h] rows then [w] columns
+  for (int32_t i = threadIdx.x; i < h + w; i += kThreads) cov_s[i] = i < h ? row_cov[i] : col_cov[i - h];
+  __syncthreads();
+  const int32_t groups = c * h * (w / VEC);  // VEC-column groups per image
+  const int32_t gpr = w / VEC;
+  for (int64_t img = blockIdx.y; img < n; img += gridDim.y) {
+    const float* xi = x + img * (int64_t)c * h * w;
+    float m = 0.0f;
+    const int32_t stride = gridDim.x * kThreads;
+    for (int32_t g0 = blockIdx.x * kThreads + threadIdx.x; g0 < groups; g0 += 4 * stride) {
+      // four groups' loads in flight before any of them is folded in
+      float v[4][VEC];
+      int32_t col[4];
+      bool ok[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int32_t gi = g0 + u * stride;
+        const int32_t rr = gi / gpr;
+        col[u] = (gi - rr * gpr) * VEC;
+        ok[u] = gi < groups && cov_s[rr % h];
+        const float* p = xi + (int64_t)rr * w + col[u];
+        if (!ok[u]) {
+#pragma unroll
+          for (int k = 0; k < VEC; ++k) v[u][k] = 0.0f;
+        } else if (VEC == 4) {
+          const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+          v[u][0] = a.x; v[u][VEC > 1 ? 1 : 0] = a.y; v[u][VEC > 2 ? 2 : 0] = a.z; v[u][VEC > 3 ? 3 : 0] = a.w;
+        } else if (VEC == 2) {
+          const float2 a = __ldg(reinterpret_cast<const float2*>(p));
+          v[u][0] = a.x; v[u][VEC > 1 ? 1 : 0] = a.y;
+        } else {
+          v[u][0] = __ldg(p);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int k = 0; k < VEC; ++k)
+          if (ok[u] && cov_s[h + col[u] + k]) m = fmaxf(m, fabsf(v[u][k]));
+    }
+    block_max_to(m, amax + img);
+    __syncthreads();  // the reduction buffer is reused by the next image
+  }
+}
+
 void launch_image_absmax(const float* x, int64_t n, int32_t c, int32_t h, int32_t w,
                          const uint8_t* row_cov, const uint8_t* col_cov, unsigned* amax_bits,
                          cudaStream_t st) {
   const int64_t per = (int64_t)c * h * w;
   if (n <= 0 || per <= 0) return;
+  if (row_cov && h + w <= 32 * 1024 && per < ((int64_t)1 << 30)) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(x);
+    const int vec = (w % 4 == 0 && (a & 15) == 0) ? 4 : (w % 2 == 0 && (a & 7) == 0) ? 2 : 1;
+    const int64_t groups = per / vec;
+    dim3 grid(grid_for(groups, kThreads * 4, 256), (unsigned)std::min<int64_t>(n, 65535));
+    const size_t sm = (size_t)(h + w);
+    if (vec == 4) k_image_absmax_cov<4><<<grid, kThreads, sm, st>>>(x, n, c, h, w, row_cov, col_cov, amax_bits);
+    else if (vec == 2) k_image_absmax_cov<2><<<grid, kThreads, sm, st>>>(x, n, c, h, w, row_cov, col_cov, amax_bits);
+    else k_image_absmax_cov<1><<<grid, kThreads, sm, st>>>(x, n, c, h, w, row_cov, col_cov, amax_bits);
+    return;
+  }
   const int64_t work = row_cov ? (int64_t)c * h * 32 : per;  // lanes in use per image
   dim3 grid(grid_for(work, kThreads * 8, 64), (unsigned)std::min<int64_t>(n, 65535));
   const bool cov_smem = row_cov && h + w <= 32 * 1024;  // the masks fit the default shared memory
@@ -346,11 +392,11 @@ void launch_image_absmax(const float* x, int64_t n, int32_t c, int32_t h, int32_
 }
 
 void launch_image_quantize_planar16(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t cpad,
-                                    const unsigned* amax_bits, int8_t* q, float* scales_out, cudaStream_t st) {
+                                    bool bounded, const unsigned* amax_bits, int8_t* q, float* scales_out,
+                                    cudaStream_t st) {
   const int32_t hw = h * w;
   if (n <= 0 || hw <= 0) return;
-  dim3 grid((unsigned)((hw + 31) / 32), (unsigned)(cpad / 64), (unsigned)n);
-  k_image_quantize_nhwc_t64<<<grid, 256, 0, st>>>(x, c, hw, cpad, true, amax_bits, q, scales_out);
+  launch_g16<true>(x, n, c, hw, cpad, bounded, amax_bits, q, scales_out, st);
 }
 
 void launch_image_quantize_s2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, const unsigned* amax_bits,
@@ -363,7 +409,7 @@ void launch_image_quantize_s2d(const float* x, int64_t n, int32_t c, int32_t h, 
 }
 
 void launch_image_quantize_nhwc(const float* x, int64_t n, int32_t c, int32_t h, int32_t w,
-                                int32_t cpad, const unsigned* amax_bits, int8_t* q,
+                                int32_t cpad, bool bounded, const unsigned* amax_bits, int8_t* q,
                                 float* scales_out, cudaStream_t st) {
   const int64_t total = n * (int64_t)h * w;
   if (total <= 0) return;
@@ -374,16 +420,8 @@ void launch_image_quantize_nhwc(const float* x, int64_t n, int32_t c, int32_t h,
     k_image_quantize_nhwc4<<<grid, kThreads, 0, st>>>(x, n, c, hw, amax_bits, q, scales_out);
     return;
   }
-  if ((cpad & 63) == 0 && n <= 65535) {
-    const int32_t hw = h * w;
-    dim3 grid((unsigned)((hw + 31) / 32), (unsigned)(cpad / 64), (unsigned)n);
-    k_image_quantize_nhwc_t64<<<grid, 256, 0, st>>>(x, c, hw, cpad, false, amax_bits, q, scales_out);
-    return;
-  }
-  if ((cpad & 15) == 0 && n <= 65535) {  // channel-padded layout: tiled transpose (grid.z = image)
-    const int32_t hw = h * w;
-    dim3 grid((unsigned)((hw + 31) / 32), (unsigned)(cpad / 16), (unsigned)n);
-    k_image_quantize_nhwc_tiled<<<grid, 128, 0, st>>>(x, c, hw, cpad, amax_bits, q, scales_out);
+  if ((cpad & 15) == 0 && n <= 65535) {
+    launch_g16<false>(x, n, c, h * w, cpad, bounded, amax_bits, q, scales_out, st);
     return;
   }
   k_image_quantize_nhwc<<<grid_for(total, kThreads, 148 * 32), kThreads, 0, st>>>(

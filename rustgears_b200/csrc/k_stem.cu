@@ -18,9 +18,10 @@
 // TMA load brings the padded s2d rows oy - 2 .. (zero rows and columns outside the
 // image), and 8 MMAs (K 32: two vertically adjacent taps, LBO = one padded row) read
 // the taps at constant offsets.  Each CTA owns a contiguous range of pool rows and
-// computes the conv rows they need in order; the epilogue stages a conv row in shared
-// memory, folds each pooling window's three columns (the reference's scan order within
-// the row), then folds the rows into the running window (row order) -- the same
+// computes the conv rows they need in order; the epilogue folds each pooling window's
+// three columns of the conv row (the reference's scan order within the row; the
+// neighbouring columns come from the neighbouring TMEM lanes by warp shuffles), then
+// folds the rows into the running window (row order) -- the same
 // result as the reference's row-major scan, NaN and signed zeros included: the scan
 // returns the last NaN, else the first maximal element in row-major order, and
 // folding per-row results in row order preserves both.
@@ -28,9 +29,9 @@
 //   warp 0     producer (lane 0): one TMA load per conv row; the weights once
 //   warp 1     MMA issuer (lane 0): 8 tcgen05.mma per conv row into one of two
 //              TMEM accumulators
-//   warps 2-17 epilogue: tcgen05.ld, act(f32(acc) * (s_img * s_w) + bias) into
-//              shared memory, then the pooling folds, NCHW pool stores and the
-//              per-image absmax of the pooled tensor
+//   warps 2-17 epilogue: tcgen05.ld, act(f32(acc) * (s_img * s_w) + bias), the
+//              pooling folds in registers, NCHW pool stores and the per-image absmax
+//              of the pooled tensor
 // Every mbarrier wait is bounded; on timeout the CTA raises an abort flag, the roles
 // leave their loops together, copies and MMAs in flight are drained, TMEM is freed and
 // a device error word is set for the host.
@@ -60,8 +61,6 @@ constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kThreads = 64 + kEpiThreads;
 constexpr int kTaps = 8;         // MMAs per tile: (ay pair, ax)
 constexpr int kWBytes = kTaps * 2 * BN * 16;  // 16 KB of arranged weights
-constexpr int kRowPitch = 128;   // floats per staged conv row (per channel)
-constexpr int kItems = 7;        // pool outputs per epilogue thread and pool row (64 * pw <= 7 * 512)
 constexpr int kRing = 6;
 constexpr int kBarBytes = 256;
 
@@ -131,7 +130,16 @@ struct RowIter {
   }
 };
 
-__device__ __forceinline__ float pool_fold(float best, float v) { return (v > best || v != v) ? v : best; }
+// One step of the reference's window scan, best = (v > best || v is NaN) ? v : best, as
+// predicated selects (no branch).
+__device__ __forceinline__ float pool_fold(float best, float v) {
+  float r;
+  asm("{\n .reg .pred p, q;\n setp.gt.f32 p, %2, %1;\n setp.nan.f32 q, %2, %2;\n or.pred p, p, q;\n"
+      " selp.f32 %0, %2, %1, p;\n}"
+      : "=f"(r)
+      : "f"(best), "f"(v));
+  return r;
+}
 
 template <int ACT>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -140,8 +148,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;                                            // [kRing][slot_bytes]
   uint8_t* wsm = ring + (size_t)kRing * p.slot_bytes;              // [kWBytes]
-  float* crow = reinterpret_cast<float*>(wsm + kWBytes);           // [2][BN][kRowPitch]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(crow + 2 * BN * kRowPitch);
+  float* xch = reinterpret_cast<float*>(wsm + kWBytes);            // [2][4 parts][4 quadrants][16]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xch + 2 * 4 * 4 * 16);
   uint64_t* full = bars;              // [kRing]
   uint64_t* empty = full + kRing;     // [kRing]
   uint64_t* tfull = empty + kRing;    // [2]
@@ -242,82 +250,88 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue ----------------
+    // Lane ox holds conv column ox of its 16 channels; the pool window's columns ox + 1
+    // and ox + 2 come from the neighbouring lanes (lane 30's ox + 2 from lane 0 of the
+    // next quadrant's warp, through shared memory); the row folds run in registers.
     const int e = warp - 2;
     const int q = warp & 3;                 // TMEM lane quadrant this warp may access
     const int part = e >> 2;                // channels part * 16 .. + 15
-    const int tid = threadIdx.x - 64;       // 0 .. kEpiThreads - 1
     const int32_t ox = q * 32 + lane;       // conv output column of this lane
-    const int32_t items = BN * p.pw;
+    const int32_t px = ox >> 1;
+    const bool centre = (ox & 1) == 0 && px < p.pw;  // the first column of pool window px
     const int32_t plane = p.ph * p.pw;
-    // this thread's pool outputs (channel c, column px): staged-row and output offsets
-    int32_t roff[kItems], ooff[kItems];
+    float bias_r[16];
 #pragma unroll
-    for (int k = 0; k < kItems; ++k) {
-      const int32_t idx = tid + k * kEpiThreads;
-      const int32_t c = idx / p.pw, px = idx - c * p.pw;
-      roff[k] = c * kRowPitch + 2 * px;
-      ooff[k] = c * plane + px;
-    }
-    float vs[kItems];                       // running window fold per pool output
+    for (int j = 0; j < 16; ++j) bias_r[j] = __ldg(p.bias + part * 16 + j);
+    int32_t cs_img = -1;
+    float sa = 0.0f, cs_t = 0.0f;           // the image's scale, times the tensor weight scale
+    float vs[16];                           // running window fold per channel (pool column px)
     float mx = 0.0f;
     int iter = 0;
     RowIter it;
     for (it.start(g0, g1, p.ph); it.valid(); it.next(p.ph), ++iter) {
       const int buf = iter & 1;
       const uint32_t aphase = (iter >> 1) & 1;
-      float* cr = crow + (size_t)buf * BN * kRowPitch;
+      float o[16];
       const bool got = mbar_wait(&tfull[buf], aphase, abort);
       if (__all_sync(0xffffffffu, got)) {
         tc_fence_after();
         uint32_t v[16];
         tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + part * 16), v);
         tmem_ld_wait();
-        if (ox < p.w2) {
-          const float sa = p.a_scale[it.img];
-          const float cs_tensor = __fmul_rn(sa, p.w_scale);
+        if (it.img != cs_img) {
+          cs_img = it.img;
+          sa = p.a_scale[it.img];
+          cs_t = __fmul_rn(sa, p.w_scale);
+        }
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int32_t c = part * 16 + j;
-            const float cs = p.w_scale_ch ? __fmul_rn(sa, __ldg(p.w_scale_ch + c)) : cs_tensor;
-            cr[c * kRowPitch + ox] = epilogue_t<ACT>((int32_t)v[j], cs, __ldg(p.bias + c), p.act_param);
-          }
+        for (int j = 0; j < 16; ++j) {
+          const float cs = p.w_scale_ch ? __fmul_rn(sa, __ldg(p.w_scale_ch + part * 16 + j)) : cs_t;
+          o[j] = epilogue_t<ACT>((int32_t)v[j], cs, bias_r[j], p.act_param);
         }
         tc_fence_before();
+        if (lane == 0) {
+          float* xs = xch + ((buf * 4 + part) * 4 + q) * 16;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) xs[j] = o[j];
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
-      // the whole conv row is staged (and every epilogue warp got its accumulator)
-      if (!bar_and(1, kEpiThreads, got)) {
+      // the part's four quadrant warps: exchange published, accumulators all received
+      if (!bar_and(2 + part, 128, got)) {
         *abort = 1;
         break;
       }
       const bool first = it.y == 2 * it.ra;
       const bool closes = !first && (it.y & 1) == 0;  // completes pool row y / 2 - 1
+      const float* xn = xch + ((buf * 4 + part) * 4 + ((q + 1) & 3)) * 16;
+      float* orow = p.out + ((int64_t)it.img * BN + part * 16) * plane + (it.y / 2 - 1) * p.pw + px;
 #pragma unroll
-      for (int k = 0; k < kItems; ++k) {
-        const int32_t idx = tid + k * kEpiThreads;
-        if (idx < items) {
-          const float* rp = cr + roff[k];
-          float h = pool_fold(-INFINITY, rp[0]);
-          h = pool_fold(h, rp[1]);
-          h = pool_fold(h, rp[2]);
-          if (first) {
-            vs[k] = pool_fold(-INFINITY, h);
-          } else if (!closes) {
-            vs[k] = pool_fold(vs[k], h);
-          } else {
-            const float best = pool_fold(vs[k], h);
-            p.out[(int64_t)it.img * BN * plane + ooff[k] + (it.y / 2 - 1) * p.pw] = best;
+      for (int j = 0; j < 16; ++j) {
+        const float n1 = __shfl_down_sync(0xffffffffu, o[j], 1);
+        float n2 = __shfl_down_sync(0xffffffffu, o[j], 2);
+        if (lane == 30) n2 = xn[j];
+        // the window's row: columns 2 px, 2 px + 1, 2 px + 2 in the reference's order
+        const float h = pool_fold(pool_fold(o[j], n1), n2);
+        if (first) {
+          vs[j] = h;
+        } else if (!closes) {
+          vs[j] = pool_fold(vs[j], h);
+        } else {
+          const float best = pool_fold(vs[j], h);
+          if (centre) {
+            orow[(int64_t)j * plane] = best;
             mx = fmaxf(mx, fabsf(best));
-            vs[k] = pool_fold(-INFINITY, h);
           }
+          vs[j] = h;
         }
       }
       if (it.y == 2 * it.rb) {  // the image's last conv row in this CTA: flush its absmax
         if (p.amax) {
           float m = mx;
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          for (int k = 16; k > 0; k >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, k));
           if (lane == 0 && m > 0.0f) atomicMax(p.amax + (p.amax_per_image ? it.img : 0), __float_as_uint(m));
         }
         mx = 0.0f;
@@ -373,7 +387,7 @@ bool launch_t(const StemPoolArgs& a, int num_sms, cudaStream_t st) {
   p.act_param = a.act_param; p.out = a.out;
   p.amax = a.amax.ptr;
   p.amax_per_image = a.amax.ptr && a.amax.elems_per_slot > 0;
-  const int smem = 1024 + kRing * p.slot_bytes + kWBytes + 2 * BN * kRowPitch * 4 + kBarBytes;
+  const int smem = 1024 + kRing * p.slot_bytes + kWBytes + 2 * 4 * 4 * 16 * 4 + kBarBytes;
   if (smem > 227 * 1024) return false;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -392,8 +406,7 @@ bool stem_pool_shape_ok(int64_t n_img, int32_t c, int32_t h, int32_t w, int32_t 
                         int32_t out_channels, int32_t pool_k, int32_t pool_s) {
   if (k != 7 || stride != 2 || pad != 3 || c < 1 || c > 4 || out_channels != BN) return false;
   if (pool_k != 3 || pool_s != 2 || (h & 1) || (w & 1) || h < 6 || w < 6) return false;
-  // the M tile (w / 2 <= 125 with the box width) and 64 x pool width <= 7 x 512 items
-  if (w / 2 > 113 || n_img < 1 || n_img > 65535) return false;
+  if (w / 2 > 125 || n_img < 1 || n_img > 65535) return false;  // the M tile and the TMA box width
   if (n_img * (int64_t)((h / 2 - 3) / 2 + 1) > ((int64_t)1 << 40)) return false;
   return tma_encode_fn() != nullptr;
 }

@@ -1146,8 +1146,9 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
           // the direct 3x3 kernel reads 16-channel chunk planes; every other conv, NHWC
           use3 = op.kind == RG_LAYER_CONV2D && op.d_w3.p && !s.trace &&
                  conv3x3_shape_ok(N, H, W, op.cpad, op.k, op.stride, op.pad, op.out_c);
-          if (use3) launch_image_quantize_planar16(src, N, C, H, W, op.cpad, my_amax, q, my_scale, st);
-          else launch_image_quantize_nhwc(src, N, C, H, W, op.cpad, my_amax, q, my_scale, st);
+          const bool bounded = rc[i] == nullptr;  // the absmax covers every pixel quantized
+          if (use3) launch_image_quantize_planar16(src, N, C, H, W, op.cpad, bounded, my_amax, q, my_scale, st);
+          else launch_image_quantize_nhwc(src, N, C, H, W, op.cpad, bounded, my_amax, q, my_scale, st);
           ++launches;
           RG_LAUNCHED("image_quantize");
           g.a = q; g.conv = true;

@@ -27,13 +27,16 @@ void launch_image_absmax(const float* x, int64_t n, int32_t c, int32_t h, int32_
                          const uint8_t* row_cov, const uint8_t* col_cov, unsigned* amax_bits,
                          cudaStream_t st);
 // NCHW f32 -> NHWC i8 (channels padded to cpad with zeros) with per-image scales.
+// bounded: the scale's absmax covers every element quantized (no strided-conv coverage
+// mask), so the clamp to +-127 can be left out.
 void launch_image_quantize_nhwc(const float* x, int64_t n, int32_t c, int32_t h, int32_t w,
-                                int32_t cpad, const unsigned* amax_bits, int8_t* q,
+                                int32_t cpad, bool bounded, const unsigned* amax_bits, int8_t* q,
                                 float* scales_out, cudaStream_t st);
 // The same scale, written as 16-channel chunk planes [n][cpad / 16][h * w][16] (cpad a
-// multiple of 64, n <= 65535): the input layout of the direct 3x3 conv.
+// multiple of 16, n <= 65535): the input layout of the direct 3x3 conv.
 void launch_image_quantize_planar16(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t cpad,
-                                    const unsigned* amax_bits, int8_t* q, float* scales_out, cudaStream_t st);
+                                    bool bounded, const unsigned* amax_bits, int8_t* q, float* scales_out,
+                                    cudaStream_t st);
 // NCHW f32 (c <= 4, even h, w) -> space-to-depth i8 pixels [n][h/2][w/2][16 B] (byte
 // (dy * 2 + dx) * 4 + ch), per-image scales: the input layout of the fused stem.
 void launch_image_quantize_s2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, const unsigned* amax_bits,
