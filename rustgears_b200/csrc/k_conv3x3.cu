@@ -25,6 +25,7 @@
 //              of two TMEM accumulators
 //   warps 2-17 epilogue: tcgen05.ld, act(f32(acc) * (s_img * s_w) + bias), optional
 //              fused residual add, NCHW stores, per-image absmax for the next conv
+//              (and, optionally, over the pixels a later strided 1x1 conv reads)
 // Every mbarrier wait is bounded; on timeout the CTA raises an abort flag, the roles
 // leave their loops, copies and MMAs in flight are drained, TMEM is freed and a device
 // error word is set for the host.
@@ -73,6 +74,8 @@ struct C3Params {
   int32_t* acc;                    // optional i32 dump, NCHW
   unsigned* amax;                  // optional absmax sink
   int64_t amax_per_slot;           // 0: one slot; else n * h * w (per image)
+  unsigned* amax2;                 // optional per-image absmax over the pixels a later
+  int32_t cov_s, cov_oh, cov_ow;   // 1x1 / pad 0 / stride cov_s conv reads
 };
 
 __device__ int g_c3_error;
@@ -241,6 +244,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int32_t f = wp + 1 + BM * mt + q * 32 + lane;  // this lane's centre position
       const int32_t py = f / wp, px = f - py * wp;
       const bool valid = py >= 1 && py <= p.h && px >= 1 && px <= p.w;
+      // read by the later strided 1x1 conv: rows and columns cov_s * i, i < cov_oh / cov_ow
+      const int32_t iy = py - 1, ix = px - 1;
+      const bool cov2 = valid && p.amax2 && iy % p.cov_s == 0 && ix % p.cov_s == 0 && iy / p.cov_s < p.cov_oh &&
+                        ix / p.cov_s < p.cov_ow;
       const int64_t pix = valid ? (int64_t)(py - 1) * p.w + (px - 1) : 0;
       const float sa = p.a_scale[img];
       const float cs_tensor = __fmul_rn(sa, p.w_scale);
@@ -258,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool got = mbar_wait(&tfull[buf], aphase, abort);
       if (!__all_sync(0xffffffffu, got)) { *abort = 1; break; }
       tc_fence_after();
-      float mx = 0.0f;
+      float mx = 0.0f, mx2 = 0.0f;
 #pragma unroll
       for (int cc = 0; cc < kCols; cc += 16) {
         uint32_t v[16];
@@ -281,6 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               obase[(int64_t)c * hw] = o;
               if (p.acc) p.acc[(int64_t)img * p.n * hw + (int64_t)c * hw + pix] = (int32_t)v[j];
               mx = fmaxf(mx, fabsf(o));
+              if (cov2) mx2 = fmaxf(mx2, fabsf(o));
             }
           }
         }
@@ -289,6 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
       if (p.amax) flush_slot_max(p.amax, p.amax_per_slot ? img : 0, mx);
+      if (p.amax2) flush_slot_max(p.amax2, img, mx2);
     }
   }
 
@@ -345,6 +354,7 @@ bool launch_bn(const GemmArgs& a, const int8_t* wd, int num_sms, cudaStream_t st
   p.act_param = a.act_param; p.out = a.out; p.acc = a.acc;
   p.residual = a.residual; p.res_act = a.res_act; p.res_param = a.res_param;
   p.amax = a.amax.ptr; p.amax_per_slot = a.amax.elems_per_slot;
+  p.amax2 = a.amax2; p.cov_s = a.cov_s > 0 ? a.cov_s : 1; p.cov_oh = a.cov_oh; p.cov_ow = a.cov_ow;
   const int64_t tiles = (int64_t)p.n_img * p.tiles_m * p.tiles_n;
   const int grid = tiles < num_sms ? (int)tiles : num_sms;
   k_conv3x3<BN, ACT><<<grid, kThreads, smem, st>>>(mi, p);

@@ -268,6 +268,37 @@ __global__ void __launch_bounds__(256) k_image_quantize_g16(const float* __restr
   }
 }
 
+// The strided 1x1 conv's operand: output pixel (oy, ox) of the compact [n][oh][ow][cpad]
+// NHWC tensor is input pixel (s oy, s ox); the scale's absmax covers exactly these
+// pixels (no clamp).
+__global__ void __launch_bounds__(256) k_image_quantize_sub16(const float* __restrict__ x, int32_t c, int32_t h,
+                                                              int32_t w, int32_t s, int32_t oh, int32_t ow,
+                                                              int32_t cpad, const unsigned* __restrict__ amax,
+                                                              int8_t* __restrict__ q, float* __restrict__ scales) {
+  const int64_t img = blockIdx.z;
+  const int32_t g = blockIdx.y;
+  const float scale = quant_scale(__uint_as_float(amax[img]));
+  const float inv = quant_inv(scale);
+  if (scales && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) scales[img] = scale;
+  const int32_t nch = c - 16 * g;
+  const int64_t hw = (int64_t)h * w;
+  const float* src = x + (img * c + 16 * g) * hw;
+  const int32_t ohw = oh * ow;
+  for (int32_t op = blockIdx.x * 256 + threadIdx.x; op < ohw; op += gridDim.x * 256) {
+    const int32_t oy = op / ow, ox = op - oy * ow;
+    const int64_t px = (int64_t)(s * oy) * w + s * ox;
+    float v[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) v[k] = k < nch ? __ldg(src + (int64_t)k * hw + px) : 0.0f;
+    int32_t t[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) t[k] = quant1_bounded(v[k], inv);
+    const uint4 word = make_uint4(pack4_i8(t[0], t[1], t[2], t[3]), pack4_i8(t[4], t[5], t[6], t[7]),
+                                  pack4_i8(t[8], t[9], t[10], t[11]), pack4_i8(t[12], t[13], t[14], t[15]));
+    *reinterpret_cast<uint4*>(q + (img * ohw + op) * (int64_t)cpad + 16 * g) = word;
+  }
+}
+
 template <bool PLANAR>
 void launch_g16(const float* x, int64_t n, int32_t c, int32_t hw, int32_t cpad, bool bounded, const unsigned* amax,
                 int8_t* q, float* scales, cudaStream_t st) {
@@ -397,6 +428,15 @@ void launch_image_quantize_planar16(const float* x, int64_t n, int32_t c, int32_
   const int32_t hw = h * w;
   if (n <= 0 || hw <= 0) return;
   launch_g16<true>(x, n, c, hw, cpad, bounded, amax_bits, q, scales_out, st);
+}
+
+void launch_image_quantize_subsampled(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t s,
+                                      int32_t oh, int32_t ow, int32_t cpad, const unsigned* amax_bits, int8_t* q,
+                                      float* scales_out, cudaStream_t st) {
+  const int32_t ohw = oh * ow;
+  if (n <= 0 || ohw <= 0) return;
+  const dim3 grid((unsigned)std::min<int64_t>((ohw + 255) / 256, 1024), (unsigned)(cpad / 16), (unsigned)n);
+  k_image_quantize_sub16<<<grid, 256, 0, st>>>(x, c, h, w, s, oh, ow, cpad, amax_bits, q, scales_out);
 }
 
 void launch_image_quantize_s2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, const unsigned* amax_bits,

@@ -14,24 +14,28 @@
 // 0..6.  The i32 sums are those of the reference's im2col GEMM (the extra products are
 // zero, integer addition is exact in any order).
 //
-// A tile is one conv output row (M = 128 TMEM lanes, ox = lane, w/2 <= 125 valid): a
-// TMA load brings the padded s2d rows oy - 2 .. (zero rows and columns outside the
-// image), and 8 MMAs (K 32: two vertically adjacent taps, LBO = one padded row) read
-// the taps at constant offsets.  Each CTA owns a contiguous range of pool rows and
-// computes the conv rows they need in order; the epilogue folds each pooling window's
-// three columns of the conv row (the reference's scan order within the row; the
-// neighbouring columns come from the neighbouring TMEM lanes by warp shuffles), then
-// folds the rows into the running window (row order) -- the same
-// result as the reference's row-major scan, NaN and signed zeros included: the scan
-// returns the last NaN, else the first maximal element in row-major order, and
-// folding per-row results in row order preserves both.
+// A tile is two conv output rows y, y + 1 (y even).  The weights are the MMA's A operand
+// (M = 128: rows 0-63 the 64 channels of row y, rows 64-127 the same channels of row
+// y + 1, their taps shifted by one s2d row), the s2d positions its B operand (N = the
+// row's w/2 columns, rows 16 bytes apart): a TMA load brings the padded s2d rows y - 2 ..
+// y + 3 (zero rows and columns outside the image) and 12 MMAs (K 32 = two vertically
+// adjacent s2d rows; 3 row pairs x 4 column shifts) accumulate the tile in TMEM with a
+// channel per lane and a conv column per TMEM column.  So an epilogue thread holds 32
+// consecutive conv columns of one channel and row in registers: the pooling window's
+// three columns fold there (the reference's scan order within a row), the row y + 1
+// thread hands its folded row to the row y thread through shared memory, and the row
+// folds run in row order across tiles -- the same result as the reference's row-major
+// scan, NaN and signed zeros included: the scan returns the last NaN, else the first
+// maximal element in row-major order, and folding per-row results in row order
+// preserves both.  Each CTA owns a contiguous range of pool rows.
 //
-//   warp 0     producer (lane 0): one TMA load per conv row; the weights once
-//   warp 1     MMA issuer (lane 0): 8 tcgen05.mma per conv row into one of two
-//              TMEM accumulators
-//   warps 2-17 epilogue: tcgen05.ld, act(f32(acc) * (s_img * s_w) + bias), the
-//              pooling folds in registers, NCHW pool stores and the per-image absmax
-//              of the pooled tensor
+//   warp 0     producer (lane 0): one TMA load per tile; the weights once
+//   warp 1     MMA issuer (lane 0): 12 tcgen05.mma per tile into one of two TMEM
+//              accumulators
+//   warps 2-17 epilogue: warp w reads TMEM lane quadrant w % 4 (channel half, row of
+//              the tile) and conv columns 28 (w - 2) / 4 ..; act(f32(acc) * (s_img *
+//              s_w) + bias), the window folds, NCHW pool stores (row y threads) and
+//              the per-image absmax of the pooled tensor
 // Every mbarrier wait is bounded; on timeout the CTA raises an abort flag, the roles
 // leave their loops together, copies and MMAs in flight are drained, TMEM is freed and
 // a device error word is set for the host.
@@ -54,23 +58,26 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128;          // conv output columns per tile (TMEM lanes)
 constexpr int BN = 64;           // output channels
-constexpr int kEpiWarps = 16;    // 4 per TMEM lane quadrant, 16 channels each
-constexpr int kEpiThreads = 32 * kEpiWarps;
-constexpr int kThreads = 64 + kEpiThreads;
-constexpr int kTaps = 8;         // MMAs per tile: (ay pair, ax)
-constexpr int kWBytes = kTaps * 2 * BN * 16;  // 16 KB of arranged weights
+constexpr int kEpiWarps = 16;    // 4 per TMEM lane quadrant, one column range each
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kMmas = 12;        // per tile: (s2d row pair 0..2) x (column shift 0..3)
+constexpr int kWBytes = kMmas * 2 * 128 * 16;  // 48 KB of arranged weights
+constexpr int kXchBytes = 2 * 4 * 16 * BN * 4; // [2 buffers][4 column ranges][16 px][64 channels] f32
+constexpr int kRbox = 6;         // padded s2d rows per tile: y - 2 .. y + 3
+constexpr int kTmemCols = 256;   // two accumulators of up to 112 columns
+constexpr int kMaxW2 = 112;
 constexpr int kRing = 6;
 constexpr int kBarBytes = 256;
 
 struct StemParams {
   int32_t n_img, h2, w2;           // s2d grid = conv output grid
   int32_t ph, pw;                  // pool output
-  int32_t rbox;                    // padded s2d rows per TMA box
-  int32_t slot_bytes;              // ring slot (rbox * (w2 + 3) * 16, rounded to 128)
+  int32_t n_mma;                   // MMA N: w2 rounded up to 16
+  int32_t span;                    // pool columns per epilogue column range: ceil(pw / 4)
+  int32_t slot_bytes;              // ring slot (kRbox * (w2 + 3) * 16 + read-past margin, rounded to 128)
   int64_t pool_rows;               // n_img * ph
-  const int8_t* wd;                // [8 taps][2 K chunks][64 rows][16 B]
+  const int8_t* wd;                // [12 MMAs][2 K chunks][128 rows][16 B]
   const float* a_scale;            // per image
   float w_scale;
   const float* w_scale_ch;
@@ -102,11 +109,12 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// The conv rows a CTA computes, in order: for each image its pool rows [ra, rb) need
-// conv rows 2 ra .. 2 rb (pool row r reads conv rows 2r, 2r + 1, 2r + 2).
-struct RowIter {
+// The tiles a CTA computes, in order: for each image its pool rows [ra, rb) need conv
+// rows 2 ra .. 2 rb (pool row r reads conv rows 2r, 2r + 1, 2r + 2), i.e. the tiles
+// (2r, 2r + 1) for r = ra .. rb (the last tile's second row is not used).
+struct TileIter {
   int64_t g, g_end;   // global pool rows img * ph + r still to finish
-  int32_t img, ra, rb, y;
+  int32_t img, ra, rb, r;
   __device__ void start(int64_t g0, int64_t g1, int32_t ph) {
     g = g0;
     g_end = g1;
@@ -117,12 +125,12 @@ struct RowIter {
     ra = (int32_t)(g - (int64_t)img * ph);
     const int64_t left = g_end - g;
     rb = left < (int64_t)(ph - ra) ? ra + (int32_t)left : ph;
-    y = 2 * ra;
+    r = ra;
   }
   __device__ bool valid() const { return g < g_end; }
   __device__ void next(int32_t ph) {
-    if (y < 2 * rb) {
-      ++y;
+    if (r < rb) {
+      ++r;
       return;
     }
     g += rb - ra;
@@ -134,7 +142,7 @@ struct RowIter {
 // predicated selects (no branch).
 __device__ __forceinline__ float pool_fold(float best, float v) {
   float r;
-  asm("{\n .reg .pred p, q;\n setp.gt.f32 p, %2, %1;\n setp.nan.f32 q, %2, %2;\n or.pred p, p, q;\n"
+  asm("{\n .reg .pred p, q;\n setp.nan.f32 q, %2, %2;\n setp.gt.or.f32 p, %2, %1, q;\n"
       " selp.f32 %0, %2, %1, p;\n}"
       : "=f"(r)
       : "f"(best), "f"(v));
@@ -148,8 +156,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;                                            // [kRing][slot_bytes]
   uint8_t* wsm = ring + (size_t)kRing * p.slot_bytes;              // [kWBytes]
-  float* xch = reinterpret_cast<float*>(wsm + kWBytes);            // [2][4 parts][4 quadrants][16]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(xch + 2 * 4 * 4 * 16);
+  float* xch = reinterpret_cast<float*>(wsm + kWBytes);            // [2][4][16][64]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xch) + kXchBytes);
   uint64_t* full = bars;              // [kRing]
   uint64_t* empty = full + kRing;     // [kRing]
   uint64_t* tfull = empty + kRing;    // [2]
@@ -158,7 +166,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* done = wbar + 1;          // every MMA retired
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  constexpr int kTmemCols = 2 * BN;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int32_t wp = p.w2 + 3;  // 2 zero columns left, 1 right
@@ -191,18 +198,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       mbar_arrive_expect_tx(wbar, kWBytes);
       bulk_load(wsm, p.wd, kWBytes, wbar);
-      const uint32_t a_bytes = (uint32_t)(p.rbox * wp * 16);
+      const uint32_t a_bytes = (uint32_t)(kRbox * wp * 16);
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued_parity[kRing];
       bool issued[kRing];
       for (int s = 0; s < kRing; ++s) issued[s] = false;
-      RowIter it;
+      TileIter it;
       for (it.start(g0, g1, p.ph); it.valid(); it.next(p.ph)) {
         if (!mbar_wait(&empty[stage], phase ^ 1, abort)) break;
         mbar_arrive_expect_tx(&full[stage], a_bytes);
-        // padded rows y - 2 .. y - 2 + rbox - 1, columns from s2d pixel -2 (x = -4 eight-byte elements)
-        tma_load_3d(ring + (size_t)stage * p.slot_bytes, &map_in, &full[stage], -4, it.y - 2, it.img);
+        // padded s2d rows 2r - 2 .. 2r + 3, columns from s2d pixel -2 (x = -4 eight-byte elements)
+        tma_load_3d(ring + (size_t)stage * p.slot_bytes, &map_in, &full[stage], -4, 2 * it.r - 2, it.img);
         issued[stage] = true;
         issued_parity[stage] = phase;
         if (++stage == kRing) { stage = 0; phase ^= 1; }
@@ -216,28 +223,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_i8(BM, BN);
+      const uint32_t idesc = idesc_i8(128, p.n_mma);
       const uint32_t sw = smem_addr(wsm);
       int stage = 0;
       uint32_t phase = 0;
       int iter = 0;
       bool ok = mbar_wait(wbar, 0, abort);
       if (ok) tc_fence_after();
-      RowIter it;
+      TileIter it;
       for (it.start(g0, g1, p.ph); ok && it.valid(); it.next(p.ph), ++iter) {
         const int buf = iter & 1;
         const uint32_t aphase = (iter >> 1) & 1;
         if (!mbar_wait(&tempty[buf], aphase ^ 1, abort)) break;
         if (!mbar_wait(&full[stage], phase, abort)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(buf * p.n_mma);
         const uint32_t sa = smem_addr(ring + (size_t)stage * p.slot_bytes);
 #pragma unroll
-        for (int t = 0; t < kTaps; ++t) {
-          // taps (ay, ax) and (ay + 1, ax), ay = 2 (t / 4) - 2, ax = t % 4 - 2: padded row
-          // 2 (t / 4), padded column ox + t % 4
+        for (int t = 0; t < kMmas; ++t) {
+          // s2d rows 2r - 2 + 2 (t / 4) and the next one (K chunks one padded row apart),
+          // columns shifted by t % 4 - 2
           const uint32_t pos = (uint32_t)((t / 4) * 2 * wp + (t % 4));
-          mma_i8(d_tmem, desc_rows16(sa + pos * 16u, (uint32_t)wp * 16u), desc_rows16(sw + t * 2 * BN * 16, BN * 16),
+          mma_i8(d_tmem, desc_rows16(sw + t * 2 * 128 * 16, 128 * 16), desc_rows16(sa + pos * 16u, (uint32_t)wp * 16u),
                  idesc, t != 0);
         }
         mma_commit(&empty[stage]);
@@ -250,88 +257,80 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue ----------------
-    // Lane ox holds conv column ox of its 16 channels; the pool window's columns ox + 1
-    // and ox + 2 come from the neighbouring lanes (lane 30's ox + 2 from lane 0 of the
-    // next quadrant's warp, through shared memory); the row folds run in registers.
-    const int e = warp - 2;
-    const int q = warp & 3;                 // TMEM lane quadrant this warp may access
-    const int part = e >> 2;                // channels part * 16 .. + 15
-    const int32_t ox = q * 32 + lane;       // conv output column of this lane
-    const int32_t px = ox >> 1;
-    const bool centre = (ox & 1) == 0 && px < p.pw;  // the first column of pool window px
+    const int q = warp & 3;                 // TMEM lane quadrant: channel half q & 1, tile row q >> 1
+    const int k = (warp - 2) >> 2;          // column range: pool columns k * span .. + span - 1
+    const bool row0 = q < 2;                // this thread holds row y (else y + 1)
+    const int32_t c = (q & 1) * 32 + lane;  // channel
+    const int32_t px0 = k * p.span;
+    const int32_t npx = min(p.span, p.pw - px0);  // pool columns of this range (may be <= 0)
     const int32_t plane = p.ph * p.pw;
-    float bias_r[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) bias_r[j] = __ldg(p.bias + part * 16 + j);
+    const float bias_c = __ldg(p.bias + c);
+    const float wsc = p.w_scale_ch ? __ldg(p.w_scale_ch + c) : p.w_scale;
+    const int bar_id = 1 + k * 2 + (q & 1);  // the row-y and row-(y + 1) warps of this range and half
     int32_t cs_img = -1;
-    float sa = 0.0f, cs_t = 0.0f;           // the image's scale, times the tensor weight scale
-    float vs[16];                           // running window fold per channel (pool column px)
+    float cs = 0.0f;
+    float part[16];                         // fold of pool row r's first two rows (row y threads)
     float mx = 0.0f;
     int iter = 0;
-    RowIter it;
+    TileIter it;
     for (it.start(g0, g1, p.ph); it.valid(); it.next(p.ph), ++iter) {
       const int buf = iter & 1;
       const uint32_t aphase = (iter >> 1) & 1;
-      float o[16];
+      float h[16];                          // the window's row folded, per pool column
       const bool got = mbar_wait(&tfull[buf], aphase, abort);
       if (__all_sync(0xffffffffu, got)) {
         tc_fence_after();
-        uint32_t v[16];
-        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + part * 16), v);
+        uint32_t v[32];
+        const uint32_t ta = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * p.n_mma + 2 * px0);
+        tmem_ld16(ta, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+        tmem_ld16(ta + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
         tmem_ld_wait();
+        tc_fence_before();
         if (it.img != cs_img) {
           cs_img = it.img;
-          sa = p.a_scale[it.img];
-          cs_t = __fmul_rn(sa, p.w_scale);
+          cs = __fmul_rn(p.a_scale[it.img], wsc);
         }
+        float o[32];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float cs = p.w_scale_ch ? __fmul_rn(sa, __ldg(p.w_scale_ch + part * 16 + j)) : cs_t;
-          o[j] = epilogue_t<ACT>((int32_t)v[j], cs, bias_r[j], p.act_param);
-        }
-        tc_fence_before();
-        if (lane == 0) {
-          float* xs = xch + ((buf * 4 + part) * 4 + q) * 16;
+        for (int i = 0; i < 32; ++i) o[i] = epilogue_t<ACT>((int32_t)v[i], cs, bias_c, p.act_param);
+        // the window's columns 2 px, 2 px + 1, 2 px + 2 in the reference's order
 #pragma unroll
-          for (int j = 0; j < 16; ++j) xs[j] = o[j];
-        }
+        for (int j = 0; j < 15; ++j) h[j] = pool_fold(pool_fold(o[2 * j], o[2 * j + 1]), o[2 * j + 2]);
+        h[15] = o[30];
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
-      // the part's four quadrant warps: exchange published, accumulators all received
-      if (!bar_and(2 + part, 128, got)) {
+      float* xb = xch + ((size_t)(buf * 4 + k) * 16) * BN + c;  // [j][channel]
+      if (!row0) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) xb[j * BN] = h[j];
+      }
+      // the row-(y + 1) folds are published (and both warps got their accumulators)
+      if (!bar_and(bar_id, 64, got)) {
         *abort = 1;
         break;
       }
-      const bool first = it.y == 2 * it.ra;
-      const bool closes = !first && (it.y & 1) == 0;  // completes pool row y / 2 - 1
-      const float* xn = xch + ((buf * 4 + part) * 4 + ((q + 1) & 3)) * 16;
-      float* orow = p.out + ((int64_t)it.img * BN + part * 16) * plane + (it.y / 2 - 1) * p.pw + px;
+      if (row0) {
+        const bool emits = it.r > it.ra;   // completes pool row r - 1 with row 2r
+        const bool starts = it.r < it.rb;  // pool row r: rows 2r, 2r + 1 folded here
+        float* orow = p.out + ((int64_t)it.img * BN + c) * plane + (int64_t)(it.r - 1) * p.pw + px0;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float n1 = __shfl_down_sync(0xffffffffu, o[j], 1);
-        float n2 = __shfl_down_sync(0xffffffffu, o[j], 2);
-        if (lane == 30) n2 = xn[j];
-        // the window's row: columns 2 px, 2 px + 1, 2 px + 2 in the reference's order
-        const float h = pool_fold(pool_fold(o[j], n1), n2);
-        if (first) {
-          vs[j] = h;
-        } else if (!closes) {
-          vs[j] = pool_fold(vs[j], h);
-        } else {
-          const float best = pool_fold(vs[j], h);
-          if (centre) {
-            orow[(int64_t)j * plane] = best;
-            mx = fmaxf(mx, fabsf(best));
+        for (int j = 0; j < 16; ++j) {
+          if (j < npx) {
+            if (emits) {
+              const float best = pool_fold(part[j], h[j]);
+              orow[j] = best;
+              mx = fmaxf(mx, fabsf(best));
+            }
+            if (starts) part[j] = pool_fold(h[j], xb[j * BN]);
           }
-          vs[j] = h;
         }
       }
-      if (it.y == 2 * it.rb) {  // the image's last conv row in this CTA: flush its absmax
+      if (it.r == it.rb) {  // the image's last tile in this CTA: flush its absmax
         if (p.amax) {
           float m = mx;
 #pragma unroll
-          for (int k = 16; k > 0; k >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, k));
+          for (int o2 = 16; o2 > 0; o2 >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o2));
           if (lane == 0 && m > 0.0f) atomicMax(p.amax + (p.amax_per_image ? it.img : 0), __float_as_uint(m));
         }
         mx = 0.0f;
@@ -362,15 +361,6 @@ bool make_s2d_map(CUtensorMap* map, const void* base, int32_t n, int32_t h2, int
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int32_t stem_rbox(int32_t w2) {
-  const int32_t wp = w2 + 3;
-  // the last tap pair's second row, read at column up to 127 + 3 (positions past the
-  // image row are discarded), must stay inside the box
-  const int32_t need = 3 * wp + BM + 3;
-  const int32_t r = (need + wp - 1) / wp;
-  return r < 5 ? 5 : r;
-}
-
 template <int ACT>
 bool launch_t(const StemPoolArgs& a, int num_sms, cudaStream_t st) {
   StemParams p;
@@ -379,22 +369,24 @@ bool launch_t(const StemPoolArgs& a, int num_sms, cudaStream_t st) {
   p.w2 = a.w / 2;
   p.ph = (p.h2 - 3) / 2 + 1;
   p.pw = (p.w2 - 3) / 2 + 1;
-  p.rbox = stem_rbox(p.w2);
-  p.slot_bytes = (p.rbox * (p.w2 + 3) * 16 + 127) / 128 * 128;
+  p.n_mma = (p.w2 + 15) / 16 * 16;
+  p.span = (p.pw + 3) / 4;
+  // the last MMA's B rows reach n_mma - 1 + 3 columns into the sixth row
+  p.slot_bytes = (kRbox * (p.w2 + 3) * 16 + (p.n_mma - p.w2) * 16 + 127) / 128 * 128;
   p.pool_rows = a.n * p.ph;
   p.wd = a.wd;
   p.a_scale = a.a_scale; p.w_scale = a.w_scale; p.w_scale_ch = a.w_scale_ch; p.bias = a.bias;
   p.act_param = a.act_param; p.out = a.out;
   p.amax = a.amax.ptr;
   p.amax_per_image = a.amax.ptr && a.amax.elems_per_slot > 0;
-  const int smem = 1024 + kRing * p.slot_bytes + kWBytes + 2 * 4 * 4 * 16 * 4 + kBarBytes;
+  const int smem = 1024 + kRing * p.slot_bytes + kWBytes + kXchBytes + kBarBytes;
   if (smem > 227 * 1024) return false;
   static std::once_flag once;
   std::call_once(once, [] {
     cudaFuncSetAttribute(k_stem_pool<ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   });
   CUtensorMap mi;
-  if (!make_s2d_map(&mi, a.q, p.n_img, p.h2, p.w2, p.rbox)) return false;
+  if (!make_s2d_map(&mi, a.q, p.n_img, p.h2, p.w2, kRbox)) return false;
   const int64_t grid = p.pool_rows < num_sms ? p.pool_rows : num_sms;
   k_stem_pool<ACT><<<(unsigned)grid, kThreads, smem, st>>>(mi, p);
   return true;
@@ -406,30 +398,35 @@ bool stem_pool_shape_ok(int64_t n_img, int32_t c, int32_t h, int32_t w, int32_t 
                         int32_t out_channels, int32_t pool_k, int32_t pool_s) {
   if (k != 7 || stride != 2 || pad != 3 || c < 1 || c > 4 || out_channels != BN) return false;
   if (pool_k != 3 || pool_s != 2 || (h & 1) || (w & 1) || h < 6 || w < 6) return false;
-  if (w / 2 > 125 || n_img < 1 || n_img > 65535) return false;  // the M tile and the TMA box width
-  if (n_img * (int64_t)((h / 2 - 3) / 2 + 1) > ((int64_t)1 << 40)) return false;
+  // two accumulators of w/2 columns in TMEM (each epilogue warp reads 32 columns from
+  // 2 x ceil(pw / 4) x 3), 16 pool columns per range at most
+  if (w / 2 > kMaxW2 || n_img < 1 || n_img > 65535) return false;
   return tma_encode_fn() != nullptr;
 }
 
 size_t stem_weight_bytes() { return (size_t)kWBytes; }
 
-// w [64][C][7][7] quantized (reference layout) -> [8 taps][2 K chunks][64 rows][16 B]:
-// tap t = (ay pair t / 4, ax = t % 4 - 2), chunk kc: ay = 2 (t / 4) - 2 + kc; byte
-// (dy * 2 + dx) * 4 + c holds w[o][c][2 ay + dy + 3][2 ax + dx + 3] (zero outside 0..6).
+// w [64][C][7][7] quantized (reference layout) -> [12 MMAs][2 K chunks][128 rows][16 B]:
+// MMA t reads s2d rows 2r - 2 + 2 (t / 4) + kc (kc = K chunk) at column shift
+// ax = t % 4 - 2; row m < 64 is channel m of conv row 2r (tap ay = 2 (t / 4) - 2 + kc),
+// row m >= 64 channel m - 64 of conv row 2r + 1 (tap ay - 1); byte (dy * 2 + dx) * 4 + c
+// holds w[o][c][2 ay + dy + 3][2 ax + dx + 3], zero where a tap index leaves -2..1 or a
+// kernel index leaves 0..6.
 void stem_arrange_weights(const int8_t* wq, int32_t c, int8_t* out) {
   memset(out, 0, kWBytes);
-  for (int t = 0; t < kTaps; ++t)
-    for (int kc = 0; kc < 2; ++kc) {
-      const int ay = 2 * (t / 4) - 2 + kc, ax = t % 4 - 2;
-      for (int o = 0; o < BN; ++o)
+  for (int t = 0; t < kMmas; ++t)
+    for (int kc = 0; kc < 2; ++kc)
+      for (int m = 0; m < 128; ++m) {
+        const int o = m % BN, ay = 2 * (t / 4) - 2 + kc - m / BN, ax = t % 4 - 2;
+        if (ay < -2 || ay > 1) continue;
         for (int dy = 0; dy < 2; ++dy)
           for (int dx = 0; dx < 2; ++dx) {
             const int ky = 2 * ay + dy + 3, kx = 2 * ax + dx + 3;
             if (ky < 0 || ky > 6 || kx < 0 || kx > 6) continue;
             for (int ch = 0; ch < c; ++ch)
-              out[((t * 2 + kc) * BN + o) * 16 + (dy * 2 + dx) * 4 + ch] = wq[((o * c + ch) * 7 + ky) * 7 + kx];
+              out[((t * 2 + kc) * 128 + m) * 16 + (dy * 2 + dx) * 4 + ch] = wq[((o * c + ch) * 7 + ky) * 7 + kx];
           }
-    }
+      }
 }
 
 bool launch_stem_pool(const StemPoolArgs& a, int num_sms, cudaStream_t st) {

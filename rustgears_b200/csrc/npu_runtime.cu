@@ -710,6 +710,10 @@ struct RunPlan {
   size_t cov_bytes = 0;
   std::vector<uint8_t> block_start;  // op i starts a fused Conv-Pool-Conv-Pool block
   std::vector<uint8_t> stem_start;   // op i is a 7x7 / 2 stem conv fused with the MaxPool(3, 2) after it
+  // strided 1x1 / pad 0 shortcut convs: the op whose output is their block input (its
+  // direct-3x3 producer can take their absmax into its epilogue), else -1; and the
+  // reverse map, producer op -> shortcut op
+  std::vector<int> amax2_src, amax2_for;
 };
 
 // Ops that leave the main-path tensor as it is (reshape, saving a block input, a
@@ -793,6 +797,27 @@ static rg_status make_plan(const Session& s, const int64_t* shape, int32_t ndim,
       P.amax_src[i] = j;
   }
   P.total_slots = off;
+  P.amax2_src.assign(n, -1);
+  P.amax2_for.assign(n, -1);
+  for (size_t i = 0; i < n; ++i) {
+    const Op& op = s.ops[i];
+    if (op.kind != RG_LAYER_SHORTCUT_CONV2D || op.k != 1 || op.pad != 0 || op.stride < 2 ||
+        (s.flags & RG_SESSION_NO_FUSION))
+      continue;
+    int depth = 0, b = -1;  // the residual begin that opens the shortcut's block
+    for (int j = (int)i - 1; j >= 0 && b < 0; --j) {
+      if (s.ops[(size_t)j].kind == RG_LAYER_RESIDUAL_END) ++depth;
+      if (s.ops[(size_t)j].kind == RG_LAYER_RESIDUAL_BEGIN) {
+        if (depth == 0) b = j;
+        else --depth;
+      }
+    }
+    int j = b - 1;
+    while (j >= 0 && main_path_noop(s.ops[(size_t)j].kind)) --j;
+    if (b < 0 || j < 0 || P.amax2_for[(size_t)j] >= 0) continue;
+    P.amax2_src[i] = j;
+    P.amax2_for[(size_t)j] = (int)i;
+  }
   P.block_start.assign(n, 0);
   P.stem_start.assign(n, 0);
   for (size_t i = 0; i < n; ++i)
@@ -960,6 +985,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
 
   RG_PENDING("the first launch");
   bool fused_residual = false;
+  std::vector<uint8_t> amax2_done(n, 0);  // a shortcut's absmax came from its block input's producer
   const float* cur = x_dev;
   int32_t launches = 0;
   s.ev_of.assign(n + 1, 0);
@@ -1142,19 +1168,32 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         } else {
           const int64_t N = os.in[0];
           const int32_t C = op.in_c, H = (int32_t)os.in[2], W = (int32_t)os.in[3];
-          if (P.amax_src[i] < 0) { launch_image_absmax(src, N, C, H, W, rc[i], cc[i], my_amax, st); ++launches; RG_LAUNCHED("image_absmax"); }
+          if (P.amax_src[i] < 0 && !amax2_done[i]) {
+            launch_image_absmax(src, N, C, H, W, rc[i], cc[i], my_amax, st);
+            ++launches;
+            RG_LAUNCHED("image_absmax");
+          }
           // the direct 3x3 kernel reads 16-channel chunk planes; every other conv, NHWC
           use3 = op.kind == RG_LAYER_CONV2D && op.d_w3.p && !s.trace &&
                  conv3x3_shape_ok(N, H, W, op.cpad, op.k, op.stride, op.pad, op.out_c);
+          // a strided 1x1 / pad 0 conv reads every s-th row and column: only those pixels
+          // are quantized, into a compact operand, and the conv runs as a 1x1 / stride 1
+          // conv over it
+          const bool sub = op.k == 1 && op.pad == 0 && op.stride > 1 && !s.trace && (op.cpad & 15) == 0 &&
+                           N <= 65535;
           const bool bounded = rc[i] == nullptr;  // the absmax covers every pixel quantized
           if (use3) launch_image_quantize_planar16(src, N, C, H, W, op.cpad, bounded, my_amax, q, my_scale, st);
+          else if (sub)
+            launch_image_quantize_subsampled(src, N, C, H, W, op.stride, (int32_t)os.out[2], (int32_t)os.out[3],
+                                             op.cpad, my_amax, q, my_scale, st);
           else launch_image_quantize_nhwc(src, N, C, H, W, op.cpad, bounded, my_amax, q, my_scale, st);
           ++launches;
           RG_LAUNCHED("image_quantize");
           g.a = q; g.conv = true;
           // padded channels hold zeros in both operands: the reduction runs over cpad per tap
-          g.g.h = H; g.g.w = W; g.g.c = op.cpad; g.g.cpad = op.cpad; g.g.k = op.k; g.g.kxp = op.kxp;
-          g.g.stride = op.stride;
+          g.g.h = sub ? (int32_t)os.out[2] : H; g.g.w = sub ? (int32_t)os.out[3] : W;
+          g.g.c = op.cpad; g.g.cpad = op.cpad; g.g.k = op.k; g.g.kxp = op.kxp;
+          g.g.stride = sub ? 1 : op.stride;
           g.g.pad = op.pad;
           g.g.oh = (int32_t)os.out[2]; g.g.ow = (int32_t)os.out[3];
           const int64_t L = os.out[2] * os.out[3];
@@ -1201,6 +1240,16 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
           }
           g.amax = rsink;
           fused_residual = true;
+        }
+        // the absmax of a later strided shortcut over this op's output (its block input)
+        const int sc = use3 ? P.amax2_for[fused_residual ? i + 1 : i] : -1;
+        if (sc >= 0 && !amax2_done[(size_t)sc] && P.shapes[(size_t)sc].in[2] == os.out[2] &&
+            P.shapes[(size_t)sc].in[3] == os.out[3]) {
+          g.amax2 = amax + P.amax_off[(size_t)sc];
+          g.cov_s = s.ops[(size_t)sc].stride;
+          g.cov_oh = (int32_t)P.shapes[(size_t)sc].out[2];
+          g.cov_ow = (int32_t)P.shapes[(size_t)sc].out[3];
+          amax2_done[(size_t)sc] = 1;
         }
         if (use3 && (!conv3x3_eligible(g) || !launch_conv3x3(g, op.d_w3.as<int8_t>(), s.num_sms, st)))
           return fail(RG_ERR_CUDA, "op %zu: the direct 3x3 conv could not be launched", i);

@@ -41,6 +41,13 @@ void launch_image_quantize_planar16(const float* x, int64_t n, int32_t c, int32_
 // (dy * 2 + dx) * 4 + ch), per-image scales: the input layout of the fused stem.
 void launch_image_quantize_s2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, const unsigned* amax_bits,
                                int8_t* q, float* scales_out, cudaStream_t st);
+// The pixels a 1x1 / pad 0 / stride s conv reads, (s * oy, s * ox) for oy < oh, ox < ow,
+// quantized with the per-image scale of their own absmax into a compact NHWC operand
+// [n][oh][ow][cpad] (cpad a multiple of 16, n <= 65535): the conv becomes a 1x1
+// stride-1 conv over it.
+void launch_image_quantize_subsampled(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t s,
+                                      int32_t oh, int32_t ow, int32_t cpad, const unsigned* amax_bits, int8_t* q,
+                                      float* scales_out, cudaStream_t st);
 // NHWC i8 (cpad) -> NCHW i8 (c) for traces.
 void launch_nhwc_to_nchw_i8(const int8_t* q, int64_t n, int32_t c, int32_t cpad, int32_t h,
                             int32_t w, int8_t* out, cudaStream_t st);
@@ -84,6 +91,10 @@ struct GemmArgs {
   const float* residual = nullptr;
   int32_t res_act = 0;
   float res_param = 0.0f;
+  // direct 3x3 conv only: a second per-image absmax of out over the pixels a later
+  // 1x1 / pad 0 / stride cov_s conv reads (rows and columns cov_s * i, i < cov_oh / cov_ow)
+  unsigned* amax2 = nullptr;
+  int32_t cov_s = 1, cov_oh = 0, cov_ow = 0;
 };
 
 void launch_gemm_simt(const GemmArgs& a, cudaStream_t st);

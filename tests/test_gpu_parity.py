@@ -334,8 +334,8 @@ def test_direct_3x3_conv(gpu, oracle_lib, b, c, n, h, w, act):
         assert_same(session_for(blk).run(x), ref2, "residual")
 
 
-@pytest.mark.parametrize("b,c,h,w,act", [(2, 3, 224, 224, 1), (3, 1, 32, 46, 0), (1, 4, 20, 226, 5), (5, 2, 8, 8, 4),
-                                         (2, 3, 64, 30, 2)])
+@pytest.mark.parametrize("b,c,h,w,act", [(2, 3, 224, 224, 1), (3, 1, 32, 46, 0), (1, 4, 20, 224, 5), (5, 2, 8, 8, 4),
+                                         (2, 3, 64, 30, 2), (1, 3, 14, 230, 1)])
 def test_fused_stem(gpu, oracle_lib, b, c, h, w, act):
     """Conv(k7 s2 p3 -> 64) + activation + MaxPool(3, 2), the ResNet stem: one kernel over
     the space-to-depth operand with the pool folded into the conv's epilogue, against the
@@ -353,7 +353,23 @@ def test_fused_stem(gpu, oracle_lib, b, c, h, w, act):
     ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
     sess = session_for(layers)
     assert_same(sess.run(x), ref, f"stem {c}ch {h}x{w}")
-    assert sess.last_npu_profile().kernel_launches == 3  # absmax, s2d quantizer, fused stem
+    if w // 2 <= 112:  # rows up to 112 conv columns wide: absmax, s2d quantizer, fused stem
+        assert sess.last_npu_profile().kernel_launches == 3
     plain = session_for(layers, flags=_native.RG_SESSION_NO_FUSION)
     assert_same(plain.run(x), ref, "unfused")
     assert plain.last_npu_profile().kernel_launches > 3
+
+
+@pytest.mark.parametrize("batch,image", [(3, 96), (2, 112), (2, 130)])
+def test_resnet_two_stage_paths(gpu, oracle_lib, batch, image):
+    """ResNet-18 widths (64, 128) at small images: the fused stem, direct 3x3 convs with
+    the block's residual add, the stage-2 projection shortcut (its covered-pixel absmax
+    taken in the epilogue of the conv that writes its block input, its compact
+    every-other-pixel operand), against the oracle; one image holds an inf."""
+    layers, x = configs.resnet(batch, image, (64, 128), 10, seed=image)
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=16)
+    assert_same(session_for(layers).run(x), ref, f"resnet {image}")
+    x = x.copy()
+    x[batch - 1, 1, 5, 7] = np.inf
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=16)
+    assert_same(session_for(layers).run(x), ref, f"resnet {image} with inf")
