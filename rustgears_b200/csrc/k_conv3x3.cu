@@ -56,6 +56,7 @@ constexpr int kBarBytes = 256;
 
 struct C3Params {
   int32_t n_img, h, w, cpad, n;    // n: output channels
+  int32_t n_pad;                   // n rounded up to BN (staged per-channel constants)
   int32_t tiles_m, tiles_n, stages_k;  // tiles per image, N tiles, 64-channel stages
   int32_t rbox;                    // padded rows per TMA box
   int32_t plane_bytes;             // rbox * (w + 2) * 16: what one TMA load writes
@@ -127,6 +128,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* done = tempty + 2;        // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // per-channel bias and weight scales, [n_pad] each (n_pad = n rounded up to BN)
+  float* bias_s = reinterpret_cast<float*>(smem + (size_t)p.ring * p.stage_bytes + kBarBytes);
+  float* wsc_s = bias_s + p.n_pad;
   constexpr int kBBytes = 9 * 4 * BN * 16;
   constexpr int kTmemCols = 2 * BN;
 
@@ -147,6 +151,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort = 0;
     fence_mbar_init();
     tma_prefetch_desc(&map_in);
+  }
+  for (int32_t i = threadIdx.x; i < p.n_pad; i += kThreads) {
+    bias_s[i] = i < p.n ? p.bias[i] : 0.0f;
+    wsc_s[i] = i < p.n && p.w_scale_ch ? p.w_scale_ch[i] : 0.0f;
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before();
@@ -234,37 +242,62 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;           // TMEM lane quadrant this warp may access
     const int part = e >> 2;          // which quarter of the BN columns
     constexpr int kCols = BN / (kEpiWarps / 4);
-    const int64_t hw = (int64_t)p.h * p.w;
-    int iter = 0;
-    for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++iter) {
-      int32_t img, mt, nb;
+    const int32_t hw = p.h * p.w;     // n * hw < 2^31 (conv3x3_eligible)
+    const int64_t img_stride = (int64_t)p.n * hw;
+    // Per tile and lane: the centre position, whether it is an image pixel, its pixel index.
+    auto lane_pixel = [&](int64_t tile, int32_t& img, int32_t& nb, bool& valid, int32_t& pix, int32_t& iy,
+                          int32_t& ix) {
+      int32_t mt;
       c3_coords(tile, p, img, mt, nb);
-      const int buf = iter & 1;
-      const uint32_t aphase = (iter >> 1) & 1;
       const int32_t f = wp + 1 + BM * mt + q * 32 + lane;  // this lane's centre position
       const int32_t py = f / wp, px = f - py * wp;
-      const bool valid = py >= 1 && py <= p.h && px >= 1 && px <= p.w;
+      valid = py >= 1 && py <= p.h && px >= 1 && px <= p.w;
+      iy = py - 1;
+      ix = px - 1;
+      pix = valid ? iy * p.w + ix : 0;
+    };
+    // The residual block's add: res[] holds the residual of the tile being processed; as
+    // each value is used, the load of the same channel for the CTA's next tile is issued
+    // in its place, so the loads are in flight for a whole tile.
+    float res[kCols];
+    if (p.residual) {
+      int32_t img, nb, pix, iy, ix;
+      bool valid;
+      lane_pixel(blockIdx.x, img, nb, valid, pix, iy, ix);
+      const int32_t colw = nb * BN + part * kCols;
+      const float* rb = p.residual + (int64_t)img * img_stride + pix;
+#pragma unroll
+      for (int j = 0; j < kCols; ++j) res[j] = valid && colw + j < p.n ? __ldg(rb + (colw + j) * hw) : 0.0f;
+    }
+    int iter = 0;
+    for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++iter) {
+      int32_t img, nb, pix, iy, ix;
+      bool valid;
+      lane_pixel(tile, img, nb, valid, pix, iy, ix);
+      const int buf = iter & 1;
+      const uint32_t aphase = (iter >> 1) & 1;
       // read by the later strided 1x1 conv: rows and columns cov_s * i, i < cov_oh / cov_ow
-      const int32_t iy = py - 1, ix = px - 1;
       const bool cov2 = valid && p.amax2 && iy % p.cov_s == 0 && ix % p.cov_s == 0 && iy / p.cov_s < p.cov_oh &&
                         ix / p.cov_s < p.cov_ow;
-      const int64_t pix = valid ? (int64_t)(py - 1) * p.w + (px - 1) : 0;
+      const int32_t colw = nb * BN + part * kCols;  // this warp's first column
       const float sa = p.a_scale[img];
       const float cs_tensor = __fmul_rn(sa, p.w_scale);
-      float* obase = p.out + (int64_t)img * p.n * hw + pix;
-      const float* rbase = p.residual ? p.residual + (int64_t)img * p.n * hw + pix : nullptr;
-      const int32_t colw = nb * BN + part * kCols;  // this warp's first column
-      // the residual values do not depend on the accumulator: their loads are in flight
-      // while the MMAs of this tile finish
-      float res[kCols];
-      if (rbase) {
-#pragma unroll
-        for (int j = 0; j < kCols; ++j)
-          res[j] = valid && colw + j < p.n ? __ldg(rbase + (int64_t)(colw + j) * hw) : 0.0f;
+      float* ob = p.out + (int64_t)img * img_stride + colw * hw + pix;
+      // the next tile's residual (rolling prefetch)
+      const float* rn = nullptr;
+      int32_t ncols = 0;
+      if (p.residual && tile + gridDim.x < num_tiles) {
+        int32_t img2, nb2, pix2, iy2, ix2;
+        bool valid2;
+        lane_pixel(tile + gridDim.x, img2, nb2, valid2, pix2, iy2, ix2);
+        const int32_t colw2 = nb2 * BN + part * kCols;
+        rn = p.residual + (int64_t)img2 * img_stride + colw2 * hw + pix2;
+        ncols = valid2 ? p.n - colw2 : 0;  // columns of the next tile this lane loads
       }
       const bool got = mbar_wait(&tfull[buf], aphase, abort);
       if (!__all_sync(0xffffffffu, got)) { *abort = 1; break; }
       tc_fence_after();
+      const bool fast = !p.acc && colw + kCols <= p.n;  // every column exists, no i32 dump
       float mx = 0.0f, mx2 = 0.0f;
 #pragma unroll
       for (int cc = 0; cc < kCols; cc += 16) {
@@ -272,27 +305,73 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();  // the warp-wide TMEM load runs converged
         tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + part * kCols + cc), v);
         tmem_ld_wait();
-        const int32_t col0 = colw + cc;
-        if (valid && col0 < p.n) {
+        if (fast) {
+          // per-channel constants from shared memory (16-byte loads, all lanes the same address)
+          float bz[16], cz[16];
+#pragma unroll
+          for (int j4 = 0; j4 < 16; j4 += 4) {
+            const float4 b4 = *reinterpret_cast<const float4*>(bias_s + colw + cc + j4);
+            bz[j4] = b4.x; bz[j4 + 1] = b4.y; bz[j4 + 2] = b4.z; bz[j4 + 3] = b4.w;
+            if (p.w_scale_ch) {
+              const float4 w4 = *reinterpret_cast<const float4*>(wsc_s + colw + cc + j4);
+              cz[j4] = __fmul_rn(sa, w4.x); cz[j4 + 1] = __fmul_rn(sa, w4.y);
+              cz[j4 + 2] = __fmul_rn(sa, w4.z); cz[j4 + 3] = __fmul_rn(sa, w4.w);
+            } else {
+              cz[j4] = cz[j4 + 1] = cz[j4 + 2] = cz[j4 + 3] = cs_tensor;
+            }
+          }
+          float o[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] = epilogue_t<ACT>((int32_t)v[j], cz[j], bz[j], p.act_param);
+          if (p.residual) {  // the residual block's activation: none, ReLU or LeakyReLU
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              o[j] = __fadd_rn(o[j], res[cc + j]);
+              res[cc + j] = cc + j < ncols ? __ldg(rn + (cc + j) * hw) : 0.0f;
+            }
+            if (p.res_act == ACT_RELU) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) o[j] = fmaxf(o[j], 0.0f);
+            } else if (p.res_act == ACT_LEAKY_RELU) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) o[j] = o[j] > 0.0f ? o[j] : __fmul_rn(p.res_param, o[j]);
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            if (valid) ob[(cc + j) * hw] = o[j];
+            mx = fmaxf(mx, fabsf(o[j]));
+          }
+          if (p.amax2) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) mx2 = fmaxf(mx2, fabsf(o[j]));
+          }
+        } else {
+          const int32_t col0 = colw + cc;
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int32_t c = col0 + j;
             if (c < p.n) {
               const float cs = p.w_scale_ch ? __fmul_rn(sa, __ldg(p.w_scale_ch + c)) : cs_tensor;
               float o = epilogue_t<ACT>((int32_t)v[j], cs, __ldg(p.bias + c), p.act_param);
-              if (rbase) {  // the residual block's activation: none, ReLU or LeakyReLU
+              if (p.residual) {
                 o = __fadd_rn(o, res[cc + j]);
                 if (p.res_act == ACT_RELU) o = fmaxf(o, 0.0f);
                 else if (p.res_act == ACT_LEAKY_RELU) o = o > 0.0f ? o : __fmul_rn(p.res_param, o);
               }
-              obase[(int64_t)c * hw] = o;
-              if (p.acc) p.acc[(int64_t)img * p.n * hw + (int64_t)c * hw + pix] = (int32_t)v[j];
+              if (valid) {
+                ob[(cc + j) * hw] = o;
+                if (p.acc) p.acc[(int64_t)img * img_stride + (int64_t)c * hw + pix] = (int32_t)v[j];
+              }
               mx = fmaxf(mx, fabsf(o));
-              if (cov2) mx2 = fmaxf(mx2, fabsf(o));
+              mx2 = fmaxf(mx2, fabsf(o));
             }
+            if (p.residual) res[cc + j] = cc + j < ncols ? __ldg(rn + (cc + j) * hw) : 0.0f;
           }
         }
       }
+      if (!valid) mx = 0.0f;   // padding positions: computed, not part of the output
+      if (!cov2) mx2 = 0.0f;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
@@ -339,10 +418,11 @@ bool launch_bn(const GemmArgs& a, const int8_t* wd, int num_sms, cudaStream_t st
   p.plane_stride = (p.plane_bytes + 127) / 128 * 128;
   const int a_bytes = 4 * p.plane_stride;
   p.stage_bytes = (a_bytes + 9 * 4 * BN * 16 + 1023) / 1024 * 1024;
-  p.ring = (227 * 1024 - 1024 - kBarBytes) / p.stage_bytes;
+  p.ring = (227 * 1024 - 1024 - kBarBytes - 2 * p.tiles_n * BN * 4) / p.stage_bytes;
   if (p.ring > 8) p.ring = 8;
   if (p.ring < 2) return false;
-  const int smem = 1024 + p.ring * p.stage_bytes + kBarBytes;
+  p.n_pad = p.tiles_n * BN;
+  const int smem = 1024 + p.ring * p.stage_bytes + kBarBytes + 2 * p.n_pad * 4;
   static std::once_flag once;
   std::call_once(once, [] {
     cudaFuncSetAttribute(k_conv3x3<BN, ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
@@ -391,6 +471,7 @@ bool conv3x3_eligible(const GemmArgs& a) {
   if (a.g.c != a.g.cpad || a.g.oh != a.g.h || a.g.ow != a.g.w) return false;
   if (!conv3x3_shape_ok(a.m / a.out_l, a.g.h, a.g.w, a.g.cpad, a.g.k, a.g.stride, a.g.pad, (int32_t)a.n)) return false;
   if (a.amax.ptr && a.amax.elems_per_slot != 0 && a.amax.elems_per_slot != a.n * a.out_l) return false;
+  if (a.n * a.out_l >= ((int64_t)1 << 31)) return false;  // per-image offsets in 32 bits
   if (reinterpret_cast<uintptr_t>(a.a) & 15) return false;
   if (a.m * a.n * a.k < (int64_t)1 << 22) return false;
   return tma_encode_fn() != nullptr;
