@@ -34,8 +34,9 @@
 //              accumulators
 //   warps 2-17 epilogue: warp w reads TMEM lane quadrant w % 4 (channel half, row of
 //              the tile) and conv columns 28 (w - 2) / 4 ..; act(f32(acc) * (s_img *
-//              s_w) + bias), the window folds, NCHW pool stores (row y threads) and
-//              the per-image absmax of the pooled tensor
+//              s_w) + bias), the window folds, the pooled row staged in shared memory
+//              and stored a channel row at a time, the per-image absmax of the pooled
+//              tensor
 // Every mbarrier wait is bounded; on timeout the CTA raises an abort flag, the roles
 // leave their loops together, copies and MMAs in flight are drained, TMEM is freed and
 // a device error word is set for the host.
@@ -60,10 +61,13 @@ using namespace sm100;
 
 constexpr int BN = 64;           // output channels
 constexpr int kEpiWarps = 16;    // 4 per TMEM lane quadrant, one column range each
-constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kThreads = 64 + kEpiThreads;
 constexpr int kMmas = 12;        // per tile: (s2d row pair 0..2) x (column shift 0..3)
 constexpr int kWBytes = kMmas * 2 * 128 * 16;  // 48 KB of arranged weights
-constexpr int kXchBytes = 2 * 4 * 16 * BN * 4; // [2 buffers][4 column ranges][16 px][64 channels] f32
+constexpr int kXchBytes = 4 * 16 * BN * 4;     // [4 column ranges][16 px][64 channels] f32
+constexpr int kStgPitch = 57;                  // staged pool row: [64 channels][57] f32 (odd pitch)
+constexpr int kStgBytes = BN * kStgPitch * 4;
 constexpr int kRbox = 6;         // padded s2d rows per tile: y - 2 .. y + 3
 constexpr int kTmemCols = 256;   // two accumulators of up to 112 columns
 constexpr int kMaxW2 = 112;
@@ -140,6 +144,10 @@ struct TileIter {
 
 // One step of the reference's window scan, best = (v > best || v is NaN) ? v : best, as
 // predicated selects (no branch).
+__device__ __forceinline__ void named_bar(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 __device__ __forceinline__ float pool_fold(float best, float v) {
   float r;
   asm("{\n .reg .pred p, q;\n setp.nan.f32 q, %2, %2;\n setp.gt.or.f32 p, %2, %1, q;\n"
@@ -156,8 +164,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;                                            // [kRing][slot_bytes]
   uint8_t* wsm = ring + (size_t)kRing * p.slot_bytes;              // [kWBytes]
-  float* xch = reinterpret_cast<float*>(wsm + kWBytes);            // [2][4][16][64]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xch) + kXchBytes);
+  float* xch = reinterpret_cast<float*>(wsm + kWBytes);            // [4][16][64]
+  float* stg = xch + kXchBytes / 4;                                // [64][kStgPitch]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(stg) + kStgBytes);
   uint64_t* full = bars;              // [kRing]
   uint64_t* empty = full + kRing;     // [kRing]
   uint64_t* tfull = empty + kRing;    // [2]
@@ -257,6 +266,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue ----------------
+    // Per tile: (A) every warp folds its 32 columns' windows; the row-(y + 1) warps
+    // publish theirs; (B) the row-y warps fold the rows and stage the finished pool row
+    // r - 1 in shared memory as [channel][column]; (C) all warps store it, a channel row
+    // per store instruction (coalesced).
     const int q = warp & 3;                 // TMEM lane quadrant: channel half q & 1, tile row q >> 1
     const int k = (warp - 2) >> 2;          // column range: pool columns k * span .. + span - 1
     const bool row0 = q < 2;                // this thread holds row y (else y + 1)
@@ -266,7 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int32_t plane = p.ph * p.pw;
     const float bias_c = __ldg(p.bias + c);
     const float wsc = p.w_scale_ch ? __ldg(p.w_scale_ch + c) : p.w_scale;
-    const int bar_id = 1 + k * 2 + (q & 1);  // the row-y and row-(y + 1) warps of this range and half
+    float* xb = xch + (size_t)(k * 16) * BN + c;  // [j][channel]
     int32_t cs_img = -1;
     float cs = 0.0f;
     float part[16];                         // fold of pool row r's first two rows (row y threads)
@@ -290,9 +303,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           cs_img = it.img;
           cs = __fmul_rn(p.a_scale[it.img], wsc);
         }
+        // |acc| <= 147 taps x 127 x 127 < 2^22
         float o[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = epilogue_t<ACT>((int32_t)v[i], cs, bias_c, p.act_param);
+        for (int i = 0; i < 32; ++i) o[i] = epilogue_small_t<ACT>((int32_t)v[i], cs, bias_c, p.act_param);
         // the window's columns 2 px, 2 px + 1, 2 px + 2 in the reference's order
 #pragma unroll
         for (int j = 0; j < 15; ++j) h[j] = pool_fold(pool_fold(o[2 * j], o[2 * j + 1]), o[2 * j + 2]);
@@ -300,30 +314,55 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
-      float* xb = xch + ((size_t)(buf * 4 + k) * 16) * BN + c;  // [j][channel]
       if (!row0) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) xb[j * BN] = h[j];
       }
-      // the row-(y + 1) folds are published (and both warps got their accumulators)
-      if (!bar_and(bar_id, 64, got)) {
+      // (A) done everywhere: the row-(y + 1) folds are published, every accumulator read
+      if (!bar_and(1, kEpiThreads, got)) {
         *abort = 1;
         break;
       }
+      const bool emits = it.r > it.ra;   // completes pool row r - 1 with row 2r
+      const bool starts = it.r < it.rb;  // pool row r: rows 2r, 2r + 1 folded here
       if (row0) {
-        const bool emits = it.r > it.ra;   // completes pool row r - 1 with row 2r
-        const bool starts = it.r < it.rb;  // pool row r: rows 2r, 2r + 1 folded here
-        float* orow = p.out + ((int64_t)it.img * BN + c) * plane + (int64_t)(it.r - 1) * p.pw + px0;
+        // all shared-memory loads first: the stores below may not be reordered above them
+        float hn[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if (j < npx) {
-            if (emits) {
-              const float best = pool_fold(part[j], h[j]);
-              orow[j] = best;
+        for (int j = 0; j < 16; ++j) hn[j] = xb[j * BN];
+        if (emits) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float best = pool_fold(part[j], h[j]);
+            if (j < npx) {
+              stg[c * kStgPitch + px0 + j] = best;
               mx = fmaxf(mx, fabsf(best));
             }
-            if (starts) part[j] = pool_fold(h[j], xb[j * BN]);
           }
+        }
+        if (starts) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) part[j] = pool_fold(h[j], hn[j]);
+        }
+      }
+      // (B) done: pool row r - 1 staged, the row-(y + 1) folds read (the exchange buffer
+      // is free for the next tile)
+      named_bar(2, kEpiThreads);
+      if (emits) {
+        // (C) warp e stores channels 4e .. 4e + 3 of pool row r - 1
+        const int e = warp - 2;
+        float* orow = p.out + ((int64_t)it.img * BN + 4 * e) * plane + (int64_t)(it.r - 1) * p.pw;
+        // columns lane and lane + 32 (pw <= 56 < 64), staged rows are kStgPitch = 57 wide
+        float sv[8];
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          sv[2 * cc] = stg[(4 * e + cc) * kStgPitch + lane];
+          sv[2 * cc + 1] = lane + 32 < kStgPitch ? stg[(4 * e + cc) * kStgPitch + lane + 32] : 0.0f;
+        }
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          if (lane < p.pw) orow[(int64_t)cc * plane + lane] = sv[2 * cc];
+          if (lane + 32 < p.pw) orow[(int64_t)cc * plane + lane + 32] = sv[2 * cc + 1];
         }
       }
       if (it.r == it.rb) {  // the image's last tile in this CTA: flush its absmax
@@ -379,7 +418,7 @@ bool launch_t(const StemPoolArgs& a, int num_sms, cudaStream_t st) {
   p.act_param = a.act_param; p.out = a.out;
   p.amax = a.amax.ptr;
   p.amax_per_image = a.amax.ptr && a.amax.elems_per_slot > 0;
-  const int smem = 1024 + kRing * p.slot_bytes + kWBytes + kXchBytes + kBarBytes;
+  const int smem = 1024 + kRing * p.slot_bytes + kWBytes + kXchBytes + kStgBytes + kBarBytes;
   if (smem > 227 * 1024) return false;
   static std::once_flag once;
   std::call_once(once, [] {

@@ -415,5 +415,23 @@ RG_HD float epilogue_t(int32_t acc, float cs, float bias, float p) {
   return epilogue(acc, cs, bias, ACT, p);
 }
 
+// f32(acc) for |acc| < 2^22 without a conversion instruction: 1.5 * 2^23 + acc is an
+// integer in [2^23, 2^24), where f32 spacing is exactly 1, so its bit pattern is
+// 0x4B400000 + acc and subtracting 1.5 * 2^23 is exact.  Equal to the round-to-nearest
+// conversion on that range (both exact).
+RG_HD float small_i32_to_f32(int32_t acc) {
+#ifdef __CUDA_ARCH__
+  return __fsub_rn(__int_as_float(0x4B400000 + acc), 12582912.0f);
+#else
+  return (float)acc;
+#endif
+}
+
+// epilogue_t for accumulators known to satisfy |acc| < 2^22.
+template <int ACT>
+RG_HD float epilogue_small_t(int32_t acc, float cs, float bias, float p) {
+  return act_apply(ACT, p, RG_ADD(RG_MUL(small_i32_to_f32(acc), cs), bias));
+}
+
 
 }  // namespace rg
