@@ -33,6 +33,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 
@@ -59,6 +60,10 @@ struct C3Params {
   int32_t n_pad;                   // n rounded up to BN (staged per-channel constants)
   int32_t tiles_m, tiles_n, stages_k;  // tiles per image, N tiles, 64-channel stages
   int32_t rbox;                    // padded rows per TMA box
+  int32_t wp, pad_t, pad_l;        // padded row length; zero rows / columns before the image
+  int32_t f0;                      // flat position of output (0, 0): pad_t * wp + pad_l
+  int32_t min_off;                 // smallest tap offset (flat positions)
+  int32_t toff[9];                 // tap offsets relative to the centre, dy * wp + dx
   int32_t plane_bytes;             // rbox * (w + 2) * 16: what one TMA load writes
   int32_t plane_stride;            // plane_bytes rounded up to 128 (TMA destination alignment)
   int32_t stage_bytes, ring;       // bytes per ring slot (A planes + weights), slots
@@ -115,7 +120,7 @@ __device__ __forceinline__ void flush_slot_max(unsigned* base, int64_t slot, flo
   if ((threadIdx.x & 31) == 0 && v > 0.0f && slot >= 0) atomicMax(base + slot, __float_as_uint(v));
 }
 
-template <int BN, int ACT>
+template <int BN, int ACT, int TAPS>
 __global__ void __launch_bounds__(kThreads, 1)
     k_conv3x3(const __grid_constant__ CUtensorMap map_in, const C3Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -131,12 +136,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   // per-channel bias and weight scales, [n_pad] each (n_pad = n rounded up to BN)
   float* bias_s = reinterpret_cast<float*>(smem + (size_t)p.ring * p.stage_bytes + kBarBytes);
   float* wsc_s = bias_s + p.n_pad;
-  constexpr int kBBytes = 9 * 4 * BN * 16;
+  constexpr int kBBytes = TAPS * 4 * BN * 16;
   constexpr int kTmemCols = 2 * BN;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t num_tiles = (int64_t)p.n_img * p.tiles_m * p.tiles_n;
-  const int32_t wp = p.w + 2;
+  const int32_t wp = p.wp;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.ring; ++s) {
@@ -176,14 +181,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         int32_t img, mt, nb;
         c3_coords(tile, p, img, mt, nb);
-        const int32_t r_lo = (BM * mt) / wp;  // first padded row the tile reads
+        const int32_t r_lo = (p.f0 + BM * mt + p.min_off) / wp;  // first padded row the tile reads
         for (int s = 0; s < p.stages_k; ++s) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort)) { ok = false; break; }
           uint8_t* sa = smem + (size_t)stage * p.stage_bytes;
           mbar_arrive_expect_tx(&full[stage], a_bytes + kBBytes);
 #pragma unroll
-          for (int j = 0; j < 4; ++j)  // chunk plane j: channels s*64 + 16j .. +15; x from pixel -1
-            tma_load_4d(sa + j * p.plane_stride, &map_in, &full[stage], -2, r_lo - 1, s * 4 + j, img);
+          for (int j = 0; j < 4; ++j)  // chunk plane j: channels s*64 + 16j .. +15; x from pixel -pad_l
+            tma_load_4d(sa + j * p.plane_stride, &map_in, &full[stage], -2 * p.pad_l, r_lo - p.pad_t, s * 4 + j, img);
           bulk_load(sa + a_span, p.wd + ((int64_t)nb * p.stages_k + s) * kBBytes, kBBytes, &full[stage]);
           issued[stage] = true;
           issued_parity[stage] = phase;
@@ -206,8 +211,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++iter) {
         int32_t img, mt, nb;
         c3_coords(tile, p, img, mt, nb);
-        const int32_t r_lo = (BM * mt) / wp;
-        const int32_t a_row0 = wp + 1 + BM * mt - r_lo * wp;  // centre f0 in the tile's flat rows
+        const int32_t r_lo = (p.f0 + BM * mt + p.min_off) / wp;
+        const int32_t a_row0 = p.f0 + BM * mt - r_lo * wp;  // the tile's first centre in its loaded rows
         const int buf = iter & 1;
         const uint32_t aphase = (iter >> 1) & 1;
         if (!mbar_wait(&tempty[buf], aphase ^ 1, abort)) break;
@@ -219,8 +224,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sa = smem_addr(smem + (size_t)stage * p.stage_bytes);
           const uint32_t sb = sa + 4u * (uint32_t)p.plane_stride;
 #pragma unroll
-          for (int t = 0; t < 9; ++t) {
-            const int32_t row = a_row0 + (t / 3 - 1) * wp + (t % 3 - 1);
+          for (int t = 0; t < TAPS; ++t) {
+            const int32_t row = a_row0 + p.toff[t];
 #pragma unroll
             for (int kk = 0; kk < 2; ++kk)
               mma_i8(d_tmem, desc_rows16(sa + (uint32_t)(2 * kk * p.plane_stride + row * 16), (uint32_t)p.plane_stride),
@@ -249,11 +254,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                           int32_t& ix) {
       int32_t mt;
       c3_coords(tile, p, img, mt, nb);
-      const int32_t f = wp + 1 + BM * mt + q * 32 + lane;  // this lane's centre position
-      const int32_t py = f / wp, px = f - py * wp;
-      valid = py >= 1 && py <= p.h && px >= 1 && px <= p.w;
-      iy = py - 1;
-      ix = px - 1;
+      const int32_t f = p.f0 + BM * mt + q * 32 + lane;  // this lane's centre position
+      const int32_t py = f / wp;
+      iy = py - p.pad_t;
+      ix = f - py * wp - p.pad_l;
+      valid = iy >= 0 && iy < p.h && ix >= 0 && ix < p.w;
       pix = valid ? iy * p.w + ix : 0;
     };
     // The residual block's add: res[] holds the residual of the tile being processed; as
@@ -390,34 +395,67 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // Input map: chunk-planar i8 [n][cpad / 16][h][w][16 B] as 4 dims of 8-byte elements
-// (2w, h, chunks, n); boxes of one chunk plane x rbox rows x (w + 2) pixels, starting one
-// pixel (two elements, 16 bytes) left of the image.
-bool make_in_map(CUtensorMap* map, const void* base, int32_t n, int32_t h, int32_t w, int32_t cpad, int32_t rbox) {
+// (2w, h, chunks, n); boxes of one chunk plane x rbox rows x wp pixels, starting pad_l
+// pixels left of the image.
+bool make_in_map(CUtensorMap* map, const void* base, int32_t n, int32_t h, int32_t w, int32_t cpad, int32_t wp,
+                 int32_t rbox) {
   auto fn = tma_encode_fn();
   if (!fn) return false;
   cuuint64_t dims[4] = {(cuuint64_t)2 * w, (cuuint64_t)h, (cuuint64_t)(cpad / 16), (cuuint64_t)n};
   cuuint64_t strides[3] = {(cuuint64_t)16 * w, (cuuint64_t)16 * w * h, (cuuint64_t)16 * w * h * (cpad / 16)};
-  cuuint32_t box[4] = {(cuuint32_t)(2 * (w + 2)), (cuuint32_t)rbox, 1, 1};
+  cuuint32_t box[4] = {(cuuint32_t)(2 * wp), (cuuint32_t)rbox, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int ACT>
-bool launch_bn(const GemmArgs& a, const int8_t* wd, int num_sms, cudaStream_t st) {
-  const int32_t W = a.g.w, H = a.g.h, wp = W + 2;
+// The tap geometry of a mode over an h x w operand grid (= the output grid).
+struct TapGeom {
+  int taps = 0, pad_t = 0, pad_l = 0, wp = 0, f0 = 0, min_off = 0, max_off = 0, rbox = 0, tiles_m = 0;
+  int toff[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+};
+
+TapGeom tap_geom(int mode, int32_t h, int32_t w) {
+  TapGeom g;
+  if (mode == DCONV_3X3) {
+    g.taps = 9; g.pad_t = 1; g.pad_l = 1; g.wp = w + 2;
+    for (int t = 0; t < 9; ++t) g.toff[t] = (t / 3 - 1) * g.wp + (t % 3 - 1);
+  } else if (mode == DCONV_S2D) {  // taps (ay, ax) in {-1, 0}^2 over 2x2 pixel blocks
+    g.taps = 4; g.pad_t = 1; g.pad_l = 1; g.wp = w + 1;
+    for (int t = 0; t < 4; ++t) g.toff[t] = (t / 2 - 1) * g.wp + (t % 2 - 1);
+  } else {
+    g.taps = 1; g.wp = w;
+  }
+  g.f0 = g.pad_t * g.wp + g.pad_l;
+  g.min_off = g.max_off = g.toff[0];
+  for (int t = 1; t < g.taps; ++t) {
+    g.min_off = std::min(g.min_off, g.toff[t]);
+    g.max_off = std::max(g.max_off, g.toff[t]);
+  }
+  // 128 consecutive centres from any start span at most this many padded rows
+  g.rbox = (g.wp + 126 + (g.max_off - g.min_off)) / g.wp + 1;
+  g.tiles_m = (int)(((int64_t)(h - 1) * g.wp + w + BM - 1) / BM);
+  return g;
+}
+
+template <int BN, int ACT, int TAPS>
+bool launch_bn(const GemmArgs& a, int mode, int32_t H, int32_t W, int32_t cpad, const int8_t* wd, int num_sms,
+               cudaStream_t st) {
+  const TapGeom tg = tap_geom(mode, H, W);
   C3Params p;
   p.n_img = (int32_t)(a.m / ((int64_t)H * W));
-  p.h = H; p.w = W; p.cpad = a.g.cpad; p.n = (int32_t)a.n;
-  p.tiles_m = (H * wp - 2 + BM - 1) / BM;
+  p.h = H; p.w = W; p.cpad = cpad; p.n = (int32_t)a.n;
+  p.tiles_m = tg.tiles_m;
   p.tiles_n = (int32_t)((a.n + BN - 1) / BN);
-  p.stages_k = a.g.cpad / kCS;
-  p.rbox = (3 * W + 134) / wp + 1;
-  p.plane_bytes = p.rbox * wp * 16;
+  p.stages_k = cpad / kCS;
+  p.rbox = tg.rbox;
+  p.wp = tg.wp; p.pad_t = tg.pad_t; p.pad_l = tg.pad_l; p.f0 = tg.f0; p.min_off = tg.min_off;
+  for (int t = 0; t < 9; ++t) p.toff[t] = tg.toff[t];
+  p.plane_bytes = p.rbox * tg.wp * 16;
   p.plane_stride = (p.plane_bytes + 127) / 128 * 128;
   const int a_bytes = 4 * p.plane_stride;
-  p.stage_bytes = (a_bytes + 9 * 4 * BN * 16 + 1023) / 1024 * 1024;
+  p.stage_bytes = (a_bytes + TAPS * 4 * BN * 16 + 1023) / 1024 * 1024;
   p.ring = (227 * 1024 - 1024 - kBarBytes - 2 * p.tiles_n * BN * 4) / p.stage_bytes;
   if (p.ring > 8) p.ring = 8;
   if (p.ring < 2) return false;
@@ -425,10 +463,10 @@ bool launch_bn(const GemmArgs& a, const int8_t* wd, int num_sms, cudaStream_t st
   const int smem = 1024 + p.ring * p.stage_bytes + kBarBytes + 2 * p.n_pad * 4;
   static std::once_flag once;
   std::call_once(once, [] {
-    cudaFuncSetAttribute(k_conv3x3<BN, ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(k_conv3x3<BN, ACT, TAPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   });
   CUtensorMap mi;
-  if (!make_in_map(&mi, a.a, p.n_img, H, W, a.g.cpad, p.rbox)) return false;
+  if (!make_in_map(&mi, a.a, p.n_img, H, W, cpad, tg.wp, p.rbox)) return false;
   p.wd = wd;
   p.a_scale = a.a_scale; p.w_scale = a.w_scale; p.w_scale_ch = a.w_scale_ch; p.bias = a.bias;
   p.act_param = a.act_param; p.out = a.out; p.acc = a.acc;
@@ -437,69 +475,126 @@ bool launch_bn(const GemmArgs& a, const int8_t* wd, int num_sms, cudaStream_t st
   p.amax2 = a.amax2; p.cov_s = a.cov_s > 0 ? a.cov_s : 1; p.cov_oh = a.cov_oh; p.cov_ow = a.cov_ow;
   const int64_t tiles = (int64_t)p.n_img * p.tiles_m * p.tiles_n;
   const int grid = tiles < num_sms ? (int)tiles : num_sms;
-  k_conv3x3<BN, ACT><<<grid, kThreads, smem, st>>>(mi, p);
+  k_conv3x3<BN, ACT, TAPS><<<grid, kThreads, smem, st>>>(mi, p);
   return true;
 }
 
-template <int BN>
-bool launch_act(const GemmArgs& a, const int8_t* wd, int num_sms, cudaStream_t st) {
+template <int BN, int TAPS>
+bool launch_act(const GemmArgs& a, int mode, int32_t h, int32_t w, int32_t cpad, const int8_t* wd, int num_sms,
+                cudaStream_t st) {
   switch (a.act) {
-    case ACT_NONE: return launch_bn<BN, ACT_NONE>(a, wd, num_sms, st);
-    case ACT_RELU: return launch_bn<BN, ACT_RELU>(a, wd, num_sms, st);
-    case ACT_SIGMOID: return launch_bn<BN, ACT_SIGMOID>(a, wd, num_sms, st);
-    case ACT_TANH: return launch_bn<BN, ACT_TANH>(a, wd, num_sms, st);
-    case ACT_GELU: return launch_bn<BN, ACT_GELU>(a, wd, num_sms, st);
-    case ACT_LEAKY_RELU: return launch_bn<BN, ACT_LEAKY_RELU>(a, wd, num_sms, st);
+    case ACT_NONE: return launch_bn<BN, ACT_NONE, TAPS>(a, mode, h, w, cpad, wd, num_sms, st);
+    case ACT_RELU: return launch_bn<BN, ACT_RELU, TAPS>(a, mode, h, w, cpad, wd, num_sms, st);
+    case ACT_SIGMOID: return launch_bn<BN, ACT_SIGMOID, TAPS>(a, mode, h, w, cpad, wd, num_sms, st);
+    case ACT_TANH: return launch_bn<BN, ACT_TANH, TAPS>(a, mode, h, w, cpad, wd, num_sms, st);
+    case ACT_GELU: return launch_bn<BN, ACT_GELU, TAPS>(a, mode, h, w, cpad, wd, num_sms, st);
+    case ACT_LEAKY_RELU: return launch_bn<BN, ACT_LEAKY_RELU, TAPS>(a, mode, h, w, cpad, wd, num_sms, st);
     default: return false;
   }
 }
+
+int mode_taps(int mode) { return mode == DCONV_3X3 ? 9 : mode == DCONV_S2D ? 4 : 1; }
 
 }  // namespace
 
 int conv3x3_bn(int32_t out_channels) { return out_channels >= 128 ? 128 : 64; }
 
+bool dconv_shape_ok(int mode, int64_t n_img, int32_t h, int32_t w, int32_t cpad, int32_t out_channels) {
+  if (mode < DCONV_3X3 || mode > DCONV_1X1) return false;
+  if ((cpad & 63) || out_channels < 16 || n_img < 1 || n_img > 65535 || h < 1 || w < 1) return false;
+  const TapGeom tg = tap_geom(mode, h, w);
+  if (2 * tg.wp > 256 || tg.rbox > 256) return false;  // TMA box extents
+  if (n_img * h * w * (int64_t)out_channels * tg.taps * cpad < (int64_t)1 << 22) return false;
+  return tma_encode_fn() != nullptr;
+}
+
 bool conv3x3_shape_ok(int64_t n_img, int32_t h, int32_t w, int32_t cpad, int32_t k, int32_t stride, int32_t pad,
                       int32_t out_channels) {
-  if (k != 3 || stride != 1 || pad != 1 || (cpad & 63) || out_channels < 16 || n_img > 65535) return false;
-  if (2 * (w + 2) > 256 || (3 * w + 134) / (w + 2) + 1 > 256) return false;  // box extents
-  if (n_img * h * w * (int64_t)out_channels * 9 * cpad < (int64_t)1 << 22) return false;
+  return k == 3 && stride == 1 && pad == 1 && dconv_shape_ok(DCONV_3X3, n_img, h, w, cpad, out_channels);
+}
+
+bool dconv_eligible(const GemmArgs& a, int mode, int32_t h, int32_t w, int32_t cpad) {
+  if (!a.conv || a.out_l <= 0 || a.out_l != (int64_t)h * w || a.rows_per_scale != a.out_l) return false;
+  if (!dconv_shape_ok(mode, a.m / a.out_l, h, w, cpad, (int32_t)a.n)) return false;
+  if (a.amax.ptr && a.amax.elems_per_slot != 0 && a.amax.elems_per_slot != a.n * a.out_l) return false;
+  if (a.n * a.out_l >= ((int64_t)1 << 31)) return false;  // per-image offsets in 32 bits
+  if (reinterpret_cast<uintptr_t>(a.a) & 15) return false;
   return tma_encode_fn() != nullptr;
 }
 
 bool conv3x3_eligible(const GemmArgs& a) {
-  if (!a.conv || a.out_l <= 0 || a.rows_per_scale != a.out_l) return false;
-  if (a.g.c != a.g.cpad || a.g.oh != a.g.h || a.g.ow != a.g.w) return false;
-  if (!conv3x3_shape_ok(a.m / a.out_l, a.g.h, a.g.w, a.g.cpad, a.g.k, a.g.stride, a.g.pad, (int32_t)a.n)) return false;
-  if (a.amax.ptr && a.amax.elems_per_slot != 0 && a.amax.elems_per_slot != a.n * a.out_l) return false;
-  if (a.n * a.out_l >= ((int64_t)1 << 31)) return false;  // per-image offsets in 32 bits
-  if (reinterpret_cast<uintptr_t>(a.a) & 15) return false;
-  if (a.m * a.n * a.k < (int64_t)1 << 22) return false;
-  return tma_encode_fn() != nullptr;
+  if (a.g.c != a.g.cpad || a.g.oh != a.g.h || a.g.ow != a.g.w || a.g.k != 3 || a.g.stride != 1 || a.g.pad != 1)
+    return false;
+  return dconv_eligible(a, DCONV_3X3, a.g.h, a.g.w, a.g.cpad);
 }
 
-// Host-side weight arrangement: w [N][C * 9] (reference order c, ky, kx) quantized ->
-// [tiles_n][C / 64][9 taps][4 chunks][BN rows][16 B], zero-padded rows past N.
-void conv3x3_arrange_weights(const int8_t* wq, int32_t n, int32_t c, int32_t cpad, int8_t* out) {
-  const int32_t bn = conv3x3_bn(n), tiles_n = (n + bn - 1) / bn, sk = cpad / kCS;
-  const size_t per = (size_t)9 * 4 * bn * 16;
+// Host-side weight arrangement: w [N][C][k][k] quantized (reference layout) ->
+// [tiles_n][cpad_op / 64][taps][4 chunks][BN rows][16 B], zero where no weight applies.
+// Operand channel sc of tap t:
+//   3x3: channel sc, kernel (t / 3, t % 3);            1x1: channel sc;
+//   s2d: sc = (dy * 2 + dx) * cpad + c, tap (ay, ax) = (t / 2 - 1, t % 2 - 1), kernel
+//        (2 ay + dy + 1, 2 ax + dx + 1) when inside 0..2 (pixel 2 oy - 1 + ky of the
+//        stride-2 / pad-1 conv is s2d row oy + ay, sub-row dy).
+void dconv_arrange_weights(int mode, const int8_t* wq, int32_t n, int32_t c, int32_t k, int32_t cpad, int8_t* out) {
+  const int32_t bn = conv3x3_bn(n), tiles_n = (n + bn - 1) / bn;
+  const int taps = mode_taps(mode);
+  const int32_t cop = mode == DCONV_S2D ? 4 * cpad : cpad, sk = cop / kCS;
+  const size_t per = (size_t)taps * 4 * bn * 16;
   memset(out, 0, per * sk * tiles_n);
   for (int32_t o = 0; o < n; ++o) {
     const int32_t nb = o / bn, r = o % bn;
-    for (int32_t ch = 0; ch < c; ++ch) {
-      const int32_t s = ch / kCS, j = (ch % kCS) / 16, b = ch % 16;
-      for (int32_t t = 0; t < 9; ++t)
-        out[((size_t)nb * sk + s) * per + (((size_t)t * 4 + j) * bn + r) * 16 + b] = wq[((size_t)o * c + ch) * 9 + t];
+    for (int32_t sc = 0; sc < cop; ++sc) {
+      const int32_t s = sc / kCS, j = (sc % kCS) / 16, b = sc % 16;
+      for (int t = 0; t < taps; ++t) {
+        int32_t ch = sc, ky = 0, kx = 0;
+        if (mode == DCONV_3X3) {
+          ky = t / 3; kx = t % 3;
+        } else if (mode == DCONV_S2D) {
+          const int32_t dd = sc / cpad, dy = dd / 2, dx = dd % 2;
+          ch = sc % cpad;
+          ky = 2 * (t / 2 - 1) + dy + 1;
+          kx = 2 * (t % 2 - 1) + dx + 1;
+          if (ky < 0 || ky > 2 || kx < 0 || kx > 2) continue;
+        }
+        if (ch >= c) continue;
+        out[((size_t)nb * sk + s) * per + (((size_t)t * 4 + j) * bn + r) * 16 + b] =
+            wq[(((size_t)o * c + ch) * k + ky) * k + kx];
+      }
     }
   }
 }
 
-size_t conv3x3_weight_bytes(int32_t n, int32_t cpad) {
+size_t dconv_weight_bytes(int mode, int32_t n, int32_t cpad) {
   const int32_t bn = conv3x3_bn(n);
-  return (size_t)((n + bn - 1) / bn) * (cpad / kCS) * 9 * 4 * bn * 16;
+  const int32_t cop = mode == DCONV_S2D ? 4 * cpad : cpad;
+  return (size_t)((n + bn - 1) / bn) * (cop / kCS) * mode_taps(mode) * 4 * bn * 16;
+}
+
+void conv3x3_arrange_weights(const int8_t* wq, int32_t n, int32_t c, int32_t cpad, int8_t* out) {
+  dconv_arrange_weights(DCONV_3X3, wq, n, c, 3, cpad, out);
+}
+
+size_t conv3x3_weight_bytes(int32_t n, int32_t cpad) { return dconv_weight_bytes(DCONV_3X3, n, cpad); }
+
+bool launch_dconv(const GemmArgs& a, int mode, int32_t h, int32_t w, int32_t cpad, const int8_t* wd, int num_sms,
+                  cudaStream_t st) {
+  const bool b128 = conv3x3_bn((int32_t)a.n) == 128;
+  switch (mode) {
+    case DCONV_3X3:
+      return b128 ? launch_act<128, 9>(a, mode, h, w, cpad, wd, num_sms, st)
+                  : launch_act<64, 9>(a, mode, h, w, cpad, wd, num_sms, st);
+    case DCONV_S2D:
+      return b128 ? launch_act<128, 4>(a, mode, h, w, cpad, wd, num_sms, st)
+                  : launch_act<64, 4>(a, mode, h, w, cpad, wd, num_sms, st);
+    case DCONV_1X1:
+      return b128 ? launch_act<128, 1>(a, mode, h, w, cpad, wd, num_sms, st)
+                  : launch_act<64, 1>(a, mode, h, w, cpad, wd, num_sms, st);
+    default: return false;
+  }
 }
 
 bool launch_conv3x3(const GemmArgs& a, const int8_t* wd, int num_sms, cudaStream_t st) {
-  return conv3x3_bn((int32_t)a.n) == 128 ? launch_act<128>(a, wd, num_sms, st) : launch_act<64>(a, wd, num_sms, st);
+  return launch_dconv(a, DCONV_3X3, a.g.h, a.g.w, a.g.cpad, wd, num_sms, st);
 }
 
 int conv3x3_take_error() {

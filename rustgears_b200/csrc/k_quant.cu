@@ -271,6 +271,7 @@ __global__ void __launch_bounds__(256) k_image_quantize_g16(const float* __restr
 // The strided 1x1 conv's operand: output pixel (oy, ox) of the compact [n][oh][ow][cpad]
 // NHWC tensor is input pixel (s oy, s ox); the scale's absmax covers exactly these
 // pixels (no clamp).
+template <bool PLANAR>
 __global__ void __launch_bounds__(256) k_image_quantize_sub16(const float* __restrict__ x, int32_t c, int32_t h,
                                                               int32_t w, int32_t s, int32_t oh, int32_t ow,
                                                               int32_t cpad, const unsigned* __restrict__ amax,
@@ -295,7 +296,44 @@ __global__ void __launch_bounds__(256) k_image_quantize_sub16(const float* __res
     for (int k = 0; k < 16; ++k) t[k] = quant1_bounded(v[k], inv);
     const uint4 word = make_uint4(pack4_i8(t[0], t[1], t[2], t[3]), pack4_i8(t[4], t[5], t[6], t[7]),
                                   pack4_i8(t[8], t[9], t[10], t[11]), pack4_i8(t[12], t[13], t[14], t[15]));
-    *reinterpret_cast<uint4*>(q + (img * ohw + op) * (int64_t)cpad + 16 * g) = word;
+    const int64_t off = PLANAR ? ((img * (cpad / 16) + g) * (int64_t)ohw + op) * 16 : (img * ohw + op) * (int64_t)cpad + 16 * g;
+    *reinterpret_cast<uint4*>(q + off) = word;
+  }
+}
+
+// The space-to-depth operand of a 3x3 / stride 2 / pad 1 conv: chunk g of s2d pixel
+// (sy, sx) holds channels c0 .. c0 + 15 (16 g = dd * cpad + c0, dd = dy * 2 + dx) of
+// input pixel (2 sy + dy, 2 sx + dx), zero past an odd h or w (that row / column is the
+// conv's own bottom / right padding); every input pixel is read by the conv, so the
+// absmax covers them all (no clamp).
+__global__ void __launch_bounds__(256) k_image_quantize_s2d16(const float* __restrict__ x, int32_t c, int32_t h,
+                                                              int32_t w, int32_t cpad,
+                                                              const unsigned* __restrict__ amax,
+                                                              int8_t* __restrict__ q, float* __restrict__ scales) {
+  const int64_t img = blockIdx.z;
+  const int32_t g = blockIdx.y;
+  const float scale = quant_scale(__uint_as_float(amax[img]));
+  const float inv = quant_inv(scale);
+  if (scales && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) scales[img] = scale;
+  const int32_t dd = (16 * g) / cpad, c0 = (16 * g) % cpad, dy = dd >> 1, dx = dd & 1;
+  const int32_t nch = c - c0;
+  const int64_t hw = (int64_t)h * w;
+  const float* src = x + (img * c + c0) * hw;
+  const int32_t w2 = (w + 1) / 2, hw2 = ((h + 1) / 2) * w2;
+  for (int32_t sp = blockIdx.x * 256 + threadIdx.x; sp < hw2; sp += gridDim.x * 256) {
+    const int32_t sy = sp / w2, sx = sp - sy * w2;
+    const int32_t iy = 2 * sy + dy, ix = 2 * sx + dx;
+    const int32_t nv = iy < h && ix < w ? nch : 0;  // channels present at this pixel
+    const int64_t px = (int64_t)iy * w + ix;
+    float v[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) v[k] = k < nv ? __ldg(src + (int64_t)k * hw + px) : 0.0f;
+    int32_t t[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) t[k] = quant1_bounded(v[k], inv);
+    const uint4 word = make_uint4(pack4_i8(t[0], t[1], t[2], t[3]), pack4_i8(t[4], t[5], t[6], t[7]),
+                                  pack4_i8(t[8], t[9], t[10], t[11]), pack4_i8(t[12], t[13], t[14], t[15]));
+    *reinterpret_cast<uint4*>(q + ((img * (4 * cpad / 16) + g) * (int64_t)hw2 + sp) * 16) = word;
   }
 }
 
@@ -431,12 +469,23 @@ void launch_image_quantize_planar16(const float* x, int64_t n, int32_t c, int32_
 }
 
 void launch_image_quantize_subsampled(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t s,
-                                      int32_t oh, int32_t ow, int32_t cpad, const unsigned* amax_bits, int8_t* q,
-                                      float* scales_out, cudaStream_t st) {
+                                      int32_t oh, int32_t ow, int32_t cpad, bool planar, const unsigned* amax_bits,
+                                      int8_t* q, float* scales_out, cudaStream_t st) {
   const int32_t ohw = oh * ow;
   if (n <= 0 || ohw <= 0) return;
   const dim3 grid((unsigned)std::min<int64_t>((ohw + 255) / 256, 1024), (unsigned)(cpad / 16), (unsigned)n);
-  k_image_quantize_sub16<<<grid, 256, 0, st>>>(x, c, h, w, s, oh, ow, cpad, amax_bits, q, scales_out);
+  if (planar)
+    k_image_quantize_sub16<true><<<grid, 256, 0, st>>>(x, c, h, w, s, oh, ow, cpad, amax_bits, q, scales_out);
+  else
+    k_image_quantize_sub16<false><<<grid, 256, 0, st>>>(x, c, h, w, s, oh, ow, cpad, amax_bits, q, scales_out);
+}
+
+void launch_image_quantize_s2d_planar(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t cpad,
+                                      const unsigned* amax_bits, int8_t* q, float* scales_out, cudaStream_t st) {
+  const int32_t hw2 = ((h + 1) / 2) * ((w + 1) / 2);
+  if (n <= 0 || hw2 <= 0) return;
+  const dim3 grid((unsigned)std::min<int64_t>((hw2 + 255) / 256, 1024), (unsigned)(4 * cpad / 16), (unsigned)n);
+  k_image_quantize_s2d16<<<grid, 256, 0, st>>>(x, c, h, w, cpad, amax_bits, q, scales_out);
 }
 
 void launch_image_quantize_s2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, const unsigned* amax_bits,

@@ -145,7 +145,8 @@ struct Op {
   int32_t cpad = 0;               // conv: channels per tap in the device layouts (16-aligned, 4, or 1)
   int32_t kxp = 0;                // conv: taps per kernel row in the K order (k; with cpad 4: a multiple of 4)
   DevBuf d_w, d_bias, d_wsc;     // device weights [N, kpad] (conv: (ky,kx,c) order)
-  DevBuf d_w3;                   // 3x3 / stride 1 convs: the direct kernel's weight arrangement
+  DevBuf d_w3;                   // direct-conv weight arrangement for mode dmode
+  int32_t dmode = -1;            // DCONV_3X3 / DCONV_S2D / DCONV_1X1, or -1 (implicit GEMM only)
   DevBuf d_ws;                   // 7x7 / stride 2 stems (<= 4 channels -> 64): the fused stem's arrangement
   bool bias_finite = true;
   std::string label;
@@ -406,9 +407,20 @@ static rg_status upload_op(Op& op) {
   }
   RG_TRY(op.d_w.ensure(dev.size()));
   RG_CUDA_TRY(cudaMemcpy(op.d_w.p, dev.data(), dev.size(), cudaMemcpyHostToDevice));
-  if (op.kind == RG_LAYER_CONV2D && op.k == 3 && op.stride == 1 && op.pad == 1 && op.cpad % 64 == 0) {
-    std::vector<int8_t> w3(conv3x3_weight_bytes(op.out_c, op.cpad));
-    conv3x3_arrange_weights(op.wq.data(), op.out_c, op.in_c, op.cpad, w3.data());
+  // the direct (tap-shifted) conv kernel: 3x3 / stride 1 / pad 1, 3x3 / stride 2 / pad 1
+  // (space-to-depth), 1x1 / pad 0 (any stride, over the compact operand)
+  op.dmode = -1;
+  if (op.kind == RG_LAYER_CONV2D || op.kind == RG_LAYER_SHORTCUT_CONV2D) {
+    if (op.kind == RG_LAYER_CONV2D && op.k == 3 && op.stride == 1 && op.pad == 1 && op.cpad % 64 == 0)
+      op.dmode = DCONV_3X3;
+    else if (op.k == 3 && op.stride == 2 && op.pad == 1 && op.cpad % 16 == 0)
+      op.dmode = DCONV_S2D;
+    else if (op.k == 1 && op.pad == 0 && op.cpad % 64 == 0)
+      op.dmode = DCONV_1X1;
+  }
+  if (op.dmode >= 0) {
+    std::vector<int8_t> w3(dconv_weight_bytes(op.dmode, op.out_c, op.cpad));
+    dconv_arrange_weights(op.dmode, op.wq.data(), op.out_c, op.in_c, op.k, op.cpad, w3.data());
     RG_TRY(op.d_w3.ensure(w3.size()));
     RG_CUDA_TRY(cudaMemcpy(op.d_w3.p, w3.data(), w3.size(), cudaMemcpyHostToDevice));
   }
@@ -917,6 +929,8 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
       const std::vector<int64_t>& in = P.shapes[i].in;  // NHWC with channels padded to cpad
       // (the fused stem's space-to-depth operand: 16 bytes per 2 x 2 pixels)
       max_q = std::max(max_q, in[0] * in[2] * in[3] * std::max<int64_t>(op.cpad, P.stem_start[i] ? 4 : 0));
+      // the space-to-depth operand covers the image rounded up to even sizes
+      if (op.dmode == DCONV_S2D) max_q = std::max(max_q, in[0] * ((in[2] + 1) / 2 * 2) * ((in[3] + 1) / 2 * 2) * op.cpad);
     }
     if (op.kind == RG_LAYER_ATTENTION || op.kind == RG_LAYER_SWIGLU) {
       const int64_t rows = P.shapes[i].in_elems / op.in_f;
@@ -1136,6 +1150,8 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         const bool shortcut = op.kind == RG_LAYER_SHORTCUT_CONV2D;
         fused_residual = false;
         bool use3 = false;
+        int dmode = -1;                  // direct-conv mode and its operand grid / channels
+        int32_t d_h = 0, d_w = 0, d_cp = 0;
         const float* src = shortcut ? saved.back() : cur;
         unsigned* my_amax = amax + P.amax_off[i];
         float* my_scale = scales + P.amax_off[i];
@@ -1173,20 +1189,40 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
             ++launches;
             RG_LAUNCHED("image_absmax");
           }
-          // the direct 3x3 kernel reads 16-channel chunk planes; every other conv, NHWC
-          use3 = op.kind == RG_LAYER_CONV2D && op.d_w3.p && !s.trace &&
-                 conv3x3_shape_ok(N, H, W, op.cpad, op.k, op.stride, op.pad, op.out_c);
+          const int32_t OH = (int32_t)os.out[2], OW = (int32_t)os.out[3];
+          // The direct kernel reads 16-channel chunk planes of an operand whose grid is the
+          // output grid: the image (3x3 / stride 1), its 2x2 pixel blocks (3x3 / stride 2,
+          // even sizes), or the pixels a 1x1 conv reads.  Every other conv: NHWC, implicit GEMM.
+          if (op.dmode >= 0 && op.d_w3.p && !s.trace && N <= 65535) {
+            int32_t dh = OH, dw = OW, dcp = op.cpad;
+            bool ok = true;
+            if (op.dmode == DCONV_3X3) {
+              ok = OH == H && OW == W;
+            } else if (op.dmode == DCONV_S2D) {
+              ok = OH == (H + 1) / 2 && OW == (W + 1) / 2 && rc[i] == nullptr;
+              dcp = 4 * op.cpad;
+            }
+            if (ok && dconv_shape_ok(op.dmode, N, dh, dw, dcp, op.out_c)) {
+              dmode = op.dmode;
+              d_h = dh; d_w = dw; d_cp = dcp;
+            }
+          }
+          use3 = dmode >= 0;
           // a strided 1x1 / pad 0 conv reads every s-th row and column: only those pixels
           // are quantized, into a compact operand, and the conv runs as a 1x1 / stride 1
           // conv over it
           const bool sub = op.k == 1 && op.pad == 0 && op.stride > 1 && !s.trace && (op.cpad & 15) == 0 &&
                            N <= 65535;
           const bool bounded = rc[i] == nullptr;  // the absmax covers every pixel quantized
-          if (use3) launch_image_quantize_planar16(src, N, C, H, W, op.cpad, bounded, my_amax, q, my_scale, st);
+          if (dmode == DCONV_S2D)
+            launch_image_quantize_s2d_planar(src, N, C, H, W, op.cpad, my_amax, q, my_scale, st);
           else if (sub)
-            launch_image_quantize_subsampled(src, N, C, H, W, op.stride, (int32_t)os.out[2], (int32_t)os.out[3],
-                                             op.cpad, my_amax, q, my_scale, st);
-          else launch_image_quantize_nhwc(src, N, C, H, W, op.cpad, bounded, my_amax, q, my_scale, st);
+            launch_image_quantize_subsampled(src, N, C, H, W, op.stride, OH, OW, op.cpad, use3, my_amax, q, my_scale,
+                                             st);
+          else if (use3)
+            launch_image_quantize_planar16(src, N, C, H, W, op.cpad, bounded, my_amax, q, my_scale, st);
+          else
+            launch_image_quantize_nhwc(src, N, C, H, W, op.cpad, bounded, my_amax, q, my_scale, st);
           ++launches;
           RG_LAUNCHED("image_quantize");
           g.a = q; g.conv = true;
@@ -1216,7 +1252,8 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         // residual (the f32 add commutes): its output becomes the main path.
         if ((op.kind == RG_LAYER_CONV2D || shortcut) && !s.trace && i + 1 < n &&
             s.ops[i + 1].kind == RG_LAYER_RESIDUAL_END && !saved.empty() &&
-            P.shapes[i + 1].in_elems == os.out_elems && (use3 ? conv3x3_eligible(g) : conv_tc_eligible(g)) &&
+            P.shapes[i + 1].in_elems == os.out_elems &&
+            (use3 ? dconv_eligible(g, dmode, d_h, d_w, d_cp) : conv_tc_eligible(g)) &&
             (s.ops[i + 1].act == RG_ACT_NONE || s.ops[i + 1].act == RG_ACT_RELU ||
              s.ops[i + 1].act == RG_ACT_LEAKY_RELU)) {
           const Op& re = s.ops[i + 1];
@@ -1251,8 +1288,9 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
           g.cov_ow = (int32_t)P.shapes[(size_t)sc].out[3];
           amax2_done[(size_t)sc] = 1;
         }
-        if (use3 && (!conv3x3_eligible(g) || !launch_conv3x3(g, op.d_w3.as<int8_t>(), s.num_sms, st)))
-          return fail(RG_ERR_CUDA, "op %zu: the direct 3x3 conv could not be launched", i);
+        if (use3 && (!dconv_eligible(g, dmode, d_h, d_w, d_cp) ||
+                     !launch_dconv(g, dmode, d_h, d_w, d_cp, op.d_w3.as<int8_t>(), s.num_sms, st)))
+          return fail(RG_ERR_CUDA, "op %zu: the direct conv could not be launched", i);
         const bool conv3 = use3;
         const bool conv_tc = !conv3 && g.conv && conv_tc_eligible(g);
         const bool tc = !fused_q && !g.conv && gemm_tc_eligible(g);

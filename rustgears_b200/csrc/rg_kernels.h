@@ -46,8 +46,14 @@ void launch_image_quantize_s2d(const float* x, int64_t n, int32_t c, int32_t h, 
 // [n][oh][ow][cpad] (cpad a multiple of 16, n <= 65535): the conv becomes a 1x1
 // stride-1 conv over it.
 void launch_image_quantize_subsampled(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t s,
-                                      int32_t oh, int32_t ow, int32_t cpad, const unsigned* amax_bits, int8_t* q,
-                                      float* scales_out, cudaStream_t st);
+                                      int32_t oh, int32_t ow, int32_t cpad, bool planar, const unsigned* amax_bits,
+                                      int8_t* q, float* scales_out, cudaStream_t st);
+// NCHW f32 -> the space-to-depth operand of a 3x3 / stride 2 / pad 1 conv as 16-channel
+// chunk planes [n][4 cpad / 16][ceil(h / 2)][ceil(w / 2)][16 B]: channel (dy * 2 + dx) *
+// cpad + c of s2d pixel (sy, sx) = channel c of pixel (2 sy + dy, 2 sx + dx), zero for
+// c >= c_in and past an odd h or w.
+void launch_image_quantize_s2d_planar(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t cpad,
+                                      const unsigned* amax_bits, int8_t* q, float* scales_out, cudaStream_t st);
 // NHWC i8 (cpad) -> NCHW i8 (c) for traces.
 void launch_nhwc_to_nchw_i8(const int8_t* q, int64_t n, int32_t c, int32_t cpad, int32_t h,
                             int32_t w, int8_t* out, cudaStream_t st);
@@ -117,6 +123,21 @@ int conv_tc_take_error();
 // conv3x3_arrange_weights into conv3x3_weight_bytes(n, cpad) bytes.  launch() returns
 // false when the tensor map could not be encoded (nothing was launched).
 bool conv3x3_eligible(const GemmArgs& a);
+// The same kernel over other tap sets (the operand: 16-channel chunk planes of an h x w
+// grid equal to the output grid, cpad a multiple of 64):
+//   DCONV_3X3  3x3 / stride 1 / pad 1;
+//   DCONV_S2D  3x3 / stride 2 / pad 1 over the space-to-depth operand
+//              (launch_image_quantize_s2d_planar, 4 x the conv's channels): 2x2 taps;
+//   DCONV_1X1  1x1 over the operand (a strided 1x1 conv's compact operand,
+//              launch_image_quantize_subsampled with planar output).
+enum { DCONV_3X3 = 0, DCONV_S2D = 1, DCONV_1X1 = 2 };
+bool dconv_shape_ok(int mode, int64_t n_img, int32_t h, int32_t w, int32_t cpad, int32_t out_channels);
+bool dconv_eligible(const GemmArgs& a, int mode, int32_t h, int32_t w, int32_t cpad);
+// weights [n][c][k][k] quantized; cpad = the conv's padded channel count (the s2d operand has 4 x cpad)
+size_t dconv_weight_bytes(int mode, int32_t n, int32_t cpad);
+void dconv_arrange_weights(int mode, const int8_t* wq, int32_t n, int32_t c, int32_t k, int32_t cpad, int8_t* out);
+bool launch_dconv(const GemmArgs& a, int mode, int32_t h, int32_t w, int32_t cpad, const int8_t* wd, int num_sms,
+                  cudaStream_t st);
 // The shape test of conv3x3_eligible, before the operand is quantized (which layout).
 bool conv3x3_shape_ok(int64_t n_img, int32_t h, int32_t w, int32_t cpad, int32_t k, int32_t stride, int32_t pad,
                       int32_t out_channels);

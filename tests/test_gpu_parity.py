@@ -373,3 +373,28 @@ def test_resnet_two_stage_paths(gpu, oracle_lib, batch, image):
     x[batch - 1, 1, 5, 7] = np.inf
     ref, _, _ = oracle.Program(layers).execute(x, nthreads=16)
     assert_same(session_for(layers).run(x), ref, f"resnet {image} with inf")
+
+
+@pytest.mark.parametrize("b,c,n,h,w,k,st,pad,act", [
+    (2, 64, 128, 55, 55, 3, 2, 1, 1),   # odd size: the space-to-depth operand's last row / column is padding
+    (3, 64, 64, 28, 28, 3, 2, 1, 0),
+    (2, 128, 256, 14, 14, 3, 2, 1, 1),
+    (1, 192, 80, 9, 13, 3, 2, 1, 5),
+    (2, 64, 128, 55, 55, 1, 2, 0, 0),   # strided 1x1: compact operand
+    (2, 128, 64, 20, 20, 1, 1, 0, 1),
+    (1, 256, 512, 7, 7, 1, 1, 0, 0),
+])
+def test_direct_conv_modes(gpu, oracle_lib, b, c, n, h, w, k, st, pad, act):
+    """The direct conv kernel's other tap sets: 3x3 / stride 2 / pad 1 as 2x2 taps over
+    the space-to-depth operand, 1x1 over the image or over the pixels a strided 1x1
+    conv reads; against the oracle."""
+    rng = np.random.default_rng(b * 1000 + c + n + h * w + k * st)
+    wgt = (rng.standard_normal((n, c, k, k)) * 0.05).astype(np.float32)
+    bias = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    x = rng.standard_normal((b, c, h, w)).astype(np.float32)
+    layers = [dict(kind=oracle.CONV2D, in_channels=c, out_channels=n, kernel=k, stride=st, padding=pad, weight=wgt,
+                   bias=bias)]
+    if act:
+        layers.append(dict(kind=oracle.ACTIVATION, act=act, act_param=0.1))
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
+    assert_same(session_for(layers).run(x), ref, f"conv k{k} s{st} {c}->{n} {h}x{w}")
