@@ -67,6 +67,8 @@ struct C3Params {
   int32_t plane_bytes;             // rbox * (w + 2) * 16: what one TMA load writes
   int32_t plane_stride;            // plane_bytes rounded up to 128 (TMA destination alignment)
   int32_t stage_bytes, ring;       // bytes per ring slot (A planes + weights), slots
+  int32_t resident;                // one K stage and one N tile: the weights are loaded once
+                                   // into their own region, the ring slots hold A only
   const int8_t* wd;                // weights [tiles_n][stages_k][9][4][BN][16]
   const float* a_scale;            // per image
   float w_scale;
@@ -106,13 +108,34 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
 }
 
 // tile -> (image, centre tile within the image, N tile); N tiles vary fastest so the
-// CTAs working on one image's input tile run close together (L2 reuse).
-__device__ __forceinline__ void c3_coords(int64_t tile, const C3Params& p, int32_t& img, int32_t& mt, int32_t& nb) {
-  nb = (int32_t)(tile % p.tiles_n);
-  const int64_t rest = tile / p.tiles_n;
-  mt = (int32_t)(rest % p.tiles_m);
-  img = (int32_t)(rest / p.tiles_m);
-}
+// CTAs working on one image's input tile run close together (L2 reuse).  A CTA's tiles
+// are blockIdx.x + k gridDim.x: the walk adds gridDim.x's decomposition with carries
+// instead of dividing every tile index (the tile count is below 2^31).
+struct TileWalk {
+  int32_t img, mt, nb;        // current tile
+  int32_t d_img, d_mt, d_nb;  // gridDim.x decomposed
+  int32_t tiles_m, tiles_n;
+  __device__ void start(const C3Params& p, uint32_t first) {
+    tiles_m = p.tiles_m;
+    tiles_n = p.tiles_n;
+    const uint32_t g = gridDim.x;
+    d_nb = (int32_t)(g % (uint32_t)tiles_n);
+    d_mt = (int32_t)((g / (uint32_t)tiles_n) % (uint32_t)tiles_m);
+    d_img = (int32_t)((g / (uint32_t)tiles_n) / (uint32_t)tiles_m);
+    nb = (int32_t)(first % (uint32_t)tiles_n);
+    mt = (int32_t)((first / (uint32_t)tiles_n) % (uint32_t)tiles_m);
+    img = (int32_t)((first / (uint32_t)tiles_n) / (uint32_t)tiles_m);
+  }
+  __device__ void advance() {
+    nb += d_nb;
+    int32_t c = 0;
+    if (nb >= tiles_n) { nb -= tiles_n; c = 1; }
+    mt += d_mt + c;
+    c = 0;
+    if (mt >= tiles_m) { mt -= tiles_m; c = 1; }
+    img += d_img + c;
+  }
+};
 
 __device__ __forceinline__ void flush_slot_max(unsigned* base, int64_t slot, float v) {
 #pragma unroll
@@ -131,11 +154,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tfull = empty + p.ring;   // [2]
   uint64_t* tempty = tfull + 2;       // [2]
   uint64_t* done = tempty + 2;        // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* wbar = done + 1;          // [1] resident weights landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wbar + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // per-channel bias and weight scales, [n_pad] each (n_pad = n rounded up to BN)
   float* bias_s = reinterpret_cast<float*>(smem + (size_t)p.ring * p.stage_bytes + kBarBytes);
   float* wsc_s = bias_s + p.n_pad;
+  uint8_t* wres = reinterpret_cast<uint8_t*>(wsc_s + p.n_pad);  // resident weights
   constexpr int kBBytes = TAPS * 4 * BN * 16;
   constexpr int kTmemCols = 2 * BN;
 
@@ -153,6 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[b], kEpiWarps);
     }
     mbar_init(done, 1);
+    mbar_init(wbar, 1);
     *abort = 0;
     fence_mbar_init();
     tma_prefetch_desc(&map_in);
@@ -175,21 +201,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       const uint32_t a_bytes = 4u * (uint32_t)p.plane_bytes;
       const uint32_t a_span = 4u * (uint32_t)p.plane_stride;
+      if (p.resident) {
+        mbar_arrive_expect_tx(wbar, kBBytes);
+        bulk_load(wres, p.wd, kBBytes, wbar);
+      }
       uint32_t issued_parity[8];
       bool issued[8];
       for (int s = 0; s < 8; ++s) issued[s] = false;
-      for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        int32_t img, mt, nb;
-        c3_coords(tile, p, img, mt, nb);
+      TileWalk tw;
+      tw.start(p, blockIdx.x);
+      for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, tw.advance()) {
+        const int32_t img = tw.img, mt = tw.mt, nb = tw.nb;
         const int32_t r_lo = (p.f0 + BM * mt + p.min_off) / wp;  // first padded row the tile reads
         for (int s = 0; s < p.stages_k; ++s) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort)) { ok = false; break; }
           uint8_t* sa = smem + (size_t)stage * p.stage_bytes;
-          mbar_arrive_expect_tx(&full[stage], a_bytes + kBBytes);
+          mbar_arrive_expect_tx(&full[stage], a_bytes + (p.resident ? 0u : (uint32_t)kBBytes));
 #pragma unroll
           for (int j = 0; j < 4; ++j)  // chunk plane j: channels s*64 + 16j .. +15; x from pixel -pad_l
             tma_load_4d(sa + j * p.plane_stride, &map_in, &full[stage], -2 * p.pad_l, r_lo - p.pad_t, s * 4 + j, img);
-          bulk_load(sa + a_span, p.wd + ((int64_t)nb * p.stages_k + s) * kBBytes, kBBytes, &full[stage]);
+          if (!p.resident)
+            bulk_load(sa + a_span, p.wd + ((int64_t)nb * p.stages_k + s) * kBBytes, kBBytes, &full[stage]);
           issued[stage] = true;
           issued_parity[stage] = phase;
           if (++stage == p.ring) { stage = 0; phase ^= 1; }
@@ -197,6 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // drain: every copy issued must have landed before the CTA exits
       volatile int never = 0;
+      if (p.resident) mbar_wait(wbar, 0, &never, 200000000ull);
       for (int s = 0; s < p.ring; ++s)
         if (issued[s]) mbar_wait(&full[s], issued_parity[s], &never, 200000000ull);
     }
@@ -208,9 +241,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int iter = 0;
       bool ok = true;
-      for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++iter) {
-        int32_t img, mt, nb;
-        c3_coords(tile, p, img, mt, nb);
+      if (p.resident) {
+        ok = mbar_wait(wbar, 0, abort);
+        tc_fence_after();
+      }
+      TileWalk tw;
+      tw.start(p, blockIdx.x);
+      for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++iter, tw.advance()) {
+        const int32_t mt = tw.mt;
         const int32_t r_lo = (p.f0 + BM * mt + p.min_off) / wp;
         const int32_t a_row0 = p.f0 + BM * mt - r_lo * wp;  // the tile's first centre in its loaded rows
         const int buf = iter & 1;
@@ -222,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(&full[stage], phase, abort)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_addr(smem + (size_t)stage * p.stage_bytes);
-          const uint32_t sb = sa + 4u * (uint32_t)p.plane_stride;
+          const uint32_t sb = p.resident ? smem_addr(wres) : sa + 4u * (uint32_t)p.plane_stride;
 #pragma unroll
           for (int t = 0; t < TAPS; ++t) {
             const int32_t row = a_row0 + p.toff[t];
@@ -250,10 +288,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int32_t hw = p.h * p.w;     // n * hw < 2^31 (conv3x3_eligible)
     const int64_t img_stride = (int64_t)p.n * hw;
     // Per tile and lane: the centre position, whether it is an image pixel, its pixel index.
-    auto lane_pixel = [&](int64_t tile, int32_t& img, int32_t& nb, bool& valid, int32_t& pix, int32_t& iy,
+    auto lane_pixel = [&](const TileWalk& t, int32_t& img, int32_t& nb, bool& valid, int32_t& pix, int32_t& iy,
                           int32_t& ix) {
-      int32_t mt;
-      c3_coords(tile, p, img, mt, nb);
+      img = t.img;
+      nb = t.nb;
+      const int32_t mt = t.mt;
       const int32_t f = p.f0 + BM * mt + q * 32 + lane;  // this lane's centre position
       const int32_t py = f / wp;
       iy = py - p.pad_t;
@@ -265,20 +304,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     // each value is used, the load of the same channel for the CTA's next tile is issued
     // in its place, so the loads are in flight for a whole tile.
     float res[kCols];
+    TileWalk tw;  // this tile
+    tw.start(p, blockIdx.x);
     if (p.residual) {
       int32_t img, nb, pix, iy, ix;
       bool valid;
-      lane_pixel(blockIdx.x, img, nb, valid, pix, iy, ix);
+      lane_pixel(tw, img, nb, valid, pix, iy, ix);
       const int32_t colw = nb * BN + part * kCols;
       const float* rb = p.residual + (int64_t)img * img_stride + pix;
 #pragma unroll
       for (int j = 0; j < kCols; ++j) res[j] = valid && colw + j < p.n ? __ldg(rb + (colw + j) * hw) : 0.0f;
     }
     int iter = 0;
-    for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++iter) {
+    for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++iter, tw.advance()) {
       int32_t img, nb, pix, iy, ix;
       bool valid;
-      lane_pixel(tile, img, nb, valid, pix, iy, ix);
+      lane_pixel(tw, img, nb, valid, pix, iy, ix);
       const int buf = iter & 1;
       const uint32_t aphase = (iter >> 1) & 1;
       // read by the later strided 1x1 conv: rows and columns cov_s * i, i < cov_oh / cov_ow
@@ -294,7 +335,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (p.residual && tile + gridDim.x < num_tiles) {
         int32_t img2, nb2, pix2, iy2, ix2;
         bool valid2;
-        lane_pixel(tile + gridDim.x, img2, nb2, valid2, pix2, iy2, ix2);
+        TileWalk tn = tw;
+        tn.advance();
+        lane_pixel(tn, img2, nb2, valid2, pix2, iy2, ix2);
         const int32_t colw2 = nb2 * BN + part * kCols;
         rn = p.residual + (int64_t)img2 * img_stride + colw2 * hw + pix2;
         ncols = valid2 ? p.n - colw2 : 0;  // columns of the next tile this lane loads
@@ -312,22 +355,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
         if (fast) {
           // per-channel constants from shared memory (16-byte loads, all lanes the same address)
-          float bz[16], cz[16];
+          float bz[16];
 #pragma unroll
           for (int j4 = 0; j4 < 16; j4 += 4) {
             const float4 b4 = *reinterpret_cast<const float4*>(bias_s + colw + cc + j4);
             bz[j4] = b4.x; bz[j4 + 1] = b4.y; bz[j4 + 2] = b4.z; bz[j4 + 3] = b4.w;
-            if (p.w_scale_ch) {
-              const float4 w4 = *reinterpret_cast<const float4*>(wsc_s + colw + cc + j4);
-              cz[j4] = __fmul_rn(sa, w4.x); cz[j4 + 1] = __fmul_rn(sa, w4.y);
-              cz[j4 + 2] = __fmul_rn(sa, w4.z); cz[j4 + 3] = __fmul_rn(sa, w4.w);
-            } else {
-              cz[j4] = cz[j4 + 1] = cz[j4 + 2] = cz[j4 + 3] = cs_tensor;
-            }
           }
           float o[16];
+          if (p.w_scale_ch) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) o[j] = epilogue_t<ACT>((int32_t)v[j], cz[j], bz[j], p.act_param);
+            for (int j = 0; j < 16; ++j)
+              o[j] = epilogue_t<ACT>((int32_t)v[j], __fmul_rn(sa, wsc_s[colw + cc + j]), bz[j], p.act_param);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) o[j] = epilogue_t<ACT>((int32_t)v[j], cs_tensor, bz[j], p.act_param);
+          }
           if (p.residual) {  // the residual block's activation: none, ReLU or LeakyReLU
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
@@ -455,12 +497,14 @@ bool launch_bn(const GemmArgs& a, int mode, int32_t H, int32_t W, int32_t cpad, 
   p.plane_bytes = p.rbox * tg.wp * 16;
   p.plane_stride = (p.plane_bytes + 127) / 128 * 128;
   const int a_bytes = 4 * p.plane_stride;
-  p.stage_bytes = (a_bytes + TAPS * 4 * BN * 16 + 1023) / 1024 * 1024;
-  p.ring = (227 * 1024 - 1024 - kBarBytes - 2 * p.tiles_n * BN * 4) / p.stage_bytes;
+  p.resident = p.stages_k == 1 && p.tiles_n == 1;
+  const int wres_bytes = p.resident ? TAPS * 4 * BN * 16 : 0;
+  p.stage_bytes = (a_bytes + (p.resident ? 0 : TAPS * 4 * BN * 16) + 1023) / 1024 * 1024;
+  p.ring = (227 * 1024 - 1024 - kBarBytes - 2 * p.tiles_n * BN * 4 - wres_bytes) / p.stage_bytes;
   if (p.ring > 8) p.ring = 8;
   if (p.ring < 2) return false;
   p.n_pad = p.tiles_n * BN;
-  const int smem = 1024 + p.ring * p.stage_bytes + kBarBytes + 2 * p.n_pad * 4;
+  const int smem = 1024 + p.ring * p.stage_bytes + kBarBytes + 2 * p.n_pad * 4 + wres_bytes;
   static std::once_flag once;
   std::call_once(once, [] {
     cudaFuncSetAttribute(k_conv3x3<BN, ACT, TAPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
@@ -518,6 +562,8 @@ bool dconv_eligible(const GemmArgs& a, int mode, int32_t h, int32_t w, int32_t c
   if (!dconv_shape_ok(mode, a.m / a.out_l, h, w, cpad, (int32_t)a.n)) return false;
   if (a.amax.ptr && a.amax.elems_per_slot != 0 && a.amax.elems_per_slot != a.n * a.out_l) return false;
   if (a.n * a.out_l >= ((int64_t)1 << 31)) return false;  // per-image offsets in 32 bits
+  if ((a.m / a.out_l) * tap_geom(mode, h, w).tiles_m * ((a.n + 63) / 64) >= ((int64_t)1 << 31))
+    return false;  // tile indices in 32 bits
   if (reinterpret_cast<uintptr_t>(a.a) & 15) return false;
   return tma_encode_fn() != nullptr;
 }
