@@ -54,6 +54,10 @@ constexpr int kCS = 64;         // channels per stage (4 chunk planes of 16 byte
 constexpr int kEpiWarps = 16;   // 4 per TMEM lane quadrant (the stores and residual loads are latency-bound)
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kBarBytes = 256;
+// Four TMEM accumulators: an epilogue warp may run up to three tiles ahead of the
+// slowest one, so the warps drift out of step and one's global stores overlap
+// another's TMEM loads and arithmetic (the store path is the epilogue's bound).
+constexpr int kAccBufs = 4;
 
 struct C3Params {
   int32_t n_img, h, w, cpad, n;    // n: output channels
@@ -151,9 +155,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)p.ring * p.stage_bytes);
   uint64_t* full = bars;              // [ring]
   uint64_t* empty = bars + p.ring;    // [ring]
-  uint64_t* tfull = empty + p.ring;   // [2]
-  uint64_t* tempty = tfull + 2;       // [2]
-  uint64_t* done = tempty + 2;        // [1]
+  uint64_t* tfull = empty + p.ring;   // [kAccBufs]
+  uint64_t* tempty = tfull + kAccBufs;  // [kAccBufs]
+  uint64_t* done = tempty + kAccBufs;   // [1]
   uint64_t* wbar = done + 1;          // [1] resident weights landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wbar + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -162,7 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* wsc_s = bias_s + p.n_pad;
   uint8_t* wres = reinterpret_cast<uint8_t*>(wsc_s + p.n_pad);  // resident weights
   constexpr int kBBytes = TAPS * 4 * BN * 16;
-  constexpr int kTmemCols = 2 * BN;
+  constexpr int kTmemCols = kAccBufs * BN;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t num_tiles = (int64_t)p.n_img * p.tiles_m * p.tiles_n;
@@ -173,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kAccBufs; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], kEpiWarps);
     }
@@ -251,8 +255,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int32_t mt = tw.mt;
         const int32_t r_lo = (p.f0 + BM * mt + p.min_off) / wp;
         const int32_t a_row0 = p.f0 + BM * mt - r_lo * wp;  // the tile's first centre in its loaded rows
-        const int buf = iter & 1;
-        const uint32_t aphase = (iter >> 1) & 1;
+        const int buf = iter & (kAccBufs - 1);
+        const uint32_t aphase = (iter / kAccBufs) & 1;
         if (!mbar_wait(&tempty[buf], aphase ^ 1, abort)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
@@ -320,8 +324,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int32_t img, nb, pix, iy, ix;
       bool valid;
       lane_pixel(tw, img, nb, valid, pix, iy, ix);
-      const int buf = iter & 1;
-      const uint32_t aphase = (iter >> 1) & 1;
+      const int buf = iter & (kAccBufs - 1);
+      const uint32_t aphase = (iter / kAccBufs) & 1;
       // read by the later strided 1x1 conv: rows and columns cov_s * i, i < cov_oh / cov_ow
       const bool cov2 = valid && p.amax2 && iy % p.cov_s == 0 && ix % p.cov_s == 0 && iy / p.cov_s < p.cov_oh &&
                         ix / p.cov_s < p.cov_ow;
