@@ -102,7 +102,9 @@ typedef struct rg_session rg_session;
 
 typedef struct rg_session_options {
   int32_t device;        /* CUDA ordinal */
-  int32_t precision;     /* RG_PREC_INT8 (only INT8 is implemented) */
+  int32_t precision;     /* RG_PREC_INT8, or RG_PREC_FP16 (NpuPrecision::Fp16, npu.rs:425-445:
+                            fp16-rounded operands, f32 sums in k order; attention and SwiGLU
+                            blocks are INT8 only) */
   int32_t weight_quant;  /* 0 = per-tensor (reference, quantize.rs:18-24); 1 = per-output-channel (extension) */
   int32_t flags;         /* RG_SESSION_* bits */
 } rg_session_options;

@@ -194,6 +194,41 @@ static void og_gemm_rows(void* p, int64_t b, int64_t e) {
   }
 }
 
+/* round_fp16 (quantize.rs:50-64): exponent below -14 -> +0, above 15 -> +-65504
+ * (inf and NaN included), else keep 10 mantissa bits, the 13th bit rounding up. */
+float og_round_fp16(float x) {
+  uint32_t bits; memcpy(&bits, &x, 4);
+  uint32_t sign = bits & 0x80000000u;
+  int32_t e = (int32_t)((bits >> 23) & 0xffu) - 127;
+  if (e < -14) return 0.0f;
+  uint32_t r = e > 15 ? (sign | 0x477fe000u) : ((bits + (1u << 12)) & ~0x1fffu);
+  float y; memcpy(&y, &r, 4);
+  return y;
+}
+
+/* fp16_gemm_fused_into (npu.rs:431-445) for rows [b,e): a [m,k] f32, w [n,k]:
+ * acc = 0; acc += round_fp16(a) * w in k order; out = act(round_fp16(acc + bias)). */
+typedef struct {
+  const float* a; const float* w; const float* bias;
+  int64_t k, n; int32_t act; float param; float* out;
+} og_fp16_ctx;
+
+static void og_fp16_rows(void* p, int64_t b, int64_t e) {
+  og_fp16_ctx* c = (og_fp16_ctx*)p;
+  for (int64_t r = b; r < e; ++r) {
+    const float* arow = c->a + r * c->k;
+    for (int64_t j = 0; j < c->n; ++j) {
+      const float* brow = c->w + j * c->k;
+      float acc = 0.0f;
+      for (int64_t i = 0; i < c->k; ++i) {
+        float t = og_round_fp16(arow[i]) * brow[i];
+        acc = acc + t;
+      }
+      c->out[r * c->n + j] = og_act_apply(c->act, c->param, og_round_fp16(acc + c->bias[j]));
+    }
+  }
+}
+
 /* ------------------------------------------------------------------------ */
 /* kernels.rs / shape.rs helpers                                             */
 /* ------------------------------------------------------------------------ */
@@ -525,11 +560,14 @@ og_program* og_compile(const og_layer* layers, int32_t n_layers, int32_t precisi
         float* wt = (float*)malloc(sizeof(float) * (size_t)(wl > 0 ? wl : 1));
         og_transpose2d(l->w, l->in_f, l->out_f, wt);       /* npu.rs:208: [in,out] -> [out,in] */
         op->w_scale = og_quantize_into(wt, wl, op->wq);    /* npu.rs:209: per-tensor */
-        free(wt);
+        op->wh = wt; op->wh_len = wl;                      /* npu.rs:210: round_fp16 of w_t */
+        for (int64_t j = 0; j < wl; ++j) op->wh[j] = og_round_fp16(op->wh[j]);
       } else {
         op->in_channels = l->in_c; op->out_channels = l->out_c; op->kernel = l->k;
         op->stride = l->stride; op->padding = l->pad;
         op->w_scale = og_quantize_into(l->w, wl, op->wq);  /* npu.rs:231: [O, C*k*k] per-tensor */
+        op->wh = (float*)malloc(sizeof(float) * (size_t)(wl > 0 ? wl : 1)); op->wh_len = wl;
+        for (int64_t j = 0; j < wl; ++j) op->wh[j] = og_round_fp16(l->w[j]);  /* npu.rs:232 */
       }
       op->bias = (float*)malloc(sizeof(float) * (size_t)(l->b_len > 0 ? l->b_len : 1));
       memcpy(op->bias, l->b, sizeof(float) * (size_t)l->b_len); op->bias_len = l->b_len;
@@ -544,7 +582,7 @@ og_program* og_compile(const og_layer* layers, int32_t n_layers, int32_t precisi
       op->kind = OG_LAYER_LINEAR; op->in_features = (int32_t)c; op->out_features = (int32_t)c;
       op->wq = (int8_t*)malloc((size_t)(c * c > 0 ? c * c : 1)); op->wq_len = c * c;
       op->w_scale = og_quantize_into(w, c * c, op->wq);
-      free(w);
+      op->wh = w; op->wh_len = c * c;                    /* npu.rs:266: the unrounded diagonal */
       op->bias = (float*)malloc(sizeof(float) * (size_t)(c > 0 ? c : 1));
       memcpy(op->bias, l->b, sizeof(float) * (size_t)c); op->bias_len = c;
       op->act = OG_ACT_NONE;
@@ -584,7 +622,7 @@ void og_program_free(og_program* p) {
   if (!p) return;
   for (int32_t i = 0; i < p->n_ops; ++i) {
     for (int32_t j = 0; j < p->ops[i].n_sub; ++j) { free(p->ops[i].sub[j].wq); free(p->ops[i].sub[j].bias); }
-    free(p->ops[i].sub); free(p->ops[i].extra);
+    free(p->ops[i].sub); free(p->ops[i].extra); free(p->ops[i].wh);
     free(p->ops[i].wq); free(p->ops[i].bias);
   }
   free(p->ops); free(p);
@@ -705,6 +743,7 @@ void og_op_linear_rows(const og_op* op, const float* x, int64_t rows, int64_t r0
 typedef struct {
   const og_op* op; const float* x; float* y; float* a_scales; int8_t* aq; int32_t* acc;
   int32_t c, h, w, oh, ow;
+  int32_t fp16;  /* NpuPrecision::Fp16 arm (npu.rs:351-353) */
 } og_conv_ctx;
 
 static void og_conv_images(void* p, int64_t b, int64_t e) { /* npu.rs:331-359 per image */
@@ -722,6 +761,12 @@ static void og_conv_images(void* p, int64_t b, int64_t e) { /* npu.rs:331-359 pe
     const float* img = c->x + im * img_stride;
     og_im2col(img, c->c, c->h, c->w, op->kernel, op->stride, op->padding, c->oh, c->ow, cols);
     og_transpose2d(cols, ckk, l, cols_t);
+    if (c->fp16) {                                       /* fp16_gemm_fused_into */
+      og_fp16_ctx g = { cols_t, op->wh, op->bias, ckk, O, op->act, op->act_param, ylo };
+      og_fp16_rows(&g, 0, l);
+      og_transpose2d(ylo, l, O, c->y + im * O * l);
+      continue;
+    }
     float sa = og_quantize_into(cols_t, ckk * l, q);     /* per-image scale */
     if (c->a_scales) c->a_scales[im] = sa;
     if (c->aq) { float inv = 1.0f / sa; for (int64_t i = 0; i < img_stride; ++i) c->aq[im * img_stride + i] = og_q1(img[i], inv); }
@@ -739,7 +784,22 @@ void og_op_conv2d(const og_op* op, const float* x, int64_t n, int32_t h, int32_t
                   float* a_scales, int8_t* aq, int32_t* acc, int32_t nthreads) {
   og_conv_ctx c = { op, x, y, a_scales, aq, acc, op->in_channels, h, w,
                     (int32_t)og_out_size(h, op->kernel, op->stride, op->padding),
-                    (int32_t)og_out_size(w, op->kernel, op->stride, op->padding) };
+                    (int32_t)og_out_size(w, op->kernel, op->stride, op->padding), 0 };
+  int64_t out_stride = (int64_t)op->out_channels * c.oh * c.ow;
+  og_parallel_for(n, (n >= 2 && out_stride > 0) ? nthreads : 1, og_conv_images, &c);
+}
+
+/* The FP16 arms of FusedLinear (npu.rs:317) and FusedConv2d (npu.rs:351-353, 372-374). */
+void og_op_linear_fp16(const og_op* op, const float* x, int64_t rows, float* y, int32_t nthreads) {
+  og_fp16_ctx c = { x, op->wh, op->bias, op->in_features, op->out_features, op->act, op->act_param, y };
+  og_parallel_for(rows, nthreads, og_fp16_rows, &c);     /* serial in the reference; rows are independent */
+}
+
+void og_op_conv2d_fp16(const og_op* op, const float* x, int64_t n, int32_t h, int32_t w, float* y,
+                       int32_t nthreads) {
+  og_conv_ctx c = { op, x, y, NULL, NULL, NULL, op->in_channels, h, w,
+                    (int32_t)og_out_size(h, op->kernel, op->stride, op->padding),
+                    (int32_t)og_out_size(w, op->kernel, op->stride, op->padding), 1 };
   int64_t out_stride = (int64_t)op->out_channels * c.oh * c.ow;
   og_parallel_for(n, (n >= 2 && out_stride > 0) ? nthreads : 1, og_conv_images, &c);
 }
@@ -754,7 +814,8 @@ int32_t og_execute(const og_program* p, const float* x, const int64_t* shape, in
                    int32_t nthreads, int64_t* op_ns, int64_t* op_macs) {
   int64_t sh[8]; int32_t nd = ndim;
   if (ndim < 1 || ndim > 8) return -1;
-  if (p->precision != OG_PREC_INT8) return -5;  /* only the Int8 arm is restated */
+  const int32_t fp16 = p->precision == OG_PREC_FP16;
+  if (!fp16 && p->precision != OG_PREC_INT8) return -5;
   int64_t len = 1;
   for (int32_t i = 0; i < ndim; ++i) { sh[i] = shape[i]; len *= shape[i]; }
   float* data = (float*)malloc(sizeof(float) * (size_t)(len > 0 ? len : 1));
@@ -772,7 +833,8 @@ int32_t og_execute(const og_program* p, const float* x, const int64_t* shape, in
         int64_t rows = len / op->in_features;
         macs = rows * op->in_features * op->out_features;
         out = (float*)malloc(sizeof(float) * (size_t)(rows * op->out_features > 0 ? rows * op->out_features : 1));
-        og_op_linear(op, data, rows, out, NULL, NULL, NULL, nthreads);
+        if (fp16) og_op_linear_fp16(op, data, rows, out, nthreads);
+        else og_op_linear(op, data, rows, out, NULL, NULL, NULL, nthreads);
         sh[nd - 1] = op->out_features; len = rows * op->out_features;
         break;
       }
@@ -784,7 +846,8 @@ int32_t og_execute(const og_program* p, const float* x, const int64_t* shape, in
         if (oh <= 0 || ow <= 0) OG_EXEC_FAIL(-2);
         macs = n * op->out_channels * (int64_t)op->in_channels * op->kernel * op->kernel * oh * ow;
         out = (float*)malloc(sizeof(float) * (size_t)(n * op->out_channels * oh * ow > 0 ? n * op->out_channels * oh * ow : 1));
-        og_op_conv2d(op, data, n, (int32_t)h, (int32_t)w, out, NULL, NULL, NULL, nthreads);
+        if (fp16) og_op_conv2d_fp16(op, data, n, (int32_t)h, (int32_t)w, out, nthreads);
+        else og_op_conv2d(op, data, n, (int32_t)h, (int32_t)w, out, NULL, NULL, NULL, nthreads);
         sh[1] = op->out_channels; sh[2] = oh; sh[3] = ow; len = n * op->out_channels * oh * ow;
         break;
       }
@@ -832,7 +895,8 @@ int32_t og_execute(const og_program* p, const float* x, const int64_t* shape, in
         macs = n * op->out_channels * (int64_t)op->in_channels * op->kernel * op->kernel * oh * ow;
         int64_t olen = n * op->out_channels * oh * ow;
         float* so = (float*)malloc(sizeof(float) * (size_t)(olen > 0 ? olen : 1));
-        og_op_conv2d(op, saved[depth - 1], n, (int32_t)h, (int32_t)w, so, NULL, NULL, NULL, nthreads);
+        if (fp16) og_op_conv2d_fp16(op, saved[depth - 1], n, (int32_t)h, (int32_t)w, so, nthreads);
+        else og_op_conv2d(op, saved[depth - 1], n, (int32_t)h, (int32_t)w, so, NULL, NULL, NULL, nthreads);
         free(saved[depth - 1]);
         saved[depth - 1] = so;
         ss[1] = op->out_channels; ss[2] = oh; ss[3] = ow; saved_len[depth - 1] = olen;
@@ -871,6 +935,7 @@ int32_t og_execute(const og_program* p, const float* x, const int64_t* shape, in
         break;
       }
       case OG_LAYER_ATTENTION: {
+        if (fp16) OG_EXEC_FAIL(-5);  /* extension blocks: INT8 Linears only */
         if (nd != 3 || sh[2] != op->in_features || op->out_features <= 0 || op->in_features % op->out_features)
           OG_EXEC_FAIL(-2);
         const int64_t t = sh[1], dh = op->in_features / op->out_features;
@@ -881,6 +946,7 @@ int32_t og_execute(const og_program* p, const float* x, const int64_t* shape, in
         break;
       }
       case OG_LAYER_SWIGLU: {
+        if (fp16) OG_EXEC_FAIL(-5);  /* extension blocks: INT8 Linears only */
         if (sh[nd - 1] != op->in_features) OG_EXEC_FAIL(-2);
         const int64_t rows = len / op->in_features;
         macs = 3 * rows * (int64_t)op->in_features * op->out_features;

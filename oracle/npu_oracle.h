@@ -72,6 +72,9 @@ typedef struct og_op {
    * (gate, up, down), and an f32 array (embedding table [V, d], RMSNorm weight [d]) */
   struct og_op* sub; int32_t n_sub, _pad2;
   float* extra; int64_t extra_len;
+  /* FP16 arm (npu.rs:207-210, 231-232, 258-268): the weights in the reference layout
+   * rounded by round_fp16 (a standalone ChannelAffine keeps its unrounded diagonal) */
+  float* wh; int64_t wh_len;
 } og_op;
 
 typedef struct {
@@ -83,6 +86,7 @@ typedef struct {
 float og_act_apply(int32_t act, float param, float x);      /* mod.rs:38-53 + device/backend.rs:61-78 */
 float og_quant_scale(const float* v, int64_t n);            /* quantize.rs:19-20 */
 float og_quantize_into(const float* v, int64_t n, int8_t* out); /* quantize.rs:27-35 */
+float og_round_fp16(float x);                               /* quantize.rs:50-64 */
 
 og_program* og_compile(const og_layer* layers, int32_t n_layers, int32_t precision); /* npu.rs:188-276 */
 void og_program_free(og_program* p);

@@ -58,6 +58,7 @@ _Op._fields_ = [
     ("act", C.c_int32), ("act_param", C.c_float),
     ("sub", C.POINTER(_Op)), ("n_sub", C.c_int32), ("_pad2", C.c_int32),
     ("extra", C.POINTER(C.c_float)), ("extra_len", C.c_int64),
+    ("wh", C.POINTER(C.c_float)), ("wh_len", C.c_int64),
 ]
 
 
@@ -104,6 +105,8 @@ def lib():
         L.og_act_apply.restype = C.c_float
         L.og_quantize_into.argtypes = [f32p, C.c_int64, i8p]
         L.og_quantize_into.restype = C.c_float
+        L.og_round_fp16.argtypes = [C.c_float]
+        L.og_round_fp16.restype = C.c_float
         L.og_compile.argtypes = [C.POINTER(_Layer), C.c_int32, C.c_int32]
         L.og_compile.restype = C.POINTER(_Program)
         L.og_program_free.argtypes = [C.POINTER(_Program)]
@@ -241,11 +244,12 @@ class Op:
     def __init__(self, raw: _Op):
         self.raw = raw
         for f, _ in _Op._fields_:
-            if f not in ("wq", "bias", "sub", "extra"):
+            if f not in ("wq", "bias", "sub", "extra", "wh"):
                 setattr(self, f, getattr(raw, f))
         self.sub = [Op(raw.sub[j]) for j in range(raw.n_sub)]
         self.wq = np.ctypeslib.as_array(raw.wq, shape=(raw.wq_len,)).copy() if raw.wq_len else None
         self.bias = np.ctypeslib.as_array(raw.bias, shape=(raw.bias_len,)).copy() if raw.bias_len else None
+        self.wh = np.ctypeslib.as_array(raw.wh, shape=(raw.wh_len,)).copy() if raw.wh_len else None
 
     def label(self) -> str:
         buf = C.create_string_buffer(256)

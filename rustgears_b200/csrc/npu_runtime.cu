@@ -148,6 +148,8 @@ struct Op {
   DevBuf d_w3;                   // direct-conv weight arrangement for mode dmode
   int32_t dmode = -1;            // DCONV_3X3 / DCONV_S2D / DCONV_1X1, or -1 (implicit GEMM only)
   DevBuf d_ws;                   // 7x7 / stride 2 stems (<= 4 channels -> 64): the fused stem's arrangement
+  DevBuf d_wh;                   // FP16 arm: f32 weights rounded by round_fp16, reference layout [N, K]
+  bool wh_exact = true;          // every d_wh value is an fp16 value (not the affine diagonal)
   bool bias_finite = true;
   std::string label;
   // transformer extension: the INT8 Linears inside an op (attention: fused QKV
@@ -483,6 +485,18 @@ static rg_status fuse_linears(Session& s, int32_t in, int32_t out_each, const st
   return upload_op(op);
 }
 
+// The FP16 arm's weights (npu.rs:210, 232): round_fp16 of the reference-layout f32
+// weights, kept in f32 on the device; `round` false keeps them as given (the
+// diagonal of a standalone ChannelAffine, npu.rs:258-268).
+static rg_status upload_fp16(Op& op, const std::vector<float>& w, bool round) {
+  std::vector<float> h(w.size());
+  for (size_t j = 0; j < w.size(); ++j) h[j] = round ? round_fp16(w[j]) : w[j];
+  op.wh_exact = round;
+  RG_TRY(op.d_wh.ensure(h.size() * sizeof(float)));
+  if (!h.empty()) RG_CUDA_TRY(cudaMemcpy(op.d_wh.p, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice));
+  return RG_OK;
+}
+
 // npu::compile (npu.rs:188-276).
 static rg_status compile(Session& s, const rg_layer_spec* layers, int32_t n) {
   for (int32_t i = 0; i < n; ++i) RG_TRY(validate_layer(layers[i], i));
@@ -515,6 +529,7 @@ static rg_status compile(Session& s, const rg_layer_spec* layers, int32_t n) {
           for (int64_t c = 0; c < l.out_f; ++c) wt[(size_t)(c * l.in_f + r)] = l.w[(size_t)(r * l.out_f + c)];
         quantize_weights(op, wt.data(), l.out_f, l.in_f, s.weight_quant);
         op.kdim = l.in_f;
+        if (s.precision == RG_PREC_FP16) RG_TRY(upload_fp16(op, wt, true));  // npu.rs:210
       } else {
         op.in_c = l.in_c; op.out_c = l.out_c; op.k = l.k; op.stride = l.stride; op.pad = l.pad;
         // channels padded to 16 per tap so the tensor-core conv gathers 16-byte chunks
@@ -525,6 +540,7 @@ static rg_status compile(Session& s, const rg_layer_spec* layers, int32_t n) {
         op.kxp = op.cpad == 4 ? (int32_t)round_up(l.k, 4) : l.k;
         quantize_weights(op, l.w.data(), l.out_c, (int64_t)l.in_c * l.k * l.k, s.weight_quant);
         op.kdim = (int64_t)op.cpad * l.k * op.kxp;
+        if (s.precision == RG_PREC_FP16) RG_TRY(upload_fp16(op, l.w, true));  // npu.rs:232
       }
       op.kpad = round_up(op.kdim, 16);
       op.bias = l.b;
@@ -540,8 +556,11 @@ static rg_status compile(Session& s, const rg_layer_spec* layers, int32_t n) {
       op.kind = RG_LAYER_LINEAR; op.in_f = (int32_t)c; op.out_f = (int32_t)c;
       quantize_weights(op, w.data(), c, c, s.weight_quant);
       op.kdim = c; op.kpad = round_up(c, 16);
+      if (s.precision == RG_PREC_FP16) RG_TRY(upload_fp16(op, w, false));  // npu.rs:266: unrounded
       op.bias = l.b;
       op.act = RG_ACT_NONE;
+    } else if ((l.kind == RG_LAYER_ATTENTION || l.kind == RG_LAYER_SWIGLU) && s.precision != RG_PREC_INT8) {
+      return fail(RG_ERR_UNSUPPORTED, "layer %zu: attention and SwiGLU blocks run on the INT8 arm only", i);
     } else if (l.kind == RG_LAYER_ATTENTION) {
       const int32_t d = l.in_f;
       op.kind = l.kind; op.in_f = d; op.out_f = l.out_f;  // out_f = heads
@@ -795,7 +814,7 @@ static rg_status make_plan(const Session& s, const int64_t* shape, int32_t ndim,
       if (!full) P.cov_bytes += P.rowcov[i].size() + P.colcov[i].size();
     }
     // a shortcut conv reads the saved block input: its own absmax pass
-    if (op.kind == RG_LAYER_SHORTCUT_CONV2D) continue;
+    if (op.kind == RG_LAYER_SHORTCUT_CONV2D || s.precision != RG_PREC_INT8) continue;
     // the producing op (Flatten only reshapes; a residual begin / shortcut leaves the main path)
     int j = (int)i - 1;
     while (j >= 0 && main_path_noop(s.ops[(size_t)j].kind)) --j;
@@ -814,7 +833,7 @@ static rg_status make_plan(const Session& s, const int64_t* shape, int32_t ndim,
   for (size_t i = 0; i < n; ++i) {
     const Op& op = s.ops[i];
     if (op.kind != RG_LAYER_SHORTCUT_CONV2D || op.k != 1 || op.pad != 0 || op.stride < 2 ||
-        (s.flags & RG_SESSION_NO_FUSION))
+        (s.flags & RG_SESSION_NO_FUSION) || s.precision != RG_PREC_INT8)
       continue;
     int depth = 0, b = -1;  // the residual begin that opens the shortcut's block
     for (int j = (int)i - 1; j >= 0 && b < 0; --j) {
@@ -832,7 +851,7 @@ static rg_status make_plan(const Session& s, const int64_t* shape, int32_t ndim,
   }
   P.block_start.assign(n, 0);
   P.stem_start.assign(n, 0);
-  for (size_t i = 0; i < n; ++i)
+  for (size_t i = 0; i < n && s.precision == RG_PREC_INT8; ++i)
     if (block_at(s, P.shapes, i)) {
       P.block_start[i] = 1;
       i += 3;
@@ -1149,6 +1168,34 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
       case RG_LAYER_SHORTCUT_CONV2D: {
         const bool shortcut = op.kind == RG_LAYER_SHORTCUT_CONV2D;
         fused_residual = false;
+        if (s.precision == RG_PREC_FP16) {  // fp16_gemm_fused_into (npu.rs:431-445), no quantization
+          Fp16Args f;
+          f.x = shortcut ? saved.back() : cur;
+          f.wt = op.d_wh.as<float>();
+          f.bias = op.d_bias.as<float>();
+          f.out = dst;
+          f.act = op.act; f.act_param = op.param;
+          f.exact = op.wh_exact ? 1 : 0;
+          if (op.kind == RG_LAYER_LINEAR) {
+            f.m = os.in_elems / op.in_f; f.n = op.out_f; f.k = op.in_f;
+          } else {
+            f.conv = 1;
+            f.c = op.in_c; f.h = (int32_t)os.in[2]; f.w = (int32_t)os.in[3];
+            f.ks = op.k; f.stride = op.stride; f.pad = op.pad;
+            f.oh = (int32_t)os.out[2]; f.ow = (int32_t)os.out[3];
+            f.m = os.in[0] * os.out[2] * os.out[3]; f.n = op.out_c; f.k = (int64_t)op.in_c * op.k * op.k;
+          }
+          launch_fp16_gemm(f, st);
+          ++launches;
+          RG_LAUNCHED("fp16_gemm");
+          if (shortcut) {
+            saved.back() = dst;
+            if (s.trace) RG_TRY(d2h_vec(s.traces[i].out, dst, os.out_elems, st));
+          } else {
+            cur = dst;
+          }
+          break;
+        }
         bool use3 = false;
         int dmode = -1;                  // direct-conv mode and its operand grid / channels
         int32_t d_h = 0, d_w = 0, d_cp = 0;
@@ -1610,8 +1657,8 @@ rg_status rg_session_create(const rg_layer_spec* layers, int32_t n_layers, const
   *out = nullptr;
   rg_session_options o = {0, RG_PREC_INT8, 0, 0};
   if (opts) o = *opts;
-  if (o.precision != RG_PREC_INT8)
-    return fail(RG_ERR_UNSUPPORTED, "precision %d: only NpuPrecision::Int8 runs on this provider", o.precision);
+  if (o.precision != RG_PREC_INT8 && o.precision != RG_PREC_FP16)
+    return fail(RG_ERR_INVALID_ARG, "precision %d: not an NpuPrecision", o.precision);
   RG_TRY(check_device(o.device));
   RG_CUDA_TRY(cudaSetDevice(o.device));
   std::unique_ptr<rg_session> h(new rg_session());

@@ -103,6 +103,21 @@ struct GemmArgs {
   int32_t cov_s = 1, cov_oh = 0, cov_ow = 0;
 };
 
+// FP16 arm (fp16_gemm_fused_into, npu.rs:431-445) on the CUDA cores: out =
+// act(round_fp16(sum_k round_fp16(a) * w + bias)) with the sum in k order, bit-exact.
+struct Fp16Args {
+  const float* x = nullptr;     // Linear: [m, k] row-major; conv: NCHW input
+  const float* wt = nullptr;    // weights [n, k] row-major (reference layout; conv k = (c, ky, kx))
+  const float* bias = nullptr;  // [n]
+  float* out = nullptr;         // Linear: [m, n]; conv: NCHW
+  int64_t m = 0, n = 0, k = 0;  // conv: m = images * oh * ow
+  int32_t act = 0;
+  float act_param = 0.0f;
+  int32_t exact = 1;            // every weight is an fp16 value (FMA chain is exact)
+  int32_t conv = 0, c = 0, h = 0, w = 0, ks = 0, stride = 1, pad = 0, oh = 0, ow = 0;
+};
+void launch_fp16_gemm(const Fp16Args& a, cudaStream_t st);
+
 void launch_gemm_simt(const GemmArgs& a, cudaStream_t st);
 // Narrow dense GEMM (N <= 32) on the CUDA cores: one thread per output row; takes an
 // i8 A, or an f32 A (af) that it quantizes on the fly.

@@ -338,6 +338,18 @@ RG_HD float gelu_f32(float x) {
   return RG_MUL(RG_MUL(0.5f, x), RG_ADD(1.0f, t));
 }
 
+// round_fp16 (src/inference/quantize.rs:50-64), the FP16 arm's emulation of a
+// binary16 value: exponent below -14 -> +0 (sign dropped), above 15 -> +-65504
+// (infinities and NaN included), otherwise 10 mantissa bits kept with the 13th
+// bit rounding the magnitude up (a carry may reach 65536).
+RG_HD float round_fp16(float x) {
+  const uint32_t bits = f2u(x);
+  const int32_t e = (int32_t)((bits >> 23) & 0xffu) - 127;
+  if (e < -14) return 0.0f;
+  if (e > 15) return u2f((bits & 0x80000000u) | 0x477fe000u);
+  return u2f((bits + (1u << 12)) & ~0x1fffu);
+}
+
 // Activation::apply (src/inference/mod.rs:38-53, src/device/backend.rs:61-78).
 RG_HD float act_apply(int32_t act, float p, float x) {
   switch (act) {

@@ -1,4 +1,4 @@
-"""``InferenceSession`` over ``ExecutionProvider::Npu(Int8)`` on the B200 library.
+"""``InferenceSession`` over ``ExecutionProvider::Npu(Int8 | Fp16)`` on the B200 library.
 
 Mirrors the reference surface (src/inference/mod.rs:102-222, npu.rs:107-176):
 ``InferenceSession.from_module / from_layers / run / last_npu_profile /
@@ -31,8 +31,8 @@ class NpuPrecision(enum.Enum):  # npu.rs:25-41
 
 
 class ExecutionProvider:
-    """`ExecutionProvider` (mod.rs:102-138).  Only ``Npu(Int8)`` runs here; the
-    f32 ``Cpu``/``Gpu(i)`` providers belong to the reference's own runtime."""
+    """`ExecutionProvider` (mod.rs:102-138).  ``Npu(Int8)`` and ``Npu(Fp16)`` run
+    here; the f32 ``Cpu``/``Gpu(i)`` providers belong to the reference's own runtime."""
 
     __slots__ = ("kind", "index", "precision")
 
@@ -170,7 +170,7 @@ def _layer_structs(layers):
 
 
 class InferenceSession:
-    """A compiled Npu(Int8) program resident on one B200."""
+    """A compiled Npu program (Int8 or Fp16 arm) resident on one B200."""
 
     def __init__(self, handle, provider: ExecutionProvider, raw_layers, device: int):
         self._h = handle
@@ -192,7 +192,7 @@ class InferenceSession:
         """`from_layers` (mod.rs:162-180) -> `npu::compile` on the device library."""
         if provider.kind != "Npu":
             raise _native.RgError(_native.RG_ERR_UNSUPPORTED,
-                                  f"provider {provider} is not the Npu(Int8) path this library implements")
+                                  f"provider {provider} is not an Npu path this library implements")
         opts = _native.SessionOptions(device, provider.precision.value,
                                       {"per_tensor": 0, "per_channel": 1}[weight_quant], flags)
         arr, _keep = _layer_structs(layers)
