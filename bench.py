@@ -1,7 +1,8 @@
 #!/usr/bin/env python3
 """INT8 samples/s and achieved INT8 TOPS of the B200 Npu(Int8) execution provider.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c1|c3a|c3b|c3c] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c1|c3a|c3b|c3c|c4|c5]
+                    [--impl ours|reference] [--precision int8|fp16]
 
 N > 1 runs under torchrun (one process per GPU).  Weak scaling: every rank
 runs its own shard of a global batch of N x per-GPU batch; each Linear's
@@ -33,6 +34,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "INT8 samples/sec and achieved TOPS vs B200 dense INT8 peak at 1/2/4/8 GPUs"
+# --precision fp16: the Npu(Fp16) arm (fp16-rounded operands, f32 sums in k order)
+METRIC_FP16 = "FP16 NPU (Npu(Fp16)) samples/sec and achieved f32 FMA TFLOP/s"
 L2_FLUSH_BYTES = 256 << 20
 NOMINAL_INT8_TOPS = 4500.0
 
@@ -139,7 +142,12 @@ def measured_peaks() -> dict:
         return {}
 
 
-def op_roofline(cfg, sess, per_op_ns, steps, x_shape, peaks, traffic=None):
+def fp32_fma_peak(sms: int, mhz: float) -> float:
+    """FP32 FMA rate in TFLOP/s: SMs x 128 FMA/clk x 2 FLOP at the SM clock."""
+    return sms * 128 * 2 * mhz * 1e6 / 1e12
+
+
+def op_roofline(cfg, sess, per_op_ns, steps, x_shape, peaks, traffic=None, fp32_peak=None):
     """Roofline of the dominant kernel.  A kernel covers one op, or several when the
     library fused them (the fused-away ops report no time).  Algorithmic work: 2 x
     the INT8 MACs; algorithmic bytes: the kernel's f32 input read + f32 output
@@ -168,6 +176,16 @@ def op_roofline(cfg, sess, per_op_ns, steps, x_shape, peaks, traffic=None):
     label = " + ".join(prof.records[k].op for k in range(a, b))
     common = {"kernel": label, "ops_per_launch": ops, "algorithmic_bytes": algo, "mean_launch_us": dur_s * 1e6,
               "traffic": traffic}
+    if fp32_peak:  # the FP16 arm: f32 FMA chains on the CUDA cores (f32 weights in HBM)
+        algo = in_bytes + out_bytes + sum(4 * (sess.op_info(k)["wq_len"] + sess.op_info(k)["bias_len"])
+                                          for k in range(a, b))
+        common["algorithmic_bytes"] = algo
+        if ops / max(algo, 1) > fp32_peak * 1e12 / (hbm * 1e9):
+            achieved = ops / dur_s / 1e12
+            return dict(common, bound="fp32", achieved=achieved, peak=fp32_peak, unit="TFLOP/s",
+                        frac=achieved / fp32_peak,
+                        peak_source="FP32 FMA peak: SMs x 128 FMA/clk x 2 at the sampled SM clock "
+                                    "(no FP32 figure in MEASURED_PEAKS.json)")
     if ops / max(algo, 1) > int8_peak * 1e12 / (hbm * 1e9):
         achieved = ops / dur_s / 1e12
         return dict(common, bound="tensor", achieved=achieved, peak=int8_peak, unit="TOPS", frac=achieved / int8_peak,
@@ -264,13 +282,13 @@ def _out_shape(info, shape):
     return shape
 
 
-def cpu_baseline(cfg: str, model, x, steps: int = 0, target_s: float = 12.0):
+def cpu_baseline(cfg: str, model, x, steps: int = 0, target_s: float = 12.0, precision: int = 0):
     """The oracle (CPU restatement of the reference path) on a bounded sample,
     with every host core (the reference's rayon decomposition)."""
     from oracle import oracle
     from rustgears_b200.spec import as_dict
     layers = [as_dict(l) for l in model.export()]
-    prog = oracle.Program(layers)
+    prog = oracle.Program(layers, precision)
     cores = os.cpu_count() or 1
     if cfg.startswith("c3"):
         # rows sampled from the full activation (the absmax covers all rows, as the reference's serial pass)
@@ -309,7 +327,8 @@ def run_reference(args, rank: int, world: int):
     model, x, units = build_workload(cfg, 0, 1, args.batch)
     from oracle import oracle
     from rustgears_b200.spec import as_dict
-    prog = oracle.Program([as_dict(l) for l in model.export()])
+    fp16 = args.precision == "fp16"
+    prog = oracle.Program([as_dict(l) for l in model.export()], 1 if fp16 else 0)
     cores = os.cpu_count() or 1
     c3 = cfg.startswith("c3")
     sample = 64 if c3 else min(units, {"c2": 2048, "c4": 4, "c5": 1}.get(cfg, units))
@@ -329,13 +348,13 @@ def run_reference(args, rank: int, world: int):
     else:
         value = sample * args.steps / dt
         unit = "samples/s"
-    line = {"metric": METRIC, "impl": "reference", "value": value, "unit": unit, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+    line = {"metric": METRIC_FP16 if fp16 else METRIC, "impl": "reference", "value": value, "unit": unit,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16" if fp16 else "int8",
             "data": "synthetic", "config": {"workload": WORKLOADS[cfg]["name"], "per_step_sample": sample},
             "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port",
                              "sample": f"{sample} {'rows' if c3 else 'samples'} per step, {cores} threads "
-                                       "(CPU restatement of the reference Npu(Int8) path)"},
+                                       f"(CPU restatement of the reference Npu({'Fp16' if fp16 else 'Int8'}) path)"},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -346,7 +365,8 @@ def run_probe(args):
 
     from rustgears_b200 import ExecutionProvider, InferenceSession
     model, x, _ = build_workload(args.config, 0, 1, args.batch)
-    sess = InferenceSession.from_module(model, ExecutionProvider.npu_int8(), device=0)
+    prov = ExecutionProvider.npu_fp16() if args.precision == "fp16" else ExecutionProvider.npu_int8()
+    sess = InferenceSession.from_module(model, prov, device=0)
     xd = torch.from_numpy(x).cuda()
     for _ in range(args.steps):
         sess.run_device(xd)
@@ -363,6 +383,8 @@ def main():
     ap.add_argument("--batch", type=int, default=None, help="per-GPU batch (rows for c3)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--precision", default="int8", choices=["int8", "fp16"],
+                    help="Npu(Int8) (the headline) or the Npu(Fp16) arm")
     ap.add_argument("--probe", action="store_true",
                     help="run the workload --steps times and print the profile (for ncu captures; no timing)")
     args = ap.parse_args()
@@ -389,7 +411,11 @@ def main():
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
     cfg = args.config
     model, x, units = build_workload(cfg, rank, world, args.batch)
-    sess = InferenceSession.from_module(model, ExecutionProvider.npu_int8(), device=local)
+    fp16 = args.precision == "fp16"
+    if fp16 and cfg == "c5":
+        raise SystemExit("the transformer's attention and SwiGLU blocks run on the INT8 arm only")
+    prov = ExecutionProvider.npu_fp16() if fp16 else ExecutionProvider.npu_int8()
+    sess = InferenceSession.from_module(model, prov, device=local)
     if world > 1:
         uid = dist.exchange_unique_id(rank)
         dist.attach(sess, rank, world, uid)
@@ -461,27 +487,33 @@ def main():
     e2e_value = units_all * e2e_steps / e2e_s
 
     peaks = measured_peaks()
+    clk = clocks.summary()
+    fp32_peak = fp32_fma_peak(torch.cuda.get_device_properties(dev).multi_processor_count,
+                              clk.get("sm_mhz") or 1965.0) if fp16 else None
     line = {
-        "metric": METRIC, "value": value, "unit": "samples/s" if not cfg.startswith("c3") else "samples/s (GEMM rows)",
+        "metric": METRIC_FP16 if fp16 else METRIC, "value": value, "unit": "samples/s" if not cfg.startswith("c3") else "samples/s (GEMM rows)",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp16 (round_fp16 operands, f32 FMA sums)" if fp16 else "int8",
         "data": "synthetic (reference generator, manual_seed(42))",
         "config": {"workload": WORKLOADS[cfg]["name"], "global_batch": units_all, "per_gpu_batch": units,
                    "parallelism": f"dp{world}", "l2": "flushed before every timed step (256 MiB write)"},
-        "tops": tops, "tops_frac_of_nominal_int8": tops / NOMINAL_INT8_TOPS,
+        "tops": tops, "tops_frac_of_nominal_int8": None if fp16 else tops / NOMINAL_INT8_TOPS,
         "int8_macs_per_unit": macs_unit,
-        "roofline": op_roofline(cfg, sess, per_op_ns, args.steps, x.shape, peaks),
+        "roofline": op_roofline(cfg, sess, per_op_ns, args.steps, x.shape, peaks, fp32_peak=fp32_peak),
         "e2e": {"value": e2e_value, "unit": "samples/s" if not cfg.startswith("c3") else "samples/s (GEMM rows)",
                 "h2d_bytes_per_step": int(xh.nbytes), "d2h_bytes_per_step": int(yh.nbytes),
                 "api": "InferenceSession.run (rg_session_run), pinned host buffers", "steps": e2e_steps},
         "gpu_launches": launches,
-        "clocks": clocks.summary(),
+        "clocks": clk,
     }
+    if fp16:
+        line["config"]["precision"] = "Npu(Fp16)"
     if cfg == "c5":
         line["roofline_int8_projections"] = line["roofline"]
         line["roofline"] = attention_roofline(x.shape, dev, line["clocks"])
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(cfg, model, x)
+        line["cpu_baseline"] = cpu_baseline(cfg, model, x, precision=1 if fp16 else 0)
     if rank == 0:
         print(json.dumps(line), flush=True)
     del sess
