@@ -17,11 +17,14 @@
 // Zero operands (padding, K tails, flushed values) add +0 or -0 to an accumulator that
 // is never -0, so they change nothing and the padded tiles stay exact.
 //
-// Register-tiled f32 GEMM on the CUDA cores: 64 x 64 output tiles, 256 threads with
-// 4 x 4 outputs each, 16-deep K slices staged in shared memory (A rounded as it is
-// staged), the next slice's global loads in flight while the current one is used.
-// A convolution is the same GEMM over rows (image, oy, ox) and the reference's im2col
-// order k = (c, ky, kx), gathered from the NCHW input; outputs go to NCHW.
+// Register-tiled f32 GEMM on the CUDA cores: 256 threads with 4 x 4 outputs each,
+// the tile as wide as the layer needs (16, 32 or 64 columns over 256, 128 or 64 rows),
+// 16-deep K slices staged in shared memory (A rounded as it is staged), the next
+// slice's global loads in flight while the current one is used.  A convolution is
+// the same GEMM over rows (image, oy, ox) and the reference's im2col order
+// k = (c, ky, kx), gathered from the NCHW input through a per-CTA table of the
+// (c, ky, kx) offsets; a thread's rows are spread across the warp's lanes so that
+// both the gathers and the NCHW stores of one instruction touch consecutive pixels.
 #include <cuda_runtime.h>
 
 #include "rg_kernels.h"
@@ -30,89 +33,108 @@
 namespace rg {
 namespace {
 
-constexpr int TM = 64, TN = 64, TK = 16, kThreads = 256;
+constexpr int TK = 16, kThreads = 256;
+constexpr int64_t kMaxConvK = 16384;  // table of (c, ky, kx) offsets: 8 bytes per k in shared memory
 
 struct Fp16Params {
   Fp16Args a;
   int64_t L;  // conv: output pixels per image
 };
 
-template <bool CONV>
-__device__ __forceinline__ void load_a(const Fp16Params& P, int64_t row, int64_t k0, float (&v)[4]) {
-  const Fp16Args& a = P.a;
-  if (!CONV) {
-    const float* src = a.x + row * a.k;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) v[q] = (row < a.m && k0 + q < a.k) ? __ldg(src + k0 + q) : 0.0f;
-    return;
-  }
-  if (row >= a.m) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) v[q] = 0.0f;
-    return;
-  }
-  const int64_t img = row / P.L;
-  const int32_t l = (int32_t)(row - img * P.L);
-  const int32_t oy = l / a.ow, ox = l - oy * a.ow;
-  const int32_t iy0 = oy * a.stride - a.pad, ix0 = ox * a.stride - a.pad;
-  const float* base = a.x + img * (int64_t)a.c * a.h * a.w;
-  const int32_t kk2 = a.ks * a.ks;
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const int64_t kk = k0 + q;
-    float val = 0.0f;
-    if (kk < a.k) {
-      const int32_t c = (int32_t)(kk / kk2), rem = (int32_t)(kk - (int64_t)c * kk2);
-      const int32_t ky = rem / a.ks, kx = rem - ky * a.ks;
-      const int32_t iy = iy0 + ky, ix = ix0 + kx;
-      if (iy >= 0 && iy < a.h && ix >= 0 && ix < a.w) val = __ldg(base + ((int64_t)c * a.h + iy) * a.w + ix);
-    }
-    v[q] = val;
-  }
-}
-
-__device__ __forceinline__ void load_w(const Fp16Params& P, int64_t col, int64_t k0, float (&v)[4]) {
-  const Fp16Args& a = P.a;
-  const float* src = a.wt + col * a.k;
-#pragma unroll
-  for (int q = 0; q < 4; ++q) v[q] = (col < a.n && k0 + q < a.k) ? __ldg(src + k0 + q) : 0.0f;
-}
-
-template <bool CONV, bool EXACT>
+template <int TX, bool CONV, bool EXACT>
 __global__ void __launch_bounds__(kThreads) k_fp16_gemm(const Fp16Params P) {
+  constexpr int TY = kThreads / TX, TM = 4 * TY, TN = 4 * TX;
+  constexpr int KPT = TK * TM / kThreads;  // A values one thread stages per slice
+  constexpr int WPT = TK * TN / kThreads;  // weights one thread stages per slice
   __shared__ __align__(16) float As[TK][TM];
   __shared__ __align__(16) float Ws[TK][TN];
+  extern __shared__ int2 ktab[];           // conv: {c H W + ky W + kx, ky << 16 | kx} per k
   const Fp16Args& a = P.a;
   const int tid = threadIdx.x;
-  const int ty = tid >> 4, tx = tid & 15;      // 4 x 4 outputs: rows 4 ty.., columns 4 tx..
-  const int lr = tid & 63, lq = tid >> 6;      // staging: row / column lr, K quarter lq
+  const int ty = tid / TX, tx = tid % TX;
+  const int lr = tid % TM, ak = (tid / TM) * KPT;  // staged A row and first k of the slice
+  const int lc = tid % TN, wk = (tid / TN) * WPT;  // staged weight row (output column) and first k
   const int64_t m0 = (int64_t)blockIdx.x * TM, n0 = (int64_t)blockIdx.y * TN;
   const int64_t ktiles = (a.k + TK - 1) / TK;
+  const int64_t row = m0 + lr;
+  const bool row_ok = row < a.m;
+  // the staged row: a Linear row, or the output pixel whose receptive field is gathered
+  const float* arow = nullptr;
+  int32_t iy0 = 0, ix0 = 0;
+  if (CONV) {
+    for (int64_t kk = tid; kk < a.k; kk += kThreads) {
+      const int32_t k2 = a.ks * a.ks;
+      const int32_t c = (int32_t)(kk / k2), rem = (int32_t)(kk - (int64_t)c * k2);
+      const int32_t ky = rem / a.ks, kx = rem - ky * a.ks;
+      ktab[kk] = make_int2((c * a.h + ky) * a.w + kx, (ky << 16) | kx);
+    }
+    if (row_ok) {  // rows < 2^31 (checked at launch): 32-bit division
+      const uint32_t img = (uint32_t)row / (uint32_t)P.L;
+      const int32_t l = (int32_t)((uint32_t)row - img * (uint32_t)P.L);
+      const int32_t oy = l / a.ow, ox = l - oy * a.ow;
+      iy0 = oy * a.stride - a.pad;
+      ix0 = ox * a.stride - a.pad;
+      arow = a.x + img * (int64_t)a.c * a.h * a.w;
+    }
+    __syncthreads();
+  } else if (row_ok) {
+    arow = a.x + row * a.k;
+  }
+  const int64_t corner = (int64_t)iy0 * a.w + ix0;  // conv: offset of tap (0, 0) of channel 0
+  auto load_a = [&](int64_t k0, float (&v)[KPT]) {
+#pragma unroll
+    for (int q = 0; q < KPT; ++q) {
+      const int64_t kk = k0 + q;
+      float val = 0.0f;
+      if (row_ok && kk < a.k) {
+        if (CONV) {
+          const int2 e = ktab[kk];
+          const int32_t iy = iy0 + (e.y >> 16), ix = ix0 + (e.y & 0xffff);
+          if (iy >= 0 && iy < a.h && ix >= 0 && ix < a.w) val = __ldg(arow + corner + e.x);
+        } else {
+          val = __ldg(arow + kk);
+        }
+      }
+      v[q] = val;
+    }
+  };
+  const float* wrow = a.wt + (n0 + lc) * a.k;
+  const bool col_ok = n0 + lc < a.n;
+  auto load_w = [&](int64_t k0, float (&v)[WPT]) {
+#pragma unroll
+    for (int q = 0; q < WPT; ++q) v[q] = (col_ok && k0 + q < a.k) ? __ldg(wrow + k0 + q) : 0.0f;
+  };
   float acc[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
-  float va[4], vw[4];
-  load_a<CONV>(P, m0 + lr, lq * 4, va);
-  load_w(P, n0 + lr, lq * 4, vw);
+  float va[KPT], vw[WPT];
+  load_a(ak, va);
+  load_w(wk, vw);
   for (int64_t t = 0; t < ktiles; ++t) {
     __syncthreads();  // the previous slice has been used
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      As[lq * 4 + q][lr] = round_fp16(va[q]);
-      Ws[lq * 4 + q][lr] = vw[q];
-    }
+    for (int q = 0; q < KPT; ++q) As[ak + q][lr] = round_fp16(va[q]);
+#pragma unroll
+    for (int q = 0; q < WPT; ++q) Ws[wk + q][lc] = vw[q];
     __syncthreads();
     if (t + 1 < ktiles) {
-      load_a<CONV>(P, m0 + lr, (t + 1) * TK + lq * 4, va);
-      load_w(P, n0 + lr, (t + 1) * TK + lq * 4, vw);
+      load_a((t + 1) * TK + ak, va);
+      load_w((t + 1) * TK + wk, vw);
     }
 #pragma unroll
     for (int kk = 0; kk < TK; ++kk) {
-      const float4 av = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
+      float ar[4];
+      if (CONV) {  // rows ty + TY i: consecutive pixels across the warp
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ar[i] = As[kk][ty + TY * i];
+      } else {     // rows 4 ty + i
+        const float4 av = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
+        ar[0] = av.x; ar[1] = av.y; ar[2] = av.z; ar[3] = av.w;
+      }
       const float4 wv = *reinterpret_cast<const float4*>(&Ws[kk][tx * 4]);
-      const float ar[4] = {av.x, av.y, av.z, av.w}, wr[4] = {wv.x, wv.y, wv.z, wv.w};
+      const float wr[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -121,18 +143,25 @@ __global__ void __launch_bounds__(kThreads) k_fp16_gemm(const Fp16Params P) {
     }
   }
   // epilogue: act(round_fp16(acc + bias)), row-major [m, n] or NCHW
+  uint32_t img_e = 0, l_e = 0;  // conv: (image, pixel) of row m0 + ty, advanced by TY per i
+  if (CONV) {
+    img_e = (uint32_t)(m0 + ty) / (uint32_t)P.L;
+    l_e = (uint32_t)(m0 + ty) - img_e * (uint32_t)P.L;
+  }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const int64_t row = m0 + ty * 4 + i;
-    if (row >= a.m) continue;
-    int64_t obase;
-    int64_t cstride;
+    const int64_t r = m0 + (CONV ? ty + TY * i : ty * 4 + i);
+    if (CONV && i > 0) {
+      l_e += TY;
+      while (l_e >= (uint32_t)P.L) { l_e -= (uint32_t)P.L; ++img_e; }
+    }
+    if (r >= a.m) continue;
+    int64_t obase, cstride;
     if (CONV) {
-      const int64_t img = row / P.L, l = row - img * P.L;
-      obase = img * a.n * P.L + l;
+      obase = (int64_t)img_e * a.n * P.L + l_e;
       cstride = P.L;
     } else {
-      obase = row * a.n;
+      obase = r * a.n;
       cstride = 1;
     }
 #pragma unroll
@@ -145,21 +174,38 @@ __global__ void __launch_bounds__(kThreads) k_fp16_gemm(const Fp16Params P) {
   }
 }
 
+template <int TX>
+bool launch_tx(const Fp16Params& P, cudaStream_t st) {
+  const Fp16Args& a = P.a;
+  constexpr int TM = 4 * (kThreads / TX), TN = 4 * TX;
+  const dim3 grid((unsigned)((a.m + TM - 1) / TM), (unsigned)((a.n + TN - 1) / TN));
+  if (a.conv) {
+    const size_t smem = (size_t)a.k * sizeof(int2);
+    auto kern = a.exact ? k_fp16_gemm<TX, true, true> : k_fp16_gemm<TX, true, false>;
+    if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return false;
+    kern<<<grid, kThreads, smem, st>>>(P);
+  } else {
+    auto kern = a.exact ? k_fp16_gemm<TX, false, true> : k_fp16_gemm<TX, false, false>;
+    kern<<<grid, kThreads, 0, st>>>(P);
+  }
+  return true;
+}
+
 }  // namespace
 
-void launch_fp16_gemm(const Fp16Args& a, cudaStream_t st) {
-  if (a.m <= 0 || a.n <= 0) return;
+bool launch_fp16_gemm(const Fp16Args& a, cudaStream_t st) {
+  if (a.m <= 0 || a.n <= 0) return true;
+  if (a.conv && (a.k > kMaxConvK || a.h >= 65536 || a.w >= 65536 || a.ks >= 65536 ||
+                 (int64_t)a.c * a.h * a.w >= ((int64_t)1 << 31) || a.m + 1024 >= ((int64_t)1 << 31)))
+    return false;
   Fp16Params P;
   P.a = a;
   P.L = a.conv ? (int64_t)a.oh * a.ow : 0;
-  const dim3 grid((unsigned)((a.m + TM - 1) / TM), (unsigned)((a.n + TN - 1) / TN));
-  if (a.conv) {
-    if (a.exact) k_fp16_gemm<true, true><<<grid, kThreads, 0, st>>>(P);
-    else k_fp16_gemm<true, false><<<grid, kThreads, 0, st>>>(P);
-  } else {
-    if (a.exact) k_fp16_gemm<false, true><<<grid, kThreads, 0, st>>>(P);
-    else k_fp16_gemm<false, false><<<grid, kThreads, 0, st>>>(P);
-  }
+  // as wide as the layer: 16, 32 or 64 output columns per tile
+  if (a.n <= 16) return launch_tx<4>(P, st);
+  if (a.n <= 32) return launch_tx<8>(P, st);
+  return launch_tx<16>(P, st);
 }
 
 }  // namespace rg

@@ -1185,7 +1185,9 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
             f.oh = (int32_t)os.out[2]; f.ow = (int32_t)os.out[3];
             f.m = os.in[0] * os.out[2] * os.out[3]; f.n = op.out_c; f.k = (int64_t)op.in_c * op.k * op.k;
           }
-          launch_fp16_gemm(f, st);
+          if (!launch_fp16_gemm(f, st))
+            return fail(RG_ERR_UNSUPPORTED, "op %zu: FP16 conv beyond the kernel's limits (C*k*k = %lld > 16384, "
+                        "an image of 2^31 elements, or 2^31 output pixels in the batch)", i, (long long)f.k);
           ++launches;
           RG_LAUNCHED("fp16_gemm");
           if (shortcut) {

@@ -116,7 +116,8 @@ struct Fp16Args {
   int32_t exact = 1;            // every weight is an fp16 value (FMA chain is exact)
   int32_t conv = 0, c = 0, h = 0, w = 0, ks = 0, stride = 1, pad = 0, oh = 0, ow = 0;
 };
-void launch_fp16_gemm(const Fp16Args& a, cudaStream_t st);
+// false: a conv whose reduction (C k k > 16384) or geometry the kernel does not take
+bool launch_fp16_gemm(const Fp16Args& a, cudaStream_t st);
 
 void launch_gemm_simt(const GemmArgs& a, cudaStream_t st);
 // Narrow dense GEMM (N <= 32) on the CUDA cores: one thread per output row; takes an
