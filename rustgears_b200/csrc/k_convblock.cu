@@ -148,10 +148,11 @@ __device__ __forceinline__ uint64_t desc_noswz(uint32_t saddr, uint32_t lbo, uin
 
 __host__ __device__ __forceinline__ int canon(int r, int j, int sbo) { return (r & 7) * 16 + (r >> 3) * sbo + j * 128; }
 
+// Max over the warp of absolute values (NaN ignored, as f32::max): non-negative floats
+// order like their bit patterns, so one redux.sync on the bits replaces five shuffle
+// rounds; fmaxf(v, 0) first turns a NaN (a thread whose values were all NaN) into 0.
 __device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
+  return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fmaxf(v, 0.0f))));
 }
 
 template <int ACT>
@@ -389,9 +390,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_convblock(const CBParams p) {
     const int win = 128 * g + 32 * q + lane;  // this lane's pool window
     const bool win_ok = win < P1 * P1;
     const bool busy = 128 * g + 32 * q < P1 * P1;  // a warp with no valid window only hands over
-    float bias1[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) bias1[j] = b1s[j];
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
     const int q2off = (win / P1 + 1) * Q2ROW + ((win % P1 + 1) & 1) * 128 + ((win % P1 + 1) >> 1) * 16;
     for (int it = 0; it < n_it; ++it) {
@@ -406,20 +404,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_convblock(const CBParams p) {
         tc_fence_after();
         const uint32_t tb = lane_base + (uint32_t)(b * 128 + 4 * g * C1);
         if (isfinite(cs1)) {
-          int32_t mx[16];
-          uint32_t acc[16], acc2[16];
+          // the window's four positions in one TMEM round trip; biases broadcast from smem
+          uint32_t acc[16], acc2[16], acc3[16], acc4[16];
           tmem_ld16(tb, acc);
           tmem_ld16(tb + (uint32_t)C1, acc2);
+          tmem_ld16(tb + (uint32_t)(2 * C1), acc3);
+          tmem_ld16(tb + (uint32_t)(3 * C1), acc4);
           tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) mx[j] = max((int32_t)acc[j], (int32_t)acc2[j]);
-          tmem_ld16(tb + (uint32_t)(2 * C1), acc);
-          tmem_ld16(tb + (uint32_t)(3 * C1), acc2);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 16; ++j) mx[j] = max(mx[j], max((int32_t)acc[j], (int32_t)acc2[j]));
-#pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = epi<ACT1>(mx[j], cs1, bias1[j], p.p1);
+          for (int j = 0; j < 16; ++j) {
+            const int32_t mx = max(max((int32_t)acc[j], (int32_t)acc2[j]), max((int32_t)acc3[j], (int32_t)acc4[j]));
+            v[j] = epi<ACT1>(mx, cs1, b1s[j], p.p1);
+          }
         } else {  // reference order: activation per pixel, NaN-propagating max in (dy, dx) order
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] = -INFINITY;
@@ -430,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_convblock(const CBParams p) {
             tmem_ld_wait();
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              const float ev = epi<ACT1>((int32_t)acc[j], cs1, bias1[j], p.p1);
+              const float ev = epi<ACT1>((int32_t)acc[j], cs1, b1s[j], p.p1);
               if (ev > v[j] || ev != ev) v[j] = ev;
             }
           }
