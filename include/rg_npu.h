@@ -81,7 +81,10 @@ typedef enum rg_layer_kind {
 
 typedef enum rg_activation {
   RG_ACT_NONE = 0, RG_ACT_RELU = 1, RG_ACT_SIGMOID = 2, RG_ACT_TANH = 3,
-  RG_ACT_GELU = 4, RG_ACT_LEAKY_RELU = 5
+  RG_ACT_GELU = 4, RG_ACT_LEAKY_RELU = 5,
+  /* Extension (no reference Activation variant or .rtim code): SiLU x * sigmoid(x), the
+   * reference's nn::Silu forward (src/nn/layers.rs:337-346: x.mul(x.sigmoid())) */
+  RG_ACT_SILU = 6
 } rg_activation;
 
 typedef enum rg_precision { RG_PREC_INT8 = 0, RG_PREC_FP16 = 1 } rg_precision;

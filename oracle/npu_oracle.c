@@ -129,6 +129,9 @@ float og_act_apply(int32_t act, float param, float x) {
       return h * s;
     }
     case OG_ACT_LEAKY_RELU: return x > 0.0f ? x : param * x;
+    /* extension: nn::Silu (nn/layers.rs:337-346) = x.mul(x.sigmoid()), the sigmoid of
+     * UnaryOp::apply (device/backend.rs:72) */
+    case OG_ACT_SILU: { float sg = 1.0f / (1.0f + expf(-x)); return x * sg; }
     default: return x;
   }
 }
@@ -651,6 +654,7 @@ static const char* og_act_name(int32_t act, float param, char* tmp, int cap) {
     case OG_ACT_TANH: return "Tanh";
     case OG_ACT_GELU: return "GELU";
     case OG_ACT_LEAKY_RELU: { char f[64]; og_fmt_f32(param, f, 64); snprintf(tmp, (size_t)cap, "LeakyReLU(%s)", f); return tmp; }
+    case OG_ACT_SILU: return "SiLU";
     default: return "?";
   }
 }

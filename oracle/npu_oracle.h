@@ -48,7 +48,7 @@ enum {
   OG_LAYER_EMBEDDING = 12, OG_LAYER_RMSNORM = 13, OG_LAYER_ATTENTION = 14, OG_LAYER_SWIGLU = 15
 };
 enum { OG_ACT_NONE = 0, OG_ACT_RELU = 1, OG_ACT_SIGMOID = 2, OG_ACT_TANH = 3,
-       OG_ACT_GELU = 4, OG_ACT_LEAKY_RELU = 5 };
+       OG_ACT_GELU = 4, OG_ACT_LEAKY_RELU = 5, OG_ACT_SILU = 6 /* extension */ };
 enum { OG_PREC_INT8 = 0, OG_PREC_FP16 = 1 };
 
 typedef struct {

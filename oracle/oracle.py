@@ -28,6 +28,7 @@ RESIDUAL_BEGIN, RESIDUAL_END, SHORTCUT_CONV2D, ADAPTIVE_AVGPOOL2D = 8, 9, 10, 11
 # extensions for the transformer configuration
 EMBEDDING, RMSNORM, ATTENTION, SWIGLU = 12, 13, 14, 15
 ACT_NONE, ACT_RELU, ACT_SIGMOID, ACT_TANH, ACT_GELU, ACT_LEAKY_RELU = 0, 1, 2, 3, 4, 5
+ACT_SILU = 6  # extension: nn::Silu (nn/layers.rs:337-346)
 
 
 class _Rng(C.Structure):

@@ -537,6 +537,7 @@ bool launch_act(const GemmArgs& a, int mode, int32_t h, int32_t w, int32_t cpad,
     case ACT_TANH: return launch_bn<BN, ACT_TANH, TAPS>(a, mode, h, w, cpad, wd, num_sms, st);
     case ACT_GELU: return launch_bn<BN, ACT_GELU, TAPS>(a, mode, h, w, cpad, wd, num_sms, st);
     case ACT_LEAKY_RELU: return launch_bn<BN, ACT_LEAKY_RELU, TAPS>(a, mode, h, w, cpad, wd, num_sms, st);
+    case ACT_SILU: return launch_bn<BN, ACT_SILU, TAPS>(a, mode, h, w, cpad, wd, num_sms, st);
     default: return false;
   }
 }

@@ -407,6 +407,7 @@ bool launch_act(const GemmArgs& a, int num_sms, cudaStream_t st) {
     case ACT_TANH: return launch_bn<BN, ACT_TANH, NARROW>(a, num_sms, st);
     case ACT_GELU: return launch_bn<BN, ACT_GELU, NARROW>(a, num_sms, st);
     case ACT_LEAKY_RELU: return launch_bn<BN, ACT_LEAKY_RELU, NARROW>(a, num_sms, st);
+    case ACT_SILU: return launch_bn<BN, ACT_SILU, NARROW>(a, num_sms, st);
     default: return false;
   }
 }

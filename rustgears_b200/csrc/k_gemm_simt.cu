@@ -362,6 +362,7 @@ void launch_gemm_simt(const GemmArgs& a, cudaStream_t st) {
     case ACT_TANH: k_gemm_simt<ACT_TANH><<<grid, kThreads, 0, st>>>(a); break;
     case ACT_GELU: k_gemm_simt<ACT_GELU><<<grid, kThreads, 0, st>>>(a); break;
     case ACT_LEAKY_RELU: k_gemm_simt<ACT_LEAKY_RELU><<<grid, kThreads, 0, st>>>(a); break;
+    case ACT_SILU: k_gemm_simt<ACT_SILU><<<grid, kThreads, 0, st>>>(a); break;
     default: k_gemm_simt<ACT_NONE><<<grid, kThreads, 0, st>>>(a); break;
   }
 }

@@ -369,6 +369,7 @@ bool launch_act(const GemmArgs& a, int num_sms, cudaStream_t st) {
     case ACT_TANH: return launch_bn<BN, ACT_TANH>(a, num_sms, st);
     case ACT_GELU: return launch_bn<BN, ACT_GELU>(a, num_sms, st);
     case ACT_LEAKY_RELU: return launch_bn<BN, ACT_LEAKY_RELU>(a, num_sms, st);
+    case ACT_SILU: return launch_bn<BN, ACT_SILU>(a, num_sms, st);
     default: return false;
   }
 }

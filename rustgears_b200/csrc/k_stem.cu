@@ -478,6 +478,7 @@ bool launch_stem_pool(const StemPoolArgs& a, int num_sms, cudaStream_t st) {
     case ACT_TANH: return launch_t<ACT_TANH>(a, num_sms, st);
     case ACT_GELU: return launch_t<ACT_GELU>(a, num_sms, st);
     case ACT_LEAKY_RELU: return launch_t<ACT_LEAKY_RELU>(a, num_sms, st);
+    case ACT_SILU: return launch_t<ACT_SILU>(a, num_sms, st);
     default: return false;
   }
 }

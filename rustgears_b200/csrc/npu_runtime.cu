@@ -242,6 +242,7 @@ static void act_name(int32_t act, float p, char* out, size_t cap) {
       snprintf(out, cap, "LeakyReLU(%s)", num);
       break;
     }
+    case RG_ACT_SILU: snprintf(out, cap, "SiLU"); break;  // extension: nn::Silu
     default: snprintf(out, cap, "?"); break;
   }
 }
@@ -326,7 +327,7 @@ static rg_status validate_layer(const rg_layer_spec& l, int idx) {
       return RG_OK;
     case RG_LAYER_RESIDUAL_END:
     case RG_LAYER_ACTIVATION:
-      if (l.act < RG_ACT_NONE || l.act > RG_ACT_LEAKY_RELU)
+      if (l.act < RG_ACT_NONE || l.act > RG_ACT_SILU)
         return fail(RG_ERR_INVALID_ARG, "layer %d: unknown activation tag %d", idx, l.act);
       return RG_OK;
     case RG_LAYER_EMBEDDING:
@@ -2066,7 +2067,7 @@ rg_status rg_gemm_i8_fused(const int8_t* a, const int8_t* w, int64_t m, int64_t 
                            float w_scale, const float* bias, int32_t act, float act_param, float* out, int32_t* acc,
                            float* out_amax, void* stream) {
   RG_TRY(gemm_args_check(a, w, m, n, ld, a_scale, bias, out));
-  if (act < RG_ACT_NONE || act > RG_ACT_LEAKY_RELU) return fail(RG_ERR_INVALID_ARG, "unknown activation %d", act);
+  if (act < RG_ACT_NONE || act > RG_ACT_SILU) return fail(RG_ERR_INVALID_ARG, "unknown activation %d", act);
   GemmArgs g;
   g.a = a; g.lda = ld; g.w = w; g.ldb = ld; g.m = m; g.n = n; g.k = ld;
   g.a_scale = a_scale; g.w_scale = w_scale; g.bias = bias; g.act = act; g.act_param = act_param;
@@ -2118,7 +2119,7 @@ rg_status rg_softmax_f32(const float* x, int64_t outer, int64_t last, float* y, 
 
 rg_status rg_activation_f32(const float* x, int64_t n, int32_t act, float act_param, float* y, void* stream) {
   if (!x || !y) return fail(RG_ERR_INVALID_ARG, "null argument");
-  if (act < RG_ACT_NONE || act > RG_ACT_LEAKY_RELU) return fail(RG_ERR_INVALID_ARG, "unknown activation %d", act);
+  if (act < RG_ACT_NONE || act > RG_ACT_SILU) return fail(RG_ERR_INVALID_ARG, "unknown activation %d", act);
   launch_activation(x, n, act, act_param, y, AmaxSink(), (cudaStream_t)stream);
   RG_CUDA_TRY(cudaGetLastError());
   return RG_OK;

@@ -31,7 +31,7 @@
 namespace rg {
 
 enum : int32_t { ACT_NONE = 0, ACT_RELU = 1, ACT_SIGMOID = 2, ACT_TANH = 3, ACT_GELU = 4,
-                 ACT_LEAKY_RELU = 5 };
+                 ACT_LEAKY_RELU = 5, ACT_SILU = 6 };
 
 RG_HD uint32_t f2u(float f) {
 #ifdef __CUDA_ARCH__
@@ -358,6 +358,8 @@ RG_HD float act_apply(int32_t act, float p, float x) {
     case ACT_TANH: return tanh_f32(x);
     case ACT_GELU: return gelu_f32(x);
     case ACT_LEAKY_RELU: return x > 0.0f ? x : RG_MUL(p, x);
+    // extension: nn::Silu (src/nn/layers.rs:337-346), x * sigmoid(x) with the sigmoid above
+    case ACT_SILU: return RG_MUL(x, RG_DIV(1.0f, RG_ADD(1.0f, exp_f32(-x))));
     default: return x;
   }
 }

@@ -188,6 +188,12 @@ class Gelu(_Act):
     ACT = Activation.GELU
 
 
+class Silu(_Act):
+    """nn::Silu (layers.rs:337-346): x * sigmoid(x).  Extension export: the reference
+    has the layer but no Activation variant for it."""
+    ACT = Activation.SILU
+
+
 class LeakyRelu(Module):
     def __init__(self, slope: float):
         self.slope = slope

@@ -40,6 +40,8 @@ def encode_layers(layers) -> bytes:
         elif k == FLATTEN:
             out += [struct.pack("<I", 5)]
         elif k == ACTIVATION:
+            if l.act.code > 5:
+                raise RtimError(f"activation {l.act} has no .rtim tag (save.rs:206-214)")
             out += [struct.pack("<II", 6, l.act.code), struct.pack("<f", l.act.param)]
         elif k == SOFTMAX:
             out += [struct.pack("<I", 7)]

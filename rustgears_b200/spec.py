@@ -24,15 +24,17 @@ def _fmt_f32(v: float) -> str:
 
 
 class Activation:
-    """`Activation` enum (mod.rs:24-33); codes are the .rtim tags (save.rs:206-214)."""
+    """`Activation` enum (mod.rs:24-33); codes are the .rtim tags (save.rs:206-214).
+    Code 6, SiLU (the reference's nn::Silu, layers.rs:337-346), is an extension with
+    no .rtim tag."""
 
-    NONE_CODE, RELU_CODE, SIGMOID_CODE, TANH_CODE, GELU_CODE, LEAKY_RELU_CODE = range(6)
-    _NAMES = {0: "none", 1: "ReLU", 2: "Sigmoid", 3: "Tanh", 4: "GELU"}
+    NONE_CODE, RELU_CODE, SIGMOID_CODE, TANH_CODE, GELU_CODE, LEAKY_RELU_CODE, SILU_CODE = range(7)
+    _NAMES = {0: "none", 1: "ReLU", 2: "Sigmoid", 3: "Tanh", 4: "GELU", 6: "SiLU"}
 
     __slots__ = ("code", "param")
 
     def __init__(self, code: int, param: float = 0.0):
-        if code not in range(6):
+        if code not in range(7):
             raise ValueError(f"unknown activation tag {code}")
         self.code = int(code)
         self.param = float(np.float32(param)) if code == 5 else 0.0
@@ -61,6 +63,7 @@ Activation.RELU = Activation(1)
 Activation.SIGMOID = Activation(2)
 Activation.TANH = Activation(3)
 Activation.GELU = Activation(4)
+Activation.SILU = Activation(6)
 
 
 def _f32(a) -> np.ndarray:

@@ -315,7 +315,8 @@ def test_residual_ir_errors(gpu):
 
 
 @pytest.mark.parametrize("b,c,n,h,w,act", [(2, 64, 64, 56, 56, 1), (3, 128, 80, 13, 9, 0), (1, 64, 256, 7, 7, 4),
-                                           (2, 192, 64, 5, 31, 1), (4, 64, 128, 1, 1, 0), (1, 64, 64, 3, 120, 5)])
+                                           (2, 192, 64, 5, 31, 1), (4, 64, 128, 1, 1, 0), (1, 64, 64, 3, 120, 5),
+                                           (2, 64, 64, 14, 14, 6)])
 def test_direct_3x3_conv(gpu, oracle_lib, b, c, n, h, w, act):
     """3x3 / stride 1 / pad 1 convs with channels padded to a multiple of 64 run on the
     direct kernel (zero-padded TMA tiles, shifted A operands): every shape class against
@@ -335,7 +336,7 @@ def test_direct_3x3_conv(gpu, oracle_lib, b, c, n, h, w, act):
 
 
 @pytest.mark.parametrize("b,c,h,w,act", [(2, 3, 224, 224, 1), (3, 1, 32, 46, 0), (1, 4, 20, 224, 5), (5, 2, 8, 8, 4),
-                                         (2, 3, 64, 30, 2), (1, 3, 14, 230, 1)])
+                                         (2, 3, 64, 30, 2), (1, 3, 14, 230, 1), (2, 3, 64, 64, 6)])
 def test_fused_stem(gpu, oracle_lib, b, c, h, w, act):
     """Conv(k7 s2 p3 -> 64) + activation + MaxPool(3, 2), the ResNet stem: one kernel over
     the space-to-depth operand with the pool folded into the conv's epilogue, against the
@@ -377,6 +378,7 @@ def test_resnet_two_stage_paths(gpu, oracle_lib, batch, image):
 
 @pytest.mark.parametrize("b,c,n,h,w,k,st,pad,act", [
     (2, 64, 128, 55, 55, 3, 2, 1, 1),   # odd size: the space-to-depth operand's last row / column is padding
+    (2, 64, 128, 28, 28, 3, 2, 1, 6),   # SiLU (activation extension)
     (3, 64, 64, 28, 28, 3, 2, 1, 0),
     (2, 128, 256, 14, 14, 3, 2, 1, 1),
     (1, 192, 80, 9, 13, 3, 2, 1, 5),
@@ -398,3 +400,41 @@ def test_direct_conv_modes(gpu, oracle_lib, b, c, n, h, w, k, st, pad, act):
         layers.append(dict(kind=oracle.ACTIVATION, act=act, act_param=0.1))
     ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
     assert_same(session_for(layers).run(x), ref, f"conv k{k} s{st} {c}->{n} {h}x{w}")
+
+
+@pytest.mark.parametrize("mkn", [(512, 1568, 128), (300, 64, 10), (77, 100, 48), (4100, 4096, 260)])
+def test_silu_linear(gpu, oracle_lib, mkn):
+    """The SiLU activation extension (nn::Silu, src/nn/layers.rs:337-346) fused into the
+    Linear epilogues: tensor-core, narrow and SIMT GEMMs, bit-exact against the oracle."""
+    from oracle.oracle import ACT_SILU
+    m, k, n = mkn
+    rng = np.random.default_rng(m + k + n)
+    w = (rng.standard_normal((k, n)) * 0.05).astype(np.float32)
+    b = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    layers = [dict(kind=oracle.LINEAR, in_features=k, out_features=n, weight=w, bias=b),
+              dict(kind=oracle.ACTIVATION, act=ACT_SILU)]
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
+    sess = session_for(layers)
+    assert sess.op_info(0)["label"].endswith(", SiLU)")
+    assert_same(sess.run(x), ref, f"silu linear {mkn}")
+
+
+def test_silu_conv_implicit_gemm(gpu, oracle_lib):
+    """A 5x5 conv (implicit-GEMM tensor-core path) with the SiLU extension; a CNN block
+    with SiLU (not monotone, so the pooled fused block does not apply) runs op by op."""
+    from oracle.oracle import ACT_SILU
+    rng = np.random.default_rng(55)
+    w = (rng.standard_normal((32, 16, 5, 5)) * 0.05).astype(np.float32)
+    b = (rng.standard_normal(32) * 0.1).astype(np.float32)
+    layers = [dict(kind=oracle.CONV2D, in_channels=16, out_channels=32, kernel=5, stride=1, padding=2, weight=w,
+                   bias=b), dict(kind=oracle.ACTIVATION, act=ACT_SILU)]
+    x = rng.standard_normal((3, 16, 20, 18)).astype(np.float32)
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
+    assert_same(session_for(layers).run(x), ref, "silu conv 5x5")
+    layers, x = configs.c2_cnn(64)
+    for l in layers:
+        if l["kind"] == oracle.ACTIVATION:
+            l["act"] = ACT_SILU
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
+    assert_same(session_for(layers).run(x), ref, "c2 with SiLU")

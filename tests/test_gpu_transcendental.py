@@ -20,7 +20,7 @@ def sweep(stride=251):
     return np.concatenate([x, edge])
 
 
-@pytest.mark.parametrize("act,param", [(4, 0.0), (2, 0.0), (3, 0.0), (5, 0.01)])
+@pytest.mark.parametrize("act,param", [(4, 0.0), (2, 0.0), (3, 0.0), (5, 0.01), (6, 0.0)])
 def test_activation_sweep(gpu, oracle_lib, act, param):
     torch = gpu
     x = sweep()
