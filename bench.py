@@ -2,7 +2,7 @@
 """INT8 samples/s and achieved INT8 TOPS of the B200 Npu(Int8) execution provider.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c1|c3a|c3b|c3c|c4|c5]
-                    [--impl ours|reference] [--precision int8|fp16]
+                    [--impl ours|reference] [--precision int8|fp16|f32]
 
 N > 1 runs under torchrun (one process per GPU).  Weak scaling: every rank
 runs its own shard of a global batch of N x per-GPU batch; each Linear's
@@ -36,6 +36,8 @@ sys.path.insert(0, ROOT)
 METRIC = "INT8 samples/sec and achieved TOPS vs B200 dense INT8 peak at 1/2/4/8 GPUs"
 # --precision fp16: the Npu(Fp16) arm (fp16-rounded operands, f32 sums in k order)
 METRIC_FP16 = "FP16 NPU (Npu(Fp16)) samples/sec and achieved f32 FMA TFLOP/s"
+# --precision f32: the f32 ExecutionProvider::Cpu arm (run_standard) on the B200
+METRIC_F32 = "f32 Cpu-provider (run_standard) samples/sec and achieved f32 FMA TFLOP/s"
 L2_FLUSH_BYTES = 256 << 20
 NOMINAL_INT8_TOPS = 4500.0
 
@@ -288,8 +290,15 @@ def cpu_baseline(cfg: str, model, x, steps: int = 0, target_s: float = 12.0, pre
     from oracle import oracle
     from rustgears_b200.spec import as_dict
     layers = [as_dict(l) for l in model.export()]
-    prog = oracle.Program(layers, precision)
     cores = os.cpu_count() or 1
+    if precision == 2:  # the f32 Cpu provider's run_standard (single-threaded restatement)
+        n = min(x.shape[0], 16)
+        t0 = time.perf_counter()
+        oracle.run_standard(layers, x[:n])
+        dt = time.perf_counter() - t0
+        return {"value": n / dt, "unit": "samples/s", "cores": 1, "kind": "port",
+                "sample": f"{n} samples through og_run_standard, 1 thread", "sample_seconds": dt}
+    prog = oracle.Program(layers, precision)
     if cfg.startswith("c3"):
         # rows sampled from the full activation (the absmax covers all rows, as the reference's serial pass)
         rows = 16
@@ -328,14 +337,20 @@ def run_reference(args, rank: int, world: int):
     from oracle import oracle
     from rustgears_b200.spec import as_dict
     fp16 = args.precision == "fp16"
-    prog = oracle.Program([as_dict(l) for l in model.export()], 1 if fp16 else 0)
-    cores = os.cpu_count() or 1
+    f32 = args.precision == "f32"
+    layers = [as_dict(l) for l in model.export()]
+    prog = oracle.Program(layers, 1 if fp16 else 0)
+    cores = 1 if f32 else (os.cpu_count() or 1)   # og_run_standard is single-threaded
     c3 = cfg.startswith("c3")
     sample = 64 if c3 else min(units, {"c2": 2048, "c4": 4, "c5": 1}.get(cfg, units))
+    if f32:
+        sample = 8 if c3 else min(units, 16)
     ts = []
     for step in range(args.warmup + args.steps):
         t0 = time.perf_counter()
-        if c3:
+        if f32:
+            oracle.run_standard(layers, x[:sample])
+        elif c3:
             oracle.linear_rows(prog.ops[0], prog, 0, x, 0, sample, nthreads=cores)
         else:
             prog.execute(x[:sample], nthreads=cores)
@@ -348,13 +363,15 @@ def run_reference(args, rank: int, world: int):
     else:
         value = sample * args.steps / dt
         unit = "samples/s"
-    line = {"metric": METRIC_FP16 if fp16 else METRIC, "impl": "reference", "value": value, "unit": unit,
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16" if fp16 else "int8",
+    line = {"metric": METRIC_FP16 if fp16 else METRIC_F32 if f32 else METRIC, "impl": "reference", "value": value,
+            "unit": unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp16" if fp16 else "f32" if f32 else "int8",
             "data": "synthetic", "config": {"workload": WORKLOADS[cfg]["name"], "per_step_sample": sample},
             "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port",
                              "sample": f"{sample} {'rows' if c3 else 'samples'} per step, {cores} threads "
-                                       f"(CPU restatement of the reference Npu({'Fp16' if fp16 else 'Int8'}) path)"},
+                                       "(CPU restatement of the reference "
+                                       f"{'Npu(Fp16)' if fp16 else 'Cpu provider' if f32 else 'Npu(Int8)'} path)"},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -365,7 +382,8 @@ def run_probe(args):
 
     from rustgears_b200 import ExecutionProvider, InferenceSession
     model, x, _ = build_workload(args.config, 0, 1, args.batch)
-    prov = ExecutionProvider.npu_fp16() if args.precision == "fp16" else ExecutionProvider.npu_int8()
+    prov = {"fp16": ExecutionProvider.npu_fp16(), "f32": ExecutionProvider.cpu()}.get(args.precision,
+                                                                                       ExecutionProvider.npu_int8())
     sess = InferenceSession.from_module(model, prov, device=0)
     xd = torch.from_numpy(x).cuda()
     for _ in range(args.steps):
@@ -383,8 +401,8 @@ def main():
     ap.add_argument("--batch", type=int, default=None, help="per-GPU batch (rows for c3)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--precision", default="int8", choices=["int8", "fp16"],
-                    help="Npu(Int8) (the headline) or the Npu(Fp16) arm")
+    ap.add_argument("--precision", default="int8", choices=["int8", "fp16", "f32"],
+                    help="Npu(Int8) (the headline), the Npu(Fp16) arm, or the f32 Cpu provider's arithmetic")
     ap.add_argument("--probe", action="store_true",
                     help="run the workload --steps times and print the profile (for ncu captures; no timing)")
     args = ap.parse_args()
@@ -412,9 +430,10 @@ def main():
     cfg = args.config
     model, x, units = build_workload(cfg, rank, world, args.batch)
     fp16 = args.precision == "fp16"
-    if fp16 and cfg == "c5":
-        raise SystemExit("the transformer's attention and SwiGLU blocks run on the INT8 arm only")
-    prov = ExecutionProvider.npu_fp16() if fp16 else ExecutionProvider.npu_int8()
+    f32 = args.precision == "f32"
+    if (fp16 or f32) and cfg in ("c4", "c5"):
+        raise SystemExit("the ResNet and transformer extensions run on the INT8 arm only")
+    prov = ExecutionProvider.npu_fp16() if fp16 else ExecutionProvider.cpu() if f32 else ExecutionProvider.npu_int8()
     sess = InferenceSession.from_module(model, prov, device=local)
     if world > 1:
         uid = dist.exchange_unique_id(rank)
@@ -437,7 +456,10 @@ def main():
         flush.fill_(1)
         sess.run_device(xd, yd, asynchronous=True)
     sess.run_device(xd, yd)                            # a synchronous run: error words, launch count
-    launches_per_run = sess.last_npu_profile().kernel_launches
+    if f32:  # no NpuProfile: every op but Flatten launches one kernel
+        launches_per_run = sum(1 for i in range(sess.num_ops()) if sess.op_info(i)["kind"] != 5)
+    else:
+        launches_per_run = sess.last_npu_profile().kernel_launches
     nops = sess.num_ops()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     barrier()
@@ -454,7 +476,7 @@ def main():
     # per-op CUDA-event durations (the roofline's kernel times) from profiled runs
     prof_runs = max(3, min(args.steps, 10))
     per_op_ns = np.zeros(nops)
-    for s in range(prof_runs):
+    for s in range(prof_runs if not f32 else 0):
         flush.fill_(s & 0xff)
         sess.run_device(xd, yd)
         per_op_ns += np.array([r.duration_ns for r in sess.last_npu_profile().records], dtype=np.float64)
@@ -465,7 +487,8 @@ def main():
         tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
         total_ms = float(t.item())
     ms_per_step = total_ms / args.steps
-    macs_unit = program_macs(sess, x.shape) if not cfg.startswith("c3") else int(np.prod(WORKLOADS[cfg]["shape"][1:]))
+    macs_sess = sess if not f32 else InferenceSession.from_module(model, ExecutionProvider.npu_int8(), device=local)
+    macs_unit = program_macs(macs_sess, x.shape) if not cfg.startswith("c3") else int(np.prod(WORKLOADS[cfg]["shape"][1:]))
     units_all = units * world
     value = units_all / (ms_per_step / 1e3)
     tops = value * 2.0 * macs_unit / 1e12
@@ -489,18 +512,23 @@ def main():
     peaks = measured_peaks()
     clk = clocks.summary()
     fp32_peak = fp32_fma_peak(torch.cuda.get_device_properties(dev).multi_processor_count,
-                              clk.get("sm_mhz") or 1965.0) if fp16 else None
+                              clk.get("sm_mhz") or 1965.0) if (fp16 or f32) else None
     line = {
-        "metric": METRIC_FP16 if fp16 else METRIC, "value": value, "unit": "samples/s" if not cfg.startswith("c3") else "samples/s (GEMM rows)",
+        "metric": METRIC_FP16 if fp16 else METRIC_F32 if f32 else METRIC, "value": value, "unit": "samples/s" if not cfg.startswith("c3") else "samples/s (GEMM rows)",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "fp16 (round_fp16 operands, f32 FMA sums)" if fp16 else "int8",
+        "dtype": "fp16 (round_fp16 operands, f32 FMA sums)" if fp16 else "f32" if f32 else "int8",
         "data": "synthetic (reference generator, manual_seed(42))",
         "config": {"workload": WORKLOADS[cfg]["name"], "global_batch": units_all, "per_gpu_batch": units,
                    "parallelism": f"dp{world}", "l2": "flushed before every timed step (256 MiB write)"},
-        "tops": tops, "tops_frac_of_nominal_int8": None if fp16 else tops / NOMINAL_INT8_TOPS,
+        "tops": tops, "tops_frac_of_nominal_int8": None if (fp16 or f32) else tops / NOMINAL_INT8_TOPS,
         "int8_macs_per_unit": macs_unit,
-        "roofline": op_roofline(cfg, sess, per_op_ns, args.steps, x.shape, peaks, fp32_peak=fp32_peak),
+        "roofline": (op_roofline(cfg, sess, per_op_ns, args.steps, x.shape, peaks, fp32_peak=fp32_peak) if not f32
+                     else {"kernel": "whole program (the f32 provider records no per-op times)", "bound": "fp32",
+                           "achieved": tops, "peak": fp32_peak, "unit": "TFLOP/s", "frac": tops / fp32_peak,
+                           "mean_launch_us": ms_per_step * 1e3, "traffic": None,
+                           "peak_source": "FP32 FMA peak: SMs x 128 FMA/clk x 2 at the sampled SM clock "
+                                          "(no FP32 figure in MEASURED_PEAKS.json)"}),
         "e2e": {"value": e2e_value, "unit": "samples/s" if not cfg.startswith("c3") else "samples/s (GEMM rows)",
                 "h2d_bytes_per_step": int(xh.nbytes), "d2h_bytes_per_step": int(yh.nbytes),
                 "api": "InferenceSession.run (rg_session_run), pinned host buffers", "steps": e2e_steps},
@@ -509,11 +537,13 @@ def main():
     }
     if fp16:
         line["config"]["precision"] = "Npu(Fp16)"
+    if f32:
+        line["config"]["precision"] = "Cpu provider (f32 run_standard)"
     if cfg == "c5":
         line["roofline_int8_projections"] = line["roofline"]
         line["roofline"] = attention_roofline(x.shape, dev, line["clocks"])
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(cfg, model, x, precision=1 if fp16 else 0)
+        line["cpu_baseline"] = cpu_baseline(cfg, model, x, precision=1 if fp16 else 2 if f32 else 0)
     if rank == 0:
         print(json.dumps(line), flush=True)
     del sess

@@ -87,7 +87,10 @@ typedef enum rg_activation {
   RG_ACT_SILU = 6
 } rg_activation;
 
-typedef enum rg_precision { RG_PREC_INT8 = 0, RG_PREC_FP16 = 1 } rg_precision;
+/* RG_PREC_F32: the f32 ExecutionProvider::Cpu arm (run_standard, src/inference/mod.rs:260-331):
+ * BatchNorm folded, no fusion, f32 matmuls in the reference CPU matmul's FMA order; its
+ * sessions record no NpuProfile (rg_session_last_profile returns RG_ERR_NO_PROFILE). */
+typedef enum rg_precision { RG_PREC_INT8 = 0, RG_PREC_FP16 = 1, RG_PREC_F32 = 2 } rg_precision;
 
 typedef struct rg_layer_spec {
   int32_t kind;
@@ -107,7 +110,8 @@ typedef struct rg_session_options {
   int32_t device;        /* CUDA ordinal */
   int32_t precision;     /* RG_PREC_INT8, or RG_PREC_FP16 (NpuPrecision::Fp16, npu.rs:425-445:
                             fp16-rounded operands, f32 sums in k order; attention and SwiGLU
-                            blocks are INT8 only) */
+                            blocks are INT8 only), or RG_PREC_F32 (the Cpu provider: the
+                            reference's layer kinds 1-7 only) */
   int32_t weight_quant;  /* 0 = per-tensor (reference, quantize.rs:18-24); 1 = per-output-channel (extension) */
   int32_t flags;         /* RG_SESSION_* bits */
 } rg_session_options;

@@ -973,3 +973,104 @@ int32_t og_execute(const og_program* p, const float* x, const int64_t* shape, in
   return 0;
 }
 #undef OG_EXEC_FAIL
+
+/* ------------------------------------------------------------------------ */
+/* f32 ExecutionProvider::Cpu (run_standard, mod.rs:260-331)                */
+/* ------------------------------------------------------------------------ */
+int32_t og_run_standard(const og_layer* layers, int32_t n_layers, const float* x, const int64_t* shape,
+                        int32_t ndim, float* y, int64_t y_cap, int64_t* y_shape, int32_t* y_ndim) {
+  if (ndim < 1 || ndim > 8) return -1;
+  int32_t m = 0;
+  og_flayer* f = og_fold(layers, n_layers, &m);          /* from_layers folds for Cpu (mod.rs:163-166) */
+  int64_t sh[8], len = 1; int32_t nd = ndim;
+  for (int32_t i = 0; i < ndim; ++i) { sh[i] = shape[i]; len *= shape[i]; }
+  float* data = (float*)malloc(sizeof(float) * (size_t)(len > 0 ? len : 1));
+  memcpy(data, x, sizeof(float) * (size_t)len);
+  int32_t rc = 0;
+  for (int32_t li = 0; li < m && rc == 0; ++li) {
+    const og_flayer* l = &f[li];
+    float* out = NULL;
+    switch (l->kind) {
+      case OG_LAYER_LINEAR: {                               /* be.matmul(data, W[in,out]) then += bias */
+        if (sh[nd - 1] != l->in_f) { rc = -2; break; }
+        const int64_t rows = len / l->in_f;
+        out = (float*)malloc(sizeof(float) * (size_t)(rows * l->out_f > 0 ? rows * l->out_f : 1));
+        og_bmm_fma(data, l->w, 1, rows, l->in_f, l->out_f, out);
+        for (int64_t r = 0; r < rows; ++r)
+          for (int64_t c = 0; c < l->out_f; ++c) out[r * l->out_f + c] += l->b[c];
+        sh[nd - 1] = l->out_f; len = rows * l->out_f;
+        break;
+      }
+      case OG_LAYER_CONV2D: {                               /* conv2d_forward (kernels.rs:218-263) + bias */
+        if (nd != 4 || sh[1] != l->in_c) { rc = -2; break; }
+        const int64_t n = sh[0], h = sh[2], w = sh[3];
+        const int64_t oh = og_out_size(h, l->k, l->stride, l->pad), ow = og_out_size(w, l->k, l->stride, l->pad);
+        if (oh <= 0 || ow <= 0) { rc = -2; break; }
+        const int64_t L = oh * ow, ckk = (int64_t)l->in_c * l->k * l->k, O = l->out_c;
+        out = (float*)malloc(sizeof(float) * (size_t)(n * O * L > 0 ? n * O * L : 1));
+        float* cols = (float*)malloc(sizeof(float) * (size_t)(ckk * L > 0 ? ckk * L : 1));
+        for (int64_t b = 0; b < n; ++b) {
+          og_im2col(data + b * l->in_c * h * w, l->in_c, (int32_t)h, (int32_t)w, l->k, l->stride, l->pad,
+                    (int32_t)oh, (int32_t)ow, cols);
+          og_bmm_fma(l->w, cols, 1, O, ckk, L, out + b * O * L);   /* W[O, ckk] @ cols[ckk, L] */
+          for (int64_t o = 0; o < O; ++o)
+            for (int64_t p = 0; p < L; ++p) out[(b * O + o) * L + p] += l->b[o];
+        }
+        free(cols);
+        sh[1] = O; sh[2] = oh; sh[3] = ow; len = n * O * L;
+        break;
+      }
+      case OG_LAYER_CHANNEL_AFFINE: {                       /* v * scale + shift over dim 1 */
+        const int64_t c = l->w_len;
+        if (nd < 2 || sh[1] != c) { rc = -2; break; }
+        int64_t inner = 1;
+        for (int32_t d = 2; d < nd; ++d) inner *= sh[d];
+        for (int64_t nn = 0; nn < sh[0]; ++nn)
+          for (int64_t ch = 0; ch < c; ++ch)
+            for (int64_t i = 0; i < inner; ++i) {
+              float* v = &data[(nn * c + ch) * inner + i];
+              const float t = *v * l->w[ch];
+              *v = t + l->b[ch];
+            }
+        break;
+      }
+      case OG_LAYER_MAXPOOL2D: {
+        if (nd != 4) { rc = -2; break; }
+        const int64_t oh = og_out_size(sh[2], l->k, l->stride, 0), ow = og_out_size(sh[3], l->k, l->stride, 0);
+        if (oh <= 0 || ow <= 0) { rc = -2; break; }
+        out = (float*)malloc(sizeof(float) * (size_t)(sh[0] * sh[1] * oh * ow > 0 ? sh[0] * sh[1] * oh * ow : 1));
+        og_maxpool2d(data, sh[0], (int32_t)sh[1], (int32_t)sh[2], (int32_t)sh[3], l->k, l->stride, out, 1);
+        sh[2] = oh; sh[3] = ow; len = sh[0] * sh[1] * oh * ow;
+        break;
+      }
+      case OG_LAYER_FLATTEN: {
+        int64_t rest = 1;
+        for (int32_t d = 1; d < nd; ++d) rest *= sh[d];
+        sh[1] = rest; nd = 2;
+        break;
+      }
+      case OG_LAYER_ACTIVATION:
+        og_activation(data, len, l->act, l->param, data);
+        break;
+      case OG_LAYER_SOFTMAX: {
+        const int64_t last = sh[nd - 1];
+        out = (float*)malloc(sizeof(float) * (size_t)(len > 0 ? len : 1));
+        og_softmax(data, last ? len / last : 0, last, out);
+        break;
+      }
+      default:
+        rc = -5;
+    }
+    if (out) { free(data); data = out; }
+  }
+  if (rc == 0 && len > y_cap) rc = -3;
+  if (rc == 0) {
+    memcpy(y, data, sizeof(float) * (size_t)len);
+    for (int32_t d = 0; d < nd; ++d) y_shape[d] = sh[d];
+    *y_ndim = nd;
+  }
+  free(data);
+  for (int32_t i = 0; i < m; ++i) { free(f[i].w); free(f[i].b); }
+  free(f);
+  return rc;
+}

@@ -89,6 +89,11 @@ float og_quantize_into(const float* v, int64_t n, int8_t* out); /* quantize.rs:2
 float og_round_fp16(float x);                               /* quantize.rs:50-64 */
 
 og_program* og_compile(const og_layer* layers, int32_t n_layers, int32_t precision); /* npu.rs:188-276 */
+/* The f32 ExecutionProvider::Cpu arm: fold_batch_norm then run_standard (mod.rs:162-166,
+ * 260-331) over the reference's layer kinds 1-7.  Returns 0, -1 (bad input rank), -2
+ * (shape mismatch), -3 (output capacity) or -5 (a layer kind outside 1-7). */
+int32_t og_run_standard(const og_layer* layers, int32_t n_layers, const float* x, const int64_t* shape,
+                        int32_t ndim, float* y, int64_t y_cap, int64_t* y_shape, int32_t* y_ndim);
 void og_program_free(og_program* p);
 /* NpuOp::label (npu.rs:83-104); returns bytes written (excluding NUL). */
 int32_t og_op_label(const og_op* op, char* buf, int32_t cap);

@@ -140,6 +140,9 @@ def lib():
         L.og_execute.argtypes = [C.POINTER(_Program), f32p, i64p, C.c_int32, f32p, C.c_int64,
                                  i64p, i32p, C.c_int32, i64p, i64p]
         L.og_execute.restype = C.c_int32
+        L.og_run_standard.argtypes = [C.POINTER(_Layer), C.c_int32, f32p, i64p, C.c_int32, f32p, C.c_int64,
+                                      i64p, i32p]
+        L.og_run_standard.restype = C.c_int32
         _lib = L
     return _lib
 
@@ -583,3 +586,21 @@ def linear_rows(op: Op, prog: Program, op_index: int, x, r0: int, r1: int, nthre
     lib().og_op_linear_rows(C.byref(prog._p.contents.ops[op_index]), _p(x, C.c_float), rows, r0, r1,
                             _p(y, C.c_float), C.byref(sa), _p(acc, C.c_int32), nthreads)
     return y, acc, np.float32(sa.value)
+
+
+def run_standard(specs, x):
+    """The f32 ExecutionProvider::Cpu arm: fold_batch_norm + run_standard (mod.rs:162-166,
+    260-331), the matmuls in the reference CPU matmul's FMA order (og_bmm_fma)."""
+    arr, keep = _to_layers(list(specs))
+    x = _f32(x)
+    shape = np.array(x.shape, np.int64)
+    cap = max(1, _out_capacity(Program(specs), x.shape))  # shapes are those of the Int8 program
+    y = np.empty(cap, np.float32)
+    ys = np.zeros(8, np.int64)
+    nd = C.c_int32(0)
+    rc = lib().og_run_standard(arr, len(specs), _p(x, C.c_float), _p(shape, C.c_int64), x.ndim, _p(y, C.c_float), cap,
+                               _p(ys, C.c_int64), C.byref(nd))
+    if rc != 0:
+        raise RuntimeError(f"og_run_standard failed with {rc}")
+    out_shape = tuple(int(v) for v in ys[: nd.value])
+    return y[: int(np.prod(out_shape))].reshape(out_shape).copy()

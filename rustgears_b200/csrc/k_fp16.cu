@@ -17,6 +17,14 @@
 // Zero operands (padding, K tails, flushed values) add +0 or -0 to an accumulator that
 // is never -0, so they change nothing and the padded tiles stay exact.
 //
+// The same kernel in its second mode runs the f32 ExecutionProvider::Cpu arm
+// (run_standard, src/inference/mod.rs:260-331): the reference's CPU matmul
+// (src/device/cpu.rs:43-64, 233-395) gives every output an FMA chain in k order from 0,
+// except the matmul's output columns past the last full 8-wide block, which accumulate
+// unfused (c += a * b); the bias is added afterwards (one rounding), no activation.
+// The matmul's columns are a Linear's output features, and a conv's output pixels
+// (W[O, C k k] @ cols[C k k, L] per image, src/kernels.rs:218-263).
+//
 // Register-tiled f32 GEMM on the CUDA cores: 256 threads with 4 x 4 outputs each,
 // the tile as wide as the layer needs (16, 32 or 64 columns over 256, 128 or 64 rows),
 // 16-deep K slices staged in shared memory (A rounded as it is staged), the next
@@ -26,6 +34,8 @@
 // (c, ky, kx) offsets; a thread's rows are spread across the warp's lanes so that
 // both the gathers and the NCHW stores of one instruction touch consecutive pixels.
 #include <cuda_runtime.h>
+
+#include <algorithm>
 
 #include "rg_kernels.h"
 #include "rg_math.cuh"
@@ -41,7 +51,8 @@ struct Fp16Params {
   int64_t L;  // conv: output pixels per image
 };
 
-template <int TX, bool CONV, bool EXACT>
+// MODE 0: FP16 arm (EXACT: FMA chains, else separate product and sum); MODE 1: f32 arm.
+template <int TX, bool CONV, bool EXACT, int MODE = 0>
 __global__ void __launch_bounds__(kThreads) k_fp16_gemm(const Fp16Params P) {
   constexpr int TY = kThreads / TX, TM = 4 * TY, TN = 4 * TX;
   constexpr int KPT = TK * TM / kThreads;  // A values one thread stages per slice
@@ -109,13 +120,34 @@ __global__ void __launch_bounds__(kThreads) k_fp16_gemm(const Fp16Params P) {
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+  // f32 arm: which of this thread's outputs take the FMA chain (matmul column in a full
+  // 8-wide block): a Linear's columns 4 tx.. share one answer (blocks of 8 align with 4);
+  // a conv's rows are pixels, each with its own
+  bool fuse[4] = {true, true, true, true};
+  bool all_fused = true;
+  if (MODE == 1) {
+    if (CONV) {
+      const int64_t nvL = P.L / 8 * 8;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t r = m0 + ty + TY * i;
+        fuse[i] = (r % P.L) < nvL;
+        all_fused = all_fused && fuse[i];
+      }
+    } else {
+      const bool f = n0 + tx * 4 < a.n / 8 * 8;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) fuse[i] = f;
+      all_fused = f;
+    }
+  }
   float va[KPT], vw[WPT];
   load_a(ak, va);
   load_w(wk, vw);
   for (int64_t t = 0; t < ktiles; ++t) {
     __syncthreads();  // the previous slice has been used
 #pragma unroll
-    for (int q = 0; q < KPT; ++q) As[ak + q][lr] = round_fp16(va[q]);
+    for (int q = 0; q < KPT; ++q) As[ak + q][lr] = MODE == 1 ? va[q] : round_fp16(va[q]);
 #pragma unroll
     for (int q = 0; q < WPT; ++q) Ws[wk + q][lc] = vw[q];
     __syncthreads();
@@ -135,11 +167,19 @@ __global__ void __launch_bounds__(kThreads) k_fp16_gemm(const Fp16Params P) {
       }
       const float4 wv = *reinterpret_cast<const float4*>(&Ws[kk][tx * 4]);
       const float wr[4] = {wv.x, wv.y, wv.z, wv.w};
+      if (MODE == 1 && !all_fused) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          acc[i][j] = EXACT ? __fmaf_rn(ar[i], wr[j], acc[i][j]) : __fadd_rn(acc[i][j], __fmul_rn(ar[i], wr[j]));
+          for (int j = 0; j < 4; ++j)
+            acc[i][j] = fuse[i] ? __fmaf_rn(ar[i], wr[j], acc[i][j]) : __fadd_rn(acc[i][j], __fmul_rn(ar[i], wr[j]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            acc[i][j] = EXACT ? __fmaf_rn(ar[i], wr[j], acc[i][j]) : __fadd_rn(acc[i][j], __fmul_rn(ar[i], wr[j]));
+      }
     }
   }
   // epilogue: act(round_fp16(acc + bias)), row-major [m, n] or NCHW
@@ -168,6 +208,10 @@ __global__ void __launch_bounds__(kThreads) k_fp16_gemm(const Fp16Params P) {
     for (int j = 0; j < 4; ++j) {
       const int64_t col = n0 + tx * 4 + j;
       if (col >= a.n) continue;
+      if (MODE == 1) {  // matmul, then `+= bias` (mod.rs:270-274, 285-291)
+        a.out[obase + col * cstride] = __fadd_rn(acc[i][j], __ldg(a.bias + col));
+        continue;
+      }
       const float v = round_fp16(__fadd_rn(acc[i][j], __ldg(a.bias + col)));
       a.out[obase + col * cstride] = act_apply(a.act, a.act_param, v);
     }
@@ -181,18 +225,35 @@ bool launch_tx(const Fp16Params& P, cudaStream_t st) {
   const dim3 grid((unsigned)((a.m + TM - 1) / TM), (unsigned)((a.n + TN - 1) / TN));
   if (a.conv) {
     const size_t smem = (size_t)a.k * sizeof(int2);
-    auto kern = a.exact ? k_fp16_gemm<TX, true, true> : k_fp16_gemm<TX, true, false>;
+    auto kern = a.f32 ? k_fp16_gemm<TX, true, true, 1> : a.exact ? k_fp16_gemm<TX, true, true> : k_fp16_gemm<TX, true, false>;
     if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return false;
     kern<<<grid, kThreads, smem, st>>>(P);
   } else {
-    auto kern = a.exact ? k_fp16_gemm<TX, false, true> : k_fp16_gemm<TX, false, false>;
+    auto kern = a.f32 ? k_fp16_gemm<TX, false, true, 1> : a.exact ? k_fp16_gemm<TX, false, true> : k_fp16_gemm<TX, false, false>;
     kern<<<grid, kThreads, 0, st>>>(P);
   }
   return true;
 }
 
+// ChannelAffine of the f32 arm (mod.rs:293-303): v * scale[ch] + shift[ch] over
+// [n][c][inner], product and sum rounded separately.
+__global__ void k_channel_affine(const float* __restrict__ x, int64_t total, int64_t c, int64_t inner,
+                                 const float* __restrict__ scale, const float* __restrict__ shift, float* y) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t ch = (i / inner) % c;
+    y[i] = __fadd_rn(__fmul_rn(x[i], __ldg(scale + ch)), __ldg(shift + ch));
+  }
+}
+
 }  // namespace
+
+void launch_channel_affine(const float* x, int64_t total, int64_t c, int64_t inner, const float* scale,
+                           const float* shift, float* y, cudaStream_t st) {
+  if (total <= 0) return;
+  const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 16);
+  k_channel_affine<<<(unsigned)blocks, 256, 0, st>>>(x, total, c, inner, scale, shift, y);
+}
 
 bool launch_fp16_gemm(const Fp16Args& a, cudaStream_t st) {
   if (a.m <= 0 || a.n <= 0) return true;

@@ -515,9 +515,13 @@ static rg_status compile(Session& s, const rg_layer_spec* layers, int32_t n) {
   s.original_layers = n;
   for (size_t i = 0; i < f.size(); ++i) {
     HostLayer& l = f[i];
-    // an Activation after a shortcut conv belongs to the main path: not fused into it
-    const bool next_act =
-        i + 1 < f.size() && f[i + 1].kind == RG_LAYER_ACTIVATION && l.kind != RG_LAYER_SHORTCUT_CONV2D;
+    // an Activation after a shortcut conv belongs to the main path: not fused into it;
+    // the f32 provider fuses nothing (run_standard walks the folded layers one by one)
+    const bool f32 = s.precision == RG_PREC_F32;
+    if (f32 && l.kind > RG_LAYER_SOFTMAX)
+      return fail(RG_ERR_UNSUPPORTED, "layer %zu: the f32 provider runs the reference's layer kinds 1-7 only", i);
+    const bool next_act = !f32 && i + 1 < f.size() && f[i + 1].kind == RG_LAYER_ACTIVATION &&
+                          l.kind != RG_LAYER_SHORTCUT_CONV2D;
     Op op;
     if (l.kind == RG_LAYER_LINEAR || l.kind == RG_LAYER_CONV2D || l.kind == RG_LAYER_SHORTCUT_CONV2D) {
       op.kind = l.kind;
@@ -531,6 +535,7 @@ static rg_status compile(Session& s, const rg_layer_spec* layers, int32_t n) {
         quantize_weights(op, wt.data(), l.out_f, l.in_f, s.weight_quant);
         op.kdim = l.in_f;
         if (s.precision == RG_PREC_FP16) RG_TRY(upload_fp16(op, wt, true));  // npu.rs:210
+        if (f32) RG_TRY(upload_fp16(op, wt, false));  // f32 weights, [out, in] for the kernel
       } else {
         op.in_c = l.in_c; op.out_c = l.out_c; op.k = l.k; op.stride = l.stride; op.pad = l.pad;
         // channels padded to 16 per tap so the tensor-core conv gathers 16-byte chunks
@@ -542,6 +547,7 @@ static rg_status compile(Session& s, const rg_layer_spec* layers, int32_t n) {
         quantize_weights(op, l.w.data(), l.out_c, (int64_t)l.in_c * l.k * l.k, s.weight_quant);
         op.kdim = (int64_t)op.cpad * l.k * op.kxp;
         if (s.precision == RG_PREC_FP16) RG_TRY(upload_fp16(op, l.w, true));  // npu.rs:232
+        if (f32) RG_TRY(upload_fp16(op, l.w, false));
       }
       op.kpad = round_up(op.kdim, 16);
       op.bias = l.b;
@@ -549,6 +555,14 @@ static rg_status compile(Session& s, const rg_layer_spec* layers, int32_t n) {
       s.npu_bytes += s.precision == RG_PREC_INT8 ? ((int64_t)op.wq.size() + 4) + (int64_t)l.b.size() * 4
                                                  : (int64_t)l.w.size() * 2 + (int64_t)l.b.size() * 2;
       if (next_act) ++i;
+    } else if (l.kind == RG_LAYER_CHANNEL_AFFINE && f32) {
+      // the f32 provider applies a standalone affine elementwise (mod.rs:293-303)
+      op.kind = RG_LAYER_CHANNEL_AFFINE; op.in_f = (int32_t)l.w.size();
+      op.bias = l.b;
+      RG_TRY(upload_fp16(op, l.w, false));
+      RG_TRY(op.d_bias.ensure(op.bias.size() * sizeof(float)));
+      if (!op.bias.empty())
+        RG_CUDA_TRY(cudaMemcpy(op.d_bias.p, op.bias.data(), op.bias.size() * sizeof(float), cudaMemcpyHostToDevice));
     } else if (l.kind == RG_LAYER_CHANNEL_AFFINE) {
       // standalone affine -> diagonal FusedLinear (npu.rs:254-270), no byte accounting
       const int64_t c = (int64_t)l.w.size();
@@ -697,6 +711,10 @@ static rg_status plan_shapes(const Session& s, const int64_t* shape, int32_t ndi
           return fail(RG_ERR_SHAPE, "op %zu (%s): last dim %lld != %d", i, op.label.c_str(), (long long)sh.back(),
                       op.in_f);
         if (op.kind == RG_LAYER_SWIGLU) os.macs = 3ull * (uint64_t)(os.in_elems / op.in_f) * op.in_f * op.out_f;
+        break;
+      case RG_LAYER_CHANNEL_AFFINE:  // the f32 provider's elementwise affine over dim 1
+        if (sh.size() < 2 || sh[1] != op.in_f)
+          return fail(RG_ERR_SHAPE, "op %zu: ChannelAffine over %d channels needs dim 1 = %d", i, op.in_f, op.in_f);
         break;
       case RG_LAYER_ATTENTION:
         if (sh.size() != 3 || sh[2] != op.in_f)
@@ -1169,8 +1187,9 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
       case RG_LAYER_SHORTCUT_CONV2D: {
         const bool shortcut = op.kind == RG_LAYER_SHORTCUT_CONV2D;
         fused_residual = false;
-        if (s.precision == RG_PREC_FP16) {  // fp16_gemm_fused_into (npu.rs:431-445), no quantization
+        if (s.precision != RG_PREC_INT8) {  // fp16_gemm_fused_into (npu.rs:431-445) or the f32 matmul
           Fp16Args f;
+          f.f32 = s.precision == RG_PREC_F32 ? 1 : 0;
           f.x = shortcut ? saved.back() : cur;
           f.wt = op.d_wh.as<float>();
           f.bias = op.d_bias.as<float>();
@@ -1395,6 +1414,14 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         saved.pop_back();
         cur = dst;
         break;
+      case RG_LAYER_CHANNEL_AFFINE: {  // f32 provider only (mod.rs:293-303)
+        const int64_t c = op.in_f, inner = c > 0 && os.in[0] > 0 ? os.in_elems / (os.in[0] * c) : 0;
+        launch_channel_affine(cur, os.in_elems, c, inner, op.d_wh.as<float>(), op.d_bias.as<float>(), dst, st);
+        ++launches;
+        RG_LAUNCHED("channel_affine");
+        cur = dst;
+        break;
+      }
       case RG_LAYER_ADAPTIVE_AVGPOOL2D:
         launch_adaptive_avgpool(cur, os.in[0], (int32_t)os.in[1], (int32_t)os.in[2], (int32_t)os.in[3], op.k,
                                 op.stride, dst, sink, st);
@@ -1660,8 +1687,8 @@ rg_status rg_session_create(const rg_layer_spec* layers, int32_t n_layers, const
   *out = nullptr;
   rg_session_options o = {0, RG_PREC_INT8, 0, 0};
   if (opts) o = *opts;
-  if (o.precision != RG_PREC_INT8 && o.precision != RG_PREC_FP16)
-    return fail(RG_ERR_INVALID_ARG, "precision %d: not an NpuPrecision", o.precision);
+  if (o.precision != RG_PREC_INT8 && o.precision != RG_PREC_FP16 && o.precision != RG_PREC_F32)
+    return fail(RG_ERR_INVALID_ARG, "precision %d: not an NpuPrecision or the f32 provider", o.precision);
   RG_TRY(check_device(o.device));
   RG_CUDA_TRY(cudaSetDevice(o.device));
   std::unique_ptr<rg_session> h(new rg_session());
@@ -1889,6 +1916,18 @@ rg_status rg_session_compilation_report(rg_session* h, char* buf, int64_t cap, i
   const Session& s = h->s;
   const float ratio = s.npu_bytes == 0 ? 1.0f : (float)s.fp32_bytes / (float)s.npu_bytes;
   char head[512];
+  if (s.precision == RG_PREC_F32) {  // CompiledProgram::Standard (mod.rs:200-206)
+    snprintf(head, sizeof head, "InferenceSession [provider = CPU (FP32), device = cpu, ops = %zu (from %d raw layers)]",
+             s.ops.size(), s.original_layers);
+    const std::string r = head;
+    if (needed) *needed = (int64_t)r.size() + 1;
+    if (buf && cap > 0) {
+      const size_t n = std::min<size_t>(r.size(), (size_t)cap - 1);
+      memcpy(buf, r.data(), n);
+      buf[n] = 0;
+    }
+    return RG_OK;
+  }
   snprintf(head, sizeof head,
            "InferenceSession [provider = NPU (%s), layers: %d -> %zu fused ops, weights: %lld B -> %lld B (%.2fx compression)]\n  Pipeline: ",
            s.precision == RG_PREC_INT8 ? "INT8" : "FP16", s.original_layers, s.ops.size(), (long long)s.fp32_bytes,
@@ -1912,6 +1951,8 @@ rg_status rg_session_last_profile(rg_session* h, rg_profile* prof, rg_op_record*
   Session& s = h->s;
   std::lock_guard<std::mutex> lock(s.mu);
   if (!s.last.valid) return fail(RG_ERR_NO_PROFILE, "no run yet");
+  if (s.precision == RG_PREC_F32)  // last_npu_profile is None for the Cpu provider (mod.rs:193-195, 212-214)
+    return fail(RG_ERR_NO_PROFILE, "the f32 provider records no NpuProfile");
   prof->precision = s.precision;
   prof->original_layers = s.original_layers;
   prof->fused_ops = (int32_t)s.ops.size();

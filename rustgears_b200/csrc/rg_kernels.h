@@ -114,10 +114,16 @@ struct Fp16Args {
   int32_t act = 0;
   float act_param = 0.0f;
   int32_t exact = 1;            // every weight is an fp16 value (FMA chain is exact)
+  int32_t f32 = 0;              // the f32 arm instead (ExecutionProvider::Cpu, run_standard): no
+                                // rounding, FMA chains except past the matmul's last full
+                                // 8-wide column block, out = acc + bias
   int32_t conv = 0, c = 0, h = 0, w = 0, ks = 0, stride = 1, pad = 0, oh = 0, ow = 0;
 };
 // false: a conv whose reduction (C k k > 16384) or geometry the kernel does not take
 bool launch_fp16_gemm(const Fp16Args& a, cudaStream_t st);
+// ChannelAffine of the f32 arm: y = x * scale[ch] + shift[ch], ch = (i / inner) % c.
+void launch_channel_affine(const float* x, int64_t total, int64_t c, int64_t inner, const float* scale,
+                           const float* shift, float* y, cudaStream_t st);
 
 void launch_gemm_simt(const GemmArgs& a, cudaStream_t st);
 // Narrow dense GEMM (N <= 32) on the CUDA cores: one thread per output row; takes an

@@ -31,8 +31,9 @@ class NpuPrecision(enum.Enum):  # npu.rs:25-41
 
 
 class ExecutionProvider:
-    """`ExecutionProvider` (mod.rs:102-138).  ``Npu(Int8)`` and ``Npu(Fp16)`` run
-    here; the f32 ``Cpu``/``Gpu(i)`` providers belong to the reference's own runtime."""
+    """`ExecutionProvider` (mod.rs:102-138).  ``Npu(Int8)``, ``Npu(Fp16)`` and the f32
+    ``Cpu`` provider (its arithmetic, on the B200) run here; ``Gpu(i)`` is the
+    reference's wgpu runtime, which needs a graphics stack (unavailable on this box)."""
 
     __slots__ = ("kind", "index", "precision")
 
@@ -55,6 +56,15 @@ class ExecutionProvider:
     def Npu(cls, precision: NpuPrecision) -> "ExecutionProvider":
         return cls("Npu", precision=precision)
 
+    @classmethod
+    def cpu(cls) -> "ExecutionProvider":
+        """`ExecutionProvider::Cpu`: run_standard's f32 arithmetic (mod.rs:260-331)."""
+        return cls("Cpu")
+
+    @classmethod
+    def gpu(cls, index: int = 0) -> "ExecutionProvider":
+        return cls("Gpu", index=index)
+
     def __eq__(self, o):
         return isinstance(o, ExecutionProvider) and (self.kind, self.index, self.precision) == (
             o.kind, o.index, o.precision)
@@ -65,6 +75,17 @@ class ExecutionProvider:
         if self.kind == "Gpu":
             return f"GPU:{self.index} (FP32)"
         return "CPU (FP32)"
+
+
+def _precision_code(provider: ExecutionProvider) -> int:
+    """rg_session_options.precision: 0 Npu(Int8), 1 Npu(Fp16), 2 the f32 Cpu provider."""
+    if provider.kind == "Npu":
+        return provider.precision.value
+    if provider.kind == "Cpu":
+        return 2
+    raise _native.RgError(_native.RG_ERR_UNSUPPORTED,
+                          f"provider {provider}: the reference's wgpu runtime needs a graphics stack, "
+                          "unavailable on this box")
 
 
 def _fmt_duration(ns: int) -> str:
@@ -190,10 +211,7 @@ class InferenceSession:
     def from_layers(cls, layers, provider: ExecutionProvider, device: int = 0,
                     weight_quant: str = "per_tensor", flags: int = 0) -> "InferenceSession":
         """`from_layers` (mod.rs:162-180) -> `npu::compile` on the device library."""
-        if provider.kind != "Npu":
-            raise _native.RgError(_native.RG_ERR_UNSUPPORTED,
-                                  f"provider {provider} is not an Npu path this library implements")
-        opts = _native.SessionOptions(device, provider.precision.value,
+        opts = _native.SessionOptions(device, _precision_code(provider),
                                       {"per_tensor": 0, "per_channel": 1}[weight_quant], flags)
         arr, _keep = _layer_structs(layers)
         h = C.c_void_p()
@@ -205,7 +223,7 @@ class InferenceSession:
                   weight_quant: str = "per_tensor", flags: int = 0) -> "InferenceSession":
         """`load_inference_layers(path)` + `from_layers`, parsed by the library itself."""
         from .rtim import load_inference_layers
-        opts = _native.SessionOptions(device, provider.precision.value,
+        opts = _native.SessionOptions(device, _precision_code(provider),
                                       {"per_tensor": 0, "per_channel": 1}[weight_quant], flags)
         h = C.c_void_p()
         _native.check(_native.lib().rg_session_create_from_rtim(str(path).encode(), C.byref(opts), C.byref(h)))
