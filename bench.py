@@ -39,6 +39,10 @@ METRIC_FP16 = "FP16 NPU (Npu(Fp16)) samples/sec and achieved f32 FMA TFLOP/s"
 # --precision f32: the f32 ExecutionProvider::Cpu arm (run_standard) on the B200
 METRIC_F32 = "f32 Cpu-provider (run_standard) samples/sec and achieved f32 FMA TFLOP/s"
 L2_FLUSH_BYTES = 256 << 20
+# DRAM bytes (read + write) of one launch of the dominant kernel, from a one-pass ncu
+# capture of the same workload (dram__bytes_read.sum + dram__bytes_write.sum,
+# profiles/k_convblock_c2_b32768_dram.md); other workloads report null.
+MEASURED_TRAFFIC = {("c2", 32768): 102837504 + 146597376}
 NOMINAL_INT8_TOPS = 4500.0
 
 WORKLOADS = {
@@ -523,7 +527,8 @@ def main():
                    "parallelism": f"dp{world}", "l2": "flushed before every timed step (256 MiB write)"},
         "tops": tops, "tops_frac_of_nominal_int8": None if (fp16 or f32) else tops / NOMINAL_INT8_TOPS,
         "int8_macs_per_unit": macs_unit,
-        "roofline": (op_roofline(cfg, sess, per_op_ns, args.steps, x.shape, peaks, fp32_peak=fp32_peak) if not f32
+        "roofline": (op_roofline(cfg, sess, per_op_ns, args.steps, x.shape, peaks, fp32_peak=fp32_peak,
+                                 traffic=None if (fp16 or f32) else MEASURED_TRAFFIC.get((cfg, units))) if not f32
                      else {"kernel": "whole program (the f32 provider records no per-op times)", "bound": "fp32",
                            "achieved": tops, "peak": fp32_peak, "unit": "TFLOP/s", "frac": tops / fp32_peak,
                            "mean_launch_us": ms_per_step * 1e3, "traffic": None,
