@@ -1,13 +1,20 @@
 #!/usr/bin/env python3
 """INT8 samples/s and achieved INT8 TOPS of the B200 Npu(Int8) execution provider.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c1|c3a|c3b|c3c|c4|c5]
-                    [--impl ours|reference] [--precision int8|fp16|f32]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3c|c3a|c3b|c2|c1|c4|c5]
+                    [--impl ours|reference] [--precision int8|fp16|f32] [--weight-quant per_tensor|per_channel]
+
+The default workload is the largest single-GPU configuration, C3c: one fused
+INT8 Linear + GELU of 65536 x 4096 x 14336 (a sample is a row of the GEMM).
 
 N > 1 runs under torchrun (one process per GPU).  Weak scaling: every rank
 runs its own shard of a global batch of N x per-GPU batch; each Linear's
-activation absmax is max-all-reduced over NCCL so every rank quantizes
-exactly as one device running the global batch would.
+activation absmax is max-all-reduced over NCCL inside the session's CUDA
+graph, so every rank quantizes exactly as one device running the global batch
+would.  At N > 1 the line also carries a gather-inclusive figure (each step
+followed by the all-gather of every rank's output over NVLink) and
+`sharded_bit_exact`: a small global batch run sharded through the library's
+NCCL path, gathered, and compared bit for bit with one device running it whole.
 
 `value` times the program on device-resident inputs: the steps are enqueued
 back to back as asynchronous runs (a CUDA graph of the program after the
@@ -15,12 +22,13 @@ second identical run), CUDA events on the launching stream bracket each run,
 L2 is flushed by a 256 MiB write before every timed step, max over ranks.  `e2e` times the public host-buffer call
 (InferenceSession.run -> rg_session_run) from pinned memory, H2D and D2H
 included.  `--impl reference` times the CPU restatement of the reference
-Npu(Int8) path (oracle/) on the host cores, the reference itself being
-Rust that this image cannot compile.
+Npu(Int8) path (oracle/, built from oracle/configs.py only) on the host
+cores, the reference itself being Rust that this image cannot compile.
 """
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 import os
 import subprocess
@@ -39,11 +47,30 @@ METRIC_FP16 = "FP16 NPU (Npu(Fp16)) samples/sec and achieved f32 FMA TFLOP/s"
 # --precision f32: the f32 ExecutionProvider::Cpu arm (run_standard) on the B200
 METRIC_F32 = "f32 Cpu-provider (run_standard) samples/sec and achieved f32 FMA TFLOP/s"
 L2_FLUSH_BYTES = 256 << 20
-# DRAM bytes (read + write) of one launch of the dominant kernel, from a one-pass ncu
-# capture of the same workload (dram__bytes_read.sum + dram__bytes_write.sum,
-# profiles/k_convblock_c2_b32768_dram.md); other workloads report null.
-MEASURED_TRAFFIC = {("c2", 32768): 102837504 + 146597376}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the
+# dominant kernel, taken from a one-pass ncu capture of the same workload.  Each
+# figure is a fixed constant tied to the SHA-256 of the kernel source it was
+# captured from: once that source changes the line reports null (with the reason)
+# instead of a figure that no longer describes the kernel.
+MEASURED_TRAFFIC = {
+    ("c2", 32768): dict(bytes=102837504 + 146597376, source="rustgears_b200/csrc/k_convblock.cu",
+                        sha256="430322660bc351e2950c0f81d0e1bf8eefe4b0b190d1b69b2d007565c6f7b7b7"),
+}
 NOMINAL_INT8_TOPS = 4500.0
+
+
+def measured_traffic(cfg: str, units: int):
+    t = MEASURED_TRAFFIC.get((cfg, units))
+    if t is None:
+        return None, "no capture of this workload"
+    try:
+        with open(os.path.join(ROOT, t["source"]), "rb") as f:
+            digest = hashlib.sha256(f.read()).hexdigest()
+    except OSError:
+        return None, f"{t['source']} not found"
+    if digest != t["sha256"]:
+        return None, f"{t['source']} changed since the capture"
+    return t["bytes"], f"one-pass ncu capture of {os.path.basename(t['source'])} (source sha256 {digest[:12]})"
 
 WORKLOADS = {
     "c2": dict(name="small CNN INT8 (Conv(1,16,3,p1)+BN+ReLU, MaxPool2, Conv(16,32,3,p1)+BN+ReLU, MaxPool2, "
@@ -288,94 +315,135 @@ def _out_shape(info, shape):
     return shape
 
 
-def cpu_baseline(cfg: str, model, x, steps: int = 0, target_s: float = 12.0, precision: int = 0):
-    """The oracle (CPU restatement of the reference path) on a bounded sample,
-    with every host core (the reference's rayon decomposition)."""
+def reference_step(cfg: str, prog, layers, x, sample: int, cores: int, precision: int):
+    """One step of the CPU restatement of the reference path on `sample` units of the
+    workload.  Returns (seconds measured, seconds of it that do not scale with the
+    batch).  For C3 the second figure is the reference's serial absmax pass over the
+    whole activation (npu.rs:312), timed on its own: a row sample still pays it in full."""
+    from oracle import oracle
+    if precision == 2:  # the f32 Cpu provider's run_standard (single-threaded restatement)
+        t0 = time.perf_counter()
+        oracle.run_standard(layers, x[:sample])
+        return time.perf_counter() - t0, 0.0
+    if cfg.startswith("c3"):
+        t0 = time.perf_counter()
+        oracle.linear_rows(prog.ops[0], prog, 0, x, 0, 0, nthreads=cores)        # the absmax pass alone
+        t_fixed = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        oracle.linear_rows(prog.ops[0], prog, 0, x, 0, sample, nthreads=cores)   # absmax + `sample` rows
+        return time.perf_counter() - t0, t_fixed
+    t0 = time.perf_counter()
+    prog.execute(x[:sample], nthreads=cores)
+    return time.perf_counter() - t0, 0.0
+
+
+def extrapolate(units: int, sample: int, t: float, t_fixed: float) -> float:
+    """Seconds the whole batch of `units` would take: the fixed part once, the rest
+    linearly in the number of units (every unit costs the same: same shapes)."""
+    return t_fixed + (t - t_fixed) * units / max(sample, 1)
+
+
+def cpu_baseline(cfg: str, model, x, units: int, target_s: float = 10.0, precision: int = 0):
+    """The oracle (CPU restatement of the reference path) on a bounded sample of the
+    benchmark batch, with every host core (the reference's rayon decomposition); the
+    throughput is extrapolated linearly to the whole batch."""
     from oracle import oracle
     from rustgears_b200.spec import as_dict
     layers = [as_dict(l) for l in model.export()]
-    cores = os.cpu_count() or 1
-    if precision == 2:  # the f32 Cpu provider's run_standard (single-threaded restatement)
-        n = min(x.shape[0], 16)
-        t0 = time.perf_counter()
-        oracle.run_standard(layers, x[:n])
-        dt = time.perf_counter() - t0
-        return {"value": n / dt, "unit": "samples/s", "cores": 1, "kind": "port",
-                "sample": f"{n} samples through og_run_standard, 1 thread", "sample_seconds": dt}
-    prog = oracle.Program(layers, precision)
+    cores = 1 if precision == 2 else (os.cpu_count() or 1)
+    prog = None if precision == 2 else oracle.Program(layers, precision)
+    c3 = cfg.startswith("c3")
+    sample = min(units, 16 if c3 or precision == 2 else {"c4": 2, "c5": 1}.get(cfg, 64))
+    t, tf = reference_step(cfg, prog, layers, x, sample, cores, precision)
+    per_unit = (t - tf) / sample
+    grow = int(min(units, max(sample, (target_s - tf) / max(per_unit, 1e-9))))
+    if c3:
+        grow = min(grow, 1024)
+    if grow > sample and t < target_s / 2:
+        sample = grow
+        t, tf = reference_step(cfg, prog, layers, x, sample, cores, precision)
+    full = extrapolate(units, sample, t, tf)
+    what = "rows" if c3 else "samples"
+    how = ("og_run_standard, 1 thread" if precision == 2 else
+           f"og_op_linear_rows, {cores} threads; the absmax over all {units} rows timed separately"
+           if c3 else f"og_execute, {cores} threads")
+    return {"value": units / full, "unit": "samples/s (GEMM rows)" if c3 else "samples/s", "cores": cores,
+            "kind": "port",
+            "sample": f"{sample} of {units} {what} of the benchmark batch ({how}), extrapolated linearly to the batch",
+            "sample_seconds": t}
+
+
+def _reference_workload(cfg: str, units: int, precision: int):
+    """The benchmark workload built by the oracle's own generator (oracle/configs.py,
+    the CPU restatement of the reference RNG and initialisers): (layers, x, sample).
+    The input is drawn after the weights, so the first `sample` units of the batch
+    are the first rows of a batch of `sample`; C3 draws the whole activation, whose
+    absmax the reference's serial pass covers."""
+    from oracle import configs as oc
+    c3 = cfg.startswith("c3")
+    if c3:
+        _, k, n = WORKLOADS[cfg]["shape"]
+        layers, x = oc.c3_linear(units, k, n)
+        return layers, x, 8 if precision == 2 else 64
+    sample = min(units, 16 if precision == 2 else {"c2": 2048, "c4": 4, "c5": 1}.get(cfg, units))
+    build = {"c1": oc.c1_mlp, "c2": oc.c2_cnn, "c4": oc.resnet18,
+             "c5": lambda b: oc.transformer_c5(batch=b)}[cfg]
+    layers, x = build(sample)
+    return layers, x, sample
+
+
+def workload_units(cfg: str, batch):
+    w = WORKLOADS[cfg]
+    return batch or (w["shape"][0] if cfg.startswith("c3") else w["batch"])
+
+
+def workload_config(cfg: str, units: int, world: int, weight_quant: str) -> dict:
+    c = {"workload": WORKLOADS[cfg]["name"], "global_batch": units * world, "per_gpu_batch": units,
+         "parallelism": f"dp{world}", "l2": "flushed before every timed step (256 MiB write)"}
     if cfg.startswith("c3"):
-        # rows sampled from the full activation (the absmax covers all rows, as the reference's serial pass)
-        rows = 16
-        t0 = time.perf_counter()
-        oracle.linear_rows(prog.ops[0], prog, 0, x, 0, rows, nthreads=cores)
-        dt = time.perf_counter() - t0
-        per_row = dt / rows
-        rows = max(16, min(x.shape[0], int(target_s / max(per_row, 1e-9))))
-        rows = min(rows, 1024)
-        t0 = time.perf_counter()
-        oracle.linear_rows(prog.ops[0], prog, 0, x, 0, rows, nthreads=cores)
-        dt = time.perf_counter() - t0
-        m = x.shape[0]
-        return {"value": rows / dt, "unit": "samples/s (GEMM rows)", "cores": cores, "kind": "port",
-                "sample": f"{rows} of {m} rows (scale over all rows), {cores} threads; extrapolated linearly in M",
-                "sample_seconds": dt}
-    n = min({"c4": 2, "c5": 1}.get(cfg, 64), x.shape[0])
-    t0 = time.perf_counter()
-    prog.execute(x[:n], nthreads=cores)
-    dt = time.perf_counter() - t0
-    if dt < target_s / 2:
-        n = int(min(x.shape[0], max(n, target_s / max(dt / n, 1e-9))))
-        t0 = time.perf_counter()
-        prog.execute(x[:n], nthreads=cores)
-        dt = time.perf_counter() - t0
-    return {"value": n / dt, "unit": "samples/s", "cores": cores, "kind": "port",
-            "sample": f"{n} samples of the benchmark batch through og_execute, {cores} threads",
-            "sample_seconds": dt}
+        c["weights"] = f"{weight_quant} symmetric i8"
+    return c
 
 
 def run_reference(args, rank: int, world: int):
+    """The reference arm: the CPU restatement of the reference path (oracle/) on the
+    host cores, the model and input built by oracle/configs.py alone (no part of the
+    product library is loaded).  Each step times a bounded sample of the workload;
+    `value` extrapolates it linearly to the whole per-GPU batch."""
     if rank != 0:
         return
-    cfg = args.config
-    model, x, units = build_workload(cfg, 0, 1, args.batch)
     from oracle import oracle
-    from rustgears_b200.spec import as_dict
+    cfg = args.config
     fp16 = args.precision == "fp16"
     f32 = args.precision == "f32"
-    layers = [as_dict(l) for l in model.export()]
-    prog = oracle.Program(layers, 1 if fp16 else 0)
+    precision = 1 if fp16 else 2 if f32 else 0
+    units = workload_units(cfg, args.batch)
+    layers, x, sample = _reference_workload(cfg, units, precision)
+    wq = 1 if args.weight_quant == "per_channel" else 0
+    prog = None if f32 else oracle.Program(layers, precision, weight_quant=wq)
     cores = 1 if f32 else (os.cpu_count() or 1)   # og_run_standard is single-threaded
     c3 = cfg.startswith("c3")
-    sample = 64 if c3 else min(units, {"c2": 2048, "c4": 4, "c5": 1}.get(cfg, units))
-    if f32:
-        sample = 8 if c3 else min(units, 16)
-    ts = []
+    measured, full = [], []
     for step in range(args.warmup + args.steps):
-        t0 = time.perf_counter()
-        if f32:
-            oracle.run_standard(layers, x[:sample])
-        elif c3:
-            oracle.linear_rows(prog.ops[0], prog, 0, x, 0, sample, nthreads=cores)
-        else:
-            prog.execute(x[:sample], nthreads=cores)
+        t, tf = reference_step(cfg, prog, layers, x, sample, cores, precision)
         if step >= args.warmup:
-            ts.append(time.perf_counter() - t0)
-    dt = float(np.sum(ts))
-    if c3:  # each step computes `sample` of the GEMM's rows (a row is one sample)
-        value = sample * args.steps / dt
-        unit = "samples/s (GEMM rows)"
-    else:
-        value = sample * args.steps / dt
-        unit = "samples/s"
+            measured.append(t + tf)
+            full.append(extrapolate(units, sample, t, tf))
+    value = units * args.steps / float(np.sum(full))
+    unit = "samples/s (GEMM rows)" if c3 else "samples/s"
+    path = "Npu(Fp16)" if fp16 else "Cpu provider" if f32 else "Npu(Int8)"
     line = {"metric": METRIC_FP16 if fp16 else METRIC_F32 if f32 else METRIC, "impl": "reference", "value": value,
             "unit": unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "fp16" if fp16 else "f32" if f32 else "int8",
-            "data": "synthetic", "config": {"workload": WORKLOADS[cfg]["name"], "per_step_sample": sample},
+            "ms_per_step": float(np.mean(measured)) * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16" if fp16 else "f32" if f32 else "int8",
+            "data": "synthetic (reference generator, manual_seed(42))",
+            "config": workload_config(cfg, units, 1, args.weight_quant),
+            "sample_per_step": sample,
             "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port",
-                             "sample": f"{sample} {'rows' if c3 else 'samples'} per step, {cores} threads "
-                                       "(CPU restatement of the reference "
-                                       f"{'Npu(Fp16)' if fp16 else 'Cpu provider' if f32 else 'Npu(Int8)'} path)"},
+                             "sample": f"{sample} {'rows' if c3 else 'samples'} of the {units}-unit batch per step, "
+                                       f"{cores} threads (CPU restatement of the reference {path} path); "
+                                       "value extrapolated linearly to the whole batch"
+                                       + ("; the absmax pass over every row timed in full each step" if c3 else "")},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -388,7 +456,7 @@ def run_probe(args):
     model, x, _ = build_workload(args.config, 0, 1, args.batch)
     prov = {"fp16": ExecutionProvider.npu_fp16(), "f32": ExecutionProvider.cpu()}.get(args.precision,
                                                                                        ExecutionProvider.npu_int8())
-    sess = InferenceSession.from_module(model, prov, device=0)
+    sess = InferenceSession.from_module(model, prov, device=0, weight_quant=args.weight_quant)
     xd = torch.from_numpy(x).cuda()
     for _ in range(args.steps):
         sess.run_device(xd)
@@ -396,17 +464,103 @@ def run_probe(args):
     print(sess.last_npu_profile())
 
 
+def gemm_kernel_roofline(sess, xd, yd, stream, flush, peaks, reps: int = 10):
+    """C3's dominant kernel is the fused tcgen05 GEMM (k_gemm_tc); the op's profile time
+    also holds its absmax and quantize passes.  The kernel is timed alone here through
+    the kernel-level entry point rg_gemm_i8_fused on the session's own quantized
+    weights and the quantized activation, with CUDA events on the launching stream,
+    L2 flushed before every launch."""
+    import ctypes as C
+
+    import torch
+
+    from rustgears_b200 import _native
+    L = _native.lib()
+    dev = xd.device
+    info = sess.op_info(0)
+    k, n = info["in_features"], info["out_features"]
+    m = xd.numel() // k
+    ld = (k + 15) // 16 * 16
+    wq, b = sess.op_weights(0)
+    w = torch.zeros((n, ld), dtype=torch.int8, device=dev)
+    w[:, :k] = torch.from_numpy(wq.reshape(n, k)).to(dev)
+    bias = torch.from_numpy(b).to(dev)
+    amax = torch.zeros(1, dtype=torch.float32, device=dev)
+    scale = torch.zeros(1, dtype=torch.float32, device=dev)
+    q = torch.empty((m, ld), dtype=torch.int8, device=dev)
+    p = lambda t: C.c_void_p(t.data_ptr())
+    st = C.c_void_p(stream.cuda_stream)
+    _native.check(L.rg_absmax_f32(p(xd), m * k, p(amax), st))
+    _native.check(L.rg_quantize_f32_i8(p(xd), m, k, ld, p(amax), p(q), p(scale), st))
+    w_scale = info["w_scale"] if info["w_scale"] > 0 else 1.0 / 127.0   # per-channel: any scale, same work
+    call = lambda: _native.check(L.rg_gemm_i8_fused(p(q), p(w), m, n, ld, p(scale), C.c_float(w_scale), p(bias),
+                                                    info["act"], C.c_float(info["act_param"]), p(yd), None, None, st))
+    call()
+    call()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    torch.cuda.synchronize(dev)
+    for e0, e1 in evs:
+        flush.fill_(3)
+        e0.record(stream)
+        call()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    dur_s = float(np.mean([e0.elapsed_time(e1) for e0, e1 in evs])) / 1e3
+    ops = 2.0 * m * n * k
+    int8_peak = 2.0 * peaks.get("bf16_tflops", 1590.0)
+    achieved = ops / dur_s / 1e12
+    del q, w
+    return {"kernel": f"k_gemm_tc (tcgen05 kind::i8 GEMM + fused dequant/bias/{'GELU' if info['act'] == 4 else 'act'} "
+                      f"epilogue), {m}x{k}x{n}", "bound": "tensor", "achieved": achieved, "peak": int8_peak,
+            "unit": "TOPS", "frac": achieved / int8_peak, "frac_of_nominal_int8": achieved / NOMINAL_INT8_TOPS,
+            "ops_per_launch": ops, "mean_launch_us": dur_s * 1e6,
+            "algorithmic_bytes": m * ld + n * ld + 4 * m * n + 8 * n,
+            "peak_source": "2 x measured bf16 dense burst (MEASURED_PEAKS.json) as the INT8 denominator, "
+                           "no INT8 figure being in that file (nominal INT8 dense 4500)",
+            "timing": f"kernel alone via rg_gemm_i8_fused, mean of {reps} launches, L2 flushed before each"}
+
+
+def sharded_parity(sess, model, prov, x, weight_quant, rank, world, dev, tdist, per_rank: int):
+    """A small global batch (the first `per_rank` units of every rank's shard, gathered)
+    run sharded through the library's NCCL path -- the per-Linear max all-reduce -- its
+    outputs all-gathered by rg_session_allgather, against one device running the whole
+    batch without a communicator.  Every rank takes the same collective steps."""
+    import torch
+
+    from rustgears_b200 import InferenceSession, dist
+    xs = torch.from_numpy(np.ascontiguousarray(x[:per_rank])).to(dev)
+    xg = torch.empty((world * per_rank,) + tuple(xs.shape[1:]), dtype=torch.float32, device=dev)
+    tdist.all_gather_into_tensor(xg, xs)
+    ys = sess.run_device(xs)
+    recv = torch.empty((world * ys.numel(),), dtype=torch.float32, device=dev)
+    dist.allgather(sess, ys.reshape(-1), recv)
+    torch.cuda.synchronize(dev)
+    ok = torch.ones(1, dtype=torch.int32, device=dev)
+    if rank == 0:
+        single = InferenceSession.from_module(model, prov, device=dev.index, weight_quant=weight_quant)
+        yg = single.run_device(xg)
+        torch.cuda.synchronize(dev)
+        a, b = recv.view(yg.shape), yg
+        same = bool(torch.all((a == b) | (torch.isnan(a) & torch.isnan(b))).item())
+        ok.fill_(int(same))
+        del single
+    tdist.broadcast(ok, src=0)
+    return bool(ok.item()), world * per_rank
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c2", choices=sorted(WORKLOADS))
+    ap.add_argument("--config", default="c3c", choices=sorted(WORKLOADS))
     ap.add_argument("--batch", type=int, default=None, help="per-GPU batch (rows for c3)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--precision", default="int8", choices=["int8", "fp16", "f32"],
                     help="Npu(Int8) (the headline), the Npu(Fp16) arm, or the f32 Cpu provider's arithmetic")
+    ap.add_argument("--weight-quant", default="per_tensor", choices=["per_tensor", "per_channel"],
+                    help="i8 weight scales: per tensor (the reference) or per output channel (extension)")
     ap.add_argument("--probe", action="store_true",
                     help="run the workload --steps times and print the profile (for ncu captures; no timing)")
     args = ap.parse_args()
@@ -432,13 +586,14 @@ def main():
     if world > 1:
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
     cfg = args.config
+    c3 = cfg.startswith("c3")
     model, x, units = build_workload(cfg, rank, world, args.batch)
     fp16 = args.precision == "fp16"
     f32 = args.precision == "f32"
     if (fp16 or f32) and cfg in ("c4", "c5"):
         raise SystemExit("the ResNet and transformer extensions run on the INT8 arm only")
     prov = ExecutionProvider.npu_fp16() if fp16 else ExecutionProvider.cpu() if f32 else ExecutionProvider.npu_int8()
-    sess = InferenceSession.from_module(model, prov, device=local)
+    sess = InferenceSession.from_module(model, prov, device=local, weight_quant=args.weight_quant)
     if world > 1:
         uid = dist.exchange_unique_id(rank)
         dist.attach(sess, rank, world, uid)
@@ -477,6 +632,40 @@ def main():
             evs[s][1].record(stream)
         barrier()
     launches = launches_per_run * args.steps
+    total_ms = float(sum(a.elapsed_time(b) for a, b in evs))
+    if world > 1:
+        t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+
+    # gather-inclusive: each step followed by the all-gather of every rank's output
+    gather = None
+    if world > 1:
+        g_steps = max(3, min(args.steps, 10))
+        recv = torch.empty((world * yd.numel(),), dtype=torch.float32, device=dev)
+        for _ in range(2):
+            sess.run_device(xd, yd, asynchronous=True)
+            dist.allgather(sess, yd.view(-1), recv)
+        barrier()
+        gevs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(g_steps)]
+        for s in range(g_steps):
+            flush.fill_(s & 0xff)
+            gevs[s][0].record(stream)
+            sess.run_device(xd, yd, asynchronous=True)
+            dist.allgather(sess, yd.view(-1), recv)
+            gevs[s][1].record(stream)
+        barrier()
+        g_ms = float(sum(a.elapsed_time(b) for a, b in gevs))
+        t = torch.tensor([g_ms], dtype=torch.float64, device=dev)
+        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+        g_ms = float(t.item()) / g_steps
+        del recv
+        gather = {"value": units * world / (g_ms / 1e3), "ms_per_step": g_ms, "steps": g_steps,
+                  "gather_bytes_per_rank": int(yd.numel() * 4 * (world - 1)),
+                  "what": "each step's outputs all-gathered to every rank over NVLink (rg_session_allgather, NCCL) "
+                          "inside the timed region; compute-only `value` leaves them sharded"}
+
     # per-op CUDA-event durations (the roofline's kernel times) from profiled runs
     prof_runs = max(3, min(args.steps, 10))
     per_op_ns = np.zeros(nops)
@@ -485,17 +674,30 @@ def main():
         sess.run_device(xd, yd)
         per_op_ns += np.array([r.duration_ns for r in sess.last_npu_profile().records], dtype=np.float64)
     per_op_ns *= args.steps / prof_runs
-    total_ms = float(sum(a.elapsed_time(b) for a, b in evs))
-    if world > 1:
-        t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
-        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
-        total_ms = float(t.item())
-    ms_per_step = total_ms / args.steps
     macs_sess = sess if not f32 else InferenceSession.from_module(model, ExecutionProvider.npu_int8(), device=local)
-    macs_unit = program_macs(macs_sess, x.shape) if not cfg.startswith("c3") else int(np.prod(WORKLOADS[cfg]["shape"][1:]))
+    macs_unit = program_macs(macs_sess, x.shape) if not c3 else int(np.prod(WORKLOADS[cfg]["shape"][1:]))
     units_all = units * world
     value = units_all / (ms_per_step / 1e3)
     tops = value * 2.0 * macs_unit / 1e12
+
+    peaks = measured_peaks()
+    clk = clocks.summary()
+    fp32_peak = fp32_fma_peak(torch.cuda.get_device_properties(dev).multi_processor_count,
+                              clk.get("sm_mhz") or 1965.0) if (fp16 or f32) else None
+    traffic, traffic_src = (None, "not captured for this arm") if (fp16 or f32) else measured_traffic(cfg, units)
+    if f32:
+        roofline = {"kernel": "whole program (the f32 provider records no per-op times)", "bound": "fp32",
+                    "achieved": tops, "peak": fp32_peak, "unit": "TFLOP/s", "frac": tops / fp32_peak,
+                    "mean_launch_us": ms_per_step * 1e3, "traffic": None,
+                    "peak_source": "FP32 FMA peak: SMs x 128 FMA/clk x 2 at the sampled SM clock "
+                                   "(no FP32 figure in MEASURED_PEAKS.json)"}
+    elif c3 and not fp16:
+        roofline = gemm_kernel_roofline(sess, xd, yd, stream, flush, peaks)
+        roofline["traffic"] = traffic
+        roofline["op_roofline"] = op_roofline(cfg, sess, per_op_ns, args.steps, x.shape, peaks)
+    else:
+        roofline = op_roofline(cfg, sess, per_op_ns, args.steps, x.shape, peaks, fp32_peak=fp32_peak, traffic=traffic)
+    roofline["traffic_source"] = traffic_src
 
     # end to end through the public host-buffer call, pinned host memory
     xh = torch.from_numpy(x).pin_memory().numpy()
@@ -513,33 +715,37 @@ def main():
         e2e_s = float(t.item())
     e2e_value = units_all * e2e_steps / e2e_s
 
-    peaks = measured_peaks()
-    clk = clocks.summary()
-    fp32_peak = fp32_fma_peak(torch.cuda.get_device_properties(dev).multi_processor_count,
-                              clk.get("sm_mhz") or 1965.0) if (fp16 or f32) else None
+    sharded = None
+    if world > 1:
+        per_rank = min(units, {"c4": 2, "c5": 1}.get(cfg, 64))
+        ok, n_global = sharded_parity(sess, model, prov, x, args.weight_quant, rank, world, dev, tdist, per_rank)
+        sharded = {"sharded_bit_exact": ok, "global_batch": n_global,
+                   "how": "the batch sharded over the ranks through the library's NCCL path (per-Linear max "
+                          "all-reduce), outputs all-gathered by rg_session_allgather, compared bit for bit with "
+                          "one device running the whole batch"}
+
+    unit = "samples/s (GEMM rows)" if c3 else "samples/s"
     line = {
-        "metric": METRIC_FP16 if fp16 else METRIC_F32 if f32 else METRIC, "value": value, "unit": "samples/s" if not cfg.startswith("c3") else "samples/s (GEMM rows)",
+        "metric": METRIC_FP16 if fp16 else METRIC_F32 if f32 else METRIC, "value": value, "unit": unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "fp16 (round_fp16 operands, f32 FMA sums)" if fp16 else "f32" if f32 else "int8",
         "data": "synthetic (reference generator, manual_seed(42))",
-        "config": {"workload": WORKLOADS[cfg]["name"], "global_batch": units_all, "per_gpu_batch": units,
-                   "parallelism": f"dp{world}", "l2": "flushed before every timed step (256 MiB write)"},
+        "config": workload_config(cfg, units, world, args.weight_quant),
         "tops": tops, "tops_frac_of_nominal_int8": None if (fp16 or f32) else tops / NOMINAL_INT8_TOPS,
         "int8_macs_per_unit": macs_unit,
-        "roofline": (op_roofline(cfg, sess, per_op_ns, args.steps, x.shape, peaks, fp32_peak=fp32_peak,
-                                 traffic=None if (fp16 or f32) else MEASURED_TRAFFIC.get((cfg, units))) if not f32
-                     else {"kernel": "whole program (the f32 provider records no per-op times)", "bound": "fp32",
-                           "achieved": tops, "peak": fp32_peak, "unit": "TFLOP/s", "frac": tops / fp32_peak,
-                           "mean_launch_us": ms_per_step * 1e3, "traffic": None,
-                           "peak_source": "FP32 FMA peak: SMs x 128 FMA/clk x 2 at the sampled SM clock "
-                                          "(no FP32 figure in MEASURED_PEAKS.json)"}),
-        "e2e": {"value": e2e_value, "unit": "samples/s" if not cfg.startswith("c3") else "samples/s (GEMM rows)",
+        "roofline": roofline,
+        "e2e": {"value": e2e_value, "unit": unit,
                 "h2d_bytes_per_step": int(xh.nbytes), "d2h_bytes_per_step": int(yh.nbytes),
                 "api": "InferenceSession.run (rg_session_run), pinned host buffers", "steps": e2e_steps},
         "gpu_launches": launches,
         "clocks": clk,
     }
+    if gather is not None:
+        line["gather_inclusive"] = gather
+    if sharded is not None:
+        line["sharded_bit_exact"] = sharded["sharded_bit_exact"]
+        line["sharded_check"] = sharded
     if fp16:
         line["config"]["precision"] = "Npu(Fp16)"
     if f32:
@@ -548,7 +754,7 @@ def main():
         line["roofline_int8_projections"] = line["roofline"]
         line["roofline"] = attention_roofline(x.shape, dev, line["clocks"])
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(cfg, model, x, precision=1 if fp16 else 2 if f32 else 0)
+        line["cpu_baseline"] = cpu_baseline(cfg, model, x, units, precision=1 if fp16 else 2 if f32 else 0)
     if rank == 0:
         print(json.dumps(line), flush=True)
     del sess

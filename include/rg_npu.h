@@ -219,7 +219,9 @@ rg_status rg_nccl_unique_id(uint8_t id[128]);
 rg_status rg_session_attach_comm(rg_session* s, const uint8_t id[128], int32_t rank,
                                  int32_t world);
 /* All-gather of equal-sized f32 shards (device buffers) over the session's
- * communicator: recv holds world * count elements in rank order. */
+ * communicator: recv holds world * count elements in rank order.  With a NULL
+ * stream it runs on the session's stream and returns when done; on a caller's
+ * stream it is enqueued there and returns at once (every rank must enqueue it). */
 rg_status rg_session_allgather(rg_session* s, const float* send_dev, float* recv_dev,
                                int64_t count, void* stream);
 

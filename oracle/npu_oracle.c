@@ -180,6 +180,7 @@ typedef struct {
   const int8_t* a; const int8_t* w; const float* bias; float cs;
   int64_t k, n; int32_t act; float param; float* out; int32_t* acc;
   int64_t row0;  /* row offset of out/acc relative to a */
+  const float* wsc; float sa;  /* per-channel weights: column j's scale is sa * wsc[j] */
 } og_gemm_ctx;
 
 static void og_gemm_rows(void* p, int64_t b, int64_t e) {
@@ -190,7 +191,8 @@ static void og_gemm_rows(void* p, int64_t b, int64_t e) {
     for (int64_t j = 0; j < c->n; ++j) {
       int32_t acc = og_dot_i8(arow, c->w + j * c->k, c->k);
       if (c->acc) c->acc[(r - c->row0) * c->n + j] = acc;
-      float v = (float)acc * c->cs;       /* (acc as f32) * combined_scale */
+      const float cs = c->wsc ? c->sa * c->wsc[j] : c->cs;
+      float v = (float)acc * cs;          /* (acc as f32) * combined_scale */
       v = v + c->bias[j];                 /* + bias[c] */
       orow[j] = og_act_apply(c->act, c->param, v);
     }
@@ -537,7 +539,19 @@ static void og_make_linear(og_program* p, og_op* op, const float* w_in_out, int3
   p->npu_bytes += (wl + 4) + (b ? out : 0) * 4;
 }
 
+/* Per-output-channel weight quantization (extension): each of the `rows` rows of the
+ * [rows, cols] matrix gets its own QuantTensor::from_f32 scale (quantize.rs:18-24). */
+static void og_quantize_rows_per_channel(og_op* op, const float* w, int64_t rows, int64_t cols) {
+  op->w_scale = 0.0f;
+  op->w_scale_ch = (float*)malloc(sizeof(float) * (size_t)(rows > 0 ? rows : 1));
+  for (int64_t r = 0; r < rows; ++r) op->w_scale_ch[r] = og_quantize_into(w + r * cols, cols, op->wq + r * cols);
+}
+
 og_program* og_compile(const og_layer* layers, int32_t n_layers, int32_t precision) {
+  return og_compile_ex(layers, n_layers, precision, 0);
+}
+
+og_program* og_compile_ex(const og_layer* layers, int32_t n_layers, int32_t precision, int32_t weight_quant) {
   int32_t m = 0;
   og_flayer* f = og_fold(layers, n_layers, &m);
   og_program* p = (og_program*)calloc(1, sizeof(og_program));
@@ -562,20 +576,23 @@ og_program* og_compile(const og_layer* layers, int32_t n_layers, int32_t precisi
         op->in_features = l->in_f; op->out_features = l->out_f;
         float* wt = (float*)malloc(sizeof(float) * (size_t)(wl > 0 ? wl : 1));
         og_transpose2d(l->w, l->in_f, l->out_f, wt);       /* npu.rs:208: [in,out] -> [out,in] */
-        op->w_scale = og_quantize_into(wt, wl, op->wq);    /* npu.rs:209: per-tensor */
+        if (weight_quant) og_quantize_rows_per_channel(op, wt, l->out_f, l->in_f);
+        else op->w_scale = og_quantize_into(wt, wl, op->wq);  /* npu.rs:209: per-tensor */
         op->wh = wt; op->wh_len = wl;                      /* npu.rs:210: round_fp16 of w_t */
         for (int64_t j = 0; j < wl; ++j) op->wh[j] = og_round_fp16(op->wh[j]);
       } else {
         op->in_channels = l->in_c; op->out_channels = l->out_c; op->kernel = l->k;
         op->stride = l->stride; op->padding = l->pad;
-        op->w_scale = og_quantize_into(l->w, wl, op->wq);  /* npu.rs:231: [O, C*k*k] per-tensor */
+        if (weight_quant) og_quantize_rows_per_channel(op, l->w, l->out_c, wl / (l->out_c > 0 ? l->out_c : 1));
+        else op->w_scale = og_quantize_into(l->w, wl, op->wq);  /* npu.rs:231: [O, C*k*k] per-tensor */
         op->wh = (float*)malloc(sizeof(float) * (size_t)(wl > 0 ? wl : 1)); op->wh_len = wl;
         for (int64_t j = 0; j < wl; ++j) op->wh[j] = og_round_fp16(l->w[j]);  /* npu.rs:232 */
       }
       op->bias = (float*)malloc(sizeof(float) * (size_t)(l->b_len > 0 ? l->b_len : 1));
       memcpy(op->bias, l->b, sizeof(float) * (size_t)l->b_len); op->bias_len = l->b_len;
       p->fp32_bytes += (l->w_len + l->b_len) * 4;
-      p->npu_bytes += precision == OG_PREC_INT8 ? (wl + 4) + l->b_len * 4 : l->w_len * 2 + l->b_len * 2;
+      const int64_t n_scales = weight_quant ? (l->kind == OG_LAYER_LINEAR ? l->out_f : l->out_c) : 1;
+      p->npu_bytes += precision == OG_PREC_INT8 ? (wl + 4 * n_scales) + l->b_len * 4 : l->w_len * 2 + l->b_len * 2;
       if (next_act) ++i;
     } else if (l->kind == OG_LAYER_CHANNEL_AFFINE) {
       /* standalone affine -> diagonal FusedLinear (npu.rs:254-270); no byte accounting */
@@ -584,7 +601,8 @@ og_program* og_compile(const og_layer* layers, int32_t n_layers, int32_t precisi
       for (int64_t j = 0; j < c; ++j) w[j * c + j] = l->w[j];
       op->kind = OG_LAYER_LINEAR; op->in_features = (int32_t)c; op->out_features = (int32_t)c;
       op->wq = (int8_t*)malloc((size_t)(c * c > 0 ? c * c : 1)); op->wq_len = c * c;
-      op->w_scale = og_quantize_into(w, c * c, op->wq);
+      if (weight_quant) og_quantize_rows_per_channel(op, w, c, c);
+      else op->w_scale = og_quantize_into(w, c * c, op->wq);
       op->wh = w; op->wh_len = c * c;                    /* npu.rs:266: the unrounded diagonal */
       op->bias = (float*)malloc(sizeof(float) * (size_t)(c > 0 ? c : 1));
       memcpy(op->bias, l->b, sizeof(float) * (size_t)c); op->bias_len = c;
@@ -626,7 +644,7 @@ void og_program_free(og_program* p) {
   for (int32_t i = 0; i < p->n_ops; ++i) {
     for (int32_t j = 0; j < p->ops[i].n_sub; ++j) { free(p->ops[i].sub[j].wq); free(p->ops[i].sub[j].bias); }
     free(p->ops[i].sub); free(p->ops[i].extra); free(p->ops[i].wh);
-    free(p->ops[i].wq); free(p->ops[i].bias);
+    free(p->ops[i].wq); free(p->ops[i].bias); free(p->ops[i].w_scale_ch);
   }
   free(p->ops); free(p);
 }
@@ -710,7 +728,8 @@ void og_op_linear(const og_op* op, const float* x, int64_t rows, float* y,
   int8_t* q = aq ? aq : (int8_t*)malloc((size_t)(rows * k > 0 ? rows * k : 1));
   float sa = og_quantize_into(x, rows * k, q);            /* QuantTensor::from_f32 (serial) */
   if (a_scale) *a_scale = sa;
-  og_gemm_ctx c = { q, op->wq, op->bias, sa * op->w_scale, k, n, op->act, op->act_param, y, acc, 0 };
+  og_gemm_ctx c = { q, op->wq, op->bias, sa * op->w_scale, k, n, op->act, op->act_param, y, acc, 0,
+                    op->w_scale_ch, sa };
   int32_t par = rows * k * n >= 32 * 1024;                /* quantize.rs:104 */
   og_parallel_for(rows, par ? nthreads : 1, og_gemm_rows, &c);
   if (!aq) free(q);
@@ -725,7 +744,8 @@ void og_op_linear_with_amax(const og_op* op, const float* x, int64_t rows, float
   float inv = 1.0f / sa;
   int8_t* q = (int8_t*)malloc((size_t)(rows * k > 0 ? rows * k : 1));
   for (int64_t i = 0; i < rows * k; ++i) q[i] = og_q1(x[i], inv);
-  og_gemm_ctx c = { q, op->wq, op->bias, sa * op->w_scale, k, n, op->act, op->act_param, y, NULL, 0 };
+  og_gemm_ctx c = { q, op->wq, op->bias, sa * op->w_scale, k, n, op->act, op->act_param, y, NULL, 0,
+                    op->w_scale_ch, sa };
   og_parallel_for(rows, rows * k * n >= 32 * 1024 ? nthreads : 1, og_gemm_rows, &c);
   free(q);
 }
@@ -739,7 +759,8 @@ void og_op_linear_rows(const og_op* op, const float* x, int64_t rows, int64_t r0
   int8_t* q = (int8_t*)malloc((size_t)(sub * k > 0 ? sub * k : 1));
   for (int64_t i = 0; i < sub * k; ++i) q[i] = og_q1(x[r0 * k + i], inv);
   if (a_scale) *a_scale = sa;
-  og_gemm_ctx c = { q, op->wq, op->bias, sa * op->w_scale, k, n, op->act, op->act_param, y, acc, 0 };
+  og_gemm_ctx c = { q, op->wq, op->bias, sa * op->w_scale, k, n, op->act, op->act_param, y, acc, 0,
+                    op->w_scale_ch, sa };
   og_parallel_for(sub, nthreads, og_gemm_rows, &c);
   free(q);
 }
@@ -774,7 +795,8 @@ static void og_conv_images(void* p, int64_t b, int64_t e) { /* npu.rs:331-359 pe
     float sa = og_quantize_into(cols_t, ckk * l, q);     /* per-image scale */
     if (c->a_scales) c->a_scales[im] = sa;
     if (c->aq) { float inv = 1.0f / sa; for (int64_t i = 0; i < img_stride; ++i) c->aq[im * img_stride + i] = og_q1(img[i], inv); }
-    og_gemm_ctx g = { q, op->wq, op->bias, sa * op->w_scale, ckk, O, op->act, op->act_param, ylo, alo, 0 };
+    og_gemm_ctx g = { q, op->wq, op->bias, sa * op->w_scale, ckk, O, op->act, op->act_param, ylo, alo, 0,
+                      op->w_scale_ch, sa };
     og_gemm_rows(&g, 0, l);                              /* int8_gemm_fused_serial */
     og_transpose2d(ylo, l, O, c->y + im * O * l);        /* [L,O] -> [O,L] */
     if (alo)

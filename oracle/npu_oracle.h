@@ -75,6 +75,10 @@ typedef struct og_op {
   /* FP16 arm (npu.rs:207-210, 231-232, 258-268): the weights in the reference layout
    * rounded by round_fp16 (a standalone ChannelAffine keeps its unrounded diagonal) */
   float* wh; int64_t wh_len;
+  /* per-output-channel weight scales (NULL: per-tensor, the reference's only mode;
+   * the extension quantizes each row of the [out, in] / [O, C*k*k] matrix with
+   * QuantTensor::from_f32's arithmetic, quantize.rs:18-24) */
+  float* w_scale_ch;
 } og_op;
 
 typedef struct {
@@ -89,6 +93,10 @@ float og_quantize_into(const float* v, int64_t n, int8_t* out); /* quantize.rs:2
 float og_round_fp16(float x);                               /* quantize.rs:50-64 */
 
 og_program* og_compile(const og_layer* layers, int32_t n_layers, int32_t precision); /* npu.rs:188-276 */
+/* og_compile with the weight-quantization mode: 0 per-tensor (the reference), 1 per
+ * output channel (extension; byte accounting 4 B per scale, as quantize.rs:43-45). */
+og_program* og_compile_ex(const og_layer* layers, int32_t n_layers, int32_t precision,
+                          int32_t weight_quant);
 /* The f32 ExecutionProvider::Cpu arm: fold_batch_norm then run_standard (mod.rs:162-166,
  * 260-331) over the reference's layer kinds 1-7.  Returns 0, -1 (bad input rank), -2
  * (shape mismatch), -3 (output capacity) or -5 (a layer kind outside 1-7). */

@@ -60,6 +60,7 @@ _Op._fields_ = [
     ("sub", C.POINTER(_Op)), ("n_sub", C.c_int32), ("_pad2", C.c_int32),
     ("extra", C.POINTER(C.c_float)), ("extra_len", C.c_int64),
     ("wh", C.POINTER(C.c_float)), ("wh_len", C.c_int64),
+    ("w_scale_ch", C.POINTER(C.c_float)),
 ]
 
 
@@ -110,6 +111,8 @@ def lib():
         L.og_round_fp16.restype = C.c_float
         L.og_compile.argtypes = [C.POINTER(_Layer), C.c_int32, C.c_int32]
         L.og_compile.restype = C.POINTER(_Program)
+        L.og_compile_ex.argtypes = [C.POINTER(_Layer), C.c_int32, C.c_int32, C.c_int32]
+        L.og_compile_ex.restype = C.POINTER(_Program)
         L.og_program_free.argtypes = [C.POINTER(_Program)]
         L.og_op_label.argtypes = [C.POINTER(_Op), C.c_char_p, C.c_int32]
         L.og_op_label.restype = C.c_int32
@@ -248,12 +251,16 @@ class Op:
     def __init__(self, raw: _Op):
         self.raw = raw
         for f, _ in _Op._fields_:
-            if f not in ("wq", "bias", "sub", "extra", "wh"):
+            if f not in ("wq", "bias", "sub", "extra", "wh", "w_scale_ch"):
                 setattr(self, f, getattr(raw, f))
         self.sub = [Op(raw.sub[j]) for j in range(raw.n_sub)]
         self.wq = np.ctypeslib.as_array(raw.wq, shape=(raw.wq_len,)).copy() if raw.wq_len else None
         self.bias = np.ctypeslib.as_array(raw.bias, shape=(raw.bias_len,)).copy() if raw.bias_len else None
         self.wh = np.ctypeslib.as_array(raw.wh, shape=(raw.wh_len,)).copy() if raw.wh_len else None
+        # per-output-channel weight scales (weight_quant=1), else None
+        nsc = raw.out_features if raw.kind == LINEAR else raw.out_channels
+        self.w_scale_ch = (np.ctypeslib.as_array(raw.w_scale_ch, shape=(nsc,)).copy()
+                           if bool(raw.w_scale_ch) and nsc > 0 else None)
 
     def label(self) -> str:
         buf = C.create_string_buffer(256)
@@ -264,9 +271,11 @@ class Op:
 class Program:
     """``npu::compile`` output (npu.rs:188-276) plus per-op executors."""
 
-    def __init__(self, specs, precision: int = 0):
+    def __init__(self, specs, precision: int = 0, weight_quant: int = 0):
+        """weight_quant 0: per-tensor weights (the reference, quantize.rs:18-24);
+        1: per output channel (extension, BASELINE's "symmetric per-channel")."""
         arr, keep = _to_layers(list(specs))
-        self._p = lib().og_compile(arr, len(specs), precision)
+        self._p = lib().og_compile_ex(arr, len(specs), precision, weight_quant)
         P = self._p.contents
         self.precision = P.precision
         self.original_layers = P.original_layers
@@ -586,6 +595,18 @@ def linear_rows(op: Op, prog: Program, op_index: int, x, r0: int, r1: int, nthre
     lib().og_op_linear_rows(C.byref(prog._p.contents.ops[op_index]), _p(x, C.c_float), rows, r0, r1,
                             _p(y, C.c_float), C.byref(sa), _p(acc, C.c_int32), nthreads)
     return y, acc, np.float32(sa.value)
+
+
+def linear_given_amax(prog: Program, op_index: int, x, amax: float, nthreads: int = 1):
+    """FusedLinear (npu.rs:307-318) on the rows of x, quantized with the scale of the
+    given absmax instead of x's own: the absmax of a larger tensor these rows were
+    sampled from (or of every shard of a sharded batch)."""
+    x = _f32(x)
+    op = prog._p.contents.ops[op_index]
+    rows = x.size // op.in_features
+    y = np.empty((rows, op.out_features), np.float32)
+    lib().og_op_linear_with_amax(C.byref(op), _p(x, C.c_float), rows, C.c_float(amax), _p(y, C.c_float), nthreads)
+    return y
 
 
 def run_standard(specs, x):

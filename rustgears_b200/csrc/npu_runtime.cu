@@ -552,7 +552,9 @@ static rg_status compile(Session& s, const rg_layer_spec* layers, int32_t n) {
       op.kpad = round_up(op.kdim, 16);
       op.bias = l.b;
       s.fp32_bytes += (int64_t)(l.w.size() + l.b.size()) * 4;
-      s.npu_bytes += s.precision == RG_PREC_INT8 ? ((int64_t)op.wq.size() + 4) + (int64_t)l.b.size() * 4
+      // 4 bytes per weight scale (quantize.rs:43-45): one per tensor, or one per output channel
+      const int64_t n_scales = op.w_scale_ch.empty() ? 1 : (int64_t)op.w_scale_ch.size();
+      s.npu_bytes += s.precision == RG_PREC_INT8 ? ((int64_t)op.wq.size() + 4 * n_scales) + (int64_t)l.b.size() * 4
                                                  : (int64_t)l.w.size() * 2 + (int64_t)l.b.size() * 2;
       if (next_act) ++i;
     } else if (l.kind == RG_LAYER_CHANNEL_AFFINE && f32) {
@@ -1717,14 +1719,15 @@ void rg_session_destroy(rg_session* h) {
   cudaSetDevice(s.device);
   if (s.stream) cudaStreamSynchronize(s.stream);
   if (s.copy_stream) cudaStreamSynchronize(s.copy_stream);
+  // a captured program holds the communicator's all-reduce nodes: release it first
+  if (s.graph.exec) cudaGraphExecDestroy(s.graph.exec);
+  s.graph.exec = nullptr;
   if (s.comm) ncclCommDestroy(s.comm);
   for (cudaEvent_t e : s.events) cudaEventDestroy(e);
   for (cudaEvent_t e : s.chunk_events)
     if (e) cudaEventDestroy(e);
   if (s.t0) cudaEventDestroy(s.t0);
   if (s.t1) cudaEventDestroy(s.t1);
-  if (s.graph.exec) cudaGraphExecDestroy(s.graph.exec);
-  s.graph.exec = nullptr;
   if (s.stream) cudaStreamDestroy(s.stream);
   if (s.copy_stream) cudaStreamDestroy(s.copy_stream);
   delete h;
@@ -1866,7 +1869,9 @@ static rg_status run_impl(rg_session* h, const float* x, bool x_host, const int6
   if (s.ops.empty()) {
     if (in_elems) RG_CUDA_TRY(cudaMemcpyAsync(yd, xd, (size_t)in_elems * 4, cudaMemcpyDeviceToDevice, st));
     done = true;
-  } else if (!x_host && !y_host && !s.trace && s.world == 1 && !(s.flags & RG_SESSION_NO_GRAPH)) {
+  } else if (!x_host && !y_host && !s.trace && !(s.flags & RG_SESSION_NO_GRAPH)) {
+    // (with a communicator the capture holds the per-Linear max all-reduces too, so a
+    // sharded step is one graph launch and host-side skew between ranks stays off it)
     std::shared_ptr<RunPlan> Pg;
     rs = run_graph(s, xd, shape, ndim, yd, st, events, Pg, done);
     if (rs == RG_OK && done && Pg) Pp = Pg;
@@ -2053,6 +2058,10 @@ rg_status rg_session_attach_comm(rg_session* h, const uint8_t id[128], int32_t r
   Session& s = h->s;
   std::lock_guard<std::mutex> lock(s.mu);
   RG_CUDA_TRY(cudaSetDevice(s.device));
+  // a program captured with the previous communicator (or none) is stale
+  RG_CUDA_TRY(cudaStreamSynchronize(s.stream));
+  if (s.graph.exec) cudaGraphExecDestroy(s.graph.exec);
+  s.graph = Session::Graph();
   if (s.comm) {
     ncclCommDestroy(s.comm);
     s.comm = nullptr;
@@ -2072,7 +2081,7 @@ rg_status rg_session_allgather(rg_session* h, const float* send_dev, float* recv
   RG_CUDA_TRY(cudaSetDevice(s.device));
   cudaStream_t st = stream ? (cudaStream_t)stream : s.stream;
   RG_NCCL_TRY(ncclAllGather(send_dev, recv_dev, (size_t)count, ncclFloat32, s.comm, st));
-  RG_CUDA_TRY(cudaStreamSynchronize(st));
+  if (!stream) RG_CUDA_TRY(cudaStreamSynchronize(st));  // on a caller's stream it stays enqueued
   return RG_OK;
 }
 
