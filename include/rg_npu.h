@@ -239,14 +239,22 @@ rg_status rg_quantize_f32_i8(const float* x, int64_t rows, int64_t k, int64_t ld
  * ("B transposed"), ld a multiple of 16 with zero padding beyond k;
  * out[r,c] = act(f32(sum_k a*w) * (a_scale*w_scale) + bias[c]).  acc (i32
  * [m,n]) and out_amax (max |out|, accumulated with max into *out_amax) are
- * optional (NULL). */
+ * optional (NULL).
+ * Shapes that run on the tensor cores (m*n*k >= 2^22, n >= 16, k >= 32) use a
+ * kernel whose pipeline waits are bounded: the call waits for it on `stream`
+ * and returns RG_ERR_TIMEOUT if a wait gave up (its output is then invalid).
+ * The word that reports it belongs to this call alone (a slot of a static
+ * device array held for the call).  Inside a stream capture the call is
+ * recorded without that check.  Other shapes run on the CUDA cores, have no
+ * waits, and the call returns once they are enqueued. */
 rg_status rg_gemm_i8_fused(const int8_t* a, const int8_t* w, int64_t m, int64_t n, int64_t ld,
                            const float* a_scale, float w_scale, const float* bias, int32_t act,
                            float act_param, float* out, int32_t* acc, float* out_amax,
                            void* stream);
 /* One FusedLinear op (npu.rs:307-318): absmax + quantize of x [m,k] f32 and
  * the fused GEMM against w [n,ld] i8.  `workspace` must hold
- * rg_linear_i8_workspace_size(m, ld) bytes of device memory. */
+ * rg_linear_i8_workspace_size(m, ld) bytes of device memory.  Timeouts are
+ * reported as by rg_gemm_i8_fused. */
 int64_t rg_linear_i8_workspace_size(int64_t m, int64_t ld);
 rg_status rg_linear_i8(const float* x, int64_t m, int64_t k, const int8_t* w, int64_t n,
                        int64_t ld, float w_scale, const float* bias, int32_t act,
@@ -259,11 +267,27 @@ rg_status rg_linear_i8(const float* x, int64_t m, int64_t k, const int8_t* w, in
  * m * ld <= 16 MiB; larger calls fail with RG_ERR_INVALID_ARG), held by every
  * GPU that loads the library until exit.  All calls on a device share it:
  * calls that overlap on the GPU race.  The first call on a device looks up
- * the scratch address and should come before any stream capture. */
+ * the scratch address and should come before any stream capture; the address
+ * is kept for the life of the process, so a process that resets a device
+ * (cudaDeviceReset) must not call this entry point on it afterwards.
+ * Timeouts are reported as by rg_gemm_i8_fused. */
 #define RG_LINEAR_NOALLOC_MAX_BYTES (16u << 20)
 rg_status rg_linear_i8_noalloc(const float* x, int64_t m, int64_t k, const int8_t* w, int64_t n,
                                int64_t ld, float w_scale, const float* bias, int32_t act,
                                float act_param, float* out, void* stream);
+/* The status a run reports for its device error words (no counterpart in the
+ * reference): words[0] set -> RG_ERR_TIMEOUT (a tensor-core kernel gave up on a
+ * bounded wait), words[1] set -> RG_ERR_INVALID_ARG (an embedding id not below
+ * the vocabulary size), else RG_OK.  Host-only; every run and kernel-level call
+ * maps its words through it. */
+rg_status rg_status_from_error_words(const int32_t words[2]);
+/* Test hook of the bounded-wait failure path (no counterpart in the reference):
+ * tcgen05 GEMM launches that follow bound every pipeline wait by wait_ns
+ * (0 restores the 2 s default), and with starve_loads != 0 issue no operand
+ * loads, so the first wait on them runs out and the call reports
+ * RG_ERR_TIMEOUT.  Launch parameters are fixed when a session captures its
+ * CUDA graph: test on host-buffer runs or RG_SESSION_NO_GRAPH sessions. */
+void rg_debug_set_tc_wait(uint64_t wait_ns, int32_t starve_loads);
 /* max_pool2d (src/kernels.rs:165-213), NCHW f32, no padding. */
 rg_status rg_maxpool2d_f32(const float* x, int64_t n, int32_t c, int32_t h, int32_t w,
                            int32_t k, int32_t stride, float* y, void* stream);

@@ -100,6 +100,8 @@ SIGNATURES = {
     "rg_linear_i8_workspace_size": ([_i64, _i64], _i64),
     "rg_linear_i8": ([_vp, _i64, _i64, _vp, _i64, _i64, _f32, _vp, _i32, _f32, _vp, _vp, _vp], _i32),
     "rg_linear_i8_noalloc": ([_vp, _i64, _i64, _vp, _i64, _i64, _f32, _vp, _i32, _f32, _vp, _vp], _i32),
+    "rg_status_from_error_words": ([_i32p], _i32),
+    "rg_debug_set_tc_wait": ([_u64, _i32], None),
     "rg_maxpool2d_f32": ([_vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _vp], _i32),
     "rg_softmax_f32": ([_vp, _i64, _i64, _vp, _vp], _i32),
     "rg_attention_f32": ([_vp, _i64, _i64, _i32, _i32, _i32, _vp, _i64, _vp], _i32),

@@ -88,9 +88,8 @@ struct C3Params {
   int64_t amax_per_slot;           // 0: one slot; else n * h * w (per image)
   unsigned* amax2;                 // optional per-image absmax over the pixels a later
   int32_t cov_s, cov_oh, cov_ow;   // 1x1 / pad 0 / stride cov_s conv reads
+  int* err;                        // this call's error word: set to 1 when a bounded wait gave up
 };
-
-__device__ int g_c3_error;
 
 __device__ __forceinline__ uint64_t desc_rows16(uint32_t saddr, uint32_t lbo) {
   // no-swizzle K-major: rows 16 bytes apart (8-row groups 128 B apart), K chunks `lbo` apart
@@ -433,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0 && *abort) atomicExch(&g_c3_error, 1);
+  if (threadIdx.x == 0 && *abort) atomicExch(p.err, 1);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
@@ -521,6 +520,7 @@ bool launch_bn(const GemmArgs& a, int mode, int32_t H, int32_t W, int32_t cpad, 
   p.residual = a.residual; p.res_act = a.res_act; p.res_param = a.res_param;
   p.amax = a.amax.ptr; p.amax_per_slot = a.amax.elems_per_slot;
   p.amax2 = a.amax2; p.cov_s = a.cov_s > 0 ? a.cov_s : 1; p.cov_oh = a.cov_oh; p.cov_ow = a.cov_ow;
+  p.err = a.err;
   const int64_t tiles = (int64_t)p.n_img * p.tiles_m * p.tiles_n;
   const int grid = tiles < num_sms ? (int)tiles : num_sms;
   k_conv3x3<BN, ACT, TAPS><<<grid, kThreads, smem, st>>>(mi, p);
@@ -629,6 +629,7 @@ size_t conv3x3_weight_bytes(int32_t n, int32_t cpad) { return dconv_weight_bytes
 
 bool launch_dconv(const GemmArgs& a, int mode, int32_t h, int32_t w, int32_t cpad, const int8_t* wd, int num_sms,
                   cudaStream_t st) {
+  if (!a.err) return false;
   const bool b128 = conv3x3_bn((int32_t)a.n) == 128;
   switch (mode) {
     case DCONV_3X3:
@@ -648,11 +649,5 @@ bool launch_conv3x3(const GemmArgs& a, const int8_t* wd, int num_sms, cudaStream
   return launch_dconv(a, DCONV_3X3, a.g.h, a.g.w, a.g.cpad, wd, num_sms, st);
 }
 
-int conv3x3_take_error() {
-  int h = 0, z = 0;
-  if (cudaMemcpyFromSymbol(&h, g_c3_error, sizeof h) != cudaSuccess) return -1;
-  if (h) cudaMemcpyToSymbol(g_c3_error, &z, sizeof z);
-  return h;
-}
 
 }  // namespace rg

@@ -81,9 +81,8 @@ struct ConvTcParams {
   unsigned* amax;           // optional absmax sink
   int64_t amax_per_slot;    // 0: one slot; else elements per slot (n * oh * ow: per image)
   int32_t tiles_m, tiles_n;
+  int* err;                 // this call's error word: set to 1 when a bounded wait gave up
 };
-
-__device__ int g_conv_error;
 
 __device__ __forceinline__ uint64_t desc_noswz(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   uint64_t d = 0;
@@ -351,7 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0 && *abort) atomicExch(&g_conv_error, 1);
+  if (threadIdx.x == 0 && *abort) atomicExch(p.err, 1);
   if (warp == kWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
@@ -392,6 +391,7 @@ bool launch_bn(const GemmArgs& a, int num_sms, cudaStream_t st) {
   p.amax = a.amax.ptr; p.amax_per_slot = a.amax.elems_per_slot;
   p.tiles_m = (int)((a.m + BM - 1) / BM);
   p.tiles_n = (int)((a.n + BN - 1) / BN);
+  p.err = a.err;
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < num_sms ? tiles : num_sms;
   k_conv_tc<BN, ACT, NARROW><<<grid, kThreads, C::kSmem, st>>>(mw, p);
@@ -431,17 +431,12 @@ bool conv_tc_eligible(const GemmArgs& a) {
 }
 
 bool launch_conv_tc(const GemmArgs& a, int num_sms, cudaStream_t st) {
+  if (!a.err) return false;
   if (a.g.cpad == 4) return launch_act<64, true>(a, num_sms, st);
   if (a.n >= 256) return launch_act<256>(a, num_sms, st);
   if (a.n >= 128) return launch_act<128>(a, num_sms, st);
   return launch_act<64>(a, num_sms, st);
 }
 
-int conv_tc_take_error() {
-  int h = 0, z = 0;
-  if (cudaMemcpyFromSymbol(&h, g_conv_error, sizeof h) != cudaSuccess) return -1;
-  if (h) cudaMemcpyToSymbol(g_conv_error, &z, sizeof z);
-  return h;
-}
 
 }  // namespace rg

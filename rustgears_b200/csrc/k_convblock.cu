@@ -58,8 +58,6 @@ namespace {
 
 using namespace sm100;
 
-__device__ int g_cb_error;  // set when a bounded wait gave up (read by the host)
-
 constexpr int H = 28, W = 28, C1 = 16;
 constexpr int P1 = 14;                 // pooled conv1 map is 14 x 14 (16 x 16 padded)
 constexpr int P2 = 7;                  // pooled conv2 map is 7 x 7
@@ -135,6 +133,7 @@ struct CBParams {
   float* out;              // [n, C2, 7, 7]
   unsigned* amax;          // optional sink of the output's absmax
   int64_t amax_per_image;
+  int* err;                // this call's error word: set to 1 when a bounded wait gave up
 };
 
 __device__ __forceinline__ uint64_t desc_noswz(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -552,7 +551,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_convblock(const CBParams p) {
 
   tc_fence_before();
   __syncthreads();
-  if (tid == 0 && ms.abort) atomicExch(&g_cb_error, 1);
+  if (tid == 0 && ms.abort) atomicExch(p.err, 1);
   if (warp == kWarpMma1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
@@ -571,6 +570,7 @@ void launch_cfg(const ConvBlockArgs& a, int num_sms, cudaStream_t st) {
   p.x = a.x; p.n = a.n; p.w1 = a.w1; p.kpad1 = a.kpad1; p.w2 = a.w2; p.kpad2 = a.kpad2;
   p.w1_scale = a.w1_scale; p.w2_scale = a.w2_scale; p.b1 = a.b1; p.b2 = a.b2; p.p1 = a.p1; p.p2 = a.p2;
   p.out = a.out; p.amax = a.amax; p.amax_per_image = a.amax_per_image;
+  p.err = a.err;
   const int grid = (int)(a.n < num_sms ? a.n : num_sms);
   k_convblock<C2, ACT1, ACT2><<<grid, kThreads, L::SMEM, st>>>(p);
 }
@@ -598,15 +598,8 @@ bool convblock_supported(int c0, int c1, int c2, int h, int w, int act1, int act
   return (simple(act1) && simple(act2)) || (act1 == ACT_LEAKY_RELU && act2 == ACT_LEAKY_RELU);
 }
 
-int convblock_take_error() {
-  int h = 0, z = 0;
-  if (cudaMemcpyFromSymbol(&h, g_cb_error, sizeof h) != cudaSuccess) return -1;
-  if (h) cudaMemcpyToSymbol(g_cb_error, &z, sizeof z);
-  return h;
-}
-
 void launch_convblock(const ConvBlockArgs& a, int num_sms, cudaStream_t st) {
-  if (a.n <= 0) return;
+  if (a.n <= 0 || !a.err) return;
   if (a.c2 == 32) launch_c2<32>(a, num_sms, st);
   else launch_c2<16>(a, num_sms, st);
 }

@@ -37,6 +37,7 @@ constexpr int BM = 128;          // rows per tile (TMEM lanes)
 constexpr int BK = 128;          // K bytes per stage (one 128-byte swizzle row)
 constexpr int kEpiWarps = 16;   // 4 per SM sub-partition: the exact GELU epilogue is long
 constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr uint64_t kDefaultWaitNs = 2000000000ull;  // pipeline waits give up after 2 s
 
 template <int BN>
 struct Cfg {
@@ -65,9 +66,10 @@ struct TcParams {
   int32_t tiles_m, tiles_n;
   int32_t tma_store;        // out written through map_o (n % 4 == 0, 16-byte aligned base)
   int32_t vec_cols;         // bias / w_scale_ch 16-byte aligned and n % 4 == 0: vector loads
+  int* err;                 // this call's error word: set to 1 when a bounded wait gave up
+  uint64_t wait_ns;         // limit of every pipeline wait
+  int32_t starve;           // test hook: the producer issues no loads (the MMA's waits run out)
 };
-
-__device__ int g_tc_error;  // set when a bounded wait gave up (read by the host)
 
 // Grouped tile order: 16 M-tiles sweep all N-tiles so the W panel stays in L2.
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& mb, int& nb) {
@@ -138,9 +140,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         int mb, nb;
         tile_coords(tile, p.tiles_m, p.tiles_n, mb, nb);
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort)) { ok = false; break; }
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.wait_ns)) { ok = false; break; }
           uint8_t* sa = stage_base + stage * C::kStageBytes;
           uint8_t* sb = sa + C::kABytes;
+          if (p.starve) {  // nothing arrives on full[stage]: the MMA issuer's wait runs out
+            if (++stage == C::kStages) { stage = 0; phase ^= 1; }
+            continue;
+          }
           mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
           tma_load_2d(sa, &map_a, &full[stage], kb * BK, mb * BM);
           tma_load_2d(sb, &map_w, &full[stage], kb * BK, nb * BN);
@@ -165,11 +171,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++iter) {
         const int buf = iter & 1;
         const uint32_t aphase = (iter >> 1) & 1;
-        if (!mbar_wait(&tempty[buf], aphase ^ 1, abort)) break;
+        if (!mbar_wait(&tempty[buf], aphase ^ 1, abort, p.wait_ns)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort)) { ok = false; break; }
+          if (!mbar_wait(&full[stage], phase, abort, p.wait_ns)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_addr(stage_base + stage * C::kStageBytes);
           const uint32_t sb = sa + C::kABytes;
@@ -203,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int buf = iter & 1;
       const uint32_t aphase = (iter >> 1) & 1;
       // every lane waits; the vote keeps the warp converged for the warp-wide tcgen05.ld
-      const bool got = mbar_wait(&tfull[buf], aphase, abort);
+      const bool got = mbar_wait(&tfull[buf], aphase, abort, p.wait_ns);
       if (!__all_sync(0xffffffffu, got)) { *abort = 1; break; }
       tc_fence_after();
       const int64_t row0 = (int64_t)mb * BM + q * 32;
@@ -288,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0 && *abort) atomicExch(&g_tc_error, 1);
+  if (threadIdx.x == 0 && *abort) atomicExch(p.err, 1);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
@@ -354,6 +360,9 @@ bool launch_bn(const GemmArgs& a, int num_sms, cudaStream_t st) {
   p.tma_store = tma_store ? 1 : 0;
   p.vec_cols = (a.n & 3) == 0 &&
                ((reinterpret_cast<uintptr_t>(a.bias) | reinterpret_cast<uintptr_t>(a.w_scale_ch)) & 15) == 0;
+  p.err = a.err;
+  p.wait_ns = a.wait_ns ? a.wait_ns : kDefaultWaitNs;
+  p.starve = a.starve;
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < num_sms ? tiles : num_sms;
   k_gemm_tc<BN, ACT><<<grid, kThreads, C::kSmem, st>>>(ma, mw, mo, p);
@@ -387,14 +396,8 @@ bool gemm_tc_eligible(const GemmArgs& a) {
 }
 
 bool launch_gemm_tc(const GemmArgs& a, int num_sms, cudaStream_t st) {
+  if (!a.err) return false;
   return a.n >= 256 ? launch_act<256>(a, num_sms, st) : launch_act<128>(a, num_sms, st);
-}
-
-int gemm_tc_take_error() {
-  int h = 0, z = 0;
-  if (cudaMemcpyFromSymbol(&h, g_tc_error, sizeof h) != cudaSuccess) return -1;
-  if (h) cudaMemcpyToSymbol(g_tc_error, &z, sizeof z);
-  return h;
 }
 
 }  // namespace rg

@@ -90,9 +90,8 @@ struct StemParams {
   float* out;                      // NCHW [n_img, 64, ph, pw]
   unsigned* amax;                  // optional absmax sink of out
   int32_t amax_per_image;
+  int* err;                        // this call's error word: set to 1 when a bounded wait gave up
 };
-
-__device__ int g_stem_error;
 
 __device__ __forceinline__ uint64_t desc_rows16(uint32_t saddr, uint32_t lbo) {
   // no-swizzle K-major: rows 16 bytes apart (8-row groups 128 B apart), K chunks `lbo` apart
@@ -379,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0 && *abort) atomicExch(&g_stem_error, 1);
+  if (threadIdx.x == 0 && *abort) atomicExch(p.err, 1);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
@@ -418,6 +417,8 @@ bool launch_t(const StemPoolArgs& a, int num_sms, cudaStream_t st) {
   p.act_param = a.act_param; p.out = a.out;
   p.amax = a.amax.ptr;
   p.amax_per_image = a.amax.ptr && a.amax.elems_per_slot > 0;
+  p.err = a.err;
+  if (!p.err) return false;
   const int smem = 1024 + kRing * p.slot_bytes + kWBytes + kXchBytes + kStgBytes + kBarBytes;
   if (smem > 227 * 1024) return false;
   static std::once_flag once;
@@ -481,13 +482,6 @@ bool launch_stem_pool(const StemPoolArgs& a, int num_sms, cudaStream_t st) {
     case ACT_SILU: return launch_t<ACT_SILU>(a, num_sms, st);
     default: return false;
   }
-}
-
-int stem_take_error() {
-  int h = 0, z = 0;
-  if (cudaMemcpyFromSymbol(&h, g_stem_error, sizeof h) != cudaSuccess) return -1;
-  if (h) cudaMemcpyToSymbol(g_stem_error, &z, sizeof z);
-  return h;
 }
 
 }  // namespace rg

@@ -21,8 +21,6 @@
 
 namespace rg {
 
-__device__ int g_embed_error = 0;  // 1: a token id was >= V (the reference's assertion)
-
 namespace {
 
 constexpr int kThreads = 256;
@@ -52,7 +50,7 @@ __device__ __forceinline__ void block_max_to(float v, unsigned* dst) {
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads) k_embedding(const float* __restrict__ ids, int64_t n,
                                                         const float* __restrict__ table, int64_t v, int32_t d,
-                                                        float* __restrict__ y, unsigned* amax) {
+                                                        float* __restrict__ y, unsigned* amax, int* err) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (kThreads / 32);
   float m = 0.0f;
@@ -64,7 +62,7 @@ __global__ void __launch_bounds__(kThreads) k_embedding(const float* __restrict_
     else if (f >= 1.0f) idx = __float2ull_rz(f);
     float* yr = y + r * d;
     if (idx >= (unsigned long long)v) {
-      if (lane == 0) atomicExch(&g_embed_error, 1);
+      if (lane == 0) atomicExch(err, 1);  // the reference's assertion (layers.rs:438-446)
       for (int32_t c = lane; c < d; c += 32) yr[c] = 0.0f;
       continue;
     }
@@ -552,9 +550,9 @@ size_t attention64_smem(int32_t t) {
 }
 
 void launch_embedding(const float* ids, int64_t n, const float* table, int64_t v, int32_t d, float* y,
-                      AmaxSink amax, cudaStream_t st) {
+                      AmaxSink amax, int* err, cudaStream_t st) {
   if (n <= 0) return;
-  k_embedding<<<grid_for(n, kThreads / 32, 148 * 16), kThreads, 0, st>>>(ids, n, table, v, d, y, amax.ptr);
+  k_embedding<<<grid_for(n, kThreads / 32, 148 * 16), kThreads, 0, st>>>(ids, n, table, v, d, y, amax.ptr, err);
 }
 
 rg_status launch_rmsnorm(const float* x, int64_t rows, int32_t d, const float* w, float eps, float inv_d, float* y,
@@ -614,11 +612,5 @@ rg_status launch_attention(const float* qkv, int64_t ld, int64_t b, int32_t t, i
   return RG_OK;
 }
 
-int embedding_take_error() {
-  int v = 0, z = 0;
-  cudaMemcpyFromSymbol(&v, g_embed_error, sizeof(int));
-  if (v) cudaMemcpyToSymbol(g_embed_error, &z, sizeof(int));
-  return v;
-}
 
 }  // namespace rg

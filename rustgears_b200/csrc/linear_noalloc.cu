@@ -20,7 +20,12 @@
 //     streams, or two host threads without ordering) race on the scratch.
 //   * the first call on each device looks up the array's device address
 //     (cudaGetSymbolAddress, with that device current) and caches it; make that
-//     first call before any stream capture begins.
+//     first call before any stream capture begins.  The cached address lives as
+//     long as the process: after a cudaDeviceReset of a device it would be stale,
+//     so a process that resets a device must not call this entry point on it again;
+//   * like rg_linear_i8, a call whose GEMM runs on the tensor cores waits for it
+//     and returns RG_ERR_TIMEOUT if one of its bounded waits gave up (the word
+//     that reports it is a slot of a static device array held for this call).
 #include <cuda_runtime.h>
 #include <stdio.h>
 
@@ -69,11 +74,12 @@ extern "C" rg_status rg_linear_i8_noalloc(const float* x, int64_t m, int64_t k, 
                                           int64_t ld, float w_scale, const float* bias, int32_t act,
                                           float act_param, float* out, void* stream) {
   if (m < 0 || ld <= 0) return rg::set_last_error(RG_ERR_INVALID_ARG, "rg_linear_i8_noalloc: bad m or ld");
-  if (m * ld > (int64_t)kMaxQuantBytes) {
-    char msg[160];
+  // m * ld <= limit, tested by division so that no product can wrap
+  if (m > (int64_t)kMaxQuantBytes / ld) {
+    char msg[192];
     snprintf(msg, sizeof msg,
-             "rg_linear_i8_noalloc: m * ld = %lld bytes exceeds the %zu-byte static scratch; use rg_linear_i8",
-             (long long)(m * ld), kMaxQuantBytes);
+             "rg_linear_i8_noalloc: m = %lld rows of ld = %lld bytes exceeds the %zu-byte static scratch; "
+             "use rg_linear_i8", (long long)m, (long long)ld, kMaxQuantBytes);
     return rg::set_last_error(RG_ERR_INVALID_ARG, msg);
   }
   int dev = 0;

@@ -16,8 +16,9 @@
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
-#include <memory>
+#include <condition_variable>
 #include <memory>
 #include <mutex>
 #include <string>
@@ -33,6 +34,10 @@ namespace rg {
 // errors
 // ----------------------------------------------------------------------------
 static thread_local std::string g_err = "ok";
+
+// Test hook state (rg_debug_set_tc_wait): copied into every tcgen05 GEMM launch.
+static std::atomic<uint64_t> g_tc_wait_ns{0};
+static std::atomic<int32_t> g_tc_starve{0};
 
 static rg_status fail(rg_status st, const char* fmt, ...) {
   char buf[1024];
@@ -192,6 +197,11 @@ struct Session {
   std::mutex mu;
   // workspace
   DevBuf act0, act1, act2, act3, qbuf, amax, scales, accbuf, xin, yout, covbuf;
+  // This session's device error words, set by its kernels and read (and cleared) by
+  // the host after a synchronous run: [0] a tensor-core kernel gave up on a bounded
+  // wait; [1] an embedding id was not below the vocabulary size.  Per session, so a
+  // failure is reported to the run it happened in and to no other session.
+  DevBuf errw;
   DevBuf ext0, ext1;  // attention / SwiGLU intermediates (QKV or gate|up, merged heads or g*u)
   // profile + trace
   Profile last;
@@ -939,6 +949,9 @@ static rg_status run_inner_linear(Session& s, const Op& lin, const float* src, i
   g.act = RG_ACT_NONE;
   g.out = out;
   g.amax = sink;
+  g.err = s.errw.as<int>();
+  g.wait_ns = g_tc_wait_ns.load();
+  g.starve = g_tc_starve.load();
   const bool tc = gemm_tc_eligible(g);
   const bool narrow = !tc && gemm_narrow_eligible(g);
   if (tc) {
@@ -1086,6 +1099,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
       cb.act1 = op.act; cb.act2 = c2.act; cb.p1 = op.param; cb.p2 = c2.param;
       float* bdst = (i + 3 + 1 == n && y_dev) ? y_dev : dst;
       cb.out = bdst;
+      cb.err = s.errw.as<int>();
       const int bcons = find_consumer(s, i + 3);
       if (bcons >= 0 && P.amax_src[(size_t)bcons] == (int)(i + 3)) {
         cb.amax = amax + P.amax_off[(size_t)bcons];
@@ -1151,6 +1165,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
       sp.bias = op.d_bias.as<float>();
       sp.act = op.act; sp.act_param = op.param;
       sp.out = (i + 2 == n && y_dev) ? y_dev : dst;
+      sp.err = s.errw.as<int>();
       const int pcons = find_consumer(s, i + 1);
       if (pcons >= 0 && P.amax_src[(size_t)pcons] == (int)(i + 1)) {
         sp.amax.ptr = amax + P.amax_off[(size_t)pcons];
@@ -1228,6 +1243,9 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         float* my_scale = scales + P.amax_off[i];
         int8_t* q = s.qbuf.as<int8_t>();
         GemmArgs g;
+        g.err = s.errw.as<int>();
+        g.wait_ns = g_tc_wait_ns.load();
+        g.starve = g_tc_starve.load();
         bool fused_q = false;
         if (op.kind == RG_LAYER_LINEAR) {
           const int64_t rows = os.in_elems / op.in_f;
@@ -1455,7 +1473,8 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         break;
       }
       case RG_LAYER_EMBEDDING:
-        launch_embedding(cur, os.in_elems, op.d_ext.as<float>(), op.in_f, op.out_f, dst, sink, st);
+        launch_embedding(cur, os.in_elems, op.d_ext.as<float>(), op.in_f, op.out_f, dst, sink,
+                         s.errw.as<int>() + 1, st);
         ++launches;
         RG_LAUNCHED("embedding");
         s.used_embed = true;
@@ -1663,6 +1682,58 @@ struct rg_session {
   Session s;
 };
 
+// ---- error words of the kernel-level entry points ------------------------------
+// A kernel-level call that runs a tensor-core kernel holds one word of this array for
+// its duration, taken from a host-side free list per device: concurrent calls never
+// share a word, and no call allocates device memory.  The last word is the sink of
+// calls recorded in a stream capture (never read).
+constexpr int kCallErrSlots = 64;
+constexpr int kCallErrDevices = 64;
+static __device__ int32_t g_call_err[kCallErrSlots];
+
+struct CallErrPool {
+  std::mutex mu;
+  std::condition_variable cv;
+  int32_t* base[kCallErrDevices] = {};
+  uint64_t busy[kCallErrDevices] = {};
+};
+static CallErrPool g_err_pool;
+
+struct CallErrSlot {
+  int32_t* ptr = nullptr;
+  int dev = -1, bit = -1;
+  // the current device is `device` (its array's address is looked up with it current)
+  rg_status acquire(int device, bool capture_sink) {
+    if (device < 0 || device >= kCallErrDevices) return fail(RG_ERR_CUDA, "device %d out of range", device);
+    std::unique_lock<std::mutex> lock(g_err_pool.mu);
+    if (!g_err_pool.base[device]) {
+      void* p = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&p, g_call_err);
+      if (e != cudaSuccess) return fail(RG_ERR_CUDA, "error-word array: %s", cudaGetErrorString(e));
+      g_err_pool.base[device] = static_cast<int32_t*>(p);
+    }
+    dev = device;
+    if (capture_sink) {
+      ptr = g_err_pool.base[device] + (kCallErrSlots - 1);
+      return RG_OK;
+    }
+    constexpr uint64_t kAll = (1ull << (kCallErrSlots - 1)) - 1;  // every word but the sink
+    g_err_pool.cv.wait(lock, [&] { return (g_err_pool.busy[device] & kAll) != kAll; });
+    bit = __builtin_ctzll(~g_err_pool.busy[device] & kAll);
+    g_err_pool.busy[device] |= 1ull << bit;
+    ptr = g_err_pool.base[device] + bit;
+    return RG_OK;
+  }
+  ~CallErrSlot() {
+    if (bit < 0) return;
+    {
+      std::lock_guard<std::mutex> lock(g_err_pool.mu);
+      g_err_pool.busy[dev] &= ~(1ull << bit);
+    }
+    g_err_pool.cv.notify_one();
+  }
+};
+
 extern "C" {
 
 const char* rg_last_error(void) { return g_err.c_str(); }
@@ -1701,6 +1772,8 @@ rg_status rg_session_create(const rg_layer_spec* layers, int32_t n_layers, const
   RG_CUDA_TRY(cudaStreamCreateWithFlags(&s.copy_stream, cudaStreamNonBlocking));
   s.chunk_events.assign(kFeedMaxChunks, nullptr);
   for (auto& e : s.chunk_events) RG_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  RG_TRY(s.errw.ensure(2 * sizeof(int)));
+  RG_CUDA_TRY(cudaMemset(s.errw.p, 0, 2 * sizeof(int)));
   RG_TRY(compile(s, layers, n_layers));
   *out = h.release();
   return RG_OK;
@@ -1885,16 +1958,12 @@ static rg_status run_impl(rg_session* h, const float* x, bool x_host, const int6
   *y_ndim = (int32_t)oshape.size();
   if (async_run) return RG_OK;
   RG_CUDA_TRY(cudaStreamSynchronize(st));
-  if (s.used_tc) {
-    s.used_tc = false;
-    if (gemm_tc_take_error() != 0 || convblock_take_error() != 0 || conv_tc_take_error() != 0 ||
-        conv3x3_take_error() != 0 || stem_take_error() != 0)
-      return fail(RG_ERR_TIMEOUT, "a tensor-core kernel gave up on a bounded wait; results are invalid");
-  }
-  if (s.used_embed) {
-    s.used_embed = false;
-    if (embedding_take_error() != 0)
-      return fail(RG_ERR_INVALID_ARG, "Embedding: a token id is not below the vocabulary size");
+  if (s.used_tc || s.used_embed) {
+    s.used_tc = s.used_embed = false;
+    int32_t e[2] = {0, 0};
+    RG_CUDA_TRY(cudaMemcpy(e, s.errw.p, sizeof e, cudaMemcpyDeviceToHost));
+    if (e[0] || e[1]) RG_CUDA_TRY(cudaMemset(s.errw.p, 0, sizeof e));
+    RG_TRY(rg_status_from_error_words(e));
   }
   int64_t total_ns = 0;
   if (events) {
@@ -2126,15 +2195,44 @@ rg_status rg_gemm_i8_fused(const int8_t* a, const int8_t* w, int64_t m, int64_t 
   int dev = 0, sms = 148;
   RG_CUDA_TRY(cudaGetDevice(&dev));
   RG_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  if (gemm_tc_eligible(g)) {
-    if (!launch_gemm_tc(g, sms, (cudaStream_t)stream)) return fail(RG_ERR_CUDA, "TMA descriptor encoding failed");
-  } else if (gemm_narrow_eligible(g)) {
-    launch_gemm_narrow(g, (cudaStream_t)stream);
-  } else {
-    launch_gemm_simt(g, (cudaStream_t)stream);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (!gemm_tc_eligible(g)) {  // CUDA-core kernels: no waits, enqueued and returned
+    if (gemm_narrow_eligible(g)) launch_gemm_narrow(g, st);
+    else launch_gemm_simt(g, st);
+    RG_CUDA_TRY(cudaGetLastError());
+    return RG_OK;
   }
+  // The tensor-core kernel reports a bounded wait that gave up through an error word
+  // of this call alone; the call waits for the kernel and turns the word into its
+  // status.  Inside a stream capture nothing can be waited for: the captured kernel
+  // writes a word no call reads (a timeout in a replay of that graph goes unreported).
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  RG_CUDA_TRY(cudaStreamIsCapturing(st, &cap));
+  CallErrSlot slot;
+  RG_TRY(slot.acquire(dev, cap != cudaStreamCaptureStatusNone));
+  RG_CUDA_TRY(cudaMemsetAsync(slot.ptr, 0, sizeof(int32_t), st));
+  g.err = slot.ptr;
+  g.wait_ns = g_tc_wait_ns.load();
+  g.starve = g_tc_starve.load();
+  if (!launch_gemm_tc(g, sms, st)) return fail(RG_ERR_CUDA, "TMA descriptor encoding failed");
   RG_CUDA_TRY(cudaGetLastError());
+  if (cap != cudaStreamCaptureStatusNone) return RG_OK;
+  int32_t e[2] = {0, 0};
+  RG_CUDA_TRY(cudaMemcpyAsync(e, slot.ptr, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+  RG_CUDA_TRY(cudaStreamSynchronize(st));
+  return rg_status_from_error_words(e);
+}
+
+rg_status rg_status_from_error_words(const int32_t words[2]) {
+  if (!words) return fail(RG_ERR_INVALID_ARG, "null argument");
+  if (words[0]) return fail(RG_ERR_TIMEOUT, "a tensor-core kernel gave up on a bounded wait; results are invalid");
+  if (words[1]) return fail(RG_ERR_INVALID_ARG, "Embedding: a token id is not below the vocabulary size");
   return RG_OK;
+}
+
+void rg_debug_set_tc_wait(uint64_t wait_ns, int32_t starve_loads) {
+  g_tc_wait_ns.store(wait_ns);
+  g_tc_starve.store(starve_loads ? 1 : 0);
 }
 
 int64_t rg_linear_i8_workspace_size(int64_t m, int64_t ld) { return round_up(m * ld, 256) + 256; }

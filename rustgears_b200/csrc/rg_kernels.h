@@ -101,6 +101,11 @@ struct GemmArgs {
   // 1x1 / pad 0 / stride cov_s conv reads (rows and columns cov_s * i, i < cov_oh / cov_ow)
   unsigned* amax2 = nullptr;
   int32_t cov_s = 1, cov_oh = 0, cov_ow = 0;
+  // tensor-core kernels: this call's device error word (required; set to 1 when a
+  // bounded wait gave up) and the limit of their pipeline waits (0: the default)
+  int* err = nullptr;
+  uint64_t wait_ns = 0;
+  int32_t starve = 0;  // test hook (k_gemm_tc): issue no operand loads, so the waits run out
 };
 
 // FP16 arm (fp16_gemm_fused_into, npu.rs:431-445) on the CUDA cores: out =
@@ -138,7 +143,6 @@ bool launch_gemm_tc(const GemmArgs& a, int num_sms, cudaStream_t st);
 // a multiple of 16, g.c == g.cpad; NCHW output, per-image scales).
 bool conv_tc_eligible(const GemmArgs& a);
 bool launch_conv_tc(const GemmArgs& a, int num_sms, cudaStream_t st);
-int conv_tc_take_error();
 // 3x3 / stride 1 / pad 1 convs (channels padded to a multiple of 64) as a direct
 // convolution over zero-padded TMA input tiles of the chunk-planar operand
 // (launch_image_quantize_planar16); weights pre-arranged by
@@ -166,10 +170,6 @@ bool conv3x3_shape_ok(int64_t n_img, int32_t h, int32_t w, int32_t cpad, int32_t
 size_t conv3x3_weight_bytes(int32_t n, int32_t cpad);
 void conv3x3_arrange_weights(const int8_t* wq, int32_t n, int32_t c, int32_t cpad, int8_t* out);
 bool launch_conv3x3(const GemmArgs& a, const int8_t* wd, int num_sms, cudaStream_t st);
-int conv3x3_take_error();
-// Reads and clears the device error word the tcgen05 kernels set when a bounded
-// wait gave up (synchronous; 0 = no error).
-int gemm_tc_take_error();
 
 // ---- fused stem (k_stem.cu) ------------------------------------------------------
 // Conv2d(c <= 4 -> 64, k 7, s 2, p 3) + act, then MaxPool2d(3, 2), one kernel over the
@@ -188,13 +188,13 @@ struct StemPoolArgs {
   float act_param = 0.0f;
   float* out = nullptr;
   AmaxSink amax;                   // of the pooled output
+  int* err = nullptr;              // this call's error word (required)
 };
 bool stem_pool_shape_ok(int64_t n_img, int32_t c, int32_t h, int32_t w, int32_t k, int32_t stride, int32_t pad,
                         int32_t out_channels, int32_t pool_k, int32_t pool_s);
 size_t stem_weight_bytes();
 void stem_arrange_weights(const int8_t* wq, int32_t c, int8_t* out);
 bool launch_stem_pool(const StemPoolArgs& a, int num_sms, cudaStream_t st);
-int stem_take_error();
 
 // ---- fused CNN block (k_convblock.cu) ------------------------------------------
 // Conv(C0->C1,k3,s1,p1)+act -> MaxPool(2,2) -> Conv(C1->C2,k3,s1,p1)+act -> MaxPool(2,2),
@@ -215,11 +215,10 @@ struct ConvBlockArgs {
   float* out = nullptr;              // [n, c2, h/4, w/4]
   unsigned* amax = nullptr;          // optional absmax sink of out
   int64_t amax_per_image = 0;
+  int* err = nullptr;                // this call's error word (required)
 };
 bool convblock_supported(int c0, int c1, int c2, int h, int w, int act1, int act2);
 void launch_convblock(const ConvBlockArgs& a, int num_sms, cudaStream_t st);
-// Reads and clears the device error word the fused block sets when a bounded wait gave up.
-int convblock_take_error();
 
 // ---- misc (k_misc.cu) ----------------------------------------------------------
 void launch_maxpool2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w, int32_t k,
@@ -238,10 +237,9 @@ void launch_activation(const float* x, int64_t n, int32_t act, float p, float* y
 void launch_softmax(const float* x, int64_t outer, int64_t last, float* y, AmaxSink amax,
                     cudaStream_t st);
 // Transformer extension (k_transformer.cu).  Token ids are f32 values; an id >= v sets
-// a device error word (embedding_take_error reads and clears it, synchronously).
+// the caller's device error word *err to 1.
 void launch_embedding(const float* ids, int64_t n, const float* table, int64_t v, int32_t d, float* y,
-                      AmaxSink amax, cudaStream_t st);
-int embedding_take_error();
+                      AmaxSink amax, int* err, cudaStream_t st);
 rg_status launch_rmsnorm(const float* x, int64_t rows, int32_t d, const float* w, float eps, float inv_d, float* y,
                          AmaxSink amax, cudaStream_t st);
 // gu [rows, 2h] = [g | u] -> y [rows, h] = (g * sigmoid(g)) * u

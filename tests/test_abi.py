@@ -60,3 +60,17 @@ def test_rng_abi_values():
     L.rg_rng_seed(C.byref(r), 0x9E3779B97F4A7C15)
     assert L.rg_rng_next_u64(C.byref(r)) == 0xE220A8397B1DCDAF
     assert np.float32(L.rg_kaiming_bound(4)) == np.sqrt(np.float32(6.0) / np.float32(4.0))
+
+
+def test_error_words_map_to_statuses():
+    """The mapping every run and kernel-level call applies to its device error words,
+    driven from the host with forced words (no device needed)."""
+    L = _native.lib()
+    words = (C.c_int32 * 2)
+    assert L.rg_status_from_error_words(words(0, 0)) == _native.RG_OK
+    assert L.rg_status_from_error_words(words(1, 0)) == _native.RG_ERR_TIMEOUT
+    assert "bounded wait" in _native.last_error()
+    assert L.rg_status_from_error_words(words(1, 1)) == _native.RG_ERR_TIMEOUT
+    assert L.rg_status_from_error_words(words(0, 1)) == _native.RG_ERR_INVALID_ARG
+    assert "vocabulary" in _native.last_error()
+    assert L.rg_status_from_error_words(None) == _native.RG_ERR_INVALID_ARG
