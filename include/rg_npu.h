@@ -308,8 +308,10 @@ rg_status rg_attention_f32(const float* qkv, int64_t ld, int64_t batch, int32_t 
  * and the plain IEEE / libdevice form and counts the inputs whose results differ:
  * mismatches[0] tanh, [1] GELU (division), [2] the quantization scale from an
  * absmax (non-negative inputs), [3] its reciprocal, [4] the rounding of a
- * quantization argument (|t| < 2^23 and NaN).  Synchronous, current device, ~0.2 s. */
-rg_status rg_selftest_fast_paths(uint64_t mismatches[5]);
+ * quantization argument (|t| < 2^23 and NaN), [5] the GEMM epilogue's
+ * common-range tanh (and GELU through it) against the general one, on every
+ * input where the epilogue uses it.  Synchronous, current device, ~0.3 s. */
+rg_status rg_selftest_fast_paths(uint64_t mismatches[6]);
 
 /* ---------------------------------------------------------------------------
  * Deterministic generator used by the benchmark configurations: SplitMix64

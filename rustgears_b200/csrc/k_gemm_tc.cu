@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
         const int64_t col0 = (int64_t)nb * BN + c0;
         if (col0 >= p.n || row0 >= p.m) continue;  // warp-uniform
-        float o[16];
+        float o[16];  // (acc as f32) * cs + bias, then the activation in place
         if (p.vec_cols && col0 + 16 <= p.n) {
           // Full chunk: scale and bias as 16-byte loads.
           const float4* bp = reinterpret_cast<const float4*>(p.bias + col0);
@@ -235,14 +235,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float4 sw = __ldg(sp + j4);
               cs = make_float4(__fmul_rn(sa, sw.x), __fmul_rn(sa, sw.y), __fmul_rn(sa, sw.z), __fmul_rn(sa, sw.w));
             }
-            o[4 * j4] = epilogue_t<ACT>((int32_t)v[4 * j4], cs.x, b.x, p.act_param);
-            o[4 * j4 + 1] = epilogue_t<ACT>((int32_t)v[4 * j4 + 1], cs.y, b.y, p.act_param);
-            o[4 * j4 + 2] = epilogue_t<ACT>((int32_t)v[4 * j4 + 2], cs.z, b.z, p.act_param);
-            o[4 * j4 + 3] = epilogue_t<ACT>((int32_t)v[4 * j4 + 3], cs.w, b.w, p.act_param);
-          }
-          if (row_ok) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(o[j]));
+            o[4 * j4] = dequant((int32_t)v[4 * j4], cs.x, b.x);
+            o[4 * j4 + 1] = dequant((int32_t)v[4 * j4 + 1], cs.y, b.y);
+            o[4 * j4 + 2] = dequant((int32_t)v[4 * j4 + 2], cs.z, b.z);
+            o[4 * j4 + 3] = dequant((int32_t)v[4 * j4 + 3], cs.w, b.w);
           }
         } else {
 #pragma unroll
@@ -250,9 +246,43 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int64_t c = col0 + j;
             const int64_t cc = c < p.n ? c : p.n - 1;
             const float cs = p.w_scale_ch ? __fmul_rn(sa, __ldg(p.w_scale_ch + cc)) : cs_tensor;
-            o[j] = epilogue_t<ACT>((int32_t)v[j], cs, __ldg(p.bias + cc), p.act_param);
-            if (c < p.n && row_ok) amax = fmaxf(amax, fabsf(o[j]));
+            o[j] = dequant((int32_t)v[j], cs, __ldg(p.bias + cc));
           }
+        }
+        if constexpr (ACT == ACT_GELU) {
+          // Every value takes the restatement with only the common range's cases
+          // (bit-identical to the general one there); the values whose tanh argument
+          // lies outside it (|u| >= 7.5, |u| < 2^-25, non-finite) are recomputed with
+          // the general restatement, one value per lane per round, in a loop holding a
+          // single copy of it.
+          float t[16];
+          uint32_t redo = 0;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float u = gelu_arg(o[j]);
+            t[j] = tanh_f32_common(u);
+            redo |= (uint32_t)!tanh_common_range(u) << j;
+          }
+          while (__any_sync(0xffffffffu, redo != 0)) {
+            const int jr = redo ? __ffs(redo) - 1 : 0;
+            float xr = o[0];
+#pragma unroll
+            for (int j = 1; j < 16; ++j) xr = jr == j ? o[j] : xr;
+            const float tr = tanh_f32(gelu_arg(xr));
+#pragma unroll
+            for (int j = 0; j < 16; ++j) t[j] = (redo && jr == j) ? tr : t[j];
+            redo &= redo - 1;
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] = gelu_from_tanh(o[j], t[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] = act_apply(ACT, p.act_param, o[j]);
+        }
+        if (row_ok) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (col0 + j < p.n) amax = fmaxf(amax, fabsf(o[j]));
         }
         if (p.tma_store) {
           // The previous chunk's store must have finished reading the staging tile.

@@ -2285,16 +2285,16 @@ rg_status rg_attention_f32(const float* qkv, int64_t ld, int64_t batch, int32_t 
   return RG_OK;
 }
 
-rg_status rg_selftest_fast_paths(uint64_t mismatches[5]) {
+rg_status rg_selftest_fast_paths(uint64_t mismatches[6]) {
   if (!mismatches) return fail(RG_ERR_INVALID_ARG, "null argument");
   DevBuf counts;
-  const rg_status st = counts.ensure(5 * sizeof(unsigned long long));
+  const rg_status st = counts.ensure(6 * sizeof(unsigned long long));
   if (st != RG_OK) return st;
   launch_selftest_fast_division(counts.as<unsigned long long>(), nullptr);
   RG_CUDA_TRY(cudaGetLastError());
-  unsigned long long h[5];
+  unsigned long long h[6];
   RG_CUDA_TRY(cudaMemcpy(h, counts.p, sizeof h, cudaMemcpyDeviceToHost));
-  for (int i = 0; i < 5; ++i) mismatches[i] = h[i];
+  for (int i = 0; i < 6; ++i) mismatches[i] = h[i];
   return RG_OK;
 }
 

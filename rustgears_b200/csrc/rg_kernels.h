@@ -225,7 +225,7 @@ void launch_maxpool2d(const float* x, int64_t n, int32_t c, int32_t h, int32_t w
                       int32_t s, float* y, AmaxSink amax, cudaStream_t st);
 // Counts f32 inputs where a fast path changes a result, over all 2^32 bit patterns
 // (zeroed first): counts[0] tanh, [1] GELU, [2] quant_scale, [3] quant_inv,
-// [4] round_half_away.
+// [4] round_half_away, [5] tanh_f32_common / GELU through it on its range.
 void launch_selftest_fast_division(unsigned long long* counts, cudaStream_t st);
 // Extensions: y = act(x + s) elementwise; adaptive average pooling to oh x ow.
 void launch_residual_add(const float* x, const float* s, int64_t n, int32_t act, float p, float* y,

@@ -238,6 +238,61 @@ RG_HD float tanh_f32(float x) {
   return z;
 }
 
+// tanh_f32 on its common range |x| in [2^-25, 7.5) (finite), with only the steps
+// that range can take.  There the expm1 argument a = +-2|x| has 2^-24 <= |a| < 15,
+// so the reduction's k lies in {-3, -2, -1, 0} (|x| < 1) or [3, 22] (|x| >= 1): the
+// k = 0 and k = -1 reconstructions, and the k <= -2 and 2 <= k < 23 ones, which
+// share their operand (e2 - x) and differ only in the constant it is subtracted from
+// (1, or 1 - 2^-k) and in a final - 1; the |x| >= 22, |x| < 2^-55, |a| < 2^-25, NaN and
+// 23 <= k <= 56 cases cannot occur.  Every value is computed by the same operations
+// in the same order as tanh_f32, so the two agree bit for bit on the range (checked
+// on every f32 of it, on the host and by the device self-test).
+RG_HD bool tanh_common_range(float x) {
+  const uint32_t ix = f2u(x) & 0x7fffffffu;
+  return ix >= 0x33000000u && ix < 0x40f00000u;
+}
+template <bool kNR = true>
+RG_HD float tanh_f32_common(float x) {
+  const float ln2_hi = u2f(0x3f317180u), ln2_lo = u2f(0x3717f7d1u), invln2 = u2f(0x3fb8aa3bu);
+  const float q1 = u2f(0xbd088889u), q2 = u2f(0x3ad00d01u), q3 = u2f(0xb8a670cdu),
+              q4 = u2f(0x36867e54u), q5 = u2f(0xb457edbbu);
+  const uint32_t jx = f2u(x), ix = jx & 0x7fffffffu;
+  const bool big = ix >= 0x3f800000u;                 // |x| >= 1
+  const float two_ax = RG_MUL(2.0f, fabsf(x));
+  // expm1_tanh_arg(a) on 2^-24 <= |a| < 15
+  const float a = big ? two_ax : -two_ax;
+  const uint32_t hx = f2u(two_ax);
+  int k = (int)RG_ADD(RG_MUL(invln2, a), big ? 0.5f : -0.5f);
+  k = hx < 0x3F851592u ? (big ? 1 : -1) : k;
+  k = hx > 0x3eb17218u ? k : 0;
+  const float t = (float)k;
+  const float hi = RG_SUB(a, RG_MUL(t, ln2_hi));
+  const float lo = RG_MUL(t, ln2_lo);
+  const float xr = RG_SUB(hi, lo);
+  const float c = RG_SUB(RG_SUB(hi, xr), lo);
+  const float hfx = RG_MUL(0.5f, xr);
+  const float hxs = RG_MUL(xr, hfx);
+  float r1 = RG_MUL(hxs, q5);
+  r1 = RG_MUL(hxs, RG_ADD(q4, r1));
+  r1 = RG_MUL(hxs, RG_ADD(q3, r1));
+  r1 = RG_MUL(hxs, RG_ADD(q2, r1));
+  r1 = RG_MUL(hxs, RG_ADD(q1, r1));
+  r1 = RG_ADD(1.0f, r1);
+  const float tt = RG_SUB(3.0f, RG_MUL(r1, hfx));
+  const float e = RG_MUL(hxs, div_path<kNR>(RG_SUB(r1, tt), RG_SUB(6.0f, RG_MUL(xr, tt))));
+  const float res0 = RG_SUB(xr, RG_SUB(RG_MUL(xr, e), hxs));                 // k == 0
+  const float e2 = RG_SUB(RG_SUB(RG_MUL(xr, RG_SUB(e, c)), c), hxs);
+  const float res_m1 = RG_SUB(RG_MUL(0.5f, RG_SUB(xr, e2)), 0.5f);          // k == -1
+  const float base = k < 0 ? 1.0f : u2f(0x3f800000u - (0x1000000u >> (k & 31)));
+  const float sc = u2f(f2u(RG_SUB(base, RG_SUB(e2, xr))) + ((uint32_t)k << 23));
+  const float res_ab = k < 0 ? RG_SUB(sc, 1.0f) : sc;                       // k <= -2; 3 <= k <= 22
+  const float em1 = k == 0 ? res0 : (k == -1 ? res_m1 : res_ab);
+  // tanh from expm1
+  const float q = div_path<kNR>(big ? 2.0f : -em1, RG_ADD(em1, 2.0f));
+  const float z = big ? RG_SUB(1.0f, q) : q;
+  return (jx >> 31) ? -z : z;
+}
+
 // 2^(i/32) rounded to double, minus i << 47 (the table of the expf method).
 #define RG_EXP2_TABLE                                                                  \
   {0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full,                 \
@@ -327,15 +382,19 @@ RG_HD float exp_f32_with(float x, Tab tab) {
 
 RG_HD float exp_f32(float x) { return exp_f32_with(x, ExpTableConst{}); }
 
-// GELU (tanh form) of Activation::apply (src/device/backend.rs:61-68).
-template <bool kNR = true>
-RG_HD float gelu_f32(float x) {
+// GELU (tanh form) of Activation::apply (src/device/backend.rs:61-68):
+// 0.5 * x * (1 + tanh(u)) with u = GELU_C * (x + 0.044715 * x * x * x).
+RG_HD float gelu_arg(float x) {
   const float gelu_c = 0.7978846f;                               // GELU_C (backend.rs:61)
   float c = RG_MUL(0.044715f, x);
   c = RG_MUL(c, x);
   c = RG_MUL(c, x);
-  const float t = tanh_f32<kNR>(RG_MUL(gelu_c, RG_ADD(x, c)));
-  return RG_MUL(RG_MUL(0.5f, x), RG_ADD(1.0f, t));
+  return RG_MUL(gelu_c, RG_ADD(x, c));
+}
+RG_HD float gelu_from_tanh(float x, float t) { return RG_MUL(RG_MUL(0.5f, x), RG_ADD(1.0f, t)); }
+template <bool kNR = true>
+RG_HD float gelu_f32(float x) {
+  return gelu_from_tanh(x, tanh_f32<kNR>(gelu_arg(x)));
 }
 
 // round_fp16 (src/inference/quantize.rs:50-64), the FP16 arm's emulation of a
@@ -412,14 +471,19 @@ RG_HD int32_t round_half_away(float t) {
 // |v * inv| <= 127 (1 + 3 * 2^-24) < 127.5, so the clamp never acts and is left out.
 RG_HD int32_t quant1_bounded(float v, float inv) { return round_half_away(RG_MUL(v, inv)); }
 
-// Epilogue of int8_gemm_fused (quantize.rs:109-111): act((acc as f32) * cs + bias).
-RG_HD float epilogue(int32_t acc, float cs, float bias, int32_t act, float p) {
+// (acc as f32) * cs + bias, the pre-activation value of int8_gemm_fused's epilogue.
+RG_HD float dequant(int32_t acc, float cs, float bias) {
 #ifdef __CUDA_ARCH__
   const float a = __int2float_rn(acc);
 #else
   const float a = (float)acc;
 #endif
-  return act_apply(act, p, RG_ADD(RG_MUL(a, cs), bias));
+  return RG_ADD(RG_MUL(a, cs), bias);
+}
+
+// Epilogue of int8_gemm_fused (quantize.rs:109-111): act((acc as f32) * cs + bias).
+RG_HD float epilogue(int32_t acc, float cs, float bias, int32_t act, float p) {
+  return act_apply(act, p, dequant(acc, cs, bias));
 }
 
 // Same with the activation fixed at compile time: the switch folds away, so a

@@ -438,3 +438,23 @@ def test_silu_conv_implicit_gemm(gpu, oracle_lib):
             l["act"] = ACT_SILU
     ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
     assert_same(session_for(layers).run(x), ref, "c2 with SiLU")
+
+
+@pytest.mark.parametrize("scale", [1.0, 8.0, 1e3, 1e-30])
+def test_gelu_epilogue_outside_the_common_range(gpu, oracle_lib, scale):
+    """The tensor-core GEMM's GELU epilogue takes a short tanh path for arguments in
+    [2^-25, 7.5) and recomputes the others with the general one: pre-activations scaled
+    so that few, most or all values leave that range (and inf / NaN rows), bit-exact
+    against the oracle."""
+    layers, x = configs.c3_linear(512, 512, 384, seed=21)
+    layers = [dict(l, weight=np.asarray(l["weight"]) * np.float32(scale)) if l["kind"] == oracle.LINEAR else l
+              for l in layers]
+    x = x.copy()
+    x[7, 3] = np.inf
+    x[9, 0] = np.nan
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
+    assert_same(session_for(layers).run(x), ref, f"gelu scale {scale}")
+    x[7, 3] = 0.0
+    x[9, 0] = 0.0
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
+    assert_same(session_for(layers).run(x), ref, f"gelu scale {scale}, finite")
