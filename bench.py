@@ -103,6 +103,18 @@ def build_workload(cfg: str, rank: int, world: int, batch: int | None):
     return model, x, mb
 
 
+def calibration_input(cfg: str, units: int, world: int, rank: int, n: int):
+    """A calibration batch for --calibrated: n samples drawn right after every rank's
+    benchmark shard (disjoint from the measured batch), this rank's n of them."""
+    from rustgears_b200 import configs
+    off = world * units + rank * n
+    if cfg.startswith("c3"):
+        _, k, nn_ = WORKLOADS[cfg]["shape"]
+        return configs.c3_linear(0, k, nn_, rows=n, row_offset=off)[1]
+    fn = {"c1": configs.c1_mlp, "c2": configs.c2_cnn, "c4": configs.c4_resnet18, "c5": configs.c5_transformer}[cfg]
+    return fn(n, row_offset=off)[1]
+
+
 def program_macs(sess, x_shape) -> int:
     import numpy as _np
     one = (1,) + tuple(x_shape[1:])
@@ -180,7 +192,7 @@ def fp32_fma_peak(sms: int, mhz: float) -> float:
     return sms * 128 * 2 * mhz * 1e6 / 1e12
 
 
-def op_roofline(cfg, sess, per_op_ns, steps, x_shape, peaks, traffic=None, fp32_peak=None):
+def op_roofline(cfg, sess, per_op_ns, steps, x_shape, peaks, traffic=None, fp32_peak=None, i8_out=False):
     """Roofline of the dominant kernel.  A kernel covers one op, or several when the
     library fused them (the fused-away ops report no time).  Algorithmic work: 2 x
     the INT8 MACs; algorithmic bytes: the kernel's f32 input read + f32 output
@@ -200,7 +212,8 @@ def op_roofline(cfg, sess, per_op_ns, steps, x_shape, peaks, traffic=None, fp32_
     dur_s = per_op_ns[a:b].sum() / steps / 1e9
     shapes = _op_shapes(sess, x_shape)
     in_bytes = 4 * int(np.prod(shapes[a][0]))
-    out_bytes = 4 * int(np.prod(shapes[b - 1][1]))
+    # a calibrated producer writes the next Linear's i8 operand: one byte per element
+    out_bytes = (1 if i8_out else 4) * int(np.prod(shapes[b - 1][1]))
     wbytes = sum(sess.op_info(k)["wq_len"] + 4 * sess.op_info(k)["bias_len"] for k in range(a, b))
     algo = in_bytes + out_bytes + wbytes
     ops = 2.0 * sum(prof.records[k].macs for k in range(a, b))
@@ -520,7 +533,7 @@ def gemm_kernel_roofline(sess, xd, yd, stream, flush, peaks, reps: int = 10):
             "timing": f"kernel alone via rg_gemm_i8_fused, mean of {reps} launches, L2 flushed before each"}
 
 
-def sharded_parity(sess, model, prov, x, weight_quant, rank, world, dev, tdist, per_rank: int):
+def sharded_parity(sess, model, prov, x, weight_quant, rank, world, dev, tdist, per_rank: int, scales=None):
     """A small global batch (the first `per_rank` units of every rank's shard, gathered)
     run sharded through the library's NCCL path -- the per-Linear max all-reduce -- its
     outputs all-gathered by rg_session_allgather, against one device running the whole
@@ -538,6 +551,8 @@ def sharded_parity(sess, model, prov, x, weight_quant, rank, world, dev, tdist, 
     ok = torch.ones(1, dtype=torch.int32, device=dev)
     if rank == 0:
         single = InferenceSession.from_module(model, prov, device=dev.index, weight_quant=weight_quant)
+        if scales is not None:
+            single.set_calibration(scales)
         yg = single.run_device(xg)
         torch.cuda.synchronize(dev)
         a, b = recv.view(yg.shape), yg
@@ -561,6 +576,9 @@ def main():
                     help="Npu(Int8) (the headline), the Npu(Fp16) arm, or the f32 Cpu provider's arithmetic")
     ap.add_argument("--weight-quant", default="per_tensor", choices=["per_tensor", "per_channel"],
                     help="i8 weight scales: per tensor (the reference) or per output channel (extension)")
+    ap.add_argument("--calibrated", action="store_true",
+                    help="static calibration (extension): frozen Linear input scales from a calibration batch "
+                         "disjoint from the measured one; producers write the Linears' i8 operands")
     ap.add_argument("--probe", action="store_true",
                     help="run the workload --steps times and print the profile (for ncu captures; no timing)")
     args = ap.parse_args()
@@ -597,6 +615,16 @@ def main():
     if world > 1:
         uid = dist.exchange_unique_id(rank)
         dist.attach(sess, rank, world, uid)
+    calib = None
+    if args.calibrated:
+        if fp16 or f32:
+            raise SystemExit("--calibrated is an Npu(Int8) extension")
+        n_cal = min(units, {"c3a": 4096, "c3b": 4096, "c3c": 4096, "c4": 16, "c5": 4}.get(cfg, 2048))
+        xcal = calibration_input(cfg, units, world, rank, n_cal)
+        scales = sess.calibrate(xcal)        # collective at N > 1: the scales cover every rank's batch
+        calib = {"samples": int(n_cal * world), "scales": int(scales.size),
+                 "how": "frozen per-tensor Linear input scales from a calibration batch drawn after the measured "
+                        "one (static-calibration extension; values beyond them clamp)"}
     xd = torch.from_numpy(x).to(dev)
     oshape = sess.output_shape(tuple(x.shape))
     yd = torch.empty(oshape, dtype=torch.float32, device=dev)
@@ -699,7 +727,8 @@ def main():
         roofline["traffic"] = traffic
         roofline["op_roofline"] = op_roofline(cfg, sess, per_op_ns, args.steps, x.shape, peaks)
     else:
-        roofline = op_roofline(cfg, sess, per_op_ns, args.steps, x.shape, peaks, fp32_peak=fp32_peak, traffic=traffic)
+        roofline = op_roofline(cfg, sess, per_op_ns, args.steps, x.shape, peaks, fp32_peak=fp32_peak,
+                               traffic=None if calib else traffic, i8_out=bool(calib) and cfg == "c2")
     roofline["traffic_source"] = traffic_src
 
     # end to end through the public host-buffer call, pinned host memory
@@ -721,7 +750,8 @@ def main():
     sharded = None
     if world > 1:
         per_rank = min(units, {"c4": 2, "c5": 1}.get(cfg, 64))
-        ok, n_global = sharded_parity(sess, model, prov, x, args.weight_quant, rank, world, dev, tdist, per_rank)
+        ok, n_global = sharded_parity(sess, model, prov, x, args.weight_quant, rank, world, dev, tdist, per_rank,
+                                      scales=sess.calibration() if calib else None)
         sharded = {"sharded_bit_exact": ok, "global_batch": n_global,
                    "how": "the batch sharded over the ranks through the library's NCCL path (per-Linear max "
                           "all-reduce), outputs all-gathered by rg_session_allgather, compared bit for bit with "
@@ -749,6 +779,9 @@ def main():
     if sharded is not None:
         line["sharded_bit_exact"] = sharded["sharded_bit_exact"]
         line["sharded_check"] = sharded
+    if calib:
+        line["config"]["calibration"] = calib
+        line["roofline"]["traffic_source"] = "no capture of the calibrated workload"
     if fp16:
         line["config"]["precision"] = "Npu(Fp16)"
     if f32:

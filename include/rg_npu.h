@@ -198,6 +198,28 @@ rg_status rg_session_op_info(rg_session* s, int32_t op, rg_op_info* info);
 rg_status rg_session_op_weights(rg_session* s, int32_t op, int8_t* wq, int64_t cap, float* bias,
                                 int64_t bias_cap);
 
+/* ---------------------------------------------------------------------------
+ * Static calibration (extension; no counterpart in the reference, whose every
+ * Linear quantizes its input with the absmax of the batch it is given,
+ * src/inference/npu.rs:312).  A calibrated session quantizes each Linear input
+ * with a frozen per-tensor scale instead: no absmax pass and, across GPUs, no
+ * all-reduce; the producers that can (the fused CNN block, RMSNorm, the SwiGLU
+ * gate product) write the Linear's i8 operand directly instead of f32.  Values
+ * beyond a frozen scale's range clamp to +-127.  Conv inputs keep their per-image
+ * scales.  One target per Linear; two per attention / SwiGLU block (its input,
+ * and the inner activation its second projection reads), in op order.
+ * ------------------------------------------------------------------------- */
+rg_status rg_session_calibration_targets(rg_session* s, int32_t* n);
+/* Runs x (host buffer) with the reference's dynamic scales and freezes the scale
+ * each target quantized with (QuantTensor::from_f32's absmax / 127, over every
+ * rank's shard when a communicator is attached: a collective call then). */
+rg_status rg_session_calibrate(rg_session* s, const float* x, const int64_t* shape, int32_t ndim);
+/* Installs n frozen scales (finite, positive; n = the target count), or with
+ * n = 0 returns to the reference's dynamic scales. */
+rg_status rg_session_set_calibration(rg_session* s, const float* scales, int32_t n);
+/* The frozen scales (RG_ERR_INVALID_ARG when the session is not calibrated). */
+rg_status rg_session_get_calibration(rg_session* s, float* scales, int32_t cap);
+
 /* Per-op trace for parity tests: when enabled, `run` keeps every op's
  * activation scale(s), i8 input, i32 accumulators and f32 output. */
 typedef enum rg_trace_item {

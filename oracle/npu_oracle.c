@@ -722,11 +722,25 @@ int32_t og_program_summary(const og_program* p, int32_t raw_count, char* buf, in
 /* ------------------------------------------------------------------------ */
 /* per-op execution                                                          */
 /* ------------------------------------------------------------------------ */
+/* Quantization with a scale fixed in advance (the calibration extension): the
+ * reference's rounding and clamp (quantize.rs:22) with inv = 1 / scale. */
+static void og_quantize_with_scale(const float* v, int64_t n, float scale, int8_t* out) {
+  float inv = 1.0f / scale;
+  for (int64_t i = 0; i < n; ++i) out[i] = og_q1(v[i], inv);
+}
+
 void og_op_linear(const og_op* op, const float* x, int64_t rows, float* y,
                   float* a_scale, int8_t* aq, int32_t* acc, int32_t nthreads) {
   int64_t k = op->in_features, n = op->out_features;
   int8_t* q = aq ? aq : (int8_t*)malloc((size_t)(rows * k > 0 ? rows * k : 1));
-  float sa = og_quantize_into(x, rows * k, q);            /* QuantTensor::from_f32 (serial) */
+  float sa;
+  if (op->frozen) {
+    sa = op->frozen_scale;
+    og_quantize_with_scale(x, rows * k, sa, q);
+  } else {
+    sa = og_quantize_into(x, rows * k, q);                /* QuantTensor::from_f32 (serial) */
+  }
+  ((og_op*)op)->seen_scale = sa;
   if (a_scale) *a_scale = sa;
   og_gemm_ctx c = { q, op->wq, op->bias, sa * op->w_scale, k, n, op->act, op->act_param, y, acc, 0,
                     op->w_scale_ch, sa };
@@ -740,7 +754,7 @@ void og_op_linear_with_amax(const og_op* op, const float* x, int64_t rows, float
   /* FusedLinear with the activation absmax supplied by the caller (a batch shard
    * quantizing with the max over every shard: the multi-device restatement). */
   int64_t k = op->in_features, n = op->out_features;
-  float sa = amax < 1e-12f ? 1.0f : amax / 127.0f;
+  float sa = op->frozen ? op->frozen_scale : (amax < 1e-12f ? 1.0f : amax / 127.0f);
   float inv = 1.0f / sa;
   int8_t* q = (int8_t*)malloc((size_t)(rows * k > 0 ? rows * k : 1));
   for (int64_t i = 0; i < rows * k; ++i) q[i] = og_q1(x[i], inv);
@@ -753,7 +767,7 @@ void og_op_linear_with_amax(const og_op* op, const float* x, int64_t rows, float
 void og_op_linear_rows(const og_op* op, const float* x, int64_t rows, int64_t r0, int64_t r1,
                        float* y, float* a_scale, int32_t* acc, int32_t nthreads) {
   int64_t k = op->in_features, n = op->out_features;
-  float sa = og_quant_scale(x, rows * k);
+  float sa = op->frozen ? op->frozen_scale : og_quant_scale(x, rows * k);
   float inv = 1.0f / sa;
   int64_t sub = r1 - r0;
   int8_t* q = (int8_t*)malloc((size_t)(sub * k > 0 ? sub * k : 1));

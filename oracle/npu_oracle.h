@@ -79,6 +79,11 @@ typedef struct og_op {
    * the extension quantizes each row of the [out, in] / [O, C*k*k] matrix with
    * QuantTensor::from_f32's arithmetic, quantize.rs:18-24) */
   float* w_scale_ch;
+  /* static-calibration extension (no counterpart in the reference): with `frozen` set,
+   * a Linear quantizes its input with frozen_scale instead of the scale of the input's
+   * own absmax (values beyond the calibrated range clamp to +-127); seen_scale is the
+   * scale the last run quantized with (how a calibration run records it) */
+  int32_t frozen; float frozen_scale; float seen_scale; int32_t _pad3;
 } og_op;
 
 typedef struct {

@@ -61,6 +61,7 @@ _Op._fields_ = [
     ("extra", C.POINTER(C.c_float)), ("extra_len", C.c_int64),
     ("wh", C.POINTER(C.c_float)), ("wh_len", C.c_int64),
     ("w_scale_ch", C.POINTER(C.c_float)),
+    ("frozen", C.c_int32), ("frozen_scale", C.c_float), ("seen_scale", C.c_float), ("_pad3", C.c_int32),
 ]
 
 
@@ -251,7 +252,7 @@ class Op:
     def __init__(self, raw: _Op):
         self.raw = raw
         for f, _ in _Op._fields_:
-            if f not in ("wq", "bias", "sub", "extra", "wh", "w_scale_ch"):
+            if f not in ("wq", "bias", "sub", "extra", "wh", "w_scale_ch", "frozen", "frozen_scale", "seen_scale"):
                 setattr(self, f, getattr(raw, f))
         self.sub = [Op(raw.sub[j]) for j in range(raw.n_sub)]
         self.wq = np.ctypeslib.as_array(raw.wq, shape=(raw.wq_len,)).copy() if raw.wq_len else None
@@ -288,6 +289,40 @@ class Program:
             lib().og_program_free(self._p)
         except Exception:
             pass
+
+    # ---- static calibration (extension; no counterpart in the reference) ----------
+    # One frozen per-tensor scale per Linear input: a Linear has one; an attention
+    # block two (its input, shared by the q / k / v projections, and the attention
+    # output that Wo reads); a SwiGLU block two (its input, shared by gate and up, and
+    # the gated product that the down projection reads).
+    def _calib_targets(self):
+        out = []
+        for i in range(len(self.ops)):
+            raw = self._p.contents.ops[i]
+            if raw.kind == LINEAR:
+                out.append([raw])
+            elif raw.kind == ATTENTION:
+                out += [[raw.sub[0], raw.sub[1], raw.sub[2]], [raw.sub[3]]]
+            elif raw.kind == SWIGLU:
+                out += [[raw.sub[0], raw.sub[1]], [raw.sub[2]]]
+        return out
+
+    def calibrate(self, x, nthreads: int = 1) -> np.ndarray:
+        """Runs x with the reference's dynamic scales and returns, per calibration
+        target, the scale its Linear quantized with (the batch absmax / 127)."""
+        self.set_calibration(None)
+        self.execute(x, nthreads=nthreads)
+        return np.array([t[0].seen_scale for t in self._calib_targets()], np.float32)
+
+    def set_calibration(self, scales) -> None:
+        """Freeze the Linear input scales (None: back to the reference's dynamic scales)."""
+        targets = self._calib_targets()
+        if scales is not None and len(scales) != len(targets):
+            raise ValueError(f"{len(targets)} calibration scales expected, got {len(scales)}")
+        for j, group in enumerate(targets):
+            for raw in group:
+                raw.frozen = 0 if scales is None else 1
+                raw.frozen_scale = 0.0 if scales is None else float(np.float32(scales[j]))
 
     def summary(self, raw_count: int) -> str:
         buf = C.create_string_buffer(1 << 16)

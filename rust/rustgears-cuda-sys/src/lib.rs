@@ -183,6 +183,10 @@ extern "C" {
     pub fn rg_session_op_info(s: *mut rg_session, op: i32, info: *mut rg_op_info) -> rg_status;
     pub fn rg_session_op_weights(s: *mut rg_session, op: i32, wq: *mut i8, cap: i64, bias: *mut f32,
                                  bias_cap: i64) -> rg_status;
+    pub fn rg_session_calibration_targets(s: *mut rg_session, n: *mut i32) -> rg_status;
+    pub fn rg_session_calibrate(s: *mut rg_session, x: *const f32, shape: *const i64, ndim: i32) -> rg_status;
+    pub fn rg_session_set_calibration(s: *mut rg_session, scales: *const f32, n: i32) -> rg_status;
+    pub fn rg_session_get_calibration(s: *mut rg_session, scales: *mut f32, cap: i32) -> rg_status;
     pub fn rg_session_set_trace(s: *mut rg_session, enable: i32) -> rg_status;
     pub fn rg_session_trace_get(s: *mut rg_session, op: i32, item: i32, buf: *mut c_void, cap_bytes: i64,
                                 n_bytes: *mut i64) -> rg_status;

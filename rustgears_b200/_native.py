@@ -89,6 +89,10 @@ SIGNATURES = {
     "rg_session_num_ops": ([_vp, _i32p], _i32),
     "rg_session_op_info": ([_vp, _i32, C.POINTER(OpInfoC)], _i32),
     "rg_session_op_weights": ([_vp, _i32, _i8p, _i64, _f32p, _i64], _i32),
+    "rg_session_calibration_targets": ([_vp, _i32p], _i32),
+    "rg_session_calibrate": ([_vp, _f32p, _i64p, _i32], _i32),
+    "rg_session_set_calibration": ([_vp, _f32p, _i32], _i32),
+    "rg_session_get_calibration": ([_vp, _f32p, _i32], _i32),
     "rg_session_set_trace": ([_vp, _i32], _i32),
     "rg_session_trace_get": ([_vp, _i32, _i32, _vp, _i64, _i64p], _i32),
     "rg_nccl_unique_id": ([C.POINTER(C.c_uint8)], _i32),

@@ -134,6 +134,8 @@ struct CBParams {
   unsigned* amax;          // optional sink of the output's absmax
   int64_t amax_per_image;
   int* err;                // this call's error word: set to 1 when a bounded wait gave up
+  int8_t* out_q;           // calibration extension: i8 output [n, C2 * 49] with the frozen scale
+  const float* q_scale;
 };
 
 __device__ __forceinline__ uint64_t desc_noswz(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -466,6 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_convblock(const CBParams p) {
     const int py = y >> 1, half = y & 1;  // half: which 8 of 16 channels this lane finishes
     const bool pos_ok = py < P2 && j < P2;
     float feat_amax = 0.0f;
+    const float q_inv = p.out_q ? quant_inv(*p.q_scale) : 0.0f;
     for (int it = 0; it < n_it; ++it) {
       const int b = it & 1;
       const uint32_t ph = (it >> 1) & 1;
@@ -518,11 +521,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_convblock(const CBParams p) {
             for (int k = 0; k < 8; ++k) out[k] = half ? best[8 + k] : best[k];
           }
           if (pos_ok) {
-            float* og = p.out + img * (int64_t)(C2 * P2 * P2) + (int64_t)(c0 + half * 8) * (P2 * P2) + py * P2 + j;
+            const int64_t o0 = img * (int64_t)(C2 * P2 * P2) + (int64_t)(c0 + half * 8) * (P2 * P2) + py * P2 + j;
+            if (p.out_q) {  // the next Linear's operand, quantized with its calibrated scale
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              og[k * (P2 * P2)] = out[k];
-              mo = fmaxf(mo, fabsf(out[k]));
+              for (int k = 0; k < 8; ++k) p.out_q[o0 + k * (P2 * P2)] = (int8_t)quant1(out[k], q_inv);
+            } else {
+              float* og = p.out + o0;
+#pragma unroll
+              for (int k = 0; k < 8; ++k) {
+                og[k * (P2 * P2)] = out[k];
+                mo = fmaxf(mo, fabsf(out[k]));
+              }
             }
           }
         }
@@ -571,6 +580,7 @@ void launch_cfg(const ConvBlockArgs& a, int num_sms, cudaStream_t st) {
   p.w1_scale = a.w1_scale; p.w2_scale = a.w2_scale; p.b1 = a.b1; p.b2 = a.b2; p.p1 = a.p1; p.p2 = a.p2;
   p.out = a.out; p.amax = a.amax; p.amax_per_image = a.amax_per_image;
   p.err = a.err;
+  p.out_q = a.out_q; p.q_scale = a.q_scale;
   const int grid = (int)(a.n < num_sms ? a.n : num_sms);
   k_convblock<C2, ACT1, ACT2><<<grid, kThreads, L::SMEM, st>>>(p);
 }

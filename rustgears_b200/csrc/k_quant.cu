@@ -42,7 +42,19 @@ __global__ void __launch_bounds__(kThreads) k_absmax(const float* __restrict__ x
   if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
     const int64_t n4 = n >> 2;
     const float4* x4 = reinterpret_cast<const float4*>(x);
-    for (int64_t i = tid; i < n4; i += stride) {
+    int64_t i = tid;
+    // four independent 16-byte loads in flight per thread before they are folded in
+    for (; i + 3 * stride < n4; i += 4 * stride) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = __ldg(x4 + i + u * stride);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        m = fmaxf(m, fabsf(v[u].x)); m = fmaxf(m, fabsf(v[u].y));
+        m = fmaxf(m, fabsf(v[u].z)); m = fmaxf(m, fabsf(v[u].w));
+      }
+    }
+    for (; i < n4; i += stride) {
       const float4 v = __ldg(x4 + i);
       m = fmaxf(m, fabsf(v.x)); m = fmaxf(m, fabsf(v.y));
       m = fmaxf(m, fabsf(v.z)); m = fmaxf(m, fabsf(v.w));
@@ -55,14 +67,18 @@ __global__ void __launch_bounds__(kThreads) k_absmax(const float* __restrict__ x
 }
 
 // One thread per 16 output bytes of a row.
+// FROZEN: the scale is given (a calibrated scale, extension) instead of derived from
+// the tensor's absmax; values beyond its range clamp to +-127 (quant1).
+template <bool FROZEN>
 __global__ void __launch_bounds__(kThreads) k_quantize_rows(const float* __restrict__ x, int64_t rows,
                                                             int64_t k, int64_t ldq,
                                                             const unsigned* __restrict__ amax_bits,
+                                                            const float* __restrict__ frozen_scale,
                                                             int8_t* __restrict__ q,
                                                             float* __restrict__ scale_out) {
-  const float scale = quant_scale(__uint_as_float(*amax_bits));
+  const float scale = FROZEN ? *frozen_scale : quant_scale(__uint_as_float(*amax_bits));
   const float inv = quant_inv(scale);
-  if (blockIdx.x == 0 && threadIdx.x == 0 && scale_out) *scale_out = scale;
+  if (!FROZEN && blockIdx.x == 0 && threadIdx.x == 0 && scale_out) *scale_out = scale;
   const int64_t chunks = ldq >> 4;
   const int64_t total = rows * chunks;
   const bool vec = ((k & 3) == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
@@ -378,8 +394,16 @@ void launch_quantize_rows(const float* x, int64_t rows, int64_t k, int64_t ldq,
                           const unsigned* amax_bits, int8_t* q, float* scale_out, cudaStream_t st) {
   const int64_t work = rows * (ldq >> 4);
   if (work <= 0) return;
-  k_quantize_rows<<<grid_for(work, kThreads, 148 * 32), kThreads, 0, st>>>(x, rows, k, ldq, amax_bits, q,
-                                                                           scale_out);
+  k_quantize_rows<false><<<grid_for(work, kThreads, 148 * 32), kThreads, 0, st>>>(x, rows, k, ldq, amax_bits,
+                                                                                  nullptr, q, scale_out);
+}
+
+void launch_quantize_rows_frozen(const float* x, int64_t rows, int64_t k, int64_t ldq, const float* scale, int8_t* q,
+                                 cudaStream_t st) {
+  const int64_t work = rows * (ldq >> 4);
+  if (work <= 0) return;
+  k_quantize_rows<true><<<grid_for(work, kThreads, 148 * 32), kThreads, 0, st>>>(x, rows, k, ldq, nullptr, scale, q,
+                                                                                 nullptr);
 }
 
 // Per-image absmax over the pixels a strided conv reads, VEC consecutive columns per

@@ -92,9 +92,14 @@ __global__ void __launch_bounds__(kThreads) k_embedding(const float* __restrict_
 // adds the squares serially, then all threads normalise from shared memory.  Several
 // blocks per SM overlap one block's serial sums with the others' copies.
 // ---------------------------------------------------------------------------
+// yq (calibration extension): instead of y, the output quantized with the frozen scale
+// *q_scale into i8 rows of ldq bytes (columns d..ldq zero).
 __global__ void __launch_bounds__(kThreads) k_rmsnorm(const float* __restrict__ x, int64_t rows, int32_t d,
                                                       int32_t rpb, bool vec, const float* __restrict__ w, float eps,
-                                                      float inv_d, float* __restrict__ y, unsigned* amax) {
+                                                      float inv_d, float* __restrict__ y, unsigned* amax,
+                                                      int8_t* __restrict__ yq, int64_t ldq,
+                                                      const float* __restrict__ q_scale) {
+  const float qinv = yq ? quant_inv(*q_scale) : 0.0f;
   extern __shared__ float xs[];  // [rpb][d + 1]
   __shared__ float rms_s[32];
   const int ld = d + 1;
@@ -126,6 +131,12 @@ __global__ void __launch_bounds__(kThreads) k_rmsnorm(const float* __restrict__ 
     __syncthreads();
     for (int r = 0; r < nr; ++r) {
       const float rr = rms_s[r];
+      if (yq) {
+        int8_t* qr = yq + (r0 + r) * ldq;
+        for (int c = threadIdx.x; c < ldq; c += kThreads)
+          qr[c] = c < d ? (int8_t)quant1(__fmul_rn(__fdiv_rn(xs[r * ld + c], rr), __ldg(w + c)), qinv) : 0;
+        continue;
+      }
       float* yr = y + (r0 + r) * d;
       for (int c = threadIdx.x; c < d; c += kThreads) {
         const float v = __fmul_rn(__fdiv_rn(xs[r * ld + c], rr), __ldg(w + c));
@@ -148,16 +159,27 @@ __device__ __forceinline__ float swiglu1(float g, float u, ExpTablePtr et) {
   return __fmul_rn(__fmul_rn(g, sig), u);
 }
 
+// yq (calibration extension): instead of y, the product quantized with the frozen
+// scale *q_scale into i8 rows of ldq bytes (columns h..ldq zero).
 __global__ void __launch_bounds__(kThreads) k_swiglu_mul(const float* __restrict__ gu, int64_t rows, int32_t h,
-                                                         bool vec, float* __restrict__ y, unsigned* amax) {
+                                                         bool vec, float* __restrict__ y, unsigned* amax,
+                                                         int8_t* __restrict__ yq, int64_t ldq,
+                                                         const float* __restrict__ q_scale) {
   __shared__ uint64_t tab[32];
   if (threadIdx.x < 32) tab[threadIdx.x] = ExpTableConst{}(threadIdx.x);
   __syncthreads();
   const ExpTablePtr et{tab};
+  const float qinv = yq ? quant_inv(*q_scale) : 0.0f;
   float m = 0.0f;
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const float* gr = gu + r * 2 * h;
     const float* ur = gr + h;
+    if (yq) {
+      int8_t* qr = yq + r * ldq;
+      for (int64_t c = threadIdx.x; c < ldq; c += kThreads)
+        qr[c] = c < h ? (int8_t)quant1(swiglu1(__ldg(gr + c), __ldg(ur + c), et), qinv) : 0;
+      continue;
+    }
     float* yr = y + r * h;
     if (vec) {  // h % 4 == 0 and gu, y 16-byte aligned
       for (int32_t c = threadIdx.x; c < (h >> 2); c += kThreads) {
@@ -556,7 +578,7 @@ void launch_embedding(const float* ids, int64_t n, const float* table, int64_t v
 }
 
 rg_status launch_rmsnorm(const float* x, int64_t rows, int32_t d, const float* w, float eps, float inv_d, float* y,
-                         AmaxSink amax, cudaStream_t st) {
+                         AmaxSink amax, cudaStream_t st, int8_t* yq, int64_t ldq, const float* q_scale) {
   if (rows <= 0) return RG_OK;
   const int32_t rpb = (int32_t)std::max<int64_t>(1, std::min<int64_t>(32, 16384 / d));
   const size_t smem = (size_t)rpb * (d + 1) * sizeof(float);
@@ -566,15 +588,18 @@ rg_status launch_rmsnorm(const float* x, int64_t rows, int32_t d, const float* w
     return set_last_error(RG_ERR_CUDA, "RMSNorm: shared-memory opt-in failed");
   const bool vec = (d & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
   const int64_t blocks = std::min<int64_t>((rows + rpb - 1) / rpb, 148 * 32);
-  k_rmsnorm<<<(unsigned)blocks, kThreads, smem, st>>>(x, rows, d, rpb, vec, w, eps, inv_d, y, amax.ptr);
+  k_rmsnorm<<<(unsigned)blocks, kThreads, smem, st>>>(x, rows, d, rpb, vec, w, eps, inv_d, y, amax.ptr, yq, ldq,
+                                                       q_scale);
   return RG_OK;
 }
 
-void launch_swiglu_mul(const float* gu, int64_t rows, int32_t h, float* y, AmaxSink amax, cudaStream_t st) {
+void launch_swiglu_mul(const float* gu, int64_t rows, int32_t h, float* y, AmaxSink amax, cudaStream_t st,
+                       int8_t* yq, int64_t ldq, const float* q_scale) {
   if (rows <= 0 || h <= 0) return;
   // the vector path needs 16-byte aligned rows; a caller's odd base takes the scalar one
   const bool vec = (h & 3) == 0 && ((reinterpret_cast<uintptr_t>(gu) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
-  k_swiglu_mul<<<(unsigned)std::min<int64_t>(rows, 148 * 64), kThreads, 0, st>>>(gu, rows, h, vec, y, amax.ptr);
+  k_swiglu_mul<<<(unsigned)std::min<int64_t>(rows, 148 * 64), kThreads, 0, st>>>(gu, rows, h, vec, y, amax.ptr, yq,
+                                                                                  ldq, q_scale);
 }
 
 bool attention_fast_eligible(int32_t t, int32_t dh, const float* qkv, int64_t ld, const float* out, int64_t ldo) {

@@ -209,6 +209,18 @@ struct Session {
   std::vector<TraceRec> traces;
   bool used_tc = false;  // a tcgen05 kernel ran since the last error-word check
   bool used_embed = false;  // an embedding gather ran since the last error-word check
+  // Static calibration (extension, no counterpart in the reference): one frozen
+  // per-tensor scale per Linear input -- a Linear has one; an attention or SwiGLU block
+  // two (its input, and the inner activation its second projection reads).  With
+  // scales installed, those Linears quantize with them (clamping beyond the calibrated
+  // range) instead of the batch absmax, need no absmax pass or all-reduce, and the
+  // producers that can (the fused CNN block, RMSNorm, the SwiGLU gate product) write
+  // the Linear's i8 operand directly.
+  std::vector<int32_t> calib_off;  // per op: index of its first scale, or -1
+  int32_t calib_targets = 0;
+  bool calibrated = false;
+  std::vector<float> calib;
+  DevBuf d_calib;
   // multi-GPU
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1;
@@ -776,6 +788,10 @@ struct RunPlan {
   // direct-3x3 producer can take their absmax into its epilogue), else -1; and the
   // reverse map, producer op -> shortcut op
   std::vector<int> amax2_src, amax2_for;
+  // calibrated sessions: i8_out[j] = the consumer op whose i8 operand op j writes
+  // directly (-1: none); i8_in[i]: op i's first Linear finds its operand written
+  std::vector<int> i8_out;
+  std::vector<uint8_t> i8_in;
 };
 
 // Ops that leave the main-path tensor as it is (reshape, saving a block input, a
@@ -890,6 +906,27 @@ static rg_status make_plan(const Session& s, const int64_t* shape, int32_t ndim,
       P.stem_start[i] = 1;
       ++i;
     }
+  P.i8_out.assign(n, -1);
+  P.i8_in.assign(n, 0);
+  if (s.calibrated) {
+    for (size_t i = 0; i < n; ++i) {
+      if (s.calib_off[i] < 0) continue;
+      P.amax_src[i] = -1;  // frozen scale: the producer computes no absmax for it
+      if (s.trace || (s.flags & RG_SESSION_NO_FUSION)) continue;
+      int j = (int)i - 1;
+      while (j >= 0 && main_path_noop(s.ops[(size_t)j].kind)) --j;
+      if (j < 0) continue;
+      const Op& c = s.ops[i];
+      if (c.kind == RG_LAYER_LINEAR && j >= 3 && P.block_start[(size_t)j - 3] && c.kpad == c.in_f) {
+        P.i8_out[(size_t)j - 3] = (int)i;  // the fused block writes the Linear's operand
+        P.i8_in[i] = 1;
+      } else if ((c.kind == RG_LAYER_ATTENTION || c.kind == RG_LAYER_SWIGLU) &&
+                 s.ops[(size_t)j].kind == RG_LAYER_RMSNORM) {
+        P.i8_out[(size_t)j] = (int)i;      // RMSNorm writes the block's projection operand
+        P.i8_in[i] = 1;
+      }
+    }
+  }
   return RG_OK;
 }
 
@@ -928,21 +965,16 @@ static bool feed_chunked(const Session& s, const RunPlan& P) {
   return !s.ops.empty() && P.block_start[0] && !s.trace && P.shapes[0].in[0] >= 2 * kFeedMinChunk;
 }
 
-// One INT8 Linear inside an extension op: the f32 input quantized with the per-tensor
-// scale of absmax *am (first taken as the max over all ranks), then the GEMM; out is
-// [rows, lin.out_f] f32, its absmax optionally sent to `sink`.
-static rg_status run_inner_linear(Session& s, const Op& lin, const float* src, int64_t rows, unsigned* am,
-                                  float* sc, float* out, AmaxSink sink, cudaStream_t st, int32_t& launches) {
-  if (s.comm && s.world > 1) RG_NCCL_TRY(ncclAllReduce(am, am, 1, ncclUint32, ncclMax, s.comm, st));
-  int8_t* q = s.qbuf.as<int8_t>();
-  launch_quantize_rows(src, rows, lin.in_f, lin.kpad, am, q, sc, st);
-  ++launches;
-  RG_LAUNCHED("quantize_rows");
+// The GEMM of one INT8 Linear inside an extension op on its quantized operand q
+// [rows, lin.kpad] with activation scale *a_scale; out is [rows, lin.out_f] f32, its
+// absmax optionally sent to `sink`.
+static rg_status run_gemm_q(Session& s, const Op& lin, const int8_t* q, int64_t rows, const float* a_scale, float* out,
+                            AmaxSink sink, cudaStream_t st, int32_t& launches) {
   GemmArgs g;
   g.a = q; g.lda = lin.kpad;
   g.m = rows; g.n = lin.out_f; g.k = lin.kpad;
   g.w = lin.d_w.as<int8_t>(); g.ldb = lin.kpad;
-  g.a_scale = sc;
+  g.a_scale = a_scale;
   g.w_scale = lin.w_scale;
   g.w_scale_ch = lin.w_scale_ch.empty() ? nullptr : lin.d_wsc.as<float>();
   g.bias = lin.d_bias.as<float>();
@@ -965,6 +997,18 @@ static rg_status run_inner_linear(Session& s, const Op& lin, const float* src, i
   ++launches;
   RG_LAUNCHED(tc ? "gemm_tc" : narrow ? "gemm_narrow" : "gemm_simt");
   return RG_OK;
+}
+
+// One INT8 Linear inside an extension op: the f32 input quantized with the per-tensor
+// scale of absmax *am (first taken as the max over all ranks), then the GEMM.
+static rg_status run_inner_linear(Session& s, const Op& lin, const float* src, int64_t rows, unsigned* am,
+                                  float* sc, float* out, AmaxSink sink, cudaStream_t st, int32_t& launches) {
+  if (s.comm && s.world > 1) RG_NCCL_TRY(ncclAllReduce(am, am, 1, ncclUint32, ncclMax, s.comm, st));
+  int8_t* q = s.qbuf.as<int8_t>();
+  launch_quantize_rows(src, rows, lin.in_f, lin.kpad, am, q, sc, st);
+  ++launches;
+  RG_LAUNCHED("quantize_rows");
+  return run_gemm_q(s, lin, q, rows, sc, out, sink, st, launches);
 }
 
 // Runs the program on device buffers. x_dev is read only (with a HostFeed it is
@@ -1100,6 +1144,10 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
       float* bdst = (i + 3 + 1 == n && y_dev) ? y_dev : dst;
       cb.out = bdst;
       cb.err = s.errw.as<int>();
+      if (P.i8_out[i] >= 0) {  // calibrated: the block writes the next Linear's i8 operand
+        cb.out_q = s.qbuf.as<int8_t>();
+        cb.q_scale = s.d_calib.as<float>() + s.calib_off[(size_t)P.i8_out[i]];
+      }
       const int bcons = find_consumer(s, i + 3);
       if (bcons >= 0 && P.amax_src[(size_t)bcons] == (int)(i + 3)) {
         cb.amax = amax + P.amax_off[(size_t)bcons];
@@ -1120,6 +1168,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
           cc.x = xs + off * img_in;
           cc.n = cnt;
           cc.out = bdst + off * img_out;
+          if (cb.out_q) cc.out_q = cb.out_q + off * img_out;
           if (cb.amax && cb.amax_per_image) cc.amax = cb.amax + off;
           launch_convblock(cc, s.num_sms, st);
           ++launches;
@@ -1247,7 +1296,21 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         g.wait_ns = g_tc_wait_ns.load();
         g.starve = g_tc_starve.load();
         bool fused_q = false;
-        if (op.kind == RG_LAYER_LINEAR) {
+        // a calibrated Linear's frozen activation scale (device), else null
+        const float* frozen = s.calibrated && s.calib_off[i] >= 0 ? s.d_calib.as<float>() + s.calib_off[i] : nullptr;
+        if (op.kind == RG_LAYER_LINEAR && frozen) {
+          const int64_t rows = os.in_elems / op.in_f;
+          g.conv = false;
+          g.m = rows; g.n = op.out_f; g.k = op.kpad;
+          g.rows_per_scale = 0;
+          g.out_l = 0;
+          if (!P.i8_in[i]) {  // (else its producer wrote the operand)
+            launch_quantize_rows_frozen(cur, rows, op.in_f, op.kpad, frozen, q, st);
+            ++launches;
+            RG_LAUNCHED("quantize_rows");
+          }
+          g.a = q; g.lda = op.kpad;
+        } else if (op.kind == RG_LAYER_LINEAR) {
           const int64_t rows = os.in_elems / op.in_f;
           if (P.amax_src[i] < 0) { launch_absmax(cur, os.in_elems, my_amax, st); ++launches; RG_LAUNCHED("absmax"); }
           if (s.comm && s.world > 1)
@@ -1327,7 +1390,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
           g.out_l = L;
         }
         g.w = op.d_w.as<int8_t>(); g.ldb = op.kpad;
-        g.a_scale = my_scale;
+        g.a_scale = frozen ? frozen : my_scale;
         g.w_scale = op.w_scale;
         g.w_scale_ch = op.w_scale_ch.empty() ? nullptr : op.d_wsc.as<float>();
         g.bias = op.d_bias.as<float>();
@@ -1401,7 +1464,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         RG_LAUNCHED(conv3 ? "conv3x3" : conv_tc ? "conv_tc" : tc ? "gemm_tc" : narrow ? "gemm_narrow" : "gemm_simt");
         if (s.trace) {
           TraceRec& t = s.traces[i];
-          RG_TRY(d2h_vec(t.scales, my_scale, P.amax_slots[i], st));
+          RG_TRY(d2h_vec(t.scales, frozen ? frozen : my_scale, P.amax_slots[i], st));
           RG_TRY(d2h_vec(t.acc, s.accbuf.p, os.out_elems, st));
           if (op.kind == RG_LAYER_LINEAR) {
             const int64_t rows = os.in_elems / op.in_f;
@@ -1482,8 +1545,15 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         break;
       case RG_LAYER_RMSNORM:
         // mean_dim multiplies the sum by 1/d (tensor/ops.rs:755-758)
-        RG_TRY(launch_rmsnorm(cur, os.in_elems / op.in_f, op.in_f, op.d_ext.as<float>(), op.param,
-                              1.0f / (float)op.in_f, dst, sink, st));
+        if (P.i8_out[i] >= 0) {  // calibrated: the consumer block's first projection operand
+          const size_t c = (size_t)P.i8_out[i];
+          RG_TRY(launch_rmsnorm(cur, os.in_elems / op.in_f, op.in_f, op.d_ext.as<float>(), op.param,
+                                1.0f / (float)op.in_f, nullptr, AmaxSink(), st, s.qbuf.as<int8_t>(),
+                                s.ops[c].subs[0].kpad, s.d_calib.as<float>() + s.calib_off[c]));
+        } else {
+          RG_TRY(launch_rmsnorm(cur, os.in_elems / op.in_f, op.in_f, op.d_ext.as<float>(), op.param,
+                                1.0f / (float)op.in_f, dst, sink, st));
+        }
         ++launches;
         RG_LAUNCHED("rmsnorm");
         cur = dst;
@@ -1493,24 +1563,46 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         unsigned* am = amax + P.amax_off[i];  // [0]: the op's input, [1]: the inner activation
         float* sc = scales + P.amax_off[i];
         const int64_t rows = os.in_elems / op.in_f;
-        if (P.amax_src[i] < 0) { launch_absmax(cur, os.in_elems, am, st); ++launches; RG_LAUNCHED("absmax"); }
+        // calibrated: frozen scales fz[0] (the input) and fz[1] (the inner activation)
+        const float* fz = s.calibrated ? s.d_calib.as<float>() + s.calib_off[i] : nullptr;
+        int8_t* q = s.qbuf.as<int8_t>();
+        if (!fz && P.amax_src[i] < 0) { launch_absmax(cur, os.in_elems, am, st); ++launches; RG_LAUNCHED("absmax"); }
         AmaxSink inner;
-        inner.ptr = am + 1;
+        inner.ptr = fz ? nullptr : am + 1;
         float* e0 = s.ext0.as<float>();
         float* e1 = s.ext1.as<float>();
-        RG_TRY(run_inner_linear(s, op.subs[0], cur, rows, am, sc, e0, AmaxSink(), st, launches));
+        if (fz) {
+          if (!P.i8_in[i]) {
+            launch_quantize_rows_frozen(cur, rows, op.in_f, op.subs[0].kpad, fz, q, st);
+            ++launches;
+            RG_LAUNCHED("quantize_rows");
+          }
+          RG_TRY(run_gemm_q(s, op.subs[0], q, rows, fz, e0, AmaxSink(), st, launches));
+        } else {
+          RG_TRY(run_inner_linear(s, op.subs[0], cur, rows, am, sc, e0, AmaxSink(), st, launches));
+        }
         if (op.kind == RG_LAYER_ATTENTION) {
           const int32_t d = op.in_f, heads = op.out_f, dh = d / heads;
           const float scale = 1.0f / std::sqrt((float)dh);  // attention.rs: mul_scalar(1 / sqrt(dh))
           RG_TRY(launch_attention(e0, 3 * (int64_t)d, os.in[0], (int32_t)os.in[1], heads, dh, scale, e1, d, inner, st));
           ++launches;
           RG_LAUNCHED("attention");
+          if (fz) {
+            launch_quantize_rows_frozen(e1, rows, d, op.subs[1].kpad, fz + 1, q, st);
+            ++launches;
+            RG_LAUNCHED("quantize_rows");
+          }
+        } else if (fz) {  // the gate product written as the down projection's i8 operand
+          launch_swiglu_mul(e0, rows, op.out_f, nullptr, AmaxSink(), st, q, op.subs[1].kpad, fz + 1);
+          ++launches;
+          RG_LAUNCHED("swiglu_mul");
         } else {
           launch_swiglu_mul(e0, rows, op.out_f, e1, inner, st);
           ++launches;
           RG_LAUNCHED("swiglu_mul");
         }
-        RG_TRY(run_inner_linear(s, op.subs[1], e1, rows, am + 1, sc + 1, dst, sink, st, launches));
+        if (fz) RG_TRY(run_gemm_q(s, op.subs[1], q, rows, fz + 1, dst, sink, st, launches));
+        else RG_TRY(run_inner_linear(s, op.subs[1], e1, rows, am + 1, sc + 1, dst, sink, st, launches));
         cur = dst;
         break;
       }
@@ -1775,6 +1867,14 @@ rg_status rg_session_create(const rg_layer_spec* layers, int32_t n_layers, const
   RG_TRY(s.errw.ensure(2 * sizeof(int)));
   RG_CUDA_TRY(cudaMemset(s.errw.p, 0, 2 * sizeof(int)));
   RG_TRY(compile(s, layers, n_layers));
+  // calibration targets: one per Linear input (two per attention / SwiGLU block)
+  s.calib_off.assign(s.ops.size(), -1);
+  for (size_t i = 0; i < s.ops.size() && s.precision == RG_PREC_INT8; ++i) {
+    const int32_t k = s.ops[i].kind;
+    if (k != RG_LAYER_LINEAR && k != RG_LAYER_ATTENTION && k != RG_LAYER_SWIGLU) continue;
+    s.calib_off[i] = s.calib_targets;
+    s.calib_targets += k == RG_LAYER_LINEAR ? 1 : 2;
+  }
   *out = h.release();
   return RG_OK;
 }
@@ -2110,6 +2210,88 @@ rg_status rg_session_trace_get(rg_session* h, int32_t op, int32_t item, void* bu
     if (bytes) memcpy(buf, src, (size_t)bytes);
   }
   return RG_OK;
+}
+
+// ---- static calibration (extension) ---------------------------------------------
+// Installs (n > 0) or clears (n == 0) the frozen scales; the session's captured
+// program no longer matches and is released.  Caller holds s.mu.
+static rg_status set_calibration_locked(Session& s, const float* scales, int32_t n) {
+  if (n != 0 && (!scales || n != s.calib_targets))
+    return fail(RG_ERR_INVALID_ARG, "the session has %d calibration targets, got %d scales", s.calib_targets, n);
+  for (int32_t j = 0; j < n; ++j)
+    if (!(scales[j] > 0.0f) || !std::isfinite(scales[j]))
+      return fail(RG_ERR_INVALID_ARG, "calibration scale %d is %g: scales must be finite and positive", j,
+                  (double)scales[j]);
+  RG_CUDA_TRY(cudaSetDevice(s.device));
+  RG_CUDA_TRY(cudaStreamSynchronize(s.stream));
+  if (s.graph.exec) cudaGraphExecDestroy(s.graph.exec);
+  s.graph = Session::Graph();
+  if (n == 0) {
+    s.calibrated = false;
+    s.calib.clear();
+    return RG_OK;
+  }
+  s.calib.assign(scales, scales + n);
+  RG_TRY(s.d_calib.ensure((size_t)n * sizeof(float)));
+  RG_CUDA_TRY(cudaMemcpy(s.d_calib.p, scales, (size_t)n * sizeof(float), cudaMemcpyHostToDevice));
+  s.calibrated = true;
+  return RG_OK;
+}
+
+rg_status rg_session_calibration_targets(rg_session* h, int32_t* n) {
+  if (!h || !n) return fail(RG_ERR_INVALID_ARG, "null argument");
+  *n = h->s.calib_targets;
+  return RG_OK;
+}
+
+rg_status rg_session_set_calibration(rg_session* h, const float* scales, int32_t n) {
+  if (!h || n < 0) return fail(RG_ERR_INVALID_ARG, "null argument");
+  Session& s = h->s;
+  if (s.precision != RG_PREC_INT8) return fail(RG_ERR_UNSUPPORTED, "static calibration is for Npu(Int8) sessions");
+  std::lock_guard<std::mutex> lock(s.mu);
+  return set_calibration_locked(s, scales, n);
+}
+
+rg_status rg_session_get_calibration(rg_session* h, float* scales, int32_t cap) {
+  if (!h || (!scales && cap > 0)) return fail(RG_ERR_INVALID_ARG, "null argument");
+  Session& s = h->s;
+  std::lock_guard<std::mutex> lock(s.mu);
+  if (!s.calibrated) return fail(RG_ERR_INVALID_ARG, "the session is not calibrated");
+  if (cap < s.calib_targets) return fail(RG_ERR_INVALID_ARG, "%d scales, capacity %d", s.calib_targets, cap);
+  std::copy(s.calib.begin(), s.calib.end(), scales);
+  return RG_OK;
+}
+
+rg_status rg_session_calibrate(rg_session* h, const float* x, const int64_t* shape, int32_t ndim) {
+  if (!h || !x || !shape || ndim < 1 || ndim > 8) return fail(RG_ERR_INVALID_ARG, "bad calibration input");
+  Session& s = h->s;
+  if (s.precision != RG_PREC_INT8) return fail(RG_ERR_UNSUPPORTED, "static calibration is for Npu(Int8) sessions");
+  {
+    std::lock_guard<std::mutex> lock(s.mu);
+    RG_TRY(set_calibration_locked(s, nullptr, 0));
+  }
+  // a run with the reference's dynamic scales leaves every Linear input's absmax (over
+  // all ranks, when a communicator is attached) in its slot of the amax buffer
+  int64_t ys[8];
+  int32_t ynd = 0;
+  RG_TRY(rg_session_output_shape(h, shape, ndim, ys, &ynd));
+  int64_t out_elems = 1;
+  for (int32_t i = 0; i < ynd; ++i) out_elems *= ys[i];
+  std::vector<float> y((size_t)std::max<int64_t>(out_elems, 1));
+  RG_TRY(run_impl(h, x, true, shape, ndim, y.data(), true, out_elems, ys, &ynd, nullptr, false));
+  std::lock_guard<std::mutex> lock(s.mu);
+  RunPlan P;
+  RG_TRY(make_plan(s, shape, ndim, P));
+  std::vector<uint32_t> bits((size_t)std::max<int64_t>(P.total_slots, 1), 0u);
+  if (P.total_slots) RG_CUDA_TRY(cudaMemcpy(bits.data(), s.amax.p, (size_t)P.total_slots * 4, cudaMemcpyDeviceToHost));
+  std::vector<float> sc((size_t)s.calib_targets);
+  for (size_t i = 0; i < s.ops.size(); ++i) {
+    if (s.calib_off[i] < 0) continue;
+    const int parts = s.ops[i].kind == RG_LAYER_LINEAR ? 1 : 2;
+    for (int j = 0; j < parts; ++j)  // QuantTensor::from_f32's scale (quantize.rs:19-20)
+      sc[(size_t)(s.calib_off[i] + j)] = quant_scale<false>(u2f(bits[(size_t)(P.amax_off[i] + j)]));
+  }
+  return set_calibration_locked(s, sc.data(), s.calib_targets);
 }
 
 rg_status rg_nccl_unique_id(uint8_t id[128]) {

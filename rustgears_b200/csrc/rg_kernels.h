@@ -22,6 +22,9 @@ void launch_absmax(const float* x, int64_t n, unsigned* amax_bits, cudaStream_t 
 // x [rows,k] f32 -> q [rows,ldq] i8 with the per-tensor scale from amax_bits; scale_out[0] = scale.
 void launch_quantize_rows(const float* x, int64_t rows, int64_t k, int64_t ldq,
                           const unsigned* amax_bits, int8_t* q, float* scale_out, cudaStream_t st);
+// The same with a given (calibrated) scale *scale; values beyond its range clamp to +-127.
+void launch_quantize_rows_frozen(const float* x, int64_t rows, int64_t k, int64_t ldq, const float* scale, int8_t* q,
+                                 cudaStream_t st);
 // Per-image absmax over the pixels a conv actually reads (row/col coverage masks; NULL = all).
 void launch_image_absmax(const float* x, int64_t n, int32_t c, int32_t h, int32_t w,
                          const uint8_t* row_cov, const uint8_t* col_cov, unsigned* amax_bits,
@@ -216,6 +219,10 @@ struct ConvBlockArgs {
   unsigned* amax = nullptr;          // optional absmax sink of out
   int64_t amax_per_image = 0;
   int* err = nullptr;                // this call's error word (required)
+  // calibration extension: out_q non-null writes the output quantized with the frozen
+  // scale *q_scale as i8 [n, c2 * (h/4) * (w/4)] instead of the f32 out
+  int8_t* out_q = nullptr;
+  const float* q_scale = nullptr;
 };
 bool convblock_supported(int c0, int c1, int c2, int h, int w, int act1, int act2);
 void launch_convblock(const ConvBlockArgs& a, int num_sms, cudaStream_t st);
@@ -240,10 +247,14 @@ void launch_softmax(const float* x, int64_t outer, int64_t last, float* y, AmaxS
 // the caller's device error word *err to 1.
 void launch_embedding(const float* ids, int64_t n, const float* table, int64_t v, int32_t d, float* y,
                       AmaxSink amax, int* err, cudaStream_t st);
+// yq non-null (calibration extension): the output is written quantized with the frozen
+// scale *q_scale into i8 rows of ldq bytes (zero-padded) instead of y.
 rg_status launch_rmsnorm(const float* x, int64_t rows, int32_t d, const float* w, float eps, float inv_d, float* y,
-                         AmaxSink amax, cudaStream_t st);
-// gu [rows, 2h] = [g | u] -> y [rows, h] = (g * sigmoid(g)) * u
-void launch_swiglu_mul(const float* gu, int64_t rows, int32_t h, float* y, AmaxSink amax, cudaStream_t st);
+                         AmaxSink amax, cudaStream_t st, int8_t* yq = nullptr, int64_t ldq = 0,
+                         const float* q_scale = nullptr);
+// gu [rows, 2h] = [g | u] -> y [rows, h] = (g * sigmoid(g)) * u (or yq, as for RMSNorm)
+void launch_swiglu_mul(const float* gu, int64_t rows, int32_t h, float* y, AmaxSink amax, cudaStream_t st,
+                       int8_t* yq = nullptr, int64_t ldq = 0, const float* q_scale = nullptr);
 // qkv [b*t, ld] (q, k, v of head hh at columns hh*dh, d + hh*dh, 2d + hh*dh) ->
 // out [b*t, ldo] with the heads merged; scores scaled by `scale` before the softmax.
 rg_status launch_attention(const float* qkv, int64_t ld, int64_t b, int32_t t, int32_t heads, int32_t dh,

@@ -336,6 +336,42 @@ class InferenceSession:
             b.ctypes.data_as(C.POINTER(C.c_float)), b.size))
         return wq, b
 
+    # -- static calibration (extension; no counterpart in the reference) -------------
+    def calibration_targets(self) -> int:
+        """Frozen scales a calibration holds: one per Linear, two per attention / SwiGLU block."""
+        n = C.c_int32(0)
+        _native.check(_native.lib().rg_session_calibration_targets(self._h, C.byref(n)))
+        return n.value
+
+    def calibrate(self, x) -> np.ndarray:
+        """Runs x with the reference's dynamic scales and freezes every Linear input's
+        scale; later runs quantize with them (no absmax pass, no all-reduce; values
+        beyond the calibrated range clamp).  Returns the frozen scales."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        shape = np.asarray(x.shape, np.int64)
+        _native.check(_native.lib().rg_session_calibrate(self._h, x.ctypes.data_as(C.POINTER(C.c_float)),
+                                                         shape.ctypes.data_as(C.POINTER(C.c_int64)), x.ndim))
+        return self.calibration()
+
+    def set_calibration(self, scales) -> None:
+        """Install frozen scales, or ``None`` for the reference's dynamic scales."""
+        if scales is None:
+            _native.check(_native.lib().rg_session_set_calibration(self._h, None, 0))
+            return
+        sc = np.ascontiguousarray(scales, dtype=np.float32)
+        _native.check(_native.lib().rg_session_set_calibration(self._h, sc.ctypes.data_as(C.POINTER(C.c_float)),
+                                                               sc.size))
+
+    def calibration(self):
+        """The frozen scales, or ``None`` when the session uses dynamic scales."""
+        n = self.calibration_targets()
+        out = np.empty(max(n, 1), np.float32)
+        st = _native.lib().rg_session_get_calibration(self._h, out.ctypes.data_as(C.POINTER(C.c_float)), out.size)
+        if st == _native.RG_ERR_INVALID_ARG and "not calibrated" in _native.last_error():
+            return None
+        _native.check(st)
+        return out[:n].copy()
+
     def set_trace(self, enable: bool) -> None:
         _native.check(_native.lib().rg_session_set_trace(self._h, int(enable)))
 

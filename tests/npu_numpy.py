@@ -265,18 +265,25 @@ def summary(prog) -> str:
 
 
 # ---- execute ----------------------------------------------------------------------------
-def execute_traced(prog, x):
+def execute_traced(prog, x, frozen=None):
     """NpuProgram::execute on the Int8 arm; returns (y, [per-op dict(label, y, and for
-    Linear / Conv2d: scales, aq, acc)])."""
+    Linear / Conv2d: scales, aq, acc)]).  `frozen` (the static-calibration extension):
+    one scale per Linear, in op order, used instead of the batch absmax's."""
     data = np.asarray(x, F)
     trace = []
+    li = 0
     for op in prog["ops"]:
         rec = {"label": label(op)}
         k = op["kind"]
         if k == LINEAR:
             rows = data.size // op["fin"]
             a2 = data.reshape(rows, op["fin"])
-            aq, sa = quantize(a2)                 # per tensor over the whole batch
+            if frozen is None:
+                aq, sa = quantize(a2)             # per tensor over the whole batch
+            else:
+                sa = F(frozen[li])
+                aq = quantize_with(a2, sa)        # the same rounding and clamp, a fixed scale
+            li += 1
             aq = aq.reshape(rows, op["fin"])
             y, acc = gemm_fused(aq, sa, op)
             rec.update(scales=np.array([sa], F), aq=aq, acc=acc)

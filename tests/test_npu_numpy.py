@@ -64,3 +64,26 @@ def test_special_values_agree(oracle_lib, what):
     ref, _, _ = oracle.Program(layers).execute(x)
     y, _ = npn.execute_traced(npn.compile_program(layers), x)
     assert_same(y, ref, what)
+
+
+@pytest.mark.parametrize("name", ["c1_mlp_64", "c2_cnn_4", "acts_mlp", "affine_first", "integration"])
+def test_static_calibration_restatements_agree(oracle_lib, name):
+    """The calibration extension: the oracle's calibration scales equal the numpy
+    restatement's dynamic Linear scales on the calibration batch, and both run another
+    batch (twice the range, so values clamp) with those scales frozen, bit for bit."""
+    from oracle import oracle
+    layers, x = configs.CASES[name]()
+    prog = oracle.Program(layers)
+    scales = prog.calibrate(x)
+    npp = npn.compile_program(layers)
+    _, trace = npn.execute_traced(npp, x)
+    dyn = np.array([t["scales"][0] for t, op in zip(trace, npp["ops"]) if op["kind"] == npn.LINEAR], np.float32)
+    assert_same(scales, dyn, "calibration scales")
+    x2 = (x * np.float32(2.0)).astype(np.float32)
+    prog.set_calibration(scales)
+    y_c, _, _ = prog.execute(x2)
+    y_n, tr2 = npn.execute_traced(npp, x2, frozen=scales)
+    assert_same(y_c, y_n, f"{name} frozen")
+    assert any(np.abs(t["aq"]).max() == 127 for t in tr2 if "aq" in t)
+    prog.set_calibration(None)
+    assert_same(prog.execute(x2)[0], npn.execute_traced(npp, x2)[0], f"{name} dynamic again")
