@@ -53,8 +53,10 @@ L2_FLUSH_BYTES = 256 << 20
 # captured from: once that source changes the line reports null (with the reason)
 # instead of a figure that no longer describes the kernel.
 MEASURED_TRAFFIC = {
-    ("c2", 32768): dict(bytes=102837504 + 146597376, source="rustgears_b200/csrc/k_convblock.cu",
-                        sha256="430322660bc351e2950c0f81d0e1bf8eefe4b0b190d1b69b2d007565c6f7b7b7"),
+    ("c2", 32768): dict(bytes=102898432 + 146457856, source="rustgears_b200/csrc/k_convblock.cu",
+                        sha256="146f0d5bcb7af96aa633b2c7eb863b1ee83598a9b96375c2c08c654d3eecbd14"),
+    ("c3c", 65536): dict(bytes=2737971968 + 3717008128, source="rustgears_b200/csrc/k_gemm_tc.cu",
+                         sha256="484762ca70678d42428b59df734f6fd082e8c27d9e80fbe8c55b720fa397e060"),
 }
 NOMINAL_INT8_TOPS = 4500.0
 
@@ -397,7 +399,7 @@ def _reference_workload(cfg: str, units: int, precision: int):
     if c3:
         _, k, n = WORKLOADS[cfg]["shape"]
         layers, x = oc.c3_linear(units, k, n)
-        return layers, x, 8 if precision == 2 else 64
+        return layers, x, 8 if precision == 2 else 256
     sample = min(units, 16 if precision == 2 else {"c2": 2048, "c4": 4, "c5": 1}.get(cfg, units))
     build = {"c1": oc.c1_mlp, "c2": oc.c2_cnn, "c4": oc.resnet18,
              "c5": lambda b: oc.transformer_c5(batch=b)}[cfg]
@@ -664,10 +666,13 @@ def main():
         barrier()
     launches = launches_per_run * args.steps
     total_ms = float(sum(a.elapsed_time(b) for a, b in evs))
+    per_rank_ms = None
     if world > 1:
         t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
-        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
-        total_ms = float(t.item())
+        every = torch.empty(world, dtype=torch.float64, device=dev)
+        tdist.all_gather_into_tensor(every, t)
+        per_rank_ms = [float(v) / args.steps for v in every.tolist()]
+        total_ms = max(per_rank_ms) * args.steps
     ms_per_step = total_ms / args.steps
 
     # gather-inclusive: each step followed by the all-gather of every rank's output
@@ -774,6 +779,8 @@ def main():
         "gpu_launches": launches,
         "clocks": clk,
     }
+    if per_rank_ms is not None:
+        line["per_rank_ms_per_step"] = per_rank_ms   # device time of each rank's timed steps
     if gather is not None:
         line["gather_inclusive"] = gather
     if sharded is not None:

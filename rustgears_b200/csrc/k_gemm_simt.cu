@@ -190,6 +190,9 @@ __device__ __forceinline__ int32_t load_q4(const GemmArgs& p, const float* row, 
     v.z = k0 + 2 < p.af_k ? __ldg(row + k0 + 2) : 0.0f;
     v.w = k0 + 3 < p.af_k ? __ldg(row + k0 + 3) : 0.0f;
   }
+  if (p.af_scale)  // a calibrated scale: values beyond its range clamp (quant1)
+    return (int32_t)((uint32_t)(quant1(v.x, inv) & 0xff) | ((uint32_t)(quant1(v.y, inv) & 0xff) << 8) |
+                     ((uint32_t)(quant1(v.z, inv) & 0xff) << 16) | ((uint32_t)(quant1(v.w, inv) & 0xff) << 24));
   return (int32_t)((uint32_t)(quant1_bounded(v.x, inv) & 0xff) | ((uint32_t)(quant1_bounded(v.y, inv) & 0xff) << 8) |
                    ((uint32_t)(quant1_bounded(v.z, inv) & 0xff) << 16) |
                    ((uint32_t)(quant1_bounded(v.w, inv) & 0xff) << 24));
@@ -211,7 +214,7 @@ __global__ void __launch_bounds__(kNarrowThreads) k_gemm_narrow(const GemmArgs p
   }
   float sa = 0.0f, inv = 0.0f;
   if (QA) {
-    sa = quant_scale(__uint_as_float(*p.af_amax));
+    sa = p.af_scale ? *p.af_scale : quant_scale(__uint_as_float(*p.af_amax));
     inv = quant_inv(sa);
   } else {
     sa = p.a_scale[0];
@@ -300,7 +303,7 @@ size_t narrow_smem(int nt, int64_t k) { return (size_t)nt * k + (size_t)kNarrowT
 }  // namespace
 
 bool gemm_narrow_eligible(const GemmArgs& a) {
-  const bool a_ok = a.af ? (a.af_amax != nullptr && a.af_k <= a.k)
+  const bool a_ok = a.af ? ((a.af_amax != nullptr || a.af_scale != nullptr) && a.af_k <= a.k)
                          : (a.lda == a.k && (reinterpret_cast<uintptr_t>(a.a) & 15) == 0);
   return a.n >= 1 && a.n <= kNarrowMaxN && narrow_smem(narrow_width(a.n), a.k) <= 48 * 1024 && !a.conv &&
          a.out_l == 0 && a.rows_per_scale == 0 && a.amax.elems_per_slot == 0 && (a.k & 15) == 0 && a_ok &&

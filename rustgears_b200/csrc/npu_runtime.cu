@@ -1304,12 +1304,21 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
           g.m = rows; g.n = op.out_f; g.k = op.kpad;
           g.rows_per_scale = 0;
           g.out_l = 0;
-          if (!P.i8_in[i]) {  // (else its producer wrote the operand)
-            launch_quantize_rows_frozen(cur, rows, op.in_f, op.kpad, frozen, q, st);
-            ++launches;
-            RG_LAUNCHED("quantize_rows");
-          }
           g.a = q; g.lda = op.kpad;
+          if (!P.i8_in[i]) {  // (else its producer wrote the operand)
+            // narrow layers quantize the f32 input with the frozen scale while loading it
+            GemmArgs gf = g;
+            gf.a = nullptr; gf.af = cur; gf.af_k = op.in_f; gf.af_scale = frozen;
+            gf.w = op.d_w.as<int8_t>(); gf.ldb = op.kpad; gf.amax = sink;
+            fused_q = !s.trace && gemm_narrow_eligible(gf);
+            if (fused_q) {
+              g.a = nullptr; g.af = cur; g.af_k = op.in_f; g.af_scale = frozen;
+            } else {
+              launch_quantize_rows_frozen(cur, rows, op.in_f, op.kpad, frozen, q, st);
+              ++launches;
+              RG_LAUNCHED("quantize_rows");
+            }
+          }
         } else if (op.kind == RG_LAYER_LINEAR) {
           const int64_t rows = os.in_elems / op.in_f;
           if (P.amax_src[i] < 0) { launch_absmax(cur, os.in_elems, my_amax, st); ++launches; RG_LAUNCHED("absmax"); }

@@ -77,6 +77,8 @@ struct GemmArgs {
   const float* af = nullptr;
   int64_t af_k = 0;
   const unsigned* af_amax = nullptr;
+  // ... or with a given (calibrated) scale *af_scale, values beyond its range clamping
+  const float* af_scale = nullptr;
   bool conv = false;
   ConvGeom g;
   // B: weights [n, ldb] i8, K-contiguous (ldb multiple of 16, zero-padded)
