@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 16; ++j) o[j] = act_apply(ACT, p.act_param, o[j]);
         }
-        if (row_ok) {
+        if (p.amax && row_ok) {  // (a consumer quantizes this output: its absmax)
 #pragma unroll
           for (int j = 0; j < 16; ++j)
             if (col0 + j < p.n) amax = fmaxf(amax, fabsf(o[j]));
