@@ -755,6 +755,7 @@ void og_op_linear_with_amax(const og_op* op, const float* x, int64_t rows, float
    * quantizing with the max over every shard: the multi-device restatement). */
   int64_t k = op->in_features, n = op->out_features;
   float sa = op->frozen ? op->frozen_scale : (amax < 1e-12f ? 1.0f : amax / 127.0f);
+  ((og_op*)op)->seen_scale = sa;
   float inv = 1.0f / sa;
   int8_t* q = (int8_t*)malloc((size_t)(rows * k > 0 ? rows * k : 1));
   for (int64_t i = 0; i < rows * k; ++i) q[i] = og_q1(x[i], inv);

@@ -312,6 +312,11 @@ class Program:
         target, the scale its Linear quantized with (the batch absmax / 127)."""
         self.set_calibration(None)
         self.execute(x, nthreads=nthreads)
+        return self.seen_scales()
+
+    def seen_scales(self) -> np.ndarray:
+        """Per calibration target, the scale the last run (execute or run_sharded)
+        quantized with: a sharded calibration reads them after run_sharded."""
         return np.array([t[0].seen_scale for t in self._calib_targets()], np.float32)
 
     def set_calibration(self, scales) -> None:
