@@ -1,5 +1,8 @@
 //! `src/device/cuda.rs` for RustGears: the safe wrapper its `CompiledProgram::NpuCuda`
-//! arm holds (the dispatch change is shown in INTEGRATION.md of the B200 library).
+//! arm holds.  The dispatch change in `src/inference/mod.rs`: a variant
+//! `NpuCuda(crate::device::cuda::Session)` built by `from_layers` for
+//! `ExecutionProvider::Npu(p)`, whose `run` stores the returned profile in
+//! `last_profile` and whose `compilation_report` is `Session::report`.
 //!
 //! It turns the reference IR (`LayerSpec`, `src/inference/mod.rs:70-100`) into the
 //! C ABI's `rg_layer_spec` (kind = the `.rtim` tag, `src/save.rs:176-219`;
