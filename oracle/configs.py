@@ -159,7 +159,7 @@ def basic_block(rng: Rng, cin: int, cout: int, stride: int) -> list:
 
 
 def resnet(batch: int, image: int, widths, classes: int, seed: int = 42, stem_k: int = 7):
-    """ResNet-18 layout: conv7x7/2 p3 + BN + ReLU, MaxPool 3x3/2
+    """ResNet-18 layout (the ResNet benchmark configuration): conv7x7/2 p3 + BN + ReLU, MaxPool 3x3/2
     (pad 0, the reference's max_pool2d), 4 stages of 2 basic blocks (first block of
     stages 2-4 stride 2 with a projection), AdaptiveAvgPool2d(1), Flatten, Linear.
     x ~ N(0,1) [batch, 3, image, image].  Conv and Linear weights are drawn in module

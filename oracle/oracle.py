@@ -274,7 +274,7 @@ class Program:
 
     def __init__(self, specs, precision: int = 0, weight_quant: int = 0):
         """weight_quant 0: per-tensor weights (the reference, quantize.rs:18-24);
-        1: per output channel (extension, BASELINE's "symmetric per-channel")."""
+        1: per output channel (extension: the fused-Linear benchmark's "symmetric per-channel")."""
         arr, keep = _to_layers(list(specs))
         self._p = lib().og_compile_ex(arr, len(specs), precision, weight_quant)
         P = self._p.contents

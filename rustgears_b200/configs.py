@@ -70,7 +70,7 @@ def resnet(batch: int, image: int, widths, classes: int, seed: int = 42, stem_k:
 
 
 def c4_resnet18(batch: int = 128, seed: int = 42, row_offset: int = 0, image: int = 224):
-    """ResNet-18-shaped INT8 CNN, x [B,3,224,224] ~ N(0,1), 1000 classes."""
+    """The ResNet-18-shaped INT8 CNN benchmark: x [B,3,224,224] ~ N(0,1), 1000 classes."""
     return resnet(batch, image, (64, 128, 256, 512), 1000, seed, 7, row_offset)
 
 

@@ -1,4 +1,4 @@
-"""Every BASELINE configuration at the size it is stated at, against the oracle,
+"""Every benchmark configuration at the size it is stated at, against the oracle,
 through the C ABI (InferenceSession -> librg_npu.so):
 
 * C2 small CNN at B = 32768 (the whole batch compared), host and device buffers;
@@ -10,7 +10,7 @@ through the C ABI (InferenceSession -> librg_npu.so):
   absmax over all 128 images' pooled features);
 * C5 transformer: 12 layers, d_model 1024, 16 heads, SwiGLU 2816, one sequence
   of 512 tokens;
-* C3 with per-output-channel i8 weights (BASELINE's "symmetric per-channel";
+* C3 with per-output-channel i8 weights (the configuration's "symmetric per-channel";
   an extension of the reference's per-tensor QuantTensor, restated in the
   oracle as og_compile_ex(weight_quant = 1)).
 
