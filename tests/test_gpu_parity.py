@@ -274,7 +274,7 @@ def test_host_input_fed_in_chunks(gpu, oracle_lib):
 
 
 def test_resnet18_full_size_matches_oracle(gpu, oracle_lib):
-    """BASELINE configs[3] layout at 224 x 224 (batch 2): residual blocks, projection
+    """The ResNet-18 benchmark layout at 224 x 224 (batch 2): residual blocks, projection
     shortcuts, stride-2 convs with their covered-pixel absmax, adaptive pooling."""
     layers, x = configs.resnet18(2)
     ref, _, _ = oracle.Program(layers).execute(x, nthreads=16)
