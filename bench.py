@@ -471,12 +471,18 @@ def run_probe(args):
     model, x, _ = build_workload(args.config, 0, 1, args.batch)
     prov = {"fp16": ExecutionProvider.npu_fp16(), "f32": ExecutionProvider.cpu()}.get(args.precision,
                                                                                        ExecutionProvider.npu_int8())
-    sess = InferenceSession.from_module(model, prov, device=0, weight_quant=args.weight_quant)
+    sess = InferenceSession.from_module(model, prov, device=0, weight_quant=args.weight_quant,
+                                        flags=session_flags(args))
     xd = torch.from_numpy(x).cuda()
     for _ in range(args.steps):
         sess.run_device(xd)
     torch.cuda.synchronize()
     print(sess.last_npu_profile())
+
+
+def session_flags(args) -> int:
+    from rustgears_b200 import _native
+    return _native.RG_SESSION_NO_FUSION if args.no_fusion else 0
 
 
 def gemm_kernel_roofline(sess, xd, yd, stream, flush, peaks, reps: int = 10):
@@ -581,6 +587,8 @@ def main():
     ap.add_argument("--calibrated", action="store_true",
                     help="static calibration (extension): frozen Linear input scales from a calibration batch "
                          "disjoint from the measured one; producers write the Linears' i8 operands")
+    ap.add_argument("--no-fusion", action="store_true",
+                    help="every op on its own kernel (no fused CNN block or stem): the op-by-op path")
     ap.add_argument("--probe", action="store_true",
                     help="run the workload --steps times and print the profile (for ncu captures; no timing)")
     args = ap.parse_args()
@@ -613,7 +621,8 @@ def main():
     if (fp16 or f32) and cfg in ("c4", "c5"):
         raise SystemExit("the ResNet and transformer extensions run on the INT8 arm only")
     prov = ExecutionProvider.npu_fp16() if fp16 else ExecutionProvider.cpu() if f32 else ExecutionProvider.npu_int8()
-    sess = InferenceSession.from_module(model, prov, device=local, weight_quant=args.weight_quant)
+    sess = InferenceSession.from_module(model, prov, device=local, weight_quant=args.weight_quant,
+                                        flags=session_flags(args))
     if world > 1:
         uid = dist.exchange_unique_id(rank)
         dist.attach(sess, rank, world, uid)
@@ -786,6 +795,8 @@ def main():
     if sharded is not None:
         line["sharded_bit_exact"] = sharded["sharded_bit_exact"]
         line["sharded_check"] = sharded
+    if args.no_fusion:
+        line["config"]["fusion"] = "off (RG_SESSION_NO_FUSION: every op on its own kernel)"
     if calib:
         line["config"]["calibration"] = calib
         line["roofline"]["traffic_source"] = "no capture of the calibrated workload"
