@@ -134,7 +134,7 @@ struct CBParams {
   unsigned* amax;          // optional sink of the output's absmax
   int64_t amax_per_image;
   int* err;                // this call's error word: set to 1 when a bounded wait gave up
-  int8_t* out_q;           // calibration extension: i8 output [n, 49, C2] with the frozen scale
+  int8_t* out_q;           // calibration extension: i8 output [n, C2 * 49] with the frozen scale
   const float* q_scale;
 };
 
@@ -522,12 +522,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_convblock(const CBParams p) {
           }
           if (pos_ok) {
             const int64_t o0 = img * (int64_t)(C2 * P2 * P2) + (int64_t)(c0 + half * 8) * (P2 * P2) + py * P2 + j;
-            if (p.out_q) {  // the next Linear's operand, (pixel, channel) order: one 8-byte store
-              uint32_t w[2] = {0u, 0u};
+            if (p.out_q) {  // the next Linear's operand, quantized with its calibrated scale
 #pragma unroll
-              for (int k = 0; k < 8; ++k) w[k >> 2] |= (uint32_t)(quant1(out[k], q_inv) & 0xff) << (8 * (k & 3));
-              *reinterpret_cast<uint2*>(p.out_q + img * (int64_t)(C2 * P2 * P2) + (py * P2 + j) * C2 + c0 +
-                                        half * 8) = make_uint2(w[0], w[1]);
+              for (int k = 0; k < 8; ++k) p.out_q[o0 + k * (P2 * P2)] = (int8_t)quant1(out[k], q_inv);
             } else {
               float* og = p.out + o0;
 #pragma unroll

@@ -154,8 +154,6 @@ struct Op {
   int32_t dmode = -1;            // DCONV_3X3 / DCONV_S2D / DCONV_1X1, or -1 (implicit GEMM only)
   DevBuf d_ws;                   // 7x7 / stride 2 stems (<= 4 channels -> 64): the fused stem's arrangement
   DevBuf d_wh;                   // FP16 arm: f32 weights rounded by round_fp16, reference layout [N, K]
-  DevBuf d_w_pc;                 // calibrated Linear after a fused CNN block: weights with K in the block's
-                                 // i8 output order, (pixel, channel) instead of (channel, pixel)
   bool wh_exact = true;          // every d_wh value is an fp16 value (not the affine diagonal)
   bool bias_finite = true;
   std::string label;
@@ -919,7 +917,7 @@ static rg_status make_plan(const Session& s, const int64_t* shape, int32_t ndim,
       while (j >= 0 && main_path_noop(s.ops[(size_t)j].kind)) --j;
       if (j < 0) continue;
       const Op& c = s.ops[i];
-      if (c.kind == RG_LAYER_LINEAR && j >= 3 && P.block_start[(size_t)j - 3] && c.kpad == c.in_f && c.d_w_pc.p) {
+      if (c.kind == RG_LAYER_LINEAR && j >= 3 && P.block_start[(size_t)j - 3] && c.kpad == c.in_f) {
         P.i8_out[(size_t)j - 3] = (int)i;  // the fused block writes the Linear's operand
         P.i8_in[i] = 1;
       } else if ((c.kind == RG_LAYER_ATTENTION || c.kind == RG_LAYER_SWIGLU) &&
@@ -1400,9 +1398,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
           g.rows_per_scale = L;
           g.out_l = L;
         }
-        // (a Linear whose operand the fused block wrote reads it in (pixel, channel) order)
-        g.w = (frozen && P.i8_in[i]) ? op.d_w_pc.as<int8_t>() : op.d_w.as<int8_t>();
-        g.ldb = op.kpad;
+        g.w = op.d_w.as<int8_t>(); g.ldb = op.kpad;
         g.a_scale = frozen ? frozen : my_scale;
         g.w_scale = op.w_scale;
         g.w_scale_ch = op.w_scale_ch.empty() ? nullptr : op.d_wsc.as<float>();
@@ -2245,30 +2241,6 @@ static rg_status set_calibration_locked(Session& s, const float* scales, int32_t
     return RG_OK;
   }
   s.calib.assign(scales, scales + n);
-  // A Linear after Conv(k3 s1 p1) MaxPool(2) Conv(k3 s1 p1) MaxPool(2) [Flatten] may find
-  // its operand written by the fused block in (pixel, channel) order: its weights with
-  // K permuted to match (the i32 sums do not depend on the order of K).
-  for (size_t i = 0; i < s.ops.size(); ++i) {
-    Op& op = s.ops[i];
-    if (op.kind != RG_LAYER_LINEAR || op.kpad != op.in_f || op.d_w_pc.p) continue;
-    int j = (int)i - 1;
-    while (j >= 0 && s.ops[(size_t)j].kind == RG_LAYER_FLATTEN) --j;
-    if (j < 3) continue;
-    const Op& c1 = s.ops[(size_t)j - 3];
-    const Op& m1 = s.ops[(size_t)j - 2];
-    const Op& c2 = s.ops[(size_t)j - 1];
-    const Op& m2 = s.ops[(size_t)j];
-    auto conv3 = [](const Op& c) { return c.kind == RG_LAYER_CONV2D && c.k == 3 && c.stride == 1 && c.pad == 1; };
-    auto pool2 = [](const Op& m) { return m.kind == RG_LAYER_MAXPOOL2D && m.k == 2 && m.stride == 2; };
-    if (!conv3(c1) || !pool2(m1) || !conv3(c2) || !pool2(m2) || c2.out_c <= 0 || op.in_f % c2.out_c) continue;
-    const int64_t ch = c2.out_c, px = op.in_f / ch, rows = op.out_f;
-    std::vector<int8_t> w((size_t)(rows * op.kpad));
-    for (int64_t r = 0; r < rows; ++r)
-      for (int64_t c = 0; c < ch; ++c)
-        for (int64_t q = 0; q < px; ++q) w[(size_t)(r * op.kpad + q * ch + c)] = op.wq[(size_t)(r * op.in_f + c * px + q)];
-    RG_TRY(op.d_w_pc.ensure(w.size()));
-    RG_CUDA_TRY(cudaMemcpy(op.d_w_pc.p, w.data(), w.size(), cudaMemcpyHostToDevice));
-  }
   RG_TRY(s.d_calib.ensure((size_t)n * sizeof(float)));
   RG_CUDA_TRY(cudaMemcpy(s.d_calib.p, scales, (size_t)n * sizeof(float), cudaMemcpyHostToDevice));
   s.calibrated = true;

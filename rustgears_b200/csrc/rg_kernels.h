@@ -222,8 +222,7 @@ struct ConvBlockArgs {
   int64_t amax_per_image = 0;
   int* err = nullptr;                // this call's error word (required)
   // calibration extension: out_q non-null writes the output quantized with the frozen
-  // scale *q_scale as i8 [n, (h/4) * (w/4), c2] -- (pixel, channel) order, the next
-  // Linear's weights permuted to match -- instead of the f32 out
+  // scale *q_scale as i8 [n, c2 * (h/4) * (w/4)] instead of the f32 out
   int8_t* out_q = nullptr;
   const float* q_scale = nullptr;
 };
