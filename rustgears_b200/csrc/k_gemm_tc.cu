@@ -71,9 +71,11 @@ struct TcParams {
   int32_t starve;           // test hook: the producer issues no loads (the MMA's waits run out)
 };
 
-// Grouped tile order: 16 M-tiles sweep all N-tiles so the W panel stays in L2.
+// Grouped tile order: 32 M-tiles sweep all N-tiles, so the 32 A panels in flight and the
+// W panel stay in L2 (with 148 CTAs the wave spans about 5 N-tiles of one group).  At
+// 65536 x 4096 x 14336 this read 1.46 GB from DRAM per launch against 2.47 GB with 16.
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& mb, int& nb) {
-  constexpr int G = 16;
+  constexpr int G = 32;
   const int per_group = G * tiles_n;
   const int group = tile / per_group;
   const int first_m = group * G;
@@ -295,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&map_o, stg, (int32_t)col0, (int32_t)row0);
+            tma_store_2d_evict_first(&map_o, stg, (int32_t)col0, (int32_t)row0);
             bulk_commit();
           }
         } else if (row_ok) {

@@ -123,6 +123,17 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
                "r"(smem_addr(src)), "r"(x), "r"(y)
                : "memory");
 }
+// The same store with an L2 evict-first policy: a streamed output tile should not push
+// the operand panels that later tiles re-read out of L2.
+__device__ __forceinline__ void tma_store_2d_evict_first(const CUtensorMap* map, const void* src, int32_t x,
+                                                         int32_t y) {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_addr(src)), "r"(x), "r"(y), "l"(pol)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until every committed bulk store has finished reading its shared-memory source.
 __device__ __forceinline__ void bulk_wait_read_all() {
