@@ -26,6 +26,7 @@
 
 #include "rg_kernels.h"
 #include "rg_math.cuh"
+#include "rg_f32x2.cuh"
 #include "rg_sm100.cuh"
 
 namespace rg {
@@ -85,7 +86,12 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
   nb = in / gm;
 }
 
-template <int BN, int ACT>
+// FULL: every tile is whole (m % BM == 0, n % BN == 0), the output leaves through TMA
+// tile stores, bias loads are 16-byte vectors, the weight scale is per tensor, and
+// no absmax or accumulator dump is asked for.  The epilogue then has no per-chunk
+// branch besides the out-of-range tanh loop (each one a branch-resolution stall of
+// every epilogue warp).
+template <int BN, int ACT, bool FULL>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
               const __grid_constant__ CUtensorMap map_o, const TcParams p) {
@@ -216,16 +222,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int64_t row0 = (int64_t)mb * BM + q * 32;
       const int64_t row = row0 + lane;
-      const bool row_ok = row < p.m;
+      const bool row_ok = FULL || row < p.m;
 #pragma unroll 1
       for (int c0 = part * kCols; c0 < (part + 1) * kCols; c0 += 16) {
         uint32_t v[16];
         tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + c0), v);
         tmem_ld_wait();
         const int64_t col0 = (int64_t)nb * BN + c0;
-        if (col0 >= p.n || row0 >= p.m) continue;  // warp-uniform
+        if (!FULL && (col0 >= p.n || row0 >= p.m)) continue;  // warp-uniform
         float o[16];  // (acc as f32) * cs + bias, then the activation in place
-        if (p.vec_cols && col0 + 16 <= p.n) {
+        if (FULL || (p.vec_cols && col0 + 16 <= p.n)) {
           // Full chunk: scale and bias as 16-byte loads.
           const float4* bp = reinterpret_cast<const float4*>(p.bias + col0);
           const float4* sp = reinterpret_cast<const float4*>(p.w_scale_ch + col0);
@@ -233,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j4 = 0; j4 < 4; ++j4) {
             const float4 b = __ldg(bp + j4);
             float4 cs = make_float4(cs_tensor, cs_tensor, cs_tensor, cs_tensor);
-            if (p.w_scale_ch) {
+            if (!FULL && p.w_scale_ch) {
               const float4 sw = __ldg(sp + j4);
               cs = make_float4(__fmul_rn(sa, sw.x), __fmul_rn(sa, sw.y), __fmul_rn(sa, sw.z), __fmul_rn(sa, sw.w));
             }
@@ -253,17 +259,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if constexpr (ACT == ACT_GELU) {
           // Every value takes the restatement with only the common range's cases
-          // (bit-identical to the general one there); the values whose tanh argument
-          // lies outside it (|u| >= 7.5, |u| < 2^-25, non-finite) are recomputed with
-          // the general restatement, one value per lane per round, in a loop holding a
-          // single copy of it.
+          // (bit-identical to the general one there), two values per packed f32x2
+          // instruction; the values whose tanh argument lies outside it (|u| >= 7.5,
+          // |u| < 2^-25, non-finite) are recomputed with the general restatement, one
+          // value per lane per round, in a loop holding a single copy of it.
           float t[16];
           uint32_t redo = 0;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float u = gelu_arg(o[j]);
-            t[j] = tanh_f32_common(u);
-            redo |= (uint32_t)!tanh_common_range(u) << j;
+          for (int j = 0; j < 16; j += 2) {
+            const f32x2 u = gelu_arg_x2(pack2(o[j], o[j + 1]));
+            tanh_f32_common_x2(lo2(u), hi2(u), t[j], t[j + 1]);
+            redo |= (uint32_t)!tanh_common_range(lo2(u)) << j;
+            redo |= (uint32_t)!tanh_common_range(hi2(u)) << (j + 1);
           }
           while (__any_sync(0xffffffffu, redo != 0)) {
             const int jr = redo ? __ffs(redo) - 1 : 0;
@@ -276,17 +283,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             redo &= redo - 1;
           }
 #pragma unroll
-          for (int j = 0; j < 16; ++j) o[j] = gelu_from_tanh(o[j], t[j]);
+          for (int j = 0; j < 16; j += 2) {
+            const f32x2 g = gelu_from_tanh_x2(pack2(o[j], o[j + 1]), pack2(t[j], t[j + 1]));
+            o[j] = lo2(g);
+            o[j + 1] = hi2(g);
+          }
         } else {
 #pragma unroll
           for (int j = 0; j < 16; ++j) o[j] = act_apply(ACT, p.act_param, o[j]);
         }
-        if (p.amax && row_ok) {  // (a consumer quantizes this output: its absmax)
+        if (!FULL && p.amax && row_ok) {  // (a consumer quantizes this output: its absmax)
 #pragma unroll
           for (int j = 0; j < 16; ++j)
             if (col0 + j < p.n) amax = fmaxf(amax, fabsf(o[j]));
         }
-        if (p.tma_store) {
+        if (FULL || p.tma_store) {
           // The previous chunk's store must have finished reading the staging tile.
           if (lane == 0) bulk_wait_read_all();
           __syncwarp();
@@ -306,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 16; ++j)
             if (col0 + j < p.n) dst[j] = o[j];
         }
-        if (p.acc && row_ok) {
+        if (!FULL && p.acc && row_ok) {
 #pragma unroll
           for (int j = 0; j < 16; ++j)
             if (col0 + j < p.n) p.acc[row * p.n + col0 + j] = (int32_t)v[j];
@@ -371,12 +382,12 @@ bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t ld, int 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int ACT>
-bool launch_bn(const GemmArgs& a, int num_sms, cudaStream_t st) {
+template <int BN, int ACT, bool FULL>
+bool launch_inst(const GemmArgs& a, int num_sms, cudaStream_t st) {
   using C = Cfg<BN>;
   static std::once_flag once;
   std::call_once(once, [] {
-    cudaFuncSetAttribute(k_gemm_tc<BN, ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    cudaFuncSetAttribute(k_gemm_tc<BN, ACT, FULL>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
   });
   CUtensorMap ma, mw, mo;
   if (!make_map(&ma, a.a, a.m, a.lda, BM) || !make_map(&mw, a.w, a.n, a.ldb, BN)) return false;
@@ -397,8 +408,17 @@ bool launch_bn(const GemmArgs& a, int num_sms, cudaStream_t st) {
   p.starve = a.starve;
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < num_sms ? tiles : num_sms;
-  k_gemm_tc<BN, ACT><<<grid, kThreads, C::kSmem, st>>>(ma, mw, mo, p);
+  if (FULL && !(tma_store && p.vec_cols)) return false;
+  k_gemm_tc<BN, ACT, FULL><<<grid, kThreads, C::kSmem, st>>>(ma, mw, mo, p);
   return true;
+}
+
+template <int BN, int ACT>
+bool launch_bn(const GemmArgs& a, int num_sms, cudaStream_t st) {
+  const bool full = a.m % BM == 0 && a.n % BN == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(a.bias) & 15) == 0 && a.w_scale_ch == nullptr &&
+                    a.amax.ptr == nullptr && a.acc == nullptr && a.out_l == 0;
+  return full ? launch_inst<BN, ACT, true>(a, num_sms, st) : launch_inst<BN, ACT, false>(a, num_sms, st);
 }
 
 template <int BN>
