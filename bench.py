@@ -485,6 +485,28 @@ def session_flags(args) -> int:
     return _native.RG_SESSION_NO_FUSION if args.no_fusion else 0
 
 
+def int8_library_tops(dev, size: int = 8192, reps: int = 10) -> float:
+    """A measured INT8 tensor-core figure on this box: torch._int_mm (cuBLASLt,
+    i8 x i8 -> i32, no epilogue) at size^3, best of `reps` launches after warm-up,
+    CUDA events on the current stream."""
+    import torch
+    g = torch.Generator(device=dev).manual_seed(7)
+    a = torch.randint(-127, 128, (size, size), dtype=torch.int8, device=dev, generator=g)
+    b = torch.randint(-127, 128, (size, size), dtype=torch.int8, device=dev, generator=g)
+    for _ in range(3):
+        c = torch._int_mm(a, b)
+    best = float("inf")
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        c = torch._int_mm(a, b)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        best = min(best, e0.elapsed_time(e1) / 1e3)
+    del a, b, c
+    return 2.0 * size ** 3 / best / 1e12
+
+
 def gemm_kernel_roofline(sess, xd, yd, stream, flush, peaks, reps: int = 10):
     """C3's dominant kernel is the fused tcgen05 GEMM (k_gemm_tc); the op's profile time
     also holds its absmax and quantize passes.  The kernel is timed alone here through
@@ -531,6 +553,12 @@ def gemm_kernel_roofline(sess, xd, yd, stream, flush, peaks, reps: int = 10):
     int8_peak = 2.0 * peaks.get("bf16_tflops", 1590.0)
     achieved = ops / dur_s / 1e12
     del q, w
+    try:
+        lib_tops = int8_library_tops(dev)
+    except Exception as exc:  # noqa: BLE001 -- a reported reference figure, not the measurement
+        lib_tops, lib_err = None, f"{type(exc).__name__}: {exc}"
+    else:
+        lib_err = None
     return {"kernel": f"k_gemm_tc (tcgen05 kind::i8 GEMM + fused dequant/bias/{'GELU' if info['act'] == 4 else 'act'} "
                       f"epilogue), {m}x{k}x{n}", "bound": "tensor", "achieved": achieved, "peak": int8_peak,
             "unit": "TOPS", "frac": achieved / int8_peak, "frac_of_nominal_int8": achieved / NOMINAL_INT8_TOPS,
@@ -538,7 +566,10 @@ def gemm_kernel_roofline(sess, xd, yd, stream, flush, peaks, reps: int = 10):
             "algorithmic_bytes": m * ld + n * ld + 4 * m * n + 8 * n,
             "peak_source": "2 x measured bf16 dense burst (MEASURED_PEAKS.json) as the INT8 denominator, "
                            "no INT8 figure being in that file (nominal INT8 dense 4500)",
-            "timing": f"kernel alone via rg_gemm_i8_fused, mean of {reps} launches, L2 flushed before each"}
+            "timing": f"kernel alone via rg_gemm_i8_fused, mean of {reps} launches, L2 flushed before each",
+            "int8_library": {"tops": lib_tops, "frac": achieved / lib_tops if lib_tops else None,
+                             "how": "torch._int_mm (cuBLASLt) i8 x i8 -> i32 without epilogue, 8192^3, best of 10, "
+                                    "CUDA events, measured in this run" if lib_tops else lib_err}}
 
 
 def sharded_parity(sess, model, prov, x, weight_quant, rank, world, dev, tdist, per_rank: int, scales=None):
