@@ -458,3 +458,21 @@ def test_gelu_epilogue_outside_the_common_range(gpu, oracle_lib, scale):
     x[9, 0] = 0.0
     ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
     assert_same(session_for(layers).run(x), ref, f"gelu scale {scale}, finite")
+
+
+@pytest.mark.parametrize("mkn", [(256, 512, 512), (200, 512, 264)])
+@pytest.mark.parametrize("act", [None, 1, 2, 3, 4, 5, 6])
+def test_tensor_core_gemm_every_activation(gpu, oracle_lib, act, mkn):
+    """Every activation through the tcgen05 GEMM's two instance families: whole tiles
+    (M a multiple of 128, N of 256, per-tensor scale, no absmax or accumulator dump:
+    the branch-free instance) and ragged tiles, bit-exact against the oracle."""
+    m, k, n = mkn
+    rng = np.random.default_rng(m + n + (act or 0))
+    w = (rng.standard_normal((k, n)) * 0.05).astype(np.float32)
+    b = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    layers = [dict(kind=oracle.LINEAR, in_features=k, out_features=n, weight=w, bias=b)]
+    if act is not None:
+        layers.append(dict(kind=oracle.ACTIVATION, act=act, act_param=0.1))
+    x = (rng.standard_normal((m, k)) * 2.0).astype(np.float32)
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
+    assert_same(session_for(layers).run(x), ref, f"act {act} linear {mkn}")
