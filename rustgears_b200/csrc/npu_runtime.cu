@@ -190,8 +190,10 @@ struct Session {
   int64_t fp32_bytes = 0, npu_bytes = 0;
   std::vector<Op> ops;
   cudaStream_t stream = nullptr;
-  cudaStream_t copy_stream = nullptr;      // host-input copies that overlap the first op
+  cudaStream_t copy_stream = nullptr;      // host copies that overlap the first / last op
   std::vector<cudaEvent_t> chunk_events;   // one per input chunk (timing disabled)
+  std::vector<cudaEvent_t> drain_events;   // one per output chunk (timing disabled)
+  cudaEvent_t drain_done = nullptr;        // the last output chunk has reached the host
   std::vector<cudaEvent_t> events;
   std::vector<int> ev_of;  // ev_of[i]: event marking the start of op i (ops that launch nothing share one)
   std::mutex mu;
@@ -961,6 +963,48 @@ struct HostFeed {
 constexpr int64_t kFeedMinChunk = 2048;  // images; smaller chunks underfill the GPU
 constexpr int kFeedMaxChunks = 8;
 
+// Host output drained in chunks: when the program ends with a Linear on the tensor-core
+// GEMM and the caller's output is page-locked host memory, the GEMM runs in row chunks
+// and each chunk's device-to-host copy starts on the copy stream as soon as that chunk
+// is written, so the PCIe transfer overlaps the rest of the GEMM.  Rows are independent
+// in the GEMM, so the output is the same as one launch's.
+struct HostDrain {
+  float* y = nullptr;  // page-locked host output, nullptr: no drain
+  bool done = false;   // the last op copied its output (drain_done marks the end)
+};
+constexpr int kDrainChunks = 8;
+constexpr int64_t kDrainMinBytes = 64ll << 20;
+
+static rg_status gemm_tc_drained(Session& s, const GemmArgs& g, HostDrain& d, cudaStream_t st, int32_t& launches) {
+  const int64_t step = round_up((g.m + kDrainChunks - 1) / kDrainChunks, 128);
+  int c = 0;
+  for (int64_t r0 = 0; r0 < g.m; r0 += step, ++c) {
+    GemmArgs gc = g;
+    gc.m = std::min<int64_t>(step, g.m - r0);
+    gc.a = g.a + r0 * g.lda;
+    gc.out = g.out + r0 * g.n;
+    if (!launch_gemm_tc(gc, s.num_sms, st)) return fail(RG_ERR_CUDA, "TMA descriptor encoding failed");
+    ++launches;
+    RG_CUDA_TRY(cudaEventRecord(s.drain_events[(size_t)c], st));
+    RG_CUDA_TRY(cudaStreamWaitEvent(s.copy_stream, s.drain_events[(size_t)c], 0));
+    RG_CUDA_TRY(cudaMemcpyAsync(d.y + r0 * g.n, gc.out, (size_t)(gc.m * g.n) * 4, cudaMemcpyDeviceToHost,
+                                s.copy_stream));
+  }
+  RG_CUDA_TRY(cudaEventRecord(s.drain_done, s.copy_stream));
+  d.done = true;
+  return RG_OK;
+}
+
+// Whether every row chunk of g would take the tensor-core GEMM.
+static bool drain_eligible(const GemmArgs& g) {
+  const int64_t step = round_up((g.m + kDrainChunks - 1) / kDrainChunks, 128);
+  if (g.m < 2 * step || g.amax.ptr || g.acc) return false;
+  GemmArgs first = g, tail = g;
+  first.m = step;
+  tail.m = g.m - (g.m - 1) / step * step;
+  return gemm_tc_eligible(first) && gemm_tc_eligible(tail);
+}
+
 static bool feed_chunked(const Session& s, const RunPlan& P) {
   return !s.ops.empty() && P.block_start[0] && !s.trace && P.shapes[0].in[0] >= 2 * kFeedMinChunk;
 }
@@ -1015,7 +1059,7 @@ static rg_status run_inner_linear(Session& s, const Op& lin, const float* src, i
 // the staging buffer the feed fills); the output is left in y_dev or one of the
 // session's activation buffers.
 static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float* y_dev, cudaStream_t st,
-                         bool record_events, const HostFeed& feed = HostFeed()) {
+                         bool record_events, const HostFeed& feed = HostFeed(), HostDrain* drain = nullptr) {
   const size_t n = s.ops.size();
   int64_t max_elems = 1, max_q = 16, max_ext0 = 0, max_ext1 = 0;
   for (size_t i = 0; i < n; ++i) {
@@ -1461,6 +1505,11 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         } else if (conv_tc) {
           if (!launch_conv_tc(g, s.num_sms, st)) return fail(RG_ERR_CUDA, "op %zu: TMA descriptor encoding failed", i);
           s.used_tc = true;
+        } else if (tc && drain && drain->y && last && op.kind == RG_LAYER_LINEAR && g.out == y_dev && !s.trace &&
+                   !s.capturing && drain_eligible(g)) {
+          RG_TRY(gemm_tc_drained(s, g, *drain, st, launches));
+          --launches;  // counted per chunk
+          s.used_tc = true;
         } else if (tc) {
           if (!launch_gemm_tc(g, s.num_sms, st)) return fail(RG_ERR_CUDA, "op %zu: TMA descriptor encoding failed", i);
           s.used_tc = true;
@@ -1873,6 +1922,9 @@ rg_status rg_session_create(const rg_layer_spec* layers, int32_t n_layers, const
   RG_CUDA_TRY(cudaStreamCreateWithFlags(&s.copy_stream, cudaStreamNonBlocking));
   s.chunk_events.assign(kFeedMaxChunks, nullptr);
   for (auto& e : s.chunk_events) RG_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  s.drain_events.assign(kDrainChunks, nullptr);
+  for (auto& e : s.drain_events) RG_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  RG_CUDA_TRY(cudaEventCreateWithFlags(&s.drain_done, cudaEventDisableTiming));
   RG_TRY(s.errw.ensure(2 * sizeof(int)));
   RG_CUDA_TRY(cudaMemset(s.errw.p, 0, 2 * sizeof(int)));
   RG_TRY(compile(s, layers, n_layers));
@@ -1908,6 +1960,9 @@ void rg_session_destroy(rg_session* h) {
   for (cudaEvent_t e : s.events) cudaEventDestroy(e);
   for (cudaEvent_t e : s.chunk_events)
     if (e) cudaEventDestroy(e);
+  for (cudaEvent_t e : s.drain_events)
+    if (e) cudaEventDestroy(e);
+  if (s.drain_done) cudaEventDestroy(s.drain_done);
   if (s.t0) cudaEventDestroy(s.t0);
   if (s.t1) cudaEventDestroy(s.t1);
   if (s.stream) cudaStreamDestroy(s.stream);
@@ -2058,9 +2113,17 @@ static rg_status run_impl(rg_session* h, const float* x, bool x_host, const int6
     rs = run_graph(s, xd, shape, ndim, yd, st, events, Pg, done);
     if (rs == RG_OK && done && Pg) Pp = Pg;
   }
-  if (rs == RG_OK && !done) rs = execute(s, xd, *Pp, yd, st, events, feed);
+  HostDrain drain;
+  if (y_host && !async_run && (int64_t)out_elems * 4 >= kDrainMinBytes) {
+    cudaPointerAttributes pa;
+    if (cudaPointerGetAttributes(&pa, y) == cudaSuccess && pa.type == cudaMemoryTypeHost) drain.y = y;
+    else cudaGetLastError();  // (an unknown pointer only means: no drain)
+  }
+  if (rs == RG_OK && !done) rs = execute(s, xd, *Pp, yd, st, events, feed, &drain);
   if (rs != RG_OK) return rs;
-  if (y_host && out_elems)
+  if (drain.done)
+    RG_CUDA_TRY(cudaStreamWaitEvent(st, s.drain_done, 0));
+  else if (y_host && out_elems)
     RG_CUDA_TRY(cudaMemcpyAsync(y, yd, (size_t)out_elems * 4, cudaMemcpyDeviceToHost, st));
   if (events) RG_CUDA_TRY(cudaEventRecord(s.t1, st));
   for (size_t i = 0; i < oshape.size(); ++i) y_shape[i] = oshape[i];

@@ -476,3 +476,24 @@ def test_tensor_core_gemm_every_activation(gpu, oracle_lib, act, mkn):
     x = (rng.standard_normal((m, k)) * 2.0).astype(np.float32)
     ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
     assert_same(session_for(layers).run(x), ref, f"act {act} linear {mkn}")
+
+
+def test_host_output_drained_in_chunks(gpu, oracle_lib):
+    """A program ending in a tensor-core Linear whose host output is page-locked and at
+    least 64 MiB: the GEMM runs in row chunks, each copied to the host as soon as it
+    is written.  Same result as the single-launch path (pageable output) and the oracle,
+    twice in a row on one session."""
+    torch = gpu
+    layers, x = configs.c3_linear(8192, 1024, 2048, seed=11)
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
+    sess = session_for(layers)
+    plain = sess.run(x)
+    assert_same(plain, ref, "pageable output")
+    pinned = torch.empty(ref.shape, dtype=torch.float32, pin_memory=True)
+    for i in range(2):
+        pinned.fill_(float("nan"))
+        y = sess.run(x, out=pinned.numpy())
+        assert_same(y, ref, f"page-locked output, run {i}")
+    drained = sess.last_npu_profile().kernel_launches
+    sess.run(x)
+    assert drained > sess.last_npu_profile().kernel_launches  # one GEMM launch per chunk
