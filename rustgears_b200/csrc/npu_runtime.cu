@@ -198,7 +198,7 @@ struct Session {
   std::vector<int> ev_of;  // ev_of[i]: event marking the start of op i (ops that launch nothing share one)
   std::mutex mu;
   // workspace
-  DevBuf act0, act1, act2, act3, qbuf, amax, scales, accbuf, xin, yout, covbuf;
+  DevBuf act0, act1, act2, act3, qbuf, amax, scales, accbuf, xin, yout, covbuf, mlpws;
   // This session's device error words, set by its kernels and read (and cleared) by
   // the host after a synchronous run: [0] a tensor-core kernel gave up on a bounded
   // wait; [1] an embedding id was not below the vocabulary size.  Per session, so a
@@ -1055,6 +1055,18 @@ static rg_status run_inner_linear(Session& s, const Op& lin, const float* src, i
   return run_gemm_q(s, lin, q, rows, sc, out, sink, st, launches);
 }
 
+// A program of exactly two INT8 Linears with dynamic per-tensor quantization runs as one
+// cooperative kernel (launch_mlp2) when both are narrow; anything else op by op.
+static bool mlp2_program(const Session& s, const RunPlan& P) {
+  if (s.ops.size() != 2 || s.precision != RG_PREC_INT8 || s.trace || s.calibrated || (s.comm && s.world > 1) ||
+      (s.flags & RG_SESSION_NO_FUSION))
+    return false;
+  const Op& a = s.ops[0];
+  const Op& b = s.ops[1];
+  return a.kind == RG_LAYER_LINEAR && b.kind == RG_LAYER_LINEAR && a.w_scale_ch.empty() && b.w_scale_ch.empty() &&
+         b.in_f == a.out_f && P.amax_src[0] < 0;
+}
+
 // Runs the program on device buffers. x_dev is read only (with a HostFeed it is
 // the staging buffer the feed fills); the output is left in y_dev or one of the
 // session's activation buffers.
@@ -1172,6 +1184,33 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
       sink.elems_per_slot = (s.ops[(size_t)cons].kind == RG_LAYER_CONV2D && imgs > 0)
                                 ? P.shapes[(size_t)cons].in_elems / imgs
                                 : 0;
+    }
+    if (i == 0 && os.in_elems > 0 && mlp2_program(s, P)) {
+      // both Linears in one kernel; its time is recorded on the first op
+      const Op& l2 = s.ops[1];
+      Mlp2Args ma;
+      ma.x = cur; ma.m = os.in_elems / op.in_f;
+      ma.k1 = op.in_f; ma.kpad1 = (int32_t)op.kpad; ma.n1 = op.out_f;
+      ma.kpad2 = (int32_t)l2.kpad; ma.n2 = l2.out_f;
+      ma.w1 = op.d_w.as<int8_t>(); ma.w2 = l2.d_w.as<int8_t>();
+      ma.w1_scale = op.w_scale; ma.w2_scale = l2.w_scale;
+      ma.b1 = op.d_bias.as<float>(); ma.b2 = l2.d_bias.as<float>();
+      ma.act1 = op.act; ma.act2 = l2.act; ma.p1 = op.param; ma.p2 = l2.param;
+      float* out = y_dev ? y_dev : dst;
+      ma.y = out;
+      ma.err = s.errw.as<int>();
+      RG_TRY(s.mlpws.ensure(4 * sizeof(unsigned)));
+      if (mlp2_eligible(ma) && launch_mlp2(ma, s.mlpws.as<unsigned>(), st)) {
+        ++launches;
+        RG_LAUNCHED("mlp2");
+        RG_CUDA_TRY(cudaGetLastError());
+        s.used_tc = true;  // (its error word is read after the run, as the tensor-core kernels')
+        cur = out;
+        if (record_events) RG_CUDA_TRY(record(s.events[(size_t)next_ev]));
+        s.ev_of[1] = next_ev++;
+        s.ev_of[2] = s.ev_of[1];
+        break;
+      }
     }
     // The fused kernel bulk-copies images, so its input must start on a 16-byte
     // boundary; a caller's unaligned view takes the op-by-op path instead.

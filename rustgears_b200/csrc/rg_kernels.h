@@ -204,6 +204,29 @@ bool launch_stem_pool(const StemPoolArgs& a, int num_sms, cudaStream_t st);
 // ---- fused CNN block (k_convblock.cu) ------------------------------------------
 // Conv(C0->C1,k3,s1,p1)+act -> MaxPool(2,2) -> Conv(C1->C2,k3,s1,p1)+act -> MaxPool(2,2),
 // per-image quantization of each conv input, all intermediates in shared memory.
+// A program of two INT8 Linears, both narrow (k1 <= 64 inputs, n1 and n2 <= 32 outputs,
+// per-tensor weights), in one cooperative launch (k_mlp2.cu): input absmax, the first
+// Linear with the hidden row in registers and the hidden absmax, the second Linear.
+struct Mlp2Args {
+  const float* x = nullptr;  // [m, k1]
+  int64_t m = 0;
+  int32_t k1 = 0, kpad1 = 0, n1 = 0, kpad2 = 0, n2 = 0;
+  const int8_t* w1 = nullptr;  // [n1, kpad1]
+  const int8_t* w2 = nullptr;  // [n2, kpad2]
+  float w1_scale = 1.0f, w2_scale = 1.0f;
+  const float* b1 = nullptr;
+  const float* b2 = nullptr;
+  int32_t act1 = 0, act2 = 0;
+  float p1 = 0.0f, p2 = 0.0f;
+  float* y = nullptr;        // [m, n2]
+  unsigned* amax = nullptr;  // optional absmax sink of y
+  int* err = nullptr;        // this call's error word (a barrier wait gave up)
+};
+bool mlp2_eligible(const Mlp2Args& a);
+// false (nothing launched) when the rows exceed one per resident thread or the
+// cooperative launch is refused; ws: 4 words of device scratch owned by the caller
+bool launch_mlp2(const Mlp2Args& a, unsigned* ws, cudaStream_t st);
+
 struct ConvBlockArgs {
   const float* x = nullptr;          // [n, c0, h, w] f32
   int64_t n = 0;

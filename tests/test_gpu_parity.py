@@ -497,3 +497,29 @@ def test_host_output_drained_in_chunks(gpu, oracle_lib):
     drained = sess.last_npu_profile().kernel_launches
     sess.run(x)
     assert drained > sess.last_npu_profile().kernel_launches  # one GEMM launch per chunk
+
+
+@pytest.mark.parametrize("mkn", [(1, 4, 32, 3), (64, 4, 32, 3), (65536, 4, 32, 3), (5000, 33, 17, 10),
+                                 (3000, 64, 32, 32), (999, 16, 1, 1), (160000, 4, 32, 3)])
+def test_two_narrow_linears_in_one_launch(gpu, oracle_lib, mkn):
+    """A program of two narrow Linears runs as one cooperative kernel (input absmax, first
+    Linear with the hidden row in registers, hidden absmax, second Linear; the last shape
+    has more rows than resident threads and takes the op-by-op path): bit-exact against
+    the oracle and the unfused session, with one kernel launch per run where it fits."""
+    m, k, n1, n2 = mkn
+    rng = np.random.default_rng(m + k + n1 + n2)
+    w1 = (rng.standard_normal((k, n1)) * 0.3).astype(np.float32)
+    b1 = (rng.standard_normal(n1) * 0.1).astype(np.float32)
+    w2 = (rng.standard_normal((n1, n2)) * 0.3).astype(np.float32)
+    b2 = (rng.standard_normal(n2) * 0.1).astype(np.float32)
+    act = {(5000, 33, 17, 10): 4, (999, 16, 1, 1): 5, (3000, 64, 32, 32): 2}.get(mkn, 1)  # GELU, leaky, sigmoid
+    layers = [dict(kind=oracle.LINEAR, in_features=k, out_features=n1, weight=w1, bias=b1),
+              dict(kind=oracle.ACTIVATION, act=act, act_param=0.1),
+              dict(kind=oracle.LINEAR, in_features=n1, out_features=n2, weight=w2, bias=b2)]
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
+    sess = session_for(layers)
+    assert_same(sess.run(x), ref, f"mlp {mkn}")
+    assert_same(session_for(layers, flags=_native.RG_SESSION_NO_FUSION).run(x), ref, f"mlp {mkn} unfused")
+    if m <= 148 * 4 * 256:
+        assert sess.last_npu_profile().kernel_launches == 1
