@@ -1211,6 +1211,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
         s.ev_of[2] = s.ev_of[1];
         break;
       }
+      (void)cudaGetLastError();  // a refused cooperative launch leaves a (non-sticky) error: op by op instead
     }
     // The fused kernel bulk-copies images, so its input must start on a 16-byte
     // boundary; a caller's unaligned view takes the op-by-op path instead.
