@@ -29,7 +29,7 @@ constexpr int kMaxK1 = 64, kMaxN = 32;
 
 struct Mlp2Params {
   Mlp2Args a;
-  unsigned* ws;      // [0] input absmax bits, [1] hidden absmax bits, [2] barrier arrivals, [3] abort
+  unsigned* ws;      // [2] barrier arrivals, [3] abort (words 0, 1 unused)
   uint64_t wait_ns;  // limit of each barrier wait
 };
 
@@ -47,9 +47,10 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 
 // Grid-wide barrier number `k` (1, 2): returns false when the wait gave up (or another
 // block's did); the arrivals counter is zeroed before the launch.  Thread 0 then reads
-// word k - 1 (the absmax the barrier completed) into *word for the block: one read per
+// *src (the absmax the barrier completed) into *word for the block: one read per
 // block, not one per warp of every block on the same address.
-__device__ bool grid_barrier(unsigned* ws, unsigned k, uint64_t limit_ns, int* flag, unsigned* word) {
+__device__ bool grid_barrier(unsigned* ws, unsigned k, uint64_t limit_ns, int* flag, const unsigned* src,
+                             unsigned* word) {
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -69,7 +70,7 @@ __device__ bool grid_barrier(unsigned* ws, unsigned k, uint64_t limit_ns, int* f
     }
     __threadfence();
     *flag = ok;
-    *word = *(volatile unsigned*)(ws + k - 1);
+    *word = *(volatile const unsigned*)src;
   }
   __syncthreads();
   return *flag != 0;
@@ -125,7 +126,7 @@ __global__ void __launch_bounds__(kMlpThreads) k_mlp2(const Mlp2Params P) {
     for (int64_t i = tid; i < total; i += nth) m1 = fmaxf(m1, fabsf(__ldg(a.x + i)));
   }
   m1 = block_max(m1, red);
-  if (threadIdx.x == 0 && m1 > 0.0f) atomicMax(P.ws, __float_as_uint(m1));
+  if (threadIdx.x == 0 && m1 > 0.0f) atomicMax(a.amax1, __float_as_uint(m1));
   // this thread's row (its first 16 values) is loaded before the barrier wait
   const int64_t row = tid;
   const bool has_row = row < a.m;
@@ -134,7 +135,7 @@ __global__ void __launch_bounds__(kMlpThreads) k_mlp2(const Mlp2Params P) {
   float xpre[kPre];
 #pragma unroll
   for (int e = 0; e < kPre; ++e) xpre[e] = has_row && e < a.k1 ? __ldg(xr + e) : 0.0f;
-  if (!grid_barrier(P.ws, 1, P.wait_ns, &flag, &word)) {
+  if (!grid_barrier(P.ws, 1, P.wait_ns, &flag, a.amax1, &word)) {
     if (threadIdx.x == 0) atomicExch(a.err, 1);
     return;
   }
@@ -171,8 +172,8 @@ __global__ void __launch_bounds__(kMlpThreads) k_mlp2(const Mlp2Params P) {
     }
   }
   m2 = block_max(m2, red);
-  if (threadIdx.x == 0 && m2 > 0.0f) atomicMax(P.ws + 1, __float_as_uint(m2));
-  if (!grid_barrier(P.ws, 2, P.wait_ns, &flag, &word)) {
+  if (threadIdx.x == 0 && m2 > 0.0f) atomicMax(a.amax2, __float_as_uint(m2));
+  if (!grid_barrier(P.ws, 2, P.wait_ns, &flag, a.amax2, &word)) {
     if (threadIdx.x == 0) atomicExch(a.err, 1);
     return;
   }
@@ -246,7 +247,7 @@ bool launch_kw(const Mlp2Args& a, unsigned* ws, cudaStream_t st) {
 
 bool mlp2_eligible(const Mlp2Args& a) {
   return a.m > 0 && a.k1 >= 1 && a.k1 <= kMaxK1 && a.kpad1 >= a.k1 && (a.kpad1 & 15) == 0 && a.kpad1 <= kMaxK1 &&
-         a.n1 >= 1 && a.n1 <= kMaxN && a.n2 >= 1 && a.n2 <= kMaxN && a.kpad2 >= a.n1 && a.err &&
+         a.n1 >= 1 && a.n1 <= kMaxN && a.n2 >= 1 && a.n2 <= kMaxN && a.kpad2 >= a.n1 && a.err && a.amax1 && a.amax2 &&
          (reinterpret_cast<uintptr_t>(a.w1) & 3) == 0;
 }
 

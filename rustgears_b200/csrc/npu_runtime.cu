@@ -1198,6 +1198,9 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
       ma.act1 = op.act; ma.act2 = l2.act; ma.p1 = op.param; ma.p2 = l2.param;
       float* out = y_dev ? y_dev : dst;
       ma.y = out;
+      // the absmaxes land in the ops' own slots, where a calibration run reads them
+      ma.amax1 = amax + P.amax_off[0];
+      ma.amax2 = amax + P.amax_off[1];
       ma.err = s.errw.as<int>();
       RG_TRY(s.mlpws.ensure(4 * sizeof(unsigned)));
       if (mlp2_eligible(ma) && launch_mlp2(ma, s.mlpws.as<unsigned>(), st)) {

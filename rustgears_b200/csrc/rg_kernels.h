@@ -220,6 +220,8 @@ struct Mlp2Args {
   float p1 = 0.0f, p2 = 0.0f;
   float* y = nullptr;        // [m, n2]
   unsigned* amax = nullptr;  // optional absmax sink of y
+  unsigned* amax1 = nullptr;  // absmax of x, then of the hidden rows (float bits; zeroed by the caller)
+  unsigned* amax2 = nullptr;
   int* err = nullptr;        // this call's error word (a barrier wait gave up)
 };
 bool mlp2_eligible(const Mlp2Args& a);
