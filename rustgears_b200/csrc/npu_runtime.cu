@@ -983,7 +983,11 @@ static rg_status gemm_tc_drained(Session& s, const GemmArgs& g, HostDrain& d, cu
     gc.m = std::min<int64_t>(step, g.m - r0);
     gc.a = g.a + r0 * g.lda;
     gc.out = g.out + r0 * g.n;
-    if (!launch_gemm_tc(gc, s.num_sms, st)) return fail(RG_ERR_CUDA, "TMA descriptor encoding failed");
+    if (!launch_gemm_tc(gc, s.num_sms, st)) {
+      // copies of earlier chunks may still be writing the caller's buffer: let them end first
+      cudaStreamSynchronize(s.copy_stream);
+      return fail(RG_ERR_CUDA, "TMA descriptor encoding failed");
+    }
     ++launches;
     RG_CUDA_TRY(cudaEventRecord(s.drain_events[(size_t)c], st));
     RG_CUDA_TRY(cudaStreamWaitEvent(s.copy_stream, s.drain_events[(size_t)c], 0));
