@@ -478,13 +478,14 @@ def test_tensor_core_gemm_every_activation(gpu, oracle_lib, act, mkn):
     assert_same(session_for(layers).run(x), ref, f"act {act} linear {mkn}")
 
 
-def test_host_output_drained_in_chunks(gpu, oracle_lib):
+@pytest.mark.parametrize("mkn", [(8192, 1024, 2048), (10001, 512, 1700)])
+def test_host_output_drained_in_chunks(gpu, oracle_lib, mkn):
     """A program ending in a tensor-core Linear whose host output is page-locked and at
     least 64 MiB: the GEMM runs in row chunks, each copied to the host as soon as it
-    is written.  Same result as the single-launch path (pageable output) and the oracle,
-    twice in a row on one session."""
+    is written (whole chunks, and a ragged last chunk and row tile).  Same result as the
+    single-launch path (pageable output) and the oracle, twice in a row on one session."""
     torch = gpu
-    layers, x = configs.c3_linear(8192, 1024, 2048, seed=11)
+    layers, x = configs.c3_linear(*mkn, seed=11)
     ref, _, _ = oracle.Program(layers).execute(x, nthreads=8)
     sess = session_for(layers)
     plain = sess.run(x)
