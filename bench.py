@@ -742,6 +742,10 @@ def main():
                   "what": "each step's outputs all-gathered to every rank over NVLink (rg_session_allgather, NCCL) "
                           "inside the timed region; compute-only `value` leaves them sharded"}
 
+    # MACs per unit from a one-unit run, before the profiled full-batch runs below: the
+    # roofline reads the last profile's per-op MACs, which must be the full batch's
+    macs_sess = sess if not f32 else InferenceSession.from_module(model, ExecutionProvider.npu_int8(), device=local)
+    macs_unit = program_macs(macs_sess, x.shape) if not c3 else int(np.prod(WORKLOADS[cfg]["shape"][1:]))
     # per-op CUDA-event durations (the roofline's kernel times) from profiled runs
     prof_runs = max(3, min(args.steps, 10))
     per_op_ns = np.zeros(nops)
@@ -750,8 +754,6 @@ def main():
         sess.run_device(xd, yd)
         per_op_ns += np.array([r.duration_ns for r in sess.last_npu_profile().records], dtype=np.float64)
     per_op_ns *= args.steps / prof_runs
-    macs_sess = sess if not f32 else InferenceSession.from_module(model, ExecutionProvider.npu_int8(), device=local)
-    macs_unit = program_macs(macs_sess, x.shape) if not c3 else int(np.prod(WORKLOADS[cfg]["shape"][1:]))
     units_all = units * world
     value = units_all / (ms_per_step / 1e3)
     tops = value * 2.0 * macs_unit / 1e12

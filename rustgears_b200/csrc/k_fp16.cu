@@ -52,7 +52,12 @@ struct Fp16Params {
 };
 
 // MODE 0: FP16 arm (EXACT: FMA chains, else separate product and sum); MODE 1: f32 arm.
-template <int TX, bool CONV, bool EXACT, int MODE = 0>
+// POOL (FP16 conv): the 2 x 2 / stride 2 max-pool after the conv in the same kernel.
+// Rows are then (pool window, position): a tile holds TY windows, and the 4 rows of a
+// thread (ty + TY i) are the window's pixels in the pool's scan order (dy, dx), so the
+// thread finishes the window from its own accumulators: the epilogue of each pixel,
+// then the reference's max (a larger value or a NaN replaces the best; first of ties).
+template <int TX, bool CONV, bool EXACT, int MODE = 0, bool POOL = false>
 __global__ void __launch_bounds__(kThreads) k_fp16_gemm(const Fp16Params P) {
   constexpr int TY = kThreads / TX, TM = 4 * TY, TN = 4 * TX;
   constexpr int KPT = TK * TM / kThreads;  // A values one thread stages per slice
@@ -68,7 +73,8 @@ __global__ void __launch_bounds__(kThreads) k_fp16_gemm(const Fp16Params P) {
   const int64_t m0 = (int64_t)blockIdx.x * TM, n0 = (int64_t)blockIdx.y * TN;
   const int64_t ktiles = (a.k + TK - 1) / TK;
   const int64_t row = m0 + lr;
-  const bool row_ok = row < a.m;
+  // (POOL: the staged row's window must exist; its 4 positions always do)
+  const bool row_ok = POOL ? ((int64_t)blockIdx.x * TY + lr % TY) * 4 < a.m : row < a.m;
   // the staged row: a Linear row, or the output pixel whose receptive field is gathered
   const float* arow = nullptr;
   int32_t iy0 = 0, ix0 = 0;
@@ -79,7 +85,16 @@ __global__ void __launch_bounds__(kThreads) k_fp16_gemm(const Fp16Params P) {
       const int32_t ky = rem / a.ks, kx = rem - ky * a.ks;
       ktab[kk] = make_int2((c * a.h + ky) * a.w + kx, (ky << 16) | kx);
     }
-    if (row_ok) {  // rows < 2^31 (checked at launch): 32-bit division
+    if (POOL && row_ok) {  // row lr of the tile: window lr % TY, position lr / TY
+      const int pos = lr / TY;
+      const uint32_t gw = (uint32_t)blockIdx.x * TY + (uint32_t)(lr % TY);
+      const uint32_t per_img = (uint32_t)a.ph * (uint32_t)a.pw;
+      const uint32_t img = gw / per_img, wr = gw - img * per_img;
+      const int32_t py = (int32_t)(wr / (uint32_t)a.pw), px = (int32_t)(wr - (uint32_t)py * (uint32_t)a.pw);
+      iy0 = (2 * py + (pos >> 1)) * a.stride - a.pad;
+      ix0 = (2 * px + (pos & 1)) * a.stride - a.pad;
+      arow = a.x + img * (int64_t)a.c * a.h * a.w;
+    } else if (row_ok) {  // rows < 2^31 (checked at launch): 32-bit division
       const uint32_t img = (uint32_t)row / (uint32_t)P.L;
       const int32_t l = (int32_t)((uint32_t)row - img * (uint32_t)P.L);
       const int32_t oy = l / a.ow, ox = l - oy * a.ow;
@@ -182,6 +197,27 @@ __global__ void __launch_bounds__(kThreads) k_fp16_gemm(const Fp16Params P) {
       }
     }
   }
+  if (POOL) {  // the thread's window: blockIdx.x * TY + ty
+    const uint32_t gw = (uint32_t)blockIdx.x * TY + (uint32_t)ty;
+    if ((int64_t)gw * 4 >= a.m) return;
+    const uint32_t per_img = (uint32_t)a.ph * (uint32_t)a.pw;
+    const uint32_t img = gw / per_img, wr = gw - img * per_img;
+    float* o = a.out + (int64_t)img * a.n * per_img + wr;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t col = n0 + tx * 4 + j;
+      if (col >= a.n) continue;
+      const float b = __ldg(a.bias + col);
+      float best = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float v = act_apply(a.act, a.act_param, round_fp16(__fadd_rn(acc[i][j], b)));
+        if (v > best || v != v) best = v;
+      }
+      o[col * per_img] = best;
+    }
+    return;
+  }
   // epilogue: act(round_fp16(acc + bias)), row-major [m, n] or NCHW
   uint32_t img_e = 0, l_e = 0;  // conv: (image, pixel) of row m0 + ty, advanced by TY per i
   if (CONV) {
@@ -225,7 +261,9 @@ bool launch_tx(const Fp16Params& P, cudaStream_t st) {
   const dim3 grid((unsigned)((a.m + TM - 1) / TM), (unsigned)((a.n + TN - 1) / TN));
   if (a.conv) {
     const size_t smem = (size_t)a.k * sizeof(int2);
-    auto kern = a.f32 ? k_fp16_gemm<TX, true, true, 1> : a.exact ? k_fp16_gemm<TX, true, true> : k_fp16_gemm<TX, true, false>;
+    auto kern = a.f32 ? k_fp16_gemm<TX, true, true, 1>
+                : a.pool ? (a.exact ? k_fp16_gemm<TX, true, true, 0, true> : k_fp16_gemm<TX, true, false, 0, true>)
+                : a.exact ? k_fp16_gemm<TX, true, true> : k_fp16_gemm<TX, true, false>;
     if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return false;
     kern<<<grid, kThreads, smem, st>>>(P);
@@ -260,6 +298,7 @@ bool launch_fp16_gemm(const Fp16Args& a, cudaStream_t st) {
   if (a.conv && (a.k > kMaxConvK || a.h >= 65536 || a.w >= 65536 || a.ks >= 65536 ||
                  (int64_t)a.c * a.h * a.w >= ((int64_t)1 << 31) || a.m + 1024 >= ((int64_t)1 << 31)))
     return false;
+  if (a.pool && (a.f32 || !a.conv || a.ph <= 0 || a.pw <= 0 || a.m % 4 != 0)) return false;
   Fp16Params P;
   P.a = a;
   P.L = a.conv ? (int64_t)a.oh * a.ow : 0;

@@ -1156,6 +1156,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
 
   RG_PENDING("the first launch");
   bool fused_residual = false;
+  bool fused_pool = false;  // an FP16 conv wrote its following 2 x 2 max-pool's output
   std::vector<uint8_t> amax2_done(n, 0);  // a shortcut's absmax came from its block input's producer
   const float* cur = x_dev;
   int32_t launches = 0;
@@ -1362,6 +1363,18 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
             f.oh = (int32_t)os.out[2]; f.ow = (int32_t)os.out[3];
             f.m = os.in[0] * os.out[2] * os.out[3]; f.n = op.out_c; f.k = (int64_t)op.in_c * op.k * op.k;
           }
+          // an FP16 conv followed by MaxPool2d(2, 2) writes the pooled map directly
+          const bool pool2 = op.kind == RG_LAYER_CONV2D && s.precision == RG_PREC_FP16 && !s.trace &&
+                             !(s.flags & RG_SESSION_NO_FUSION) && i + 1 < n &&
+                             s.ops[i + 1].kind == RG_LAYER_MAXPOOL2D && s.ops[i + 1].k == 2 && s.ops[i + 1].stride == 2 &&
+                             os.out[2] >= 2 && os.out[3] >= 2;
+          if (pool2) {
+            f.pool = 1;
+            f.ph = (int32_t)(os.out[2] / 2);
+            f.pw = (int32_t)(os.out[3] / 2);
+            f.m = os.in[0] * f.ph * f.pw * 4;
+            if (i + 2 == n && y_dev) f.out = dst = y_dev;
+          }
           if (!launch_fp16_gemm(f, st))
             return fail(RG_ERR_UNSUPPORTED, "op %zu: FP16 conv beyond the kernel's limits (C*k*k = %lld > 16384, "
                         "an image of 2^31 elements, or 2^31 output pixels in the batch)", i, (long long)f.k);
@@ -1373,6 +1386,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
           } else {
             cur = dst;
           }
+          fused_pool = pool2;
           break;
         }
         bool use3 = false;
@@ -1725,6 +1739,11 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
     if (fused_residual) {  // the residual end ran inside the conv: 0 ns on its record
       fused_residual = false;
       saved.pop_back();
+      s.ev_of[i + 2] = s.ev_of[i + 1];
+      ++i;
+    }
+    if (fused_pool) {  // the pool ran inside the conv: 0 ns on its record
+      fused_pool = false;
       s.ev_of[i + 2] = s.ev_of[i + 1];
       ++i;
     }

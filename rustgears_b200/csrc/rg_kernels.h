@@ -128,6 +128,9 @@ struct Fp16Args {
                                 // rounding, FMA chains except past the matmul's last full
                                 // 8-wide column block, out = acc + bias
   int32_t conv = 0, c = 0, h = 0, w = 0, ks = 0, stride = 1, pad = 0, oh = 0, ow = 0;
+  // FP16 conv only: the MaxPool2d(2, 2) that follows, fused (out is then the pooled
+  // [images, n, ph, pw] map and m = images * ph * pw * 4)
+  int32_t pool = 0, ph = 0, pw = 0;
 };
 // false: a conv whose reduction (C k k > 16384) or geometry the kernel does not take
 bool launch_fp16_gemm(const Fp16Args& a, cudaStream_t st);

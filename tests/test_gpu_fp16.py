@@ -100,3 +100,28 @@ def test_extension_blocks_are_int8_only(gpu):
     with pytest.raises(_native.RgError) as e:
         fp16_session(layers)
     assert e.value.status == _native.RG_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("cin,cout,k,st,pad,h,w,act", [(1, 16, 3, 1, 1, 28, 28, 1), (3, 8, 3, 1, 1, 15, 13, 5),
+                                                       (5, 70, 3, 2, 1, 11, 10, 0), (2, 4, 5, 1, 2, 9, 9, 4)])
+def test_conv_with_fused_max_pool(gpu, oracle_lib, cin, cout, k, st, pad, h, w, act):
+    """An FP16 conv followed by MaxPool2d(2, 2) writes the pooled map in the same kernel
+    (odd maps drop the last row / column as the pool does); special values in the input
+    (a NaN that must propagate through the pool, an inf); against the oracle and the
+    unfused session, bit for bit, with one launch fewer."""
+    rng = np.random.default_rng(cin * 100 + cout + h)
+    wt = (rng.standard_normal((cout, cin, k, k)) * 0.3).astype(np.float32)
+    b = (rng.standard_normal(cout) * 0.1).astype(np.float32)
+    layers = [dict(kind=configs.CONV2D, in_channels=cin, out_channels=cout, kernel=k, stride=st, padding=pad,
+                   weight=wt.ravel(), bias=b), configs.act(act, 0.1),
+              dict(kind=configs.MAXPOOL2D, kernel=2, stride=2)]
+    x = rng.standard_normal((5, cin, h, w)).astype(np.float32)
+    x[1, 0, h // 2, w // 2] = np.nan
+    x[2, 0, 1, 1] = np.inf
+    ref, _ = ref_fp16(layers, x)
+    fused = fp16_session(layers)
+    assert_same(fused.run(x), ref, "fused conv + pool")
+    n_fused = fused.last_npu_profile().kernel_launches
+    unfused = fp16_session(layers, flags=_native.RG_SESSION_NO_FUSION)
+    assert_same(unfused.run(x), ref, "conv, then pool")
+    assert n_fused == unfused.last_npu_profile().kernel_launches - 1
