@@ -52,7 +52,8 @@ struct Fp16Params {
 };
 
 // MODE 0: FP16 arm (EXACT: FMA chains, else separate product and sum); MODE 1: f32 arm.
-// POOL (FP16 conv): the 2 x 2 / stride 2 max-pool after the conv in the same kernel.
+// POOL (conv): the 2 x 2 / stride 2 max-pool after the conv in the same kernel (the f32
+// arm: after the conv and its standalone activation, applied to each pixel first).
 // Rows are then (pool window, position): a tile holds TY windows, and the 4 rows of a
 // thread (ty + TY i) are the window's pixels in the pool's scan order (dy, dx), so the
 // thread finishes the window from its own accumulators: the epilogue of each pixel,
@@ -141,7 +142,19 @@ __global__ void __launch_bounds__(kThreads) k_fp16_gemm(const Fp16Params P) {
   bool fuse[4] = {true, true, true, true};
   bool all_fused = true;
   if (MODE == 1) {
-    if (CONV) {
+    if (CONV && POOL) {  // the pixel of row ty + TY i: position i of window blockIdx.x * TY + ty
+      const int64_t nvL = P.L / 8 * 8;
+      const uint32_t gw = (uint32_t)blockIdx.x * TY + (uint32_t)ty;
+      const uint32_t per_img = (uint32_t)a.ph * (uint32_t)a.pw;
+      const uint32_t wr = gw % per_img;
+      const int32_t py = (int32_t)(wr / (uint32_t)a.pw), px = (int32_t)(wr % (uint32_t)a.pw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t l = (int64_t)(2 * py + (i >> 1)) * a.ow + 2 * px + (i & 1);
+        fuse[i] = l < nvL;
+        all_fused = all_fused && fuse[i];
+      }
+    } else if (CONV) {
       const int64_t nvL = P.L / 8 * 8;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -211,7 +224,9 @@ __global__ void __launch_bounds__(kThreads) k_fp16_gemm(const Fp16Params P) {
       float best = -INFINITY;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const float v = act_apply(a.act, a.act_param, round_fp16(__fadd_rn(acc[i][j], b)));
+        // the f32 arm: matmul + bias, then its activation op; the FP16 arm: its epilogue
+        const float v = MODE == 1 ? act_apply(a.act, a.act_param, __fadd_rn(acc[i][j], b))
+                                  : act_apply(a.act, a.act_param, round_fp16(__fadd_rn(acc[i][j], b)));
         if (v > best || v != v) best = v;
       }
       o[col * per_img] = best;
@@ -261,7 +276,7 @@ bool launch_tx(const Fp16Params& P, cudaStream_t st) {
   const dim3 grid((unsigned)((a.m + TM - 1) / TM), (unsigned)((a.n + TN - 1) / TN));
   if (a.conv) {
     const size_t smem = (size_t)a.k * sizeof(int2);
-    auto kern = a.f32 ? k_fp16_gemm<TX, true, true, 1>
+    auto kern = a.f32 ? (a.pool ? k_fp16_gemm<TX, true, true, 1, true> : k_fp16_gemm<TX, true, true, 1>)
                 : a.pool ? (a.exact ? k_fp16_gemm<TX, true, true, 0, true> : k_fp16_gemm<TX, true, false, 0, true>)
                 : a.exact ? k_fp16_gemm<TX, true, true> : k_fp16_gemm<TX, true, false>;
     if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
@@ -298,7 +313,7 @@ bool launch_fp16_gemm(const Fp16Args& a, cudaStream_t st) {
   if (a.conv && (a.k > kMaxConvK || a.h >= 65536 || a.w >= 65536 || a.ks >= 65536 ||
                  (int64_t)a.c * a.h * a.w >= ((int64_t)1 << 31) || a.m + 1024 >= ((int64_t)1 << 31)))
     return false;
-  if (a.pool && (a.f32 || !a.conv || a.ph <= 0 || a.pw <= 0 || a.m % 4 != 0)) return false;
+  if (a.pool && (!a.conv || a.ph <= 0 || a.pw <= 0 || a.m % 4 != 0)) return false;
   Fp16Params P;
   P.a = a;
   P.L = a.conv ? (int64_t)a.oh * a.ow : 0;

@@ -1156,7 +1156,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
 
   RG_PENDING("the first launch");
   bool fused_residual = false;
-  bool fused_pool = false;  // an FP16 conv wrote its following 2 x 2 max-pool's output
+  int absorbed = 0;  // ops after a conv that ran inside it (an activation, a 2 x 2 max-pool)
   std::vector<uint8_t> amax2_done(n, 0);  // a shortcut's absmax came from its block input's producer
   const float* cur = x_dev;
   int32_t launches = 0;
@@ -1363,17 +1363,28 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
             f.oh = (int32_t)os.out[2]; f.ow = (int32_t)os.out[3];
             f.m = os.in[0] * os.out[2] * os.out[3]; f.n = op.out_c; f.k = (int64_t)op.in_c * op.k * op.k;
           }
-          // an FP16 conv followed by MaxPool2d(2, 2) writes the pooled map directly
-          const bool pool2 = op.kind == RG_LAYER_CONV2D && s.precision == RG_PREC_FP16 && !s.trace &&
-                             !(s.flags & RG_SESSION_NO_FUSION) && i + 1 < n &&
-                             s.ops[i + 1].kind == RG_LAYER_MAXPOOL2D && s.ops[i + 1].k == 2 && s.ops[i + 1].stride == 2 &&
-                             os.out[2] >= 2 && os.out[3] >= 2;
-          if (pool2) {
-            f.pool = 1;
-            f.ph = (int32_t)(os.out[2] / 2);
-            f.pw = (int32_t)(os.out[3] / 2);
-            f.m = os.in[0] * f.ph * f.pw * 4;
-            if (i + 2 == n && y_dev) f.out = dst = y_dev;
+          // a conv followed by MaxPool2d(2, 2) (in the f32 provider with the standalone
+          // activation between them) writes the pooled map directly
+          int absorb = 0;
+          if (op.kind == RG_LAYER_CONV2D && !s.trace && !(s.flags & RG_SESSION_NO_FUSION) && os.out[2] >= 2 &&
+              os.out[3] >= 2) {
+            size_t j = i + 1;
+            int32_t pact = op.act;
+            float pprm = op.param;
+            if (f.f32 && j < n && s.ops[j].kind == RG_LAYER_ACTIVATION) {
+              pact = s.ops[j].act;
+              pprm = s.ops[j].param;
+              ++j;
+            }
+            if (j < n && s.ops[j].kind == RG_LAYER_MAXPOOL2D && s.ops[j].k == 2 && s.ops[j].stride == 2) {
+              f.pool = 1;
+              f.act = pact; f.act_param = pprm;
+              f.ph = (int32_t)(os.out[2] / 2);
+              f.pw = (int32_t)(os.out[3] / 2);
+              f.m = os.in[0] * f.ph * f.pw * 4;
+              if (j + 1 == n && y_dev) f.out = dst = y_dev;
+              absorb = (int)(j - i);
+            }
           }
           if (!launch_fp16_gemm(f, st))
             return fail(RG_ERR_UNSUPPORTED, "op %zu: FP16 conv beyond the kernel's limits (C*k*k = %lld > 16384, "
@@ -1386,7 +1397,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
           } else {
             cur = dst;
           }
-          fused_pool = pool2;
+          absorbed = absorb;
           break;
         }
         bool use3 = false;
@@ -1742,8 +1753,7 @@ static rg_status execute(Session& s, const float* x_dev, const RunPlan& P, float
       s.ev_of[i + 2] = s.ev_of[i + 1];
       ++i;
     }
-    if (fused_pool) {  // the pool ran inside the conv: 0 ns on its record
-      fused_pool = false;
+    for (; absorbed > 0; --absorbed) {  // ops that ran inside the conv: 0 ns on their records
       s.ev_of[i + 2] = s.ev_of[i + 1];
       ++i;
     }

@@ -77,3 +77,25 @@ def test_extension_kinds_and_gpu_provider_rejected(gpu):
     with pytest.raises(_native.RgError) as e:
         InferenceSession.from_layers([spec_from_dict(l) for l in layers], ExecutionProvider.gpu(0))
     assert e.value.status == _native.RG_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("cin,cout,k,st,pad,h,w,act", [(1, 16, 3, 1, 1, 10, 10, ACT_RELU), (3, 8, 3, 1, 1, 15, 13, ACT_GELU),
+                                                       (5, 70, 3, 2, 1, 11, 10, None), (2, 4, 5, 1, 2, 9, 9, ACT_RELU)])
+def test_conv_activation_pool_in_one_kernel(gpu, oracle_lib, cin, cout, k, st, pad, h, w, act):
+    """Conv2d, its activation layer and MaxPool2d(2, 2) in one kernel: each pixel's sum
+    (FMA chain, or unfused past the matmul's last full 8-wide block of pixels: the 10 x
+    10 case puts such pixels inside pool windows), its activation, then the pool's
+    NaN-propagating max; a NaN and an inf in the input; bit-exact against run_standard."""
+    rng = np.random.default_rng(cin * 100 + cout + h)
+    wt = rng.standard_normal((cout, cin, k, k)).astype(np.float32)
+    b = rng.standard_normal(cout).astype(np.float32)
+    layers = [dict(kind=configs.CONV2D, in_channels=cin, out_channels=cout, kernel=k, stride=st, padding=pad,
+                   weight=wt.ravel(), bias=b)]
+    if act is not None:
+        layers.append(configs.act(act))
+    layers.append(dict(kind=configs.MAXPOOL2D, kernel=2, stride=2))
+    x = rng.standard_normal((4, cin, h, w)).astype(np.float32)
+    x[1, 0, h // 2, w // 2] = np.nan
+    x[2, 0, 1, 1] = np.inf
+    ref = oracle.run_standard(layers, x)
+    assert_same(cpu_session(layers).run(x), ref, "f32 conv + act + pool")
