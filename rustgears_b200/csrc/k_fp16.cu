@@ -58,7 +58,9 @@ struct Fp16Params {
 // thread (ty + TY i) are the window's pixels in the pool's scan order (dy, dx), so the
 // thread finishes the window from its own accumulators: the epilogue of each pixel,
 // then the reference's max (a larger value or a NaN replaces the best; first of ties).
-template <int TX, bool CONV, bool EXACT, int MODE = 0, bool POOL = false>
+// ACTC (POOL): the activation fixed at compile time (ReLU or none), or -1: chosen at run
+// time; a fixed one keeps the 16 unrolled pooled epilogues free of the other kinds' code.
+template <int TX, bool CONV, bool EXACT, int MODE = 0, bool POOL = false, int ACTC = -1>
 __global__ void __launch_bounds__(kThreads) k_fp16_gemm(const Fp16Params P) {
   constexpr int TY = kThreads / TX, TM = 4 * TY, TN = 4 * TX;
   constexpr int KPT = TK * TM / kThreads;  // A values one thread stages per slice
@@ -225,8 +227,8 @@ __global__ void __launch_bounds__(kThreads) k_fp16_gemm(const Fp16Params P) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         // the f32 arm: matmul + bias, then its activation op; the FP16 arm: its epilogue
-        const float v = MODE == 1 ? act_apply(a.act, a.act_param, __fadd_rn(acc[i][j], b))
-                                  : act_apply(a.act, a.act_param, round_fp16(__fadd_rn(acc[i][j], b)));
+        const float pre = MODE == 1 ? __fadd_rn(acc[i][j], b) : round_fp16(__fadd_rn(acc[i][j], b));
+        const float v = act_apply(ACTC >= 0 ? ACTC : a.act, a.act_param, pre);
         if (v > best || v != v) best = v;
       }
       o[col * per_img] = best;
@@ -269,16 +271,34 @@ __global__ void __launch_bounds__(kThreads) k_fp16_gemm(const Fp16Params P) {
   }
 }
 
+template <int TX, int ACTC>
+void launch_pool(const Fp16Params& P, dim3 grid, size_t smem, cudaStream_t st, bool& ok) {
+  const Fp16Args& a = P.a;
+  auto kern = a.f32 ? k_fp16_gemm<TX, true, true, 1, true, ACTC>
+              : a.exact ? k_fp16_gemm<TX, true, true, 0, true, ACTC> : k_fp16_gemm<TX, true, false, 0, true, ACTC>;
+  if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+    ok = false;
+    return;
+  }
+  kern<<<grid, kThreads, smem, st>>>(P);
+}
+
 template <int TX>
 bool launch_tx(const Fp16Params& P, cudaStream_t st) {
   const Fp16Args& a = P.a;
   constexpr int TM = 4 * (kThreads / TX), TN = 4 * TX;
   const dim3 grid((unsigned)((a.m + TM - 1) / TM), (unsigned)((a.n + TN - 1) / TN));
+  if (a.conv && a.pool) {
+    const size_t smem = (size_t)a.k * sizeof(int2);
+    bool ok = true;
+    if (a.act == ACT_RELU) launch_pool<TX, ACT_RELU>(P, grid, smem, st, ok);
+    else if (a.act == ACT_NONE) launch_pool<TX, ACT_NONE>(P, grid, smem, st, ok);
+    else launch_pool<TX, -1>(P, grid, smem, st, ok);
+    return ok;
+  }
   if (a.conv) {
     const size_t smem = (size_t)a.k * sizeof(int2);
-    auto kern = a.f32 ? (a.pool ? k_fp16_gemm<TX, true, true, 1, true> : k_fp16_gemm<TX, true, true, 1>)
-                : a.pool ? (a.exact ? k_fp16_gemm<TX, true, true, 0, true> : k_fp16_gemm<TX, true, false, 0, true>)
-                : a.exact ? k_fp16_gemm<TX, true, true> : k_fp16_gemm<TX, true, false>;
+    auto kern = a.f32 ? k_fp16_gemm<TX, true, true, 1> : a.exact ? k_fp16_gemm<TX, true, true> : k_fp16_gemm<TX, true, false>;
     if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return false;
     kern<<<grid, kThreads, smem, st>>>(P);
